@@ -1,0 +1,426 @@
+#!/usr/bin/env python
+"""Decode-step benchmark of the KV-cache hot path (append + GQA decode attention).
+
+Workload (the batched KV-cached decode microbench): B=256 sequences per GPU,
+cached lengths uniform in [1, 511] (seeded), 4 query / 2 KV heads, head_dim
+64, f32 KV, 16-token paged blocks handed out from a shuffled free list, 8
+layers. One step = one decode token for every sequence through all 8 layers:
+`slm_batch_begin`, 8 x `slm_batch_decode_layer` (RoPE on Q and K, paged
+append, split-K attention over the grown cache), `slm_batch_end`. After each
+step the sequences return to their drawn lengths (host bookkeeping only), so
+every step does the same work. One step reads ~544 MB of K/V, far more than
+the 126 MB L2, so no flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own 256
+sequences (weak scaling, no collective on the data path); the timed region is
+bracketed by barriers and the slowest rank's time is reported.
+
+`--impl reference` times the reference's CPU path for the same workload: the
+oracle restatement of rust/engine (the Rust engine cannot be built here), all
+host threads, one sampled batch of sequences per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "small-lm-rs_b200"))
+
+METRIC = "decode tok/s and KV-attn HBM GB/s (% of peak) at 1/2/4/8 B200 vs host CPU"
+B, LEN_LO, LEN_HI = 256, 1, 511
+LAYERS, HQ, HKV, D, CTX, BLOCK = 8, 4, 2, 64, 512, 16
+WORKLOAD = (f"batched decode microbench: B={B}, cached lengths U[{LEN_LO},{LEN_HI}], "
+            f"Hq={HQ}, Hkv={HKV}, d={D}, f32 KV, {BLOCK}-token paged blocks, shuffled "
+            f"block table, {LAYERS} layers, 1 appended token per sequence per step")
+REF_SAMPLE = 32  # sequences per reference-arm step
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def draw_lengths(seed: int):
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    return rng.integers(LEN_LO, LEN_HI + 1, size=B).astype(np.int64)
+
+
+def algorithmic_bytes(lengths, s_kv: int = 4) -> int:
+    """Bytes one decode launch must move for the batch (one layer):
+    K+V over L_i+1 positions, Q read + O write, new K/V read, the append
+    write, and the block-table entries."""
+    total = 0
+    for L in lengths:
+        Lp = int(L) + 1
+        total += (2 * HKV * D * s_kv * Lp + 2 * HQ * D * 4 + 2 * HKV * D * 4 + 2 * HKV * D * s_kv
+                  + 4 * math.ceil(Lp / BLOCK))
+    return total
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def ncu_traffic_per_launch():
+    """dram bytes (read + write) per decode launch from the committed ncu
+    summary, if one has been captured for this workload."""
+    p = ROOT / "profiles" / "decode_kernel_microbench.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock / throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.2)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        busy = [r for r in rows if r[2] > 200.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in busy for i, v in enumerate(r[3][1:5])
+                          if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in busy),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(busy), "power_w_max": max(r[2] for r in rows)}
+
+
+def cpu_baseline(lengths, seed: int, threads: int, budget_s: float = 8.0):
+    """The oracle (a restatement of the reference's decode path) on a bounded
+    sample: REF_SAMPLE sequences, all layers, repeated until ~budget_s."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    rng = np.random.default_rng(seed + 99)
+    inv = O.rope_inverse_frequencies(D, 10000.0)
+    sample = [int(x) for x in lengths[:REF_SAMPLE]]
+    caches = [O.DenseCache(LAYERS, CTX, HKV, D) for _ in sample]
+    for c, L in zip(caches, sample):
+        for layer in range(LAYERS):
+            k = rng.standard_normal((L, HKV, D)).astype(np.float32)
+            c.append_layer(layer, k, k, L)
+    n = len(sample)
+    q = rng.standard_normal((LAYERS, n, HQ, D)).astype(np.float32)
+    kv = rng.standard_normal((LAYERS, n, HKV, D)).astype(np.float32)
+
+    def one_step():
+        for layer in range(LAYERS):
+            O.forward_cached_attention_batch(caches, layer, q[layer], kv[layer], kv[layer], HQ,
+                                             inv, threads=threads)
+        for c, L in zip(caches, sample):
+            c.truncate_all(L)
+
+    one_step()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        one_step()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return n * reps / el, reps, el
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    lengths = draw_lengths(args.seed)
+    threads = O.max_threads()
+    rng = np.random.default_rng(args.seed + 7)
+    inv = O.rope_inverse_frequencies(D, 10000.0)
+    sample = [int(x) for x in lengths[:REF_SAMPLE]]
+    caches = [O.DenseCache(LAYERS, CTX, HKV, D) for _ in sample]
+    for c, L in zip(caches, sample):
+        for layer in range(LAYERS):
+            k = rng.standard_normal((L, HKV, D)).astype(np.float32)
+            _, kr = O.apply_rotary_with_offset(k.copy(), k, HKV, HKV, D, inv, 0)
+            c.append_layer(layer, kr, k, L)
+    n = len(sample)
+    q = rng.standard_normal((LAYERS, n, HQ, D)).astype(np.float32)
+    kv = rng.standard_normal((LAYERS, n, HKV, D)).astype(np.float32)
+
+    def step():
+        for layer in range(LAYERS):
+            O.forward_cached_attention_batch(caches, layer, q[layer], kv[layer], kv[layer], HQ,
+                                             inv, threads=threads)
+        for c, L in zip(caches, sample):
+            c.truncate_all(L)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = n * args.steps / el
+    sample_desc = (f"{n} of the {B} seeded sequences per step (lengths {min(sample)}..{max(sample)}),"
+                   f" all {LAYERS} layers, oracle restatement of rust/engine "
+                   "(attention.rs:794-816 per sequence), OpenMP over sequences")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "reference_sample_sequences": n},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample_desc},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import slmkv
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    seed = args.seed + 1000 * rank
+    lengths = draw_lengths(seed)
+    need_blocks = int(sum(math.ceil((int(L) + 1) / BLOCK) for L in lengths))
+    pool = slmkv.KvPool(num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV,
+                        head_dimension=D, context_length=CTX, rope_theta=10000.0,
+                        num_blocks=need_blocks + B + 64, max_sequences=B,
+                        kv_dtype=slmkv.KV_F32, device=local)
+    pool.shuffle(seed + 1)
+    caches = [pool.allocate_kv_cache(CTX) for _ in range(B)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed + 2)
+    total = int(lengths.sum())
+    with pool.begin(caches, [int(x) for x in lengths]) as b:
+        for layer in range(LAYERS):
+            k = torch.randn((total, HKV, D), generator=gen, device=dev)
+            v = torch.randn((total, HKV, D), generator=gen, device=dev)
+            b.append_layer(layer, k, v, rotate_keys=True)
+    torch.cuda.synchronize()
+    q = torch.randn((LAYERS, B, HQ, D), generator=gen, device=dev)
+    kn = torch.randn((LAYERS, B, HKV, D), generator=gen, device=dev)
+    vn = torch.randn((LAYERS, B, HKV, D), generator=gen, device=dev)
+    out = torch.empty((LAYERS, B, HQ, D), device=dev)
+    base = [int(x) for x in lengths]
+    stream = torch.cuda.current_stream()
+
+    kernel_events = []
+
+    def step(timed: bool, qq=q, kk=kn, vv=vn, oo=out):
+        batch = pool.begin(caches, 1)
+        for layer in range(LAYERS):
+            if timed:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            batch.decode_layer(layer, qq[layer], kk[layer], vv[layer], oo[layer])
+            if timed:
+                e1.record(stream)
+                kernel_events.append((e0, e1))
+        batch.end()
+        pool.truncate_many(caches, base)
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    for _ in range(max(args.warmup, 3)):
+        step(False)
+    torch.cuda.synchronize()
+    barrier()
+    launches0 = pool.launch_count()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    t_stop.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    launches = pool.launch_count() - launches0
+    clocks = sampler.stop() if sampler else None
+    ms = t_start.elapsed_time(t_stop)
+    kern_ms = [a.elapsed_time(b) for a, b in kernel_events]
+    kern_avg_ms = sum(kern_ms) / len(kern_ms)
+    if world > 1:
+        t = torch.tensor([ms, kern_avg_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, kern_avg_ms = float(t[0]), float(t[1])
+
+    # End to end through the public API with host buffers: pinned inputs are
+    # copied in and the outputs copied back inside every timed step.
+    hq_ = q.cpu().pin_memory()
+    hk_ = kn.cpu().pin_memory()
+    hv_ = vn.cpu().pin_memory()
+    ho_ = torch.empty_like(out, device="cpu").pin_memory()
+    dq, dk, dv, do = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn), torch.empty_like(out)
+
+    def e2e_step():
+        dq.copy_(hq_, non_blocking=True)
+        dk.copy_(hk_, non_blocking=True)
+        dv.copy_(hv_, non_blocking=True)
+        batch = pool.begin(caches, 1)
+        for layer in range(LAYERS):
+            batch.decode_layer(layer, dq[layer], dk[layer], dv[layer], do[layer])
+        ho_.copy_(do, non_blocking=True)
+        batch.end()
+        pool.truncate_many(caches, base)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    if not torch.equal(ho_, out.cpu()):
+        raise RuntimeError("end-to-end outputs differ from the device-resident run")
+
+    tokens = B * world * args.steps
+    value = tokens / (ms / 1e3)
+    e2e_value = tokens / (e2e_ms / 1e3)
+    peaks, peak_kind = measured_peaks()
+    alg = algorithmic_bytes(lengths)
+    achieved = alg / (kern_avg_ms / 1e3) / 1e9
+    traffic = ncu_traffic_per_launch()
+    result = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch_per_gpu": B, "layers": LAYERS,
+                   "l2": f"inputs larger than L2 ({LAYERS * alg / 1e6:.0f} MB of K/V per step)",
+                   "seed": args.seed},
+        "kv_attn_hbm_gbs": achieved,
+        "kv_attn_hbm_frac": achieved / peaks["hbm_gbs"],
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "traffic": traffic, "peak_source": peak_kind,
+                     "kernel": "decode_kernel (fused RoPE + paged append + split-K GQA attention)",
+                     "algorithmic_bytes_per_launch": alg, "avg_launch_ms": kern_avg_ms},
+        "e2e": {"value": e2e_value, "unit": "tok/s",
+                "h2d_bytes_per_step": int(q.numel() + kn.numel() + vn.numel()) * 4,
+                "d2h_bytes_per_step": int(out.numel()) * 4},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        cv, reps, el = cpu_baseline(lengths, args.seed, threads=1)
+        result["cpu_baseline"] = {
+            "value": cv, "unit": "tok/s", "cores": 1, "kind": "port",
+            "sample": (f"{REF_SAMPLE} of the {B} seeded sequences x {LAYERS} layers per step, "
+                       f"{reps} steps in {el:.1f} s, single thread (the reference's decode "
+                       "attention is serial per sequence)")}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    pool.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

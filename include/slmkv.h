@@ -1,0 +1,204 @@
+/*
+ * slmkv — B200 (sm_100a) KV-cache hot path for small-lm-rs, behind a C ABI.
+ *
+ * One context owns, on one GPU, a paged KV pool shared by many sequences:
+ *   K pool, V pool : [layer][block][kv_head][slot 0..15][head_dim]  (f32 | bf16)
+ *   block table    : [sequence slot][logical block] -> physical block id
+ * A sequence is the paged counterpart of the reference's per-request dense
+ * `KvCache` (rust/engine/src/kv_cache.rs:89-92): it keeps one logical length
+ * per layer, exactly like `LayerKvCache::sequence_length`, and the token at
+ * position p of layer l lives in slot p % 16 of physical block
+ * block_table[seq][p / 16] of layer l.
+ *
+ * Conventions (the reference's, kv_cache.rs:172-230 and error.rs:14-121):
+ *   - every call returns an slm_status; 0 is success and the negative codes
+ *     below mirror EngineError::{InvalidConfiguration, InvalidInput};
+ *   - validation completes before any host-visible state is mutated; a failed
+ *     call leaves lengths, block tables and the pool as they were;
+ *   - slm_last_error() returns the message of the last failure, formatted as
+ *     the reference formats EngineError ("invalid input for KV cache: ...").
+ * Threading: a context is used by one host thread at a time, and all calls on
+ * one context are ordered on the stream they are given (use one stream per
+ * context, or order the streams yourself).
+ * Pointers named d_* are device pointers on the context's GPU; h_* are host.
+ * No call falls back to the CPU: without a usable device every compute call
+ * fails with SLM_ERR_NO_DEVICE.
+ */
+#ifndef SLMKV_H
+#define SLMKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int slm_status;
+enum {
+  SLM_OK = 0,
+  SLM_ERR_INVALID_CONFIGURATION = -1, /* EngineError::InvalidConfiguration */
+  SLM_ERR_INVALID_INPUT = -2,         /* EngineError::InvalidInput (shape, index, state) */
+  SLM_ERR_CAPACITY = -3,              /* InvalidInput: sequence would exceed its capacity */
+  SLM_ERR_NON_FINITE = -4,            /* InvalidInput: appended K/V not finite */
+  SLM_ERR_POOL_EXHAUSTED = -5,        /* no free physical block (paged pool only) */
+  SLM_ERR_CUDA = -6,                  /* a CUDA runtime call failed */
+  SLM_ERR_DEVICE_TIMEOUT = -7,        /* a kernel's bounded wait expired */
+  SLM_ERR_NO_DEVICE = -8              /* context created without a device */
+};
+
+enum { SLM_KV_F32 = 0, SLM_KV_BF16 = 1 };
+
+/* Model-side dimensions: KvCacheConfig (kv_cache.rs:8-18) plus what the
+ * attention and RoPE need (config.rs: num_query_heads, rope_theta,
+ * context_length), plus the paged pool size. */
+typedef struct slm_config {
+  int32_t num_layers;          /* KvCacheConfig::num_layers */
+  int32_t num_query_heads;     /* ModelConfig::num_query_heads */
+  int32_t num_key_value_heads; /* KvCacheConfig::num_key_value_heads */
+  int32_t head_dimension;      /* KvCacheConfig::head_dimension (64 supported) */
+  int32_t context_length;      /* ModelConfig::context_length (max positions) */
+  float rope_theta;            /* ModelConfig::rope_theta */
+  int32_t num_blocks;          /* physical 16-token blocks in the pool */
+  int32_t max_sequences;       /* live sequence slots */
+  int32_t kv_dtype;            /* SLM_KV_F32 (reference) or SLM_KV_BF16 */
+} slm_config;
+
+typedef struct slm_ctx slm_ctx;
+typedef struct slm_batch slm_batch;
+typedef void* slm_stream; /* a cudaStream_t; NULL = the legacy default stream */
+
+/* ---- lifecycle ---------------------------------------------------------- */
+
+/* Validates the config (kv_cache.rs:43-55, rope.rs:21-31, config.rs:91-198
+ * head-divisibility) and allocates the pool, block table, RoPE table and
+ * scratch on `device`. device = -1 creates a host-only context: bookkeeping
+ * calls work, every compute call returns SLM_ERR_NO_DEVICE. */
+slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out);
+slm_status slm_destroy(slm_ctx* ctx);
+/* Message of the last failed call ("" if none). Valid until the next call. */
+const char* slm_last_error(const slm_ctx* ctx);
+/* Bytes of device memory the context holds. */
+slm_status slm_device_bytes(const slm_ctx* ctx, int64_t* bytes);
+/* Number of kernels this context has launched since it was created. */
+slm_status slm_launch_count(const slm_ctx* ctx, int64_t* launches);
+
+/* ---- sequences: the reference's KvCache, one per request ------------------ */
+
+/* KvCacheConfig::from_model + KvCache::allocate (kv_cache.rs:27-41, 101-116):
+ * max_sequence_length in 1..=context_length. Blocks are taken lazily. */
+slm_status slm_seq_create(slm_ctx* ctx, int32_t max_sequence_length, int32_t* seq_id);
+/* Dropping a KvCache: releases its blocks (shared prefix blocks are kept
+ * while other sequences or the prefix index hold them). */
+slm_status slm_seq_free(slm_ctx* ctx, int32_t seq_id);
+/* kv_cache.rs:157-170 */
+slm_status slm_seq_layer_length(const slm_ctx* ctx, int32_t seq_id, int32_t layer,
+                                int32_t* length);
+/* kv_cache.rs:129-135 (minimum over layers) */
+slm_status slm_seq_length(const slm_ctx* ctx, int32_t seq_id, int32_t* length);
+/* kv_cache.rs:139-141 and 145-150 */
+slm_status slm_seq_is_empty(const slm_ctx* ctx, int32_t seq_id, int32_t* is_empty);
+slm_status slm_seq_is_synchronized(const slm_ctx* ctx, int32_t seq_id, int32_t* is_sync);
+/* kv_cache.rs:285-293 (after the longest layer, saturating) */
+slm_status slm_seq_remaining_capacity(const slm_ctx* ctx, int32_t seq_id, int32_t* remaining);
+/* kv_cache.rs:302-321: transactional; fails unless every layer >= length. */
+slm_status slm_seq_truncate_all(slm_ctx* ctx, int32_t seq_id, int32_t length);
+/* truncate_all for n sequences at once (each transactional on its own);
+ * stops at the first failure and returns it. */
+slm_status slm_seqs_truncate_all(slm_ctx* ctx, int32_t n, const int32_t* h_seq_ids,
+                                 const int32_t* h_lengths);
+/* kv_cache.rs:323-346 */
+slm_status slm_seq_truncate_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, int32_t length);
+/* kv_cache.rs:296-300 */
+slm_status slm_seq_clear(slm_ctx* ctx, int32_t seq_id);
+/* Physical block ids of the sequence (paged layout; no reference
+ * counterpart). Writes min(n_blocks, capacity) ids and the count. */
+slm_status slm_seq_blocks(const slm_ctx* ctx, int32_t seq_id, int32_t* h_ids, int32_t capacity,
+                          int32_t* n_blocks);
+
+/* ---- single-sequence cache operations ------------------------------------- */
+
+/* KvCache::append_layer (kv_cache.rs:182-230) with the K half of
+ * ProjectedQkv::apply_rotary_with_offset (attention.rs:422-482) fused in:
+ * keys/values are [token_count, kv_heads, head_dim] f32 on the device; when
+ * `rotate_keys` is non-zero the keys are rotated at positions len..len+T-1
+ * before they are stored (values are stored as given). Stream-ordered.
+ * The finite check (kv_cache.rs:192-197) runs on the device: a non-finite
+ * value makes the call fail with SLM_ERR_NON_FINITE and the layer keeps its
+ * old length; the call synchronizes `stream` to report it. */
+slm_status slm_append_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, const float* d_keys,
+                            const float* d_values, int32_t token_count, int32_t rotate_keys,
+                            slm_stream stream);
+/* KvCache::layer_keys / layer_values (kv_cache.rs:237-248): gathers the
+ * initialized prefix of one layer through the block table into dense
+ * [len, kv_heads, head_dim] f32 device buffers (bf16 entries widen exactly).
+ * Either output may be NULL. */
+slm_status slm_gather_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, float* d_keys,
+                            float* d_values, slm_stream stream);
+/* GroupedQueryAttention::attend_cached_query (attention.rs:677-759) for one
+ * sequence: query [q_heads, head_dim] already rotated, out [q_heads*head_dim]. */
+slm_status slm_attend_cached_query(slm_ctx* ctx, int32_t seq_id, int32_t layer,
+                                   const float* d_query, float* d_out, slm_stream stream);
+
+/* ---- batched steps: many sequences, one launch per layer ------------------ */
+
+/* Opens a step for n sequences that each add token_counts[i] tokens to every
+ * layer (1 for a decode step). Each sequence must be synchronized
+ * (model.rs:345-350) and have room (kv_cache.rs:203-211); physical blocks for
+ * the new positions are taken here (copy-on-write when a target block is
+ * shared), and the step descriptor is uploaded once for all layers. Nothing
+ * is mutated when it fails. One open batch per context. */
+slm_status slm_batch_begin(slm_ctx* ctx, int32_t n, const int32_t* h_seq_ids,
+                           const int32_t* h_token_counts, slm_stream stream, slm_batch** out);
+/* Decode step of one layer for every sequence of the batch (all counts 1):
+ * GroupedQueryAttention::forward_cached_token's cache part
+ * (attention.rs:794-810): RoPE on Q and K at the pre-append position, append
+ * K/V, then attention over the grown cache, in one kernel.
+ * q: [n, q_heads, d], k/v: [n, kv_heads, d] (unrotated), out: [n, q_heads, d]. */
+slm_status slm_batch_decode_layer(slm_batch* batch, int32_t layer, const float* d_query,
+                                  const float* d_keys, const float* d_values, float* d_out);
+/* Append-only form (prompt prefill, attention.rs:863-868): keys/values are the
+ * batch's tokens concatenated in batch order, [sum(counts), kv_heads, d]. */
+slm_status slm_batch_append_layer(slm_batch* batch, int32_t layer, const float* d_keys,
+                                  const float* d_values, int32_t rotate_keys);
+/* Causal attention of the batch's new tokens over each sequence's cache
+ * (after slm_batch_append_layer for this layer): query token j of sequence i
+ * sits at position base_i + j and sees positions 0..base_i+j. With base 0 this
+ * is the prompt prefill of attention.rs:859-861 (causal_probabilities +
+ * attend_values); with an attached prefix it extends the prefix.
+ * q: [sum(counts), q_heads, d] (unrotated if rotate_query), out likewise. */
+slm_status slm_batch_prefill_attention(slm_batch* batch, int32_t layer, const float* d_query,
+                                       int32_t rotate_query, float* d_out);
+/* Closes the step: waits for its stream, and reports per sequence (h_status
+ * may be NULL) 0 or SLM_ERR_NON_FINITE. A sequence whose appends were not
+ * finite, or whose layers did not all advance by its count, is rolled back to
+ * its length at slm_batch_begin (model.rs:390-396). Returns the first failure. */
+slm_status slm_batch_end(slm_batch* batch, int32_t* h_status);
+/* Abandons the step: every sequence goes back to its begin length. */
+slm_status slm_batch_rollback(slm_batch* batch);
+
+/* ---- prefix cache (no reference counterpart; README.md:247 lists it as
+ *      future work). Full 16-token blocks are indexed by their token chain. -- */
+
+/* Attaches to an EMPTY sequence the longest chain of indexed full blocks that
+ * matches tokens[0..n_tokens); every layer's length becomes 16 * matched
+ * blocks. The blocks are shared (reference-counted) and never written again:
+ * a later write into one copies it first. */
+slm_status slm_prefix_attach(slm_ctx* ctx, int32_t seq_id, const uint32_t* h_tokens,
+                             int32_t n_tokens, int32_t* reused_tokens);
+/* Indexes the full blocks of a synchronized sequence that hold
+ * tokens[0..n_tokens) (n_tokens <= its length). Returns how many blocks are
+ * now indexed for that chain. */
+slm_status slm_prefix_publish(slm_ctx* ctx, int32_t seq_id, const uint32_t* h_tokens,
+                              int32_t n_tokens, int32_t* indexed_blocks);
+/* Number of blocks held by the index, and blocks free in the pool. */
+slm_status slm_pool_stats(const slm_ctx* ctx, int32_t* free_blocks, int32_t* indexed_blocks);
+/* Shuffles the free list with a seeded permutation, so that sequences get
+ * scattered physical blocks. Pool must be unused. */
+slm_status slm_pool_shuffle(slm_ctx* ctx, uint64_t seed);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SLMKV_H */

@@ -1,0 +1,1297 @@
+// Host engine of the KV-cache hot path: paged block pool, per-sequence
+// per-layer lengths (the reference's KvCache bookkeeping, kv_cache.rs:89-412),
+// prefix index, step descriptors, and the C ABI declared in include/slmkv.h.
+//
+// Error messages follow EngineError's Display format (error.rs:14-60):
+//   "invalid model configuration: <message>"
+//   "invalid input for <component>: <message>"
+#include <algorithm>
+#include <array>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <new>
+#include <random>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "slmkv.h"
+#include "slmkv_internal.h"
+
+using namespace slmkv;
+
+namespace {
+
+constexpr int kUploadSlots = 2;
+
+struct Seq {
+  bool live = false;
+  int32_t max_len = 0;
+  std::vector<int32_t> layer_len;
+  std::vector<int32_t> blocks;  // logical block -> physical id
+  bool in_batch = false;
+};
+
+struct BlockMeta {
+  bool indexed = false;
+  int32_t parent = -1;  // physical id of the previous block of the chain
+  uint64_t key = 0;
+  uint64_t stamp = 0;
+  std::array<uint32_t, kBlockTokens> tokens{};
+};
+
+// Pinned staging (ring of two) feeding one device region.
+struct Upload {
+  uint8_t* h[kUploadSlots] = {nullptr, nullptr};
+  cudaEvent_t ev[kUploadSlots] = {nullptr, nullptr};
+  uint8_t* d = nullptr;
+  size_t cap = 0;
+  int next = 0;
+};
+
+size_t align16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
+
+uint64_t mix64(uint64_t x) {  // splitmix64 finaliser
+  x += 0x9e3779b97f4a7c15ull;
+  x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+  x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+  return x ^ (x >> 31);
+}
+
+}  // namespace
+
+struct slm_batch {
+  slm_ctx* ctx = nullptr;
+  cudaStream_t stream = nullptr;
+  std::vector<int32_t> seq_ids, counts, base;
+  int32_t total_tokens = 0, max_count = 0, n_items = 0;
+  std::vector<uint8_t> layer_done;
+  SeqEntry* d_seqs = nullptr;
+  WorkItem* d_items = nullptr;
+  int32_t* d_status = nullptr;
+};
+
+struct slm_ctx {
+  slm_config cfg{};
+  int32_t device = -1;
+  int32_t num_sms = 0;
+  int32_t max_blocks_per_seq = 0;
+  int32_t group = 1;
+  int32_t max_items = 0;
+  int64_t device_bytes = 0;
+  int64_t launches = 0;  // kernels launched by this context
+  std::string err;
+
+  // device memory
+  void* k_pool = nullptr;
+  void* v_pool = nullptr;
+  int32_t* d_block_table = nullptr;
+  float2* d_rope = nullptr;
+  float* d_part_acc = nullptr;
+  float2* d_part_ml = nullptr;
+  int32_t* d_counters = nullptr;
+  int32_t* d_error = nullptr;
+  int32_t* h_readback = nullptr;  // pinned: [1 + max_sequences]
+  Upload up_batch, up_aux;
+  size_t upd_cap = 0, copy_cap = 0;
+
+  // host state
+  std::vector<Seq> seqs;
+  std::vector<int32_t> free_slots;
+  std::vector<int32_t> refcount;
+  std::vector<int32_t> free_list;
+  std::vector<BlockMeta> meta;
+  std::unordered_multimap<uint64_t, int32_t> index;
+  int32_t indexed_blocks = 0;
+  uint64_t clock = 0;
+  std::vector<TableUpdate> pending_updates;
+  std::vector<CopyJob> pending_copies;
+  slm_batch* open_batch = nullptr;
+
+  PoolGeom geom() const {
+    PoolGeom g{};
+    g.k = k_pool;
+    g.v = v_pool;
+    g.layer_elems = static_cast<int64_t>(cfg.num_blocks) * cfg.num_key_value_heads * kBlockTokens *
+                    cfg.head_dimension;
+    g.block_table = d_block_table;
+    g.max_blocks_per_seq = max_blocks_per_seq;
+    g.num_blocks = cfg.num_blocks;
+    g.num_layers = cfg.num_layers;
+    g.kv_heads = cfg.num_key_value_heads;
+    g.q_heads = cfg.num_query_heads;
+    g.bf16 = cfg.kv_dtype == SLM_KV_BF16;
+    g.rope = d_rope;
+    g.context_length = cfg.context_length;
+    g.error = d_error;
+    return g;
+  }
+};
+
+namespace {
+
+slm_status fail(slm_ctx* ctx, slm_status code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (ctx) ctx->err = buf;
+  return code;
+}
+slm_status input_error(slm_ctx* ctx, slm_status code, const char* component, const char* fmt,
+                       ...) {
+  char msg[400];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(msg, sizeof msg, fmt, ap);
+  va_end(ap);
+  return fail(ctx, code, "invalid input for %s: %s", component, msg);
+}
+slm_status cuda_fail(slm_ctx* ctx, cudaError_t e, const char* what) {
+  return fail(ctx, SLM_ERR_CUDA, "CUDA error in %s: %s", what, cudaGetErrorString(e));
+}
+#define CU(ctx, call)                                      \
+  do {                                                     \
+    cudaError_t _e = (call);                               \
+    if (_e != cudaSuccess) return cuda_fail(ctx, _e, #call); \
+  } while (0)
+
+bool has_device(const slm_ctx* c) { return c->device >= 0; }
+
+slm_status need_device(slm_ctx* c) {
+  if (!has_device(c))
+    return fail(c, SLM_ERR_NO_DEVICE,
+                "no device: this context was created for host bookkeeping only");
+  cudaError_t e = cudaSetDevice(c->device);
+  if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
+  return SLM_OK;
+}
+
+Seq* get_seq(slm_ctx* c, int32_t id) {
+  if (id < 0 || id >= static_cast<int32_t>(c->seqs.size()) || !c->seqs[id].live) return nullptr;
+  return &c->seqs[id];
+}
+const Seq* get_seq(const slm_ctx* c, int32_t id) {
+  if (id < 0 || id >= static_cast<int32_t>(c->seqs.size()) || !c->seqs[id].live) return nullptr;
+  return &c->seqs[id];
+}
+slm_status unknown_seq(slm_ctx* c, int32_t id) {
+  return input_error(c, SLM_ERR_INVALID_INPUT, "KV cache", "sequence %d is not live", id);
+}
+
+int32_t seq_min_len(const Seq& s) { return *std::min_element(s.layer_len.begin(), s.layer_len.end()); }
+int32_t seq_max_len(const Seq& s) { return *std::max_element(s.layer_len.begin(), s.layer_len.end()); }
+bool seq_synchronized(const Seq& s) { return seq_min_len(s) == seq_max_len(s); }
+
+// ---- block pool -------------------------------------------------------------
+
+void unindex_block(slm_ctx* c, int32_t b) {
+  BlockMeta& m = c->meta[b];
+  if (!m.indexed) return;
+  auto range = c->index.equal_range(m.key);
+  for (auto it = range.first; it != range.second; ++it)
+    if (it->second == b) {
+      c->index.erase(it);
+      break;
+    }
+  m.indexed = false;
+  --c->indexed_blocks;
+}
+
+void release_block(slm_ctx* c, int32_t b) {
+  if (--c->refcount[b] == 0) c->free_list.push_back(b);
+}
+
+// Takes a free block, evicting the least recently used block that only the
+// prefix index still holds when the free list is empty. -1 if none.
+int32_t take_block(slm_ctx* c) {
+  if (c->free_list.empty()) {
+    int32_t victim = -1;
+    uint64_t best = UINT64_MAX;
+    for (int32_t b = 0; b < c->cfg.num_blocks; ++b)
+      if (c->meta[b].indexed && c->refcount[b] == 1 && c->meta[b].stamp < best) {
+        best = c->meta[b].stamp;
+        victim = b;
+      }
+    if (victim < 0) return -1;
+    unindex_block(c, victim);
+    release_block(c, victim);
+  }
+  const int32_t b = c->free_list.back();
+  c->free_list.pop_back();
+  c->refcount[b] = 1;
+  return b;
+}
+
+void release_tail(slm_ctx* c, int32_t slot, int32_t keep_blocks) {
+  Seq& s = c->seqs[slot];
+  while (static_cast<int32_t>(s.blocks.size()) > keep_blocks) {
+    release_block(c, s.blocks.back());
+    s.blocks.pop_back();
+  }
+}
+
+int32_t blocks_for(int32_t tokens) { return (tokens + kBlockTokens - 1) / kBlockTokens; }
+
+// Ensures seq has exclusive blocks covering positions [from, to). New blocks
+// and copy-on-write replacements are recorded in `taken` (for undo) and the
+// pending table updates / copies. Returns false when the pool is exhausted.
+struct Undo {
+  std::vector<std::pair<int32_t, std::vector<int32_t>>> old_blocks;  // slot, previous block list
+  std::vector<int32_t> taken;
+  size_t updates_mark = 0, copies_mark = 0;
+};
+
+bool reserve_positions(slm_ctx* c, int32_t slot, int32_t from, int32_t to, Undo& undo) {
+  Seq& s = c->seqs[slot];
+  if (to <= from) return true;
+  const int32_t first = from / kBlockTokens, last = (to - 1) / kBlockTokens;
+  bool saved = false;
+  auto save = [&] {
+    if (!saved) {
+      undo.old_blocks.emplace_back(slot, s.blocks);
+      saved = true;
+    }
+  };
+  for (int32_t j = first; j <= last; ++j) {
+    if (j < static_cast<int32_t>(s.blocks.size())) {
+      const int32_t b = s.blocks[j];
+      if (c->refcount[b] > 1) {  // shared: copy before writing
+        const int32_t nb = take_block(c);
+        if (nb < 0) return false;
+        save();
+        undo.taken.push_back(nb);
+        c->pending_copies.push_back(CopyJob{b, nb});
+        c->pending_updates.push_back(TableUpdate{slot, j, nb, 0});
+        release_block(c, b);
+        s.blocks[j] = nb;
+      }
+    } else {
+      const int32_t nb = take_block(c);
+      if (nb < 0) return false;
+      save();
+      undo.taken.push_back(nb);
+      c->pending_updates.push_back(TableUpdate{slot, j, nb, 0});
+      s.blocks.push_back(nb);
+    }
+  }
+  return true;
+}
+
+void rollback_reserve(slm_ctx* c, Undo& undo) {
+  // Restore block lists (this re-acquires shared blocks released by COW).
+  for (auto it = undo.old_blocks.rbegin(); it != undo.old_blocks.rend(); ++it) {
+    Seq& s = c->seqs[it->first];
+    for (int32_t b : it->second)
+      if (std::find(s.blocks.begin(), s.blocks.end(), b) == s.blocks.end()) ++c->refcount[b];
+    s.blocks = it->second;
+  }
+  for (int32_t b : undo.taken) {
+    c->refcount[b] = 0;
+    c->free_list.push_back(b);
+  }
+  c->pending_updates.resize(undo.updates_mark);
+  c->pending_copies.resize(undo.copies_mark);
+}
+
+// ---- uploads ------------------------------------------------------------------
+
+slm_status upload_alloc(slm_ctx* c, Upload& u, size_t cap) {
+  u.cap = cap;
+  for (int k = 0; k < kUploadSlots; ++k) {
+    CU(c, cudaMallocHost(reinterpret_cast<void**>(&u.h[k]), cap));
+    CU(c, cudaEventCreateWithFlags(&u.ev[k], cudaEventDisableTiming));
+  }
+  CU(c, cudaMalloc(reinterpret_cast<void**>(&u.d), cap));
+  c->device_bytes += static_cast<int64_t>(cap);
+  return SLM_OK;
+}
+void upload_free(Upload& u) {
+  for (int k = 0; k < kUploadSlots; ++k) {
+    if (u.h[k]) cudaFreeHost(u.h[k]);
+    if (u.ev[k]) cudaEventDestroy(u.ev[k]);
+    u.h[k] = nullptr;
+    u.ev[k] = nullptr;
+  }
+  if (u.d) cudaFree(u.d);
+  u.d = nullptr;
+}
+uint8_t* upload_begin(Upload& u) {
+  cudaEventSynchronize(u.ev[u.next]);
+  return u.h[u.next];
+}
+cudaError_t upload_end(Upload& u, size_t bytes, cudaStream_t s) {
+  cudaError_t e = cudaMemcpyAsync(u.d, u.h[u.next], bytes, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaEventRecord(u.ev[u.next], s);
+  u.next = (u.next + 1) % kUploadSlots;
+  return e;
+}
+
+// Layout of one upload: [seqs][items][status][updates][copies].
+struct DescLayout {
+  size_t seqs = 0, items = 0, status = 0, updates = 0, copies = 0, total = 0;
+};
+DescLayout desc_layout(int32_t n, int32_t n_items, size_t nu, size_t nc) {
+  DescLayout L;
+  L.seqs = 0;
+  L.items = align16(L.seqs + sizeof(SeqEntry) * n);
+  L.status = align16(L.items + sizeof(WorkItem) * n_items);
+  L.updates = align16(L.status + sizeof(int32_t) * n);
+  L.copies = align16(L.updates + sizeof(TableUpdate) * nu);
+  L.total = align16(L.copies + sizeof(CopyJob) * nc);
+  return L;
+}
+
+// Sends pending table updates / copies that would not fit into a descriptor
+// upload, through the aux region, and applies them.
+slm_status flush_excess(slm_ctx* c, cudaStream_t s, size_t keep_updates, size_t keep_copies) {
+  while (c->pending_updates.size() > keep_updates || c->pending_copies.size() > keep_copies) {
+    const size_t nu = std::min(c->pending_updates.size(), c->upd_cap);
+    const size_t nc = std::min(c->pending_copies.size(), c->copy_cap);
+    DescLayout L = desc_layout(0, 0, nu, nc);
+    uint8_t* h = upload_begin(c->up_aux);
+    memcpy(h + L.updates, c->pending_updates.data(), nu * sizeof(TableUpdate));
+    memcpy(h + L.copies, c->pending_copies.data(), nc * sizeof(CopyJob));
+    CU(c, upload_end(c->up_aux, L.total, s));
+    CU(c, launch_apply_updates(c->geom(), reinterpret_cast<TableUpdate*>(c->up_aux.d + L.updates),
+                               static_cast<int32_t>(nu),
+                               reinterpret_cast<CopyJob*>(c->up_aux.d + L.copies),
+                               static_cast<int32_t>(nc), s));
+    ++c->launches;
+    c->pending_updates.erase(c->pending_updates.begin(), c->pending_updates.begin() + nu);
+    c->pending_copies.erase(c->pending_copies.begin(), c->pending_copies.begin() + nc);
+  }
+  return SLM_OK;
+}
+
+// Builds split-K work items for sequences with attended lengths `ctx_len`.
+void plan_items(const slm_ctx* c, std::vector<SeqEntry>& entries, std::vector<WorkItem>& items) {
+  const int S = split_blocks(c->cfg.kv_dtype == SLM_KV_BF16);
+  items.clear();
+  for (size_t i = 0; i < entries.size(); ++i) {
+    SeqEntry& e = entries[i];
+    const int32_t nblk = blocks_for(e.ctx_len);
+    e.item_base = static_cast<int32_t>(items.size());
+    e.nsplit = (nblk + S - 1) / S;
+    for (int32_t sp = 0; sp < e.nsplit; ++sp) items.push_back(WorkItem{static_cast<int32_t>(i), sp});
+  }
+}
+
+// Uploads [entries, items, zeroed status, pending updates/copies] into region
+// `u` and applies the updates; returns device pointers into the region.
+slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<SeqEntry>& entries,
+                       const std::vector<WorkItem>& items, SeqEntry** d_seqs, WorkItem** d_items,
+                       int32_t** d_status) {
+  slm_status rc = flush_excess(c, s, c->upd_cap, c->copy_cap);
+  if (rc) return rc;
+  const int32_t n = static_cast<int32_t>(entries.size());
+  const size_t nu = c->pending_updates.size(), nc = c->pending_copies.size();
+  DescLayout L = desc_layout(n, static_cast<int32_t>(items.size()), nu, nc);
+  if (L.total > u.cap)
+    return fail(c, SLM_ERR_INVALID_INPUT, "invalid input for KV cache: step descriptor too large");
+  uint8_t* h = upload_begin(u);
+  memcpy(h + L.seqs, entries.data(), sizeof(SeqEntry) * n);
+  memcpy(h + L.items, items.data(), sizeof(WorkItem) * items.size());
+  memset(h + L.status, 0, sizeof(int32_t) * n);
+  if (nu) memcpy(h + L.updates, c->pending_updates.data(), nu * sizeof(TableUpdate));
+  if (nc) memcpy(h + L.copies, c->pending_copies.data(), nc * sizeof(CopyJob));
+  CU(c, upload_end(u, L.total, s));
+  if (nu || nc) {
+    CU(c, launch_apply_updates(c->geom(), reinterpret_cast<TableUpdate*>(u.d + L.updates),
+                               static_cast<int32_t>(nu), reinterpret_cast<CopyJob*>(u.d + L.copies),
+                               static_cast<int32_t>(nc), s));
+    ++c->launches;
+    c->pending_updates.clear();
+    c->pending_copies.clear();
+  }
+  *d_seqs = reinterpret_cast<SeqEntry*>(u.d + L.seqs);
+  *d_items = reinterpret_cast<WorkItem*>(u.d + L.items);
+  *d_status = reinterpret_cast<int32_t*>(u.d + L.status);
+  return SLM_OK;
+}
+
+// Reads back and clears the context error word (stream must be idle).
+slm_status check_device_error(slm_ctx* c) {
+  int32_t e = 0;
+  CU(c, cudaMemcpy(&e, c->d_error, sizeof e, cudaMemcpyDeviceToHost));
+  if (e) {
+    CU(c, cudaMemset(c->d_error, 0, sizeof(int32_t)));
+    CU(c, cudaMemset(c->d_counters, 0,
+                     sizeof(int32_t) * c->cfg.max_sequences * c->cfg.num_key_value_heads));
+    if (e & kErrTimeout)
+      return fail(c, SLM_ERR_DEVICE_TIMEOUT, "device wait timed out (error word 0x%x)", e);
+    return fail(c, SLM_ERR_INVALID_INPUT,
+                "invalid input for KV cache: block table held an out-of-pool id (0x%x)", e);
+  }
+  return SLM_OK;
+}
+
+void compute_rope_table(const slm_config& cfg, std::vector<float2>& out) {
+  // rope.rs:33-36 inverse frequencies, rope.rs:90-93 angle = pos * inv and
+  // sin_cos, evaluated with the same libm calls the reference lowers to.
+  const int half = cfg.head_dimension / 2;
+  std::vector<float> inv(half);
+  const float denominator = static_cast<float>(cfg.head_dimension);
+  for (int i = 0; i < half; ++i) {
+    const float exponent = -(2.0f * static_cast<float>(i)) / denominator;
+    inv[i] = powf(cfg.rope_theta, exponent);
+  }
+  out.resize(static_cast<size_t>(cfg.context_length) * half);
+  for (int32_t p = 0; p < cfg.context_length; ++p) {
+    const float pos = static_cast<float>(p);
+    for (int i = 0; i < half; ++i) {
+      const float angle = pos * inv[i];
+      out[static_cast<size_t>(p) * half + i] = make_float2(cosf(angle), sinf(angle));
+    }
+  }
+}
+
+void destroy_device(slm_ctx* c) {
+  if (!has_device(c)) return;
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  void* ptrs[] = {c->k_pool, c->v_pool, c->d_block_table, c->d_rope, c->d_part_acc,
+                  c->d_part_ml, c->d_counters, c->d_error};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  if (c->h_readback) cudaFreeHost(c->h_readback);
+  upload_free(c->up_batch);
+  upload_free(c->up_aux);
+}
+
+template <typename T>
+slm_status dev_alloc(slm_ctx* c, T** p, size_t bytes, const char* what) {
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), bytes);
+  if (e != cudaSuccess) return cuda_fail(c, e, what);
+  c->device_bytes += static_cast<int64_t>(bytes);
+  return SLM_OK;
+}
+
+slm_status finish_single(slm_ctx* c, cudaStream_t s, int32_t* d_status, int32_t* status) {
+  CU(c, cudaMemcpyAsync(c->h_readback, d_status, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  CU(c, cudaStreamSynchronize(s));
+  *status = c->h_readback[0];
+  return check_device_error(c);
+}
+
+// Message of the last failed slm_create on this thread (no context exists).
+thread_local std::string g_create_error;
+
+// kv_cache.rs:43-55, rope.rs:21-31 and the config.rs head-divisibility rule,
+// plus the shapes the kernels are built for. Empty string = valid.
+std::string validate_config(const slm_config& k) {
+  if (k.num_layers <= 0 || k.num_key_value_heads <= 0 || k.head_dimension <= 0 ||
+      k.num_query_heads <= 0 || k.context_length <= 0)
+    return "all KV-cache dimensions must be greater than zero";
+  if (k.num_query_heads % k.num_key_value_heads)
+    return "num_query_heads must be divisible by num_key_value_heads";
+  if (k.head_dimension % 2) return "RoPE head_dimension must be positive and even";
+  if (!std::isfinite(k.rope_theta) || k.rope_theta <= 0.0f)
+    return "RoPE theta must be finite and greater than zero";
+  if (k.head_dimension != kHeadDim)
+    return "head_dimension 64 is the only width the kernels are built for";
+  const int32_t G = k.num_query_heads / k.num_key_value_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return "query heads per KV head must be 1, 2, 4 or 8";
+  if (k.num_blocks <= 0 || k.max_sequences <= 0)
+    return "num_blocks and max_sequences must be greater than zero";
+  if (k.kv_dtype != SLM_KV_F32 && k.kv_dtype != SLM_KV_BF16)
+    return "kv_dtype must be SLM_KV_F32 or SLM_KV_BF16";
+  return std::string();
+}
+
+}  // namespace
+
+// =============================================================================
+// C ABI
+// =============================================================================
+extern "C" {
+
+slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
+  if (!out || !config) return SLM_ERR_INVALID_INPUT;
+  *out = nullptr;
+  std::unique_ptr<slm_ctx> c(new (std::nothrow) slm_ctx());
+  if (!c) return SLM_ERR_INVALID_CONFIGURATION;
+  const slm_config& k = *config;
+  c->cfg = k;
+  std::string why = validate_config(k);
+  if (!why.empty()) {
+    g_create_error = "invalid model configuration: " + why;
+    return SLM_ERR_INVALID_CONFIGURATION;
+  }
+  const int32_t G = k.num_query_heads / k.num_key_value_heads;
+  c->group = G;
+  c->max_blocks_per_seq = blocks_for(k.context_length);
+  const int S = split_blocks(k.kv_dtype == SLM_KV_BF16);
+  c->max_items = k.max_sequences * ((c->max_blocks_per_seq + S - 1) / S);
+  c->seqs.resize(k.max_sequences);
+  for (int32_t i = k.max_sequences - 1; i >= 0; --i) c->free_slots.push_back(i);
+  c->refcount.assign(k.num_blocks, 0);
+  c->meta.resize(k.num_blocks);
+  for (int32_t b = k.num_blocks - 1; b >= 0; --b) c->free_list.push_back(b);
+  c->upd_cap = std::max<size_t>(4096, 2 * static_cast<size_t>(k.max_sequences));
+  c->copy_cap = std::max<size_t>(1024, static_cast<size_t>(k.max_sequences));
+  c->device = device;
+
+  if (device >= 0) {
+    slm_ctx* cp = c.get();
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) {
+      g_create_error = std::string("CUDA error in cudaSetDevice: ") + cudaGetErrorString(e);
+      return SLM_ERR_CUDA;
+    }
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    cp->num_sms = sms;
+    const size_t esz = k.kv_dtype == SLM_KV_BF16 ? 2 : 4;
+    const size_t pool_bytes = static_cast<size_t>(k.num_layers) * k.num_blocks *
+                              k.num_key_value_heads * kBlockTokens * k.head_dimension * esz;
+    slm_status rc = SLM_OK;
+    auto step = [&](slm_status r) {
+      if (rc == SLM_OK) rc = r;
+    };
+    step(dev_alloc(cp, &cp->k_pool, pool_bytes, "K pool"));
+    step(dev_alloc(cp, &cp->v_pool, pool_bytes, "V pool"));
+    const size_t bt_bytes = sizeof(int32_t) * k.max_sequences * cp->max_blocks_per_seq;
+    step(dev_alloc(cp, &cp->d_block_table, bt_bytes, "block table"));
+    std::vector<float2> rope;
+    compute_rope_table(k, rope);
+    step(dev_alloc(cp, &cp->d_rope, rope.size() * sizeof(float2), "RoPE table"));
+    const size_t parts = static_cast<size_t>(cp->max_items) * k.num_key_value_heads * G;
+    step(dev_alloc(cp, &cp->d_part_acc, parts * kHeadDim * sizeof(float), "split-K partials"));
+    step(dev_alloc(cp, &cp->d_part_ml, parts * sizeof(float2), "split-K partials"));
+    step(dev_alloc(cp, &cp->d_counters, sizeof(int32_t) * k.max_sequences * k.num_key_value_heads,
+                   "split-K counters"));
+    step(dev_alloc(cp, &cp->d_error, sizeof(int32_t), "error word"));
+    if (rc == SLM_OK) {
+      e = cudaMallocHost(reinterpret_cast<void**>(&cp->h_readback),
+                         sizeof(int32_t) * (k.max_sequences + 1));
+      if (e != cudaSuccess) rc = cuda_fail(cp, e, "cudaMallocHost");
+    }
+    if (rc == SLM_OK) {
+      const size_t batch_cap =
+          desc_layout(k.max_sequences, cp->max_items, cp->upd_cap, cp->copy_cap).total + 256;
+      rc = upload_alloc(cp, cp->up_batch, batch_cap);
+      if (rc == SLM_OK) rc = upload_alloc(cp, cp->up_aux, batch_cap);
+    }
+    if (rc == SLM_OK) {
+      // Unused pool memory is zero: reads of not-yet-written slots are finite.
+      if ((e = cudaMemset(cp->k_pool, 0, pool_bytes)) != cudaSuccess ||
+          (e = cudaMemset(cp->v_pool, 0, pool_bytes)) != cudaSuccess ||
+          (e = cudaMemset(cp->d_block_table, 0, bt_bytes)) != cudaSuccess ||
+          (e = cudaMemset(cp->d_counters, 0,
+                          sizeof(int32_t) * k.max_sequences * k.num_key_value_heads)) !=
+              cudaSuccess ||
+          (e = cudaMemset(cp->d_error, 0, sizeof(int32_t))) != cudaSuccess ||
+          (e = cudaMemcpy(cp->d_rope, rope.data(), rope.size() * sizeof(float2),
+                          cudaMemcpyHostToDevice)) != cudaSuccess ||
+          (e = cudaDeviceSynchronize()) != cudaSuccess)
+        rc = cuda_fail(cp, e, "context initialisation");
+    }
+    if (rc != SLM_OK) {
+      g_create_error = cp->err;
+      destroy_device(cp);
+      return rc;
+    }
+  }
+  g_create_error.clear();
+  *out = c.release();
+  return SLM_OK;
+}
+
+slm_status slm_destroy(slm_ctx* ctx) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  delete ctx->open_batch;
+  destroy_device(ctx);
+  delete ctx;
+  return SLM_OK;
+}
+
+const char* slm_last_error(const slm_ctx* ctx) {
+  return ctx ? ctx->err.c_str() : g_create_error.c_str();
+}
+
+slm_status slm_device_bytes(const slm_ctx* ctx, int64_t* bytes) {
+  if (!ctx || !bytes) return SLM_ERR_INVALID_INPUT;
+  *bytes = ctx->device_bytes;
+  return SLM_OK;
+}
+
+slm_status slm_launch_count(const slm_ctx* ctx, int64_t* launches) {
+  if (!ctx || !launches) return SLM_ERR_INVALID_INPUT;
+  *launches = ctx->launches;
+  return SLM_OK;
+}
+
+// ---- sequences -------------------------------------------------------------
+
+slm_status slm_seq_create(slm_ctx* ctx, int32_t max_sequence_length, int32_t* seq_id) {
+  if (!ctx || !seq_id) return SLM_ERR_INVALID_INPUT;
+  if (max_sequence_length <= 0 || max_sequence_length > ctx->cfg.context_length)
+    return fail(ctx, SLM_ERR_INVALID_CONFIGURATION,
+                "invalid model configuration: KV-cache max_sequence_length must be in 1..=%d",
+                ctx->cfg.context_length);
+  if (ctx->free_slots.empty())
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                       "all %d sequence slots are in use", ctx->cfg.max_sequences);
+  const int32_t id = ctx->free_slots.back();
+  ctx->free_slots.pop_back();
+  Seq& s = ctx->seqs[id];
+  s.live = true;
+  s.max_len = max_sequence_length;
+  s.layer_len.assign(ctx->cfg.num_layers, 0);
+  s.blocks.clear();
+  s.in_batch = false;
+  *seq_id = id;
+  return SLM_OK;
+}
+
+slm_status slm_seq_free(slm_ctx* ctx, int32_t seq_id) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  Seq* s = get_seq(ctx, seq_id);
+  if (!s) return unknown_seq(ctx, seq_id);
+  if (s->in_batch)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                       "sequence %d belongs to an open batch", seq_id);
+  release_tail(ctx, seq_id, 0);
+  s->live = false;
+  s->layer_len.clear();
+  ctx->free_slots.push_back(seq_id);
+  return SLM_OK;
+}
+
+slm_status slm_seq_layer_length(const slm_ctx* ctx, int32_t seq_id, int32_t layer, int32_t* length) {
+  if (!ctx || !length) return SLM_ERR_INVALID_INPUT;
+  slm_ctx* mc = const_cast<slm_ctx*>(ctx);
+  const Seq* s = get_seq(ctx, seq_id);
+  if (!s) return unknown_seq(mc, seq_id);
+  if (layer < 0 || layer >= ctx->cfg.num_layers)
+    return input_error(mc, SLM_ERR_INVALID_INPUT, "KV cache", "layer index %d is outside 0..%d",
+                       layer, ctx->cfg.num_layers);
+  *length = s->layer_len[layer];
+  return SLM_OK;
+}
+
+slm_status slm_seq_length(const slm_ctx* ctx, int32_t seq_id, int32_t* length) {
+  if (!ctx || !length) return SLM_ERR_INVALID_INPUT;
+  const Seq* s = get_seq(ctx, seq_id);
+  if (!s) return unknown_seq(const_cast<slm_ctx*>(ctx), seq_id);
+  *length = seq_min_len(*s);
+  return SLM_OK;
+}
+
+slm_status slm_seq_is_empty(const slm_ctx* ctx, int32_t seq_id, int32_t* is_empty) {
+  if (!ctx || !is_empty) return SLM_ERR_INVALID_INPUT;
+  const Seq* s = get_seq(ctx, seq_id);
+  if (!s) return unknown_seq(const_cast<slm_ctx*>(ctx), seq_id);
+  *is_empty = seq_max_len(*s) == 0;
+  return SLM_OK;
+}
+
+slm_status slm_seq_is_synchronized(const slm_ctx* ctx, int32_t seq_id, int32_t* is_sync) {
+  if (!ctx || !is_sync) return SLM_ERR_INVALID_INPUT;
+  const Seq* s = get_seq(ctx, seq_id);
+  if (!s) return unknown_seq(const_cast<slm_ctx*>(ctx), seq_id);
+  *is_sync = seq_synchronized(*s);
+  return SLM_OK;
+}
+
+slm_status slm_seq_remaining_capacity(const slm_ctx* ctx, int32_t seq_id, int32_t* remaining) {
+  if (!ctx || !remaining) return SLM_ERR_INVALID_INPUT;
+  const Seq* s = get_seq(ctx, seq_id);
+  if (!s) return unknown_seq(const_cast<slm_ctx*>(ctx), seq_id);
+  *remaining = std::max(0, s->max_len - seq_max_len(*s));
+  return SLM_OK;
+}
+
+slm_status slm_seq_truncate_all(slm_ctx* ctx, int32_t seq_id, int32_t length) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  Seq* s = get_seq(ctx, seq_id);
+  if (!s) return unknown_seq(ctx, seq_id);
+  if (s->in_batch)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                       "sequence %d belongs to an open batch", seq_id);
+  for (int32_t l = 0; l < ctx->cfg.num_layers; ++l)
+    if (s->layer_len[l] < length || length < 0)
+      return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                         "cannot restore all layers to %d: layer %d has length %d", length, l,
+                         s->layer_len[l]);
+  for (auto& v : s->layer_len) v = length;
+  release_tail(ctx, seq_id, blocks_for(length));
+  return SLM_OK;
+}
+
+slm_status slm_seqs_truncate_all(slm_ctx* ctx, int32_t n, const int32_t* h_seq_ids,
+                                 const int32_t* h_lengths) {
+  if (!ctx || n < 0 || (n > 0 && (!h_seq_ids || !h_lengths))) return SLM_ERR_INVALID_INPUT;
+  for (int32_t i = 0; i < n; ++i) {
+    slm_status rc = slm_seq_truncate_all(ctx, h_seq_ids[i], h_lengths[i]);
+    if (rc) return rc;
+  }
+  return SLM_OK;
+}
+
+slm_status slm_seq_truncate_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, int32_t length) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  Seq* s = get_seq(ctx, seq_id);
+  if (!s) return unknown_seq(ctx, seq_id);
+  if (s->in_batch)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                       "sequence %d belongs to an open batch", seq_id);
+  if (layer < 0 || layer >= ctx->cfg.num_layers)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache", "layer index %d is outside 0..%d",
+                       layer, ctx->cfg.num_layers);
+  if (length > s->layer_len[layer] || length < 0)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                       "cannot extend layer %d from %d to %d while truncating", layer,
+                       s->layer_len[layer], length);
+  s->layer_len[layer] = length;
+  release_tail(ctx, seq_id, blocks_for(seq_max_len(*s)));
+  return SLM_OK;
+}
+
+slm_status slm_seq_clear(slm_ctx* ctx, int32_t seq_id) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  Seq* s = get_seq(ctx, seq_id);
+  if (!s) return unknown_seq(ctx, seq_id);
+  if (s->in_batch)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                       "sequence %d belongs to an open batch", seq_id);
+  for (auto& v : s->layer_len) v = 0;
+  release_tail(ctx, seq_id, 0);
+  return SLM_OK;
+}
+
+slm_status slm_seq_blocks(const slm_ctx* ctx, int32_t seq_id, int32_t* h_ids, int32_t capacity,
+                          int32_t* n_blocks) {
+  if (!ctx || !n_blocks) return SLM_ERR_INVALID_INPUT;
+  const Seq* s = get_seq(ctx, seq_id);
+  if (!s) return unknown_seq(const_cast<slm_ctx*>(ctx), seq_id);
+  *n_blocks = static_cast<int32_t>(s->blocks.size());
+  for (int32_t i = 0; i < std::min(*n_blocks, capacity); ++i) h_ids[i] = s->blocks[i];
+  return SLM_OK;
+}
+
+// ---- single-sequence operations -----------------------------------------------
+
+slm_status slm_append_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, const float* d_keys,
+                            const float* d_values, int32_t token_count, int32_t rotate_keys,
+                            slm_stream stream) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  slm_status rc = need_device(ctx);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Seq* q = get_seq(ctx, seq_id);
+  if (!q) return unknown_seq(ctx, seq_id);
+  if (q->in_batch)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                       "sequence %d belongs to an open batch", seq_id);
+  if (token_count <= 0 || !d_keys || !d_values)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV-cache keys",
+                       "matrix dimensions must be greater than zero");
+  if (layer < 0 || layer >= ctx->cfg.num_layers)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache", "layer index %d is outside 0..%d",
+                       layer, ctx->cfg.num_layers);
+  const int32_t cur = q->layer_len[layer];
+  const int64_t new_len = static_cast<int64_t>(cur) + token_count;
+  if (new_len > q->max_len)
+    return input_error(ctx, SLM_ERR_CAPACITY, "KV cache",
+                       "layer %d would grow to %lld tokens, exceeding capacity %d", layer,
+                       static_cast<long long>(new_len), q->max_len);
+  Undo undo;
+  undo.updates_mark = ctx->pending_updates.size();
+  undo.copies_mark = ctx->pending_copies.size();
+  if (!reserve_positions(ctx, seq_id, cur, static_cast<int32_t>(new_len), undo)) {
+    rollback_reserve(ctx, undo);
+    return input_error(ctx, SLM_ERR_POOL_EXHAUSTED, "KV cache", "no free block in the pool");
+  }
+  std::vector<SeqEntry> e(1);
+  e[0] = SeqEntry{seq_id, cur, token_count, 0, 0, 0, static_cast<int32_t>(new_len), 0};
+  std::vector<WorkItem> items;
+  SeqEntry* d_seqs;
+  WorkItem* d_items;
+  int32_t* d_status;
+  rc = upload_step(ctx, ctx->up_aux, s, e, items, &d_seqs, &d_items, &d_status);
+  if (rc) {
+    rollback_reserve(ctx, undo);
+    return rc;
+  }
+  AppendLaunch a{};
+  a.g = ctx->geom();
+  a.layer = layer;
+  a.seqs = d_seqs;
+  a.n_seq = 1;
+  a.total_tokens = token_count;
+  a.k_in = d_keys;
+  a.v_in = d_values;
+  a.rotate = rotate_keys != 0;
+  a.status = d_status;
+  CU(ctx, launch_append(a, s));
+  ++ctx->launches;
+  int32_t status = 0;
+  rc = finish_single(ctx, s, d_status, &status);
+  if (rc) return rc;
+  if (status & kStatusNonFinite) {
+    // Nothing became visible: the length was never advanced. Blocks taken for
+    // the new positions go back to the pool.
+    release_tail(ctx, seq_id, blocks_for(seq_max_len(*q)));
+    return input_error(ctx, SLM_ERR_NON_FINITE, "KV cache",
+                       "all appended key/value values must be finite");
+  }
+  q->layer_len[layer] = static_cast<int32_t>(new_len);
+  return SLM_OK;
+}
+
+slm_status slm_gather_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, float* d_keys,
+                            float* d_values, slm_stream stream) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  slm_status rc = need_device(ctx);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Seq* q = get_seq(ctx, seq_id);
+  if (!q) return unknown_seq(ctx, seq_id);
+  if (layer < 0 || layer >= ctx->cfg.num_layers)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache", "layer index %d is outside 0..%d",
+                       layer, ctx->cfg.num_layers);
+  rc = flush_excess(ctx, s, 0, 0);
+  if (rc) return rc;
+  GatherLaunch gl{};
+  gl.g = ctx->geom();
+  gl.layer = layer;
+  gl.slot = seq_id;
+  gl.length = q->layer_len[layer];
+  gl.k_out = d_keys;
+  gl.v_out = d_values;
+  CU(ctx, launch_gather(gl, s));
+  ++ctx->launches;
+  return SLM_OK;
+}
+
+slm_status slm_attend_cached_query(slm_ctx* ctx, int32_t seq_id, int32_t layer,
+                                   const float* d_query, float* d_out, slm_stream stream) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  slm_status rc = need_device(ctx);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Seq* q = get_seq(ctx, seq_id);
+  if (!q) return unknown_seq(ctx, seq_id);
+  if (layer < 0 || layer >= ctx->cfg.num_layers)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache", "layer index %d is outside 0..%d",
+                       layer, ctx->cfg.num_layers);
+  const int32_t L = q->layer_len[layer];
+  if (L == 0)  // attention.rs:690-695
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention",
+                       "at least one cached key/value position is required");
+  std::vector<SeqEntry> e(1);
+  e[0] = SeqEntry{seq_id, L - 1, 1, 0, 0, 0, L, 0};
+  std::vector<WorkItem> items;
+  plan_items(ctx, e, items);
+  SeqEntry* d_seqs;
+  WorkItem* d_items;
+  int32_t* d_status;
+  rc = upload_step(ctx, ctx->up_aux, s, e, items, &d_seqs, &d_items, &d_status);
+  if (rc) return rc;
+  DecodeLaunch p{};
+  p.g = ctx->geom();
+  p.layer = layer;
+  p.seqs = d_seqs;
+  p.items = d_items;
+  p.n_seq = 1;
+  p.n_items = static_cast<int32_t>(items.size());
+  p.q = d_query;
+  p.out = d_out;
+  p.part_acc = ctx->d_part_acc;
+  p.part_ml = ctx->d_part_ml;
+  p.counters = ctx->d_counters;
+  p.status = d_status;
+  p.fused = 0;
+  CU(ctx, launch_decode(p, ctx->num_sms, s));
+  ++ctx->launches;
+  return SLM_OK;
+}
+
+// ---- batches ------------------------------------------------------------------
+
+slm_status slm_batch_begin(slm_ctx* ctx, int32_t n, const int32_t* h_seq_ids,
+                           const int32_t* h_token_counts, slm_stream stream, slm_batch** out) {
+  if (!ctx || !out) return SLM_ERR_INVALID_INPUT;
+  *out = nullptr;
+  slm_status rc = need_device(ctx);
+  if (rc) return rc;
+  if (ctx->open_batch)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "a batch is already open");
+  if (n <= 0 || n > ctx->cfg.max_sequences || !h_seq_ids || !h_token_counts)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "batch size %d is outside 1..=%d", n,
+                       ctx->cfg.max_sequences);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Validate everything before mutating anything.
+  auto unmark = [&](int32_t upto) {
+    for (int32_t i = 0; i < upto; ++i) ctx->seqs[h_seq_ids[i]].in_batch = false;
+  };
+  for (int32_t i = 0; i < n; ++i) {
+    const int32_t id = h_seq_ids[i];
+    Seq* q = get_seq(ctx, id);
+    if (!q) {
+      unmark(i);
+      return unknown_seq(ctx, id);
+    }
+    if (q->in_batch) {
+      unmark(i);
+      return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
+                         "sequence %d is already in a batch or appears twice", id);
+    }
+    q->in_batch = true;  // duplicate detection; undone below on every failure
+  }
+  auto clear_marks = [&] { unmark(n); };
+  for (int32_t i = 0; i < n; ++i) {
+    const Seq& q = ctx->seqs[h_seq_ids[i]];
+    if (h_token_counts[i] <= 0) {
+      clear_marks();
+      return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
+                         "sequence %d: token count must be greater than zero", h_seq_ids[i]);
+    }
+    if (!seq_synchronized(q)) {  // model.rs:345-350
+      clear_marks();
+      return input_error(ctx, SLM_ERR_INVALID_INPUT, "model cached decode",
+                         "all cache layers must have the same length before decoding");
+    }
+    const int64_t nl = static_cast<int64_t>(q.layer_len[0]) + h_token_counts[i];
+    if (nl > q.max_len) {  // kv_cache.rs:203-211
+      clear_marks();
+      return input_error(ctx, SLM_ERR_CAPACITY, "KV cache",
+                         "sequence %d would grow to %lld tokens, exceeding capacity %d",
+                         h_seq_ids[i], static_cast<long long>(nl), q.max_len);
+    }
+  }
+  Undo undo;
+  undo.updates_mark = ctx->pending_updates.size();
+  undo.copies_mark = ctx->pending_copies.size();
+  std::unique_ptr<slm_batch> b(new slm_batch());
+  b->ctx = ctx;
+  b->stream = s;
+  b->seq_ids.assign(h_seq_ids, h_seq_ids + n);
+  b->counts.assign(h_token_counts, h_token_counts + n);
+  b->base.resize(n);
+  std::vector<SeqEntry> entries(n);
+  int32_t row = 0;
+  for (int32_t i = 0; i < n; ++i) {
+    const int32_t id = h_seq_ids[i];
+    const int32_t base = ctx->seqs[id].layer_len[0];
+    if (!reserve_positions(ctx, id, base, base + h_token_counts[i], undo)) {
+      rollback_reserve(ctx, undo);
+      clear_marks();
+      return input_error(ctx, SLM_ERR_POOL_EXHAUSTED, "KV cache", "no free block in the pool");
+    }
+    b->base[i] = base;
+    entries[i] = SeqEntry{id, base, h_token_counts[i], row, 0, 0, base + h_token_counts[i], 0};
+    row += h_token_counts[i];
+    b->max_count = std::max(b->max_count, h_token_counts[i]);
+  }
+  b->total_tokens = row;
+  std::vector<WorkItem> items;
+  plan_items(ctx, entries, items);
+  b->n_items = static_cast<int32_t>(items.size());
+  rc = upload_step(ctx, ctx->up_batch, s, entries, items, &b->d_seqs, &b->d_items, &b->d_status);
+  if (rc) {
+    rollback_reserve(ctx, undo);
+    clear_marks();
+    return rc;
+  }
+  b->layer_done.assign(ctx->cfg.num_layers, 0);
+  ctx->open_batch = b.get();
+  *out = b.release();
+  return SLM_OK;
+}
+
+namespace {
+slm_status batch_layer_check(slm_batch* b, int32_t layer) {
+  slm_ctx* ctx = b->ctx;
+  if (ctx->open_batch != b)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "the batch is not open");
+  if (layer < 0 || layer >= ctx->cfg.num_layers)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache", "layer index %d is outside 0..%d",
+                       layer, ctx->cfg.num_layers);
+  return need_device(ctx);
+}
+}  // namespace
+
+slm_status slm_batch_decode_layer(slm_batch* b, int32_t layer, const float* d_query,
+                                  const float* d_keys, const float* d_values, float* d_out) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_ctx* ctx = b->ctx;
+  slm_status rc = batch_layer_check(b, layer);
+  if (rc) return rc;
+  if (b->max_count != 1)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
+                       "decode layers need exactly one new token per sequence");
+  if (b->layer_done[layer])
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "layer %d was already appended", layer);
+  if (!d_query || !d_keys || !d_values || !d_out)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "null tensor");
+  DecodeLaunch p{};
+  p.g = ctx->geom();
+  p.layer = layer;
+  p.seqs = b->d_seqs;
+  p.items = b->d_items;
+  p.n_seq = static_cast<int32_t>(b->seq_ids.size());
+  p.n_items = b->n_items;
+  p.q = d_query;
+  p.k_new = d_keys;
+  p.v_new = d_values;
+  p.out = d_out;
+  p.part_acc = ctx->d_part_acc;
+  p.part_ml = ctx->d_part_ml;
+  p.counters = ctx->d_counters;
+  p.status = b->d_status;
+  p.fused = 1;
+  CU(ctx, launch_decode(p, ctx->num_sms, b->stream));
+  ++ctx->launches;
+  b->layer_done[layer] = 1;
+  for (size_t i = 0; i < b->seq_ids.size(); ++i)
+    ctx->seqs[b->seq_ids[i]].layer_len[layer] = b->base[i] + b->counts[i];
+  return SLM_OK;
+}
+
+slm_status slm_batch_append_layer(slm_batch* b, int32_t layer, const float* d_keys,
+                                  const float* d_values, int32_t rotate_keys) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_ctx* ctx = b->ctx;
+  slm_status rc = batch_layer_check(b, layer);
+  if (rc) return rc;
+  if (b->layer_done[layer])
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "layer %d was already appended", layer);
+  if (!d_keys || !d_values) return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "null tensor");
+  AppendLaunch a{};
+  a.g = ctx->geom();
+  a.layer = layer;
+  a.seqs = b->d_seqs;
+  a.n_seq = static_cast<int32_t>(b->seq_ids.size());
+  a.total_tokens = b->total_tokens;
+  a.k_in = d_keys;
+  a.v_in = d_values;
+  a.rotate = rotate_keys != 0;
+  a.status = b->d_status;
+  CU(ctx, launch_append(a, b->stream));
+  ++ctx->launches;
+  b->layer_done[layer] = 1;
+  for (size_t i = 0; i < b->seq_ids.size(); ++i)
+    ctx->seqs[b->seq_ids[i]].layer_len[layer] = b->base[i] + b->counts[i];
+  return SLM_OK;
+}
+
+slm_status slm_batch_prefill_attention(slm_batch* b, int32_t layer, const float* d_query,
+                                       int32_t rotate_query, float* d_out) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_ctx* ctx = b->ctx;
+  slm_status rc = batch_layer_check(b, layer);
+  if (rc) return rc;
+  if (!b->layer_done[layer])
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention prefill",
+                       "layer %d must be appended before its attention", layer);
+  if (ctx->group > 4)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention prefill",
+                       "more than 4 query heads per KV head are not supported in prefill");
+  if (!d_query || !d_out) return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "null tensor");
+  PrefillLaunch p{};
+  p.g = ctx->geom();
+  p.layer = layer;
+  p.seqs = b->d_seqs;
+  p.n_seq = static_cast<int32_t>(b->seq_ids.size());
+  p.total_tokens = b->total_tokens;
+  p.q = d_query;
+  p.rotate = rotate_query != 0;
+  p.out = d_out;
+  p.max_count = b->max_count;
+  CU(ctx, launch_prefill(p, b->stream));
+  ++ctx->launches;
+  return SLM_OK;
+}
+
+namespace {
+void batch_restore(slm_batch* b, const std::vector<char>& roll) {
+  slm_ctx* ctx = b->ctx;
+  for (size_t i = 0; i < b->seq_ids.size(); ++i) {
+    Seq& q = ctx->seqs[b->seq_ids[i]];
+    q.in_batch = false;
+    if (roll[i]) {
+      for (auto& v : q.layer_len) v = b->base[i];
+      release_tail(ctx, b->seq_ids[i], blocks_for(b->base[i]));
+    }
+  }
+  ctx->open_batch = nullptr;
+  delete b;
+}
+}  // namespace
+
+slm_status slm_batch_end(slm_batch* b, int32_t* h_status) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_ctx* ctx = b->ctx;
+  if (ctx->open_batch != b)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "the batch is not open");
+  const size_t n = b->seq_ids.size();
+  std::vector<char> roll(n, 0);
+  slm_status first = SLM_OK;
+  cudaError_t e =
+      cudaMemcpyAsync(ctx->h_readback, b->d_status, sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
+                      b->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+  if (e != cudaSuccess) {
+    std::fill(roll.begin(), roll.end(), 1);
+    batch_restore(b, roll);
+    return cuda_fail(ctx, e, "slm_batch_end");
+  }
+  slm_status dev = check_device_error(ctx);
+  for (size_t i = 0; i < n; ++i) {
+    const Seq& q = ctx->seqs[b->seq_ids[i]];
+    const int32_t want = b->base[i] + b->counts[i];
+    bool complete = true;
+    for (int32_t v : q.layer_len) complete = complete && (v == want);
+    const int32_t st = ctx->h_readback[i];
+    int32_t code = SLM_OK;
+    if (dev != SLM_OK) code = dev;
+    else if (st & kStatusNonFinite) code = SLM_ERR_NON_FINITE;
+    else if (!complete) code = SLM_ERR_INVALID_INPUT;
+    if (h_status) h_status[i] = code;
+    if (code != SLM_OK) {
+      roll[i] = 1;
+      if (first == SLM_OK) first = code;
+    }
+  }
+  if (first == SLM_ERR_NON_FINITE)
+    input_error(ctx, first, "KV cache", "all appended key/value values must be finite");
+  else if (first == SLM_ERR_INVALID_INPUT && dev == SLM_OK)
+    input_error(ctx, first, "model cached decode",
+                "all cache layers must advance by exactly one step");
+  batch_restore(b, roll);
+  return first;
+}
+
+slm_status slm_batch_rollback(slm_batch* b) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  if (b->ctx->open_batch != b)
+    return input_error(b->ctx, SLM_ERR_INVALID_INPUT, "batch", "the batch is not open");
+  std::vector<char> roll(b->seq_ids.size(), 1);
+  batch_restore(b, roll);
+  return SLM_OK;
+}
+
+// ---- prefix cache -----------------------------------------------------------
+
+namespace {
+uint64_t chain_key(uint64_t parent_key, const uint32_t* toks) {
+  uint64_t h = mix64(parent_key ^ 0x51ed27a3c6b9f1d5ull);
+  for (int i = 0; i < kBlockTokens; ++i) h = mix64(h ^ toks[i]);
+  return h;
+}
+int32_t find_indexed(const slm_ctx* c, uint64_t key, int32_t parent, const uint32_t* toks) {
+  auto range = c->index.equal_range(key);
+  for (auto it = range.first; it != range.second; ++it) {
+    const BlockMeta& m = c->meta[it->second];
+    if (m.parent == parent && std::equal(m.tokens.begin(), m.tokens.end(), toks))
+      return it->second;
+  }
+  return -1;
+}
+}  // namespace
+
+slm_status slm_prefix_attach(slm_ctx* ctx, int32_t seq_id, const uint32_t* h_tokens,
+                             int32_t n_tokens, int32_t* reused_tokens) {
+  if (!ctx || !reused_tokens) return SLM_ERR_INVALID_INPUT;
+  *reused_tokens = 0;
+  Seq* q = get_seq(ctx, seq_id);
+  if (!q) return unknown_seq(ctx, seq_id);
+  if (q->in_batch || seq_max_len(*q) != 0 || !q->blocks.empty())
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "prefix cache",
+                       "a prefix can only be attached to an empty sequence");
+  if (n_tokens < 0 || (n_tokens > 0 && !h_tokens))
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "prefix cache", "invalid token span");
+  const int32_t limit = std::min(n_tokens, q->max_len) / kBlockTokens;
+  uint64_t key = 0;
+  int32_t parent = -1;
+  std::vector<int32_t> chain;
+  for (int32_t j = 0; j < limit; ++j) {
+    const uint32_t* toks = h_tokens + static_cast<size_t>(j) * kBlockTokens;
+    key = chain_key(key, toks);
+    const int32_t b = find_indexed(ctx, key, parent, toks);
+    if (b < 0) break;
+    chain.push_back(b);
+    parent = b;
+  }
+  ++ctx->clock;
+  for (size_t j = 0; j < chain.size(); ++j) {
+    const int32_t b = chain[j];
+    ++ctx->refcount[b];
+    ctx->meta[b].stamp = ctx->clock;
+    q->blocks.push_back(b);
+    ctx->pending_updates.push_back(TableUpdate{seq_id, static_cast<int32_t>(j), b, 0});
+  }
+  const int32_t reused = static_cast<int32_t>(chain.size()) * kBlockTokens;
+  for (auto& v : q->layer_len) v = reused;
+  *reused_tokens = reused;
+  return SLM_OK;
+}
+
+slm_status slm_prefix_publish(slm_ctx* ctx, int32_t seq_id, const uint32_t* h_tokens,
+                              int32_t n_tokens, int32_t* indexed_blocks) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  Seq* q = get_seq(ctx, seq_id);
+  if (!q) return unknown_seq(ctx, seq_id);
+  if (!seq_synchronized(*q))
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "prefix cache",
+                       "all cache layers must have the same length before publishing");
+  if (n_tokens < 0 || n_tokens > seq_min_len(*q) || (n_tokens > 0 && !h_tokens))
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "prefix cache",
+                       "%d tokens exceed the sequence length %d", n_tokens, seq_min_len(*q));
+  const int32_t full = n_tokens / kBlockTokens;
+  uint64_t key = 0;
+  int32_t parent = -1;
+  int32_t count = 0;
+  ++ctx->clock;
+  for (int32_t j = 0; j < full; ++j) {
+    const uint32_t* toks = h_tokens + static_cast<size_t>(j) * kBlockTokens;
+    key = chain_key(key, toks);
+    int32_t b = find_indexed(ctx, key, parent, toks);
+    if (b < 0) {
+      b = q->blocks[j];
+      BlockMeta& m = ctx->meta[b];
+      if (m.indexed) break;  // this block already stands for another chain
+      m.indexed = true;
+      m.parent = parent;
+      m.key = key;
+      std::copy(toks, toks + kBlockTokens, m.tokens.begin());
+      ctx->index.emplace(key, b);
+      ++ctx->refcount[b];
+      ++ctx->indexed_blocks;
+    }
+    ctx->meta[b].stamp = ctx->clock;
+    parent = b;
+    ++count;
+  }
+  if (indexed_blocks) *indexed_blocks = count;
+  return SLM_OK;
+}
+
+slm_status slm_pool_stats(const slm_ctx* ctx, int32_t* free_blocks, int32_t* indexed_blocks) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  if (free_blocks) *free_blocks = static_cast<int32_t>(ctx->free_list.size());
+  if (indexed_blocks) *indexed_blocks = ctx->indexed_blocks;
+  return SLM_OK;
+}
+
+slm_status slm_pool_shuffle(slm_ctx* ctx, uint64_t seed) {
+  if (!ctx) return SLM_ERR_INVALID_INPUT;
+  if (static_cast<int32_t>(ctx->free_list.size()) != ctx->cfg.num_blocks)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                       "the pool can only be shuffled while no block is in use");
+  std::mt19937_64 rng(seed);
+  std::shuffle(ctx->free_list.begin(), ctx->free_list.end(), rng);
+  return SLM_OK;
+}
+
+}  // extern "C"

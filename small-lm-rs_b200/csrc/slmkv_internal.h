@@ -1,0 +1,122 @@
+// Definitions shared by the host engine (slmkv_host.cpp) and the kernels
+// (slmkv_kernels.cu). Plain structs only: they are copied to the device as
+// kernel parameters or as the uploaded step descriptor.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace slmkv {
+
+constexpr int kBlockTokens = 16;  // tokens per physical block
+constexpr int kHeadDim = 64;      // the head width the kernels are built for
+
+// Per-sequence entry of an uploaded step descriptor.
+struct SeqEntry {
+  int32_t slot;        // block-table row
+  int32_t base;        // position of the first new token (pre-append length)
+  int32_t count;       // new tokens this step
+  int32_t row_offset;  // first row of this sequence in the batch's token rows
+  int32_t item_base;   // first split-K work item of this sequence
+  int32_t nsplit;      // split-K work items of this sequence
+  int32_t ctx_len;     // tokens attended by the last new token (base + count)
+  int32_t pad;
+};
+
+// One split-K decode work item: a range of blocks of one sequence.
+struct WorkItem {
+  int32_t seq;    // index into the step's SeqEntry array
+  int32_t split;  // 0..nsplit-1
+};
+
+// Block-table write or copy-on-write job, applied before a step's kernels.
+struct TableUpdate {
+  int32_t slot, index, block, pad;
+};
+struct CopyJob {
+  int32_t src, dst;
+};
+
+// Device status words (per batch sequence, and one per context).
+enum : int32_t { kStatusNonFinite = 1 };
+enum : int32_t { kErrTimeout = 1, kErrBadBlock = 2 };
+
+struct PoolGeom {
+  void* k;                   // pool base (layer 0)
+  void* v;
+  int64_t layer_elems;       // elements per layer per pool
+  int32_t* block_table;      // [max_sequences][max_blocks_per_seq]
+  int32_t max_blocks_per_seq;
+  int32_t num_blocks;
+  int32_t num_layers;
+  int32_t kv_heads;
+  int32_t q_heads;
+  int32_t bf16;              // element type of the pools
+  const float2* rope;        // [context_length][head_dim/2] (cos, sin)
+  int32_t context_length;
+  int32_t* error;            // context error word (kErr* bits)
+};
+
+// Split-K granularity: blocks per decode work item (32 KiB of K+V staging).
+inline int split_blocks(int bf16) { return bf16 ? 8 : 4; }
+
+// ---- kernel launchers (slmkv_kernels.cu) ----------------------------------
+struct DecodeLaunch {
+  PoolGeom g;
+  int32_t layer;
+  const SeqEntry* seqs;
+  const WorkItem* items;
+  int32_t n_seq;
+  int32_t n_items;
+  const float* q;      // [n, Hq, d]
+  const float* k_new;  // [n, Hkv, d] (fused mode) or null
+  const float* v_new;
+  float* out;          // [n, Hq, d]
+  float* part_acc;     // [n_items][Hkv][G][d]
+  float2* part_ml;     // [n_items][Hkv][G]
+  int32_t* counters;   // [n_seq][Hkv], zero between launches
+  int32_t* status;     // [n_seq]
+  int32_t fused;       // 1: rope(q,k) + append + attend; 0: attend (q rotated)
+};
+cudaError_t launch_decode(const DecodeLaunch& p, int num_sms, cudaStream_t s);
+
+struct AppendLaunch {
+  PoolGeom g;
+  int32_t layer;
+  const SeqEntry* seqs;
+  int32_t n_seq;
+  int32_t total_tokens;
+  const float* k_in;   // [total_tokens, Hkv, d]
+  const float* v_in;
+  int32_t rotate;
+  int32_t* status;     // [n_seq]
+};
+cudaError_t launch_append(const AppendLaunch& p, cudaStream_t s);
+
+struct GatherLaunch {
+  PoolGeom g;
+  int32_t layer;
+  int32_t slot;
+  int32_t length;
+  float* k_out;  // [length, Hkv, d] or null
+  float* v_out;
+};
+cudaError_t launch_gather(const GatherLaunch& p, cudaStream_t s);
+
+struct PrefillLaunch {
+  PoolGeom g;
+  int32_t layer;
+  const SeqEntry* seqs;
+  int32_t n_seq;
+  int32_t total_tokens;
+  const float* q;  // [total_tokens, Hq, d]
+  int32_t rotate;
+  float* out;
+  int32_t max_count;  // largest per-sequence token count
+};
+cudaError_t launch_prefill(const PrefillLaunch& p, cudaStream_t s);
+
+cudaError_t launch_apply_updates(const PoolGeom& g, const TableUpdate* updates, int32_t n_updates,
+                                 const CopyJob* copies, int32_t n_copies, cudaStream_t s);
+
+}  // namespace slmkv

@@ -1,0 +1,752 @@
+// sm_100a kernels of the KV-cache hot path.
+//
+//   append_kernel    KvCache::append_layer (kv_cache.rs:182-230) with the K
+//                    half of RoPE (rope.rs:82-100) fused into the store.
+//   decode_kernel    GroupedQueryAttention::forward_cached_token's cache part
+//                    (attention.rs:794-810): RoPE(Q, K) at the pre-append
+//                    position, the paged append, and attend_cached_query
+//                    (attention.rs:677-759) as split-K online softmax.
+//   prefill_kernel   causal attention of a step's new tokens over the cache
+//                    (attention.rs:195-399 when the cache starts empty).
+//   gather_kernel    KvCache::layer_keys/layer_values (kv_cache.rs:237-248).
+//   apply_updates    block-table writes and copy-on-write block copies.
+//
+// Paged pool layout: [layer][block][kv_head][slot 0..15][d=64], f32 or bf16.
+// One (layer, block, kv_head) chunk is 4 KiB (f32) / 2 KiB (bf16) and
+// contiguous, so a decode CTA stages it with one cp.async.bulk per chunk.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "slmkv_internal.h"
+
+namespace slmkv {
+namespace {
+
+constexpr int D = kHeadDim;
+constexpr unsigned kFull = 0xffffffffu;
+// 1/sqrt(64) * log2(e): scores are kept in the exp2 domain.
+constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // bounded waits: 1 s
+
+// ---------------------------------------------------------------------------
+// PTX helpers: mbarrier + bulk async copy (the TMA engine, non-tensor form).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// Global -> shared bulk copy completing on `bar`; 16-byte aligned addresses,
+// size a multiple of 16 (every chunk here is 2 or 4 KiB at chunk offsets).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Waits for phase `parity` of `bar` for at most ~1 s (and a fixed iteration
+// cap); returns false when the limit ran out.
+__device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31u) == 0 && globaltimer_ns() - start > kWaitLimitNs) break;
+  }
+  return false;
+}
+
+// ---------------------------------------------------------------------------
+// Numerics shared with the reference.
+// ---------------------------------------------------------------------------
+// rope.rs:94-97 — separately rounded products, no FMA contraction.
+__device__ __forceinline__ float2 rope_pair(float2 x, float2 cs) {
+  const float a = __fmul_rn(x.x, cs.x), b = __fmul_rn(x.y, cs.y);
+  const float e = __fmul_rn(x.x, cs.y), f = __fmul_rn(x.y, cs.x);
+  return make_float2(__fsub_rn(a, b), __fadd_rn(e, f));
+}
+// linear.rs:14-23 round-to-nearest-even, returning the 16 kept bits.
+__device__ __forceinline__ uint32_t bf16_bits(float x) {
+  const uint32_t b = __float_as_uint(x);
+  if (!isfinite(x)) return (b >> 16) | ((x != x) ? 0x0040u : 0u);  // keep NaN a NaN
+  return (b + 0x7fffu + ((b >> 16) & 1u)) >> 16;
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return bf16_bits(lo) | (bf16_bits(hi) << 16);
+}
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ bool finite2(float2 v) { return isfinite(v.x) && isfinite(v.y); }
+__device__ __forceinline__ bool finite4(float4 v) {
+  return isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+}
+
+// Q rows live in shared memory as 16 four-float units per head; unit u is
+// stored at u ^ ((u >> 3) & 1) so that the rotated unit reads of both the
+// f32 and the bf16 score loops are free of bank conflicts.
+__device__ __forceinline__ int qunit(int u) { return u ^ ((u >> 3) & 1); }
+
+__device__ __forceinline__ int32_t checked_block(const PoolGeom& g, int32_t blk) {
+  if (static_cast<uint32_t>(blk) >= static_cast<uint32_t>(g.num_blocks)) {
+    atomicOr(g.error, kErrBadBlock);
+    return 0;
+  }
+  return blk;
+}
+
+// ---------------------------------------------------------------------------
+// Score of one 16-token block against G query heads, per lane.
+// Lane l handles token t = l & 15 and dims [32*(l>>4), +32); the two halves
+// are combined with one shuffle. K is read in a rotated chunk order so that
+// the 8 lanes of each quarter-warp hit 8 distinct bank groups.
+// ---------------------------------------------------------------------------
+template <int G>
+__device__ __forceinline__ void block_scores_f32(const float* __restrict__ kb,
+                                                 const float* __restrict__ qs, int lane,
+                                                 float (&sc)[G]) {
+  const int t = lane & 15, hh = lane >> 4;
+  const float* krow = kb + t * D + hh * 32;
+#pragma unroll
+  for (int g = 0; g < G; ++g) sc[g] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = (j + t) & 7;
+    const float4 k4 = *reinterpret_cast<const float4*>(krow + 4 * c);
+    const int pu = qunit(hh * 8 + c);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float4 q4 = *reinterpret_cast<const float4*>(qs + g * D + pu * 4);
+      sc[g] = fmaf(q4.x, k4.x, sc[g]);
+      sc[g] = fmaf(q4.y, k4.y, sc[g]);
+      sc[g] = fmaf(q4.z, k4.z, sc[g]);
+      sc[g] = fmaf(q4.w, k4.w, sc[g]);
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(kFull, sc[g], 16);
+}
+
+template <int G>
+__device__ __forceinline__ void block_scores_bf16(const uint16_t* __restrict__ kb,
+                                                  const float* __restrict__ qs, int lane,
+                                                  float (&sc)[G]) {
+  const int t = lane & 15, hh = lane >> 4;
+  const uint16_t* krow = kb + t * D;
+#pragma unroll
+  for (int g = 0; g < G; ++g) sc[g] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = (2 * j + hh + t) & 7;  // chunk of 8 dims
+    const uint4 raw = *reinterpret_cast<const uint4*>(krow + 8 * c);
+    const float k0 = bf16lo(raw.x), k1 = bf16hi(raw.x), k2 = bf16lo(raw.y), k3 = bf16hi(raw.y);
+    const float k4 = bf16lo(raw.z), k5 = bf16hi(raw.z), k6 = bf16lo(raw.w), k7 = bf16hi(raw.w);
+    const int p0 = qunit(2 * c), p1 = qunit(2 * c + 1);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float4 qa = *reinterpret_cast<const float4*>(qs + g * D + p0 * 4);
+      const float4 qb = *reinterpret_cast<const float4*>(qs + g * D + p1 * 4);
+      sc[g] = fmaf(qa.x, k0, sc[g]);
+      sc[g] = fmaf(qa.y, k1, sc[g]);
+      sc[g] = fmaf(qa.z, k2, sc[g]);
+      sc[g] = fmaf(qa.w, k3, sc[g]);
+      sc[g] = fmaf(qb.x, k4, sc[g]);
+      sc[g] = fmaf(qb.y, k5, sc[g]);
+      sc[g] = fmaf(qb.z, k6, sc[g]);
+      sc[g] = fmaf(qb.w, k7, sc[g]);
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(kFull, sc[g], 16);
+}
+
+// Online-softmax update for one block, then P·V (lane owns dims 2l, 2l+1).
+// sc: raw dot products for token lane&15; nvalid >= 1 tokens are real.
+template <int G, bool BF16V>
+__device__ __forceinline__ void block_softmax_pv(const void* __restrict__ vb, int lane, int nvalid,
+                                                 const float (&sc)[G], float (&m)[G],
+                                                 float (&l)[G], float2 (&acc)[G]) {
+  const int t = lane & 15;
+  float pr[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float s = (t < nvalid) ? sc[g] * kScaleLog2 : -INFINITY;
+    float mb = s;
+    mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 8));
+    mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 4));
+    mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 2));
+    mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 1));
+    const float mnew = fmaxf(m[g], mb);  // finite: nvalid >= 1
+    const float corr = exp2f(m[g] - mnew);
+    const float p = exp2f(s - mnew);
+    float ps = p;
+    ps += __shfl_xor_sync(kFull, ps, 8);
+    ps += __shfl_xor_sync(kFull, ps, 4);
+    ps += __shfl_xor_sync(kFull, ps, 2);
+    ps += __shfl_xor_sync(kFull, ps, 1);
+    l[g] = fmaf(l[g], corr, ps);
+    acc[g].x *= corr;
+    acc[g].y *= corr;
+    m[g] = mnew;
+    pr[g] = p;
+  }
+  for (int tt = 0; tt < nvalid; ++tt) {
+    float2 v2;
+    if constexpr (BF16V) {
+      const uint32_t w = reinterpret_cast<const uint32_t*>(vb)[tt * (D / 2) + lane];
+      v2 = make_float2(bf16lo(w), bf16hi(w));
+    } else {
+      v2 = reinterpret_cast<const float2*>(vb)[tt * (D / 2) + lane];
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float pt = __shfl_sync(kFull, pr[g], tt);
+      acc[g].x = fmaf(pt, v2.x, acc[g].x);
+      acc[g].y = fmaf(pt, v2.y, acc[g].y);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Decode: one CTA per (work item, kv head). Work item = up to S blocks of one
+// sequence. All K/V chunks of the item are staged up front by one thread
+// (2*S bulk copies, 32 KiB), each warp consumes blocks w, w+4, ...; the
+// per-warp online-softmax states are merged through shared memory; with
+// several splits the last CTA of a (sequence, head) merges the partials.
+// ---------------------------------------------------------------------------
+template <int BF16, int G>
+struct DecodeShape {
+  static constexpr int kEsz = BF16 ? 2 : 4;
+  static constexpr int kChunk = kBlockTokens * D * kEsz;
+  static constexpr int kS = BF16 ? 8 : 4;
+  static constexpr int kWarps = 4;
+  static constexpr int kThreads = 32 * kWarps;
+  static constexpr int kStageBytes = 2 * kS * kChunk;
+  static constexpr int kQBytes = G * D * 4;
+  static constexpr int kRedBytes = (2 * kWarps * G + kWarps * G * D) * 4;
+  static constexpr int kBarBytes = kS * 8 + 16;
+  static constexpr int kSmem = kStageBytes + kQBytes + kRedBytes + kBarBytes;
+};
+
+template <int BF16, int G>
+__global__ void __launch_bounds__(128) decode_kernel(const DecodeLaunch p) {
+  using Sh = DecodeShape<BF16, G>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ks = smem;
+  uint8_t* vs = smem + Sh::kS * Sh::kChunk;
+  float* qs = reinterpret_cast<float*>(smem + Sh::kStageBytes);
+  float* red_m = qs + G * D;
+  float* red_l = red_m + Sh::kWarps * G;
+  float* red_acc = red_l + Sh::kWarps * G;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red_acc + Sh::kWarps * G * D);
+  int* sflag = reinterpret_cast<int*>(bars + Sh::kS);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
+  const int total = p.n_items * Hkv;
+
+  if (tid == 0) {
+    for (int s = 0; s < Sh::kS; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+    sflag[1] = 0;
+  }
+  __syncthreads();
+
+  uint32_t phase_bits = 0;  // parity to wait for, per stage barrier
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    const int item = w / Hkv, h = w - item * Hkv;
+    const WorkItem wi = p.items[item];
+    const SeqEntry se = p.seqs[wi.seq];
+    const int L = se.ctx_len;
+    const int nblk = (L + kBlockTokens - 1) / kBlockTokens;
+    const int b0 = wi.split * Sh::kS;
+    const int nb = min(nblk, b0 + Sh::kS) - b0;
+    const int pos = se.base;  // fused mode: the new token's position (L - 1)
+    const size_t layer_off = static_cast<size_t>(p.layer) * p.g.layer_elems;
+    const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
+
+    if (tid == 0) {
+      for (int j = 0; j < nb; ++j) {
+        const int32_t blk = checked_block(p.g, bt[b0 + j]);
+        const size_t off =
+            (layer_off + (static_cast<size_t>(blk) * Hkv + h) * (kBlockTokens * D)) * Sh::kEsz;
+        mbar_arrive_expect_tx(&bars[j], 2 * Sh::kChunk);
+        bulk_load(ks + j * Sh::kChunk, static_cast<const uint8_t*>(p.g.k) + off, Sh::kChunk,
+                  &bars[j]);
+        bulk_load(vs + j * Sh::kChunk, static_cast<const uint8_t*>(p.g.v) + off, Sh::kChunk,
+                  &bars[j]);
+      }
+    }
+
+    // Q heads h*G .. h*G+G-1 of this sequence, rotated at `pos` when fused.
+    {
+      const float* qsrc = p.q + (static_cast<size_t>(wi.seq) * Hq + h * G) * D;
+      for (int i = tid; i < G * (D / 2); i += Sh::kThreads) {
+        const int g = i / (D / 2), pr = i - g * (D / 2);
+        float2 x = reinterpret_cast<const float2*>(qsrc + g * D)[pr];
+        if (p.fused) x = rope_pair(x, p.g.rope[static_cast<size_t>(pos) * (D / 2) + pr]);
+        const int u = (2 * pr) >> 2;
+        *reinterpret_cast<float2*>(qs + g * D + qunit(u) * 4 + ((2 * pr) & 3)) = x;
+      }
+    }
+    __syncthreads();
+
+    float m[G], l[G];
+    float2 acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      m[g] = -INFINITY;
+      l[g] = 0.f;
+      acc[g] = make_float2(0.f, 0.f);
+    }
+    bool timed_out = false;
+    for (int j = warp; j < nb; j += Sh::kWarps) {
+      if (!mbar_wait_bounded(&bars[j], (phase_bits >> j) & 1u)) {
+        timed_out = true;
+        break;
+      }
+      const int tok0 = (b0 + j) * kBlockTokens;
+      const int nvalid = min(kBlockTokens, L - tok0);
+      uint8_t* kb = ks + j * Sh::kChunk;
+      uint8_t* vb = vs + j * Sh::kChunk;
+      if (p.fused && pos >= tok0 && pos < tok0 + kBlockTokens) {
+        // The append: rotate the new key, store K/V (rounded to the pool's
+        // type) into the staged copy and into the pool.
+        const size_t src = (static_cast<size_t>(wi.seq) * Hkv + h) * D;
+        float2 kx = reinterpret_cast<const float2*>(p.k_new + src)[lane];
+        const float2 vx = reinterpret_cast<const float2*>(p.v_new + src)[lane];
+        const bool fin = finite2(kx) && finite2(vx);
+        kx = rope_pair(kx, p.g.rope[static_cast<size_t>(pos) * (D / 2) + lane]);
+        const int slot = pos - tok0;
+        const int32_t blk = checked_block(p.g, bt[b0 + j]);
+        const size_t dst =
+            layer_off + ((static_cast<size_t>(blk) * Hkv + h) * kBlockTokens + slot) * D;
+        if constexpr (BF16) {
+          const uint32_t kq = pack_bf16x2(kx.x, kx.y), vq = pack_bf16x2(vx.x, vx.y);
+          reinterpret_cast<uint32_t*>(kb)[slot * (D / 2) + lane] = kq;
+          reinterpret_cast<uint32_t*>(vb)[slot * (D / 2) + lane] = vq;
+          reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.k) + dst)[lane] = kq;
+          reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.v) + dst)[lane] = vq;
+        } else {
+          reinterpret_cast<float2*>(kb)[slot * (D / 2) + lane] = kx;
+          reinterpret_cast<float2*>(vb)[slot * (D / 2) + lane] = vx;
+          reinterpret_cast<float2*>(static_cast<float*>(p.g.k) + dst)[lane] = kx;
+          reinterpret_cast<float2*>(static_cast<float*>(p.g.v) + dst)[lane] = vx;
+        }
+        if (!__all_sync(kFull, fin) && lane == 0) atomicOr(&p.status[wi.seq], kStatusNonFinite);
+        __syncwarp();
+      }
+      float sc[G];
+      if constexpr (BF16) {
+        block_scores_bf16<G>(reinterpret_cast<const uint16_t*>(kb), qs, lane, sc);
+      } else {
+        block_scores_f32<G>(reinterpret_cast<const float*>(kb), qs, lane, sc);
+      }
+      block_softmax_pv<G, BF16 != 0>(vb, lane, nvalid, sc, m, l, acc);
+    }
+    if (timed_out && lane == 0) {
+      atomicOr(p.g.error, kErrTimeout);
+      sflag[1] = 1;
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        red_m[warp * G + g] = m[g];
+        red_l[warp * G + g] = l[g];
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      reinterpret_cast<float2*>(red_acc + (warp * G + g) * D)[lane] = acc[g];
+    // Every stage barrier used by this item has completed once (or timed out).
+    phase_bits ^= (nb >= 32) ? 0xffffffffu : ((1u << nb) - 1u);
+    __syncthreads();
+
+    if (sflag[1]) {
+      // A wait ran out: give the copies still in flight a bounded chance to
+      // land before the CTA leaves, then stop.
+      if (tid == 0)
+        for (int j = 0; j < nb; ++j) mbar_wait_bounded(&bars[j], ((phase_bits >> j) & 1u) ^ 1u);
+      return;
+    }
+
+    const bool single = (se.nsplit == 1);
+    for (int idx = tid; idx < G * D; idx += Sh::kThreads) {
+      const int g = idx / D, dim = idx - g * D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int ww = 0; ww < Sh::kWarps; ++ww) M = fmaxf(M, red_m[ww * G + g]);
+      float Ls = 0.f, A = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < Sh::kWarps; ++ww) {
+        const float f = exp2f(red_m[ww * G + g] - M);  // empty warps: exp2(-inf) = 0
+        Ls = fmaf(red_l[ww * G + g], f, Ls);
+        A = fmaf(red_acc[(ww * G + g) * D + dim], f, A);
+      }
+      if (single) {
+        p.out[(static_cast<size_t>(wi.seq) * Hq + h * G + g) * D + dim] = A / Ls;
+      } else {
+        const size_t pi = (static_cast<size_t>(item) * Hkv + h) * G + g;
+        p.part_acc[pi * D + dim] = A;
+        if (dim == 0) p.part_ml[pi] = make_float2(M, Ls);
+      }
+    }
+    if (!single) {
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) {
+        int32_t* ctr = p.counters + static_cast<size_t>(wi.seq) * Hkv + h;
+        const int prev = atomicAdd(ctr, 1);
+        const int last = (prev == se.nsplit - 1);
+        if (last) atomicExch(ctr, 0);  // ready for the next launch
+        sflag[0] = last;
+      }
+      __syncthreads();
+      if (sflag[0]) {
+        __threadfence();
+        for (int idx = tid; idx < G * D; idx += Sh::kThreads) {
+          const int g = idx / D, dim = idx - g * D;
+          float M = -INFINITY;
+          for (int s = 0; s < se.nsplit; ++s) {
+            const size_t pi = (static_cast<size_t>(se.item_base + s) * Hkv + h) * G + g;
+            M = fmaxf(M, __ldcg(&p.part_ml[pi].x));
+          }
+          float Ls = 0.f, A = 0.f;
+          for (int s = 0; s < se.nsplit; ++s) {
+            const size_t pi = (static_cast<size_t>(se.item_base + s) * Hkv + h) * G + g;
+            const float2 ml = __ldcg(&p.part_ml[pi]);
+            const float f = exp2f(ml.x - M);
+            Ls = fmaf(ml.y, f, Ls);
+            A = fmaf(__ldcg(&p.part_acc[pi * D + dim]), f, A);
+          }
+          p.out[(static_cast<size_t>(wi.seq) * Hq + h * G + g) * D + dim] = A / Ls;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <int BF16, int G>
+cudaError_t launch_decode_t(const DecodeLaunch& p, int /*num_sms*/, cudaStream_t s) {
+  using Sh = DecodeShape<BF16, G>;
+  static_assert(Sh::kSmem <= 48 * 1024, "decode staging must fit the default smem window");
+  const int total = p.n_items * p.g.kv_heads;
+  if (total <= 0) return cudaSuccess;
+  decode_kernel<BF16, G><<<total, Sh::kThreads, Sh::kSmem, s>>>(p);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Append: 16 lanes per (token, kv head) row, 4 dims (two RoPE pairs) a lane,
+// 128-bit loads and stores.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int find_seq(const SeqEntry* seqs, int n, int row) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (seqs[mid].row_offset <= row) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int BF16>
+__global__ void __launch_bounds__(256) append_kernel(const AppendLaunch p) {
+  const int Hkv = p.g.kv_heads;
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int l16 = threadIdx.x & 15;
+  if (row >= p.total_tokens * Hkv) return;
+  const int tok = row / Hkv, h = row - tok * Hkv;
+  const int si = find_seq(p.seqs, p.n_seq, tok);
+  const SeqEntry se = p.seqs[si];
+  const int pos = se.base + (tok - se.row_offset);
+  const int32_t blk =
+      checked_block(p.g, p.g.block_table[static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq +
+                                         pos / kBlockTokens]);
+  float4 k = reinterpret_cast<const float4*>(p.k_in + static_cast<size_t>(row) * D)[l16];
+  const float4 v = reinterpret_cast<const float4*>(p.v_in + static_cast<size_t>(row) * D)[l16];
+  const bool fin = finite4(k) && finite4(v);
+  if (p.rotate) {
+    const float4 cs =
+        reinterpret_cast<const float4*>(p.g.rope + static_cast<size_t>(pos) * (D / 2))[l16];
+    const float2 a = rope_pair(make_float2(k.x, k.y), make_float2(cs.x, cs.y));
+    const float2 b = rope_pair(make_float2(k.z, k.w), make_float2(cs.z, cs.w));
+    k = make_float4(a.x, a.y, b.x, b.y);
+  }
+  const size_t dst = static_cast<size_t>(p.layer) * p.g.layer_elems +
+                     ((static_cast<size_t>(blk) * Hkv + h) * kBlockTokens + pos % kBlockTokens) * D;
+  if constexpr (BF16) {
+    reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.g.k) + dst)[l16] =
+        make_uint2(pack_bf16x2(k.x, k.y), pack_bf16x2(k.z, k.w));
+    reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.g.v) + dst)[l16] =
+        make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  } else {
+    reinterpret_cast<float4*>(static_cast<float*>(p.g.k) + dst)[l16] = k;
+    reinterpret_cast<float4*>(static_cast<float*>(p.g.v) + dst)[l16] = v;
+  }
+  if (!fin) atomicOr(&p.status[si], kStatusNonFinite);
+}
+
+// ---------------------------------------------------------------------------
+// Gather: the inverse walk, into dense [length, Hkv, d] f32 (bf16 widens
+// exactly).
+// ---------------------------------------------------------------------------
+template <int BF16>
+__global__ void __launch_bounds__(256) gather_kernel(const GatherLaunch p) {
+  const int Hkv = p.g.kv_heads;
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int l16 = threadIdx.x & 15;
+  if (row >= p.length * Hkv) return;
+  const int pos = row / Hkv, h = row - pos * Hkv;
+  const int32_t blk =
+      checked_block(p.g, p.g.block_table[static_cast<size_t>(p.slot) * p.g.max_blocks_per_seq +
+                                         pos / kBlockTokens]);
+  const size_t src = static_cast<size_t>(p.layer) * p.g.layer_elems +
+                     ((static_cast<size_t>(blk) * Hkv + h) * kBlockTokens + pos % kBlockTokens) * D;
+  float4 k, v;
+  if constexpr (BF16) {
+    const uint2 kr = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.g.k) + src)[l16];
+    const uint2 vr = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.g.v) + src)[l16];
+    k = make_float4(bf16lo(kr.x), bf16hi(kr.x), bf16lo(kr.y), bf16hi(kr.y));
+    v = make_float4(bf16lo(vr.x), bf16hi(vr.x), bf16lo(vr.y), bf16hi(vr.y));
+  } else {
+    k = reinterpret_cast<const float4*>(static_cast<const float*>(p.g.k) + src)[l16];
+    v = reinterpret_cast<const float4*>(static_cast<const float*>(p.g.v) + src)[l16];
+  }
+  if (p.k_out) reinterpret_cast<float4*>(p.k_out + static_cast<size_t>(row) * D)[l16] = k;
+  if (p.v_out) reinterpret_cast<float4*>(p.v_out + static_cast<size_t>(row) * D)[l16] = v;
+}
+
+// ---------------------------------------------------------------------------
+// Prefill / extend attention on CUDA cores: CTA = (16-query tile, sequence,
+// kv head); K/V blocks of the causal range are staged (widened to f32) in
+// shared memory; warp w owns query rows w, w+4, w+8, w+12 of the tile.
+// ---------------------------------------------------------------------------
+template <int BF16, int G>
+__global__ void __launch_bounds__(128) prefill_kernel(const PrefillLaunch p) {
+  __shared__ __align__(16) float qs[kBlockTokens * G * D];
+  __shared__ __align__(16) float kbuf[kBlockTokens * D];
+  __shared__ __align__(16) float vbuf[kBlockTokens * D];
+  const int tile = blockIdx.x, si = blockIdx.y, h = blockIdx.z;
+  const SeqEntry se = p.seqs[si];
+  const int q0 = tile * kBlockTokens;
+  if (q0 >= se.count) return;
+  const int nq = min(kBlockTokens, se.count - q0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
+
+  for (int i = tid; i < nq * G * (D / 2); i += blockDim.x) {
+    const int jq = i / (G * (D / 2));
+    const int r = i - jq * G * (D / 2);
+    const int g = r / (D / 2), pr = r - g * (D / 2);
+    const int row = se.row_offset + q0 + jq;
+    const int pos = se.base + q0 + jq;
+    float2 x = reinterpret_cast<const float2*>(p.q + (static_cast<size_t>(row) * Hq + h * G + g) * D)[pr];
+    if (p.rotate) x = rope_pair(x, p.g.rope[static_cast<size_t>(pos) * (D / 2) + pr]);
+    const int u = (2 * pr) >> 2;
+    *reinterpret_cast<float2*>(qs + (jq * G + g) * D + qunit(u) * 4 + ((2 * pr) & 3)) = x;
+  }
+
+  float m[4][G], l[4][G];
+  float2 acc[4][G];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      m[r][g] = -INFINITY;
+      l[r][g] = 0.f;
+      acc[r][g] = make_float2(0.f, 0.f);
+    }
+
+  const int last_pos = se.base + q0 + nq - 1;
+  const int nblk = last_pos / kBlockTokens + 1;
+  const size_t layer_off = static_cast<size_t>(p.layer) * p.g.layer_elems;
+  const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
+  for (int b = 0; b < nblk; ++b) {
+    __syncthreads();
+    const int32_t blk = checked_block(p.g, bt[b]);
+    const size_t off = layer_off + (static_cast<size_t>(blk) * Hkv + h) * (kBlockTokens * D);
+    for (int i = tid; i < kBlockTokens * D / 4; i += blockDim.x) {
+      float4 k, v;
+      if constexpr (BF16) {
+        const uint2 kr = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.g.k) + off)[i];
+        const uint2 vr = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.g.v) + off)[i];
+        k = make_float4(bf16lo(kr.x), bf16hi(kr.x), bf16lo(kr.y), bf16hi(kr.y));
+        v = make_float4(bf16lo(vr.x), bf16hi(vr.x), bf16lo(vr.y), bf16hi(vr.y));
+      } else {
+        k = reinterpret_cast<const float4*>(static_cast<const float*>(p.g.k) + off)[i];
+        v = reinterpret_cast<const float4*>(static_cast<const float*>(p.g.v) + off)[i];
+      }
+      reinterpret_cast<float4*>(kbuf)[i] = k;
+      reinterpret_cast<float4*>(vbuf)[i] = v;
+    }
+    __syncthreads();
+    const int tok0 = b * kBlockTokens;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int jq = warp + 4 * r;
+      if (jq >= nq) break;
+      const int qpos = se.base + q0 + jq;
+      const int nvalid = min(kBlockTokens, qpos + 1 - tok0);
+      if (nvalid <= 0) continue;
+      float sc[G];
+      block_scores_f32<G>(kbuf, qs + jq * G * D, lane, sc);
+      block_softmax_pv<G, false>(vbuf, lane, nvalid, sc, m[r], l[r], acc[r]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int jq = warp + 4 * r;
+    if (jq >= nq) break;
+    const int row = se.row_offset + q0 + jq;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float2 o = make_float2(acc[r][g].x / l[r][g], acc[r][g].y / l[r][g]);
+      reinterpret_cast<float2*>(p.out + (static_cast<size_t>(row) * Hq + h * G + g) * D)[lane] = o;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Block-table writes, then copy-on-write block copies (all layers, K and V).
+// ---------------------------------------------------------------------------
+__global__ void apply_updates_kernel(const PoolGeom g, const TableUpdate* __restrict__ up,
+                                     int32_t nu, const CopyJob* __restrict__ cp, int32_t nc) {
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = tid; i < nu; i += stride) {
+    const TableUpdate u = up[i];
+    g.block_table[static_cast<size_t>(u.slot) * g.max_blocks_per_seq + u.index] = u.block;
+  }
+  const int esz = g.bf16 ? 2 : 4;
+  const int64_t chunk16 = static_cast<int64_t>(g.kv_heads) * kBlockTokens * D * esz / 16;
+  const int64_t per_job = chunk16 * g.num_layers * 2;
+  for (int64_t i = tid; i < per_job * nc; i += stride) {
+    const int64_t job = i / per_job;
+    int64_t r = i - job * per_job;
+    const int pool = static_cast<int>(r / (chunk16 * g.num_layers));
+    r -= static_cast<int64_t>(pool) * chunk16 * g.num_layers;
+    const int layer = static_cast<int>(r / chunk16);
+    const int64_t e = r - static_cast<int64_t>(layer) * chunk16;
+    const int32_t src = checked_block(g, cp[job].src), dst = checked_block(g, cp[job].dst);
+    uint8_t* base = static_cast<uint8_t*>(pool ? g.v : g.k) +
+                    static_cast<size_t>(layer) * g.layer_elems * esz;
+    const uint4* s = reinterpret_cast<const uint4*>(base + static_cast<size_t>(src) * chunk16 * 16);
+    uint4* d = reinterpret_cast<uint4*>(base + static_cast<size_t>(dst) * chunk16 * 16);
+    d[e] = s[e];
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_decode(const DecodeLaunch& p, int num_sms, cudaStream_t s) {
+  const int G = p.g.q_heads / p.g.kv_heads;
+  if (p.g.bf16) {
+    switch (G) {
+      case 1: return launch_decode_t<1, 1>(p, num_sms, s);
+      case 2: return launch_decode_t<1, 2>(p, num_sms, s);
+      case 4: return launch_decode_t<1, 4>(p, num_sms, s);
+      case 8: return launch_decode_t<1, 8>(p, num_sms, s);
+    }
+  } else {
+    switch (G) {
+      case 1: return launch_decode_t<0, 1>(p, num_sms, s);
+      case 2: return launch_decode_t<0, 2>(p, num_sms, s);
+      case 4: return launch_decode_t<0, 4>(p, num_sms, s);
+      case 8: return launch_decode_t<0, 8>(p, num_sms, s);
+    }
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_append(const AppendLaunch& p, cudaStream_t s) {
+  const int64_t rows = static_cast<int64_t>(p.total_tokens) * p.g.kv_heads;
+  if (rows <= 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t blocks = (rows * 16 + threads - 1) / threads;
+  if (p.g.bf16) append_kernel<1><<<static_cast<unsigned>(blocks), threads, 0, s>>>(p);
+  else append_kernel<0><<<static_cast<unsigned>(blocks), threads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather(const GatherLaunch& p, cudaStream_t s) {
+  const int64_t rows = static_cast<int64_t>(p.length) * p.g.kv_heads;
+  if (rows <= 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t blocks = (rows * 16 + threads - 1) / threads;
+  if (p.g.bf16) gather_kernel<1><<<static_cast<unsigned>(blocks), threads, 0, s>>>(p);
+  else gather_kernel<0><<<static_cast<unsigned>(blocks), threads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill(const PrefillLaunch& p, cudaStream_t s) {
+  if (p.n_seq <= 0 || p.max_count <= 0) return cudaSuccess;
+  const dim3 grid((p.max_count + kBlockTokens - 1) / kBlockTokens, p.n_seq, p.g.kv_heads);
+  const int G = p.g.q_heads / p.g.kv_heads;
+#define SLMKV_PREFILL(B, GG) prefill_kernel<B, GG><<<grid, 128, 0, s>>>(p)
+  if (p.g.bf16) {
+    switch (G) {
+      case 1: SLMKV_PREFILL(1, 1); break;
+      case 2: SLMKV_PREFILL(1, 2); break;
+      case 4: SLMKV_PREFILL(1, 4); break;
+      default: return cudaErrorInvalidValue;
+    }
+  } else {
+    switch (G) {
+      case 1: SLMKV_PREFILL(0, 1); break;
+      case 2: SLMKV_PREFILL(0, 2); break;
+      case 4: SLMKV_PREFILL(0, 4); break;
+      default: return cudaErrorInvalidValue;
+    }
+  }
+#undef SLMKV_PREFILL
+  return cudaGetLastError();
+}
+
+cudaError_t launch_apply_updates(const PoolGeom& g, const TableUpdate* updates, int32_t n_updates,
+                                 const CopyJob* copies, int32_t n_copies, cudaStream_t s) {
+  if (n_updates <= 0 && n_copies <= 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t esz = g.bf16 ? 2 : 4;
+  const int64_t work =
+      n_updates + static_cast<int64_t>(n_copies) * g.num_layers * 2 * g.kv_heads * kBlockTokens * D *
+                      esz / 16;
+  int64_t blocks = (work + threads - 1) / threads;
+  if (blocks > 4096) blocks = 4096;
+  if (blocks < 1) blocks = 1;
+  apply_updates_kernel<<<static_cast<unsigned>(blocks), threads, 0, s>>>(g, updates, n_updates,
+                                                                          copies, n_copies);
+  return cudaGetLastError();
+}
+
+}  // namespace slmkv

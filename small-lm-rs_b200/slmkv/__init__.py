@@ -1,0 +1,495 @@
+"""Python mirror of small-lm-rs's KV-cache API over the B200 library.
+
+``libslmkv.so`` (built from ``../csrc``) holds the CUDA kernels and the host
+engine; this module binds its C ABI (``include/slmkv.h``) with ctypes and
+mirrors the reference's Rust surface:
+
+- ``KvCache`` follows ``rust/engine/src/kv_cache.rs`` (``allocate``,
+  ``append_layer``, ``layer_sequence_length``, ``sequence_length``,
+  ``is_empty``, ``is_synchronized``, ``remaining_capacity``, ``truncate_all``,
+  ``truncate_layer``, ``clear``, ``layer_keys``, ``layer_values``,
+  ``key_head``, ``value_head``), one instance per request as in the reference,
+  but backed by blocks of a shared paged pool on the GPU;
+- ``attend_cached_query`` follows ``attention.rs:677-759`` and
+  ``Batch.decode_layer`` the cache part of ``forward_cached_token``
+  (``attention.rs:794-810``) for many sequences in one launch;
+- errors are raised as ``InvalidConfiguration`` / ``InvalidInput``
+  (``error.rs:14-60``) carrying the library's message.
+
+Tensors are torch CUDA float32 tensors; calls run on torch's current stream.
+There is no CPU fallback: without the library or a device, calls raise.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+from typing import Sequence
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libslmkv.so"
+CSRC = HERE.parent / "csrc"
+
+OK = 0
+ERR_INVALID_CONFIGURATION = -1
+ERR_INVALID_INPUT = -2
+ERR_CAPACITY = -3
+ERR_NON_FINITE = -4
+ERR_POOL_EXHAUSTED = -5
+ERR_CUDA = -6
+ERR_DEVICE_TIMEOUT = -7
+ERR_NO_DEVICE = -8
+
+KV_F32 = 0
+KV_BF16 = 1
+
+BLOCK_TOKENS = 16
+
+
+class EngineError(RuntimeError):
+    """Base of the errors raised by the library (error.rs:14-121)."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(message or f"slmkv status {code}")
+        self.code = code
+
+
+class InvalidConfiguration(EngineError):
+    """EngineError::InvalidConfiguration."""
+
+
+class InvalidInput(EngineError):
+    """EngineError::InvalidInput (shape, index, capacity, non-finite, pool)."""
+
+
+class DeviceError(EngineError):
+    """A CUDA failure, an expired device wait, or no device."""
+
+
+def _error_class(code: int):
+    if code == ERR_INVALID_CONFIGURATION:
+        return InvalidConfiguration
+    if code in (ERR_INVALID_INPUT, ERR_CAPACITY, ERR_NON_FINITE, ERR_POOL_EXHAUSTED):
+        return InvalidInput
+    return DeviceError
+
+
+class SlmConfig(C.Structure):
+    _fields_ = [
+        ("num_layers", C.c_int32),
+        ("num_query_heads", C.c_int32),
+        ("num_key_value_heads", C.c_int32),
+        ("head_dimension", C.c_int32),
+        ("context_length", C.c_int32),
+        ("rope_theta", C.c_float),
+        ("num_blocks", C.c_int32),
+        ("max_sequences", C.c_int32),
+        ("kv_dtype", C.c_int32),
+    ]
+
+
+# Every symbol include/slmkv.h declares, with its ctypes signature.
+_i32, _i64, _u64, _vp = C.c_int32, C.c_int64, C.c_uint64, C.c_void_p
+_pi32 = C.POINTER(C.c_int32)
+_pu32 = C.POINTER(C.c_uint32)
+SIGNATURES = {
+    "slm_create": (C.c_int, [C.POINTER(SlmConfig), _i32, C.POINTER(_vp)]),
+    "slm_destroy": (C.c_int, [_vp]),
+    "slm_last_error": (C.c_char_p, [_vp]),
+    "slm_device_bytes": (C.c_int, [_vp, C.POINTER(_i64)]),
+    "slm_launch_count": (C.c_int, [_vp, C.POINTER(_i64)]),
+    "slm_seq_create": (C.c_int, [_vp, _i32, _pi32]),
+    "slm_seq_free": (C.c_int, [_vp, _i32]),
+    "slm_seq_layer_length": (C.c_int, [_vp, _i32, _i32, _pi32]),
+    "slm_seq_length": (C.c_int, [_vp, _i32, _pi32]),
+    "slm_seq_is_empty": (C.c_int, [_vp, _i32, _pi32]),
+    "slm_seq_is_synchronized": (C.c_int, [_vp, _i32, _pi32]),
+    "slm_seq_remaining_capacity": (C.c_int, [_vp, _i32, _pi32]),
+    "slm_seq_truncate_all": (C.c_int, [_vp, _i32, _i32]),
+    "slm_seqs_truncate_all": (C.c_int, [_vp, _i32, _pi32, _pi32]),
+    "slm_seq_truncate_layer": (C.c_int, [_vp, _i32, _i32, _i32]),
+    "slm_seq_clear": (C.c_int, [_vp, _i32]),
+    "slm_seq_blocks": (C.c_int, [_vp, _i32, _pi32, _i32, _pi32]),
+    "slm_append_layer": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _i32, _i32, _vp]),
+    "slm_gather_layer": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp]),
+    "slm_attend_cached_query": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp]),
+    "slm_batch_begin": (C.c_int, [_vp, _i32, _pi32, _pi32, _vp, C.POINTER(_vp)]),
+    "slm_batch_decode_layer": (C.c_int, [_vp, _i32, _vp, _vp, _vp, _vp]),
+    "slm_batch_append_layer": (C.c_int, [_vp, _i32, _vp, _vp, _i32]),
+    "slm_batch_prefill_attention": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
+    "slm_batch_end": (C.c_int, [_vp, _pi32]),
+    "slm_batch_rollback": (C.c_int, [_vp]),
+    "slm_prefix_attach": (C.c_int, [_vp, _i32, _pu32, _i32, _pi32]),
+    "slm_prefix_publish": (C.c_int, [_vp, _i32, _pu32, _i32, _pi32]),
+    "slm_pool_stats": (C.c_int, [_vp, _pi32, _pi32]),
+    "slm_pool_shuffle": (C.c_int, [_vp, _u64]),
+}
+
+_lib = None
+
+
+def build() -> None:
+    """Compile libslmkv.so for sm_100a with the committed Makefile."""
+    import subprocess
+
+    subprocess.run(["make", "-s", "-C", str(CSRC)], check=True)
+
+
+def lib() -> C.CDLL:
+    """Load the in-tree library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `make -C {CSRC}` "
+                "(there is no CPU fallback)")
+        L = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _i32_array(values: Sequence[int]):
+    arr = (C.c_int32 * max(1, len(values)))(*[int(v) for v in values])
+    return arr
+
+
+def _u32_array(values: Sequence[int]):
+    return (C.c_uint32 * max(1, len(values)))(*[int(v) for v in values])
+
+
+def _stream_ptr(stream=None):
+    import torch
+
+    if stream is None and not torch.cuda.is_available():
+        return C.c_void_p(0)  # host-only pools: the library rejects compute calls
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _ptr(t) -> C.c_void_p:
+    if t is None:
+        return C.c_void_p(0)
+    import torch
+
+    if not isinstance(t, torch.Tensor):
+        raise TypeError("expected a torch tensor")
+    if t.dtype != torch.float32 or not t.is_cuda or not t.is_contiguous():
+        raise InvalidInput(ERR_INVALID_INPUT,
+                           "invalid input for slmkv: tensors must be contiguous CUDA float32")
+    return C.c_void_p(t.data_ptr())
+
+
+class KvPool:
+    """One GPU's paged KV pool (an ``slm_ctx``): the storage that every
+    ``KvCache`` of this device lives in."""
+
+    def __init__(self, *, num_layers: int, num_query_heads: int, num_key_value_heads: int,
+                 head_dimension: int = 64, context_length: int, rope_theta: float = 10000.0,
+                 num_blocks: int, max_sequences: int, kv_dtype: int = KV_F32,
+                 device: int | None = 0):
+        self.config = SlmConfig(num_layers, num_query_heads, num_key_value_heads,
+                                head_dimension, context_length, rope_theta, num_blocks,
+                                max_sequences, kv_dtype)
+        self.device = -1 if device is None else int(device)
+        h = C.c_void_p()
+        rc = lib().slm_create(C.byref(self.config), self.device, C.byref(h))
+        if rc != OK:
+            msg = (lib().slm_last_error(None) or b"").decode()
+            raise _error_class(rc)(rc, msg)
+        self._h = h
+        self._batch = None
+
+    @classmethod
+    def from_model_config(cls, cfg: dict, *, num_blocks: int, max_sequences: int,
+                          kv_dtype: int = KV_F32, device: int | None = 0) -> "KvPool":
+        """Builds a pool from a reference model config dict (configs/model.json)."""
+        return cls(num_layers=cfg["num_layers"], num_query_heads=cfg["num_query_heads"],
+                   num_key_value_heads=cfg["num_key_value_heads"],
+                   head_dimension=cfg["head_dimension"], context_length=cfg["context_length"],
+                   rope_theta=cfg["rope_theta"], num_blocks=num_blocks,
+                   max_sequences=max_sequences, kv_dtype=kv_dtype, device=device)
+
+    # -- plumbing -----------------------------------------------------------
+    @property
+    def handle(self) -> C.c_void_p:
+        if self._h is None:
+            raise InvalidInput(ERR_INVALID_INPUT, "invalid input for slmkv: pool is closed")
+        return self._h
+
+    def check(self, rc: int) -> None:
+        if rc != OK:
+            msg = (lib().slm_last_error(self._h) or b"").decode()
+            raise _error_class(rc)(rc, msg)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None:
+            lib().slm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def num_layers(self) -> int:
+        return self.config.num_layers
+
+    @property
+    def kv_heads(self) -> int:
+        return self.config.num_key_value_heads
+
+    @property
+    def q_heads(self) -> int:
+        return self.config.num_query_heads
+
+    @property
+    def head_dim(self) -> int:
+        return self.config.head_dimension
+
+    def device_bytes(self) -> int:
+        v = C.c_int64()
+        self.check(lib().slm_device_bytes(self.handle, C.byref(v)))
+        return v.value
+
+    def launch_count(self) -> int:
+        """Kernels this pool has launched (counted by the library)."""
+        v = C.c_int64()
+        self.check(lib().slm_launch_count(self.handle, C.byref(v)))
+        return v.value
+
+    def stats(self) -> tuple[int, int]:
+        """(free blocks, blocks held by the prefix index)."""
+        f, i = C.c_int32(), C.c_int32()
+        self.check(lib().slm_pool_stats(self.handle, C.byref(f), C.byref(i)))
+        return f.value, i.value
+
+    def shuffle(self, seed: int) -> None:
+        self.check(lib().slm_pool_shuffle(self.handle, C.c_uint64(seed)))
+
+    # -- sequences ------------------------------------------------------------
+    def allocate_kv_cache(self, max_sequence_length: int) -> "KvCache":
+        """SmallLMModel::allocate_kv_cache (model.rs:64-67)."""
+        return KvCache(self, max_sequence_length)
+
+    def begin(self, caches: Sequence["KvCache"], token_counts: Sequence[int] | int = 1,
+              stream=None) -> "Batch":
+        return Batch(self, caches, token_counts, stream)
+
+    def truncate_many(self, caches: Sequence["KvCache"], lengths: Sequence[int]) -> None:
+        """truncate_all (kv_cache.rs:302-321) for many caches in one call."""
+        ids = _i32_array([c.seq_id for c in caches])
+        lens = _i32_array(lengths)
+        self.check(lib().slm_seqs_truncate_all(self.handle, len(caches), ids, lens))
+
+
+class KvCache:
+    """kv_cache.rs:89-412 — one request's cache, as blocks of a ``KvPool``."""
+
+    def __init__(self, pool: KvPool, max_sequence_length: int):
+        self.pool = pool
+        sid = C.c_int32()
+        pool.check(lib().slm_seq_create(pool.handle, int(max_sequence_length), C.byref(sid)))
+        self.seq_id = sid.value
+        self.max_sequence_length = int(max_sequence_length)
+
+    def free(self) -> None:
+        if self.seq_id is not None and self.pool._h is not None:
+            self.pool.check(lib().slm_seq_free(self.pool.handle, self.seq_id))
+        self.seq_id = None
+
+    def _q(self, fn, *args) -> int:
+        out = C.c_int32()
+        self.pool.check(fn(self.pool.handle, self.seq_id, *args, C.byref(out)))
+        return out.value
+
+    def layer_sequence_length(self, layer: int) -> int:
+        return self._q(lib().slm_seq_layer_length, int(layer))
+
+    def sequence_length(self) -> int:
+        return self._q(lib().slm_seq_length)
+
+    def is_empty(self) -> bool:
+        return bool(self._q(lib().slm_seq_is_empty))
+
+    def is_synchronized(self) -> bool:
+        return bool(self._q(lib().slm_seq_is_synchronized))
+
+    def remaining_capacity(self) -> int:
+        return self._q(lib().slm_seq_remaining_capacity)
+
+    def truncate_all(self, sequence_length: int) -> None:
+        self.pool.check(lib().slm_seq_truncate_all(self.pool.handle, self.seq_id,
+                                                   int(sequence_length)))
+
+    def truncate_layer(self, layer: int, sequence_length: int) -> None:
+        self.pool.check(lib().slm_seq_truncate_layer(self.pool.handle, self.seq_id, int(layer),
+                                                     int(sequence_length)))
+
+    def clear(self) -> None:
+        self.pool.check(lib().slm_seq_clear(self.pool.handle, self.seq_id))
+
+    def blocks(self) -> list[int]:
+        n = C.c_int32()
+        cap = self.max_sequence_length // BLOCK_TOKENS + 2
+        buf = (C.c_int32 * cap)()
+        self.pool.check(lib().slm_seq_blocks(self.pool.handle, self.seq_id, buf, cap,
+                                             C.byref(n)))
+        return list(buf[: n.value])
+
+    def append_layer(self, layer: int, keys, values, token_count: int, *,
+                     rotate_keys: bool = False, stream=None) -> None:
+        """kv_cache.rs:182-230 (keys/values [T, kv_heads, d] on the device);
+        with ``rotate_keys`` the keys get RoPE at their absolute positions
+        first (attention.rs:422-482)."""
+        p = self.pool
+        if keys.numel() != token_count * p.kv_heads * p.head_dim or \
+                values.numel() != token_count * p.kv_heads * p.head_dim:
+            raise InvalidInput(ERR_INVALID_INPUT,
+                               "invalid input for KV-cache keys: shape does not match "
+                               "[token_count, kv_heads * head_dim]")
+        p.check(lib().slm_append_layer(p.handle, self.seq_id, int(layer), _ptr(keys),
+                                       _ptr(values), int(token_count), int(bool(rotate_keys)),
+                                       _stream_ptr(stream)))
+
+    def _gather(self, layer: int, which: str, stream=None):
+        import torch
+
+        p = self.pool
+        n = self.layer_sequence_length(layer)
+        out = torch.empty((n, p.kv_heads, p.head_dim), dtype=torch.float32,
+                          device=f"cuda:{p.device}")
+        if n:
+            k = out if which == "k" else None
+            v = out if which == "v" else None
+            p.check(lib().slm_gather_layer(p.handle, self.seq_id, int(layer), _ptr(k), _ptr(v),
+                                           _stream_ptr(stream)))
+        return out
+
+    def layer_keys(self, layer: int, stream=None):
+        """kv_cache.rs:237-239 -> [len, kv_heads, d] (device)."""
+        return self._gather(layer, "k", stream)
+
+    def layer_values(self, layer: int, stream=None):
+        """kv_cache.rs:246-248 -> [len, kv_heads, d] (device)."""
+        return self._gather(layer, "v", stream)
+
+    def key_head(self, layer: int, position: int, kv_head: int):
+        """kv_cache.rs:256-263"""
+        self._check_head(layer, position, kv_head)
+        return self.layer_keys(layer)[position, kv_head]
+
+    def value_head(self, layer: int, position: int, kv_head: int):
+        """kv_cache.rs:271-278"""
+        self._check_head(layer, position, kv_head)
+        return self.layer_values(layer)[position, kv_head]
+
+    def _check_head(self, layer, position, kv_head):
+        n = self.layer_sequence_length(layer)
+        if not 0 <= position < n:
+            raise InvalidInput(ERR_INVALID_INPUT,
+                               f"invalid input for KV cache: token position {position} is "
+                               f"outside 0..{n}")
+        if not 0 <= kv_head < self.pool.kv_heads:
+            raise InvalidInput(ERR_INVALID_INPUT,
+                               f"invalid input for KV cache: key/value head {kv_head} is "
+                               f"outside 0..{self.pool.kv_heads}")
+
+    def attend_cached_query(self, layer: int, query, out=None, stream=None):
+        """attention.rs:677-759: rotated query [q_heads, d] -> [q_heads * d]."""
+        import torch
+
+        p = self.pool
+        if out is None:
+            out = torch.empty(p.q_heads * p.head_dim, dtype=torch.float32,
+                              device=f"cuda:{p.device}")
+        p.check(lib().slm_attend_cached_query(p.handle, self.seq_id, int(layer), _ptr(query),
+                                              _ptr(out), _stream_ptr(stream)))
+        return out
+
+    def attach_prefix(self, tokens: Sequence[int]) -> int:
+        """Attaches the longest indexed chain of full blocks matching
+        ``tokens`` to this (empty) cache; returns the reused token count."""
+        n = C.c_int32()
+        self.pool.check(lib().slm_prefix_attach(self.pool.handle, self.seq_id,
+                                                _u32_array(tokens), len(tokens), C.byref(n)))
+        return n.value
+
+    def publish_prefix(self, tokens: Sequence[int]) -> int:
+        """Indexes this cache's full blocks holding ``tokens``; returns how
+        many blocks of the chain are indexed."""
+        n = C.c_int32()
+        self.pool.check(lib().slm_prefix_publish(self.pool.handle, self.seq_id,
+                                                 _u32_array(tokens), len(tokens), C.byref(n)))
+        return n.value
+
+
+class Batch:
+    """One step over many caches (``slm_batch_*``). Use as a context manager:
+    leaving the block normally ends (commits) it, an exception rolls it back."""
+
+    def __init__(self, pool: KvPool, caches: Sequence[KvCache],
+                 token_counts: Sequence[int] | int = 1, stream=None):
+        self.pool = pool
+        self.caches = list(caches)
+        n = len(self.caches)
+        if isinstance(token_counts, int):
+            token_counts = [token_counts] * n
+        self.token_counts = [int(t) for t in token_counts]
+        self._ids = _i32_array([c.seq_id for c in self.caches])
+        self._counts = _i32_array(self.token_counts)
+        self._status = (C.c_int32 * max(1, n))()
+        h = C.c_void_p()
+        pool.check(lib().slm_batch_begin(pool.handle, n, self._ids, self._counts,
+                                         _stream_ptr(stream), C.byref(h)))
+        self._h = h
+        self.statuses: list[int] | None = None
+
+    def decode_layer(self, layer: int, query, keys, values, out) -> None:
+        self.pool.check(lib().slm_batch_decode_layer(self._h, int(layer), _ptr(query),
+                                                     _ptr(keys), _ptr(values), _ptr(out)))
+
+    def append_layer(self, layer: int, keys, values, rotate_keys: bool = True) -> None:
+        self.pool.check(lib().slm_batch_append_layer(self._h, int(layer), _ptr(keys),
+                                                     _ptr(values), int(bool(rotate_keys))))
+
+    def prefill_attention(self, layer: int, query, out, rotate_query: bool = True) -> None:
+        self.pool.check(lib().slm_batch_prefill_attention(self._h, int(layer), _ptr(query),
+                                                          int(bool(rotate_query)), _ptr(out)))
+
+    def end(self, raise_on_error: bool = True) -> list[int]:
+        if self._h is None:
+            return self.statuses or []
+        rc = lib().slm_batch_end(self._h, self._status)
+        self._h = None
+        self.statuses = list(self._status[: len(self.caches)])
+        if rc != OK and raise_on_error:
+            self.pool.check(rc)
+        return self.statuses
+
+    def rollback(self) -> None:
+        if self._h is not None:
+            rc = lib().slm_batch_rollback(self._h)
+            self._h = None
+            self.pool.check(rc)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        if exc_type is None:
+            self.end()
+        else:
+            self.rollback()
