@@ -54,6 +54,22 @@ struct Upload {
   int next = 0;
 };
 
+// Decode plan of one step, built on the host (which owns every block id).
+struct StreamPlan {
+  std::vector<PairEntry> pairs;
+  std::vector<int32_t> chunks;
+  std::vector<int32_t> warp_first_pair;
+};
+
+// Device addresses of one uploaded step descriptor.
+struct StepDev {
+  SeqEntry* seqs = nullptr;
+  int32_t* status = nullptr;
+  PairEntry* pairs = nullptr;
+  int32_t* chunks = nullptr;
+  int32_t* wfp = nullptr;
+};
+
 size_t align16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
 
 uint64_t mix64(uint64_t x) {  // splitmix64 finaliser
@@ -69,11 +85,10 @@ struct slm_batch {
   slm_ctx* ctx = nullptr;
   cudaStream_t stream = nullptr;
   std::vector<int32_t> seq_ids, counts, base;
-  int32_t total_tokens = 0, max_count = 0, n_items = 0;
+  int32_t total_tokens = 0, max_count = 0;
+  int32_t n_pairs = 0, total_blocks = 0;  // decode plan (when every count is 1)
   std::vector<uint8_t> layer_done;
-  SeqEntry* d_seqs = nullptr;
-  WorkItem* d_items = nullptr;
-  int32_t* d_status = nullptr;
+  StepDev dev;
 };
 
 struct slm_ctx {
@@ -82,7 +97,9 @@ struct slm_ctx {
   int32_t num_sms = 0;
   int32_t max_blocks_per_seq = 0;
   int32_t group = 1;
-  int32_t max_items = 0;
+  int32_t n_warps = 0;     // decode grid: SMs x kDecodeWarps
+  int32_t max_pairs = 0;   // max_sequences x Hkv
+  int64_t max_chunks = 0;  // max_sequences x blocks per sequence x Hkv
   int64_t device_bytes = 0;
   int64_t launches = 0;  // kernels launched by this context
   std::string err;
@@ -112,6 +129,7 @@ struct slm_ctx {
   std::vector<TableUpdate> pending_updates;
   std::vector<CopyJob> pending_copies;
   slm_batch* open_batch = nullptr;
+  StreamPlan plan;  // decode plan of the open batch (reused storage)
 
   PoolGeom geom() const {
     PoolGeom g{};
@@ -333,16 +351,20 @@ cudaError_t upload_end(Upload& u, size_t bytes, cudaStream_t s) {
   return e;
 }
 
-// Layout of one upload: [seqs][items][status][updates][copies].
+// Layout of one upload: [seqs][status][pairs][chunks][warp_first_pair]
+// [table updates][copy jobs].
 struct DescLayout {
-  size_t seqs = 0, items = 0, status = 0, updates = 0, copies = 0, total = 0;
+  size_t seqs = 0, status = 0, pairs = 0, chunks = 0, wfp = 0, updates = 0, copies = 0, total = 0;
 };
-DescLayout desc_layout(int32_t n, int32_t n_items, size_t nu, size_t nc) {
+DescLayout desc_layout(size_t n, size_t n_pairs, size_t n_chunks, size_t n_warps, size_t nu,
+                       size_t nc) {
   DescLayout L;
   L.seqs = 0;
-  L.items = align16(L.seqs + sizeof(SeqEntry) * n);
-  L.status = align16(L.items + sizeof(WorkItem) * n_items);
-  L.updates = align16(L.status + sizeof(int32_t) * n);
+  L.status = align16(L.seqs + sizeof(SeqEntry) * n);
+  L.pairs = align16(L.status + sizeof(int32_t) * n);
+  L.chunks = align16(L.pairs + sizeof(PairEntry) * n_pairs);
+  L.wfp = align16(L.chunks + sizeof(int32_t) * n_chunks);
+  L.updates = align16(L.wfp + sizeof(int32_t) * n_warps);
   L.copies = align16(L.updates + sizeof(TableUpdate) * nu);
   L.total = align16(L.copies + sizeof(CopyJob) * nc);
   return L;
@@ -354,7 +376,7 @@ slm_status flush_excess(slm_ctx* c, cudaStream_t s, size_t keep_updates, size_t 
   while (c->pending_updates.size() > keep_updates || c->pending_copies.size() > keep_copies) {
     const size_t nu = std::min(c->pending_updates.size(), c->upd_cap);
     const size_t nc = std::min(c->pending_copies.size(), c->copy_cap);
-    DescLayout L = desc_layout(0, 0, nu, nc);
+    DescLayout L = desc_layout(0, 0, 0, 0, nu, nc);
     uint8_t* h = upload_begin(c->up_aux);
     memcpy(h + L.updates, c->pending_updates.data(), nu * sizeof(TableUpdate));
     memcpy(h + L.copies, c->pending_copies.data(), nc * sizeof(CopyJob));
@@ -370,35 +392,70 @@ slm_status flush_excess(slm_ctx* c, cudaStream_t s, size_t keep_updates, size_t 
   return SLM_OK;
 }
 
-// Builds split-K work items for sequences with attended lengths `ctx_len`.
-void plan_items(const slm_ctx* c, std::vector<SeqEntry>& entries, std::vector<WorkItem>& items) {
-  const int S = split_blocks(c->cfg.kv_dtype == SLM_KV_BF16);
-  items.clear();
+// Builds the decode plan for sequences (batch rows) attending `ctx_len`
+// tokens: one PairEntry per (row, KV head), the chunk stream in pair order,
+// and an equal split of the stream over `n_warps` decode warps. Warp w owns
+// stream indices [w*T/n_warps, (w+1)*T/n_warps).
+void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, int32_t n_warps,
+                       StreamPlan& plan) {
+  const int32_t Hkv = c->cfg.num_key_value_heads;
+  plan.pairs.clear();
+  plan.chunks.clear();
   for (size_t i = 0; i < entries.size(); ++i) {
-    SeqEntry& e = entries[i];
-    const int32_t nblk = blocks_for(e.ctx_len);
-    e.item_base = static_cast<int32_t>(items.size());
-    e.nsplit = (nblk + S - 1) / S;
-    for (int32_t sp = 0; sp < e.nsplit; ++sp) items.push_back(WorkItem{static_cast<int32_t>(i), sp});
+    const SeqEntry& e = entries[i];
+    const Seq& q = c->seqs[e.slot];
+    const int32_t nb = blocks_for(e.ctx_len);
+    for (int32_t h = 0; h < Hkv; ++h) {
+      PairEntry pe{};
+      pe.seq = static_cast<int32_t>(i);
+      pe.head = h;
+      pe.ctx_len = e.ctx_len;
+      pe.blk_begin = static_cast<int32_t>(plan.chunks.size());
+      pe.nblk = nb;
+      plan.pairs.push_back(pe);
+      for (int32_t j = 0; j < nb; ++j) plan.chunks.push_back(q.blocks[j] * Hkv + h);
+    }
+  }
+  const int64_t T = static_cast<int64_t>(plan.chunks.size());
+  const int64_t NW = n_warps;
+  // Warp owning stream index x: the largest w with floor(w*T/NW) <= x.
+  auto owner = [&](int64_t x) { return static_cast<int32_t>(((x + 1) * NW - 1) / T); };
+  int32_t part = 0;
+  for (PairEntry& pe : plan.pairs) {
+    pe.first_warp = owner(pe.blk_begin);
+    pe.nseg = owner(pe.blk_begin + pe.nblk - 1) - pe.first_warp + 1;
+    pe.part_base = part;
+    if (pe.nseg > 1) part += pe.nseg;
+  }
+  plan.warp_first_pair.assign(n_warps, -1);
+  size_t pc = 0;
+  for (int64_t w = 0; w < NW; ++w) {
+    const int64_t b = w * T / NW, e = (w + 1) * T / NW;
+    if (b >= e) continue;
+    while (plan.pairs[pc].blk_begin + plan.pairs[pc].nblk <= b) ++pc;
+    plan.warp_first_pair[w] = static_cast<int32_t>(pc);
   }
 }
 
-// Uploads [entries, items, zeroed status, pending updates/copies] into region
-// `u` and applies the updates; returns device pointers into the region.
+// Uploads [entries, zeroed status, decode plan (optional), pending table
+// updates / copies] into region `u` with one copy, and applies the updates.
 slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<SeqEntry>& entries,
-                       const std::vector<WorkItem>& items, SeqEntry** d_seqs, WorkItem** d_items,
-                       int32_t** d_status) {
+                       const StreamPlan* plan, StepDev* dev) {
   slm_status rc = flush_excess(c, s, c->upd_cap, c->copy_cap);
   if (rc) return rc;
-  const int32_t n = static_cast<int32_t>(entries.size());
+  const size_t n = entries.size();
+  const size_t np = plan ? plan->pairs.size() : 0, nch = plan ? plan->chunks.size() : 0;
+  const size_t nw = plan ? plan->warp_first_pair.size() : 0;
   const size_t nu = c->pending_updates.size(), nc = c->pending_copies.size();
-  DescLayout L = desc_layout(n, static_cast<int32_t>(items.size()), nu, nc);
+  DescLayout L = desc_layout(n, np, nch, nw, nu, nc);
   if (L.total > u.cap)
     return fail(c, SLM_ERR_INVALID_INPUT, "invalid input for KV cache: step descriptor too large");
   uint8_t* h = upload_begin(u);
   memcpy(h + L.seqs, entries.data(), sizeof(SeqEntry) * n);
-  memcpy(h + L.items, items.data(), sizeof(WorkItem) * items.size());
   memset(h + L.status, 0, sizeof(int32_t) * n);
+  if (np) memcpy(h + L.pairs, plan->pairs.data(), sizeof(PairEntry) * np);
+  if (nch) memcpy(h + L.chunks, plan->chunks.data(), sizeof(int32_t) * nch);
+  if (nw) memcpy(h + L.wfp, plan->warp_first_pair.data(), sizeof(int32_t) * nw);
   if (nu) memcpy(h + L.updates, c->pending_updates.data(), nu * sizeof(TableUpdate));
   if (nc) memcpy(h + L.copies, c->pending_copies.data(), nc * sizeof(CopyJob));
   CU(c, upload_end(u, L.total, s));
@@ -410,10 +467,31 @@ slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<
     c->pending_updates.clear();
     c->pending_copies.clear();
   }
-  *d_seqs = reinterpret_cast<SeqEntry*>(u.d + L.seqs);
-  *d_items = reinterpret_cast<WorkItem*>(u.d + L.items);
-  *d_status = reinterpret_cast<int32_t*>(u.d + L.status);
+  dev->seqs = reinterpret_cast<SeqEntry*>(u.d + L.seqs);
+  dev->status = reinterpret_cast<int32_t*>(u.d + L.status);
+  dev->pairs = reinterpret_cast<PairEntry*>(u.d + L.pairs);
+  dev->chunks = reinterpret_cast<int32_t*>(u.d + L.chunks);
+  dev->wfp = reinterpret_cast<int32_t*>(u.d + L.wfp);
   return SLM_OK;
+}
+
+// Fills a decode launch for an uploaded plan.
+StreamDecodeLaunch decode_launch(slm_ctx* c, int32_t layer, const StepDev& dev,
+                                 const StreamPlan& plan) {
+  StreamDecodeLaunch p{};
+  p.g = c->geom();
+  p.layer = layer;
+  p.pairs = dev.pairs;
+  p.n_pairs = static_cast<int32_t>(plan.pairs.size());
+  p.chunks = dev.chunks;
+  p.total_blocks = static_cast<int32_t>(plan.chunks.size());
+  p.warp_first_pair = dev.wfp;
+  p.n_warps = static_cast<int32_t>(plan.warp_first_pair.size());
+  p.part_acc = c->d_part_acc;
+  p.part_ml = c->d_part_ml;
+  p.counters = c->d_counters;
+  p.status = dev.status;
+  return p;
 }
 
 // Reads back and clears the context error word (stream must be idle).
@@ -422,8 +500,7 @@ slm_status check_device_error(slm_ctx* c) {
   CU(c, cudaMemcpy(&e, c->d_error, sizeof e, cudaMemcpyDeviceToHost));
   if (e) {
     CU(c, cudaMemset(c->d_error, 0, sizeof(int32_t)));
-    CU(c, cudaMemset(c->d_counters, 0,
-                     sizeof(int32_t) * c->cfg.max_sequences * c->cfg.num_key_value_heads));
+    CU(c, cudaMemset(c->d_counters, 0, sizeof(int32_t) * c->max_pairs));
     if (e & kErrTimeout)
       return fail(c, SLM_ERR_DEVICE_TIMEOUT, "device wait timed out (error word 0x%x)", e);
     return fail(c, SLM_ERR_INVALID_INPUT,
@@ -528,8 +605,8 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
   const int32_t G = k.num_query_heads / k.num_key_value_heads;
   c->group = G;
   c->max_blocks_per_seq = blocks_for(k.context_length);
-  const int S = split_blocks(k.kv_dtype == SLM_KV_BF16);
-  c->max_items = k.max_sequences * ((c->max_blocks_per_seq + S - 1) / S);
+  c->max_pairs = k.max_sequences * k.num_key_value_heads;
+  c->max_chunks = static_cast<int64_t>(c->max_pairs) * c->max_blocks_per_seq;
   c->seqs.resize(k.max_sequences);
   for (int32_t i = k.max_sequences - 1; i >= 0; --i) c->free_slots.push_back(i);
   c->refcount.assign(k.num_blocks, 0);
@@ -549,6 +626,7 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     cp->num_sms = sms;
+    cp->n_warps = sms * kDecodeWarps;
     const size_t esz = k.kv_dtype == SLM_KV_BF16 ? 2 : 4;
     const size_t pool_bytes = static_cast<size_t>(k.num_layers) * k.num_blocks *
                               k.num_key_value_heads * kBlockTokens * k.head_dimension * esz;
@@ -563,11 +641,12 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
     std::vector<float2> rope;
     compute_rope_table(k, rope);
     step(dev_alloc(cp, &cp->d_rope, rope.size() * sizeof(float2), "RoPE table"));
-    const size_t parts = static_cast<size_t>(cp->max_items) * k.num_key_value_heads * G;
+    // A pair split over s warps takes s partial slots; at most one extra
+    // slot per warp boundary: pairs + warps bounds the total.
+    const size_t parts = (static_cast<size_t>(cp->max_pairs) + cp->n_warps) * G;
     step(dev_alloc(cp, &cp->d_part_acc, parts * kHeadDim * sizeof(float), "split-K partials"));
     step(dev_alloc(cp, &cp->d_part_ml, parts * sizeof(float2), "split-K partials"));
-    step(dev_alloc(cp, &cp->d_counters, sizeof(int32_t) * k.max_sequences * k.num_key_value_heads,
-                   "split-K counters"));
+    step(dev_alloc(cp, &cp->d_counters, sizeof(int32_t) * cp->max_pairs, "split-K counters"));
     step(dev_alloc(cp, &cp->d_error, sizeof(int32_t), "error word"));
     if (rc == SLM_OK) {
       e = cudaMallocHost(reinterpret_cast<void**>(&cp->h_readback),
@@ -575,19 +654,21 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
       if (e != cudaSuccess) rc = cuda_fail(cp, e, "cudaMallocHost");
     }
     if (rc == SLM_OK) {
-      const size_t batch_cap =
-          desc_layout(k.max_sequences, cp->max_items, cp->upd_cap, cp->copy_cap).total + 256;
+      const size_t batch_cap = desc_layout(k.max_sequences, cp->max_pairs, cp->max_chunks,
+                                           cp->n_warps, cp->upd_cap, cp->copy_cap).total + 256;
+      const size_t aux_cap =
+          desc_layout(1, k.num_key_value_heads,
+                      static_cast<size_t>(k.num_key_value_heads) * cp->max_blocks_per_seq,
+                      cp->n_warps, cp->upd_cap, cp->copy_cap).total + 256;
       rc = upload_alloc(cp, cp->up_batch, batch_cap);
-      if (rc == SLM_OK) rc = upload_alloc(cp, cp->up_aux, batch_cap);
+      if (rc == SLM_OK) rc = upload_alloc(cp, cp->up_aux, aux_cap);
     }
     if (rc == SLM_OK) {
       // Unused pool memory is zero: reads of not-yet-written slots are finite.
       if ((e = cudaMemset(cp->k_pool, 0, pool_bytes)) != cudaSuccess ||
           (e = cudaMemset(cp->v_pool, 0, pool_bytes)) != cudaSuccess ||
           (e = cudaMemset(cp->d_block_table, 0, bt_bytes)) != cudaSuccess ||
-          (e = cudaMemset(cp->d_counters, 0,
-                          sizeof(int32_t) * k.max_sequences * k.num_key_value_heads)) !=
-              cudaSuccess ||
+          (e = cudaMemset(cp->d_counters, 0, sizeof(int32_t) * cp->max_pairs)) != cudaSuccess ||
           (e = cudaMemset(cp->d_error, 0, sizeof(int32_t))) != cudaSuccess ||
           (e = cudaMemcpy(cp->d_rope, rope.data(), rope.size() * sizeof(float2),
                           cudaMemcpyHostToDevice)) != cudaSuccess ||
@@ -812,16 +893,15 @@ slm_status slm_append_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, const f
     return input_error(ctx, SLM_ERR_POOL_EXHAUSTED, "KV cache", "no free block in the pool");
   }
   std::vector<SeqEntry> e(1);
-  e[0] = SeqEntry{seq_id, cur, token_count, 0, 0, 0, static_cast<int32_t>(new_len), 0};
-  std::vector<WorkItem> items;
-  SeqEntry* d_seqs;
-  WorkItem* d_items;
-  int32_t* d_status;
-  rc = upload_step(ctx, ctx->up_aux, s, e, items, &d_seqs, &d_items, &d_status);
+  e[0] = SeqEntry{seq_id, cur, token_count, 0, static_cast<int32_t>(new_len), {0, 0, 0}};
+  StepDev dev;
+  rc = upload_step(ctx, ctx->up_aux, s, e, nullptr, &dev);
   if (rc) {
     rollback_reserve(ctx, undo);
     return rc;
   }
+  SeqEntry* d_seqs = dev.seqs;
+  int32_t* d_status = dev.status;
   AppendLaunch a{};
   a.g = ctx->geom();
   a.layer = layer;
@@ -889,29 +969,17 @@ slm_status slm_attend_cached_query(slm_ctx* ctx, int32_t seq_id, int32_t layer,
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention",
                        "at least one cached key/value position is required");
   std::vector<SeqEntry> e(1);
-  e[0] = SeqEntry{seq_id, L - 1, 1, 0, 0, 0, L, 0};
-  std::vector<WorkItem> items;
-  plan_items(ctx, e, items);
-  SeqEntry* d_seqs;
-  WorkItem* d_items;
-  int32_t* d_status;
-  rc = upload_step(ctx, ctx->up_aux, s, e, items, &d_seqs, &d_items, &d_status);
+  e[0] = SeqEntry{seq_id, L, 0, 0, L, {0, 0, 0}};
+  StreamPlan plan;
+  build_stream_plan(ctx, e, ctx->n_warps, plan);
+  StepDev dev;
+  rc = upload_step(ctx, ctx->up_aux, s, e, &plan, &dev);
   if (rc) return rc;
-  DecodeLaunch p{};
-  p.g = ctx->geom();
-  p.layer = layer;
-  p.seqs = d_seqs;
-  p.items = d_items;
-  p.n_seq = 1;
-  p.n_items = static_cast<int32_t>(items.size());
+  StreamDecodeLaunch p = decode_launch(ctx, layer, dev, plan);
   p.q = d_query;
   p.out = d_out;
-  p.part_acc = ctx->d_part_acc;
-  p.part_ml = ctx->d_part_ml;
-  p.counters = ctx->d_counters;
-  p.status = d_status;
   p.fused = 0;
-  CU(ctx, launch_decode(p, ctx->num_sms, s));
+  CU(ctx, launch_decode(p, s));
   ++ctx->launches;
   return SLM_OK;
 }
@@ -989,15 +1057,20 @@ slm_status slm_batch_begin(slm_ctx* ctx, int32_t n, const int32_t* h_seq_ids,
       return input_error(ctx, SLM_ERR_POOL_EXHAUSTED, "KV cache", "no free block in the pool");
     }
     b->base[i] = base;
-    entries[i] = SeqEntry{id, base, h_token_counts[i], row, 0, 0, base + h_token_counts[i], 0};
+    entries[i] = SeqEntry{id, base, h_token_counts[i], row, base + h_token_counts[i], {0, 0, 0}};
     row += h_token_counts[i];
     b->max_count = std::max(b->max_count, h_token_counts[i]);
   }
   b->total_tokens = row;
-  std::vector<WorkItem> items;
-  plan_items(ctx, entries, items);
-  b->n_items = static_cast<int32_t>(items.size());
-  rc = upload_step(ctx, ctx->up_batch, s, entries, items, &b->d_seqs, &b->d_items, &b->d_status);
+  // A decode step (one token each) carries its decode plan in the same upload.
+  StreamPlan& plan = ctx->plan;
+  const bool decode = (b->max_count == 1);
+  if (decode) {
+    build_stream_plan(ctx, entries, ctx->n_warps, plan);
+    b->n_pairs = static_cast<int32_t>(plan.pairs.size());
+    b->total_blocks = static_cast<int32_t>(plan.chunks.size());
+  }
+  rc = upload_step(ctx, ctx->up_batch, s, entries, decode ? &plan : nullptr, &b->dev);
   if (rc) {
     rollback_reserve(ctx, undo);
     clear_marks();
@@ -1034,23 +1107,13 @@ slm_status slm_batch_decode_layer(slm_batch* b, int32_t layer, const float* d_qu
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "layer %d was already appended", layer);
   if (!d_query || !d_keys || !d_values || !d_out)
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "null tensor");
-  DecodeLaunch p{};
-  p.g = ctx->geom();
-  p.layer = layer;
-  p.seqs = b->d_seqs;
-  p.items = b->d_items;
-  p.n_seq = static_cast<int32_t>(b->seq_ids.size());
-  p.n_items = b->n_items;
+  StreamDecodeLaunch p = decode_launch(ctx, layer, b->dev, ctx->plan);
   p.q = d_query;
   p.k_new = d_keys;
   p.v_new = d_values;
   p.out = d_out;
-  p.part_acc = ctx->d_part_acc;
-  p.part_ml = ctx->d_part_ml;
-  p.counters = ctx->d_counters;
-  p.status = b->d_status;
   p.fused = 1;
-  CU(ctx, launch_decode(p, ctx->num_sms, b->stream));
+  CU(ctx, launch_decode(p, b->stream));
   ++ctx->launches;
   b->layer_done[layer] = 1;
   for (size_t i = 0; i < b->seq_ids.size(); ++i)
@@ -1070,13 +1133,13 @@ slm_status slm_batch_append_layer(slm_batch* b, int32_t layer, const float* d_ke
   AppendLaunch a{};
   a.g = ctx->geom();
   a.layer = layer;
-  a.seqs = b->d_seqs;
+  a.seqs = b->dev.seqs;
   a.n_seq = static_cast<int32_t>(b->seq_ids.size());
   a.total_tokens = b->total_tokens;
   a.k_in = d_keys;
   a.v_in = d_values;
   a.rotate = rotate_keys != 0;
-  a.status = b->d_status;
+  a.status = b->dev.status;
   CU(ctx, launch_append(a, b->stream));
   ++ctx->launches;
   b->layer_done[layer] = 1;
@@ -1101,7 +1164,7 @@ slm_status slm_batch_prefill_attention(slm_batch* b, int32_t layer, const float*
   PrefillLaunch p{};
   p.g = ctx->geom();
   p.layer = layer;
-  p.seqs = b->d_seqs;
+  p.seqs = b->dev.seqs;
   p.n_seq = static_cast<int32_t>(b->seq_ids.size());
   p.total_tokens = b->total_tokens;
   p.q = d_query;
@@ -1138,7 +1201,7 @@ slm_status slm_batch_end(slm_batch* b, int32_t* h_status) {
   std::vector<char> roll(n, 0);
   slm_status first = SLM_OK;
   cudaError_t e =
-      cudaMemcpyAsync(ctx->h_readback, b->d_status, sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
+      cudaMemcpyAsync(ctx->h_readback, b->dev.status, sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
                       b->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
   if (e != cudaSuccess) {

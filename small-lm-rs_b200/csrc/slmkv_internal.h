@@ -17,17 +17,27 @@ struct SeqEntry {
   int32_t base;        // position of the first new token (pre-append length)
   int32_t count;       // new tokens this step
   int32_t row_offset;  // first row of this sequence in the batch's token rows
-  int32_t item_base;   // first split-K work item of this sequence
-  int32_t nsplit;      // split-K work items of this sequence
   int32_t ctx_len;     // tokens attended by the last new token (base + count)
-  int32_t pad;
+  int32_t pad[3];
 };
 
-// One split-K decode work item: a range of blocks of one sequence.
-struct WorkItem {
-  int32_t seq;    // index into the step's SeqEntry array
-  int32_t split;  // 0..nsplit-1
+// Decode plan, one entry per (sequence, KV head) in batch order. The step's
+// blocks form one stream of chunk ids (chunk = physical block * Hkv + head),
+// pair after pair; `blk_begin` is where this pair's blocks start in it.
+struct PairEntry {
+  int32_t seq;         // batch row of q / out / new K,V / status
+  int32_t head;        // KV head
+  int32_t ctx_len;     // tokens attended (the new token sits at ctx_len-1 when fused)
+  int32_t blk_begin;   // first stream index of this pair
+  int32_t nblk;        // stream entries of this pair (= ceil(ctx_len / 16))
+  int32_t part_base;   // first split-K partial slot (when nseg > 1)
+  int32_t first_warp;  // decode warp that owns stream index blk_begin
+  int32_t nseg;        // decode warps covering this pair
 };
+static_assert(sizeof(PairEntry) == 32, "PairEntry is read as two int4");
+
+// Warps per decode CTA (one CTA per SM).
+constexpr int kDecodeWarps = 8;
 
 // Block-table write or copy-on-write job, applied before a step's kernels.
 struct TableUpdate {
@@ -57,28 +67,28 @@ struct PoolGeom {
   int32_t* error;            // context error word (kErr* bits)
 };
 
-// Split-K granularity: blocks per decode work item (32 KiB of K+V staging).
-inline int split_blocks(int bf16) { return bf16 ? 8 : 4; }
 
 // ---- kernel launchers (slmkv_kernels.cu) ----------------------------------
-struct DecodeLaunch {
+struct StreamDecodeLaunch {
   PoolGeom g;
   int32_t layer;
-  const SeqEntry* seqs;
-  const WorkItem* items;
-  int32_t n_seq;
-  int32_t n_items;
+  const PairEntry* pairs;
+  int32_t n_pairs;
+  const int32_t* chunks;          // [total_blocks]
+  int32_t total_blocks;
+  const int32_t* warp_first_pair; // [n_warps]: pair holding the warp's first block
+  int32_t n_warps;                // grid = ceil(n_warps / kDecodeWarps) CTAs
   const float* q;      // [n, Hq, d]
   const float* k_new;  // [n, Hkv, d] (fused mode) or null
   const float* v_new;
   float* out;          // [n, Hq, d]
-  float* part_acc;     // [n_items][Hkv][G][d]
-  float2* part_ml;     // [n_items][Hkv][G]
-  int32_t* counters;   // [n_seq][Hkv], zero between launches
-  int32_t* status;     // [n_seq]
+  float* part_acc;     // [slots][G][d]
+  float2* part_ml;     // [slots][G]  (running max in the exp2 domain, sum)
+  int32_t* counters;   // [n_pairs], zero between launches
+  int32_t* status;     // [n]
   int32_t fused;       // 1: rope(q,k) + append + attend; 0: attend (q rotated)
 };
-cudaError_t launch_decode(const DecodeLaunch& p, int num_sms, cudaStream_t s);
+cudaError_t launch_decode(const StreamDecodeLaunch& p, cudaStream_t s);
 
 struct AppendLaunch {
   PoolGeom g;

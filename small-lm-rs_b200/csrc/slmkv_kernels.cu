@@ -237,232 +237,316 @@ __device__ __forceinline__ void block_softmax_pv(const void* __restrict__ vb, in
 }
 
 // ---------------------------------------------------------------------------
-// Decode: one CTA per (work item, kv head). Work item = up to S blocks of one
-// sequence. All K/V chunks of the item are staged up front by one thread
-// (2*S bulk copies, 32 KiB), each warp consumes blocks w, w+4, ...; the
-// per-warp online-softmax states are merged through shared memory; with
-// several splits the last CTA of a (sequence, head) merges the partials.
+// Decode (stream-K). The host flattens the step into a stream of chunk ids
+// (chunk = physical block * Hkv + kv head; one chunk = 16 tokens of one head)
+// in (sequence, head, block) order, plus one PairEntry per (sequence, head).
+// Every warp of the persistent grid takes an equal slice [g0, g1) of that
+// stream and works alone: lane 0 keeps R bulk copies (K chunk + V chunk per
+// stage) in flight ahead of the warp's own consumption, refilling each stage
+// as soon as the warp has consumed it; no barrier is shared between warps.
+// A (sequence, head) whose blocks span several warps is merged by the last
+// warp to finish it (atomic counter, no waiting).
 // ---------------------------------------------------------------------------
-template <int BF16, int G>
-struct DecodeShape {
+template <int BF16, int G, int W, int R>
+struct StreamShape {
   static constexpr int kEsz = BF16 ? 2 : 4;
   static constexpr int kChunk = kBlockTokens * D * kEsz;
-  static constexpr int kS = BF16 ? 8 : 4;
-  static constexpr int kWarps = 4;
-  static constexpr int kThreads = 32 * kWarps;
-  static constexpr int kStageBytes = 2 * kS * kChunk;
-  static constexpr int kQBytes = G * D * 4;
-  static constexpr int kRedBytes = (2 * kWarps * G + kWarps * G * D) * 4;
-  static constexpr int kBarBytes = kS * 8 + 16;
-  static constexpr int kSmem = kStageBytes + kQBytes + kRedBytes + kBarBytes;
+  static constexpr int kStage = 2 * kChunk;
+  static constexpr int kWarpStages = R * kStage;
+  static constexpr int kQ = G * D * 4;
+  static constexpr int kSmem = W * kWarpStages + W * kQ + W * R * 8;
+  static_assert(kSmem <= 227 * 1024, "decode staging exceeds shared memory");
 };
 
-template <int BF16, int G>
-__global__ void __launch_bounds__(128) decode_kernel(const DecodeLaunch p) {
-  using Sh = DecodeShape<BF16, G>;
+struct PairFields {
+  int seq, head, L, blk_begin, nblk, part_base, first_warp, nseg;
+};
+
+__device__ __forceinline__ PairFields pair_from_window(const int4& a, const int4& b, int k) {
+  PairFields f;
+  f.seq = __shfl_sync(kFull, a.x, k);
+  f.head = __shfl_sync(kFull, a.y, k);
+  f.L = __shfl_sync(kFull, a.z, k);
+  f.blk_begin = __shfl_sync(kFull, a.w, k);
+  f.nblk = __shfl_sync(kFull, b.x, k);
+  f.part_base = __shfl_sync(kFull, b.y, k);
+  f.first_warp = __shfl_sync(kFull, b.z, k);
+  f.nseg = __shfl_sync(kFull, b.w, k);
+  return f;
+}
+
+template <int BF16, int G, int W, int R>
+__global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDecodeLaunch p) {
+  using Sh = StreamShape<BF16, G, W, R>;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* ks = smem;
-  uint8_t* vs = smem + Sh::kS * Sh::kChunk;
-  float* qs = reinterpret_cast<float*>(smem + Sh::kStageBytes);
-  float* red_m = qs + G * D;
-  float* red_l = red_m + Sh::kWarps * G;
-  float* red_acc = red_l + Sh::kWarps * G;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(red_acc + Sh::kWarps * G * D);
-  int* sflag = reinterpret_cast<int*>(bars + Sh::kS);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* stages = smem + warp * Sh::kWarpStages;
+  float* qs = reinterpret_cast<float*>(smem + W * Sh::kWarpStages) + warp * G * D;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + W * Sh::kWarpStages + W * Sh::kQ) + warp * R;
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
-  const int total = p.n_items * Hkv;
+  const int gw = blockIdx.x * W + warp;
+  if (gw >= p.n_warps) return;
+  const int64_t T = p.total_blocks;
+  const int g0 = static_cast<int>(gw * T / p.n_warps);
+  const int g1 = static_cast<int>((gw + 1) * T / p.n_warps);
+  if (g0 >= g1) return;
 
-  if (tid == 0) {
-    for (int s = 0; s < Sh::kS; ++s) mbar_init(&bars[s], 1);
+  if (lane == 0) {
+    for (int s = 0; s < R; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
-    sflag[1] = 0;
   }
-  __syncthreads();
+  __syncwarp();
 
-  uint32_t phase_bits = 0;  // parity to wait for, per stage barrier
-  for (int w = blockIdx.x; w < total; w += gridDim.x) {
-    const int item = w / Hkv, h = w - item * Hkv;
-    const WorkItem wi = p.items[item];
-    const SeqEntry se = p.seqs[wi.seq];
-    const int L = se.ctx_len;
-    const int nblk = (L + kBlockTokens - 1) / kBlockTokens;
-    const int b0 = wi.split * Sh::kS;
-    const int nb = min(nblk, b0 + Sh::kS) - b0;
-    const int pos = se.base;  // fused mode: the new token's position (L - 1)
-    const size_t layer_off = static_cast<size_t>(p.layer) * p.g.layer_elems;
-    const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
+  const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
+  const size_t layer_bytes = static_cast<size_t>(p.layer) * p.g.layer_elems * Sh::kEsz;
+  const uint8_t* kbase = static_cast<const uint8_t*>(p.g.k) + layer_bytes;
+  const uint8_t* vbase = static_cast<const uint8_t*>(p.g.v) + layer_bytes;
+  const uint32_t max_chunk = static_cast<uint32_t>(p.g.num_blocks) * Hkv;
 
-    if (tid == 0) {
-      for (int j = 0; j < nb; ++j) {
-        const int32_t blk = checked_block(p.g, bt[b0 + j]);
-        const size_t off =
-            (layer_off + (static_cast<size_t>(blk) * Hkv + h) * (kBlockTokens * D)) * Sh::kEsz;
-        mbar_arrive_expect_tx(&bars[j], 2 * Sh::kChunk);
-        bulk_load(ks + j * Sh::kChunk, static_cast<const uint8_t*>(p.g.k) + off, Sh::kChunk,
-                  &bars[j]);
-        bulk_load(vs + j * Sh::kChunk, static_cast<const uint8_t*>(p.g.v) + off, Sh::kChunk,
-                  &bars[j]);
-      }
+  // ---- producer: a 32-entry window of chunk ids held one per lane ----------
+  int cwin = g0;
+  int cval = (g0 + lane < g1) ? p.chunks[g0 + lane] : 0;
+  int pg = g0;  // next stream block to issue
+  auto issue = [&](int stage) {
+    if (pg - cwin >= 32) {
+      cwin = pg;
+      cval = (pg + lane < g1) ? p.chunks[pg + lane] : 0;
     }
-
-    // Q heads h*G .. h*G+G-1 of this sequence, rotated at `pos` when fused.
-    {
-      const float* qsrc = p.q + (static_cast<size_t>(wi.seq) * Hq + h * G) * D;
-      for (int i = tid; i < G * (D / 2); i += Sh::kThreads) {
-        const int g = i / (D / 2), pr = i - g * (D / 2);
-        float2 x = reinterpret_cast<const float2*>(qsrc + g * D)[pr];
-        if (p.fused) x = rope_pair(x, p.g.rope[static_cast<size_t>(pos) * (D / 2) + pr]);
-        const int u = (2 * pr) >> 2;
-        *reinterpret_cast<float2*>(qs + g * D + qunit(u) * 4 + ((2 * pr) & 3)) = x;
+    uint32_t chunk = static_cast<uint32_t>(__shfl_sync(kFull, cval, pg - cwin));
+    if (lane == 0) {
+      if (chunk >= max_chunk) {
+        atomicOr(p.g.error, kErrBadBlock);
+        chunk = 0;
       }
+      uint8_t* st = stages + stage * Sh::kStage;
+      mbar_arrive_expect_tx(&bars[stage], Sh::kStage);
+      bulk_load(st, kbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk, &bars[stage]);
+      bulk_load(st + Sh::kChunk, vbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk,
+                &bars[stage]);
     }
-    __syncthreads();
+    ++pg;
+  };
+  for (int s = 0; s < R && pg < g1; ++s) issue(s);
 
-    float m[G], l[G];
-    float2 acc[G];
+  // ---- consumer: pair window (one PairEntry per lane) -----------------------
+  int pi = p.warp_first_pair[gw];
+  int pwin = pi;
+  int4 pa = make_int4(0, 0, 0, 0), pb = make_int4(0, 0, 0, 0);
+  auto load_window = [&](int from) {
+    pwin = from;
+    if (from + lane < p.n_pairs) {
+      const int4* e = reinterpret_cast<const int4*>(p.pairs + from + lane);
+      pa = e[0];
+      pb = e[1];
+    }
+  };
+  load_window(pi);
+  auto fields = [&](int idx) {
+    if (idx - pwin >= 32) load_window(idx);
+    return pair_from_window(pa, pb, idx - pwin);
+  };
+
+  // Per-pair inputs, prefetched one pair ahead: Q (G float2 per lane), the
+  // new K/V row (fused), and the chunk id of the pair's last block.
+  struct Inputs {
+    float2 q[G];
+    float2 kn, vn;
+    int app_chunk;
+  };
+  auto fetch = [&](const PairFields& f, Inputs& in) {
+    const float* qsrc = p.q + (static_cast<size_t>(f.seq) * Hq + f.head * G) * D;
+#pragma unroll
+    for (int g = 0; g < G; ++g) in.q[g] = reinterpret_cast<const float2*>(qsrc + g * D)[lane];
+    const int last = f.blk_begin + f.nblk - 1;
+    if (p.fused && last >= g0 && last < g1) {
+      const size_t src = (static_cast<size_t>(f.seq) * Hkv + f.head) * D;
+      in.kn = reinterpret_cast<const float2*>(p.k_new + src)[lane];
+      in.vn = reinterpret_cast<const float2*>(p.v_new + src)[lane];
+      in.app_chunk = p.chunks[last];
+    }
+  };
+
+  PairFields cur = fields(pi);
+  Inputs cin, nin;
+  fetch(cur, cin);
+  bool have_next = (cur.blk_begin + cur.nblk < g1);
+  PairFields nxt = cur;
+  if (have_next) {
+    nxt = fields(pi + 1);
+    fetch(nxt, nin);
+  }
+
+  float m[G], l[G];
+  float2 acc[G];
+  auto start_pair = [&]() {
+    const int pos = cur.L - 1;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
+      float2 x = cin.q[g];
+      if (p.fused) x = rope_pair(x, p.g.rope[static_cast<size_t>(pos) * (D / 2) + lane]);
+      *reinterpret_cast<float2*>(qs + g * D + qunit(lane >> 1) * 4 + ((2 * lane) & 3)) = x;
       m[g] = -INFINITY;
       l[g] = 0.f;
       acc[g] = make_float2(0.f, 0.f);
     }
-    bool timed_out = false;
-    for (int j = warp; j < nb; j += Sh::kWarps) {
-      if (!mbar_wait_bounded(&bars[j], (phase_bits >> j) & 1u)) {
-        timed_out = true;
-        break;
-      }
-      const int tok0 = (b0 + j) * kBlockTokens;
-      const int nvalid = min(kBlockTokens, L - tok0);
-      uint8_t* kb = ks + j * Sh::kChunk;
-      uint8_t* vb = vs + j * Sh::kChunk;
-      if (p.fused && pos >= tok0 && pos < tok0 + kBlockTokens) {
-        // The append: rotate the new key, store K/V (rounded to the pool's
-        // type) into the staged copy and into the pool.
-        const size_t src = (static_cast<size_t>(wi.seq) * Hkv + h) * D;
-        float2 kx = reinterpret_cast<const float2*>(p.k_new + src)[lane];
-        const float2 vx = reinterpret_cast<const float2*>(p.v_new + src)[lane];
-        const bool fin = finite2(kx) && finite2(vx);
-        kx = rope_pair(kx, p.g.rope[static_cast<size_t>(pos) * (D / 2) + lane]);
-        const int slot = pos - tok0;
-        const int32_t blk = checked_block(p.g, bt[b0 + j]);
-        const size_t dst =
-            layer_off + ((static_cast<size_t>(blk) * Hkv + h) * kBlockTokens + slot) * D;
-        if constexpr (BF16) {
-          const uint32_t kq = pack_bf16x2(kx.x, kx.y), vq = pack_bf16x2(vx.x, vx.y);
-          reinterpret_cast<uint32_t*>(kb)[slot * (D / 2) + lane] = kq;
-          reinterpret_cast<uint32_t*>(vb)[slot * (D / 2) + lane] = vq;
-          reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.k) + dst)[lane] = kq;
-          reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.v) + dst)[lane] = vq;
-        } else {
-          reinterpret_cast<float2*>(kb)[slot * (D / 2) + lane] = kx;
-          reinterpret_cast<float2*>(vb)[slot * (D / 2) + lane] = vx;
-          reinterpret_cast<float2*>(static_cast<float*>(p.g.k) + dst)[lane] = kx;
-          reinterpret_cast<float2*>(static_cast<float*>(p.g.v) + dst)[lane] = vx;
-        }
-        if (!__all_sync(kFull, fin) && lane == 0) atomicOr(&p.status[wi.seq], kStatusNonFinite);
-        __syncwarp();
-      }
-      float sc[G];
-      if constexpr (BF16) {
-        block_scores_bf16<G>(reinterpret_cast<const uint16_t*>(kb), qs, lane, sc);
-      } else {
-        block_scores_f32<G>(reinterpret_cast<const float*>(kb), qs, lane, sc);
-      }
-      block_softmax_pv<G, BF16 != 0>(vb, lane, nvalid, sc, m, l, acc);
-    }
-    if (timed_out && lane == 0) {
-      atomicOr(p.g.error, kErrTimeout);
-      sflag[1] = 1;
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        red_m[warp * G + g] = m[g];
-        red_l[warp * G + g] = l[g];
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-      reinterpret_cast<float2*>(red_acc + (warp * G + g) * D)[lane] = acc[g];
-    // Every stage barrier used by this item has completed once (or timed out).
-    phase_bits ^= (nb >= 32) ? 0xffffffffu : ((1u << nb) - 1u);
-    __syncthreads();
+    __syncwarp();
+  };
+  start_pair();
 
-    if (sflag[1]) {
-      // A wait ran out: give the copies still in flight a bounded chance to
-      // land before the CTA leaves, then stop.
-      if (tid == 0)
-        for (int j = 0; j < nb; ++j) mbar_wait_bounded(&bars[j], ((phase_bits >> j) & 1u) ^ 1u);
+  int seg_end = min(g1, cur.blk_begin + cur.nblk);
+  for (int g = g0, cnt = 0; g < g1; ++g, ++cnt) {
+    const int stage = cnt % R;
+    const uint32_t parity = static_cast<uint32_t>(cnt / R) & 1u;
+    if (!mbar_wait_bounded(&bars[stage], parity)) {
+      // A copy did not land within the limit: record it, give the copies
+      // still in flight a bounded chance to land, and stop this warp.
+      if (lane == 0) {
+        atomicOr(p.g.error, kErrTimeout);
+        for (int c = cnt + 1; c < pg - g0; ++c)
+          mbar_wait_bounded(&bars[c % R], static_cast<uint32_t>(c / R) & 1u);
+      }
+      __syncwarp();
       return;
     }
-
-    const bool single = (se.nsplit == 1);
-    for (int idx = tid; idx < G * D; idx += Sh::kThreads) {
-      const int g = idx / D, dim = idx - g * D;
-      float M = -INFINITY;
-#pragma unroll
-      for (int ww = 0; ww < Sh::kWarps; ++ww) M = fmaxf(M, red_m[ww * G + g]);
-      float Ls = 0.f, A = 0.f;
-#pragma unroll
-      for (int ww = 0; ww < Sh::kWarps; ++ww) {
-        const float f = exp2f(red_m[ww * G + g] - M);  // empty warps: exp2(-inf) = 0
-        Ls = fmaf(red_l[ww * G + g], f, Ls);
-        A = fmaf(red_acc[(ww * G + g) * D + dim], f, A);
+    const int j = g - cur.blk_begin;
+    const int tok0 = j * kBlockTokens;
+    const int nvalid = min(kBlockTokens, cur.L - tok0);
+    uint8_t* kb = stages + stage * Sh::kStage;
+    uint8_t* vb = kb + Sh::kChunk;
+    const bool append_here = p.fused && (j == cur.nblk - 1);
+    if (append_here) {
+      // The append: rotate the new key at position L-1, store K/V (rounded
+      // to the pool's type) into the staged block and into the pool.
+      const int pos = cur.L - 1;
+      const int slot = pos - tok0;
+      const bool fin = finite2(cin.kn) && finite2(cin.vn);
+      const float2 kx = rope_pair(cin.kn, p.g.rope[static_cast<size_t>(pos) * (D / 2) + lane]);
+      uint32_t chunk = static_cast<uint32_t>(cin.app_chunk);
+      if (chunk >= max_chunk) {
+        if (lane == 0) atomicOr(p.g.error, kErrBadBlock);
+        chunk = 0;
       }
-      if (single) {
-        p.out[(static_cast<size_t>(wi.seq) * Hq + h * G + g) * D + dim] = A / Ls;
+      const size_t dst = p.layer * static_cast<size_t>(p.g.layer_elems) +
+                         (static_cast<size_t>(chunk) * kBlockTokens + slot) * D;
+      if constexpr (BF16) {
+        const uint32_t kq = pack_bf16x2(kx.x, kx.y), vq = pack_bf16x2(cin.vn.x, cin.vn.y);
+        reinterpret_cast<uint32_t*>(kb)[slot * (D / 2) + lane] = kq;
+        reinterpret_cast<uint32_t*>(vb)[slot * (D / 2) + lane] = vq;
+        reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.k) + dst)[lane] = kq;
+        reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.v) + dst)[lane] = vq;
       } else {
-        const size_t pi = (static_cast<size_t>(item) * Hkv + h) * G + g;
-        p.part_acc[pi * D + dim] = A;
-        if (dim == 0) p.part_ml[pi] = make_float2(M, Ls);
+        reinterpret_cast<float2*>(kb)[slot * (D / 2) + lane] = kx;
+        reinterpret_cast<float2*>(vb)[slot * (D / 2) + lane] = cin.vn;
+        reinterpret_cast<float2*>(static_cast<float*>(p.g.k) + dst)[lane] = kx;
+        reinterpret_cast<float2*>(static_cast<float*>(p.g.v) + dst)[lane] = cin.vn;
       }
+      if (!__all_sync(kFull, fin) && lane == 0) atomicOr(&p.status[cur.seq], kStatusNonFinite);
+      __syncwarp();
     }
-    if (!single) {
-      __threadfence();
-      __syncthreads();
-      if (tid == 0) {
-        int32_t* ctr = p.counters + static_cast<size_t>(wi.seq) * Hkv + h;
-        const int prev = atomicAdd(ctr, 1);
-        const int last = (prev == se.nsplit - 1);
-        if (last) atomicExch(ctr, 0);  // ready for the next launch
-        sflag[0] = last;
-      }
-      __syncthreads();
-      if (sflag[0]) {
+    float sc[G];
+    if constexpr (BF16) {
+      block_scores_bf16<G>(reinterpret_cast<const uint16_t*>(kb), qs, lane, sc);
+    } else {
+      block_scores_f32<G>(reinterpret_cast<const float*>(kb), qs, lane, sc);
+    }
+    block_softmax_pv<G, BF16 != 0>(vb, lane, nvalid, sc, m, l, acc);
+    __syncwarp();
+    if (pg < g1) {
+      // The stage was just read (and maybe written) through the generic
+      // proxy; order that before the async-proxy refill.
+      if (append_here) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(stage);
+    }
+
+    if (g == seg_end - 1) {
+      // ---- finish this warp's segment of the pair --------------------------
+      if (cur.nseg == 1) {
+#pragma unroll
+        for (int g2 = 0; g2 < G; ++g2) {
+          const float inv = 1.0f / l[g2];
+          reinterpret_cast<float2*>(
+              p.out + (static_cast<size_t>(cur.seq) * Hq + cur.head * G + g2) * D)[lane] =
+              make_float2(acc[g2].x * inv, acc[g2].y * inv);
+        }
+      } else {
+        const int slot = cur.part_base + (gw - cur.first_warp);
+#pragma unroll
+        for (int g2 = 0; g2 < G; ++g2) {
+          reinterpret_cast<float2*>(p.part_acc + (static_cast<size_t>(slot) * G + g2) * D)[lane] =
+              acc[g2];
+          if (lane == 0) p.part_ml[static_cast<size_t>(slot) * G + g2] = make_float2(m[g2], l[g2]);
+        }
         __threadfence();
-        for (int idx = tid; idx < G * D; idx += Sh::kThreads) {
-          const int g = idx / D, dim = idx - g * D;
-          float M = -INFINITY;
-          for (int s = 0; s < se.nsplit; ++s) {
-            const size_t pi = (static_cast<size_t>(se.item_base + s) * Hkv + h) * G + g;
-            M = fmaxf(M, __ldcg(&p.part_ml[pi].x));
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          const int prev = atomicAdd(&p.counters[pi], 1);
+          last = (prev == cur.nseg - 1);
+          if (last) atomicExch(&p.counters[pi], 0);  // ready for the next launch
+        }
+        last = __shfl_sync(kFull, last, 0);
+        if (last) {
+          __threadfence();
+#pragma unroll
+          for (int g2 = 0; g2 < G; ++g2) {
+            float M = -INFINITY;
+            for (int s = lane; s < cur.nseg; s += 32)
+              M = fmaxf(M, __ldcg(&p.part_ml[static_cast<size_t>(cur.part_base + s) * G + g2].x));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, off));
+            float Ls = 0.f;
+            float2 A = make_float2(0.f, 0.f);
+            for (int s = 0; s < cur.nseg; ++s) {
+              const size_t ps = static_cast<size_t>(cur.part_base + s) * G + g2;
+              const float2 ml = __ldcg(&p.part_ml[ps]);
+              const float f = exp2f(ml.x - M);
+              const float2 a = __ldcg(reinterpret_cast<const float2*>(p.part_acc + ps * D) + lane);
+              Ls = fmaf(ml.y, f, Ls);
+              A.x = fmaf(a.x, f, A.x);
+              A.y = fmaf(a.y, f, A.y);
+            }
+            const float inv = 1.0f / Ls;
+            reinterpret_cast<float2*>(
+                p.out + (static_cast<size_t>(cur.seq) * Hq + cur.head * G + g2) * D)[lane] =
+                make_float2(A.x * inv, A.y * inv);
           }
-          float Ls = 0.f, A = 0.f;
-          for (int s = 0; s < se.nsplit; ++s) {
-            const size_t pi = (static_cast<size_t>(se.item_base + s) * Hkv + h) * G + g;
-            const float2 ml = __ldcg(&p.part_ml[pi]);
-            const float f = exp2f(ml.x - M);
-            Ls = fmaf(ml.y, f, Ls);
-            A = fmaf(__ldcg(&p.part_acc[pi * D + dim]), f, A);
-          }
-          p.out[(static_cast<size_t>(wi.seq) * Hq + h * G + g) * D + dim] = A / Ls;
         }
       }
+      if (g + 1 < g1) {
+        // ---- move to the next pair -----------------------------------------
+        ++pi;
+        cur = nxt;
+        cin = nin;
+        seg_end = min(g1, cur.blk_begin + cur.nblk);
+        have_next = (cur.blk_begin + cur.nblk < g1);
+        if (have_next) {
+          nxt = fields(pi + 1);
+          fetch(nxt, nin);
+        }
+        start_pair();
+      }
     }
-    __syncthreads();
   }
 }
 
 template <int BF16, int G>
-cudaError_t launch_decode_t(const DecodeLaunch& p, int /*num_sms*/, cudaStream_t s) {
-  using Sh = DecodeShape<BF16, G>;
-  static_assert(Sh::kSmem <= 48 * 1024, "decode staging must fit the default smem window");
-  const int total = p.n_items * p.g.kv_heads;
-  if (total <= 0) return cudaSuccess;
-  decode_kernel<BF16, G><<<total, Sh::kThreads, Sh::kSmem, s>>>(p);
+cudaError_t launch_decode_t(const StreamDecodeLaunch& p, cudaStream_t s) {
+  constexpr int W = kDecodeWarps;
+  constexpr int R = BF16 ? 6 : 3;
+  using Sh = StreamShape<BF16, G, W, R>;
+  if (p.total_blocks <= 0) return cudaSuccess;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static unsigned long long configured = 0;  // one bit per device
+  if (dev < 64 && !(configured & (1ull << dev))) {
+    e = cudaFuncSetAttribute(decode_stream_kernel<BF16, G, W, R>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::kSmem);
+    if (e != cudaSuccess) return e;
+    configured |= (1ull << dev);
+  }
+  const int ctas = (p.n_warps + W - 1) / W;
+  decode_stream_kernel<BF16, G, W, R><<<ctas, W * 32, Sh::kSmem, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -669,21 +753,21 @@ __global__ void apply_updates_kernel(const PoolGeom g, const TableUpdate* __rest
 
 }  // namespace
 
-cudaError_t launch_decode(const DecodeLaunch& p, int num_sms, cudaStream_t s) {
+cudaError_t launch_decode(const StreamDecodeLaunch& p, cudaStream_t s) {
   const int G = p.g.q_heads / p.g.kv_heads;
   if (p.g.bf16) {
     switch (G) {
-      case 1: return launch_decode_t<1, 1>(p, num_sms, s);
-      case 2: return launch_decode_t<1, 2>(p, num_sms, s);
-      case 4: return launch_decode_t<1, 4>(p, num_sms, s);
-      case 8: return launch_decode_t<1, 8>(p, num_sms, s);
+      case 1: return launch_decode_t<1, 1>(p, s);
+      case 2: return launch_decode_t<1, 2>(p, s);
+      case 4: return launch_decode_t<1, 4>(p, s);
+      case 8: return launch_decode_t<1, 8>(p, s);
     }
   } else {
     switch (G) {
-      case 1: return launch_decode_t<0, 1>(p, num_sms, s);
-      case 2: return launch_decode_t<0, 2>(p, num_sms, s);
-      case 4: return launch_decode_t<0, 4>(p, num_sms, s);
-      case 8: return launch_decode_t<0, 8>(p, num_sms, s);
+      case 1: return launch_decode_t<0, 1>(p, s);
+      case 2: return launch_decode_t<0, 2>(p, s);
+      case 4: return launch_decode_t<0, 4>(p, s);
+      case 8: return launch_decode_t<0, 8>(p, s);
     }
   }
   return cudaErrorInvalidValue;

@@ -133,6 +133,15 @@ def test_fused_decode_matches_oracle_small(kv_dtype):
     assert err <= TOL[kv_dtype], err
 
 
+def test_fused_decode_many_short_sequences():
+    """More sequences than decode warps have blocks: warps own zero or one
+    block, every (sequence, head) is a single-block pair."""
+    rng = np.random.default_rng(31)
+    lengths = rng.choice([0, 1, 14, 15, 16], size=300).tolist()
+    err = _decode_case(slmkv.KV_F32, lengths, layers=1, seed=33)
+    assert err <= 1e-4, err
+
+
 @pytest.mark.parametrize("hq,hkv", [(4, 4), (8, 2), (16, 2)])
 def test_fused_decode_group_sizes(hq, hkv):
     err = _decode_case(slmkv.KV_F32, [3, 40, 257, 511], layers=1, hq=hq, hkv=hkv, seed=9)
