@@ -290,43 +290,47 @@ def run_ours(args):
     out = torch.empty((LAYERS, B, HQ, D), device=dev)
     base = [int(x) for x in lengths]
     stream = torch.cuda.current_stream()
+    plan = pool.step_plan(caches, 1)
+    base_arr = plan.lengths(base)
+    ptrs = [(q[l].data_ptr(), kn[l].data_ptr(), vn[l].data_ptr(), out[l].data_ptr())
+            for l in range(LAYERS)]
+    # Kernel timing events, created up front (creation is not part of a step).
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps * LAYERS)]
 
-    kernel_events = []
-
-    def step(timed: bool, qq=q, kk=kn, vv=vn, oo=out):
-        batch = pool.begin(caches, 1)
+    def step(timed_index=None, layer_ptrs=ptrs):
+        batch = plan.begin()
         for layer in range(LAYERS):
-            if timed:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
+            if timed_index is not None:
+                e0, e1 = ev[timed_index * LAYERS + layer]
                 e0.record(stream)
-            batch.decode_layer(layer, qq[layer], kk[layer], vv[layer], oo[layer])
-            if timed:
+                batch.decode_layer_ptr(layer, *layer_ptrs[layer])
                 e1.record(stream)
-                kernel_events.append((e0, e1))
+            else:
+                batch.decode_layer_ptr(layer, *layer_ptrs[layer])
         batch.end()
-        pool.truncate_many(caches, base)
+        plan.truncate_all(base_arr)
 
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.start()
     for _ in range(max(args.warmup, 3)):
-        step(False)
+        step()
     torch.cuda.synchronize()
     barrier()
     launches0 = pool.launch_count()
     t_start = torch.cuda.Event(enable_timing=True)
     t_stop = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
-    for _ in range(args.steps):
-        step(True)
+    for i in range(args.steps):
+        step(i)
     t_stop.record(stream)
     torch.cuda.synchronize()
     barrier()
     launches = pool.launch_count() - launches0
     clocks = sampler.stop() if sampler else None
     ms = t_start.elapsed_time(t_stop)
-    kern_ms = [a.elapsed_time(b) for a, b in kernel_events]
+    kern_ms = [a.elapsed_time(b) for a, b in ev]
     kern_avg_ms = sum(kern_ms) / len(kern_ms)
     if world > 1:
         t = torch.tensor([ms, kern_avg_ms], device=dev, dtype=torch.float64)
@@ -341,16 +345,19 @@ def run_ours(args):
     ho_ = torch.empty_like(out, device="cpu").pin_memory()
     dq, dk, dv, do = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn), torch.empty_like(out)
 
+    dptrs = [(dq[l].data_ptr(), dk[l].data_ptr(), dv[l].data_ptr(), do[l].data_ptr())
+             for l in range(LAYERS)]
+
     def e2e_step():
         dq.copy_(hq_, non_blocking=True)
         dk.copy_(hk_, non_blocking=True)
         dv.copy_(hv_, non_blocking=True)
-        batch = pool.begin(caches, 1)
+        batch = plan.begin()
         for layer in range(LAYERS):
-            batch.decode_layer(layer, dq[layer], dk[layer], dv[layer], do[layer])
+            batch.decode_layer_ptr(layer, *dptrs[layer])
         ho_.copy_(do, non_blocking=True)
         batch.end()
-        pool.truncate_many(caches, base)
+        plan.truncate_all(base_arr)
 
     for _ in range(3):
         e2e_step()

@@ -417,7 +417,10 @@ void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, i
     }
   }
   const int64_t T = static_cast<int64_t>(plan.chunks.size());
-  const int64_t NW = n_warps;
+  // Never more warps than blocks: then every warp owns at least one block and
+  // the warps covering a pair are consecutive, so a pair's segment index is
+  // simply (warp - first_warp).
+  const int64_t NW = std::min<int64_t>(n_warps, T);
   // Warp owning stream index x: the largest w with floor(w*T/NW) <= x.
   auto owner = [&](int64_t x) { return static_cast<int32_t>(((x + 1) * NW - 1) / T); };
   int32_t part = 0;
@@ -427,7 +430,7 @@ void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, i
     pe.part_base = part;
     if (pe.nseg > 1) part += pe.nseg;
   }
-  plan.warp_first_pair.assign(n_warps, -1);
+  plan.warp_first_pair.assign(static_cast<size_t>(NW), -1);
   size_t pc = 0;
   for (int64_t w = 0; w < NW; ++w) {
     const int64_t b = w * T / NW, e = (w + 1) * T / NW;

@@ -288,6 +288,10 @@ class KvPool:
               stream=None) -> "Batch":
         return Batch(self, caches, token_counts, stream)
 
+    def step_plan(self, caches: Sequence["KvCache"],
+                  token_counts: Sequence[int] | int = 1) -> "StepPlan":
+        return StepPlan(self, caches, token_counts)
+
     def truncate_many(self, caches: Sequence["KvCache"], lengths: Sequence[int]) -> None:
         """truncate_all (kv_cache.rs:302-321) for many caches in one call."""
         ids = _i32_array([c.seq_id for c in caches])
@@ -436,30 +440,66 @@ class KvCache:
         return n.value
 
 
+class _Fast:
+    """ctypes entry points bound once, for the per-step calls."""
+
+    def __init__(self):
+        self._bound = False
+
+    def bind(self):
+        L = lib()
+        self.begin = L.slm_batch_begin
+        self.decode = L.slm_batch_decode_layer
+        self.end = L.slm_batch_end
+        self.truncate = L.slm_seqs_truncate_all
+        self._bound = True
+
+    def __getattr__(self, name):
+        if name.startswith("_"):
+            raise AttributeError(name)
+        self.bind()
+        return object.__getattribute__(self, name)
+
+
+_fast = _Fast()
+
+
 class Batch:
     """One step over many caches (``slm_batch_*``). Use as a context manager:
     leaving the block normally ends (commits) it, an exception rolls it back."""
 
     def __init__(self, pool: KvPool, caches: Sequence[KvCache],
-                 token_counts: Sequence[int] | int = 1, stream=None):
+                 token_counts: Sequence[int] | int = 1, stream=None, *, _arrays=None):
         self.pool = pool
-        self.caches = list(caches)
+        self.caches = caches if _arrays is not None else list(caches)
         n = len(self.caches)
-        if isinstance(token_counts, int):
-            token_counts = [token_counts] * n
-        self.token_counts = [int(t) for t in token_counts]
-        self._ids = _i32_array([c.seq_id for c in self.caches])
-        self._counts = _i32_array(self.token_counts)
-        self._status = (C.c_int32 * max(1, n))()
+        if _arrays is not None:
+            self._ids, self._counts, self._status, self.token_counts = _arrays
+        else:
+            if isinstance(token_counts, int):
+                token_counts = [token_counts] * n
+            self.token_counts = [int(t) for t in token_counts]
+            self._ids = _i32_array([c.seq_id for c in self.caches])
+            self._counts = _i32_array(self.token_counts)
+            self._status = (C.c_int32 * max(1, n))()
         h = C.c_void_p()
-        pool.check(lib().slm_batch_begin(pool.handle, n, self._ids, self._counts,
-                                         _stream_ptr(stream), C.byref(h)))
+        rc = _fast.begin(pool.handle, n, self._ids, self._counts, _stream_ptr(stream),
+                         C.byref(h))
+        if rc:
+            pool.check(rc)
         self._h = h
         self.statuses: list[int] | None = None
 
     def decode_layer(self, layer: int, query, keys, values, out) -> None:
         self.pool.check(lib().slm_batch_decode_layer(self._h, int(layer), _ptr(query),
                                                      _ptr(keys), _ptr(values), _ptr(out)))
+
+    def decode_layer_ptr(self, layer: int, query: int, keys: int, values: int, out: int) -> None:
+        """decode_layer with raw device addresses (for callers that checked
+        their tensors once, e.g. a serving loop's persistent buffers)."""
+        rc = _fast.decode(self._h, layer, query, keys, values, out)
+        if rc:
+            self.pool.check(rc)
 
     def append_layer(self, layer: int, keys, values, rotate_keys: bool = True) -> None:
         self.pool.check(lib().slm_batch_append_layer(self._h, int(layer), _ptr(keys),
@@ -472,7 +512,7 @@ class Batch:
     def end(self, raise_on_error: bool = True) -> list[int]:
         if self._h is None:
             return self.statuses or []
-        rc = lib().slm_batch_end(self._h, self._status)
+        rc = _fast.end(self._h, self._status)
         self._h = None
         self.statuses = list(self._status[: len(self.caches)])
         if rc != OK and raise_on_error:
@@ -493,3 +533,37 @@ class Batch:
             self.end()
         else:
             self.rollback()
+
+
+class StepPlan:
+    """A fixed set of caches stepped repeatedly (a running batch): the id,
+    count and status arrays handed to the library are built once."""
+
+    def __init__(self, pool: KvPool, caches: Sequence[KvCache],
+                 token_counts: Sequence[int] | int = 1):
+        self.pool = pool
+        self.caches = list(caches)
+        n = len(self.caches)
+        if isinstance(token_counts, int):
+            token_counts = [token_counts] * n
+        self.token_counts = [int(t) for t in token_counts]
+        self._ids = _i32_array([c.seq_id for c in self.caches])
+        self._counts = _i32_array(self.token_counts)
+        self._status = (C.c_int32 * max(1, n))()
+        self._stream = None
+
+    def begin(self, stream=None) -> Batch:
+        return Batch(self.pool, self.caches, stream=stream,
+                     _arrays=(self._ids, self._counts, self._status, self.token_counts))
+
+    def lengths(self, lengths: Sequence[int]):
+        """A reusable length array for truncate_all."""
+        return _i32_array(lengths)
+
+    def truncate_all(self, lengths) -> None:
+        """truncate_all (kv_cache.rs:302-321) for every cache of the plan;
+        `lengths` is a sequence or an array from `lengths()`."""
+        arr = lengths if isinstance(lengths, C.Array) else _i32_array(lengths)
+        rc = _fast.truncate(self.pool.handle, len(self.caches), self._ids, arr)
+        if rc:
+            self.pool.check(rc)
