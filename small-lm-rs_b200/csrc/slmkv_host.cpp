@@ -58,7 +58,7 @@ struct Upload {
 struct StreamPlan {
   std::vector<PairEntry> pairs;
   std::vector<int32_t> chunks;
-  std::vector<int32_t> warp_first_pair;
+  std::vector<int4> warp_start;  // 2 per warp: {first pair, seq, head, ctx_len}, {pair end, 0, 0, 0}
 };
 
 // Device addresses of one uploaded step descriptor.
@@ -67,10 +67,11 @@ struct StepDev {
   int32_t* status = nullptr;
   PairEntry* pairs = nullptr;
   int32_t* chunks = nullptr;
-  int32_t* wfp = nullptr;
+  int4* wfp = nullptr;  // warp start records
 };
 
 size_t align16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 uint64_t mix64(uint64_t x) {  // splitmix64 finaliser
   x += 0x9e3779b97f4a7c15ull;
@@ -351,7 +352,7 @@ cudaError_t upload_end(Upload& u, size_t bytes, cudaStream_t s) {
   return e;
 }
 
-// Layout of one upload: [seqs][status][pairs][chunks][warp_first_pair]
+// Layout of one upload: [seqs][status][pairs][chunks][warp start records]
 // [table updates][copy jobs].
 struct DescLayout {
   size_t seqs = 0, status = 0, pairs = 0, chunks = 0, wfp = 0, updates = 0, copies = 0, total = 0;
@@ -364,7 +365,7 @@ DescLayout desc_layout(size_t n, size_t n_pairs, size_t n_chunks, size_t n_warps
   L.pairs = align16(L.status + sizeof(int32_t) * n);
   L.chunks = align16(L.pairs + sizeof(PairEntry) * n_pairs);
   L.wfp = align16(L.chunks + sizeof(int32_t) * n_chunks);
-  L.updates = align16(L.wfp + sizeof(int32_t) * n_warps);
+  L.updates = align16(L.wfp + 2 * sizeof(int4) * n_warps);
   L.copies = align16(L.updates + sizeof(TableUpdate) * nu);
   L.total = align16(L.copies + sizeof(CopyJob) * nc);
   return L;
@@ -423,20 +424,26 @@ void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, i
   const int64_t NW = std::min<int64_t>(n_warps, T);
   // Warp owning stream index x: the largest w with floor(w*T/NW) <= x.
   auto owner = [&](int64_t x) { return static_cast<int32_t>(((x + 1) * NW - 1) / T); };
+  // Pairs merge per CTA first (kDecodeWarps consecutive warps); a pair that
+  // spans CTAs gets one global partial slot per CTA it touches.
   int32_t part = 0;
   for (PairEntry& pe : plan.pairs) {
     pe.first_warp = owner(pe.blk_begin);
-    pe.nseg = owner(pe.blk_begin + pe.nblk - 1) - pe.first_warp + 1;
+    const int32_t last_warp = owner(pe.blk_begin + pe.nblk - 1);
+    pe.nseg = last_warp - pe.first_warp + 1;
+    if (pe.first_warp * T / NW == pe.blk_begin) pe.nseg |= (1 << 30);
     pe.part_base = part;
-    if (pe.nseg > 1) part += pe.nseg;
+    const int32_t n_cta = last_warp / kDecodeWarps - pe.first_warp / kDecodeWarps + 1;
+    if (n_cta > 1) part += n_cta;
   }
-  plan.warp_first_pair.assign(static_cast<size_t>(NW), -1);
+  plan.warp_start.assign(static_cast<size_t>(2 * NW), make_int4(0, 0, 0, 0));
   size_t pc = 0;
   for (int64_t w = 0; w < NW; ++w) {
-    const int64_t b = w * T / NW, e = (w + 1) * T / NW;
-    if (b >= e) continue;
+    const int64_t b = w * T / NW;
     while (plan.pairs[pc].blk_begin + plan.pairs[pc].nblk <= b) ++pc;
-    plan.warp_first_pair[w] = static_cast<int32_t>(pc);
+    const PairEntry& pe = plan.pairs[pc];
+    plan.warp_start[2 * w] = make_int4(static_cast<int32_t>(pc), pe.seq, pe.head, pe.ctx_len);
+    plan.warp_start[2 * w + 1] = make_int4(pe.blk_begin + pe.nblk, 0, 0, 0);
   }
 }
 
@@ -448,7 +455,7 @@ slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<
   if (rc) return rc;
   const size_t n = entries.size();
   const size_t np = plan ? plan->pairs.size() : 0, nch = plan ? plan->chunks.size() : 0;
-  const size_t nw = plan ? plan->warp_first_pair.size() : 0;
+  const size_t nw = plan ? plan->warp_start.size() / 2 : 0;
   const size_t nu = c->pending_updates.size(), nc = c->pending_copies.size();
   DescLayout L = desc_layout(n, np, nch, nw, nu, nc);
   if (L.total > u.cap)
@@ -458,7 +465,7 @@ slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<
   memset(h + L.status, 0, sizeof(int32_t) * n);
   if (np) memcpy(h + L.pairs, plan->pairs.data(), sizeof(PairEntry) * np);
   if (nch) memcpy(h + L.chunks, plan->chunks.data(), sizeof(int32_t) * nch);
-  if (nw) memcpy(h + L.wfp, plan->warp_first_pair.data(), sizeof(int32_t) * nw);
+  if (nw) memcpy(h + L.wfp, plan->warp_start.data(), sizeof(int4) * 2 * nw);
   if (nu) memcpy(h + L.updates, c->pending_updates.data(), nu * sizeof(TableUpdate));
   if (nc) memcpy(h + L.copies, c->pending_copies.data(), nc * sizeof(CopyJob));
   CU(c, upload_end(u, L.total, s));
@@ -474,7 +481,7 @@ slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<
   dev->status = reinterpret_cast<int32_t*>(u.d + L.status);
   dev->pairs = reinterpret_cast<PairEntry*>(u.d + L.pairs);
   dev->chunks = reinterpret_cast<int32_t*>(u.d + L.chunks);
-  dev->wfp = reinterpret_cast<int32_t*>(u.d + L.wfp);
+  dev->wfp = reinterpret_cast<int4*>(u.d + L.wfp);
   return SLM_OK;
 }
 
@@ -488,8 +495,8 @@ StreamDecodeLaunch decode_launch(slm_ctx* c, int32_t layer, const StepDev& dev,
   p.n_pairs = static_cast<int32_t>(plan.pairs.size());
   p.chunks = dev.chunks;
   p.total_blocks = static_cast<int32_t>(plan.chunks.size());
-  p.warp_first_pair = dev.wfp;
-  p.n_warps = static_cast<int32_t>(plan.warp_first_pair.size());
+  p.warp_start = dev.wfp;
+  p.n_warps = static_cast<int32_t>(plan.warp_start.size() / 2);
   p.part_acc = c->d_part_acc;
   p.part_ml = c->d_part_ml;
   p.counters = c->d_counters;
@@ -967,6 +974,9 @@ slm_status slm_attend_cached_query(slm_ctx* ctx, int32_t seq_id, int32_t layer,
   if (layer < 0 || layer >= ctx->cfg.num_layers)
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache", "layer index %d is outside 0..%d",
                        layer, ctx->cfg.num_layers);
+  if (!d_query || !d_out || !aligned16(d_query) || !aligned16(d_out))
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention",
+                       "query and output buffers must be non-null and 16-byte aligned");
   const int32_t L = q->layer_len[layer];
   if (L == 0)  // attention.rs:690-695
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention",
@@ -1110,6 +1120,9 @@ slm_status slm_batch_decode_layer(slm_batch* b, int32_t layer, const float* d_qu
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "layer %d was already appended", layer);
   if (!d_query || !d_keys || !d_values || !d_out)
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "null tensor");
+  if (!aligned16(d_query) || !aligned16(d_keys) || !aligned16(d_values) || !aligned16(d_out))
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
+                       "query, key, value and output buffers must be 16-byte aligned");
   StreamDecodeLaunch p = decode_launch(ctx, layer, b->dev, ctx->plan);
   p.q = d_query;
   p.k_new = d_keys;

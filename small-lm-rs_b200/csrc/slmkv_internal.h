@@ -32,7 +32,8 @@ struct PairEntry {
   int32_t nblk;        // stream entries of this pair (= ceil(ctx_len / 16))
   int32_t part_base;   // first split-K partial slot (when nseg > 1)
   int32_t first_warp;  // decode warp that owns stream index blk_begin
-  int32_t nseg;        // decode warps covering this pair
+  int32_t nseg;        // decode warps covering this pair; bit 30 set when the
+                       // pair starts exactly where its first warp's range starts
 };
 static_assert(sizeof(PairEntry) == 32, "PairEntry is read as two int4");
 
@@ -76,7 +77,8 @@ struct StreamDecodeLaunch {
   int32_t n_pairs;
   const int32_t* chunks;          // [total_blocks]
   int32_t total_blocks;
-  const int32_t* warp_first_pair; // [n_warps]: pair holding the warp's first block
+  const int4* warp_start;         // [2 * n_warps]: {first pair, seq, head,
+                                  //  ctx_len}, {first pair's end in the stream, 0, 0, 0}
   int32_t n_warps;                // grid = ceil(n_warps / kDecodeWarps) CTAs
   const float* q;      // [n, Hq, d]
   const float* k_new;  // [n, Hkv, d] (fused mode) or null

@@ -76,7 +76,7 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 // Waits for phase `parity` of `bar` for at most ~1 s (and a fixed iteration
 // cap); returns false when the limit ran out.
-__device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer_ns();
   for (uint32_t i = 0; i < (1u << 24); ++i) {
@@ -84,6 +84,16 @@ __device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
     if ((i & 31u) == 0 && globaltimer_ns() - start > kWaitLimitNs) break;
   }
   return false;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity);
+}
+
+// 2^x on the MUFU unit (scores live in the exp2 domain); ex2(-inf) = +0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // ---------------------------------------------------------------------------
@@ -136,8 +146,9 @@ __device__ __forceinline__ void block_scores_f32(const float* __restrict__ kb,
                                                  float (&sc)[G]) {
   const int t = lane & 15, hh = lane >> 4;
   const float* krow = kb + t * D + hh * 32;
+  float a0[G], a1[G];  // two chains per head halve the dependent FMA depth
 #pragma unroll
-  for (int g = 0; g < G; ++g) sc[g] = 0.f;
+  for (int g = 0; g < G; ++g) a0[g] = a1[g] = 0.f;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int c = (j + t) & 7;
@@ -146,14 +157,17 @@ __device__ __forceinline__ void block_scores_f32(const float* __restrict__ kb,
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const float4 q4 = *reinterpret_cast<const float4*>(qs + g * D + pu * 4);
-      sc[g] = fmaf(q4.x, k4.x, sc[g]);
-      sc[g] = fmaf(q4.y, k4.y, sc[g]);
-      sc[g] = fmaf(q4.z, k4.z, sc[g]);
-      sc[g] = fmaf(q4.w, k4.w, sc[g]);
+      a0[g] = fmaf(q4.x, k4.x, a0[g]);
+      a1[g] = fmaf(q4.y, k4.y, a1[g]);
+      a0[g] = fmaf(q4.z, k4.z, a0[g]);
+      a1[g] = fmaf(q4.w, k4.w, a1[g]);
     }
   }
 #pragma unroll
-  for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(kFull, sc[g], 16);
+  for (int g = 0; g < G; ++g) {
+    sc[g] = a0[g] + a1[g];
+    sc[g] += __shfl_xor_sync(kFull, sc[g], 16);
+  }
 }
 
 template <int G>
@@ -162,8 +176,9 @@ __device__ __forceinline__ void block_scores_bf16(const uint16_t* __restrict__ k
                                                   float (&sc)[G]) {
   const int t = lane & 15, hh = lane >> 4;
   const uint16_t* krow = kb + t * D;
+  float a0[G], a1[G];
 #pragma unroll
-  for (int g = 0; g < G; ++g) sc[g] = 0.f;
+  for (int g = 0; g < G; ++g) a0[g] = a1[g] = 0.f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int c = (2 * j + hh + t) & 7;  // chunk of 8 dims
@@ -175,28 +190,32 @@ __device__ __forceinline__ void block_scores_bf16(const uint16_t* __restrict__ k
     for (int g = 0; g < G; ++g) {
       const float4 qa = *reinterpret_cast<const float4*>(qs + g * D + p0 * 4);
       const float4 qb = *reinterpret_cast<const float4*>(qs + g * D + p1 * 4);
-      sc[g] = fmaf(qa.x, k0, sc[g]);
-      sc[g] = fmaf(qa.y, k1, sc[g]);
-      sc[g] = fmaf(qa.z, k2, sc[g]);
-      sc[g] = fmaf(qa.w, k3, sc[g]);
-      sc[g] = fmaf(qb.x, k4, sc[g]);
-      sc[g] = fmaf(qb.y, k5, sc[g]);
-      sc[g] = fmaf(qb.z, k6, sc[g]);
-      sc[g] = fmaf(qb.w, k7, sc[g]);
+      a0[g] = fmaf(qa.x, k0, a0[g]);
+      a1[g] = fmaf(qa.y, k1, a1[g]);
+      a0[g] = fmaf(qa.z, k2, a0[g]);
+      a1[g] = fmaf(qa.w, k3, a1[g]);
+      a0[g] = fmaf(qb.x, k4, a0[g]);
+      a1[g] = fmaf(qb.y, k5, a1[g]);
+      a0[g] = fmaf(qb.z, k6, a0[g]);
+      a1[g] = fmaf(qb.w, k7, a1[g]);
     }
   }
 #pragma unroll
-  for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(kFull, sc[g], 16);
+  for (int g = 0; g < G; ++g) {
+    sc[g] = a0[g] + a1[g];
+    sc[g] += __shfl_xor_sync(kFull, sc[g], 16);
+  }
 }
 
 // Online-softmax update for one block, then P·V (lane owns dims 2l, 2l+1).
 // sc: raw dot products for token lane&15; nvalid >= 1 tokens are real.
+// pbuf: this warp's G*16 floats of shared memory for the probabilities.
+// Rows at or past nvalid are never multiplied (they may hold stale data).
 template <int G, bool BF16V>
-__device__ __forceinline__ void block_softmax_pv(const void* __restrict__ vb, int lane, int nvalid,
-                                                 const float (&sc)[G], float (&m)[G],
+__device__ __forceinline__ void block_softmax_pv(const void* __restrict__ vb, float* pbuf, int lane,
+                                                 int nvalid, const float (&sc)[G], float (&m)[G],
                                                  float (&l)[G], float2 (&acc)[G]) {
   const int t = lane & 15;
-  float pr[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     const float s = (t < nvalid) ? sc[g] * kScaleLog2 : -INFINITY;
@@ -206,8 +225,9 @@ __device__ __forceinline__ void block_softmax_pv(const void* __restrict__ vb, in
     mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 2));
     mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 1));
     const float mnew = fmaxf(m[g], mb);  // finite: nvalid >= 1
-    const float corr = exp2f(m[g] - mnew);
-    const float p = exp2f(s - mnew);
+    const float corr = fast_exp2(m[g] - mnew);
+    const float p = fast_exp2(s - mnew);
+    if (lane < 16) pbuf[g * 16 + t] = p;
     float ps = p;
     ps += __shfl_xor_sync(kFull, ps, 8);
     ps += __shfl_xor_sync(kFull, ps, 4);
@@ -217,23 +237,45 @@ __device__ __forceinline__ void block_softmax_pv(const void* __restrict__ vb, in
     acc[g].x *= corr;
     acc[g].y *= corr;
     m[g] = mnew;
-    pr[g] = p;
   }
-  for (int tt = 0; tt < nvalid; ++tt) {
-    float2 v2;
+  __syncwarp();
+  auto vrow = [&](int tt) {
     if constexpr (BF16V) {
       const uint32_t w = reinterpret_cast<const uint32_t*>(vb)[tt * (D / 2) + lane];
-      v2 = make_float2(bf16lo(w), bf16hi(w));
+      return make_float2(bf16lo(w), bf16hi(w));
     } else {
-      v2 = reinterpret_cast<const float2*>(vb)[tt * (D / 2) + lane];
+      return reinterpret_cast<const float2*>(vb)[tt * (D / 2) + lane];
     }
+  };
+  if (nvalid == kBlockTokens) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float pt = __shfl_sync(kFull, pr[g], tt);
-      acc[g].x = fmaf(pt, v2.x, acc[g].x);
-      acc[g].y = fmaf(pt, v2.y, acc[g].y);
+    for (int t4 = 0; t4 < kBlockTokens; t4 += 4) {
+      const float2 v0 = vrow(t4), v1 = vrow(t4 + 1), v2 = vrow(t4 + 2), v3 = vrow(t4 + 3);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float4 p4 = *reinterpret_cast<const float4*>(pbuf + g * 16 + t4);
+        acc[g].x = fmaf(p4.x, v0.x, acc[g].x);
+        acc[g].y = fmaf(p4.x, v0.y, acc[g].y);
+        acc[g].x = fmaf(p4.y, v1.x, acc[g].x);
+        acc[g].y = fmaf(p4.y, v1.y, acc[g].y);
+        acc[g].x = fmaf(p4.z, v2.x, acc[g].x);
+        acc[g].y = fmaf(p4.z, v2.y, acc[g].y);
+        acc[g].x = fmaf(p4.w, v3.x, acc[g].x);
+        acc[g].y = fmaf(p4.w, v3.y, acc[g].y);
+      }
+    }
+  } else {
+    for (int tt = 0; tt < nvalid; ++tt) {
+      const float2 v2 = vrow(tt);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pt = pbuf[g * 16 + tt];
+        acc[g].x = fmaf(pt, v2.x, acc[g].x);
+        acc[g].y = fmaf(pt, v2.y, acc[g].y);
+      }
     }
   }
+  __syncwarp();  // pbuf is rewritten by the next block
 }
 
 // ---------------------------------------------------------------------------
@@ -250,16 +292,30 @@ __device__ __forceinline__ void block_softmax_pv(const void* __restrict__ vb, in
 template <int BF16, int G, int W, int R>
 struct StreamShape {
   static constexpr int kEsz = BF16 ? 2 : 4;
-  static constexpr int kChunk = kBlockTokens * D * kEsz;
+  static constexpr int kChunk = kBlockTokens * D * kEsz;  // one block of one head, K or V
   static constexpr int kStage = 2 * kChunk;
-  static constexpr int kWarpStages = R * kStage;
-  static constexpr int kQ = G * D * 4;
-  static constexpr int kSmem = W * kWarpStages + W * kQ + W * R * 8;
+  // Side buffer of a stage: the pair's Q rows, its RoPE row and its new K/V
+  // rows, copied together with the pair's first block in this warp.
+  static constexpr int kSideCs = G * D * 4;
+  static constexpr int kSideKn = kSideCs + (D / 2) * 8;
+  static constexpr int kSideVn = kSideKn + D * 4;
+  static constexpr int kSide = kSideVn + D * 4;
+  static constexpr int kSlot = ((G * D * 4 + G * 8) + 15) / 16 * 16;  // one segment partial
+  static constexpr int kOffSide = W * R * kStage;
+  static constexpr int kOffQ = kOffSide + W * R * kSide;
+  static constexpr int kOffP = kOffQ + W * G * D * 4;
+  static constexpr int kOffSlots = kOffP + W * G * kBlockTokens * 4;
+  static constexpr int kOffBars = kOffSlots + 2 * W * kSlot;
+  static constexpr int kOffChunk = kOffBars + W * R * 8;
+  static constexpr int kOffCnt = kOffChunk + W * R * 4;
+  static constexpr int kSmem = kOffCnt + 2 * W * 4;
   static_assert(kSmem <= 227 * 1024, "decode staging exceeds shared memory");
+  static_assert(kChunk % 16 == 0 && kSide % 16 == 0 && kSlot % 16 == 0, "16-byte alignment");
 };
 
 struct PairFields {
   int seq, head, L, blk_begin, nblk, part_base, first_warp, nseg;
+  int at_warp_start;  // the pair's first block is its first warp's first block
 };
 
 __device__ __forceinline__ PairFields pair_from_window(const int4& a, const int4& b, int k) {
@@ -271,8 +327,61 @@ __device__ __forceinline__ PairFields pair_from_window(const int4& a, const int4
   f.nblk = __shfl_sync(kFull, b.x, k);
   f.part_base = __shfl_sync(kFull, b.y, k);
   f.first_warp = __shfl_sync(kFull, b.z, k);
-  f.nseg = __shfl_sync(kFull, b.w, k);
+  const int ns = __shfl_sync(kFull, b.w, k);
+  f.nseg = ns & 0x3fffffff;
+  f.at_warp_start = (ns >> 30) & 1;
   return f;
+}
+
+// Merges n segment partials (each G x (acc[64], (m, l))) for this lane's two
+// output dims: partial s is weighted by 2^(m_s - M), summed in slot order.
+// acc_at(s, g) / ml_at(s, g) read one partial; the (m, l) pairs are loaded
+// lane-parallel and the acc loads are issued four at a time.
+template <int G, typename Acc, typename Ml>
+__device__ __forceinline__ void merge_partials(int n, int lane, Acc acc_at, Ml ml_at, float2 (&A)[G],
+                                               float (&Mo)[G], float (&Lo)[G]) {
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float M = -INFINITY, Ls = 0.f;
+    float2 a2 = make_float2(0.f, 0.f);
+    for (int base = 0; base < n; base += 32) {
+      const int cnt = min(32, n - base);
+      const float2 mine = (lane < cnt) ? ml_at(base + lane, g) : make_float2(-INFINITY, 0.f);
+      float Mc = mine.x;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) Mc = fmaxf(Mc, __shfl_xor_sync(kFull, Mc, off));
+      const float Mn = fmaxf(M, Mc);
+      const float rescale = exp2f(M - Mn);  // M = -inf on the first chunk: 0
+      a2.x *= rescale;
+      a2.y *= rescale;
+      Ls *= rescale;
+      M = Mn;
+      const float fmine = exp2f(mine.x - M);  // lanes past cnt: 0
+      float lsum = mine.y * fmine;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(kFull, lsum, off);
+      Ls += lsum;
+      for (int s0 = 0; s0 < cnt; s0 += 4) {
+        float2 a[4];
+        float f[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          f[u] = __shfl_sync(kFull, fmine, min(s0 + u, 31));
+          a[u] = (s0 + u < cnt) ? acc_at(base + s0 + u, g) : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (s0 + u < cnt) {
+            a2.x = fmaf(a[u].x, f[u], a2.x);
+            a2.y = fmaf(a[u].y, f[u], a2.y);
+          }
+        }
+      }
+    }
+    A[g] = a2;
+    Mo[g] = M;
+    Lo[g] = Ls;
+  }
 }
 
 template <int BF16, int G, int W, int R>
@@ -280,16 +389,34 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
   using Sh = StreamShape<BF16, G, W, R>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* stages = smem + warp * Sh::kWarpStages;
-  float* qs = reinterpret_cast<float*>(smem + W * Sh::kWarpStages) + warp * G * D;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + W * Sh::kWarpStages + W * Sh::kQ) + warp * R;
+  uint8_t* stages = smem + warp * R * Sh::kStage;
+  uint8_t* sides = smem + Sh::kOffSide + warp * R * Sh::kSide;
+  float* qs = reinterpret_cast<float*>(smem + Sh::kOffQ) + warp * G * D;
+  float* pbuf = reinterpret_cast<float*>(smem + Sh::kOffP) + warp * G * kBlockTokens;
+  uint8_t* slots = smem + Sh::kOffSlots;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sh::kOffBars) + warp * R;
+  int* stage_chunk = reinterpret_cast<int*>(smem + Sh::kOffChunk) + warp * R;
+  int* cta_cnt = reinterpret_cast<int*>(smem + Sh::kOffCnt);
+
+  if (threadIdx.x < 2 * W) cta_cnt[threadIdx.x] = 0;
+  __syncthreads();  // the only CTA-wide barrier; the warps are independent after it
 
   const int gw = blockIdx.x * W + warp;
   if (gw >= p.n_warps) return;
-  const int64_t T = p.total_blocks;
-  const int g0 = static_cast<int>(gw * T / p.n_warps);
-  const int g1 = static_cast<int>((gw + 1) * T / p.n_warps);
-  if (g0 >= g1) return;
+  const int cta_w0 = blockIdx.x * W;
+  const int cta_w1 = min(cta_w0 + W, p.n_warps) - 1;
+  const int64_t T = p.total_blocks, NW = p.n_warps;
+  auto warp_begin = [&](int w) { return static_cast<int>(w * T / NW); };
+  const int g0 = warp_begin(gw), g1 = warp_begin(gw + 1);  // >= 1 block: NW <= T
+
+  const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
+  const size_t layer_elems = static_cast<size_t>(p.layer) * p.g.layer_elems;
+  const uint8_t* kbase = static_cast<const uint8_t*>(p.g.k) + layer_elems * Sh::kEsz;
+  const uint8_t* vbase = static_cast<const uint8_t*>(p.g.v) + layer_elems * Sh::kEsz;
+  const uint32_t max_chunk = static_cast<uint32_t>(p.g.num_blocks) * Hkv;
+
+  // Start record: {first pair, seq, head, ctx_len}, {pair end in the stream, -, -, -}.
+  const int4 r0 = p.warp_start[2 * gw], r1 = p.warp_start[2 * gw + 1];
 
   if (lane == 0) {
     for (int s = 0; s < R; ++s) mbar_init(&bars[s], 1);
@@ -297,17 +424,40 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
   }
   __syncwarp();
 
-  const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
-  const size_t layer_bytes = static_cast<size_t>(p.layer) * p.g.layer_elems * Sh::kEsz;
-  const uint8_t* kbase = static_cast<const uint8_t*>(p.g.k) + layer_bytes;
-  const uint8_t* vbase = static_cast<const uint8_t*>(p.g.v) + layer_bytes;
-  const uint32_t max_chunk = static_cast<uint32_t>(p.g.num_blocks) * Hkv;
+  // ---- pair window: one PairEntry per lane, shared by producer and consumer --
+  int pwin = r0.x;
+  int4 pa = make_int4(0, 0, 0, 0), pb = make_int4(0, 0, 0, 0);
+  auto load_window = [&](int from) {
+    pwin = from;
+    if (from + lane < p.n_pairs) {
+      const int4* e = reinterpret_cast<const int4*>(p.pairs + from + lane);
+      pa = e[0];
+      pb = e[1];
+    }
+  };
 
-  // ---- producer: a 32-entry window of chunk ids held one per lane ----------
+  // ---- producer: lane 0 keeps R stages in flight ahead of the consumer ------
   int cwin = g0;
   int cval = (g0 + lane < g1) ? p.chunks[g0 + lane] : 0;
   int pg = g0;  // next stream block to issue
+  int pp = r0.x, pp_seq = r0.y, pp_head = r0.z, pp_L = r0.w, pp_end = r1.x;
+  int pp_first = g0;  // first block of pair pp in this warp
+  int pc = r0.x;      // the consumer's pair; the window never moves past it
+  bool window_loaded = false;
   auto issue = [&](int stage) {
+    if (pg == pp_end) {  // the producer enters the next pair
+      ++pp;
+      if (!window_loaded || pp - pwin >= 32) {
+        load_window(pc);
+        window_loaded = true;
+      }
+      const PairFields f = pair_from_window(pa, pb, pp - pwin);
+      pp_seq = f.seq;
+      pp_head = f.head;
+      pp_L = f.L;
+      pp_first = f.blk_begin;
+      pp_end = f.blk_begin + f.nblk;
+    }
     if (pg - cwin >= 32) {
       cwin = pg;
       cval = (pg + lane < g1) ? p.chunks[pg + lane] : 0;
@@ -318,82 +468,50 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
         atomicOr(p.g.error, kErrBadBlock);
         chunk = 0;
       }
+      stage_chunk[stage] = static_cast<int>(chunk);
       uint8_t* st = stages + stage * Sh::kStage;
-      mbar_arrive_expect_tx(&bars[stage], Sh::kStage);
+      uint8_t* sd = sides + stage * Sh::kSide;
+      const bool first = (pg == pp_first);
+      const bool appends = p.fused && first && (pp_end - 1 < g1);
+      uint32_t tx = Sh::kStage;
+      if (first) tx += G * D * 4 + (p.fused ? (D / 2) * 8 : 0) + (appends ? 2 * D * 4 : 0);
+      mbar_arrive_expect_tx(&bars[stage], tx);
       bulk_load(st, kbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk, &bars[stage]);
       bulk_load(st + Sh::kChunk, vbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk,
                 &bars[stage]);
+      if (first) {
+        bulk_load(sd, p.q + (static_cast<size_t>(pp_seq) * Hq + pp_head * G) * D, G * D * 4,
+                  &bars[stage]);
+        if (p.fused)
+          bulk_load(sd + Sh::kSideCs, p.g.rope + static_cast<size_t>(pp_L - 1) * (D / 2),
+                    (D / 2) * 8, &bars[stage]);
+        if (appends) {
+          const size_t row = (static_cast<size_t>(pp_seq) * Hkv + pp_head) * D;
+          bulk_load(sd + Sh::kSideKn, p.k_new + row, D * 4, &bars[stage]);
+          bulk_load(sd + Sh::kSideVn, p.v_new + row, D * 4, &bars[stage]);
+        }
+      }
     }
     ++pg;
   };
   for (int s = 0; s < R && pg < g1; ++s) issue(s);
-
-  // ---- consumer: pair window (one PairEntry per lane) -----------------------
-  int pi = p.warp_first_pair[gw];
-  int pwin = pi;
-  int4 pa = make_int4(0, 0, 0, 0), pb = make_int4(0, 0, 0, 0);
-  auto load_window = [&](int from) {
-    pwin = from;
-    if (from + lane < p.n_pairs) {
-      const int4* e = reinterpret_cast<const int4*>(p.pairs + from + lane);
-      pa = e[0];
-      pb = e[1];
-    }
-  };
-  load_window(pi);
-  auto fields = [&](int idx) {
-    if (idx - pwin >= 32) load_window(idx);
-    return pair_from_window(pa, pb, idx - pwin);
-  };
-
-  // Per-pair inputs, prefetched one pair ahead: Q (G float2 per lane), the
-  // new K/V row (fused), and the chunk id of the pair's last block.
-  struct Inputs {
-    float2 q[G];
-    float2 kn, vn;
-    int app_chunk;
-  };
-  auto fetch = [&](const PairFields& f, Inputs& in) {
-    const float* qsrc = p.q + (static_cast<size_t>(f.seq) * Hq + f.head * G) * D;
-#pragma unroll
-    for (int g = 0; g < G; ++g) in.q[g] = reinterpret_cast<const float2*>(qsrc + g * D)[lane];
-    const int last = f.blk_begin + f.nblk - 1;
-    if (p.fused && last >= g0 && last < g1) {
-      const size_t src = (static_cast<size_t>(f.seq) * Hkv + f.head) * D;
-      in.kn = reinterpret_cast<const float2*>(p.k_new + src)[lane];
-      in.vn = reinterpret_cast<const float2*>(p.v_new + src)[lane];
-      in.app_chunk = p.chunks[last];
-    }
-  };
-
-  PairFields cur = fields(pi);
-  Inputs cin, nin;
-  fetch(cur, cin);
-  bool have_next = (cur.blk_begin + cur.nblk < g1);
-  PairFields nxt = cur;
-  if (have_next) {
-    nxt = fields(pi + 1);
-    fetch(nxt, nin);
+  if (!window_loaded) {
+    load_window(pc);
+    window_loaded = true;
   }
 
+  // ---- consumer --------------------------------------------------------------
+  PairFields cur = pair_from_window(pa, pb, pc - pwin);
   float m[G], l[G];
   float2 acc[G];
-  auto start_pair = [&]() {
-    const int pos = cur.L - 1;
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float2 x = cin.q[g];
-      if (p.fused) x = rope_pair(x, p.g.rope[static_cast<size_t>(pos) * (D / 2) + lane]);
-      *reinterpret_cast<float2*>(qs + g * D + qunit(lane >> 1) * 4 + ((2 * lane) & 3)) = x;
-      m[g] = -INFINITY;
-      l[g] = 0.f;
-      acc[g] = make_float2(0.f, 0.f);
-    }
-    __syncwarp();
-  };
-  start_pair();
-
+  float2 cs = make_float2(1.f, 0.f), kn = cs, vn = cs;
   int seg_end = min(g1, cur.blk_begin + cur.nblk);
+  bool seg_start = true;
+
+  // Cross-CTA pairs finished after the warp's last block (at most two).
+  int npend = 0;
+  int4 pend0 = make_int4(0, 0, 0, 0), pend1 = pend0;  // {pair, global slot base, n CTA segs, row}
+
   for (int g = g0, cnt = 0; g < g1; ++g, ++cnt) {
     const int stage = cnt % R;
     const uint32_t parity = static_cast<uint32_t>(cnt / R) & 1u;
@@ -408,37 +526,54 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
       __syncwarp();
       return;
     }
+    uint8_t* kb = stages + stage * Sh::kStage;
+    uint8_t* vb = kb + Sh::kChunk;
+    if (seg_start) {
+      // Pair inputs arrived with this stage: rotate Q at the new token's
+      // position into the swizzled Q buffer; keep the RoPE pair and new K/V.
+      const uint8_t* sd = sides + stage * Sh::kSide;
+      if (p.fused) {
+        cs = reinterpret_cast<const float2*>(sd + Sh::kSideCs)[lane];
+        if (cur.blk_begin + cur.nblk - 1 < g1) {
+          kn = reinterpret_cast<const float2*>(sd + Sh::kSideKn)[lane];
+          vn = reinterpret_cast<const float2*>(sd + Sh::kSideVn)[lane];
+        }
+      }
+#pragma unroll
+      for (int g2 = 0; g2 < G; ++g2) {
+        float2 x = reinterpret_cast<const float2*>(sd)[g2 * (D / 2) + lane];
+        if (p.fused) x = rope_pair(x, cs);
+        *reinterpret_cast<float2*>(qs + g2 * D + qunit(lane >> 1) * 4 + ((2 * lane) & 3)) = x;
+        m[g2] = -INFINITY;
+        l[g2] = 0.f;
+        acc[g2] = make_float2(0.f, 0.f);
+      }
+      __syncwarp();
+      seg_start = false;
+    }
     const int j = g - cur.blk_begin;
     const int tok0 = j * kBlockTokens;
     const int nvalid = min(kBlockTokens, cur.L - tok0);
-    uint8_t* kb = stages + stage * Sh::kStage;
-    uint8_t* vb = kb + Sh::kChunk;
     const bool append_here = p.fused && (j == cur.nblk - 1);
     if (append_here) {
       // The append: rotate the new key at position L-1, store K/V (rounded
       // to the pool's type) into the staged block and into the pool.
-      const int pos = cur.L - 1;
-      const int slot = pos - tok0;
-      const bool fin = finite2(cin.kn) && finite2(cin.vn);
-      const float2 kx = rope_pair(cin.kn, p.g.rope[static_cast<size_t>(pos) * (D / 2) + lane]);
-      uint32_t chunk = static_cast<uint32_t>(cin.app_chunk);
-      if (chunk >= max_chunk) {
-        if (lane == 0) atomicOr(p.g.error, kErrBadBlock);
-        chunk = 0;
-      }
-      const size_t dst = p.layer * static_cast<size_t>(p.g.layer_elems) +
-                         (static_cast<size_t>(chunk) * kBlockTokens + slot) * D;
+      const int slot = (cur.L - 1) - tok0;
+      const bool fin = finite2(kn) && finite2(vn);
+      const float2 kx = rope_pair(kn, cs);
+      const size_t dst =
+          layer_elems + (static_cast<size_t>(stage_chunk[stage]) * kBlockTokens + slot) * D;
       if constexpr (BF16) {
-        const uint32_t kq = pack_bf16x2(kx.x, kx.y), vq = pack_bf16x2(cin.vn.x, cin.vn.y);
+        const uint32_t kq = pack_bf16x2(kx.x, kx.y), vq = pack_bf16x2(vn.x, vn.y);
         reinterpret_cast<uint32_t*>(kb)[slot * (D / 2) + lane] = kq;
         reinterpret_cast<uint32_t*>(vb)[slot * (D / 2) + lane] = vq;
         reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.k) + dst)[lane] = kq;
         reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.v) + dst)[lane] = vq;
       } else {
         reinterpret_cast<float2*>(kb)[slot * (D / 2) + lane] = kx;
-        reinterpret_cast<float2*>(vb)[slot * (D / 2) + lane] = cin.vn;
+        reinterpret_cast<float2*>(vb)[slot * (D / 2) + lane] = vn;
         reinterpret_cast<float2*>(static_cast<float*>(p.g.k) + dst)[lane] = kx;
-        reinterpret_cast<float2*>(static_cast<float*>(p.g.v) + dst)[lane] = cin.vn;
+        reinterpret_cast<float2*>(static_cast<float*>(p.g.v) + dst)[lane] = vn;
       }
       if (!__all_sync(kFull, fin) && lane == 0) atomicOr(&p.status[cur.seq], kStatusNonFinite);
       __syncwarp();
@@ -449,82 +584,138 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
     } else {
       block_scores_f32<G>(reinterpret_cast<const float*>(kb), qs, lane, sc);
     }
-    block_softmax_pv<G, BF16 != 0>(vb, lane, nvalid, sc, m, l, acc);
-    __syncwarp();
+    block_softmax_pv<G, BF16 != 0>(vb, pbuf, lane, nvalid, sc, m, l, acc);
     if (pg < g1) {
-      // The stage was just read (and maybe written) through the generic
-      // proxy; order that before the async-proxy refill.
+      // The stage (and its side buffer) were read, maybe written, through
+      // the generic proxy; order that before the async-proxy refill.
       if (append_here) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(stage);
     }
 
-    if (g == seg_end - 1) {
-      // ---- finish this warp's segment of the pair --------------------------
-      if (cur.nseg == 1) {
+    if (g != seg_end - 1) continue;
+    // ---- end of this warp's segment of pair `pc` ---------------------------------
+    const size_t orow = static_cast<size_t>(cur.seq) * Hq + cur.head * G;
+    if (cur.nseg == 1) {
+#pragma unroll
+      for (int g2 = 0; g2 < G; ++g2) {
+        const float inv = 1.0f / l[g2];
+        reinterpret_cast<float2*>(p.out + (orow + g2) * D)[lane] =
+            make_float2(acc[g2].x * inv, acc[g2].y * inv);
+      }
+    } else {
+      // Warps [ka, kb] of this CTA hold the pair's segments here; they merge
+      // in shared memory, the last one to arrive does the merge.
+      const int last_warp = cur.first_warp + cur.nseg - 1;
+      const int ka = max(cur.first_warp, cta_w0), kbw = min(last_warp, cta_w1);
+      const bool whole_in_cta = (cur.first_warp >= cta_w0) && (last_warp <= cta_w1);
+      const int n_in = kbw - ka + 1;
+      // A segment sits in slot 2k+0 when it is warp k's first segment: true
+      // for every warp after ka (the pair started before them); for ka it
+      // depends on where the pair starts.
+      const int ka_off = (cur.first_warp < cta_w0 || cur.at_warp_start) ? 0 : 1;
+      auto seg_slot = [&](int w) { return 2 * (w - cta_w0) + ((w == ka) ? ka_off : 0); };
+      float2 A[G];
+      float Mo[G], Lo[G];
+      bool merged = false;
+      if (n_in == 1) {
 #pragma unroll
         for (int g2 = 0; g2 < G; ++g2) {
-          const float inv = 1.0f / l[g2];
-          reinterpret_cast<float2*>(
-              p.out + (static_cast<size_t>(cur.seq) * Hq + cur.head * G + g2) * D)[lane] =
-              make_float2(acc[g2].x * inv, acc[g2].y * inv);
+          A[g2] = acc[g2];
+          Mo[g2] = m[g2];
+          Lo[g2] = l[g2];
         }
+        merged = true;
       } else {
-        const int slot = cur.part_base + (gw - cur.first_warp);
+        uint8_t* mine = slots + seg_slot(gw) * Sh::kSlot;
 #pragma unroll
         for (int g2 = 0; g2 < G; ++g2) {
-          reinterpret_cast<float2*>(p.part_acc + (static_cast<size_t>(slot) * G + g2) * D)[lane] =
-              acc[g2];
-          if (lane == 0) p.part_ml[static_cast<size_t>(slot) * G + g2] = make_float2(m[g2], l[g2]);
+          reinterpret_cast<float2*>(mine)[g2 * (D / 2) + lane] = acc[g2];
+          if (lane == 0)
+            reinterpret_cast<float2*>(mine + G * D * 4)[g2] = make_float2(m[g2], l[g2]);
         }
-        __threadfence();
+        __threadfence_block();
         __syncwarp();
         int last = 0;
-        if (lane == 0) {
-          const int prev = atomicAdd(&p.counters[pi], 1);
-          last = (prev == cur.nseg - 1);
-          if (last) atomicExch(&p.counters[pi], 0);  // ready for the next launch
-        }
+        if (lane == 0) last = (atomicAdd(&cta_cnt[seg_slot(ka)], 1) == n_in - 1);
         last = __shfl_sync(kFull, last, 0);
         if (last) {
-          __threadfence();
+          __threadfence_block();
+          auto acc_at = [&](int s, int g2) {
+            const uint8_t* sl = slots + seg_slot(ka + s) * Sh::kSlot;
+            return reinterpret_cast<const float2*>(sl)[g2 * (D / 2) + lane];
+          };
+          auto ml_at = [&](int s, int g2) {
+            const uint8_t* sl = slots + seg_slot(ka + s) * Sh::kSlot;
+            return reinterpret_cast<const float2*>(sl + G * D * 4)[g2];
+          };
+          merge_partials<G>(n_in, lane, acc_at, ml_at, A, Mo, Lo);
+          merged = true;
+        }
+      }
+      if (merged) {
+        if (whole_in_cta) {
 #pragma unroll
           for (int g2 = 0; g2 < G; ++g2) {
-            float M = -INFINITY;
-            for (int s = lane; s < cur.nseg; s += 32)
-              M = fmaxf(M, __ldcg(&p.part_ml[static_cast<size_t>(cur.part_base + s) * G + g2].x));
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, off));
-            float Ls = 0.f;
-            float2 A = make_float2(0.f, 0.f);
-            for (int s = 0; s < cur.nseg; ++s) {
-              const size_t ps = static_cast<size_t>(cur.part_base + s) * G + g2;
-              const float2 ml = __ldcg(&p.part_ml[ps]);
-              const float f = exp2f(ml.x - M);
-              const float2 a = __ldcg(reinterpret_cast<const float2*>(p.part_acc + ps * D) + lane);
-              Ls = fmaf(ml.y, f, Ls);
-              A.x = fmaf(a.x, f, A.x);
-              A.y = fmaf(a.y, f, A.y);
-            }
-            const float inv = 1.0f / Ls;
-            reinterpret_cast<float2*>(
-                p.out + (static_cast<size_t>(cur.seq) * Hq + cur.head * G + g2) * D)[lane] =
-                make_float2(A.x * inv, A.y * inv);
+            const float inv = 1.0f / Lo[g2];
+            reinterpret_cast<float2*>(p.out + (orow + g2) * D)[lane] =
+                make_float2(A[g2].x * inv, A[g2].y * inv);
           }
+        } else {
+          // This CTA's share of a pair that spans CTAs: one global partial.
+          const int first_cta = cur.first_warp / W;
+          const int n_cta = last_warp / W - first_cta + 1;
+          const size_t gslot = static_cast<size_t>(cur.part_base) + (blockIdx.x - first_cta);
+#pragma unroll
+          for (int g2 = 0; g2 < G; ++g2) {
+            reinterpret_cast<float2*>(p.part_acc + (gslot * G + g2) * D)[lane] = A[g2];
+            if (lane == 0) p.part_ml[gslot * G + g2] = make_float2(Mo[g2], Lo[g2]);
+          }
+          const int4 e = make_int4(pc, cur.part_base, n_cta, static_cast<int>(orow));
+          if (npend == 0) pend0 = e;
+          else pend1 = e;
+          ++npend;
         }
       }
-      if (g + 1 < g1) {
-        // ---- move to the next pair -----------------------------------------
-        ++pi;
-        cur = nxt;
-        cin = nin;
-        seg_end = min(g1, cur.blk_begin + cur.nblk);
-        have_next = (cur.blk_begin + cur.nblk < g1);
-        if (have_next) {
-          nxt = fields(pi + 1);
-          fetch(nxt, nin);
-        }
-        start_pair();
-      }
+    }
+    if (g + 1 < g1) {
+      ++pc;
+      if (pc - pwin >= 32) load_window(pc);
+      cur = pair_from_window(pa, pb, pc - pwin);
+      seg_end = min(g1, cur.blk_begin + cur.nblk);
+      seg_start = true;
+    }
+  }
+
+  // ---- pairs that span CTAs: the last CTA to arrive merges the partials -----
+  if (npend == 0) return;
+  __threadfence();
+  __syncwarp();
+  for (int k = 0; k < npend; ++k) {
+    const int4 e = (k == 0) ? pend0 : pend1;
+    int last = 0;
+    if (lane == 0) {
+      const int prev = atomicAdd(&p.counters[e.x], 1);
+      last = (prev == e.z - 1);
+      if (last) atomicExch(&p.counters[e.x], 0);  // ready for the next launch
+    }
+    last = __shfl_sync(kFull, last, 0);
+    if (!last) continue;
+    __threadfence();
+    auto acc_at = [&](int s, int g2) {
+      return __ldcg(reinterpret_cast<const float2*>(
+                        p.part_acc + ((static_cast<size_t>(e.y) + s) * G + g2) * D) + lane);
+    };
+    auto ml_at = [&](int s, int g2) {
+      return __ldcg(&p.part_ml[(static_cast<size_t>(e.y) + s) * G + g2]);
+    };
+    float2 A[G];
+    float Mo[G], Lo[G];
+    merge_partials<G>(e.z, lane, acc_at, ml_at, A, Mo, Lo);
+#pragma unroll
+    for (int g2 = 0; g2 < G; ++g2) {
+      const float inv = 1.0f / Lo[g2];
+      reinterpret_cast<float2*>(p.out + (static_cast<size_t>(e.w) + g2) * D)[lane] =
+          make_float2(A[g2].x * inv, A[g2].y * inv);
     }
   }
 }
@@ -532,7 +723,7 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
 template <int BF16, int G>
 cudaError_t launch_decode_t(const StreamDecodeLaunch& p, cudaStream_t s) {
   constexpr int W = kDecodeWarps;
-  constexpr int R = BF16 ? 6 : 3;
+  constexpr int R = BF16 ? (G >= 8 ? 3 : 4) : 2;
   using Sh = StreamShape<BF16, G, W, R>;
   if (p.total_blocks <= 0) return cudaSuccess;
   int dev = 0;
@@ -641,6 +832,7 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillLaunch p) {
   __shared__ __align__(16) float qs[kBlockTokens * G * D];
   __shared__ __align__(16) float kbuf[kBlockTokens * D];
   __shared__ __align__(16) float vbuf[kBlockTokens * D];
+  __shared__ __align__(16) float pbufs[4][G * kBlockTokens];
   const int tile = blockIdx.x, si = blockIdx.y, h = blockIdx.z;
   const SeqEntry se = p.seqs[si];
   const int q0 = tile * kBlockTokens;
@@ -705,7 +897,7 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillLaunch p) {
       if (nvalid <= 0) continue;
       float sc[G];
       block_scores_f32<G>(kbuf, qs + jq * G * D, lane, sc);
-      block_softmax_pv<G, false>(vbuf, lane, nvalid, sc, m[r], l[r], acc[r]);
+      block_softmax_pv<G, false>(vbuf, pbufs[warp], lane, nvalid, sc, m[r], l[r], acc[r]);
     }
   }
 #pragma unroll
