@@ -98,7 +98,7 @@ struct slm_ctx {
   int32_t num_sms = 0;
   int32_t max_blocks_per_seq = 0;
   int32_t group = 1;
-  int32_t n_warps = 0;     // decode grid: SMs x kDecodeWarps
+  int32_t n_warps = 0;     // decode grid: SMs x decode_warps()
   int32_t max_pairs = 0;   // max_sequences x Hkv
   int64_t max_chunks = 0;  // max_sequences x blocks per sequence x Hkv
   int64_t device_bytes = 0;
@@ -400,6 +400,7 @@ slm_status flush_excess(slm_ctx* c, cudaStream_t s, size_t keep_updates, size_t 
 void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, int32_t n_warps,
                        StreamPlan& plan) {
   const int32_t Hkv = c->cfg.num_key_value_heads;
+  const int32_t W = decode_warps(c->cfg.kv_dtype == SLM_KV_BF16, c->group);
   plan.pairs.clear();
   plan.chunks.clear();
   for (size_t i = 0; i < entries.size(); ++i) {
@@ -424,7 +425,7 @@ void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, i
   const int64_t NW = std::min<int64_t>(n_warps, T);
   // Warp owning stream index x: the largest w with floor(w*T/NW) <= x.
   auto owner = [&](int64_t x) { return static_cast<int32_t>(((x + 1) * NW - 1) / T); };
-  // Pairs merge per CTA first (kDecodeWarps consecutive warps); a pair that
+  // Pairs merge per CTA first (W consecutive warps); a pair that
   // spans CTAs gets one global partial slot per CTA it touches.
   int32_t part = 0;
   for (PairEntry& pe : plan.pairs) {
@@ -433,7 +434,7 @@ void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, i
     pe.nseg = last_warp - pe.first_warp + 1;
     if (pe.first_warp * T / NW == pe.blk_begin) pe.nseg |= (1 << 30);
     pe.part_base = part;
-    const int32_t n_cta = last_warp / kDecodeWarps - pe.first_warp / kDecodeWarps + 1;
+    const int32_t n_cta = last_warp / W - pe.first_warp / W + 1;
     if (n_cta > 1) part += n_cta;
   }
   plan.warp_start.assign(static_cast<size_t>(2 * NW), make_int4(0, 0, 0, 0));
@@ -636,7 +637,7 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     cp->num_sms = sms;
-    cp->n_warps = sms * kDecodeWarps;
+    cp->n_warps = sms * decode_warps(k.kv_dtype == SLM_KV_BF16, G);
     const size_t esz = k.kv_dtype == SLM_KV_BF16 ? 2 : 4;
     const size_t pool_bytes = static_cast<size_t>(k.num_layers) * k.num_blocks *
                               k.num_key_value_heads * kBlockTokens * k.head_dimension * esz;

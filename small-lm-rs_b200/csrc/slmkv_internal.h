@@ -37,8 +37,11 @@ struct PairEntry {
 };
 static_assert(sizeof(PairEntry) == 32, "PairEntry is read as two int4");
 
-// Warps per decode CTA (one CTA per SM).
-constexpr int kDecodeWarps = 8;
+// Decode CTA shape (one CTA per SM): warps per CTA and K/V stages per warp,
+// per pool type and query heads per KV head, sized to the 227 KiB of shared
+// memory (each stage holds one 16-token block of K and V plus side inputs).
+constexpr int decode_warps(int bf16, int group) { return (!bf16 && group <= 2) ? 10 : 8; }
+constexpr int decode_stages(int bf16, int group) { return bf16 ? (group >= 8 ? 3 : 4) : 2; }
 
 // Block-table write or copy-on-write job, applied before a step's kernels.
 struct TableUpdate {
@@ -79,7 +82,7 @@ struct StreamDecodeLaunch {
   int32_t total_blocks;
   const int4* warp_start;         // [2 * n_warps]: {first pair, seq, head,
                                   //  ctx_len}, {first pair's end in the stream, 0, 0, 0}
-  int32_t n_warps;                // grid = ceil(n_warps / kDecodeWarps) CTAs
+  int32_t n_warps;                // grid = ceil(n_warps / decode_warps()) CTAs
   const float* q;      // [n, Hq, d]
   const float* k_new;  // [n, Hkv, d] (fused mode) or null
   const float* v_new;

@@ -722,8 +722,8 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
 
 template <int BF16, int G>
 cudaError_t launch_decode_t(const StreamDecodeLaunch& p, cudaStream_t s) {
-  constexpr int W = kDecodeWarps;
-  constexpr int R = BF16 ? (G >= 8 ? 3 : 4) : 2;
+  constexpr int W = decode_warps(BF16, G);
+  constexpr int R = decode_stages(BF16, G);
   using Sh = StreamShape<BF16, G, W, R>;
   if (p.total_blocks <= 0) return cudaSuccess;
   int dev = 0;
