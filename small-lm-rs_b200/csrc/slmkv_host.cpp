@@ -58,7 +58,9 @@ struct Upload {
 struct StreamPlan {
   std::vector<PairEntry> pairs;
   std::vector<int32_t> chunks;
-  std::vector<int4> warp_start;  // 2 per warp: {first pair, seq, head, ctx_len}, {pair end, 0, 0, 0}
+  // 2 per warp: {first pair, seq, head, ctx_len}, {first pair's end, g0, g1, 0}
+  std::vector<int4> warp_start;
+  std::vector<int32_t> bounds;  // warp boundaries in the stream (scratch)
 };
 
 // Device addresses of one uploaded step descriptor.
@@ -395,8 +397,9 @@ slm_status flush_excess(slm_ctx* c, cudaStream_t s, size_t keep_updates, size_t 
 
 // Builds the decode plan for sequences (batch rows) attending `ctx_len`
 // tokens: one PairEntry per (row, KV head), the chunk stream in pair order,
-// and an equal split of the stream over `n_warps` decode warps. Warp w owns
-// stream indices [w*T/n_warps, (w+1)*T/n_warps).
+// and an equal split of the stream over the decode warps: warp w owns stream
+// indices [floor(w*T/NW), floor((w+1)*T/NW)). Warp boundaries are stepped
+// without divisions and matched to pairs in one sweep.
 void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, int32_t n_warps,
                        StreamPlan& plan) {
   const int32_t Hkv = c->cfg.num_key_value_heads;
@@ -405,7 +408,7 @@ void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, i
   plan.chunks.clear();
   for (size_t i = 0; i < entries.size(); ++i) {
     const SeqEntry& e = entries[i];
-    const Seq& q = c->seqs[e.slot];
+    const int32_t* blocks = c->seqs[e.slot].blocks.data();
     const int32_t nb = blocks_for(e.ctx_len);
     for (int32_t h = 0; h < Hkv; ++h) {
       PairEntry pe{};
@@ -415,49 +418,67 @@ void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, i
       pe.blk_begin = static_cast<int32_t>(plan.chunks.size());
       pe.nblk = nb;
       plan.pairs.push_back(pe);
-      for (int32_t j = 0; j < nb; ++j) plan.chunks.push_back(q.blocks[j] * Hkv + h);
+      for (int32_t j = 0; j < nb; ++j) plan.chunks.push_back(blocks[j] * Hkv + h);
     }
   }
   const int64_t T = static_cast<int64_t>(plan.chunks.size());
-  // Never more warps than blocks: then every warp owns at least one block and
-  // the warps covering a pair are consecutive, so a pair's segment index is
-  // simply (warp - first_warp).
-  const int64_t NW = std::min<int64_t>(n_warps, T);
-  // Warp owning stream index x: the largest w with floor(w*T/NW) <= x.
-  auto owner = [&](int64_t x) { return static_cast<int32_t>(((x + 1) * NW - 1) / T); };
-  // Pairs merge per CTA first (W consecutive warps); a pair that
-  // spans CTAs gets one global partial slot per CTA it touches.
-  int32_t part = 0;
+  const int32_t NW = static_cast<int32_t>(std::min<int64_t>(n_warps, T));
+  // bounds[w] = floor(w*T/NW): T = q*NW + r, carry r each step.
+  std::vector<int32_t>& bounds = plan.bounds;
+  bounds.resize(static_cast<size_t>(NW) + 1);
+  {
+    const int64_t q = T / NW, r = T % NW;
+    int64_t b = 0, carry = 0;
+    bounds[0] = 0;
+    for (int32_t w = 0; w < NW; ++w) {
+      carry += r;
+      b += q;
+      if (carry >= NW) {
+        carry -= NW;
+        ++b;
+      }
+      bounds[w + 1] = static_cast<int32_t>(b);
+    }
+  }
+  // Owner of stream index x: the w with bounds[w] <= x < bounds[w+1]; the
+  // queries below only move forward, so a cursor per query suffices.
+  int32_t wa = 0, wb = 0, part = 0;
   for (PairEntry& pe : plan.pairs) {
-    pe.first_warp = owner(pe.blk_begin);
-    const int32_t last_warp = owner(pe.blk_begin + pe.nblk - 1);
-    pe.nseg = last_warp - pe.first_warp + 1;
-    if (pe.first_warp * T / NW == pe.blk_begin) pe.nseg |= (1 << 30);
+    while (bounds[wa + 1] <= pe.blk_begin) ++wa;
+    const int32_t last = pe.blk_begin + pe.nblk - 1;
+    if (wb < wa) wb = wa;
+    while (bounds[wb + 1] <= last) ++wb;
+    pe.first_warp = wa;
+    pe.nseg = wb - wa + 1;
+    if (bounds[wa] == pe.blk_begin) pe.nseg |= (1 << 30);
     pe.part_base = part;
-    const int32_t n_cta = last_warp / W - pe.first_warp / W + 1;
+    // Pairs merge per CTA first (W consecutive warps); a pair that spans
+    // CTAs gets one global partial slot per CTA it touches.
+    const int32_t n_cta = wb / W - wa / W + 1;
     if (n_cta > 1) part += n_cta;
   }
-  plan.warp_start.assign(static_cast<size_t>(2 * NW), make_int4(0, 0, 0, 0));
+  plan.warp_start.resize(static_cast<size_t>(2 * NW));
   size_t pc = 0;
-  for (int64_t w = 0; w < NW; ++w) {
-    const int64_t b = w * T / NW;
+  for (int32_t w = 0; w < NW; ++w) {
+    const int32_t b = bounds[w];
     while (plan.pairs[pc].blk_begin + plan.pairs[pc].nblk <= b) ++pc;
     const PairEntry& pe = plan.pairs[pc];
     plan.warp_start[2 * w] = make_int4(static_cast<int32_t>(pc), pe.seq, pe.head, pe.ctx_len);
-    plan.warp_start[2 * w + 1] = make_int4(pe.blk_begin + pe.nblk, 0, 0, 0);
+    plan.warp_start[2 * w + 1] = make_int4(pe.blk_begin + pe.nblk, b, bounds[w + 1], 0);
   }
 }
 
 // Uploads [entries, zeroed status, decode plan (optional), pending table
 // updates / copies] into region `u` with one copy, and applies the updates.
 slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<SeqEntry>& entries,
-                       const StreamPlan* plan, StepDev* dev) {
+                       const StreamPlan* plan, StepDev* dev, bool with_table_updates = true) {
   slm_status rc = flush_excess(c, s, c->upd_cap, c->copy_cap);
   if (rc) return rc;
   const size_t n = entries.size();
   const size_t np = plan ? plan->pairs.size() : 0, nch = plan ? plan->chunks.size() : 0;
   const size_t nw = plan ? plan->warp_start.size() / 2 : 0;
-  const size_t nu = c->pending_updates.size(), nc = c->pending_copies.size();
+  const size_t nu = with_table_updates ? c->pending_updates.size() : 0;
+  const size_t nc = c->pending_copies.size();
   DescLayout L = desc_layout(n, np, nch, nw, nu, nc);
   if (L.total > u.cap)
     return fail(c, SLM_ERR_INVALID_INPUT, "invalid input for KV cache: step descriptor too large");
@@ -475,7 +496,7 @@ slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<
                                static_cast<int32_t>(nu), reinterpret_cast<CopyJob*>(u.d + L.copies),
                                static_cast<int32_t>(nc), s));
     ++c->launches;
-    c->pending_updates.clear();
+    if (with_table_updates) c->pending_updates.clear();
     c->pending_copies.clear();
   }
   dev->seqs = reinterpret_cast<SeqEntry*>(u.d + L.seqs);
@@ -1084,7 +1105,11 @@ slm_status slm_batch_begin(slm_ctx* ctx, int32_t n, const int32_t* h_seq_ids,
     b->n_pairs = static_cast<int32_t>(plan.pairs.size());
     b->total_blocks = static_cast<int32_t>(plan.chunks.size());
   }
-  rc = upload_step(ctx, ctx->up_batch, s, entries, decode ? &plan : nullptr, &b->dev);
+  // The decode kernel reads the chunk stream, not the device block table, so
+  // a decode step leaves pure table writes pending (copies are applied now);
+  // every kernel that reads the table flushes them first.
+  rc = upload_step(ctx, ctx->up_batch, s, entries, decode ? &plan : nullptr, &b->dev,
+                   /*with_table_updates=*/!decode);
   if (rc) {
     rollback_reserve(ctx, undo);
     clear_marks();
@@ -1147,6 +1172,8 @@ slm_status slm_batch_append_layer(slm_batch* b, int32_t layer, const float* d_ke
   if (b->layer_done[layer])
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "layer %d was already appended", layer);
   if (!d_keys || !d_values) return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "null tensor");
+  rc = flush_excess(ctx, b->stream, 0, 0);  // the append reads the device block table
+  if (rc) return rc;
   AppendLaunch a{};
   a.g = ctx->geom();
   a.layer = layer;
@@ -1178,6 +1205,8 @@ slm_status slm_batch_prefill_attention(slm_batch* b, int32_t layer, const float*
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention prefill",
                        "more than 4 query heads per KV head are not supported in prefill");
   if (!d_query || !d_out) return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "null tensor");
+  rc = flush_excess(ctx, b->stream, 0, 0);  // the prefill reads the device block table
+  if (rc) return rc;
   PrefillLaunch p{};
   p.g = ctx->geom();
   p.layer = layer;

@@ -81,7 +81,7 @@ struct StreamDecodeLaunch {
   const int32_t* chunks;          // [total_blocks]
   int32_t total_blocks;
   const int4* warp_start;         // [2 * n_warps]: {first pair, seq, head,
-                                  //  ctx_len}, {first pair's end in the stream, 0, 0, 0}
+                                  //  ctx_len}, {first pair's end, g0, g1, 0}
   int32_t n_warps;                // grid = ceil(n_warps / decode_warps()) CTAs
   const float* q;      // [n, Hq, d]
   const float* k_new;  // [n, Hkv, d] (fused mode) or null

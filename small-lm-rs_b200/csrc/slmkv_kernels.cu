@@ -399,15 +399,16 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
   int* cta_cnt = reinterpret_cast<int*>(smem + Sh::kOffCnt);
 
   if (threadIdx.x < 2 * W) cta_cnt[threadIdx.x] = 0;
+  // Launched with programmatic stream serialization: everything above ran
+  // while the previous kernel of the stream was finishing; wait for it (and
+  // its memory) before touching anything in global memory.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();  // the only CTA-wide barrier; the warps are independent after it
 
   const int gw = blockIdx.x * W + warp;
   if (gw >= p.n_warps) return;
   const int cta_w0 = blockIdx.x * W;
   const int cta_w1 = min(cta_w0 + W, p.n_warps) - 1;
-  const int64_t T = p.total_blocks, NW = p.n_warps;
-  auto warp_begin = [&](int w) { return static_cast<int>(w * T / NW); };
-  const int g0 = warp_begin(gw), g1 = warp_begin(gw + 1);  // >= 1 block: NW <= T
 
   const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
   const size_t layer_elems = static_cast<size_t>(p.layer) * p.g.layer_elems;
@@ -415,8 +416,10 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
   const uint8_t* vbase = static_cast<const uint8_t*>(p.g.v) + layer_elems * Sh::kEsz;
   const uint32_t max_chunk = static_cast<uint32_t>(p.g.num_blocks) * Hkv;
 
-  // Start record: {first pair, seq, head, ctx_len}, {pair end in the stream, -, -, -}.
+  // Start record: {first pair, seq, head, ctx_len}, {first pair's end in the
+  // stream, g0, g1, -}; the warp owns stream blocks [g0, g1) (never empty).
   const int4 r0 = p.warp_start[2 * gw], r1 = p.warp_start[2 * gw + 1];
+  const int g0 = r1.y, g1 = r1.z;
 
   if (lane == 0) {
     for (int s = 0; s < R; ++s) mbar_init(&bars[s], 1);
@@ -736,9 +739,17 @@ cudaError_t launch_decode_t(const StreamDecodeLaunch& p, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     configured |= (1ull << dev);
   }
-  const int ctas = (p.n_warps + W - 1) / W;
-  decode_stream_kernel<BF16, G, W, R><<<ctas, W * 32, Sh::kSmem, s>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((p.n_warps + W - 1) / W);
+  cfg.blockDim = dim3(W * 32);
+  cfg.dynamicSmemBytes = Sh::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_stream_kernel<BF16, G, W, R>, p);
 }
 
 // ---------------------------------------------------------------------------

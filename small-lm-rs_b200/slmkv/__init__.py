@@ -469,7 +469,8 @@ class Batch:
     leaving the block normally ends (commits) it, an exception rolls it back."""
 
     def __init__(self, pool: KvPool, caches: Sequence[KvCache],
-                 token_counts: Sequence[int] | int = 1, stream=None, *, _arrays=None):
+                 token_counts: Sequence[int] | int = 1, stream=None, *, _arrays=None,
+                 _stream=None):
         self.pool = pool
         self.caches = caches if _arrays is not None else list(caches)
         n = len(self.caches)
@@ -483,8 +484,8 @@ class Batch:
             self._counts = _i32_array(self.token_counts)
             self._status = (C.c_int32 * max(1, n))()
         h = C.c_void_p()
-        rc = _fast.begin(pool.handle, n, self._ids, self._counts, _stream_ptr(stream),
-                         C.byref(h))
+        sp = _stream if _stream is not None else _stream_ptr(stream)
+        rc = _fast.begin(pool.handle, n, self._ids, self._counts, sp, C.byref(h))
         if rc:
             pool.check(rc)
         self._h = h
@@ -550,10 +551,18 @@ class StepPlan:
         self._ids = _i32_array([c.seq_id for c in self.caches])
         self._counts = _i32_array(self.token_counts)
         self._status = (C.c_int32 * max(1, n))()
-        self._stream = None
+        self._stream = None  # the stream of the first begin(), reused after
 
     def begin(self, stream=None) -> Batch:
-        return Batch(self.pool, self.caches, stream=stream,
+        """Opens the step on `stream` (default: torch's current stream at the
+        plan's first step, remembered for the following steps)."""
+        if stream is not None:
+            sp = _stream_ptr(stream)
+        else:
+            if self._stream is None:
+                self._stream = _stream_ptr(None)
+            sp = self._stream
+        return Batch(self.pool, self.caches, _stream=sp,
                      _arrays=(self._ids, self._counts, self._status, self.token_counts))
 
     def lengths(self, lengths: Sequence[int]):
