@@ -76,7 +76,9 @@ typedef void* slm_stream; /* a cudaStream_t; NULL = the legacy default stream */
  * calls work, every compute call returns SLM_ERR_NO_DEVICE. */
 slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out);
 slm_status slm_destroy(slm_ctx* ctx);
-/* Message of the last failed call ("" if none). Valid until the next call. */
+/* Message of the last failed call ("" if none). Valid until the next call.
+ * With ctx == NULL: the last failed call on this thread that has no context
+ * (slm_create, slm_decode_attention_noalloc). */
 const char* slm_last_error(const slm_ctx* ctx);
 /* Bytes of device memory the context holds. */
 slm_status slm_device_bytes(const slm_ctx* ctx, int64_t* bytes);
@@ -196,6 +198,36 @@ slm_status slm_pool_stats(const slm_ctx* ctx, int32_t* free_blocks, int32_t* ind
 /* Shuffles the free list with a seeded permutation, so that sequences get
  * scattered physical blocks. Pool must be unused. */
 slm_status slm_pool_shuffle(slm_ctx* ctx, uint64_t seed);
+
+/* ---- allocation-free decode attention ------------------------------------
+ * No counterpart in the reference. For callers that cannot allocate device
+ * memory: code that runs while a CUDA graph is captured on its stream,
+ * engines that hand out all device memory from one arena of their own, and
+ * plugins loaded into hosts that forbid new device allocations after
+ * start-up. It computes GroupedQueryAttention::attend_cached_query
+ * (attention.rs:677-759) for n sequences of a paged KV cache the caller owns,
+ * with the library's decode kernel, and allocates nothing: the plan, split-K
+ * partials, merge counters and error word live in one 2 MiB file-scope device
+ * array that every GPU loading this library holds until the process exits.
+ *   d_key_pool, d_value_pool  [num_blocks][kv_heads][16][64] f32, one layer
+ *   h_block_table             host [n][max_blocks_per_sequence] physical blocks
+ *   h_lengths                 host [n], each in 1..=16*max_blocks_per_sequence
+ *   d_query                   [n][q_heads][64], already rotated
+ *   d_out                     [n][q_heads][64]
+ * Limits (SLM_ERR_INVALID_INPUT beyond them): n * kv_heads <= 4096 and
+ * sum(ceil(len/16)) * kv_heads <= 131072 blocks; q_heads / kv_heads in
+ * {1, 2, 4, 8}. Runs on the calling thread's current device and returns after
+ * the result is in d_out (it synchronizes `stream`). The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture. All calls share the array and
+ * clear what must start at zero; calls that overlap on the GPU (other
+ * streams or threads) race on it. Errors: slm_last_error(NULL). */
+slm_status slm_decode_attention_noalloc(const float* d_key_pool, const float* d_value_pool,
+                                        int32_t num_blocks, int32_t num_query_heads,
+                                        int32_t num_key_value_heads, const int32_t* h_block_table,
+                                        int32_t max_blocks_per_sequence, const int32_t* h_lengths,
+                                        int32_t n, const float* d_query, float* d_out,
+                                        slm_stream stream);
 
 #ifdef __cplusplus
 }

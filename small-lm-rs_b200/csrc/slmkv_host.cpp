@@ -589,7 +589,8 @@ slm_status finish_single(slm_ctx* c, cudaStream_t s, int32_t* d_status, int32_t*
   return check_device_error(c);
 }
 
-// Message of the last failed slm_create on this thread (no context exists).
+// Message of the last failed call on this thread that had no context
+// (slm_create, slm_decode_attention_noalloc).
 thread_local std::string g_create_error;
 
 // kv_cache.rs:43-55, rope.rs:21-31 and the config.rs head-divisibility rule,
@@ -616,6 +617,12 @@ std::string validate_config(const slm_config& k) {
 }
 
 }  // namespace
+
+namespace slmkv {
+// Records the message of a failed call made without a context; read back by
+// slm_last_error(NULL).
+void set_contextless_error(const std::string& message) { g_create_error = message; }
+}  // namespace slmkv
 
 // =============================================================================
 // C ABI

@@ -124,6 +124,8 @@ SIGNATURES = {
     "slm_prefix_publish": (C.c_int, [_vp, _i32, _pu32, _i32, _pi32]),
     "slm_pool_stats": (C.c_int, [_vp, _pi32, _pi32]),
     "slm_pool_shuffle": (C.c_int, [_vp, _u64]),
+    "slm_decode_attention_noalloc": (
+        C.c_int, [_vp, _vp, _i32, _i32, _i32, _pi32, _i32, _pi32, _i32, _vp, _vp, _vp]),
 }
 
 _lib = None
@@ -576,3 +578,32 @@ class StepPlan:
         rc = _fast.truncate(self.pool.handle, len(self.caches), self._ids, arr)
         if rc:
             self.pool.check(rc)
+
+
+def decode_attention_noalloc(key_pool, value_pool, block_table, lengths, query, out=None,
+                             stream=None):
+    """slm_decode_attention_noalloc: attend_cached_query (attention.rs:677-759)
+    for n sequences of a caller-owned paged f32 cache, without any device
+    allocation by the library (for callers that cannot allocate: graph
+    capture, arena-managed memory, hosts that forbid new allocations).
+
+    key_pool/value_pool: CUDA [num_blocks, kv_heads, 16, 64]; block_table:
+    host int32 [n, max_blocks]; lengths: host int32 [n]; query: CUDA
+    [n, q_heads, 64], rotated. Returns out [n, q_heads, 64]."""
+    import numpy as np
+    import torch
+
+    nb, hkv = int(key_pool.shape[0]), int(key_pool.shape[1])
+    n, hq = int(query.shape[0]), int(query.shape[1])
+    table = np.ascontiguousarray(block_table, dtype=np.int32)
+    lens = np.ascontiguousarray(lengths, dtype=np.int32)
+    if out is None:
+        out = torch.empty_like(query)
+    rc = lib().slm_decode_attention_noalloc(
+        _ptr(key_pool), _ptr(value_pool), nb, hq, hkv,
+        table.ctypes.data_as(_pi32), int(table.shape[1]), lens.ctypes.data_as(_pi32), n,
+        _ptr(query), _ptr(out), _stream_ptr(stream))
+    if rc != OK:
+        msg = (lib().slm_last_error(None) or b"").decode()
+        raise _error_class(rc)(rc, msg)
+    return out
