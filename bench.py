@@ -250,6 +250,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import slmkv
+    from slmkv.shard import max_over_ranks
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -332,10 +333,7 @@ def run_ours(args):
     ms = t_start.elapsed_time(t_stop)
     kern_ms = [a.elapsed_time(b) / (LAYERS - 1) for a, b in ev]
     kern_avg_ms = sum(kern_ms) / len(kern_ms)
-    if world > 1:
-        t = torch.tensor([ms, kern_avg_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, kern_avg_ms = float(t[0]), float(t[1])
+    ms, kern_avg_ms = max_over_ranks([ms, kern_avg_ms], device=dev)
 
     # End to end through the public API with host buffers: pinned inputs are
     # copied in and the outputs copied back inside every timed step.
@@ -371,10 +369,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t[0])
+    (e2e_ms,) = max_over_ranks([e2e_ms], device=dev)
     if not torch.equal(ho_, out.cpu()):
         raise RuntimeError("end-to-end outputs differ from the device-resident run")
 
