@@ -61,6 +61,7 @@ struct StreamPlan {
   // 2 per warp: {first pair, seq, head, ctx_len}, {first pair's end, g0, g1, 0}
   std::vector<int4> warp_start;
   std::vector<int32_t> bounds;  // warp boundaries in the stream (scratch)
+  std::vector<int32_t> bucket_top, bucket_next, heads_left;  // pair packing (scratch)
 };
 
 // Device addresses of one uploaded step descriptor.
@@ -396,32 +397,30 @@ slm_status flush_excess(slm_ctx* c, cudaStream_t s, size_t keep_updates, size_t 
 }
 
 // Builds the decode plan for sequences (batch rows) attending `ctx_len`
-// tokens: one PairEntry per (row, KV head), the chunk stream in pair order,
-// and an equal split of the stream over the decode warps: warp w owns stream
-// indices [floor(w*T/NW), floor((w+1)*T/NW)). Warp boundaries are stepped
-// without divisions and matched to pairs in one sweep.
+// tokens: one PairEntry per (row, KV head), the chunk stream, and an equal
+// split of the stream over the decode warps: warp w owns stream indices
+// [floor(w*T/NW), floor((w+1)*T/NW)); W consecutive warps form one CTA.
+//
+// The pairs are ordered so that they fill each CTA's share of the stream
+// exactly: for the CTA being filled, the largest remaining pair that fits its
+// remaining room goes next. Only when no remaining pair fits is one cut across
+// the CTA boundary (the largest, so long contexts are cut and short ones are
+// not). A pair inside one CTA merges its warps' partials in shared memory; a
+// cut pair merges through global memory at the end of the kernel, which is
+// the kernel's tail, so the ordering removes most of that tail. Warp bounds
+// are stepped without divisions and matched to pairs in one sweep.
 void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, int32_t n_warps,
                        StreamPlan& plan) {
   const int32_t Hkv = c->cfg.num_key_value_heads;
   const int32_t W = decode_warps(c->cfg.kv_dtype == SLM_KV_BF16, c->group);
-  plan.pairs.clear();
-  plan.chunks.clear();
-  for (size_t i = 0; i < entries.size(); ++i) {
-    const SeqEntry& e = entries[i];
-    const int32_t* blocks = c->seqs[e.slot].blocks.data();
+  const int32_t n_pairs = static_cast<int32_t>(entries.size()) * Hkv;
+  int64_t T = 0;
+  int32_t maxb = 0;
+  for (const SeqEntry& e : entries) {
     const int32_t nb = blocks_for(e.ctx_len);
-    for (int32_t h = 0; h < Hkv; ++h) {
-      PairEntry pe{};
-      pe.seq = static_cast<int32_t>(i);
-      pe.head = h;
-      pe.ctx_len = e.ctx_len;
-      pe.blk_begin = static_cast<int32_t>(plan.chunks.size());
-      pe.nblk = nb;
-      plan.pairs.push_back(pe);
-      for (int32_t j = 0; j < nb; ++j) plan.chunks.push_back(blocks[j] * Hkv + h);
-    }
+    T += static_cast<int64_t>(nb) * Hkv;
+    maxb = std::max(maxb, nb);
   }
-  const int64_t T = static_cast<int64_t>(plan.chunks.size());
   const int32_t NW = static_cast<int32_t>(std::min<int64_t>(n_warps, T));
   // bounds[w] = floor(w*T/NW): T = q*NW + r, carry r each step.
   std::vector<int32_t>& bounds = plan.bounds;
@@ -439,6 +438,51 @@ void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, i
       }
       bounds[w + 1] = static_cast<int32_t>(b);
     }
+  }
+  // Rows bucketed by block count (all heads of a row have the same count);
+  // a stack per bucket, rows pushed in reverse so each pops in row order.
+  std::vector<int32_t>& top = plan.bucket_top;
+  std::vector<int32_t>& next = plan.bucket_next;
+  top.assign(static_cast<size_t>(maxb) + 1, -1);
+  next.resize(entries.size());
+  for (int32_t i = static_cast<int32_t>(entries.size()) - 1; i >= 0; --i) {
+    const int32_t nb = blocks_for(entries[i].ctx_len);
+    next[i] = top[nb];
+    top[nb] = i;
+  }
+  std::vector<int32_t>& heads_left = plan.heads_left;
+  heads_left.assign(entries.size(), Hkv);
+  int32_t hi = maxb;  // no non-empty bucket above this
+  auto take = [&](int32_t nb) {  // pops one pair of a row from bucket nb
+    const int32_t i = top[nb];
+    const int32_t h = Hkv - heads_left[i];
+    if (--heads_left[i] == 0) top[nb] = next[i];
+    return std::make_pair(i, h);
+  };
+
+  plan.pairs.resize(static_cast<size_t>(n_pairs));
+  plan.chunks.resize(static_cast<size_t>(T));
+  int32_t pos = 0, wcta = 0;  // stream position; first warp of the CTA being filled
+  for (int32_t k = 0; k < n_pairs; ++k) {
+    while (wcta + W < NW && bounds[wcta + W] <= pos) wcta += W;
+    const int32_t room = bounds[std::min(wcta + W, NW)] - pos;
+    while (hi > 0 && top[hi] < 0) --hi;
+    int32_t nb = std::min(room, hi);
+    while (nb > 0 && top[nb] < 0) --nb;
+    if (nb <= 0) nb = hi;  // nothing fits: cut the largest across the boundary
+    const auto [i, h] = take(nb);
+    const SeqEntry& e = entries[i];
+    PairEntry& pe = plan.pairs[k];
+    pe = PairEntry{};
+    pe.seq = i;
+    pe.head = h;
+    pe.ctx_len = e.ctx_len;
+    pe.blk_begin = pos;
+    pe.nblk = nb;
+    const int32_t* blocks = c->seqs[e.slot].blocks.data();
+    int32_t* out = plan.chunks.data() + pos;
+    for (int32_t j = 0; j < nb; ++j) out[j] = blocks[j] * Hkv + h;
+    pos += nb;
   }
   // Owner of stream index x: the w with bounds[w] <= x < bounds[w+1]; the
   // queries below only move forward, so a cursor per query suffices.

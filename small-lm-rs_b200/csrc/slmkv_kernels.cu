@@ -335,52 +335,76 @@ __device__ __forceinline__ PairFields pair_from_window(const int4& a, const int4
 
 // Merges n segment partials (each G x (acc[64], (m, l))) for this lane's two
 // output dims: partial s is weighted by 2^(m_s - M), summed in slot order.
-// acc_at(s, g) / ml_at(s, g) read one partial; the (m, l) pairs are loaded
-// lane-parallel and the acc loads are issued four at a time.
+// acc_at(s, g) / ml_at(s, g) read one partial. The (m, l) pairs of up to 32
+// partials are loaded lane-parallel and the first four partials' acc rows are
+// loaded before any of them is used, so a merge of up to four partials (the
+// common case) waits for one round of loads, whatever G.
 template <int G, typename Acc, typename Ml>
 __device__ __forceinline__ void merge_partials(int n, int lane, Acc acc_at, Ml ml_at, float2 (&A)[G],
                                                float (&Mo)[G], float (&Lo)[G]) {
+  float M[G], Ls[G];
+  float2 a2[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    float M = -INFINITY, Ls = 0.f;
-    float2 a2 = make_float2(0.f, 0.f);
-    for (int base = 0; base < n; base += 32) {
-      const int cnt = min(32, n - base);
-      const float2 mine = (lane < cnt) ? ml_at(base + lane, g) : make_float2(-INFINITY, 0.f);
-      float Mc = mine.x;
+    M[g] = -INFINITY;
+    Ls[g] = 0.f;
+    a2[g] = make_float2(0.f, 0.f);
+  }
+  for (int base = 0; base < n; base += 32) {
+    const int cnt = min(32, n - base);
+    float2 mine[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      mine[g] = (lane < cnt) ? ml_at(base + lane, g) : make_float2(-INFINITY, 0.f);
+    float2 a[4][G];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int g = 0; g < G; ++g) a[u][g] = (u < cnt) ? acc_at(base + u, g) : make_float2(0.f, 0.f);
+    float fmine[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float Mc = mine[g].x;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) Mc = fmaxf(Mc, __shfl_xor_sync(kFull, Mc, off));
-      const float Mn = fmaxf(M, Mc);
-      const float rescale = exp2f(M - Mn);  // M = -inf on the first chunk: 0
-      a2.x *= rescale;
-      a2.y *= rescale;
-      Ls *= rescale;
-      M = Mn;
-      const float fmine = exp2f(mine.x - M);  // lanes past cnt: 0
-      float lsum = mine.y * fmine;
+      const float Mn = fmaxf(M[g], Mc);
+      const float rescale = exp2f(M[g] - Mn);  // M = -inf on the first chunk: 0
+      a2[g].x *= rescale;
+      a2[g].y *= rescale;
+      Ls[g] *= rescale;
+      M[g] = Mn;
+      fmine[g] = exp2f(mine[g].x - Mn);  // lanes past cnt: 0
+      float lsum = mine[g].y * fmine[g];
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(kFull, lsum, off);
-      Ls += lsum;
-      for (int s0 = 0; s0 < cnt; s0 += 4) {
-        float2 a[4];
-        float f[4];
+      Ls[g] += lsum;
+    }
+    for (int s0 = 0; s0 < cnt; s0 += 4) {
+      if (s0 > 0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int g = 0; g < G; ++g)
+            a[u][g] = (s0 + u < cnt) ? acc_at(base + s0 + u, g) : make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          f[u] = __shfl_sync(kFull, fmine, min(s0 + u, 31));
-          a[u] = (s0 + u < cnt) ? acc_at(base + s0 + u, g) : make_float2(0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
+          const float f = __shfl_sync(kFull, fmine[g], min(s0 + u, 31));
           if (s0 + u < cnt) {
-            a2.x = fmaf(a[u].x, f[u], a2.x);
-            a2.y = fmaf(a[u].y, f[u], a2.y);
+            a2[g].x = fmaf(a[u][g].x, f, a2[g].x);
+            a2[g].y = fmaf(a[u][g].y, f, a2[g].y);
           }
         }
       }
     }
-    A[g] = a2;
-    Mo[g] = M;
-    Lo[g] = Ls;
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    A[g] = a2[g];
+    Mo[g] = M[g];
+    Lo[g] = Ls[g];
   }
 }
 
@@ -399,33 +423,22 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
   int* cta_cnt = reinterpret_cast<int*>(smem + Sh::kOffCnt);
 
   if (threadIdx.x < 2 * W) cta_cnt[threadIdx.x] = 0;
-  // Launched with programmatic stream serialization: everything above ran
-  // while the previous kernel of the stream was finishing; wait for it (and
-  // its memory) before touching anything in global memory.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  __syncthreads();  // the only CTA-wide barrier; the warps are independent after it
-
   const int gw = blockIdx.x * W + warp;
-  if (gw >= p.n_warps) return;
-  const int cta_w0 = blockIdx.x * W;
-  const int cta_w1 = min(cta_w0 + W, p.n_warps) - 1;
-
-  const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
-  const size_t layer_elems = static_cast<size_t>(p.layer) * p.g.layer_elems;
-  const uint8_t* kbase = static_cast<const uint8_t*>(p.g.k) + layer_elems * Sh::kEsz;
-  const uint8_t* vbase = static_cast<const uint8_t*>(p.g.v) + layer_elems * Sh::kEsz;
-  const uint32_t max_chunk = static_cast<uint32_t>(p.g.num_blocks) * Hkv;
+  const bool active = gw < p.n_warps;
 
   // Start record: {first pair, seq, head, ctx_len}, {first pair's end in the
   // stream, g0, g1, -}; the warp owns stream blocks [g0, g1) (never empty).
-  const int4 r0 = p.warp_start[2 * gw], r1 = p.warp_start[2 * gw + 1];
-  const int g0 = r1.y, g1 = r1.z;
-
-  if (lane == 0) {
-    for (int s = 0; s < R; ++s) mbar_init(&bars[s], 1);
-    fence_mbar_init();
+  // The step plan (start records, chunk stream, pair entries) is written only
+  // by host-to-device copies ordered before the previous kernel of the stream,
+  // never by a kernel, so it is read before the wait below.
+  int4 r0 = make_int4(0, 0, 0, 0), r1 = r0;
+  if (active) {
+    r0 = p.warp_start[2 * gw];
+    r1 = p.warp_start[2 * gw + 1];
   }
-  __syncwarp();
+  const int g0 = r1.y, g1 = r1.z;
+  int cwin = g0;
+  int cval = (g0 + lane < g1) ? p.chunks[g0 + lane] : 0;
 
   // ---- pair window: one PairEntry per lane, shared by producer and consumer --
   int pwin = r0.x;
@@ -438,22 +451,37 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
       pb = e[1];
     }
   };
+  if (active) load_window(r0.x);
+  if (active && lane == 0) {
+    for (int s = 0; s < R; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+
+  // Launched with programmatic stream serialization: everything above ran
+  // while the previous kernel of the stream was finishing; wait for it (and
+  // its memory) before touching the pool, the step's inputs or the split-K
+  // scratch.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __syncthreads();  // the only CTA-wide barrier; the warps are independent after it
+  if (!active) return;
+  const int cta_w0 = blockIdx.x * W;
+  const int cta_w1 = min(cta_w0 + W, p.n_warps) - 1;
+
+  const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
+  const size_t layer_elems = static_cast<size_t>(p.layer) * p.g.layer_elems;
+  const uint8_t* kbase = static_cast<const uint8_t*>(p.g.k) + layer_elems * Sh::kEsz;
+  const uint8_t* vbase = static_cast<const uint8_t*>(p.g.v) + layer_elems * Sh::kEsz;
+  const uint32_t max_chunk = static_cast<uint32_t>(p.g.num_blocks) * Hkv;
 
   // ---- producer: lane 0 keeps R stages in flight ahead of the consumer ------
-  int cwin = g0;
-  int cval = (g0 + lane < g1) ? p.chunks[g0 + lane] : 0;
   int pg = g0;  // next stream block to issue
   int pp = r0.x, pp_seq = r0.y, pp_head = r0.z, pp_L = r0.w, pp_end = r1.x;
   int pp_first = g0;  // first block of pair pp in this warp
   int pc = r0.x;      // the consumer's pair; the window never moves past it
-  bool window_loaded = false;
   auto issue = [&](int stage) {
     if (pg == pp_end) {  // the producer enters the next pair
       ++pp;
-      if (!window_loaded || pp - pwin >= 32) {
-        load_window(pc);
-        window_loaded = true;
-      }
+      if (pp - pwin >= 32) load_window(pc);
       const PairFields f = pair_from_window(pa, pb, pp - pwin);
       pp_seq = f.seq;
       pp_head = f.head;
@@ -498,10 +526,6 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
     ++pg;
   };
   for (int s = 0; s < R && pg < g1; ++s) issue(s);
-  if (!window_loaded) {
-    load_window(pc);
-    window_loaded = true;
-  }
 
   // ---- consumer --------------------------------------------------------------
   PairFields cur = pair_from_window(pa, pb, pc - pwin);
@@ -691,19 +715,29 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
 
   // ---- pairs that span CTAs: the last CTA to arrive merges the partials -----
   if (npend == 0) return;
-  __threadfence();
+  // Release this warp's partials, then arrive on each pair's counter (both
+  // arrivals in flight together); the last CTA to arrive acquires and merges.
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
   __syncwarp();
-  for (int k = 0; k < npend; ++k) {
-    const int4 e = (k == 0) ? pend0 : pend1;
-    int last = 0;
-    if (lane == 0) {
-      const int prev = atomicAdd(&p.counters[e.x], 1);
-      last = (prev == e.z - 1);
-      if (last) atomicExch(&p.counters[e.x], 0);  // ready for the next launch
+  int lastmask = 0;
+  if (lane == 0) {
+    const int prev0 = atomicAdd(&p.counters[pend0.x], 1);
+    const int prev1 = (npend > 1) ? atomicAdd(&p.counters[pend1.x], 1) : 0;
+    if (prev0 == pend0.z - 1) {
+      lastmask |= 1;
+      atomicExch(&p.counters[pend0.x], 0);  // ready for the next launch
     }
-    last = __shfl_sync(kFull, last, 0);
-    if (!last) continue;
-    __threadfence();
+    if (npend > 1 && prev1 == pend1.z - 1) {
+      lastmask |= 2;
+      atomicExch(&p.counters[pend1.x], 0);
+    }
+  }
+  lastmask = __shfl_sync(kFull, lastmask, 0);
+  if (lastmask == 0) return;
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  for (int k = 0; k < npend; ++k) {
+    if (!((lastmask >> k) & 1)) continue;
+    const int4 e = (k == 0) ? pend0 : pend1;
     auto acc_at = [&](int s, int g2) {
       return __ldcg(reinterpret_cast<const float2*>(
                         p.part_acc + ((static_cast<size_t>(e.y) + s) * G + g2) * D) + lane);
