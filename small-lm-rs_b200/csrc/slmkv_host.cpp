@@ -106,6 +106,10 @@ struct slm_ctx {
   int64_t max_chunks = 0;  // max_sequences x blocks per sequence x Hkv
   int64_t device_bytes = 0;
   int64_t launches = 0;  // kernels launched by this context
+  // Layer of the last launch when it was a batch decode, else -1: a batch
+  // decode of another layer right after it may fetch its first K/V stages
+  // before waiting on it (nothing else has written the pool since).
+  int32_t prev_decode_layer = -1;
   std::string err;
 
   // device memory
@@ -385,6 +389,7 @@ slm_status flush_excess(slm_ctx* c, cudaStream_t s, size_t keep_updates, size_t 
     memcpy(h + L.updates, c->pending_updates.data(), nu * sizeof(TableUpdate));
     memcpy(h + L.copies, c->pending_copies.data(), nc * sizeof(CopyJob));
     CU(c, upload_end(c->up_aux, L.total, s));
+    c->prev_decode_layer = -1;
     CU(c, launch_apply_updates(c->geom(), reinterpret_cast<TableUpdate*>(c->up_aux.d + L.updates),
                                static_cast<int32_t>(nu),
                                reinterpret_cast<CopyJob*>(c->up_aux.d + L.copies),
@@ -536,6 +541,7 @@ slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<
   if (nc) memcpy(h + L.copies, c->pending_copies.data(), nc * sizeof(CopyJob));
   CU(c, upload_end(u, L.total, s));
   if (nu || nc) {
+    c->prev_decode_layer = -1;
     CU(c, launch_apply_updates(c->geom(), reinterpret_cast<TableUpdate*>(u.d + L.updates),
                                static_cast<int32_t>(nu), reinterpret_cast<CopyJob*>(u.d + L.copies),
                                static_cast<int32_t>(nc), s));
@@ -995,6 +1001,7 @@ slm_status slm_append_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, const f
   a.v_in = d_values;
   a.rotate = rotate_keys != 0;
   a.status = d_status;
+  ctx->prev_decode_layer = -1;
   CU(ctx, launch_append(a, s));
   ++ctx->launches;
   int32_t status = 0;
@@ -1031,6 +1038,7 @@ slm_status slm_gather_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, float* 
   gl.length = q->layer_len[layer];
   gl.k_out = d_keys;
   gl.v_out = d_values;
+  ctx->prev_decode_layer = -1;
   CU(ctx, launch_gather(gl, s));
   ++ctx->launches;
   return SLM_OK;
@@ -1065,6 +1073,7 @@ slm_status slm_attend_cached_query(slm_ctx* ctx, int32_t seq_id, int32_t layer,
   p.q = d_query;
   p.out = d_out;
   p.fused = 0;
+  ctx->prev_decode_layer = -1;
   CU(ctx, launch_decode(p, s));
   ++ctx->launches;
   return SLM_OK;
@@ -1206,6 +1215,8 @@ slm_status slm_batch_decode_layer(slm_batch* b, int32_t layer, const float* d_qu
   p.v_new = d_values;
   p.out = d_out;
   p.fused = 1;
+  p.early_kv = (ctx->prev_decode_layer >= 0 && ctx->prev_decode_layer != layer) ? 1 : 0;
+  ctx->prev_decode_layer = layer;
   CU(ctx, launch_decode(p, b->stream));
   ++ctx->launches;
   b->layer_done[layer] = 1;
@@ -1235,6 +1246,7 @@ slm_status slm_batch_append_layer(slm_batch* b, int32_t layer, const float* d_ke
   a.v_in = d_values;
   a.rotate = rotate_keys != 0;
   a.status = b->dev.status;
+  ctx->prev_decode_layer = -1;
   CU(ctx, launch_append(a, b->stream));
   ++ctx->launches;
   b->layer_done[layer] = 1;
@@ -1268,6 +1280,7 @@ slm_status slm_batch_prefill_attention(slm_batch* b, int32_t layer, const float*
   p.rotate = rotate_query != 0;
   p.out = d_out;
   p.max_count = b->max_count;
+  ctx->prev_decode_layer = -1;
   CU(ctx, launch_prefill(p, b->stream));
   ++ctx->launches;
   return SLM_OK;

@@ -92,6 +92,10 @@ struct StreamDecodeLaunch {
   int32_t* counters;   // [n_pairs], zero between launches
   int32_t* status;     // [n]
   int32_t fused;       // 1: rope(q,k) + append + attend; 0: attend (q rotated)
+  // 1: this layer's pool region was last written by a launch that completed
+  // before the previous kernel of the stream started, so the first K/V stages
+  // may be fetched before waiting on that kernel (set by the host).
+  int32_t early_kv;
 };
 cudaError_t launch_decode(const StreamDecodeLaunch& p, cudaStream_t s);
 

@@ -308,7 +308,8 @@ struct StreamShape {
   static constexpr int kOffBars = kOffSlots + 2 * W * kSlot;
   static constexpr int kOffChunk = kOffBars + W * R * 8;
   static constexpr int kOffCnt = kOffChunk + W * R * 4;
-  static constexpr int kSmem = kOffCnt + 2 * W * 4;
+  static constexpr int kOffPend = (kOffCnt + 2 * W * 4 + 15) / 16 * 16;
+  static constexpr int kSmem = kOffPend + W * R * 16;
   static_assert(kSmem <= 227 * 1024, "decode staging exceeds shared memory");
   static_assert(kChunk % 16 == 0 && kSide % 16 == 0 && kSlot % 16 == 0, "16-byte alignment");
 };
@@ -421,6 +422,7 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sh::kOffBars) + warp * R;
   int* stage_chunk = reinterpret_cast<int*>(smem + Sh::kOffChunk) + warp * R;
   int* cta_cnt = reinterpret_cast<int*>(smem + Sh::kOffCnt);
+  int4* side_pend = reinterpret_cast<int4*>(smem + Sh::kOffPend) + warp * R;
 
   if (threadIdx.x < 2 * W) cta_cnt[threadIdx.x] = 0;
   const int gw = blockIdx.x * W + warp;
@@ -456,14 +458,6 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
     for (int s = 0; s < R; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
-
-  // Launched with programmatic stream serialization: everything above ran
-  // while the previous kernel of the stream was finishing; wait for it (and
-  // its memory) before touching the pool, the step's inputs or the split-K
-  // scratch.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  __syncthreads();  // the only CTA-wide barrier; the warps are independent after it
-  if (!active) return;
   const int cta_w0 = blockIdx.x * W;
   const int cta_w1 = min(cta_w0 + W, p.n_warps) - 1;
 
@@ -478,7 +472,24 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
   int pp = r0.x, pp_seq = r0.y, pp_head = r0.z, pp_L = r0.w, pp_end = r1.x;
   int pp_first = g0;  // first block of pair pp in this warp
   int pc = r0.x;      // the consumer's pair; the window never moves past it
-  auto issue = [&](int stage) {
+  // Side copies of a stage that starts a pair (lane 0): the pair's Q rows,
+  // its RoPE row and, when this warp ends the pair, the new K/V rows.
+  auto issue_side = [&](int stage, int seq, int head, int L, bool appends) {
+    uint8_t* sd = sides + stage * Sh::kSide;
+    bulk_load(sd, p.q + (static_cast<size_t>(seq) * Hq + head * G) * D, G * D * 4, &bars[stage]);
+    if (p.fused)
+      bulk_load(sd + Sh::kSideCs, p.g.rope + static_cast<size_t>(L - 1) * (D / 2), (D / 2) * 8,
+                &bars[stage]);
+    if (appends) {
+      const size_t row = (static_cast<size_t>(seq) * Hkv + head) * D;
+      bulk_load(sd + Sh::kSideKn, p.k_new + row, D * 4, &bars[stage]);
+      bulk_load(sd + Sh::kSideVn, p.v_new + row, D * 4, &bars[stage]);
+    }
+  };
+  // Arms the next stage and copies its K/V chunks; with defer_side the side
+  // copies are recorded in side_pend and issued later on the same barrier
+  // (its expected byte count already includes them).
+  auto issue = [&](int stage, bool defer_side) {
     if (pg == pp_end) {  // the producer enters the next pair
       ++pp;
       if (pp - pwin >= 32) load_window(pc);
@@ -501,7 +512,6 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
       }
       stage_chunk[stage] = static_cast<int>(chunk);
       uint8_t* st = stages + stage * Sh::kStage;
-      uint8_t* sd = sides + stage * Sh::kSide;
       const bool first = (pg == pp_first);
       const bool appends = p.fused && first && (pp_end - 1 < g1);
       uint32_t tx = Sh::kStage;
@@ -510,23 +520,40 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
       bulk_load(st, kbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk, &bars[stage]);
       bulk_load(st + Sh::kChunk, vbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk,
                 &bars[stage]);
-      if (first) {
-        bulk_load(sd, p.q + (static_cast<size_t>(pp_seq) * Hq + pp_head * G) * D, G * D * 4,
-                  &bars[stage]);
-        if (p.fused)
-          bulk_load(sd + Sh::kSideCs, p.g.rope + static_cast<size_t>(pp_L - 1) * (D / 2),
-                    (D / 2) * 8, &bars[stage]);
-        if (appends) {
-          const size_t row = (static_cast<size_t>(pp_seq) * Hkv + pp_head) * D;
-          bulk_load(sd + Sh::kSideKn, p.k_new + row, D * 4, &bars[stage]);
-          bulk_load(sd + Sh::kSideVn, p.v_new + row, D * 4, &bars[stage]);
-        }
-      }
+      if (defer_side)
+        side_pend[stage] = first ? make_int4(pp_seq, pp_head, pp_L, appends ? 1 : 0)
+                                 : make_int4(0, 0, 0, -1);
+      else if (first)
+        issue_side(stage, pp_seq, pp_head, pp_L, appends);
     }
     ++pg;
   };
-  for (int s = 0; s < R && pg < g1; ++s) issue(s);
 
+  // The first stages' K/V may be fetched before waiting on the previous
+  // kernel when the host says this layer's pool region was complete before
+  // that kernel started (the previous kernel is a decode of another layer).
+  if (active && p.early_kv)
+    for (int s = 0; s < R && pg < g1; ++s) issue(s, true);
+
+  // Launched with programmatic stream serialization: everything above ran
+  // while the previous kernel of the stream was finishing; wait for it (and
+  // its memory) before touching the step's inputs, the outputs or the split-K
+  // scratch. Then everything before this kernel in the stream is complete and
+  // visible, and the next kernel may launch: its CTAs start on the SMs this
+  // kernel's CTAs leave, and run their own prologue meanwhile.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __syncthreads();  // the only CTA-wide barrier; the warps are independent after it
+  if (!active) return;
+  if (p.early_kv) {
+    if (lane == 0)
+      for (int s = 0; s < pg - g0; ++s) {
+        const int4 e = side_pend[s];
+        if (e.w >= 0) issue_side(s, e.x, e.y, e.z, e.w != 0);
+      }
+  } else {
+    for (int s = 0; s < R && pg < g1; ++s) issue(s, false);
+  }
   // ---- consumer --------------------------------------------------------------
   PairFields cur = pair_from_window(pa, pb, pc - pwin);
   float m[G], l[G];
@@ -616,7 +643,7 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
       // The stage (and its side buffer) were read, maybe written, through
       // the generic proxy; order that before the async-proxy refill.
       if (append_here) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(stage);
+      issue(stage, false);
     }
 
     if (g != seg_end - 1) continue;
