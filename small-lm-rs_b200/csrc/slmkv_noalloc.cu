@@ -41,7 +41,7 @@ namespace {
 constexpr int kMaxPairs = 4096;                // (sequence, KV head) pairs per call
 constexpr int kMaxChunks = 131072;             // stream blocks per call (16-token blocks x heads)
 constexpr int kMaxSms = 160;                   // decode CTAs (one per SM)
-constexpr int kMaxWarps = kMaxSms * 10;        // decode warps: SMs x warps per CTA (<= 10)
+constexpr int kMaxWarps = kMaxSms * kMaxDecodeWarps;  // decode warps: SMs x warps per CTA
 constexpr int kMaxGroup = 8;                   // query heads per KV head
 constexpr int kMaxSlots = 2 * kMaxSms;         // cross-CTA partials: < 2 per CTA
 
