@@ -303,13 +303,26 @@ def run_ours(args):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
 
+    # Steps are pipelined (slm_batch_submit / slm_batch_wait): a step is
+    # submitted without waiting for the GPU, the next one is planned and
+    # queued while it runs, and its statuses are collected one step later.
+    # Every step's statuses are checked.
+    inflight = []
+
+    def collect(keep):
+        while len(inflight) > keep:
+            st = inflight.pop(0).wait()
+            if any(st):
+                raise RuntimeError(f"decode step failed: {st}")
+
     def step(timed_index=None, layer_ptrs=ptrs):
         batch = plan.begin()
         for layer in range(LAYERS):
             batch.decode_layer_ptr(layer, *layer_ptrs[layer])
             if timed_index is not None and layer in (0, LAYERS - 1):
                 ev[timed_index][0 if layer == 0 else 1].record(stream)
-        batch.end()
+        inflight.append(batch.submit())
+        collect(1)
         plan.truncate_all(base_arr)
 
     sampler = ClockSampler(local) if rank == 0 else None
@@ -317,6 +330,7 @@ def run_ours(args):
         sampler.start()
     for _ in range(max(args.warmup, 3)):
         step()
+    collect(0)
     torch.cuda.synchronize()
     barrier()
     launches0 = pool.launch_count()
@@ -326,6 +340,7 @@ def run_ours(args):
     for i in range(args.steps):
         step(i)
     t_stop.record(stream)
+    collect(0)
     torch.cuda.synchronize()
     barrier()
     launches = pool.launch_count() - launches0
@@ -354,11 +369,13 @@ def run_ours(args):
         for layer in range(LAYERS):
             batch.decode_layer_ptr(layer, *dptrs[layer])
         ho_.copy_(do, non_blocking=True)
-        batch.end()
+        inflight.append(batch.submit())
+        collect(1)
         plan.truncate_all(base_arr)
 
     for _ in range(3):
         e2e_step()
+    collect(0)
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -366,6 +383,7 @@ def run_ours(args):
     for _ in range(args.steps):
         e2e_step()
     e1.record(stream)
+    collect(0)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e0.elapsed_time(e1)

@@ -178,6 +178,19 @@ slm_status slm_batch_prefill_attention(slm_batch* batch, int32_t layer, const fl
 slm_status slm_batch_end(slm_batch* batch, int32_t* h_status);
 /* Abandons the step: every sequence goes back to its begin length. */
 slm_status slm_batch_rollback(slm_batch* batch);
+/* Pipelined steps (no reference counterpart: the reference runs one request
+ * at a time, worker.rs:87-98). slm_batch_submit closes the step without
+ * waiting for the GPU: the per-sequence status is copied back on the batch's
+ * stream and the next step may begin at once, planned on the advanced
+ * lengths. At most 2 submitted batches may be pending. slm_batch_wait waits
+ * for a submitted batch and reports like slm_batch_end; batches resolve in
+ * submission order (waiting for a later one resolves the earlier ones, whose
+ * own wait then returns at once), and every submitted batch must be waited
+ * for. A sequence that fails is rolled back to its length at that batch's
+ * begin, and every later batch holding it reports the same failure and rolls
+ * it back to the same length. slm_batch_end is submit + wait. */
+slm_status slm_batch_submit(slm_batch* batch);
+slm_status slm_batch_wait(slm_batch* batch, int32_t* h_status);
 
 /* ---- prefix cache (no reference counterpart; README.md:247 lists it as
  *      future work). Full 16-token blocks are indexed by their token chain. -- */

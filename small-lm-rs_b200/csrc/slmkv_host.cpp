@@ -16,6 +16,7 @@
 #include <random>
 #include <string>
 #include <unordered_map>
+#include <deque>
 #include <vector>
 
 #include <cuda_runtime.h>
@@ -28,13 +29,18 @@ using namespace slmkv;
 namespace {
 
 constexpr int kUploadSlots = 2;
+// Batches that may be submitted and not yet resolved at once, and readback
+// slots (one more, for slm_batch_end while that many are in flight).
+constexpr int kMaxInFlight = 2;
+constexpr int kReadbackSlots = kMaxInFlight + 1;
 
 struct Seq {
   bool live = false;
   int32_t max_len = 0;
   std::vector<int32_t> layer_len;
   std::vector<int32_t> blocks;  // logical block -> physical id
-  bool in_batch = false;
+  bool in_batch = false;  // in the open batch
+  int32_t in_flight = 0;  // submitted batches not yet resolved that hold it
 };
 
 struct BlockMeta {
@@ -93,6 +99,17 @@ struct slm_batch {
   int32_t n_pairs = 0, total_blocks = 0;  // decode plan (when every count is 1)
   std::vector<uint8_t> layer_done;
   StepDev dev;
+  // Submitted (slm_batch_submit): its status readback slot; per sequence
+  // whether every layer advanced, and a rollback forced by an earlier batch
+  // (poison_base >= 0: roll back to at most that length with poison_code).
+  bool submitted = false, resolved = false;
+  int32_t rb_slot = -1;
+  std::vector<uint8_t> complete;
+  std::vector<int32_t> poison_base, poison_code;
+  // Resolved: per-sequence status, the first failure and its message.
+  std::vector<int32_t> codes;
+  slm_status first = SLM_OK;
+  std::string msg;
 };
 
 struct slm_ctx {
@@ -122,6 +139,12 @@ struct slm_ctx {
   int32_t* d_counters = nullptr;
   int32_t* d_error = nullptr;
   int32_t* h_readback = nullptr;  // pinned: [1 + max_sequences]
+  // Pinned status readback of submitted batches: kReadbackSlots slots of
+  // [error word, pad, status x max_sequences], each with its event.
+  int32_t* h_rb = nullptr;
+  cudaEvent_t rb_ev[kReadbackSlots] = {};
+  bool rb_busy[kReadbackSlots] = {};
+  std::deque<slm_batch*> submitted;  // oldest first
   Upload up_batch, up_aux;
   size_t upd_cap = 0, copy_cap = 0;
 
@@ -620,6 +643,9 @@ void destroy_device(slm_ctx* c) {
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (c->h_readback) cudaFreeHost(c->h_readback);
+  if (c->h_rb) cudaFreeHost(c->h_rb);
+  for (cudaEvent_t ev : c->rb_ev)
+    if (ev) cudaEventDestroy(ev);
   upload_free(c->up_batch);
   upload_free(c->up_aux);
 }
@@ -740,6 +766,11 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
     if (rc == SLM_OK) {
       e = cudaMallocHost(reinterpret_cast<void**>(&cp->h_readback),
                          sizeof(int32_t) * (k.max_sequences + 1));
+      if (e == cudaSuccess)
+        e = cudaMallocHost(reinterpret_cast<void**>(&cp->h_rb),
+                           sizeof(int32_t) * kReadbackSlots * (k.max_sequences + 2));
+      for (int i = 0; e == cudaSuccess && i < kReadbackSlots; ++i)
+        e = cudaEventCreateWithFlags(&cp->rb_ev[i], cudaEventDisableTiming);
       if (e != cudaSuccess) rc = cuda_fail(cp, e, "cudaMallocHost");
     }
     if (rc == SLM_OK) {
@@ -778,6 +809,7 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
 slm_status slm_destroy(slm_ctx* ctx) {
   if (!ctx) return SLM_ERR_INVALID_INPUT;
   delete ctx->open_batch;
+  for (slm_batch* b : ctx->submitted) delete b;
   destroy_device(ctx);
   delete ctx;
   return SLM_OK;
@@ -829,6 +861,9 @@ slm_status slm_seq_free(slm_ctx* ctx, int32_t seq_id) {
   if (s->in_batch)
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
                        "sequence %d belongs to an open batch", seq_id);
+  if (s->in_flight)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                       "sequence %d has a submitted step; wait for it first", seq_id);
   release_tail(ctx, seq_id, 0);
   s->live = false;
   s->layer_len.clear();
@@ -1093,6 +1128,12 @@ slm_status slm_batch_begin(slm_ctx* ctx, int32_t n, const int32_t* h_seq_ids,
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "batch size %d is outside 1..=%d", n,
                        ctx->cfg.max_sequences);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The step descriptor region is reused: a step on another stream than the
+  // last submitted one starts after that one's kernels.
+  if (!ctx->submitted.empty() && ctx->submitted.back()->stream != s) {
+    const cudaError_t e = cudaStreamWaitEvent(s, ctx->rb_ev[ctx->submitted.back()->rb_slot], 0);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "slm_batch_begin");
+  }
   // Validate everything before mutating anything.
   auto unmark = [&](int32_t upto) {
     for (int32_t i = 0; i < upto; ++i) ctx->seqs[h_seq_ids[i]].in_batch = false;
@@ -1287,70 +1328,179 @@ slm_status slm_batch_prefill_attention(slm_batch* b, int32_t layer, const float*
 }
 
 namespace {
-void batch_restore(slm_batch* b, const std::vector<char>& roll) {
+// Rolls sequence `id` back to at most `target` tokens in every layer and
+// forces the same rollback on every later batch (submitted or open) that
+// holds it: those were planned on the lengths this rollback undoes.
+void roll_back_seq(slm_ctx* ctx, const slm_batch* from, int32_t id, int32_t target, int32_t code) {
+  Seq& q = ctx->seqs[id];
+  for (auto& v : q.layer_len) v = std::min(v, target);
+  release_tail(ctx, id, blocks_for(seq_max_len(q)));
+  bool later = false;
+  auto poison = [&](slm_batch* m) {
+    for (size_t j = 0; j < m->seq_ids.size(); ++j)
+      if (m->seq_ids[j] == id) {
+        if (m->poison_base[j] < 0 || target < m->poison_base[j]) m->poison_base[j] = target;
+        if (!m->poison_code[j]) m->poison_code[j] = code;
+      }
+  };
+  for (slm_batch* m : ctx->submitted) {
+    if (m == from) {
+      later = true;
+      continue;
+    }
+    if (later && !m->resolved) poison(m);
+  }
+  if (ctx->open_batch && ctx->open_batch != from) poison(ctx->open_batch);
+}
+
+// Drops an open batch (slm_batch_rollback, or a failed submit): every
+// sequence back to its begin length.
+void batch_discard(slm_batch* b) {
   slm_ctx* ctx = b->ctx;
   for (size_t i = 0; i < b->seq_ids.size(); ++i) {
-    Seq& q = ctx->seqs[b->seq_ids[i]];
-    q.in_batch = false;
-    if (roll[i]) {
-      for (auto& v : q.layer_len) v = b->base[i];
-      release_tail(ctx, b->seq_ids[i], blocks_for(b->base[i]));
-    }
+    ctx->seqs[b->seq_ids[i]].in_batch = false;
+    roll_back_seq(ctx, b, b->seq_ids[i], b->base[i], SLM_ERR_INVALID_INPUT);
   }
   ctx->open_batch = nullptr;
   delete b;
 }
-}  // namespace
 
-slm_status slm_batch_end(slm_batch* b, int32_t* h_status) {
-  if (!b) return SLM_ERR_INVALID_INPUT;
+// Resolves the oldest submitted batch: waits for its status readback, sets
+// each sequence's status and rolls failed sequences back
+// (model.rs:390-396), in submission order.
+void resolve_oldest(slm_ctx* ctx) {
+  slm_batch* b = ctx->submitted.front();
+  const size_t n = b->seq_ids.size();
+  const int32_t* rb = ctx->h_rb + static_cast<size_t>(b->rb_slot) * (ctx->cfg.max_sequences + 2);
+  const cudaError_t e = cudaEventSynchronize(ctx->rb_ev[b->rb_slot]);
+  slm_status dev = SLM_OK;
+  std::string dev_msg;
+  if (e != cudaSuccess) {
+    dev = SLM_ERR_CUDA;
+    dev_msg = std::string("CUDA error in slm_batch_wait: ") + cudaGetErrorString(e);
+  } else if (rb[0]) {
+    const int32_t w = rb[0];
+    cudaMemsetAsync(ctx->d_error, 0, sizeof(int32_t), b->stream);
+    cudaMemsetAsync(ctx->d_counters, 0, sizeof(int32_t) * ctx->max_pairs, b->stream);
+    char buf[160];
+    if (w & kErrTimeout) {
+      dev = SLM_ERR_DEVICE_TIMEOUT;
+      snprintf(buf, sizeof buf, "device wait timed out (error word 0x%x)", w);
+    } else {
+      dev = SLM_ERR_INVALID_INPUT;
+      snprintf(buf, sizeof buf,
+               "invalid input for KV cache: block table held an out-of-pool id (0x%x)", w);
+    }
+    dev_msg = buf;
+  }
+  b->codes.assign(n, SLM_OK);
+  for (size_t i = 0; i < n; ++i) {
+    const int32_t st = (dev == SLM_OK) ? rb[2 + i] : 0;
+    int32_t code = SLM_OK;
+    if (dev != SLM_OK) code = dev;
+    else if (b->poison_base[i] >= 0) code = b->poison_code[i];
+    else if (st & kStatusNonFinite) code = SLM_ERR_NON_FINITE;
+    else if (!b->complete[i]) code = SLM_ERR_INVALID_INPUT;
+    b->codes[i] = code;
+    if (code != SLM_OK && b->first == SLM_OK) b->first = code;
+  }
+  for (size_t i = 0; i < n; ++i) {
+    const int32_t id = b->seq_ids[i];
+    --ctx->seqs[id].in_flight;
+    if (b->codes[i] != SLM_OK) {
+      int32_t target = b->base[i];
+      if (b->poison_base[i] >= 0) target = std::min(target, b->poison_base[i]);
+      roll_back_seq(ctx, b, id, target, b->codes[i]);
+    }
+  }
+  if (b->first == SLM_ERR_NON_FINITE)
+    b->msg = "invalid input for KV cache: all appended key/value values must be finite";
+  else if (dev != SLM_OK)
+    b->msg = dev_msg;
+  else if (b->first == SLM_ERR_INVALID_INPUT)
+    b->msg = "invalid input for model cached decode: all cache layers must advance by exactly "
+             "one step";
+  b->resolved = true;
+  ctx->rb_busy[b->rb_slot] = false;
+  ctx->submitted.pop_front();
+}
+
+slm_status submit(slm_batch* b, bool extra_slot) {
   slm_ctx* ctx = b->ctx;
   if (ctx->open_batch != b)
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "the batch is not open");
+  if (!extra_slot && ctx->submitted.size() >= static_cast<size_t>(kMaxInFlight))
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
+                       "at most %d submitted batches may be pending; wait for one first",
+                       kMaxInFlight);
+  int slot = -1;
+  for (int k = 0; k < kReadbackSlots && slot < 0; ++k)
+    if (!ctx->rb_busy[k]) slot = k;
   const size_t n = b->seq_ids.size();
-  std::vector<char> roll(n, 0);
-  slm_status first = SLM_OK;
-  cudaError_t e =
-      cudaMemcpyAsync(ctx->h_readback, b->dev.status, sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
-                      b->stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+  cudaError_t e = cudaErrorNotReady;
+  if (slot >= 0 && has_device(ctx)) {
+    int32_t* rb = ctx->h_rb + static_cast<size_t>(slot) * (ctx->cfg.max_sequences + 2);
+    e = cudaMemcpyAsync(rb + 2, b->dev.status, sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
+                        b->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(rb, ctx->d_error, sizeof(int32_t), cudaMemcpyDeviceToHost, b->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(ctx->rb_ev[slot], b->stream);
+  }
   if (e != cudaSuccess) {
-    std::fill(roll.begin(), roll.end(), 1);
-    batch_restore(b, roll);
-    return cuda_fail(ctx, e, "slm_batch_end");
+    batch_discard(b);
+    return slot < 0 ? input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "no readback slot free")
+                    : cuda_fail(ctx, e, "slm_batch_submit");
   }
-  slm_status dev = check_device_error(ctx);
+  b->complete.assign(n, 1);
+  b->poison_base.assign(n, -1);
+  b->poison_code.assign(n, 0);
   for (size_t i = 0; i < n; ++i) {
-    const Seq& q = ctx->seqs[b->seq_ids[i]];
+    Seq& q = ctx->seqs[b->seq_ids[i]];
     const int32_t want = b->base[i] + b->counts[i];
-    bool complete = true;
-    for (int32_t v : q.layer_len) complete = complete && (v == want);
-    const int32_t st = ctx->h_readback[i];
-    int32_t code = SLM_OK;
-    if (dev != SLM_OK) code = dev;
-    else if (st & kStatusNonFinite) code = SLM_ERR_NON_FINITE;
-    else if (!complete) code = SLM_ERR_INVALID_INPUT;
-    if (h_status) h_status[i] = code;
-    if (code != SLM_OK) {
-      roll[i] = 1;
-      if (first == SLM_OK) first = code;
-    }
+    for (int32_t v : q.layer_len) b->complete[i] = b->complete[i] && (v == want);
+    q.in_batch = false;
+    ++q.in_flight;
   }
-  if (first == SLM_ERR_NON_FINITE)
-    input_error(ctx, first, "KV cache", "all appended key/value values must be finite");
-  else if (first == SLM_ERR_INVALID_INPUT && dev == SLM_OK)
-    input_error(ctx, first, "model cached decode",
-                "all cache layers must advance by exactly one step");
-  batch_restore(b, roll);
-  return first;
+  b->submitted = true;
+  b->rb_slot = slot;
+  ctx->rb_busy[slot] = true;
+  ctx->open_batch = nullptr;
+  ctx->submitted.push_back(b);
+  return SLM_OK;
+}
+}  // namespace
+
+slm_status slm_batch_submit(slm_batch* b) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  return submit(b, false);
+}
+
+slm_status slm_batch_wait(slm_batch* b, int32_t* h_status) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_ctx* ctx = b->ctx;
+  if (!b->submitted)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "the batch was not submitted");
+  while (!b->resolved) resolve_oldest(ctx);
+  if (h_status)
+    for (size_t i = 0; i < b->codes.size(); ++i) h_status[i] = b->codes[i];
+  const slm_status rc = b->first;
+  if (rc != SLM_OK) ctx->err = b->msg;
+  delete b;
+  return rc;
+}
+
+slm_status slm_batch_end(slm_batch* b, int32_t* h_status) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  const slm_status rc = submit(b, true);
+  if (rc) return rc;
+  return slm_batch_wait(b, h_status);
 }
 
 slm_status slm_batch_rollback(slm_batch* b) {
   if (!b) return SLM_ERR_INVALID_INPUT;
   if (b->ctx->open_batch != b)
     return input_error(b->ctx, SLM_ERR_INVALID_INPUT, "batch", "the batch is not open");
-  std::vector<char> roll(b->seq_ids.size(), 1);
-  batch_restore(b, roll);
+  batch_discard(b);
   return SLM_OK;
 }
 

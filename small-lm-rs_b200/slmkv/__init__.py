@@ -120,6 +120,8 @@ SIGNATURES = {
     "slm_batch_prefill_attention": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
     "slm_batch_end": (C.c_int, [_vp, _pi32]),
     "slm_batch_rollback": (C.c_int, [_vp]),
+    "slm_batch_submit": (C.c_int, [_vp]),
+    "slm_batch_wait": (C.c_int, [_vp, _pi32]),
     "slm_prefix_attach": (C.c_int, [_vp, _i32, _pu32, _i32, _pi32]),
     "slm_prefix_publish": (C.c_int, [_vp, _i32, _pu32, _i32, _pi32]),
     "slm_pool_stats": (C.c_int, [_vp, _pi32, _pi32]),
@@ -453,6 +455,8 @@ class _Fast:
         self.begin = L.slm_batch_begin
         self.decode = L.slm_batch_decode_layer
         self.end = L.slm_batch_end
+        self.submit = L.slm_batch_submit
+        self.wait = L.slm_batch_wait
         self.truncate = L.slm_seqs_truncate_all
         self._bound = True
 
@@ -518,6 +522,35 @@ class Batch:
         rc = _fast.end(self._h, self._status)
         self._h = None
         self.statuses = list(self._status[: len(self.caches)])
+        if rc != OK and raise_on_error:
+            self.pool.check(rc)
+        return self.statuses
+
+    def submit(self) -> "Batch":
+        """Closes the step without waiting for the GPU (``slm_batch_submit``):
+        the next step may begin at once; ``wait()`` collects the statuses."""
+        if self._h is None:
+            raise EngineError("the batch is not open")
+        rc = _fast.submit(self._h)
+        if rc:
+            # refused (too many pending): the step is still open; a CUDA
+            # failure has rolled it back and closed it
+            if rc != ERR_INVALID_INPUT:
+                self._h = None
+            self.pool.check(rc)
+        self._submitted, self._h = self._h, None
+        return self
+
+    def wait(self, raise_on_error: bool = True) -> list[int]:
+        """Statuses of a submitted step (``slm_batch_wait``); failed sequences
+        were rolled back, and with them every later step that holds them."""
+        h = getattr(self, "_submitted", None)
+        if h is None:
+            return self.statuses or []
+        status = self._status
+        rc = _fast.wait(h, status)
+        self._submitted = None
+        self.statuses = list(status[: len(self.caches)])
         if rc != OK and raise_on_error:
             self.pool.check(rc)
         return self.statuses
