@@ -350,25 +350,46 @@ def run_ours(args):
     kern_avg_ms = sum(kern_ms) / len(kern_ms)
     ms, kern_avg_ms = max_over_ranks([ms, kern_avg_ms], device=dev)
 
-    # End to end through the public API with host buffers: pinned inputs are
-    # copied in and the outputs copied back inside every timed step.
+    # End to end through the public API with host buffers: every step copies
+    # its inputs in from pinned host memory and its outputs back out. The
+    # copies run on their own streams into double-buffered device tensors, so
+    # step i+1's inputs cross PCIe while step i computes and step i-1's
+    # outputs come back; the compute stream waits for its inputs, and a
+    # buffer is rewritten only after the step that used it is done with it.
     hq_ = q.cpu().pin_memory()
     hk_ = kn.cpu().pin_memory()
     hv_ = vn.cpu().pin_memory()
-    ho_ = torch.empty_like(out, device="cpu").pin_memory()
-    dq, dk, dv, do = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn), torch.empty_like(out)
-
-    dptrs = [(dq[l].data_ptr(), dk[l].data_ptr(), dv[l].data_ptr(), do[l].data_ptr())
-             for l in range(LAYERS)]
+    ho_ = [torch.empty_like(out, device="cpu").pin_memory() for _ in range(2)]
+    dbuf = [(torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn), torch.empty_like(out))
+            for _ in range(2)]
+    dptrs = [[(bq[l].data_ptr(), bk[l].data_ptr(), bv[l].data_ptr(), bo[l].data_ptr())
+              for l in range(LAYERS)] for bq, bk, bv, bo in dbuf]
+    h2d, d2h = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+    read_back = [torch.cuda.Event() for _ in range(2)]
+    e2e_i = [0]
 
     def e2e_step():
-        dq.copy_(hq_, non_blocking=True)
-        dk.copy_(hk_, non_blocking=True)
-        dv.copy_(hv_, non_blocking=True)
+        j = e2e_i[0] % 2
+        e2e_i[0] += 1
+        bq, bk, bv, bo = dbuf[j]
+        with torch.cuda.stream(h2d):
+            h2d.wait_event(computed[j])  # the step that last read these inputs
+            bq.copy_(hq_, non_blocking=True)
+            bk.copy_(hk_, non_blocking=True)
+            bv.copy_(hv_, non_blocking=True)
+            in_ready[j].record(h2d)
+        stream.wait_event(in_ready[j])
+        stream.wait_event(read_back[j])  # the outputs last written here were read
         batch = plan.begin()
         for layer in range(LAYERS):
-            batch.decode_layer_ptr(layer, *dptrs[layer])
-        ho_.copy_(do, non_blocking=True)
+            batch.decode_layer_ptr(layer, *dptrs[j][layer])
+        computed[j].record(stream)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(computed[j])
+            ho_[j].copy_(bo, non_blocking=True)
+            read_back[j].record(d2h)
         inflight.append(batch.submit())
         collect(1)
         plan.truncate_all(base_arr)
@@ -382,13 +403,16 @@ def run_ours(args):
     e0.record(stream)
     for _ in range(args.steps):
         e2e_step()
+    for ev_ in read_back:  # the last outputs are on the host
+        stream.wait_event(ev_)
     e1.record(stream)
     collect(0)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
     (e2e_ms,) = max_over_ranks([e2e_ms], device=dev)
-    if not torch.equal(ho_, out.cpu()):
+    ref_out = out.cpu()
+    if not all(torch.equal(h, ref_out) for h in ho_):
         raise RuntimeError("end-to-end outputs differ from the device-resident run")
 
     tokens = B * world * args.steps
@@ -415,6 +439,7 @@ def run_ours(args):
                      "algorithmic_bytes_per_launch": alg, "avg_launch_ms": kern_avg_ms},
         "e2e": {"value": e2e_value, "unit": "tok/s",
                 "h2d_bytes_per_step": int(q.numel() + kn.numel() + vn.numel()) * 4,
+                "copies": "own H2D and D2H streams, double-buffered, overlapping compute",
                 "d2h_bytes_per_step": int(out.numel()) * 4},
         "gpu_launches": launches,
         "kernel_timing": ("CUDA events at the completion of layer 0's and layer 7's decode "
