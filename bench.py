@@ -12,6 +12,7 @@ every step does the same work. One step reads ~544 MB of K/V, far more than
 the 126 MB L2, so no flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload microbench|gqa-bf16]
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own 256
 sequences (weak scaling, no collective on the data path); the timed region is
@@ -39,12 +40,36 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "small-lm-rs_b200"))
 
 METRIC = "decode tok/s and KV-attn HBM GB/s (% of peak) at 1/2/4/8 B200 vs host CPU"
-B, LEN_LO, LEN_HI = 256, 1, 511
-LAYERS, HQ, HKV, D, CTX, BLOCK = 8, 4, 2, 64, 512, 16
-WORKLOAD = (f"batched decode microbench: B={B}, cached lengths U[{LEN_LO},{LEN_HI}], "
-            f"Hq={HQ}, Hkv={HKV}, d={D}, f32 KV, {BLOCK}-token paged blocks, shuffled "
-            f"block table, {LAYERS} layers, 1 appended token per sequence per step")
+BLOCK = 16
+APPEND_REPS = 5
 REF_SAMPLE = 32  # sequences per reference-arm step
+
+# Per-GPU workloads. "microbench" is the isolated decode-attention + append
+# microbench (the headline); "gqa-bf16" is the scaled GQA shape (Hq 32 / Hkv 8,
+# bf16 KV, 8k context; 128 sequences over 8 GPUs = 16 per GPU; cached lengths
+# stop at 8191 so the appended token fits the 8192-token context).
+WORKLOADS = {
+    "microbench": dict(B=256, LEN_LO=1, LEN_HI=511, LAYERS=8, HQ=4, HKV=2, D=64, CTX=512,
+                       BF16=False),
+    "gqa-bf16": dict(B=16, LEN_LO=1024, LEN_HI=8191, LAYERS=8, HQ=32, HKV=8, D=64, CTX=8192,
+                     BF16=True),
+}
+
+
+def select_workload(name: str) -> None:
+    global B, LEN_LO, LEN_HI, LAYERS, HQ, HKV, D, CTX, BF16, S_KV, WORKLOAD, WORKLOAD_NAME
+    w = WORKLOADS[name]
+    B, LEN_LO, LEN_HI = w["B"], w["LEN_LO"], w["LEN_HI"]
+    LAYERS, HQ, HKV, D, CTX, BF16 = w["LAYERS"], w["HQ"], w["HKV"], w["D"], w["CTX"], w["BF16"]
+    S_KV = 2 if BF16 else 4
+    WORKLOAD_NAME = name
+    kind = "batched decode microbench" if name == "microbench" else "scaled GQA decode"
+    WORKLOAD = (f"{kind}: B={B} per GPU, cached lengths U[{LEN_LO},{LEN_HI}], Hq={HQ}, "
+                f"Hkv={HKV}, d={D}, {'bf16' if BF16 else 'f32'} KV, {BLOCK}-token paged blocks, "
+                f"shuffled block table, {LAYERS} layers, 1 appended token per sequence per step")
+
+
+select_workload("microbench")
 
 
 def parse():
@@ -55,7 +80,10 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="microbench")
+    args = ap.parse_args()
+    select_workload(args.workload)
+    return args
 
 
 def draw_lengths(seed: int):
@@ -65,10 +93,11 @@ def draw_lengths(seed: int):
     return rng.integers(LEN_LO, LEN_HI + 1, size=B).astype(np.int64)
 
 
-def algorithmic_bytes(lengths, s_kv: int = 4) -> int:
+def algorithmic_bytes(lengths, s_kv: int | None = None) -> int:
     """Bytes one decode launch must move for the batch (one layer):
     K+V over L_i+1 positions, Q read + O write, new K/V read, the append
     write, and the block-table entries."""
+    s_kv = S_KV if s_kv is None else s_kv
     total = 0
     for L in lengths:
         Lp = int(L) + 1
@@ -87,7 +116,8 @@ def measured_peaks():
 def ncu_traffic_per_launch():
     """dram bytes (read + write) per decode launch from the committed ncu
     summary, if one has been captured for this workload."""
-    p = ROOT / "profiles" / "decode_kernel_microbench.md"
+    name = "microbench" if WORKLOAD_NAME == "microbench" else "gqa_bf16"
+    p = ROOT / "profiles" / f"decode_kernel_{name}.md"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -163,7 +193,7 @@ def cpu_baseline(lengths, seed: int, threads: int, budget_s: float = 8.0):
     rng = np.random.default_rng(seed + 99)
     inv = O.rope_inverse_frequencies(D, 10000.0)
     sample = [int(x) for x in lengths[:REF_SAMPLE]]
-    caches = [O.DenseCache(LAYERS, CTX, HKV, D) for _ in sample]
+    caches = [O.DenseCache(LAYERS, CTX, HKV, D, quantize_bf16=BF16) for _ in sample]
     for c, L in zip(caches, sample):
         for layer in range(LAYERS):
             k = rng.standard_normal((L, HKV, D)).astype(np.float32)
@@ -204,7 +234,7 @@ def run_reference(args):
     rng = np.random.default_rng(args.seed + 7)
     inv = O.rope_inverse_frequencies(D, 10000.0)
     sample = [int(x) for x in lengths[:REF_SAMPLE]]
-    caches = [O.DenseCache(LAYERS, CTX, HKV, D) for _ in sample]
+    caches = [O.DenseCache(LAYERS, CTX, HKV, D, quantize_bf16=BF16) for _ in sample]
     for c, L in zip(caches, sample):
         for layer in range(LAYERS):
             k = rng.standard_normal((L, HKV, D)).astype(np.float32)
@@ -273,17 +303,38 @@ def run_ours(args):
     pool = slmkv.KvPool(num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV,
                         head_dimension=D, context_length=CTX, rope_theta=10000.0,
                         num_blocks=need_blocks + B + 64, max_sequences=B,
-                        kv_dtype=slmkv.KV_F32, device=local)
+                        kv_dtype=slmkv.KV_BF16 if BF16 else slmkv.KV_F32, device=local)
     pool.shuffle(seed + 1)
     caches = [pool.allocate_kv_cache(CTX) for _ in range(B)]
     gen = torch.Generator(device=dev)
     gen.manual_seed(seed + 2)
     total = int(lengths.sum())
-    with pool.begin(caches, [int(x) for x in lengths]) as b:
+    hist_k = [torch.randn((total, HKV, D), generator=gen, device=dev) for _ in range(LAYERS)]
+    hist_v = [torch.randn((total, HKV, D), generator=gen, device=dev) for _ in range(LAYERS)]
+    counts = [int(x) for x in lengths]
+
+    def append_history(b):
         for layer in range(LAYERS):
-            k = torch.randn((total, HKV, D), generator=gen, device=dev)
-            v = torch.randn((total, HKV, D), generator=gen, device=dev)
-            b.append_layer(layer, k, v, rotate_keys=True)
+            b.append_layer(layer, hist_k[layer], hist_v[layer], rotate_keys=True)
+
+    # Append kernel (RoPE on K + paged scatter of the whole history, one
+    # launch per layer): timed over rolled-back repeats of the history
+    # prefill, 8 launches each, then the history is appended for real.
+    a_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(APPEND_REPS)]
+    for r in range(3 + APPEND_REPS):
+        b = pool.begin(caches, counts)
+        if r >= 3:
+            a_ev[r - 3][0].record(torch.cuda.current_stream())
+        append_history(b)
+        if r >= 3:
+            a_ev[r - 3][1].record(torch.cuda.current_stream())
+        b.rollback()
+    torch.cuda.synchronize()
+    append_ms = sum(x.elapsed_time(y) for x, y in a_ev) / (APPEND_REPS * LAYERS)
+    with pool.begin(caches, counts) as b:
+        append_history(b)
+    del hist_k, hist_v
     torch.cuda.synchronize()
     q = torch.randn((LAYERS, B, HQ, D), generator=gen, device=dev)
     kn = torch.randn((LAYERS, B, HKV, D), generator=gen, device=dev)
@@ -415,6 +466,8 @@ def run_ours(args):
     if not all(torch.equal(h, ref_out) for h in ho_):
         raise RuntimeError("end-to-end outputs differ from the device-resident run")
 
+    append_bytes = total * HKV * D * (4 + 4 + 2 * S_KV)  # K, V in (f32) and out (pool type)
+    (append_ms,) = max_over_ranks([append_ms], device=dev)
     tokens = B * world * args.steps
     value = tokens / (ms / 1e3)
     e2e_value = tokens / (e2e_ms / 1e3)
@@ -427,7 +480,8 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch_per_gpu": B, "layers": LAYERS,
+        "config": {"workload": WORKLOAD, "name": WORKLOAD_NAME, "batch_per_gpu": B,
+                   "layers": LAYERS, "kv_dtype": "bf16" if BF16 else "f32",
                    "l2": f"inputs larger than L2 ({LAYERS * alg / 1e6:.0f} MB of K/V per step)",
                    "seed": args.seed},
         "kv_attn_hbm_gbs": achieved,
@@ -441,6 +495,11 @@ def run_ours(args):
                 "h2d_bytes_per_step": int(q.numel() + kn.numel() + vn.numel()) * 4,
                 "copies": "own H2D and D2H streams, double-buffered, overlapping compute",
                 "d2h_bytes_per_step": int(out.numel()) * 4},
+        "append_kernel": {"achieved": append_bytes / (append_ms / 1e3) / 1e9, "unit": "GB/s",
+                          "frac": append_bytes / (append_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                          "avg_launch_ms": append_ms, "bytes_per_launch": append_bytes,
+                          "workload": f"history prefill: {total} tokens x {HKV} KV heads, "
+                                      f"RoPE on K, f32 in, {'bf16' if BF16 else 'f32'} pool"},
         "gpu_launches": launches,
         "kernel_timing": ("CUDA events at the completion of layer 0's and layer 7's decode "
                           "kernel in every timed step; interval / 7"),

@@ -817,8 +817,8 @@ cudaError_t launch_decode_t(const StreamDecodeLaunch& p, cudaStream_t s) {
 // Append: 16 lanes per (token, kv head) row, 4 dims (two RoPE pairs) a lane,
 // 128-bit loads and stores.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int find_seq(const SeqEntry* seqs, int n, int row) {
-  int lo = 0, hi = n - 1;
+// Sequence holding batch token `row` among seqs[lo..hi] (row offsets ascend).
+__device__ __forceinline__ int find_seq_in(const SeqEntry* seqs, int lo, int hi, int row) {
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (seqs[mid].row_offset <= row) lo = mid;
@@ -826,42 +826,74 @@ __device__ __forceinline__ int find_seq(const SeqEntry* seqs, int n, int row) {
   }
   return lo;
 }
+__device__ __forceinline__ int find_seq(const SeqEntry* seqs, int n, int row) {
+  return find_seq_in(seqs, 0, n - 1, row);
+}
+
+// One CTA appends kAppendRows consecutive (token, KV head) rows: 16 lanes per
+// row, four rows per lane group, every K/V load issued before any dependent
+// work. The CTA's first and last tokens bound the sequences it touches, so
+// each row's lookup searches only that range.
+constexpr int kAppendRowsPerGroup = 4;
+constexpr int kAppendRows = 16 * kAppendRowsPerGroup;  // 256 threads = 16 groups of 16
 
 template <int BF16>
 __global__ void __launch_bounds__(256) append_kernel(const AppendLaunch p) {
   const int Hkv = p.g.kv_heads;
-  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
-  const int l16 = threadIdx.x & 15;
-  if (row >= p.total_tokens * Hkv) return;
-  const int tok = row / Hkv, h = row - tok * Hkv;
-  const int si = find_seq(p.seqs, p.n_seq, tok);
-  const SeqEntry se = p.seqs[si];
-  const int pos = se.base + (tok - se.row_offset);
-  const int32_t blk =
-      checked_block(p.g, p.g.block_table[static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq +
-                                         pos / kBlockTokens]);
-  float4 k = reinterpret_cast<const float4*>(p.k_in + static_cast<size_t>(row) * D)[l16];
-  const float4 v = reinterpret_cast<const float4*>(p.v_in + static_cast<size_t>(row) * D)[l16];
-  const bool fin = finite4(k) && finite4(v);
-  if (p.rotate) {
-    const float4 cs =
-        reinterpret_cast<const float4*>(p.g.rope + static_cast<size_t>(pos) * (D / 2))[l16];
-    const float2 a = rope_pair(make_float2(k.x, k.y), make_float2(cs.x, cs.y));
-    const float2 b = rope_pair(make_float2(k.z, k.w), make_float2(cs.z, cs.w));
-    k = make_float4(a.x, a.y, b.x, b.y);
+  const int64_t n_rows = static_cast<int64_t>(p.total_tokens) * Hkv;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kAppendRows;
+  const int grp = threadIdx.x >> 4, l16 = threadIdx.x & 15;
+  __shared__ int s_range[2];
+  if (threadIdx.x == 0) {
+    const int64_t last = min(row0 + kAppendRows, n_rows) - 1;
+    s_range[0] = find_seq(p.seqs, p.n_seq, static_cast<int>(row0 / Hkv));
+    s_range[1] = find_seq(p.seqs, p.n_seq, static_cast<int>(last / Hkv));
   }
-  const size_t dst = static_cast<size_t>(p.layer) * p.g.layer_elems +
-                     ((static_cast<size_t>(blk) * Hkv + h) * kBlockTokens + pos % kBlockTokens) * D;
-  if constexpr (BF16) {
-    reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.g.k) + dst)[l16] =
-        make_uint2(pack_bf16x2(k.x, k.y), pack_bf16x2(k.z, k.w));
-    reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.g.v) + dst)[l16] =
-        make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
-  } else {
-    reinterpret_cast<float4*>(static_cast<float*>(p.g.k) + dst)[l16] = k;
-    reinterpret_cast<float4*>(static_cast<float*>(p.g.v) + dst)[l16] = v;
+  float4 kin[kAppendRowsPerGroup], vin[kAppendRowsPerGroup];
+#pragma unroll
+  for (int j = 0; j < kAppendRowsPerGroup; ++j) {
+    const int64_t row = row0 + j * 16 + grp;
+    if (row < n_rows) {
+      kin[j] = reinterpret_cast<const float4*>(p.k_in + row * D)[l16];
+      vin[j] = reinterpret_cast<const float4*>(p.v_in + row * D)[l16];
+    }
   }
-  if (!fin) atomicOr(&p.status[si], kStatusNonFinite);
+  __syncthreads();
+  const int lo = s_range[0], hi = s_range[1];
+#pragma unroll
+  for (int j = 0; j < kAppendRowsPerGroup; ++j) {
+    const int64_t row = row0 + j * 16 + grp;
+    if (row >= n_rows) break;
+    const int tok = static_cast<int>(row / Hkv), h = static_cast<int>(row - static_cast<int64_t>(tok) * Hkv);
+    const int si = find_seq_in(p.seqs, lo, hi, tok);
+    const SeqEntry se = p.seqs[si];
+    const int pos = se.base + (tok - se.row_offset);
+    const int32_t blk = checked_block(
+        p.g, p.g.block_table[static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq +
+                             pos / kBlockTokens]);
+    float4 k = kin[j];
+    const float4 v = vin[j];
+    const bool fin = finite4(k) && finite4(v);
+    if (p.rotate) {
+      const float4 cs =
+          reinterpret_cast<const float4*>(p.g.rope + static_cast<size_t>(pos) * (D / 2))[l16];
+      const float2 a = rope_pair(make_float2(k.x, k.y), make_float2(cs.x, cs.y));
+      const float2 b = rope_pair(make_float2(k.z, k.w), make_float2(cs.z, cs.w));
+      k = make_float4(a.x, a.y, b.x, b.y);
+    }
+    const size_t dst = static_cast<size_t>(p.layer) * p.g.layer_elems +
+                       ((static_cast<size_t>(blk) * Hkv + h) * kBlockTokens + pos % kBlockTokens) * D;
+    if constexpr (BF16) {
+      reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.g.k) + dst)[l16] =
+          make_uint2(pack_bf16x2(k.x, k.y), pack_bf16x2(k.z, k.w));
+      reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.g.v) + dst)[l16] =
+          make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    } else {
+      reinterpret_cast<float4*>(static_cast<float*>(p.g.k) + dst)[l16] = k;
+      reinterpret_cast<float4*>(static_cast<float*>(p.g.v) + dst)[l16] = v;
+    }
+    if (!fin) atomicOr(&p.status[si], kStatusNonFinite);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1040,10 +1072,9 @@ cudaError_t launch_decode(const StreamDecodeLaunch& p, cudaStream_t s) {
 cudaError_t launch_append(const AppendLaunch& p, cudaStream_t s) {
   const int64_t rows = static_cast<int64_t>(p.total_tokens) * p.g.kv_heads;
   if (rows <= 0) return cudaSuccess;
-  const int threads = 256;
-  const int64_t blocks = (rows * 16 + threads - 1) / threads;
-  if (p.g.bf16) append_kernel<1><<<static_cast<unsigned>(blocks), threads, 0, s>>>(p);
-  else append_kernel<0><<<static_cast<unsigned>(blocks), threads, 0, s>>>(p);
+  const int64_t blocks = (rows + kAppendRows - 1) / kAppendRows;
+  if (p.g.bf16) append_kernel<1><<<static_cast<unsigned>(blocks), 256, 0, s>>>(p);
+  else append_kernel<0><<<static_cast<unsigned>(blocks), 256, 0, s>>>(p);
   return cudaGetLastError();
 }
 
