@@ -15,11 +15,12 @@
 #include <new>
 #include <random>
 #include <string>
-#include <unordered_map>
 #include <deque>
+#include <unordered_map>
 #include <vector>
 
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include "slmkv.h"
 #include "slmkv_internal.h"
@@ -139,6 +140,7 @@ struct slm_ctx {
   int32_t* d_counters = nullptr;
   int32_t* d_error = nullptr;
   int32_t* h_readback = nullptr;  // pinned: [1 + max_sequences]
+  CUtensorMap tmap_k{}, tmap_v{};  // bf16 pools: TMA maps for the decode kernel
   // Pinned status readback of submitted batches: kReadbackSlots slots of
   // [error word, pad, status x max_sequences], each with its event.
   int32_t* h_rb = nullptr;
@@ -580,12 +582,55 @@ slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<
   return SLM_OK;
 }
 
+// TMA maps of a bf16 pool for the decode kernel: the whole pool as rows of
+// 64 bf16 (128 B; row = ((layer * num_blocks + block) * kv_heads + head) * 16
+// + slot), a box of one 16-row chunk, 128-byte swizzle. The encoder comes
+// from the driver through the runtime (no link against the driver library).
+slm_status make_pool_maps(slm_ctx* c) {
+  static const PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }();
+  if (!encode) return fail(c, SLM_ERR_CUDA, "CUDA error: cuTensorMapEncodeTiled is unavailable");
+  const slm_config& k = c->cfg;
+  const uint64_t rows = static_cast<uint64_t>(k.num_layers) * k.num_blocks *
+                        k.num_key_value_heads * kBlockTokens;
+  if (rows > static_cast<uint64_t>(INT32_MAX))
+    return fail(c, SLM_ERR_INVALID_CONFIGURATION,
+                "invalid configuration: a bf16 pool of %llu rows exceeds the 2^31 rows a TMA "
+                "coordinate addresses",
+                static_cast<unsigned long long>(rows));
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k.head_dimension), rows};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k.head_dimension) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(k.head_dimension), kBlockTokens};
+  const cuuint32_t estride[2] = {1, 1};
+  void* pools[2] = {c->k_pool, c->v_pool};
+  CUtensorMap* maps[2] = {&c->tmap_k, &c->tmap_v};
+  for (int i = 0; i < 2; ++i) {
+    const CUresult r = encode(maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, pools[i], dims,
+                              strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(c, SLM_ERR_CUDA, "CUDA error: cuTensorMapEncodeTiled failed (%d)",
+                  static_cast<int>(r));
+  }
+  return SLM_OK;
+}
+
 // Fills a decode launch for an uploaded plan.
 StreamDecodeLaunch decode_launch(slm_ctx* c, int32_t layer, const StepDev& dev,
                                  const StreamPlan& plan) {
   StreamDecodeLaunch p{};
   p.g = c->geom();
   p.layer = layer;
+  p.tmap_k = c->tmap_k;
+  p.tmap_v = c->tmap_v;
   p.pairs = dev.pairs;
   p.n_pairs = static_cast<int32_t>(plan.pairs.size());
   p.chunks = dev.chunks;
@@ -751,6 +796,7 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
     };
     step(dev_alloc(cp, &cp->k_pool, pool_bytes, "K pool"));
     step(dev_alloc(cp, &cp->v_pool, pool_bytes, "V pool"));
+    if (rc == SLM_OK && k.kv_dtype == SLM_KV_BF16) step(make_pool_maps(cp));
     const size_t bt_bytes = sizeof(int32_t) * k.max_sequences * cp->max_blocks_per_seq;
     step(dev_alloc(cp, &cp->d_block_table, bt_bytes, "block table"));
     std::vector<float2> rope;

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace slmkv {
@@ -105,6 +106,10 @@ struct StreamDecodeLaunch {
   // before the previous kernel of the stream started, so the first K/V stages
   // may be fetched before waiting on that kernel (set by the host).
   int32_t early_kv;
+  // bf16 pools: TMA maps of the whole K and V pools as rows of 64 bf16
+  // (row = ((layer * num_blocks + block) * kv_heads + head) * 16 + slot), box
+  // 16 rows, 128-byte swizzle. Unused for f32 pools.
+  CUtensorMap tmap_k, tmap_v;
 };
 cudaError_t launch_decode(const StreamDecodeLaunch& p, cudaStream_t s);
 

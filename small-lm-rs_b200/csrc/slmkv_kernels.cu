@@ -58,6 +58,15 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// TMA tiled load of a 2-D box at column 0, row y (no multicast).
+__device__ __forceinline__ void tma_load_rows(void* dst, const CUtensorMap* map, int y,
+                                              uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -279,6 +288,131 @@ __device__ __forceinline__ void block_softmax_pv(const void* __restrict__ vb, fl
 }
 
 // ---------------------------------------------------------------------------
+// bf16 K/V blocks on the tensor cores (warp-level mma.m16n8k16, f32
+// accumulate). The block's K and V chunks are staged by TMA with the 128-byte
+// swizzle: row r (a token, 64 bf16 = 128 B) lies at (r/8)*1024 + (r%8)*128,
+// its 16-byte unit u at unit u ^ (r%8), so ldmatrix reads are conflict-free.
+// The 16 MMA rows hold the G query heads twice: row g is head g rounded to
+// bf16, row g+8 the bf16 residual of the same values, so Q (and P) carry ~16
+// mantissa bits and every sum is accumulated in f32. Lane (g = lane/4,
+// t = lane%4) owns head g (when g < G): scores of tokens 8j+2t+{0,1}, j=0,1,
+// and outputs of dims 8n+2t+{0,1}, n=0..7 (hi row in o[n][0..1], residual row
+// in o[n][2..3]).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t sw128(uint32_t base, int row, int unit) {
+  return base + ((row >> 3) << 10) + ((row & 7) << 7) + (((unit ^ row) & 7) << 4);
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// (hi, lo) bf16 pairs of two f32 values: hi = RNE(x), lo = RNE(x - hi).
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16x2(x0, x1);
+  lo = pack_bf16x2(__fsub_rn(x0, bf16lo(hi)), __fsub_rn(x1, bf16hi(hi)));
+}
+
+// Q fragments of one pair: qs holds the pair's rotated Q rows [G][64] (f32);
+// each is scaled into the exp2 domain and split into (hi, lo) bf16.
+template <int G>
+__device__ __forceinline__ void load_q_frags(const float* qs, int lane, uint32_t (&qa)[4][4]) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    if (g < G) {
+      const float2 x = *reinterpret_cast<const float2*>(qs + g * D + 16 * s + 2 * t);
+      const float2 y = *reinterpret_cast<const float2*>(qs + g * D + 16 * s + 8 + 2 * t);
+      split_bf16x2(x.x * kScaleLog2, x.y * kScaleLog2, qa[s][0], qa[s][1]);
+      split_bf16x2(y.x * kScaleLog2, y.y * kScaleLog2, qa[s][2], qa[s][3]);
+    } else {
+      qa[s][0] = qa[s][1] = qa[s][2] = qa[s][3] = 0u;
+    }
+  }
+}
+
+// One block: scores on the tensor cores, the online-softmax update for this
+// lane's head, then P·V on the tensor cores. kaddr/vaddr: shared addresses of
+// the swizzled K and V chunks; tokens at or past nvalid are masked (their V
+// rows must be finite: the caller zeroes them).
+__device__ __forceinline__ void block_mma_bf16(uint32_t kaddr, uint32_t vaddr, int lane, int nvalid,
+                                               const uint32_t (&qa)[4][4], float& m_row,
+                                               float& l_row, float (&o)[8][4]) {
+  const int r = lane & 7, mtx = lane >> 3, t = lane & 3;
+  float c[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < 2; ++sp) {
+      uint32_t b0, b1, b2, b3;  // k-steps 2sp (b0, b1) and 2sp+1 (b2, b3)
+      ldsm_x4(sw128(kaddr, 8 * j + r, 4 * sp + mtx), b0, b1, b2, b3);
+      mma_bf16(c[j], qa[2 * sp][0], qa[2 * sp][1], qa[2 * sp][2], qa[2 * sp][3], b0, b1);
+      mma_bf16(c[j], qa[2 * sp + 1][0], qa[2 * sp + 1][1], qa[2 * sp + 1][2], qa[2 * sp + 1][3],
+               b2, b3);
+    }
+  }
+  float sc[2][2];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int tok = 8 * j + 2 * t + e;
+      sc[j][e] = (tok < nvalid) ? c[j][e] + c[j][2 + e] : -INFINITY;
+      mx = fmaxf(mx, sc[j][e]);
+    }
+  mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+  const float mnew = fmaxf(m_row, mx);
+  const float corr = fast_exp2(m_row - mnew);
+  float pr[2][2], ps = 0.f;
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      pr[j][e] = fast_exp2(sc[j][e] - mnew);
+      ps += pr[j][e];
+    }
+  ps += __shfl_xor_sync(kFull, ps, 1);
+  ps += __shfl_xor_sync(kFull, ps, 2);
+  l_row = fmaf(l_row, corr, ps);
+  m_row = mnew;
+  uint32_t pa0, pa1, pa2, pa3;
+  split_bf16x2(pr[0][0], pr[0][1], pa0, pa1);
+  split_bf16x2(pr[1][0], pr[1][1], pa2, pa3);
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    o[n][0] *= corr;
+    o[n][1] *= corr;
+    o[n][2] *= corr;
+    o[n][3] *= corr;
+  }
+#pragma unroll
+  for (int np = 0; np < 4; ++np) {
+    uint32_t b0, b1, b2, b3;  // dims 16np..+7 (b0, b1) and 16np+8..+15 (b2, b3)
+    ldsm_x4_t(sw128(vaddr, 8 * (mtx & 1) + r, 2 * np + (mtx >> 1)), b0, b1, b2, b3);
+    mma_bf16(o[2 * np], pa0, pa1, pa2, pa3, b0, b1);
+    mma_bf16(o[2 * np + 1], pa0, pa1, pa2, pa3, b2, b3);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Decode (stream-K). The host flattens the step into a stream of chunk ids
 // (chunk = physical block * Hkv + kv head; one chunk = 16 tokens of one head)
 // in (sequence, head, block) order, plus one PairEntry per (sequence, head).
@@ -309,7 +443,7 @@ struct StreamShape {
   static constexpr int kOffChunk = kOffBars + W * R * 8;
   static constexpr int kOffCnt = kOffChunk + W * R * 4;
   static constexpr int kOffPend = (kOffCnt + 2 * W * 4 + 15) / 16 * 16;
-  static constexpr int kSmem = kOffPend + W * R * 16;
+  static constexpr int kSmem = kOffPend + W * R * 16 + (BF16 ? 1024 : 0);  // + alignment slack
   static_assert(kSmem <= 227 * 1024, "decode staging exceeds shared memory");
   static_assert(kChunk % 16 == 0 && kSide % 16 == 0 && kSlot % 16 == 0, "16-byte alignment");
 };
@@ -410,9 +544,12 @@ __device__ __forceinline__ void merge_partials(int n, int lane, Acc acc_at, Ml m
 }
 
 template <int BF16, int G, int W, int R>
-__global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDecodeLaunch p) {
+__global__ void __launch_bounds__(W * 32, 1)
+    decode_stream_kernel(const __grid_constant__ StreamDecodeLaunch p) {
   using Sh = StreamShape<BF16, G, W, R>;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // bf16 stages are TMA boxes with the 128-byte swizzle: 1024-byte aligned.
+  uint8_t* smem = smem_raw + (BF16 ? ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) : 0u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* stages = smem + warp * R * Sh::kStage;
   uint8_t* sides = smem + Sh::kOffSide + warp * R * Sh::kSide;
@@ -517,9 +654,15 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
       uint32_t tx = Sh::kStage;
       if (first) tx += G * D * 4 + (p.fused ? (D / 2) * 8 : 0) + (appends ? 2 * D * 4 : 0);
       mbar_arrive_expect_tx(&bars[stage], tx);
-      bulk_load(st, kbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk, &bars[stage]);
-      bulk_load(st + Sh::kChunk, vbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk,
-                &bars[stage]);
+      if constexpr (BF16) {
+        const int y = (p.layer * static_cast<int>(max_chunk) + static_cast<int>(chunk)) * kBlockTokens;
+        tma_load_rows(st, &p.tmap_k, y, &bars[stage]);
+        tma_load_rows(st + Sh::kChunk, &p.tmap_v, y, &bars[stage]);
+      } else {
+        bulk_load(st, kbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk, &bars[stage]);
+        bulk_load(st + Sh::kChunk, vbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk,
+                  &bars[stage]);
+      }
       if (defer_side)
         side_pend[stage] = first ? make_int4(pp_seq, pp_head, pp_L, appends ? 1 : 0)
                                  : make_int4(0, 0, 0, -1);
@@ -558,6 +701,9 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
   PairFields cur = pair_from_window(pa, pb, pc - pwin);
   float m[G], l[G];
   float2 acc[G];
+  // bf16: this lane's head (lane/4) on the tensor cores until the segment ends.
+  uint32_t qa[4][4];
+  float m_row = -INFINITY, l_row = 0.f, o[8][4];
   float2 cs = make_float2(1.f, 0.f), kn = cs, vn = cs;
   int seg_end = min(g1, cur.blk_begin + cur.nblk);
   bool seg_start = true;
@@ -597,12 +743,22 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
       for (int g2 = 0; g2 < G; ++g2) {
         float2 x = reinterpret_cast<const float2*>(sd)[g2 * (D / 2) + lane];
         if (p.fused) x = rope_pair(x, cs);
-        *reinterpret_cast<float2*>(qs + g2 * D + qunit(lane >> 1) * 4 + ((2 * lane) & 3)) = x;
+        if constexpr (BF16)
+          reinterpret_cast<float2*>(qs + g2 * D)[lane] = x;
+        else
+          *reinterpret_cast<float2*>(qs + g2 * D + qunit(lane >> 1) * 4 + ((2 * lane) & 3)) = x;
         m[g2] = -INFINITY;
         l[g2] = 0.f;
         acc[g2] = make_float2(0.f, 0.f);
       }
       __syncwarp();
+      if constexpr (BF16) {
+        load_q_frags<G>(qs, lane, qa);
+        m_row = -INFINITY;
+        l_row = 0.f;
+#pragma unroll
+        for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      }
       seg_start = false;
     }
     const int j = g - cur.blk_begin;
@@ -619,8 +775,10 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
           layer_elems + (static_cast<size_t>(stage_chunk[stage]) * kBlockTokens + slot) * D;
       if constexpr (BF16) {
         const uint32_t kq = pack_bf16x2(kx.x, kx.y), vq = pack_bf16x2(vn.x, vn.y);
-        reinterpret_cast<uint32_t*>(kb)[slot * (D / 2) + lane] = kq;
-        reinterpret_cast<uint32_t*>(vb)[slot * (D / 2) + lane] = vq;
+        // lane's word: unit lane/4 of the swizzled row `slot`
+        const uint32_t off = sw128(0u, slot, lane >> 2) + ((lane & 3) << 2);
+        *reinterpret_cast<uint32_t*>(kb + off) = kq;
+        *reinterpret_cast<uint32_t*>(vb + off) = vq;
         reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.k) + dst)[lane] = kq;
         reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.v) + dst)[lane] = vq;
       } else {
@@ -632,22 +790,51 @@ __global__ void __launch_bounds__(W * 32, 1) decode_stream_kernel(const StreamDe
       if (!__all_sync(kFull, fin) && lane == 0) atomicOr(&p.status[cur.seq], kStatusNonFinite);
       __syncwarp();
     }
-    float sc[G];
     if constexpr (BF16) {
-      block_scores_bf16<G>(reinterpret_cast<const uint16_t*>(kb), qs, lane, sc);
+      if (nvalid < kBlockTokens) {
+        // Tokens past the length are masked, but P = 0 times a non-finite
+        // stale V value is not 0: clear those V rows (whole 128-byte rows).
+        for (int i = nvalid * 8 + lane; i < kBlockTokens * 8; i += 32)
+          reinterpret_cast<uint4*>(vb)[((i >> 3) >> 3) * 64 + ((i >> 3) & 7) * 8 + (i & 7)] =
+              make_uint4(0u, 0u, 0u, 0u);
+        __syncwarp();
+      }
+      block_mma_bf16(smem_u32(kb), smem_u32(vb), lane, nvalid, qa, m_row, l_row, o);
+      __syncwarp();
     } else {
+      float sc[G];
       block_scores_f32<G>(reinterpret_cast<const float*>(kb), qs, lane, sc);
+      block_softmax_pv<G, false>(vb, pbuf, lane, nvalid, sc, m, l, acc);
     }
-    block_softmax_pv<G, BF16 != 0>(vb, pbuf, lane, nvalid, sc, m, l, acc);
     if (pg < g1) {
       // The stage (and its side buffer) were read, maybe written, through
       // the generic proxy; order that before the async-proxy refill.
-      if (append_here) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (append_here || (BF16 && nvalid < kBlockTokens))
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(stage, false);
     }
 
     if (g != seg_end - 1) continue;
     // ---- end of this warp's segment of pair `pc` ---------------------------------
+    if constexpr (BF16) {
+      // Back to one float2 per lane and head (dims 2*lane, 2*lane+1): the
+      // layout the merges below use. qs is free: Q lives in qa.
+      const int gl = lane >> 2, tl = lane & 3;
+      if (gl < G) {
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+          *reinterpret_cast<float2*>(qs + gl * D + 8 * n + 2 * tl) =
+              make_float2(o[n][0] + o[n][2], o[n][1] + o[n][3]);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int g2 = 0; g2 < G; ++g2) {
+        acc[g2] = reinterpret_cast<const float2*>(qs + g2 * D)[lane];
+        m[g2] = __shfl_sync(kFull, m_row, 4 * g2);
+        l[g2] = __shfl_sync(kFull, l_row, 4 * g2);
+      }
+      __syncwarp();
+    }
     const size_t orow = static_cast<size_t>(cur.seq) * Hq + cur.head * G;
     if (cur.nseg == 1) {
 #pragma unroll

@@ -148,6 +148,16 @@ def test_fused_decode_group_sizes(hq, hkv):
     assert err <= 1e-4, err
 
 
+@pytest.mark.parametrize("hq,hkv", [(4, 4), (4, 2), (8, 2), (16, 2)])
+def test_fused_decode_group_sizes_bf16(hq, hkv):
+    """bf16 KV runs its blocks on the tensor cores with Q and P split into
+    bf16 (hi, lo) pairs: well inside the bf16 bar."""
+    lengths = [1, 16, 17, 40, 257, 511]
+    err = _decode_case(slmkv.KV_BF16, lengths, layers=2, hq=hq, hkv=hkv, seed=19)
+    assert err <= 2e-2, err
+    assert err <= 1e-3, err  # the split keeps ~16 mantissa bits of Q and P
+
+
 def test_fused_decode_full_microbench_shape():
     """B=256 sequences, lengths U[1,511], Hq=4, Hkv=2, d=64, f32, shuffled
     16-token blocks — checked against the oracle for every sequence."""
