@@ -510,7 +510,7 @@ def run_ours(args):
         cv, reps, el = cpu_baseline(lengths, args.seed, threads=1)
         result["cpu_baseline"] = {
             "value": cv, "unit": "tok/s", "cores": 1, "kind": "port",
-            "sample": (f"{REF_SAMPLE} of the {B} seeded sequences x {LAYERS} layers per step, "
+            "sample": (f"{min(REF_SAMPLE, B)} of the {B} seeded sequences x {LAYERS} layers per step, "
                        f"{reps} steps in {el:.1f} s, single thread (the reference's decode "
                        "attention is serial per sequence)")}
     if rank == 0:

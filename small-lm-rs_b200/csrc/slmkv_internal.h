@@ -41,12 +41,16 @@ static_assert(sizeof(PairEntry) == 32, "PairEntry is read as two int4");
 // Decode CTA shape (one CTA per SM): warps per CTA and K/V stages per warp,
 // per pool type and query heads per KV head, sized to the 227 KiB of shared
 // memory (each stage holds one 16-token block of K and V plus side inputs).
-// f32 with at most two query heads per KV head has the least math per byte:
-// more warps with one stage each hide the per-block latency best there
-// (measured on the batched decode microbench: 12 x 1 beats 10 x 2, 16 x 1).
-constexpr int decode_warps(int bf16, int group) { return (!bf16 && group <= 2) ? 12 : 8; }
+// Twelve warps per SM hide the per-block latency best where they fit in
+// shared memory (measured on the batched decode microbench for f32 with at
+// most two query heads per KV head, 12 x 1 against 10 x 2 and 16 x 1; and on
+// the scaled GQA shape for bf16 with four, 12 x 2 against 8 x 4, 8 x 2 and
+// 16 x 1). Larger query groups need more shared memory per warp.
+constexpr int decode_warps(int bf16, int group) {
+  return (bf16 ? group <= 4 : group <= 2) ? 12 : 8;
+}
 constexpr int decode_stages(int bf16, int group) {
-  return bf16 ? (group >= 8 ? 3 : 4) : (group <= 2 ? 1 : 2);
+  return bf16 ? (group <= 4 ? 2 : 3) : (group <= 2 ? 1 : 2);
 }
 constexpr int kMaxDecodeWarps = 12;  // the largest decode_warps()
 static_assert(decode_warps(0, 1) <= kMaxDecodeWarps && decode_warps(0, 8) <= kMaxDecodeWarps &&
