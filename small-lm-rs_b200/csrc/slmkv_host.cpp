@@ -1351,9 +1351,11 @@ slm_status slm_batch_prefill_attention(slm_batch* b, int32_t layer, const float*
   if (!b->layer_done[layer])
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention prefill",
                        "layer %d must be appended before its attention", layer);
-  if (ctx->group > 4)
+  // bf16 pools run on the tensor cores (any supported group); the f32 kernel
+  // keeps up to 4 query heads per KV head in shared memory.
+  if (ctx->cfg.kv_dtype != SLM_KV_BF16 && ctx->group > 4)
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention prefill",
-                       "more than 4 query heads per KV head are not supported in prefill");
+                       "more than 4 query heads per KV head are not supported in f32 prefill");
   if (!d_query || !d_out) return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "null tensor");
   rc = flush_excess(ctx, b->stream, 0, 0);  // the prefill reads the device block table
   if (rc) return rc;
@@ -1367,6 +1369,8 @@ slm_status slm_batch_prefill_attention(slm_batch* b, int32_t layer, const float*
   p.rotate = rotate_query != 0;
   p.out = d_out;
   p.max_count = b->max_count;
+  p.tmap_k = ctx->tmap_k;
+  p.tmap_v = ctx->tmap_v;
   ctx->prev_decode_layer = -1;
   CU(ctx, launch_prefill(p, b->stream));
   ++ctx->launches;

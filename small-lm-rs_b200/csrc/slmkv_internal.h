@@ -150,8 +150,12 @@ struct PrefillLaunch {
   int32_t rotate;
   float* out;
   int32_t max_count;  // largest per-sequence token count
+  CUtensorMap tmap_k, tmap_v;  // bf16 pools: the decode kernel's pool maps
 };
 cudaError_t launch_prefill(const PrefillLaunch& p, cudaStream_t s);
+// bf16 pools on the tensor cores (tcgen05): slmkv_prefill_tc.cu.
+bool prefill_tc_supported(const PrefillLaunch& p);
+cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s);
 
 cudaError_t launch_apply_updates(const PoolGeom& g, const TableUpdate* updates, int32_t n_updates,
                                  const CopyJob* copies, int32_t n_copies, cudaStream_t s);

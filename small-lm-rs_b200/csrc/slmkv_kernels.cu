@@ -1277,6 +1277,7 @@ cudaError_t launch_gather(const GatherLaunch& p, cudaStream_t s) {
 
 cudaError_t launch_prefill(const PrefillLaunch& p, cudaStream_t s) {
   if (p.n_seq <= 0 || p.max_count <= 0) return cudaSuccess;
+  if (prefill_tc_supported(p)) return launch_prefill_tc(p, s);
   const dim3 grid((p.max_count + kBlockTokens - 1) / kBlockTokens, p.n_seq, p.g.kv_heads);
   const int G = p.g.q_heads / p.g.kv_heads;
 #define SLMKV_PREFILL(B, GG) prefill_kernel<B, GG><<<grid, 128, 0, s>>>(p)

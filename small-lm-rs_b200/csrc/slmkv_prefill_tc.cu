@@ -1,0 +1,504 @@
+// Causal GQA prefill attention over a bf16 paged cache on the 5th-generation
+// tensor cores (tcgen05): the batched prompt path of
+// ProjectedQkv::{scaled_causal_scores, causal_probabilities, attend_values}
+// (rust/engine/src/attention.rs:195-399) with the cache of
+// forward_prefill_with_cache (attention.rs:835-870).
+//
+// One CTA = 128 query rows of one (sequence, KV head): the G query heads of
+// the group times 128/G consecutive new tokens (row r = token r/G, head r%G),
+// so every K/V tile is shared by the whole group. Per 128-token K/V tile:
+//   S = Q K^T        tcgen05.mma kind::f16, M=128 N=128, f32 in TMEM columns
+//                    [0,128); Q is split into bf16 (hi, lo) tiles, two passes
+//   softmax          4 warps, one row per thread (TMEM lane = row), exp2
+//                    domain, causal mask; the running max moves only when a
+//                    row's max grows by more than 2^8, then O is rescaled
+//   O += P V         M=128 N=64, P (bf16) from shared memory, V as an
+//                    MN-major operand, O in TMEM columns [128,192)
+// Q, K and V tiles are 128-byte-swizzled: K/V blocks arrive by TMA (16 rows
+// per block, block-table lookups; two tiles in flight), Q and P are written
+// by the threads in the same layout. One thread issues the MMAs and commits
+// them to mbarriers. Every wait is bounded; on expiry the CTA records an
+// error, waits (bounded) for its own MMAs and copies, frees TMEM and exits.
+#include <cstdint>
+
+#include "slmkv_internal.h"
+
+namespace slmkv {
+namespace {
+
+constexpr int kTileM = 128;    // query rows per CTA
+constexpr int kTileN = 128;    // K/V tokens per tile (8 blocks)
+constexpr int kTmemCols = 256; // S: [0,128), O: [128,192)
+constexpr int kOCol = 128;
+constexpr int kTileBytes = kTileN * kHeadDim * 2;  // 16 KiB: 128 rows of 128 B
+constexpr float kScaleLog2Tc = 0.125f * 1.4426950408889634f;
+constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s
+constexpr int kWaitSpinsMax = 1 << 26;
+
+// Shared memory (offsets from a 1024-aligned base).
+constexpr int kOffQhi = 0;
+constexpr int kOffQlo = kOffQhi + kTileBytes;
+constexpr int kOffK = kOffQlo + kTileBytes;          // 2 buffers
+constexpr int kOffV = kOffK + 2 * kTileBytes;        // 2 buffers
+constexpr int kOffP = kOffV + 2 * kTileBytes;        // tokens 0-63, 64-127
+constexpr int kOffBar = kOffP + 2 * kTileBytes;      // kv_full[2], s_done, o_done
+constexpr int kOffMisc = kOffBar + 4 * 8;            // tmem base, abort flag
+constexpr int kSmemTc = kOffMisc + 16 + 1024;        // + alignment slack
+static_assert(kSmemTc <= 227 * 1024, "prefill tiles exceed shared memory");
+
+__device__ __forceinline__ uint32_t su32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: true when the phase completed, false after ~1 s.
+__device__ __noinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+  if (bar_try(bar, parity)) return true;
+  const unsigned long long t0 = gtimer();
+  for (int i = 0; i < kWaitSpinsMax; ++i) {
+    if (bar_try(bar, parity)) return true;
+    if ((i & 255) == 255 && gtimer() - t0 > kWaitNs) return false;
+  }
+  return false;
+}
+__device__ __forceinline__ void tma_rows(uint32_t dst, const CUtensorMap* map, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(bar)
+      : "memory");
+}
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 layout: start
+// address, leading / stride byte offsets in 16-byte units, version 1).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo16, uint32_t sbo16) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) |
+         (static_cast<uint64_t>(lbo16 & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>(sbo16 & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16: f32 accumulate, bf16 A and B, A K-major.
+constexpr uint32_t idesc(int m, int n, bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t id,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(id), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
+  // round to nearest even, as linear.rs:14-23 (inputs are finite here)
+  const uint32_t ra = (a + 0x7FFFu + ((a >> 16) & 1u)) >> 16;
+  const uint32_t rb = (b + 0x7FFFu + ((b >> 16) & 1u)) >> 16;
+  return (ra & 0xFFFFu) | (rb << 16);
+}
+__device__ __forceinline__ float bf16_lo_f(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// Byte offset of 16-byte unit u of row r in a 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t swz(int r, int u) {
+  return static_cast<uint32_t>(((r >> 3) << 10) + ((r & 7) << 7) + (((u ^ r) & 7) << 4));
+}
+
+template <int G>
+__global__ void __launch_bounds__(128, 1) prefill_tc_kernel(const __grid_constant__ PrefillLaunch p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = su32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int si = blockIdx.y, h = blockIdx.z;
+  const int tile = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // long tiles first
+  constexpr int TQ = kTileM / G;  // new tokens per CTA
+  const SeqEntry se = p.seqs[si];
+  const int q0 = tile * TQ;
+  if (q0 >= se.count) return;
+  const int nq = min(TQ, se.count - q0);
+  const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
+  const int last_pos = se.base + q0 + nq - 1;
+  const int n_kv = last_pos + 1;
+  const int n_tiles = (n_kv + kTileN - 1) / kTileN;
+
+  const uint32_t bar_kv0 = sbase + kOffBar, bar_s = sbase + kOffBar + 16, bar_o = sbase + kOffBar + 24;
+  uint32_t* misc = reinterpret_cast<uint32_t*>(sm + kOffMisc);
+  if (tid == 0) {
+    bar_init(bar_kv0, 1);
+    bar_init(bar_kv0 + 8, 1);
+    bar_init(bar_s, 1);
+    bar_init(bar_o, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    misc[1] = 0;  // abort flag
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     sbase + kOffMisc),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+
+  // K/V tile j -> buffer j&1: its 16-token blocks through the block table.
+  const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
+  const int layer_row0 = p.layer * p.g.num_blocks * Hkv;
+  auto load_tile = [&](int j) {  // thread 0
+    const int b0 = j * (kTileN / kBlockTokens);
+    const int nb = min(kTileN / kBlockTokens, (n_kv + kBlockTokens - 1) / kBlockTokens - b0);
+    const uint32_t bar = bar_kv0 + 8 * (j & 1);
+    bar_expect_tx(bar, static_cast<uint32_t>(nb) * 2 * kBlockTokens * kHeadDim * 2);
+    for (int b = 0; b < nb; ++b) {
+      int32_t blk = bt[b0 + b];
+      if (static_cast<uint32_t>(blk) >= static_cast<uint32_t>(p.g.num_blocks)) {
+        atomicOr(p.g.error, kErrBadBlock);
+        blk = 0;
+      }
+      const int y = (layer_row0 + blk * Hkv + h) * kBlockTokens;
+      const uint32_t off = static_cast<uint32_t>((j & 1) * kTileBytes + b * kBlockTokens * 128);
+      tma_rows(sbase + kOffK + off, &p.tmap_k, y, bar);
+      tma_rows(sbase + kOffV + off, &p.tmap_v, y, bar);
+    }
+  };
+
+  // Q rows: RoPE at the token's position, scaled into the exp2 domain, bf16
+  // (hi, lo); rows past the CTA's tokens are zero.
+  const int r = tid;  // this thread's row (TMEM lane)
+  const int tq = r / G, gq = r % G;
+  const int qpos = se.base + q0 + tq;
+  {
+    uint8_t* qhi = sm + kOffQhi;
+    uint8_t* qlo = sm + kOffQlo;
+    const bool live = tq < nq;
+    const float2* src = reinterpret_cast<const float2*>(
+        p.q + (static_cast<size_t>(se.row_offset + q0 + (live ? tq : 0)) * Hq + h * G + gq) *
+                  kHeadDim);
+    const float2* cs = p.g.rope + static_cast<size_t>(live ? qpos : 0) * (kHeadDim / 2);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 x = live ? src[4 * u + k] : make_float2(0.f, 0.f);
+        if (live && p.rotate) {
+          const float2 c = cs[4 * u + k];
+          x = make_float2(__fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, c.y)),
+                          __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x)));
+        }
+        x.x *= kScaleLog2Tc;
+        x.y *= kScaleLog2Tc;
+        hw[k] = bf16x2(x.x, x.y);
+        lw[k] = bf16x2(__fsub_rn(x.x, bf16_lo_f(hw[k])), __fsub_rn(x.y, bf16_hi_f(hw[k])));
+      }
+      *reinterpret_cast<uint4*>(qhi + swz(r, u)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(qlo + swz(r, u)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[0];
+  const uint32_t tmem_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  if (tid == 0) {
+    load_tile(0);
+    if (n_tiles > 1) load_tile(1);
+  }
+
+  constexpr uint32_t kIdQK = idesc(kTileM, kTileN, false);
+  constexpr uint32_t kIdPV = idesc(kTileM, kHeadDim, true);
+  float m_used = -INFINITY, l_sum = 0.f;
+  // Progress, for draining on an error: tiles whose copies were issued and
+  // seen landed, S products issued and seen, P·V products issued and seen.
+  int kv_issued = min(n_tiles, 2), kv_seen = 0, s_issued = 0, s_seen = 0, o_issued = 0,
+      o_seen = 0;
+  bool ok = true;
+  // Every failure sets the shared abort flag before the next barrier, after
+  // which all threads leave the loop together.
+  for (int j = 0; j < n_tiles; ++j) {
+    const int buf = j & 1;
+    const uint32_t kaddr = sbase + kOffK + buf * kTileBytes;
+    const uint32_t vaddr = sbase + kOffV + buf * kTileBytes;
+    // ---- K/V tile landed; stale V rows of the last tile cleared ----------
+    if (bar_wait(bar_kv0 + 8 * buf, (j >> 1) & 1)) kv_seen = j + 1;
+    else ok = false;
+    const int valid = min(kTileN, n_kv - j * kTileN);
+    if (ok && valid < kTileN) {
+      // P = 0 there, but 0 times a non-finite stale value is not 0.
+      uint8_t* vt = sm + kOffV + buf * kTileBytes;
+      // row t of a swizzled tile is the 128 bytes at t*128 (units permuted)
+      for (int i = valid * 8 + tid; i < kTileN * 8; i += 128)
+        *reinterpret_cast<uint4*>(vt + (i >> 3) * 128 + (i & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (!ok) misc[1] = 1;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (misc[1]) {
+      ok = false;
+      break;
+    }
+    // ---- S = (Q_hi + Q_lo) K^T -------------------------------------------
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16(tmem, sdesc(sbase + kOffQhi + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64), kIdQK,
+                kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16(tmem, sdesc(sbase + kOffQlo + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64), kIdQK,
+                1);
+      mma_commit(bar_s);
+    }
+    s_issued = j + 1;
+    if (bar_wait(bar_s, j & 1)) {
+      s_seen = j + 1;
+    } else {
+      ok = false;
+      misc[1] = 1;
+    }
+    tc_fence_after();
+    // ---- softmax of this thread's row ---------------------------------------
+    float s[kTileN];
+#pragma unroll
+    for (int c = 0; c < kTileN / 32; ++c) {
+      float v[32];
+      tmem_ld32(tmem_row + 32 * c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) s[32 * c + i] = v[i];
+    }
+    tmem_wait_ld();
+    const bool live = tq < nq;
+    const int kp0 = j * kTileN;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kTileN; ++i) {
+      // causal (attention.rs:207): key position <= query position
+      if (live && kp0 + i > qpos) s[i] = -INFINITY;
+      if (!live) s[i] = 0.f;
+      mx = fmaxf(mx, s[i]);
+    }
+    // The previous P·V must be done before P and O are touched.
+    if (j > 0) {
+      if (bar_wait(bar_o, (j - 1) & 1)) {
+        o_seen = j;
+      } else {
+        ok = false;
+        misc[1] = 1;
+      }
+    }
+    tc_fence_after();
+    if (ok && j >= 1 && j + 1 < n_tiles) {  // into the buffer P·V just freed
+      if (tid == 0) load_tile(j + 1);
+      kv_issued = j + 2;
+    }
+    // tcgen05.ld/st are warp-collective (.sync.aligned): a warp rescales O
+    // when any of its rows moved its max; the other rows scale by 1.
+    const bool grow = mx > m_used + 8.f;
+    float corr = 1.f;
+    if (grow) {
+      corr = ex2(m_used - mx);  // 0 on the first tile
+      m_used = mx;
+    }
+    if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll
+      for (int c = 0; c < kHeadDim / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem_row + kOCol + 32 * c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= corr;
+        tmem_st32(tmem_row + kOCol + 32 * c, v);
+      }
+      tmem_wait_st();
+    }
+    float psum = 0.f;
+    uint8_t* prow = sm + kOffP;
+#pragma unroll
+    for (int u = 0; u < kTileN / 8; ++u) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float a = ex2(s[8 * u + 2 * k] - m_used), b = ex2(s[8 * u + 2 * k + 1] - m_used);
+        psum += a + b;
+        w[k] = bf16x2(a, b);
+      }
+      // tokens 0-63 in the first P tile, 64-127 in the second
+      *reinterpret_cast<uint4*>(prow + (u >> 3) * kTileBytes + swz(r, u & 7)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    l_sum = fmaf(l_sum, corr, psum);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (misc[1]) {
+      ok = false;
+      break;
+    }
+    // ---- O += P V --------------------------------------------------------------
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < kTileN / 16; ++kk)
+        mma_f16(tmem + kOCol,
+                sdesc(sbase + kOffP + (kk >> 2) * kTileBytes + 32 * (kk & 3), 1, 64),
+                sdesc(vaddr + 2048 * kk, kTileBytes >> 4, 64), kIdPV, (j > 0 || kk > 0) ? 1 : 0);
+      mma_commit(bar_o);
+    }
+    o_issued = j + 1;
+  }
+
+  // ---- epilogue: O / l to the output rows --------------------------------------
+  if (o_issued > o_seen) {
+    if (bar_wait(bar_o, (o_issued - 1) & 1)) o_seen = o_issued;
+    else misc[1] = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const bool abort = misc[1] != 0 || o_seen != n_tiles;  // the same in every thread
+  if (!abort) {
+    // every thread of the warp loads (warp-collective); live rows store
+    const float inv = 1.f / l_sum;
+    float* dst = p.out + (static_cast<size_t>(se.row_offset + q0 + (tq < nq ? tq : 0)) * Hq + h * G +
+                          gq) * kHeadDim;
+#pragma unroll
+    for (int c = 0; c < kHeadDim / 32; ++c) {
+      float v[32];
+      tmem_ld32(tmem_row + kOCol + 32 * c, v);
+      tmem_wait_ld();
+      if (tq < nq) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(dst + 32 * c + i) =
+              make_float4(v[i] * inv, v[i + 1] * inv, v[i + 2] * inv, v[i + 3] * inv);
+      }
+    }
+  } else if (tid == 0) {
+    atomicOr(p.g.error, kErrTimeout);
+    // Let this CTA's own MMAs and copies land (bounded) before its TMEM and
+    // shared memory are released.
+    if (s_issued > s_seen) bar_wait(bar_s, (s_issued - 1) & 1);
+    if (o_issued > o_seen) bar_wait(bar_o, (o_issued - 1) & 1);
+    for (int t = kv_seen; t < kv_issued; ++t) bar_wait(bar_kv0 + 8 * (t & 1), (t >> 1) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                 : "memory");
+}
+
+}  // namespace
+
+bool prefill_tc_supported(const PrefillLaunch& p) {
+  const int G = p.g.q_heads / p.g.kv_heads;
+  return p.g.bf16 && (G == 1 || G == 2 || G == 4 || G == 8);
+}
+
+cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s) {
+  if (p.n_seq <= 0 || p.max_count <= 0) return cudaSuccess;
+  const int G = p.g.q_heads / p.g.kv_heads;
+  const int tq = kTileM / G;
+  const dim3 grid((p.max_count + tq - 1) / tq, p.n_seq, p.g.kv_heads);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static unsigned long long configured[4] = {};  // per G variant, one bit per device
+  auto run = [&](auto kernel, int gi) {
+    if (dev < 64 && !(configured[gi] & (1ull << dev))) {
+      const cudaError_t a =
+          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+      if (a != cudaSuccess) return a;
+      configured[gi] |= (1ull << dev);
+    }
+    kernel<<<grid, 128, kSmemTc, s>>>(p);
+    return cudaGetLastError();
+  };
+  switch (G) {
+    case 1: return run(prefill_tc_kernel<1>, 0);
+    case 2: return run(prefill_tc_kernel<2>, 1);
+    case 4: return run(prefill_tc_kernel<4>, 2);
+    case 8: return run(prefill_tc_kernel<8>, 3);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace slmkv
