@@ -322,6 +322,13 @@ def run_ours(args):
     # prefill, 8 launches each, then the history is appended for real.
     a_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             for _ in range(APPEND_REPS)]
+    # bf16 pools: the prompt prefill's attention (layer 0, every sequence's
+    # whole prompt, causal) runs on the tensor cores; timed in the same repeats.
+    p_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(APPEND_REPS)] if BF16 else []
+    if BF16:
+        pq = torch.randn((total, HQ, D), generator=gen, device=dev)
+        pout = torch.empty_like(pq)
     for r in range(3 + APPEND_REPS):
         b = pool.begin(caches, counts)
         if r >= 3:
@@ -329,9 +336,18 @@ def run_ours(args):
         append_history(b)
         if r >= 3:
             a_ev[r - 3][1].record(torch.cuda.current_stream())
+        if BF16:
+            if r >= 3:
+                p_ev[r - 3][0].record(torch.cuda.current_stream())
+            b.prefill_attention(0, pq, pout, rotate_query=True)
+            if r >= 3:
+                p_ev[r - 3][1].record(torch.cuda.current_stream())
         b.rollback()
     torch.cuda.synchronize()
     append_ms = sum(x.elapsed_time(y) for x, y in a_ev) / (APPEND_REPS * LAYERS)
+    prefill_ms = (sum(x.elapsed_time(y) for x, y in p_ev) / APPEND_REPS) if BF16 else None
+    if BF16:
+        del pq, pout
     with pool.begin(caches, counts) as b:
         append_history(b)
     del hist_k, hist_v
@@ -468,6 +484,10 @@ def run_ours(args):
 
     append_bytes = total * HKV * D * (4 + 4 + 2 * S_KV)  # K, V in (f32) and out (pool type)
     (append_ms,) = max_over_ranks([append_ms], device=dev)
+    if BF16:
+        (prefill_ms,) = max_over_ranks([prefill_ms], device=dev)
+        # causal QK^T and PV: 2 flops per multiply-add, d per score / output
+        prefill_flops = sum(int(L) * (int(L) + 1) // 2 for L in lengths) * HQ * 4 * D
     tokens = B * world * args.steps
     value = tokens / (ms / 1e3)
     e2e_value = tokens / (e2e_ms / 1e3)
@@ -500,6 +520,15 @@ def run_ours(args):
                           "avg_launch_ms": append_ms, "bytes_per_launch": append_bytes,
                           "workload": f"history prefill: {total} tokens x {HKV} KV heads, "
                                       f"RoPE on K, f32 in, {'bf16' if BF16 else 'f32'} pool"},
+        **({"prefill_kernel": {
+            "bound": "tensor", "unit": "TFLOP/s",
+            "achieved": prefill_flops / (prefill_ms / 1e3) / 1e12,
+            "peak": peaks.get("bf16_tflops", 1590.0),
+            "frac": prefill_flops / (prefill_ms / 1e3) / 1e12 / peaks.get("bf16_tflops", 1590.0),
+            "avg_launch_ms": prefill_ms, "flops_per_launch": prefill_flops,
+            "workload": (f"prompt prefill attention, one layer: {B} prompts of the drawn lengths "
+                         f"({total} tokens), Hq={HQ}, Hkv={HKV}, causal, bf16 KV, tcgen05")}}
+           if BF16 else {}),
         "gpu_launches": launches,
         "kernel_timing": ("CUDA events at the completion of layer 0's and layer 7's decode "
                           "kernel in every timed step; interval / 7"),

@@ -653,6 +653,8 @@ slm_status check_device_error(slm_ctx* c) {
     CU(c, cudaMemset(c->d_counters, 0, sizeof(int32_t) * c->max_pairs));
     if (e & kErrTimeout)
       return fail(c, SLM_ERR_DEVICE_TIMEOUT, "device wait timed out (error word 0x%x)", e);
+    if (e & kErrLayout)
+      return fail(c, SLM_ERR_CUDA, "CUDA error: a kernel found its shared memory misaligned (0x%x)", e);
     return fail(c, SLM_ERR_INVALID_INPUT,
                 "invalid input for KV cache: block table held an out-of-pool id (0x%x)", e);
   }
@@ -1436,6 +1438,9 @@ void resolve_oldest(slm_ctx* ctx) {
     if (w & kErrTimeout) {
       dev = SLM_ERR_DEVICE_TIMEOUT;
       snprintf(buf, sizeof buf, "device wait timed out (error word 0x%x)", w);
+    } else if (w & kErrLayout) {
+      dev = SLM_ERR_CUDA;
+      snprintf(buf, sizeof buf, "CUDA error: a kernel found its shared memory misaligned (0x%x)", w);
     } else {
       dev = SLM_ERR_INVALID_INPUT;
       snprintf(buf, sizeof buf,

@@ -67,7 +67,9 @@ struct CopyJob {
 
 // Device status words (per batch sequence, and one per context).
 enum : int32_t { kStatusNonFinite = 1 };
-enum : int32_t { kErrTimeout = 1, kErrBadBlock = 2 };
+// Device error word bits: a bounded wait expired; a block table held an id
+// outside the pool; a kernel found its shared-memory layout misaligned.
+enum : int32_t { kErrTimeout = 1, kErrBadBlock = 2, kErrLayout = 4 };
 
 struct PoolGeom {
   void* k;                   // pool base (layer 0)

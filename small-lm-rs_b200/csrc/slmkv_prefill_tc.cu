@@ -8,7 +8,7 @@
 // the group times 128/G consecutive new tokens (row r = token r/G, head r%G),
 // so every K/V tile is shared by the whole group. Per 128-token K/V tile:
 //   S = Q K^T        tcgen05.mma kind::f16, M=128 N=128, f32 in TMEM columns
-//                    [0,128); Q is split into bf16 (hi, lo) tiles, two passes
+//                    [0,128); Q rounded to bf16 after RoPE and scaling
 //   softmax          4 warps, one row per thread (TMEM lane = row), exp2
 //                    domain, causal mask; the running max moves only when a
 //                    row's max grows by more than 2^8, then O is rescaled
@@ -17,8 +17,10 @@
 // Q, K and V tiles are 128-byte-swizzled: K/V blocks arrive by TMA (16 rows
 // per block, block-table lookups; two tiles in flight), Q and P are written
 // by the threads in the same layout. One thread issues the MMAs and commits
-// them to mbarriers. Every wait is bounded; on expiry the CTA records an
-// error, waits (bounded) for its own MMAs and copies, frees TMEM and exits.
+// them to mbarriers. Two CTAs share an SM (112 KiB of shared memory and 256
+// TMEM columns each), so one CTA's softmax overlaps the other's MMAs and
+// copies. Every wait is bounded; on expiry the CTA records an error, waits
+// (bounded) for its own MMAs and copies, frees TMEM and exits.
 #include <cstdint>
 
 #include "slmkv_internal.h"
@@ -35,16 +37,17 @@ constexpr float kScaleLog2Tc = 0.125f * 1.4426950408889634f;
 constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s
 constexpr int kWaitSpinsMax = 1 << 26;
 
-// Shared memory (offsets from a 1024-aligned base).
-constexpr int kOffQhi = 0;
-constexpr int kOffQlo = kOffQhi + kTileBytes;
-constexpr int kOffK = kOffQlo + kTileBytes;          // 2 buffers
+// Shared memory. The dynamic base is the start of the CTA's window (the
+// kernel has no static shared variables), 1024-aligned as the 128-byte
+// swizzle needs; the kernel checks it and reports an error otherwise.
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kTileBytes;            // 2 buffers
 constexpr int kOffV = kOffK + 2 * kTileBytes;        // 2 buffers
 constexpr int kOffP = kOffV + 2 * kTileBytes;        // tokens 0-63, 64-127
 constexpr int kOffBar = kOffP + 2 * kTileBytes;      // kv_full[2], s_done, o_done
 constexpr int kOffMisc = kOffBar + 4 * 8;            // tmem base, abort flag
-constexpr int kSmemTc = kOffMisc + 16 + 1024;        // + alignment slack
-static_assert(kSmemTc <= 227 * 1024, "prefill tiles exceed shared memory");
+constexpr int kSmemTc = kOffMisc + 16;
+static_assert(2 * (kSmemTc + 1024) <= 228 * 1024, "two prefill CTAs must fit one SM");
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -172,18 +175,19 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
   const uint32_t rb = (b + 0x7FFFu + ((b >> 16) & 1u)) >> 16;
   return (ra & 0xFFFFu) | (rb << 16);
 }
-__device__ __forceinline__ float bf16_lo_f(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16_hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 // Byte offset of 16-byte unit u of row r in a 128-byte-swizzled tile.
 __device__ __forceinline__ uint32_t swz(int r, int u) {
   return static_cast<uint32_t>(((r >> 3) << 10) + ((r & 7) << 7) + (((u ^ r) & 7) << 4));
 }
 
 template <int G>
-__global__ void __launch_bounds__(128, 1) prefill_tc_kernel(const __grid_constant__ PrefillLaunch p) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  uint8_t* sm = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
+__global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constant__ PrefillLaunch p) {
+  extern __shared__ __align__(1024) uint8_t sm[];
   const uint32_t sbase = su32(sm);
+  if (sbase & 1023u) {  // uniform over the CTA: report instead of misreading tiles
+    if (threadIdx.x == 0) atomicOr(p.g.error, kErrLayout);
+    return;
+  }
   const int tid = threadIdx.x, warp = tid >> 5;
   const int si = blockIdx.y, h = blockIdx.z;
   const int tile = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // long tiles first
@@ -242,8 +246,7 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(const __grid_constan
   const int tq = r / G, gq = r % G;
   const int qpos = se.base + q0 + tq;
   {
-    uint8_t* qhi = sm + kOffQhi;
-    uint8_t* qlo = sm + kOffQlo;
+    uint8_t* qt = sm + kOffQ;
     const bool live = tq < nq;
     const float2* src = reinterpret_cast<const float2*>(
         p.q + (static_cast<size_t>(se.row_offset + q0 + (live ? tq : 0)) * Hq + h * G + gq) *
@@ -251,7 +254,7 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(const __grid_constan
     const float2* cs = p.g.rope + static_cast<size_t>(live ? qpos : 0) * (kHeadDim / 2);
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      uint32_t hw[4], lw[4];
+      uint32_t hw[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         float2 x = live ? src[4 * u + k] : make_float2(0.f, 0.f);
@@ -263,10 +266,8 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(const __grid_constan
         x.x *= kScaleLog2Tc;
         x.y *= kScaleLog2Tc;
         hw[k] = bf16x2(x.x, x.y);
-        lw[k] = bf16x2(__fsub_rn(x.x, bf16_lo_f(hw[k])), __fsub_rn(x.y, bf16_hi_f(hw[k])));
       }
-      *reinterpret_cast<uint4*>(qhi + swz(r, u)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(qlo + swz(r, u)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      *reinterpret_cast<uint4*>(qt + swz(r, u)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     }
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -314,16 +315,12 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(const __grid_constan
       ok = false;
       break;
     }
-    // ---- S = (Q_hi + Q_lo) K^T -------------------------------------------
+    // ---- S = Q K^T ------------------------------------------------------------
     if (tid == 0) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
-        mma_f16(tmem, sdesc(sbase + kOffQhi + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64), kIdQK,
+        mma_f16(tmem, sdesc(sbase + kOffQ + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64), kIdQK,
                 kk > 0);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16(tmem, sdesc(sbase + kOffQlo + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64), kIdQK,
-                1);
       mma_commit(bar_s);
     }
     s_issued = j + 1;
