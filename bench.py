@@ -56,10 +56,10 @@ WORKLOADS = {
 }
 
 
-def select_workload(name: str) -> None:
+def select_workload(name: str, batch: int | None = None) -> None:
     global B, LEN_LO, LEN_HI, LAYERS, HQ, HKV, D, CTX, BF16, S_KV, WORKLOAD, WORKLOAD_NAME
     w = WORKLOADS[name]
-    B, LEN_LO, LEN_HI = w["B"], w["LEN_LO"], w["LEN_HI"]
+    B, LEN_LO, LEN_HI = (batch or w["B"]), w["LEN_LO"], w["LEN_HI"]
     LAYERS, HQ, HKV, D, CTX, BF16 = w["LAYERS"], w["HQ"], w["HKV"], w["D"], w["CTX"], w["BF16"]
     S_KV = 2 if BF16 else 4
     WORKLOAD_NAME = name
@@ -81,8 +81,10 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="microbench")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per GPU instead of the workload's (smaller cases for profiling)")
     args = ap.parse_args()
-    select_workload(args.workload)
+    select_workload(args.workload, args.batch)
     return args
 
 

@@ -44,8 +44,8 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTileBytes;            // 2 buffers
 constexpr int kOffV = kOffK + 2 * kTileBytes;        // 2 buffers
 constexpr int kOffP = kOffV + 2 * kTileBytes;        // tokens 0-63, 64-127
-constexpr int kOffBar = kOffP + 2 * kTileBytes;      // kv_full[2], s_done, o_done
-constexpr int kOffMisc = kOffBar + 4 * 8;            // tmem base, abort flag
+constexpr int kOffBar = kOffP + 2 * kTileBytes;      // k_full[2], v_full[2], s_done, o_done
+constexpr int kOffMisc = kOffBar + 6 * 8;            // TMEM base address
 constexpr int kSmemTc = kOffMisc + 16;
 static_assert(2 * (kSmemTc + 1024) <= 228 * 1024, "two prefill CTAs must fit one SM");
 
@@ -168,12 +168,11 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// MMA operands (Q, P) to bf16, round to nearest even, one instruction per pair.
 __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
-  const uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
-  // round to nearest even, as linear.rs:14-23 (inputs are finite here)
-  const uint32_t ra = (a + 0x7FFFu + ((a >> 16) & 1u)) >> 16;
-  const uint32_t rb = (b + 0x7FFFu + ((b >> 16) & 1u)) >> 16;
-  return (ra & 0xFFFFu) | (rb << 16);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 // Byte offset of 16-byte unit u of row r in a 128-byte-swizzled tile.
 __device__ __forceinline__ uint32_t swz(int r, int u) {
@@ -201,15 +200,17 @@ __global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constan
   const int n_kv = last_pos + 1;
   const int n_tiles = (n_kv + kTileN - 1) / kTileN;
 
-  const uint32_t bar_kv0 = sbase + kOffBar, bar_s = sbase + kOffBar + 16, bar_o = sbase + kOffBar + 24;
+  const uint32_t bar_k0 = sbase + kOffBar, bar_v0 = sbase + kOffBar + 16,
+                 bar_s = sbase + kOffBar + 32, bar_o = sbase + kOffBar + 40;
   uint32_t* misc = reinterpret_cast<uint32_t*>(sm + kOffMisc);
   if (tid == 0) {
-    bar_init(bar_kv0, 1);
-    bar_init(bar_kv0 + 8, 1);
+    bar_init(bar_k0, 1);
+    bar_init(bar_k0 + 8, 1);
+    bar_init(bar_v0, 1);
+    bar_init(bar_v0 + 8, 1);
     bar_init(bar_s, 1);
     bar_init(bar_o, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    misc[1] = 0;  // abort flag
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -219,25 +220,30 @@ __global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constan
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
 
-  // K/V tile j -> buffer j&1: its 16-token blocks through the block table.
+  // K or V tile j -> buffer j&1: its 16-token blocks through the block table,
+  // by warp 0 with one lane per block (the table lookups overlap). K tile j+2
+  // goes as soon as S_j has been read out of TMEM, V tile j+1 as soon as
+  // P·V_{j-1} is done, so copies run a tile or two ahead.
   const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
   const int layer_row0 = p.layer * p.g.num_blocks * Hkv;
-  auto load_tile = [&](int j) {  // thread 0
+  const int lane = tid & 31;
+  auto load_half = [&](int j, bool v) {  // warp 0, all lanes
     const int b0 = j * (kTileN / kBlockTokens);
     const int nb = min(kTileN / kBlockTokens, (n_kv + kBlockTokens - 1) / kBlockTokens - b0);
-    const uint32_t bar = bar_kv0 + 8 * (j & 1);
-    bar_expect_tx(bar, static_cast<uint32_t>(nb) * 2 * kBlockTokens * kHeadDim * 2);
-    for (int b = 0; b < nb; ++b) {
-      int32_t blk = bt[b0 + b];
+    const uint32_t bar = (v ? bar_v0 : bar_k0) + 8 * (j & 1);
+    if (lane == 0) bar_expect_tx(bar, static_cast<uint32_t>(nb) * kBlockTokens * kHeadDim * 2);
+    __syncwarp();
+    if (lane < nb) {
+      int32_t blk = bt[b0 + lane];
       if (static_cast<uint32_t>(blk) >= static_cast<uint32_t>(p.g.num_blocks)) {
         atomicOr(p.g.error, kErrBadBlock);
         blk = 0;
       }
       const int y = (layer_row0 + blk * Hkv + h) * kBlockTokens;
-      const uint32_t off = static_cast<uint32_t>((j & 1) * kTileBytes + b * kBlockTokens * 128);
-      tma_rows(sbase + kOffK + off, &p.tmap_k, y, bar);
-      tma_rows(sbase + kOffV + off, &p.tmap_v, y, bar);
+      const uint32_t off = static_cast<uint32_t>((j & 1) * kTileBytes + lane * kBlockTokens * 128);
+      tma_rows(sbase + (v ? kOffV : kOffK) + off, v ? &p.tmap_v : &p.tmap_k, y, bar);
     }
+    __syncwarp();
   };
 
   // Q rows: RoPE at the token's position, scaled into the exp2 domain, bf16
@@ -276,62 +282,48 @@ __global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constan
   tc_fence_after();
   const uint32_t tmem = misc[0];
   const uint32_t tmem_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  if (tid == 0) {
-    load_tile(0);
-    if (n_tiles > 1) load_tile(1);
-  }
-
   constexpr uint32_t kIdQK = idesc(kTileM, kTileN, false);
   constexpr uint32_t kIdPV = idesc(kTileM, kHeadDim, true);
+  // Progress (thread 0's view), for draining on an error: K and V tiles
+  // whose copies were issued / seen landed, S and P·V products issued / seen.
+  int k_issued = 0, k_seen = 0, v_issued = 0, v_seen = 0, s_issued = 0, s_seen = 0,
+      o_issued = 0, o_seen = 0;
+  // A failed wait sets this thread's flag; the CTA decides at its barriers
+  // with __syncthreads_or, so every thread takes the same branch.
+  bool fail = false;
+  auto issue_s = [&](int j) {  // thread 0: S_j = Q K_j^T once K_j landed
+    if (!bar_wait(bar_k0 + 8 * (j & 1), (j >> 1) & 1)) {
+      fail = true;
+      return;
+    }
+    k_seen = j + 1;
+    tc_fence_after();
+    const uint32_t kaddr = sbase + kOffK + (j & 1) * kTileBytes;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+      mma_f16(tmem, sdesc(sbase + kOffQ + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64), kIdQK,
+              kk > 0);
+    mma_commit(bar_s);
+    s_issued = j + 1;
+  };
+  if (warp == 0) {
+    for (int t = 0; t < min(n_tiles, 2); ++t) {
+      load_half(t, false);
+      load_half(t, true);
+    }
+    k_issued = v_issued = min(n_tiles, 2);
+    if (lane == 0) issue_s(0);
+  }
+
   float m_used = -INFINITY, l_sum = 0.f;
-  // Progress, for draining on an error: tiles whose copies were issued and
-  // seen landed, S products issued and seen, P·V products issued and seen.
-  int kv_issued = min(n_tiles, 2), kv_seen = 0, s_issued = 0, s_seen = 0, o_issued = 0,
-      o_seen = 0;
-  bool ok = true;
-  // Every failure sets the shared abort flag before the next barrier, after
-  // which all threads leave the loop together.
+  bool aborted = false;
   for (int j = 0; j < n_tiles; ++j) {
     const int buf = j & 1;
-    const uint32_t kaddr = sbase + kOffK + buf * kTileBytes;
     const uint32_t vaddr = sbase + kOffV + buf * kTileBytes;
-    // ---- K/V tile landed; stale V rows of the last tile cleared ----------
-    if (bar_wait(bar_kv0 + 8 * buf, (j >> 1) & 1)) kv_seen = j + 1;
-    else ok = false;
-    const int valid = min(kTileN, n_kv - j * kTileN);
-    if (ok && valid < kTileN) {
-      // P = 0 there, but 0 times a non-finite stale value is not 0.
-      uint8_t* vt = sm + kOffV + buf * kTileBytes;
-      // row t of a swizzled tile is the 128 bytes at t*128 (units permuted)
-      for (int i = valid * 8 + tid; i < kTileN * 8; i += 128)
-        *reinterpret_cast<uint4*>(vt + (i >> 3) * 128 + (i & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    }
-    if (!ok) misc[1] = 1;
-    tc_fence_before();
-    __syncthreads();
+    // ---- S_j out of TMEM into registers ----------------------------------------
+    if (!bar_wait(bar_s, j & 1)) fail = true;
+    else if (tid == 0) s_seen = j + 1;
     tc_fence_after();
-    if (misc[1]) {
-      ok = false;
-      break;
-    }
-    // ---- S = Q K^T ------------------------------------------------------------
-    if (tid == 0) {
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16(tmem, sdesc(sbase + kOffQ + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64), kIdQK,
-                kk > 0);
-      mma_commit(bar_s);
-    }
-    s_issued = j + 1;
-    if (bar_wait(bar_s, j & 1)) {
-      s_seen = j + 1;
-    } else {
-      ok = false;
-      misc[1] = 1;
-    }
-    tc_fence_after();
-    // ---- softmax of this thread's row ---------------------------------------
     float s[kTileN];
 #pragma unroll
     for (int c = 0; c < kTileN / 32; ++c) {
@@ -341,38 +333,64 @@ __global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constan
       for (int i = 0; i < 32; ++i) s[32 * c + i] = v[i];
     }
     tmem_wait_ld();
+    tc_fence_before();
+    aborted = __syncthreads_or(fail) != 0;
+    tc_fence_after();
+    if (aborted) break;
+    // S columns and K buffer j&1 are free: the next copy and product start now.
+    if (warp == 0) {
+      if (j + 2 < n_tiles) {
+        load_half(j + 2, false);
+        k_issued = j + 3;
+      }
+      if (lane == 0 && j + 1 < n_tiles) issue_s(j + 1);
+    }
+    // ---- softmax of this thread's row ---------------------------------------
     const bool live = tq < nq;
     const int kp0 = j * kTileN;
     float mx = -INFINITY;
+    // causal (attention.rs:207): key position <= query position. Only tiles
+    // reaching past the CTA's first query position need the mask (the same
+    // decision in every thread); rows past the CTA's tokens read zeros.
+    if (kp0 + kTileN - 1 > se.base + q0 || !live) {
 #pragma unroll
-    for (int i = 0; i < kTileN; ++i) {
-      // causal (attention.rs:207): key position <= query position
-      if (live && kp0 + i > qpos) s[i] = -INFINITY;
-      if (!live) s[i] = 0.f;
-      mx = fmaxf(mx, s[i]);
-    }
-    // The previous P·V must be done before P and O are touched.
-    if (j > 0) {
-      if (bar_wait(bar_o, (j - 1) & 1)) {
-        o_seen = j;
-      } else {
-        ok = false;
-        misc[1] = 1;
+      for (int i = 0; i < kTileN; ++i) {
+        if (live && kp0 + i > qpos) s[i] = -INFINITY;
+        if (!live) s[i] = 0.f;
       }
     }
-    tc_fence_after();
-    if (ok && j >= 1 && j + 1 < n_tiles) {  // into the buffer P·V just freed
-      if (tid == 0) load_tile(j + 1);
-      kv_issued = j + 2;
-    }
-    // tcgen05.ld/st are warp-collective (.sync.aligned): a warp rescales O
-    // when any of its rows moved its max; the other rows scale by 1.
+#pragma unroll
+    for (int i = 0; i < kTileN; ++i) mx = fmaxf(mx, s[i]);
     const bool grow = mx > m_used + 8.f;
     float corr = 1.f;
     if (grow) {
       corr = ex2(m_used - mx);  // 0 on the first tile
       m_used = mx;
     }
+    float psum = 0.f;
+    uint32_t pw[kTileN / 2];
+#pragma unroll
+    for (int i = 0; i < kTileN / 2; ++i) {
+      const float a = ex2(s[2 * i] - m_used), b = ex2(s[2 * i + 1] - m_used);
+      psum += a + b;
+      pw[i] = bf16x2(a, b);
+    }
+    l_sum = fmaf(l_sum, corr, psum);
+    // ---- P·V_{j-1} done: P, O and V buffer (j-1)&1 are free ------------------
+    if (j > 0) {
+      const bool o_ok = bar_wait(bar_o, (j - 1) & 1);
+      if (!o_ok) fail = true;
+      if (warp == 0 && __all_sync(0xffffffffu, o_ok)) {
+        o_seen = j;
+        if (j + 1 < n_tiles) {
+          load_half(j + 1, true);
+          v_issued = j + 2;
+        }
+      }
+    }
+    tc_fence_after();
+    // tcgen05.ld/st are warp-collective (.sync.aligned): a warp rescales O
+    // when any of its rows moved its max; the other rows scale by 1.
     if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
       for (int c = 0; c < kHeadDim / 32; ++c) {
@@ -385,51 +403,55 @@ __global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constan
       }
       tmem_wait_st();
     }
-    float psum = 0.f;
     uint8_t* prow = sm + kOffP;
 #pragma unroll
-    for (int u = 0; u < kTileN / 8; ++u) {
-      uint32_t w[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float a = ex2(s[8 * u + 2 * k] - m_used), b = ex2(s[8 * u + 2 * k + 1] - m_used);
-        psum += a + b;
-        w[k] = bf16x2(a, b);
-      }
-      // tokens 0-63 in the first P tile, 64-127 in the second
+    for (int u = 0; u < kTileN / 8; ++u)  // tokens 0-63 in the first P tile, 64-127 in the second
       *reinterpret_cast<uint4*>(prow + (u >> 3) * kTileBytes + swz(r, u & 7)) =
-          make_uint4(w[0], w[1], w[2], w[3]);
+          make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
+    const int valid = min(kTileN, n_kv - kp0);
+    if (valid < kTileN) {
+      // The last tile: P = 0 past the cache, but 0 times a non-finite stale
+      // value is not 0. Clear those V rows once the tile landed.
+      if (!bar_wait(bar_v0 + 8 * buf, (j >> 1) & 1)) fail = true;
+      uint8_t* vt = sm + kOffV + buf * kTileBytes;
+      // row t of a swizzled tile is the 128 bytes at t*128 (units permuted)
+      for (int i = valid * 8 + tid; i < kTileN * 8; i += 128)
+        *reinterpret_cast<uint4*>(vt + (i >> 3) * 128 + (i & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
     }
-    l_sum = fmaf(l_sum, corr, psum);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
-    __syncthreads();
+    aborted = __syncthreads_or(fail) != 0;
     tc_fence_after();
-    if (misc[1]) {
-      ok = false;
-      break;
-    }
-    // ---- O += P V --------------------------------------------------------------
+    if (aborted) break;
+    // ---- O += P V ----------------------------------------------------------------
     if (tid == 0) {
+      if (bar_wait(bar_v0 + 8 * buf, (j >> 1) & 1)) {
+        v_seen = j + 1;
+        tc_fence_after();
 #pragma unroll
-      for (int kk = 0; kk < kTileN / 16; ++kk)
-        mma_f16(tmem + kOCol,
-                sdesc(sbase + kOffP + (kk >> 2) * kTileBytes + 32 * (kk & 3), 1, 64),
-                sdesc(vaddr + 2048 * kk, kTileBytes >> 4, 64), kIdPV, (j > 0 || kk > 0) ? 1 : 0);
-      mma_commit(bar_o);
+        for (int kk = 0; kk < kTileN / 16; ++kk)
+          mma_f16(tmem + kOCol,
+                  sdesc(sbase + kOffP + (kk >> 2) * kTileBytes + 32 * (kk & 3), 1, 64),
+                  sdesc(vaddr + 2048 * kk, kTileBytes >> 4, 64), kIdPV, (j > 0 || kk > 0) ? 1 : 0);
+        mma_commit(bar_o);
+        o_issued = j + 1;
+      } else {
+        fail = true;
+      }
     }
-    o_issued = j + 1;
   }
 
   // ---- epilogue: O / l to the output rows --------------------------------------
-  if (o_issued > o_seen) {
-    if (bar_wait(bar_o, (o_issued - 1) & 1)) o_seen = o_issued;
-    else misc[1] = 1;
+  tc_fence_before();
+  aborted = __syncthreads_or(fail) != 0;
+  tc_fence_after();
+  if (!aborted) {
+    if (!bar_wait(bar_o, (n_tiles - 1) & 1)) fail = true;
+    else if (tid == 0) o_seen = n_tiles;
   }
   tc_fence_before();
-  __syncthreads();
+  const bool abort = __syncthreads_or(fail) != 0;  // the same in every thread
   tc_fence_after();
-  const bool abort = misc[1] != 0 || o_seen != n_tiles;  // the same in every thread
   if (!abort) {
     // every thread of the warp loads (warp-collective); live rows store
     const float inv = 1.f / l_sum;
@@ -453,7 +475,8 @@ __global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constan
     // shared memory are released.
     if (s_issued > s_seen) bar_wait(bar_s, (s_issued - 1) & 1);
     if (o_issued > o_seen) bar_wait(bar_o, (o_issued - 1) & 1);
-    for (int t = kv_seen; t < kv_issued; ++t) bar_wait(bar_kv0 + 8 * (t & 1), (t >> 1) & 1);
+    for (int t = k_seen; t < k_issued; ++t) bar_wait(bar_k0 + 8 * (t & 1), (t >> 1) & 1);
+    for (int t = v_seen; t < v_issued; ++t) bar_wait(bar_v0 + 8 * (t & 1), (t >> 1) & 1);
   }
   tc_fence_before();
   __syncthreads();
