@@ -227,14 +227,42 @@ __global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constan
   const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
   const int layer_row0 = p.layer * p.g.num_blocks * Hkv;
   const int lane = tid & 31;
+  const int n_blocks = (n_kv + kBlockTokens - 1) / kBlockTokens;
+  // Block ids of tiles [win, win+8) in warp 0's registers: blk_cur holds
+  // tiles win..win+3 (lane l: tile win + l/8, block l%8), blk_nxt the next
+  // four. The window moves at the top of an iteration, when the oldest tile
+  // still needed (V of tile j+1) has left its first half; the next four
+  // tiles' ids then load four iterations before they are needed.
+  int win = 0, blk_cur = 0, blk_nxt = 0;
+  auto fetch_window = [&](int first_tile) {
+    const int b = first_tile * (kTileN / kBlockTokens) + lane;
+    return b < n_blocks ? bt[b] : 0;
+  };
+  if (warp == 0) {
+    blk_cur = fetch_window(0);
+    blk_nxt = fetch_window(4);
+  }
+  auto advance_window = [&](int oldest) {  // warp 0
+    while (oldest >= win + 4) {
+      blk_cur = blk_nxt;
+      win += 4;
+      blk_nxt = fetch_window(win + 4);
+    }
+  };
+  auto block_of = [&](int t, int b) {  // warp 0, all lanes; win <= t < win + 8
+    const int rel = t - win;
+    const int a = __shfl_sync(0xffffffffu, blk_cur, ((rel & 3) << 3) + b);
+    const int c = __shfl_sync(0xffffffffu, blk_nxt, ((rel & 3) << 3) + b);
+    return rel < 4 ? a : c;
+  };
   auto load_half = [&](int j, bool v) {  // warp 0, all lanes
     const int b0 = j * (kTileN / kBlockTokens);
-    const int nb = min(kTileN / kBlockTokens, (n_kv + kBlockTokens - 1) / kBlockTokens - b0);
+    const int nb = min(kTileN / kBlockTokens, n_blocks - b0);
     const uint32_t bar = (v ? bar_v0 : bar_k0) + 8 * (j & 1);
+    int32_t blk = block_of(j, lane & 7);
     if (lane == 0) bar_expect_tx(bar, static_cast<uint32_t>(nb) * kBlockTokens * kHeadDim * 2);
     __syncwarp();
     if (lane < nb) {
-      int32_t blk = bt[b0 + lane];
       if (static_cast<uint32_t>(blk) >= static_cast<uint32_t>(p.g.num_blocks)) {
         atomicOr(p.g.error, kErrBadBlock);
         blk = 0;
@@ -320,6 +348,7 @@ __global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constan
   for (int j = 0; j < n_tiles; ++j) {
     const int buf = j & 1;
     const uint32_t vaddr = sbase + kOffV + buf * kTileBytes;
+    if (warp == 0) advance_window(j + 1);
     // ---- S_j out of TMEM into registers ----------------------------------------
     if (!bar_wait(bar_s, j & 1)) fail = true;
     else if (tid == 0) s_seen = j + 1;
