@@ -53,7 +53,14 @@ WORKLOADS = {
                        BF16=False),
     "gqa-bf16": dict(B=16, LEN_LO=1024, LEN_HI=8191, LAYERS=8, HQ=32, HKV=8, D=64, CTX=8192,
                      BF16=True),
+    # continuous batching: the request trace below through the scheduler
+    "serve": dict(B=512, LEN_LO=8, LEN_HI=256, LAYERS=8, HQ=4, HKV=2, D=64, CTX=512, BF16=False),
 }
+# "serve": 4096 requests in total (shared by the ranks), Poisson arrivals at
+# SERVE_RATE requests/s (seeded), prompts U[8,256], outputs U[16,256], at
+# most 512 running per GPU, the 8M model's KV shape.
+SERVE_REQUESTS, SERVE_RATE, SERVE_OUT_LO, SERVE_OUT_HI = 4096, 50000.0, 16, 256
+SERVE_PREFILL_TOKENS = 4096
 
 
 def select_workload(name: str, batch: int | None = None) -> None:
@@ -551,10 +558,137 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def serve_trace(seed: int):
+    """(arrival s, prompt length, output length) of every request, seeded."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed + 4242)
+    arrivals = np.cumsum(rng.exponential(1.0 / SERVE_RATE, size=SERVE_REQUESTS))
+    prompts = rng.integers(LEN_LO, LEN_HI + 1, size=SERVE_REQUESTS)
+    outputs = rng.integers(SERVE_OUT_LO, SERVE_OUT_HI + 1, size=SERVE_REQUESTS)
+    return arrivals, prompts, outputs
+
+
+def run_serve(args):
+    """Continuous batching of the request trace: every step the scheduler plans
+    a decode batch and a prefill batch, their KV work runs for all layers with
+    synthetic projections (the model's matmuls are outside this path), and the
+    statuses are committed. Requests arrive on the host clock. Throughput =
+    output tokens of all ranks / slowest rank's device time."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import slmkv
+    from slmkv.shard import max_over_ranks, rank_share
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    arrivals, prompts, outputs = serve_trace(args.seed)
+    mine = rank_share([int(p + o) for p, o in zip(prompts, outputs)], world, rank)
+    pool = slmkv.KvPool(num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV,
+                        head_dimension=D, context_length=CTX, num_blocks=B * (CTX // BLOCK),
+                        max_sequences=B, device=local)
+    pool.shuffle(args.seed + 1)
+    sched = slmkv.Scheduler(pool, max_running=B, max_prefill_tokens=SERVE_PREFILL_TOKENS)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + 3)
+    nd_max, np_max = B, SERVE_PREFILL_TOKENS
+    dq = torch.randn((LAYERS, nd_max, HQ, D), generator=gen, device=dev)
+    dk = torch.randn((LAYERS, nd_max, HKV, D), generator=gen, device=dev)
+    dout = torch.empty((LAYERS, nd_max, HQ, D), device=dev)
+    pq = torch.randn((LAYERS, np_max, HQ, D), generator=gen, device=dev)
+    pk = torch.randn((LAYERS, np_max, HKV, D), generator=gen, device=dev)
+    pout = torch.empty((LAYERS, np_max, HQ, D), device=dev)
+    dptr = [(dq[l].data_ptr(), dk[l].data_ptr(), dk[l].data_ptr(), dout[l].data_ptr())
+            for l in range(LAYERS)]
+    stream = torch.cuda.current_stream()
+    ones = slmkv._i32_array([1] * B)
+
+    def run_step():
+        nd, npf = sched.plan()
+        dst = pst = None
+        if nd:
+            b = slmkv.Batch.for_sequences(pool, nd, sched._dseq, ones, stream)
+            for l in range(LAYERS):
+                b.decode_layer_ptr(l, *dptr[l])
+            dst = b.end(raise_on_error=False)
+        if npf:
+            counts = list(sched._pcnt[:npf])
+            rows = sum(counts)
+            b = slmkv.Batch.for_sequences(pool, npf, sched._pseq, sched._pcnt, stream)
+            for l in range(LAYERS):
+                b.append_layer(l, pk[l, :rows], pk[l, :rows], rotate_keys=True)
+                b.prefill_attention(l, pq[l, :rows], pout[l, :rows], rotate_query=True)
+            pst = b.end(raise_on_error=False)
+        return nd, npf, sched.commit(dst, pst)
+
+    order = sorted(mine, key=lambda i: arrivals[i])
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start.record(stream)
+    t0 = time.perf_counter()
+    nxt, finished, failed, steps = 0, 0, 0, 0
+    while finished < len(order):
+        now = time.perf_counter() - t0
+        while nxt < len(order) and arrivals[order[nxt]] <= now:
+            i = order[nxt]
+            sched.submit(i, int(prompts[i]), int(outputs[i]))
+            nxt += 1
+        nd, npf, fin = run_step()
+        steps += 1
+        finished += len(fin)
+        failed += sum(1 for _, st, _ in fin if st != 0)
+        if nd == 0 and npf == 0 and nxt < len(order):
+            time.sleep(max(0.0, arrivals[order[nxt]] - (time.perf_counter() - t0)))
+    t_stop.record(stream)
+    torch.cuda.synchronize()
+    counts = sched.counts()
+    ms = t_start.elapsed_time(t_stop)
+    (ms,) = max_over_ranks([ms], device=dev)
+    tokens = torch.tensor([float(counts["generated_tokens"])], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tokens)
+    if failed:
+        raise RuntimeError(f"{failed} requests failed")
+    result = {
+        "metric": METRIC, "value": float(tokens.item()) / (ms / 1e3), "unit": "tok/s",
+        "n_gpus": world, "steps": steps, "warmup": 0, "ms_per_step": ms / max(1, steps),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": (f"continuous batching: {SERVE_REQUESTS} requests, Poisson "
+                                f"arrivals {SERVE_RATE:.0f}/s, prompts U[{LEN_LO},{LEN_HI}], "
+                                f"outputs U[{SERVE_OUT_LO},{SERVE_OUT_HI}], <= {B} running per "
+                                f"GPU, {LAYERS} layers, Hq={HQ}, Hkv={HKV}, d={D}, f32 KV; "
+                                "synthetic Q/K/V per step"),
+                   "name": "serve", "requests_per_rank": len(order), "seed": args.seed},
+        "output_tokens": int(tokens.item()), "preemptions": counts["preemptions"],
+        "gpu_launches": pool.launch_count(),
+    }
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    sched.close()
+    pool.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif WORKLOAD_NAME == "serve":
+        run_serve(args)
     else:
         run_ours(args)
 

@@ -211,6 +211,53 @@ slm_status slm_pool_stats(const slm_ctx* ctx, int32_t* free_blocks, int32_t* ind
 /* Shuffles the free list with a seeded permutation, so that sequences get
  * scattered physical blocks. Pool must be unused. */
 slm_status slm_pool_shuffle(slm_ctx* ctx, uint64_t seed);
+/* The configuration a context was created with (KvCacheConfig::from_model's
+ * inputs, kv_cache.rs:27-41). */
+slm_status slm_ctx_config(const slm_ctx* ctx, slm_config* out);
+
+/* ---- continuous batching (no reference counterpart: the reference serves
+ *      one request at a time behind a Mutex, rust/server/src/worker.rs:87-98).
+ * A scheduler owns the pool of one context: requests are admitted in arrival
+ * order while fewer than max_running are running and the pool holds their
+ * prompt; every step it plans one decode token for each running request whose
+ * prompt is cached, and prompt chunks for the others within max_prefill_tokens
+ * (a prompt may take several steps). The caller runs the step's KV work: a
+ * decode batch (slm_batch_begin with counts 1, slm_batch_decode_layer per
+ * layer) and a prefill batch (slm_batch_begin with the chunk counts,
+ * slm_batch_append_layer and slm_batch_prefill_attention per layer), then
+ * commits the statuses. The first output token comes with the end of the
+ * prompt (GenerationService: prefill logits pick it); each decode step adds
+ * one; a request is finished after max_new_tokens and its sequence is freed.
+ * When the pool cannot hold a step, the most recently admitted requests are
+ * preempted: their sequences are freed and they go back to the front of the
+ * queue, to prefill again what they had cached (recomputation). Sequence
+ * capacity per request: prompt_len + max_new_tokens <= context_length. */
+typedef struct slm_sched slm_sched;
+typedef struct {
+  int32_t max_running;         /* requests stepped together (>= 1) */
+  int32_t max_prefill_tokens;  /* prompt tokens planned per step (>= 1) */
+} slm_sched_config;
+slm_status slm_sched_create(slm_ctx* ctx, const slm_sched_config* config, slm_sched** out);
+slm_status slm_sched_destroy(slm_sched* sched);
+slm_status slm_sched_submit(slm_sched* sched, int64_t request_id, int32_t prompt_len,
+                            int32_t max_new_tokens);
+/* Plans the next step into caller arrays of capacity max_running: the decode
+ * sequences, and the prefill sequences with their token counts. A step with
+ * nothing to do returns 0 and 0. */
+slm_status slm_sched_plan(slm_sched* sched, int32_t* n_decode, int32_t* decode_seq,
+                          int32_t* n_prefill, int32_t* prefill_seq, int32_t* prefill_count);
+/* Commits the last plan: the per-sequence statuses its batches reported (in
+ * plan order; NULL when that part was empty). Requests whose sequence failed
+ * are finished with that status. Fills the requests finished by this step
+ * (arrays of capacity max_running; their output token counts in h_generated,
+ * NULL to skip). */
+slm_status slm_sched_commit(slm_sched* sched, const int32_t* decode_status,
+                            const int32_t* prefill_status, int32_t* n_finished,
+                            int64_t* finished_id, int32_t* finished_status, int32_t* h_generated);
+/* Queue sizes and counters: waiting, running, preemptions so far, output
+ * tokens so far. */
+slm_status slm_sched_counts(const slm_sched* sched, int32_t* waiting, int32_t* running,
+                            int64_t* preemptions, int64_t* generated_tokens);
 
 /* ---- allocation-free decode attention ------------------------------------
  * No counterpart in the reference. For callers that cannot allocate device

@@ -1662,6 +1662,12 @@ slm_status slm_pool_stats(const slm_ctx* ctx, int32_t* free_blocks, int32_t* ind
   return SLM_OK;
 }
 
+slm_status slm_ctx_config(const slm_ctx* ctx, slm_config* out) {
+  if (!ctx || !out) return SLM_ERR_INVALID_INPUT;
+  *out = ctx->cfg;
+  return SLM_OK;
+}
+
 slm_status slm_pool_shuffle(slm_ctx* ctx, uint64_t seed) {
   if (!ctx) return SLM_ERR_INVALID_INPUT;
   if (static_cast<int32_t>(ctx->free_list.size()) != ctx->cfg.num_blocks)

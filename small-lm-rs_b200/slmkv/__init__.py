@@ -89,6 +89,10 @@ class SlmConfig(C.Structure):
     ]
 
 
+class SchedConfig(C.Structure):
+    _fields_ = [("max_running", C.c_int32), ("max_prefill_tokens", C.c_int32)]
+
+
 # Every symbol include/slmkv.h declares, with its ctypes signature.
 _i32, _i64, _u64, _vp = C.c_int32, C.c_int64, C.c_uint64, C.c_void_p
 _pi32 = C.POINTER(C.c_int32)
@@ -126,6 +130,13 @@ SIGNATURES = {
     "slm_prefix_publish": (C.c_int, [_vp, _i32, _pu32, _i32, _pi32]),
     "slm_pool_stats": (C.c_int, [_vp, _pi32, _pi32]),
     "slm_pool_shuffle": (C.c_int, [_vp, _u64]),
+    "slm_ctx_config": (C.c_int, [_vp, C.POINTER(SlmConfig)]),
+    "slm_sched_create": (C.c_int, [_vp, C.POINTER(SchedConfig), C.POINTER(_vp)]),
+    "slm_sched_destroy": (C.c_int, [_vp]),
+    "slm_sched_submit": (C.c_int, [_vp, _i64, _i32, _i32]),
+    "slm_sched_plan": (C.c_int, [_vp, _pi32, _pi32, _pi32, _pi32, _pi32]),
+    "slm_sched_commit": (C.c_int, [_vp, _pi32, _pi32, _pi32, C.POINTER(_i64), _pi32, _pi32]),
+    "slm_sched_counts": (C.c_int, [_vp, _pi32, _pi32, C.POINTER(_i64), C.POINTER(_i64)]),
     "slm_decode_attention_noalloc": (
         C.c_int, [_vp, _vp, _i32, _i32, _i32, _pi32, _i32, _pi32, _i32, _vp, _vp, _vp]),
 }
@@ -497,6 +508,24 @@ class Batch:
         self._h = h
         self.statuses: list[int] | None = None
 
+    @classmethod
+    def for_sequences(cls, pool: KvPool, n: int, seq_ids, counts, stream=None) -> "Batch":
+        """A step over n sequence ids (ctypes int32 arrays of ids and token
+        counts, e.g. a Scheduler plan's), without KvCache objects."""
+        b = cls.__new__(cls)
+        b.pool = pool
+        b.caches = [None] * n
+        b._ids, b._counts = seq_ids, counts
+        b._status = (C.c_int32 * max(1, n))()
+        b.token_counts = None
+        h = C.c_void_p()
+        rc = _fast.begin(pool.handle, n, seq_ids, counts, _stream_ptr(stream), C.byref(h))
+        if rc:
+            pool.check(rc)
+        b._h = h
+        b.statuses = None
+        return b
+
     def decode_layer(self, layer: int, query, keys, values, out) -> None:
         self.pool.check(lib().slm_batch_decode_layer(self._h, int(layer), _ptr(query),
                                                      _ptr(keys), _ptr(values), _ptr(out)))
@@ -640,3 +669,75 @@ def decode_attention_noalloc(key_pool, value_pool, block_table, lengths, query, 
         msg = (lib().slm_last_error(None) or b"").decode()
         raise _error_class(rc)(rc, msg)
     return out
+
+
+class Scheduler:
+    """Continuous batching over one pool (``slm_sched_*``): requests are
+    admitted in arrival order, every step plans a decode token for each
+    request whose prompt is cached and prompt chunks for the others, and the
+    caller runs the step's KV batches and commits their statuses. The pool
+    belongs to the scheduler while it runs."""
+
+    def __init__(self, pool: KvPool, *, max_running: int, max_prefill_tokens: int):
+        self.pool = pool
+        h = C.c_void_p()
+        cfg = SchedConfig(int(max_running), int(max_prefill_tokens))
+        pool.check(lib().slm_sched_create(pool.handle, C.byref(cfg), C.byref(h)))
+        self._h = h
+        self.max_running = min(int(max_running), pool.config.max_sequences)
+        n = max(1, self.max_running)
+        self._dseq, self._pseq, self._pcnt = (C.c_int32 * n)(), (C.c_int32 * n)(), (C.c_int32 * n)()
+        self._fid, self._fst, self._fgen = (C.c_int64 * n)(), (C.c_int32 * n)(), (C.c_int32 * n)()
+        self._nd, self._np, self._nf = C.c_int32(), C.c_int32(), C.c_int32()
+
+    def close(self) -> None:
+        if self._h is not None:
+            lib().slm_sched_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def submit(self, request_id: int, prompt_len: int, max_new_tokens: int) -> None:
+        self.pool.check(lib().slm_sched_submit(self._h, int(request_id), int(prompt_len),
+                                               int(max_new_tokens)))
+
+    def plan(self):
+        """(decode_seq, prefill_seq, prefill_count) of the next step: ctypes
+        int32 arrays valid until the next plan, and their lengths."""
+        self.pool.check(lib().slm_sched_plan(self._h, C.byref(self._nd), self._dseq,
+                                             C.byref(self._np), self._pseq, self._pcnt))
+        return self._nd.value, self._np.value
+
+    def decode_seqs(self) -> list[int]:
+        return list(self._dseq[: self._nd.value])
+
+    def prefill_seqs(self) -> list[tuple[int, int]]:
+        return list(zip(self._pseq[: self._np.value], self._pcnt[: self._np.value]))
+
+    def commit(self, decode_status=None, prefill_status=None) -> list[tuple[int, int, int]]:
+        """Commits the last plan; returns the finished requests as
+        (request_id, status, output tokens)."""
+        def arr(x, n):
+            if n == 0:
+                return None
+            if x is None:
+                return (C.c_int32 * n)()
+            return x if isinstance(x, C.Array) else _i32_array(list(x))
+        rc = lib().slm_sched_commit(self._h, arr(decode_status, self._nd.value),
+                                    arr(prefill_status, self._np.value), C.byref(self._nf),
+                                    self._fid, self._fst, self._fgen)
+        self.pool.check(rc)
+        n = self._nf.value
+        return list(zip(self._fid[:n], self._fst[:n], self._fgen[:n]))
+
+    def counts(self) -> dict:
+        w, r = C.c_int32(), C.c_int32()
+        pre, gen = C.c_int64(), C.c_int64()
+        self.pool.check(lib().slm_sched_counts(self._h, C.byref(w), C.byref(r), C.byref(pre),
+                                               C.byref(gen)))
+        return {"waiting": w.value, "running": r.value, "preemptions": pre.value,
+                "generated_tokens": gen.value}
