@@ -55,7 +55,10 @@ WORKLOADS = {
                      BF16=True),
     # continuous batching: the request trace below through the scheduler
     "serve": dict(B=512, LEN_LO=8, LEN_HI=256, LAYERS=8, HQ=4, HKV=2, D=64, CTX=512, BF16=False),
+    # prefix reuse: 64 requests, a shared 384-token prefix + 32 own tokens each
+    "prefix": dict(B=64, LEN_LO=384, LEN_HI=32, LAYERS=8, HQ=4, HKV=2, D=64, CTX=512, BF16=False),
 }
+PREFIX_DECODE_STEPS = 96
 # "serve": 4096 requests in total (shared by the ranks), Poisson arrivals at
 # SERVE_RATE requests/s (seeded), prompts U[8,256], outputs U[16,256], at
 # most 512 running per GPU, the 8M model's KV shape.
@@ -683,12 +686,117 @@ def run_serve(args):
         dist.destroy_process_group()
 
 
+def run_prefix(args):
+    """Prefix reuse: request 0 prefills the shared prefix and publishes its
+    full blocks; the other requests attach them through the block table and
+    prefill only their own suffix over the attached cache; then every request
+    decodes PREFIX_DECODE_STEPS tokens in batched steps. Reports the prefill
+    tokens the reuse saved and the decode throughput (synthetic Q/K/V: the
+    model's projections are outside this path)."""
+    import numpy as np
+    import torch
+
+    import slmkv
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    prefix_len, suffix_len = LEN_LO, LEN_HI
+    rng = np.random.default_rng(args.seed + 77)
+    prefix_ids = [int(x) for x in rng.integers(0, 8192, size=prefix_len)]
+    suffix_ids = [[int(x) for x in rng.integers(0, 8192, size=suffix_len)] for _ in range(B)]
+    total_len = prefix_len + suffix_len + PREFIX_DECODE_STEPS
+    pool = slmkv.KvPool(num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV,
+                        head_dimension=D, context_length=CTX,
+                        num_blocks=B * ((total_len + BLOCK - 1) // BLOCK) + 64, max_sequences=B,
+                        device=local)
+    pool.shuffle(args.seed + 1)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + 5)
+
+    def qkv(rows):
+        return [(torch.randn((rows, HQ, D), generator=gen, device=dev),
+                 torch.randn((rows, HKV, D), generator=gen, device=dev),
+                 torch.randn((rows, HKV, D), generator=gen, device=dev)) for _ in range(LAYERS)]
+
+    def prefill(caches, counts, inputs):
+        rows = sum(counts)
+        out = torch.empty((rows, HQ, D), device=dev)
+        with pool.begin(caches, counts) as b:
+            for l, (q, k, v) in enumerate(inputs):
+                b.append_layer(l, k, v, rotate_keys=True)
+                b.prefill_attention(l, q, out, rotate_query=True)
+
+    caches = [pool.allocate_kv_cache(total_len) for _ in range(B)]
+    stream = torch.cuda.current_stream()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    pre_in = qkv(prefix_len)
+    suf_in = qkv(suffix_len * (B - 1))
+    first_suffix = qkv(suffix_len)
+    torch.cuda.synchronize()
+    e[0].record(stream)
+    # request 0: the prefix, published, then its own suffix
+    prefill([caches[0]], [prefix_len], pre_in)
+    indexed = caches[0].publish_prefix(prefix_ids)
+    prefill([caches[0]], [suffix_len], first_suffix)
+    # the others: attach the prefix blocks, prefill only the suffix
+    reused = [c.attach_prefix(prefix_ids + suffix_ids[i]) for i, c in enumerate(caches[1:], 1)]
+    prefill(caches[1:], [suffix_len] * (B - 1), suf_in)
+    e[1].record(stream)
+    # batched decode of every request
+    dq = torch.randn((LAYERS, B, HQ, D), generator=gen, device=dev)
+    dk = torch.randn((LAYERS, B, HKV, D), generator=gen, device=dev)
+    dout = torch.empty((LAYERS, B, HQ, D), device=dev)
+    ptrs = [(dq[l].data_ptr(), dk[l].data_ptr(), dk[l].data_ptr(), dout[l].data_ptr())
+            for l in range(LAYERS)]
+    plan = pool.step_plan(caches, 1)
+    inflight = []
+    e[2].record(stream)
+    for _ in range(PREFIX_DECODE_STEPS):
+        b = plan.begin()
+        for l in range(LAYERS):
+            b.decode_layer_ptr(l, *ptrs[l])
+        inflight.append(b.submit())
+        while len(inflight) > 1:
+            if any(inflight.pop(0).wait()):
+                raise RuntimeError("decode step failed")
+    e[3].record(stream)
+    for b in inflight:
+        if any(b.wait()):
+            raise RuntimeError("decode step failed")
+    torch.cuda.synchronize()
+    lengths = [c.sequence_length() for c in caches]
+    if lengths != [total_len] * B or any(r != prefix_len for r in reused):
+        raise RuntimeError(f"unexpected lengths {set(lengths)} or reuse {set(reused)}")
+    prefill_ms, decode_ms = e[0].elapsed_time(e[1]), e[2].elapsed_time(e[3])
+    computed = prefix_len + B * suffix_len
+    without = B * (prefix_len + suffix_len)
+    tokens = B * PREFIX_DECODE_STEPS
+    result = {
+        "metric": METRIC, "value": tokens / (decode_ms / 1e3), "unit": "tok/s", "n_gpus": 1,
+        "steps": PREFIX_DECODE_STEPS, "warmup": 0, "ms_per_step": decode_ms / PREFIX_DECODE_STEPS,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": (f"prefix reuse: {B} requests share a {prefix_len}-token prefix "
+                                f"and add {suffix_len} own tokens, then {PREFIX_DECODE_STEPS} "
+                                f"decode steps each; {LAYERS} layers, Hq={HQ}, Hkv={HKV}, d={D}, "
+                                "f32 KV; synthetic Q/K/V"), "name": "prefix", "seed": args.seed},
+        "prefill_tokens_computed": computed, "prefill_tokens_without_reuse": without,
+        "prefill_tokens_saved": without - computed, "prefix_blocks_indexed": indexed,
+        "prefill_ms": prefill_ms, "gpu_launches": pool.launch_count(),
+    }
+    print(json.dumps(result), flush=True)
+    pool.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif WORKLOAD_NAME == "serve":
         run_serve(args)
+    elif WORKLOAD_NAME == "prefix":
+        run_prefix(args)
     else:
         run_ours(args)
 
