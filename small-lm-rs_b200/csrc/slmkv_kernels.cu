@@ -1004,23 +1004,29 @@ cudaError_t launch_decode_t(const StreamDecodeLaunch& p, cudaStream_t s) {
 // Append: 16 lanes per (token, kv head) row, 4 dims (two RoPE pairs) a lane,
 // 128-bit loads and stores.
 // ---------------------------------------------------------------------------
-// Sequence holding batch token `row` among seqs[lo..hi] (row offsets ascend).
-__device__ __forceinline__ int find_seq_in(const SeqEntry* seqs, int lo, int hi, int row) {
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (seqs[mid].row_offset <= row) lo = mid;
-    else hi = mid - 1;
+
+// The sequence holding batch token `tok` (the same in every lane): 32 probes a
+// round, each round narrowing the range 32-fold (two rounds up to 1024
+// sequences).
+__device__ __forceinline__ int warp_find_seq(const SeqEntry* seqs, int n, int tok, int lane) {
+  int lo = 0, len = n;
+  while (len > 1) {
+    const int step = (len + 31) >> 5;
+    const int idx = lo + lane * step;
+    const bool ok = lane * step < len && seqs[idx].row_offset <= tok;
+    const unsigned m = __ballot_sync(0xffffffffu, ok);  // lane 0 always holds (offsets ascend from 0)
+    const int hit = 31 - __clz(m);
+    lo += hit * step;
+    len = min(step, len - hit * step);
   }
   return lo;
-}
-__device__ __forceinline__ int find_seq(const SeqEntry* seqs, int n, int row) {
-  return find_seq_in(seqs, 0, n - 1, row);
 }
 
 // One CTA appends kAppendRows consecutive (token, KV head) rows: 16 lanes per
 // row, four rows per lane group, every K/V load issued before any dependent
-// work. The CTA's first and last tokens bound the sequences it touches, so
-// each row's lookup searches only that range.
+// work. Each warp finds the sequence of its first token with a lane-parallel
+// search and walks forward from it (its rows span at most a few sequences);
+// no CTA barrier.
 constexpr int kAppendRowsPerGroup = 4;
 constexpr int kAppendRows = 16 * kAppendRowsPerGroup;  // 256 threads = 16 groups of 16
 
@@ -1029,13 +1035,7 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendLaunch p) {
   const int Hkv = p.g.kv_heads;
   const int64_t n_rows = static_cast<int64_t>(p.total_tokens) * Hkv;
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kAppendRows;
-  const int grp = threadIdx.x >> 4, l16 = threadIdx.x & 15;
-  __shared__ int s_range[2];
-  if (threadIdx.x == 0) {
-    const int64_t last = min(row0 + kAppendRows, n_rows) - 1;
-    s_range[0] = find_seq(p.seqs, p.n_seq, static_cast<int>(row0 / Hkv));
-    s_range[1] = find_seq(p.seqs, p.n_seq, static_cast<int>(last / Hkv));
-  }
+  const int grp = threadIdx.x >> 4, l16 = threadIdx.x & 15, lane = threadIdx.x & 31;
   float4 kin[kAppendRowsPerGroup], vin[kAppendRowsPerGroup];
 #pragma unroll
   for (int j = 0; j < kAppendRowsPerGroup; ++j) {
@@ -1045,14 +1045,15 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendLaunch p) {
       vin[j] = reinterpret_cast<const float4*>(p.v_in + row * D)[l16];
     }
   }
-  __syncthreads();
-  const int lo = s_range[0], hi = s_range[1];
+  // this warp's first row (groups 2w, 2w+1 of 16 rows each)
+  const int64_t wrow0 = min(row0 + (grp & ~1), n_rows - 1);
+  int si = warp_find_seq(p.seqs, p.n_seq, static_cast<int>(wrow0 / Hkv), lane);
 #pragma unroll
   for (int j = 0; j < kAppendRowsPerGroup; ++j) {
     const int64_t row = row0 + j * 16 + grp;
     if (row >= n_rows) break;
     const int tok = static_cast<int>(row / Hkv), h = static_cast<int>(row - static_cast<int64_t>(tok) * Hkv);
-    const int si = find_seq_in(p.seqs, lo, hi, tok);
+    while (si + 1 < p.n_seq && p.seqs[si + 1].row_offset <= tok) ++si;  // rows ascend
     const SeqEntry se = p.seqs[si];
     const int pos = se.base + (tok - se.row_offset);
     const int32_t blk = checked_block(

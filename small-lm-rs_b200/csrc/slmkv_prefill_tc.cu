@@ -388,22 +388,30 @@ __global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constan
         if (!live) s[i] = 0.f;
       }
     }
+    {  // eight independent chains instead of one 128-long dependency chain
+      float m8[8];
 #pragma unroll
-    for (int i = 0; i < kTileN; ++i) mx = fmaxf(mx, s[i]);
+      for (int k = 0; k < 8; ++k) m8[k] = s[k];
+#pragma unroll
+      for (int i = 8; i < kTileN; ++i) m8[i & 7] = fmaxf(m8[i & 7], s[i]);
+      mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                 fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+    }
     const bool grow = mx > m_used + 8.f;
     float corr = 1.f;
     if (grow) {
       corr = ex2(m_used - mx);  // 0 on the first tile
       m_used = mx;
     }
-    float psum = 0.f;
+    float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
     uint32_t pw[kTileN / 2];
 #pragma unroll
     for (int i = 0; i < kTileN / 2; ++i) {
       const float a = ex2(s[2 * i] - m_used), b = ex2(s[2 * i + 1] - m_used);
-      psum += a + b;
+      ps8[i & 7] += a + b;
       pw[i] = bf16x2(a, b);
     }
+    const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
     l_sum = fmaf(l_sum, corr, psum);
     // ---- P·V_{j-1} done: P, O and V buffer (j-1)&1 are free ------------------
     if (j > 0) {
