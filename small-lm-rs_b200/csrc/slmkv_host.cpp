@@ -53,12 +53,21 @@ struct BlockMeta {
 };
 
 // Pinned staging (ring of two) feeding one device region.
+// Pinned staging (ring of two) feeding device memory. A single device region
+// is written on the caller's stream; a dual one (the batch descriptors) has a
+// device buffer per slot, written on the context's copy stream while the
+// previous step's kernels run, once the kernels that last read that buffer
+// are done (`consumed`), with the caller's stream waiting for the copy.
 struct Upload {
   uint8_t* h[kUploadSlots] = {nullptr, nullptr};
-  cudaEvent_t ev[kUploadSlots] = {nullptr, nullptr};
-  uint8_t* d = nullptr;
+  cudaEvent_t ev[kUploadSlots] = {nullptr, nullptr};        // copy of slot k done
+  cudaEvent_t consumed[kUploadSlots] = {nullptr, nullptr};  // kernels reading slot k done
+  uint8_t* d = nullptr;                                     // single
+  uint8_t* dd[kUploadSlots] = {nullptr, nullptr};           // dual
+  bool dual = false;
   size_t cap = 0;
-  int next = 0;
+  int next = 0, last = 0;
+  uint8_t* device() const { return dual ? dd[last] : d; }   // of the last upload
 };
 
 // Decode plan of one step, built on the host (which owns every block id).
@@ -100,6 +109,7 @@ struct slm_batch {
   int32_t n_pairs = 0, total_blocks = 0;  // decode plan (when every count is 1)
   std::vector<uint8_t> layer_done;
   StepDev dev;
+  int32_t up_slot = 0;  // descriptor slot (its `consumed` event is recorded at the end)
   // Submitted (slm_batch_submit): its status readback slot; per sequence
   // whether every layer advanced, and a rollback forced by an earlier batch
   // (poison_base >= 0: roll back to at most that length with poison_code).
@@ -147,6 +157,10 @@ struct slm_ctx {
   cudaEvent_t rb_ev[kReadbackSlots] = {};
   bool rb_busy[kReadbackSlots] = {};
   std::deque<slm_batch*> submitted;  // oldest first
+  // Batch descriptors go in on copy_stream; statuses come back on
+  // readback_stream (a readback waits for its step's kernels, and must not
+  // hold up the next step's descriptor behind it).
+  cudaStream_t copy_stream = nullptr, readback_stream = nullptr;
   Upload up_batch, up_aux;
   size_t upd_cap = 0, copy_cap = 0;
 
@@ -353,22 +367,32 @@ void rollback_reserve(slm_ctx* c, Undo& undo) {
 
 // ---- uploads ------------------------------------------------------------------
 
-slm_status upload_alloc(slm_ctx* c, Upload& u, size_t cap) {
+slm_status upload_alloc(slm_ctx* c, Upload& u, size_t cap, bool dual) {
   u.cap = cap;
+  u.dual = dual;
   for (int k = 0; k < kUploadSlots; ++k) {
     CU(c, cudaMallocHost(reinterpret_cast<void**>(&u.h[k]), cap));
     CU(c, cudaEventCreateWithFlags(&u.ev[k], cudaEventDisableTiming));
+    CU(c, cudaEventCreateWithFlags(&u.consumed[k], cudaEventDisableTiming));
+    if (dual) {
+      CU(c, cudaMalloc(reinterpret_cast<void**>(&u.dd[k]), cap));
+      c->device_bytes += static_cast<int64_t>(cap);
+    }
   }
-  CU(c, cudaMalloc(reinterpret_cast<void**>(&u.d), cap));
-  c->device_bytes += static_cast<int64_t>(cap);
+  if (!dual) {
+    CU(c, cudaMalloc(reinterpret_cast<void**>(&u.d), cap));
+    c->device_bytes += static_cast<int64_t>(cap);
+  }
   return SLM_OK;
 }
 void upload_free(Upload& u) {
   for (int k = 0; k < kUploadSlots; ++k) {
     if (u.h[k]) cudaFreeHost(u.h[k]);
     if (u.ev[k]) cudaEventDestroy(u.ev[k]);
-    u.h[k] = nullptr;
-    u.ev[k] = nullptr;
+    if (u.consumed[k]) cudaEventDestroy(u.consumed[k]);
+    if (u.dd[k]) cudaFree(u.dd[k]);
+    u.h[k] = u.dd[k] = nullptr;
+    u.ev[k] = u.consumed[k] = nullptr;
   }
   if (u.d) cudaFree(u.d);
   u.d = nullptr;
@@ -377,10 +401,21 @@ uint8_t* upload_begin(Upload& u) {
   cudaEventSynchronize(u.ev[u.next]);
   return u.h[u.next];
 }
-cudaError_t upload_end(Upload& u, size_t bytes, cudaStream_t s) {
-  cudaError_t e = cudaMemcpyAsync(u.d, u.h[u.next], bytes, cudaMemcpyHostToDevice, s);
-  if (e == cudaSuccess) e = cudaEventRecord(u.ev[u.next], s);
-  u.next = (u.next + 1) % kUploadSlots;
+cudaError_t upload_end(Upload& u, size_t bytes, cudaStream_t s, cudaStream_t copy) {
+  const int k = u.next;
+  cudaError_t e;
+  if (u.dual) {
+    e = cudaStreamWaitEvent(copy, u.consumed[k], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(u.dd[k], u.h[k], bytes, cudaMemcpyHostToDevice, copy);
+    if (e == cudaSuccess) e = cudaEventRecord(u.ev[k], copy);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, u.ev[k], 0);
+  } else {
+    e = cudaMemcpyAsync(u.d, u.h[k], bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaEventRecord(u.ev[k], s);
+  }
+  u.last = k;
+  u.next = (k + 1) % kUploadSlots;
   return e;
 }
 
@@ -413,7 +448,7 @@ slm_status flush_excess(slm_ctx* c, cudaStream_t s, size_t keep_updates, size_t 
     uint8_t* h = upload_begin(c->up_aux);
     memcpy(h + L.updates, c->pending_updates.data(), nu * sizeof(TableUpdate));
     memcpy(h + L.copies, c->pending_copies.data(), nc * sizeof(CopyJob));
-    CU(c, upload_end(c->up_aux, L.total, s));
+    CU(c, upload_end(c->up_aux, L.total, s, c->copy_stream));
     c->prev_decode_layer = -1;
     CU(c, launch_apply_updates(c->geom(), reinterpret_cast<TableUpdate*>(c->up_aux.d + L.updates),
                                static_cast<int32_t>(nu),
@@ -564,21 +599,22 @@ slm_status upload_step(slm_ctx* c, Upload& u, cudaStream_t s, const std::vector<
   if (nw) memcpy(h + L.wfp, plan->warp_start.data(), sizeof(int4) * 2 * nw);
   if (nu) memcpy(h + L.updates, c->pending_updates.data(), nu * sizeof(TableUpdate));
   if (nc) memcpy(h + L.copies, c->pending_copies.data(), nc * sizeof(CopyJob));
-  CU(c, upload_end(u, L.total, s));
+  CU(c, upload_end(u, L.total, s, c->copy_stream));
+  uint8_t* d = u.device();
   if (nu || nc) {
     c->prev_decode_layer = -1;
-    CU(c, launch_apply_updates(c->geom(), reinterpret_cast<TableUpdate*>(u.d + L.updates),
-                               static_cast<int32_t>(nu), reinterpret_cast<CopyJob*>(u.d + L.copies),
+    CU(c, launch_apply_updates(c->geom(), reinterpret_cast<TableUpdate*>(d + L.updates),
+                               static_cast<int32_t>(nu), reinterpret_cast<CopyJob*>(d + L.copies),
                                static_cast<int32_t>(nc), s));
     ++c->launches;
     if (with_table_updates) c->pending_updates.clear();
     c->pending_copies.clear();
   }
-  dev->seqs = reinterpret_cast<SeqEntry*>(u.d + L.seqs);
-  dev->status = reinterpret_cast<int32_t*>(u.d + L.status);
-  dev->pairs = reinterpret_cast<PairEntry*>(u.d + L.pairs);
-  dev->chunks = reinterpret_cast<int32_t*>(u.d + L.chunks);
-  dev->wfp = reinterpret_cast<int4*>(u.d + L.wfp);
+  dev->seqs = reinterpret_cast<SeqEntry*>(d + L.seqs);
+  dev->status = reinterpret_cast<int32_t*>(d + L.status);
+  dev->pairs = reinterpret_cast<PairEntry*>(d + L.pairs);
+  dev->chunks = reinterpret_cast<int32_t*>(d + L.chunks);
+  dev->wfp = reinterpret_cast<int4*>(d + L.wfp);
   return SLM_OK;
 }
 
@@ -695,6 +731,8 @@ void destroy_device(slm_ctx* c) {
     if (ev) cudaEventDestroy(ev);
   upload_free(c->up_batch);
   upload_free(c->up_aux);
+  if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+  if (c->readback_stream) cudaStreamDestroy(c->readback_stream);
 }
 
 template <typename T>
@@ -828,8 +866,11 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
           desc_layout(1, k.num_key_value_heads,
                       static_cast<size_t>(k.num_key_value_heads) * cp->max_blocks_per_seq,
                       cp->n_warps, cp->upd_cap, cp->copy_cap).total + 256;
-      rc = upload_alloc(cp, cp->up_batch, batch_cap);
-      if (rc == SLM_OK) rc = upload_alloc(cp, cp->up_aux, aux_cap);
+      e = cudaStreamCreateWithFlags(&cp->copy_stream, cudaStreamNonBlocking);
+      if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&cp->readback_stream, cudaStreamNonBlocking);
+      rc = (e == cudaSuccess) ? upload_alloc(cp, cp->up_batch, batch_cap, true)
+                              : cuda_fail(cp, e, "cudaStreamCreate");
+      if (rc == SLM_OK) rc = upload_alloc(cp, cp->up_aux, aux_cap, false);
     }
     if (rc == SLM_OK) {
       // Unused pool memory is zero: reads of not-yet-written slots are finite.
@@ -1257,6 +1298,7 @@ slm_status slm_batch_begin(slm_ctx* ctx, int32_t n, const int32_t* h_seq_ids,
   // The decode kernel reads the chunk stream, not the device block table, so
   // a decode step leaves pure table writes pending (copies are applied now);
   // every kernel that reads the table flushes them first.
+  b->up_slot = ctx->up_batch.next;
   rc = upload_step(ctx, ctx->up_batch, s, entries, decode ? &plan : nullptr, &b->dev,
                    /*with_table_updates=*/!decode);
   if (rc) {
@@ -1409,6 +1451,7 @@ void roll_back_seq(slm_ctx* ctx, const slm_batch* from, int32_t id, int32_t targ
 // sequence back to its begin length.
 void batch_discard(slm_batch* b) {
   slm_ctx* ctx = b->ctx;
+  if (has_device(ctx)) cudaEventRecord(ctx->up_batch.consumed[b->up_slot], b->stream);
   for (size_t i = 0; i < b->seq_ids.size(); ++i) {
     ctx->seqs[b->seq_ids[i]].in_batch = false;
     roll_back_seq(ctx, b, b->seq_ids[i], b->base[i], SLM_ERR_INVALID_INPUT);
@@ -1495,11 +1538,16 @@ slm_status submit(slm_batch* b, bool extra_slot) {
   cudaError_t e = cudaErrorNotReady;
   if (slot >= 0 && has_device(ctx)) {
     int32_t* rb = ctx->h_rb + static_cast<size_t>(slot) * (ctx->cfg.max_sequences + 2);
-    e = cudaMemcpyAsync(rb + 2, b->dev.status, sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
-                        b->stream);
+    // After the batch's kernels (which are then done with its descriptor)
+    // the statuses come back on the readback stream.
+    cudaStream_t cs = ctx->readback_stream;
+    e = cudaEventRecord(ctx->up_batch.consumed[b->up_slot], b->stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, ctx->up_batch.consumed[b->up_slot], 0);
     if (e == cudaSuccess)
-      e = cudaMemcpyAsync(rb, ctx->d_error, sizeof(int32_t), cudaMemcpyDeviceToHost, b->stream);
-    if (e == cudaSuccess) e = cudaEventRecord(ctx->rb_ev[slot], b->stream);
+      e = cudaMemcpyAsync(rb + 2, b->dev.status, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(rb, ctx->d_error, sizeof(int32_t), cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess) e = cudaEventRecord(ctx->rb_ev[slot], cs);
   }
   if (e != cudaSuccess) {
     batch_discard(b);
