@@ -616,13 +616,16 @@ def run_serve(args):
     ones = slmkv._i32_array([1] * B)
 
     def run_step():
+        # the decode batch is submitted and the prefill batch queued behind it:
+        # one wait per step
         nd, npf = sched.plan()
         dst = pst = None
+        dec = None
         if nd:
-            b = slmkv.Batch.for_sequences(pool, nd, sched._dseq, ones, stream)
+            dec = slmkv.Batch.for_sequences(pool, nd, sched._dseq, ones, stream)
             for l in range(LAYERS):
-                b.decode_layer_ptr(l, *dptr[l])
-            dst = b.end(raise_on_error=False)
+                dec.decode_layer_ptr(l, *dptr[l])
+            dec.submit()
         if npf:
             counts = list(sched._pcnt[:npf])
             rows = sum(counts)
@@ -631,6 +634,8 @@ def run_serve(args):
                 b.append_layer(l, pk[l, :rows], pk[l, :rows], rotate_keys=True)
                 b.prefill_attention(l, pq[l, :rows], pout[l, :rows], rotate_query=True)
             pst = b.end(raise_on_error=False)
+        if dec is not None:
+            dst = dec.wait(raise_on_error=False)
         return nd, npf, sched.commit(dst, pst)
 
     order = sorted(mine, key=lambda i: arrivals[i])

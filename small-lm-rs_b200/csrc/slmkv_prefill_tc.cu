@@ -4,23 +4,21 @@
 // (rust/engine/src/attention.rs:195-399) with the cache of
 // forward_prefill_with_cache (attention.rs:835-870).
 //
-// One CTA = 128 query rows of one (sequence, KV head): the G query heads of
-// the group times 128/G consecutive new tokens (row r = token r/G, head r%G),
-// so every K/V tile is shared by the whole group. Per 128-token K/V tile:
-//   S = Q K^T        tcgen05.mma kind::f16, M=128 N=128, f32 in TMEM columns
-//                    [0,128); Q rounded to bf16 after RoPE and scaling
-//   softmax          4 warps, one row per thread (TMEM lane = row), exp2
-//                    domain, causal mask; the running max moves only when a
-//                    row's max grows by more than 2^8, then O is rescaled
+// A CTA covers 256 query rows of one (sequence, KV head) as two 128-row
+// query tiles (A, B); a query tile is the G query heads of the group times
+// 128/G consecutive new tokens (row r = token r/G, head r%G), so every K/V
+// tile is shared by the whole group. Per 128-token K/V tile and query tile:
+//   S = Q K^T        tcgen05.mma kind::f16, M=128 N=128, f32 in TMEM; Q
+//                    rounded to bf16 after RoPE and scaling
+//   softmax          one warpgroup per query tile, one row per thread (TMEM
+//                    lane = row), exp2 domain, causal mask; the running max
+//                    moves only when a row's max grows by more than 2^8, then
+//                    O is rescaled in TMEM
 //   O += P V         M=128 N=64, P (bf16) from shared memory, V as an
-//                    MN-major operand, O in TMEM columns [128,192)
+//                    MN-major operand, O in TMEM
 // Q, K and V tiles are 128-byte-swizzled: K/V blocks arrive by TMA (16 rows
-// per block, block-table lookups; two tiles in flight), Q and P are written
-// by the threads in the same layout. One thread issues the MMAs and commits
-// them to mbarriers. Two CTAs share an SM (112 KiB of shared memory and 256
-// TMEM columns each), so one CTA's softmax overlaps the other's MMAs and
-// copies. Every wait is bounded; on expiry the CTA records an error, waits
-// (bounded) for its own MMAs and copies, frees TMEM and exits.
+// per block, block-table lookups), Q and P are written by the threads in the
+// same layout.
 #include <cstdint>
 
 #include "slmkv_internal.h"
@@ -30,24 +28,10 @@ namespace {
 
 constexpr int kTileM = 128;    // query rows per CTA
 constexpr int kTileN = 128;    // K/V tokens per tile (8 blocks)
-constexpr int kTmemCols = 256; // S: [0,128), O: [128,192)
-constexpr int kOCol = 128;
 constexpr int kTileBytes = kTileN * kHeadDim * 2;  // 16 KiB: 128 rows of 128 B
 constexpr float kScaleLog2Tc = 0.125f * 1.4426950408889634f;
 constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s
 constexpr int kWaitSpinsMax = 1 << 26;
-
-// Shared memory. The dynamic base is the start of the CTA's window (the
-// kernel has no static shared variables), 1024-aligned as the 128-byte
-// swizzle needs; the kernel checks it and reports an error otherwise.
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTileBytes;            // 2 buffers
-constexpr int kOffV = kOffK + 2 * kTileBytes;        // 2 buffers
-constexpr int kOffP = kOffV + 2 * kTileBytes;        // tokens 0-63, 64-127
-constexpr int kOffBar = kOffP + 2 * kTileBytes;      // k_full[2], v_full[2], s_done, o_done
-constexpr int kOffMisc = kOffBar + 6 * 8;            // TMEM base address
-constexpr int kSmemTc = kOffMisc + 16;
-static_assert(2 * (kSmemTc + 1024) <= 228 * 1024, "two prefill CTAs must fit one SM");
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -76,7 +60,7 @@ __device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: true when the phase completed, false after ~1 s.
-__device__ __noinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
   if (bar_try(bar, parity)) return true;
   const unsigned long long t0 = gtimer();
   for (int i = 0; i < kWaitSpinsMax; ++i) {
@@ -179,347 +163,478 @@ __device__ __forceinline__ uint32_t swz(int r, int u) {
   return static_cast<uint32_t>(((r >> 3) << 10) + ((r & 7) << 7) + (((u ^ r) & 7) << 4));
 }
 
+// 384 threads in three warpgroups. Warpgroups 0 and 1 each own a 128-row query
+// tile (A: the CTA's first 128/G tokens, B: the next 128/G) and run its
+// softmax; in warpgroup 2, warp 8 loads K/V tiles (3 stages each) and warp 9
+// issues the MMAs. TMEM holds S_A, S_B (128 columns each) and O_A, O_B (64
+// each), so the tensor cores compute one tile's scores while the other tile's
+// softmax runs. Every handoff is an mbarrier:
+//   k_full/v_full[s]  copies landed (TMA transaction bytes)   loader -> MMA
+//   k_free/v_free[s]  the MMAs reading the stage are done     MMA -> loader
+//   q_full[w]         Q tile w written (4 warp arrivals)      softmax -> MMA
+//   s_full[w]         S_w of the next K tile is in TMEM       MMA -> softmax
+//   s_free[w]         S_w read out of TMEM (4 arrivals)       softmax -> MMA
+//   p_full[w]         P_w in shared memory, O_w rescaled      softmax -> MMA
+//   o_done[w]         P_w V done: P_w and O_w free            MMA -> softmax
+// Each completes once per K/V tile in order, so its phase parity is the
+// tile index's low bit. Registers are rebalanced with setmaxnreg: the
+// softmax warpgroups rise to 224 (a 128-score row stays in registers), the
+// producer warpgroup drops to 56; 128 * (2 * 224 + 56) = 384 * 168, the
+// registers the CTA is launched with (checked on the host before launch).
+// A wait that runs out (1 s) sets the CTA's abort flag, which ends every
+// other wait at once; the loader then waits (bounded) for its own copies and
+// the MMA warp for its own MMAs before TMEM is released.
+constexpr int kWsThreads = 384;
+constexpr int kWsStages = 3;
+constexpr int kWsTmemCols = 512;  // S_A [0,128), S_B [128,256), O_A [256,320), O_B [320,384)
+constexpr int kWsOCol = 256;
+constexpr int kWsRegsSoftmax = 224, kWsRegsProducer = 56, kWsRegsLaunch = 168;
+static_assert(128 * (2 * kWsRegsSoftmax + kWsRegsProducer) <= kWsThreads * kWsRegsLaunch,
+              "the setmaxnreg split must fit the registers the CTA is launched with");
+static_assert(kWsRegsLaunch == (65536 / kWsThreads) / 8 * 8, "launch registers of a 384-thread CTA");
+
+constexpr int kWsOffQ = 0;                                // Q_A, Q_B
+constexpr int kWsOffK = kWsOffQ + 2 * kTileBytes;          // kWsStages buffers
+constexpr int kWsOffV = kWsOffK + kWsStages * kTileBytes;  // kWsStages buffers
+constexpr int kWsOffP = kWsOffV + kWsStages * kTileBytes;  // P_A (two tiles), P_B (two tiles)
+constexpr int kWsOffBar = kWsOffP + 4 * kTileBytes;
+enum : int {
+  kBarKFull = 0,
+  kBarVFull = kBarKFull + kWsStages,
+  kBarKFree = kBarVFull + kWsStages,
+  kBarVFree = kBarKFree + kWsStages,
+  kBarQFull = kBarVFree + kWsStages,
+  kBarSFull = kBarQFull + 2,
+  kBarSFree = kBarSFull + 2,
+  kBarPFull = kBarSFree + 2,
+  kBarODone = kBarPFull + 2,
+  kBarDrain = kBarODone + 2,
+  kWsBars
+};
+constexpr int kWsOffMisc = kWsOffBar + 8 * kWsBars;  // TMEM base, abort flag
+constexpr int kSmemWs = kWsOffMisc + 16;
+static_assert(kSmemWs <= 227 * 1024, "shared memory of one CTA");
+
+__device__ __forceinline__ void bar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Bounded wait that also gives up as soon as another role raised the abort flag.
+__device__ __forceinline__ bool bar_wait_ab(uint32_t bar, uint32_t parity, const volatile uint32_t* abort) {
+  if (bar_try(bar, parity)) return true;
+  const unsigned long long t0 = gtimer();
+  for (int i = 0; i < kWaitSpinsMax; ++i) {
+    if (bar_try(bar, parity)) return true;
+    if (*abort) return false;
+    if ((i & 255) == 255 && gtimer() - t0 > kWaitNs) return false;
+  }
+  return false;
+}
+
 template <int G>
-__global__ void __launch_bounds__(128, 2) prefill_tc_kernel(const __grid_constant__ PrefillLaunch p) {
+__global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_constant__ PrefillLaunch p) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const uint32_t sbase = su32(sm);
   if (sbase & 1023u) {  // uniform over the CTA: report instead of misreading tiles
     if (threadIdx.x == 0) atomicOr(p.g.error, kErrLayout);
     return;
   }
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int si = blockIdx.y, h = blockIdx.z;
+  constexpr int TQ = kTileM / G;  // new tokens per query tile
   const int tile = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // long tiles first
-  constexpr int TQ = kTileM / G;  // new tokens per CTA
   const SeqEntry se = p.seqs[si];
-  const int q0 = tile * TQ;
+  const int q0 = tile * 2 * TQ;
   if (q0 >= se.count) return;
-  const int nq = min(TQ, se.count - q0);
+  // Query tile w: tokens [q0 + w*TQ, +nq_w); it attends K/V tiles [0, nt_w).
+  const int nq0 = min(TQ, se.count - q0), nq1 = max(0, min(TQ, se.count - q0 - TQ));
+  const int nt0 = (se.base + q0 + nq0 - 1) / kTileN + 1;
+  const int nt1 = nq1 > 0 ? (se.base + q0 + TQ + nq1 - 1) / kTileN + 1 : 0;
+  const int n_kv = se.base + q0 + nq0 + nq1;  // keys the CTA reads
+  const int n_load = max(nt0, nt1);           // = (n_kv + 127) / 128
   const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
-  const int last_pos = se.base + q0 + nq - 1;
-  const int n_kv = last_pos + 1;
-  const int n_tiles = (n_kv + kTileN - 1) / kTileN;
 
-  const uint32_t bar_k0 = sbase + kOffBar, bar_v0 = sbase + kOffBar + 16,
-                 bar_s = sbase + kOffBar + 32, bar_o = sbase + kOffBar + 40;
-  uint32_t* misc = reinterpret_cast<uint32_t*>(sm + kOffMisc);
+  auto bar = [&](int i) { return sbase + kWsOffBar + 8u * static_cast<uint32_t>(i); };
+  uint32_t* misc = reinterpret_cast<uint32_t*>(sm + kWsOffMisc);
+  volatile uint32_t* abort_flag = misc + 1;
   if (tid == 0) {
-    bar_init(bar_k0, 1);
-    bar_init(bar_k0 + 8, 1);
-    bar_init(bar_v0, 1);
-    bar_init(bar_v0 + 8, 1);
-    bar_init(bar_s, 1);
-    bar_init(bar_o, 1);
+    for (int s = 0; s < kWsStages; ++s) {
+      bar_init(bar(kBarKFull + s), 1);
+      bar_init(bar(kBarVFull + s), 1);
+      bar_init(bar(kBarKFree + s), 1);
+      bar_init(bar(kBarVFree + s), 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      bar_init(bar(kBarQFull + w), 4);
+      bar_init(bar(kBarSFull + w), 1);
+      bar_init(bar(kBarSFree + w), 4);
+      bar_init(bar(kBarPFull + w), 4);
+      bar_init(bar(kBarODone + w), 1);
+    }
+    bar_init(bar(kBarDrain), 1);
+    *abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 0) {
+  if (warp == 9) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     sbase + kOffMisc),
-                 "r"(kTmemCols)
+                     sbase + kWsOffMisc),
+                 "r"(kWsTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-
-  // K or V tile j -> buffer j&1: its 16-token blocks through the block table,
-  // by warp 0 with one lane per block (the table lookups overlap). K tile j+2
-  // goes as soon as S_j has been read out of TMEM, V tile j+1 as soon as
-  // P·V_{j-1} is done, so copies run a tile or two ahead.
-  const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
-  const int layer_row0 = p.layer * p.g.num_blocks * Hkv;
-  const int lane = tid & 31;
-  const int n_blocks = (n_kv + kBlockTokens - 1) / kBlockTokens;
-  // Block ids of tiles [win, win+8) in warp 0's registers: blk_cur holds
-  // tiles win..win+3 (lane l: tile win + l/8, block l%8), blk_nxt the next
-  // four. The window moves at the top of an iteration, when the oldest tile
-  // still needed (V of tile j+1) has left its first half; the next four
-  // tiles' ids then load four iterations before they are needed.
-  int win = 0, blk_cur = 0, blk_nxt = 0;
-  auto fetch_window = [&](int first_tile) {
-    const int b = first_tile * (kTileN / kBlockTokens) + lane;
-    return b < n_blocks ? bt[b] : 0;
-  };
-  if (warp == 0) {
-    blk_cur = fetch_window(0);
-    blk_nxt = fetch_window(4);
-  }
-  auto advance_window = [&](int oldest) {  // warp 0
-    while (oldest >= win + 4) {
-      blk_cur = blk_nxt;
-      win += 4;
-      blk_nxt = fetch_window(win + 4);
-    }
-  };
-  auto block_of = [&](int t, int b) {  // warp 0, all lanes; win <= t < win + 8
-    const int rel = t - win;
-    const int a = __shfl_sync(0xffffffffu, blk_cur, ((rel & 3) << 3) + b);
-    const int c = __shfl_sync(0xffffffffu, blk_nxt, ((rel & 3) << 3) + b);
-    return rel < 4 ? a : c;
-  };
-  auto load_half = [&](int j, bool v) {  // warp 0, all lanes
-    const int b0 = j * (kTileN / kBlockTokens);
-    const int nb = min(kTileN / kBlockTokens, n_blocks - b0);
-    const uint32_t bar = (v ? bar_v0 : bar_k0) + 8 * (j & 1);
-    int32_t blk = block_of(j, lane & 7);
-    if (lane == 0) bar_expect_tx(bar, static_cast<uint32_t>(nb) * kBlockTokens * kHeadDim * 2);
-    __syncwarp();
-    if (lane < nb) {
-      if (static_cast<uint32_t>(blk) >= static_cast<uint32_t>(p.g.num_blocks)) {
-        atomicOr(p.g.error, kErrBadBlock);
-        blk = 0;
-      }
-      const int y = (layer_row0 + blk * Hkv + h) * kBlockTokens;
-      const uint32_t off = static_cast<uint32_t>((j & 1) * kTileBytes + lane * kBlockTokens * 128);
-      tma_rows(sbase + (v ? kOffV : kOffK) + off, v ? &p.tmap_v : &p.tmap_k, y, bar);
-    }
-    __syncwarp();
-  };
-
-  // Q rows: RoPE at the token's position, scaled into the exp2 domain, bf16
-  // (hi, lo); rows past the CTA's tokens are zero.
-  const int r = tid;  // this thread's row (TMEM lane)
-  const int tq = r / G, gq = r % G;
-  const int qpos = se.base + q0 + tq;
-  {
-    uint8_t* qt = sm + kOffQ;
-    const bool live = tq < nq;
-    const float2* src = reinterpret_cast<const float2*>(
-        p.q + (static_cast<size_t>(se.row_offset + q0 + (live ? tq : 0)) * Hq + h * G + gq) *
-                  kHeadDim);
-    const float2* cs = p.g.rope + static_cast<size_t>(live ? qpos : 0) * (kHeadDim / 2);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      uint32_t hw[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float2 x = live ? src[4 * u + k] : make_float2(0.f, 0.f);
-        if (live && p.rotate) {
-          const float2 c = cs[4 * u + k];
-          x = make_float2(__fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, c.y)),
-                          __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x)));
-        }
-        x.x *= kScaleLog2Tc;
-        x.y *= kScaleLog2Tc;
-        hw[k] = bf16x2(x.x, x.y);
-      }
-      *reinterpret_cast<uint4*>(qt + swz(r, u)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    }
-  }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc[0];
-  const uint32_t tmem_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  constexpr uint32_t kIdQK = idesc(kTileM, kTileN, false);
-  constexpr uint32_t kIdPV = idesc(kTileM, kHeadDim, true);
-  // Progress (thread 0's view), for draining on an error: K and V tiles
-  // whose copies were issued / seen landed, S and P·V products issued / seen.
-  int k_issued = 0, k_seen = 0, v_issued = 0, v_seen = 0, s_issued = 0, s_seen = 0,
-      o_issued = 0, o_seen = 0;
-  // A failed wait sets this thread's flag; the CTA decides at its barriers
-  // with __syncthreads_or, so every thread takes the same branch.
-  bool fail = false;
-  auto issue_s = [&](int j) {  // thread 0: S_j = Q K_j^T once K_j landed
-    if (!bar_wait(bar_k0 + 8 * (j & 1), (j >> 1) & 1)) {
-      fail = true;
-      return;
+  // One lane of a warp reports a failed (warp-uniform) wait.
+  auto raise_abort = [&]() {
+    if (lane == 0) {
+      *abort_flag = 1u;
+      atomicOr(p.g.error, kErrTimeout);
     }
-    k_seen = j + 1;
-    tc_fence_after();
-    const uint32_t kaddr = sbase + kOffK + (j & 1) * kTileBytes;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
-      mma_f16(tmem, sdesc(sbase + kOffQ + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64), kIdQK,
-              kk > 0);
-    mma_commit(bar_s);
-    s_issued = j + 1;
   };
-  if (warp == 0) {
-    for (int t = 0; t < min(n_tiles, 2); ++t) {
-      load_half(t, false);
-      load_half(t, true);
-    }
-    k_issued = v_issued = min(n_tiles, 2);
-    if (lane == 0) issue_s(0);
-  }
+  auto wait_warp = [&](uint32_t b, uint32_t parity) {
+    const bool ok = bar_wait_ab(b, parity, abort_flag);
+    return __all_sync(0xffffffffu, ok);
+  };
 
-  float m_used = -INFINITY, l_sum = 0.f;
-  bool aborted = false;
-  for (int j = 0; j < n_tiles; ++j) {
-    const int buf = j & 1;
-    const uint32_t vaddr = sbase + kOffV + buf * kTileBytes;
-    if (warp == 0) advance_window(j + 1);
-    // ---- S_j out of TMEM into registers ----------------------------------------
-    if (!bar_wait(bar_s, j & 1)) fail = true;
-    else if (tid == 0) s_seen = j + 1;
-    tc_fence_after();
-    float s[kTileN];
+  if (warp < 8) {
+    // ================= softmax warpgroups =================
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWsRegsSoftmax));
+    const int w = warp >> 2;
+    const int r = tid & 127;  // this thread's row = TMEM lane
+    const int qw0 = q0 + w * TQ, nqw = w ? nq1 : nq0, ntw = w ? nt1 : nt0;
+    const int tq = r / G, gq = r % G;
+    const bool live = tq < nqw;
+    const int qpos = se.base + qw0 + tq;
+    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t s_col = static_cast<uint32_t>(w * kTileN), o_col = kWsOCol + w * kHeadDim;
+    if (ntw > 0) {
+      // Q rows: RoPE at the token's position, scaled into the exp2 domain,
+      // bf16; rows past the tile's tokens are zero.
+      uint8_t* qt = sm + kWsOffQ + w * kTileBytes;
+      const float2* src = reinterpret_cast<const float2*>(
+          p.q + (static_cast<size_t>(se.row_offset + qw0 + (live ? tq : 0)) * Hq + h * G + gq) *
+                    kHeadDim);
+      const float2* cs = p.g.rope + static_cast<size_t>(live ? qpos : 0) * (kHeadDim / 2);
 #pragma unroll
-    for (int c = 0; c < kTileN / 32; ++c) {
-      float v[32];
-      tmem_ld32(tmem_row + 32 * c, v);
+      for (int u = 0; u < 8; ++u) {
+        uint32_t hw[4];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) s[32 * c + i] = v[i];
-    }
-    tmem_wait_ld();
-    tc_fence_before();
-    aborted = __syncthreads_or(fail) != 0;
-    tc_fence_after();
-    if (aborted) break;
-    // S columns and K buffer j&1 are free: the next copy and product start now.
-    if (warp == 0) {
-      if (j + 2 < n_tiles) {
-        load_half(j + 2, false);
-        k_issued = j + 3;
+        for (int k = 0; k < 4; ++k) {
+          float2 x = live ? src[4 * u + k] : make_float2(0.f, 0.f);
+          if (live && p.rotate) {
+            const float2 c = cs[4 * u + k];
+            x = make_float2(__fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, c.y)),
+                            __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x)));
+          }
+          hw[k] = bf16x2(x.x * kScaleLog2Tc, x.y * kScaleLog2Tc);
+        }
+        *reinterpret_cast<uint4*>(qt + swz(r, u)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
       }
-      if (lane == 0 && j + 1 < n_tiles) issue_s(j + 1);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) bar_arrive(bar(kBarQFull + w));
     }
-    // ---- softmax of this thread's row ---------------------------------------
-    const bool live = tq < nq;
-    const int kp0 = j * kTileN;
-    float mx = -INFINITY;
-    // causal (attention.rs:207): key position <= query position. Only tiles
-    // reaching past the CTA's first query position need the mask (the same
-    // decision in every thread); rows past the CTA's tokens read zeros.
-    if (kp0 + kTileN - 1 > se.base + q0 || !live) {
-#pragma unroll
-      for (int i = 0; i < kTileN; ++i) {
-        if (live && kp0 + i > qpos) s[i] = -INFINITY;
-        if (!live) s[i] = 0.f;
+    float m_used = -INFINITY, l_sum = 0.f;
+    bool ok = true;  // warp-uniform
+    uint8_t* prow = sm + kWsOffP + w * 2 * kTileBytes;
+    for (int j = 0; j < ntw; ++j) {
+      // ---- S_j out of TMEM; the columns go back to the MMA warp at once ----
+      if (!wait_warp(bar(kBarSFull + w), j & 1)) {
+        ok = false;
+        break;
       }
-    }
-    {  // eight independent chains instead of one 128-long dependency chain
-      float m8[8];
+      tc_fence_after();
+      float s[kTileN];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m8[k] = s[k];
+      for (int c = 0; c < kTileN / 32; ++c) {
+        float v[32];
+        tmem_ld32(trow + s_col + 32 * c, v);
 #pragma unroll
-      for (int i = 8; i < kTileN; ++i) m8[i & 7] = fmaxf(m8[i & 7], s[i]);
-      mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                 fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-    }
-    const bool grow = mx > m_used + 8.f;
-    float corr = 1.f;
-    if (grow) {
-      corr = ex2(m_used - mx);  // 0 on the first tile
-      m_used = mx;
-    }
-    float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
-    uint32_t pw[kTileN / 2];
+        for (int i = 0; i < 32; ++i) s[32 * c + i] = v[i];
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(bar(kBarSFree + w));
+      // ---- softmax of this thread's row ---------------------------------------
+      const int kp0 = j * kTileN;
+      // causal (attention.rs:207): key position <= query position. Only tiles
+      // reaching past the tile's first query position need the mask; rows
+      // past the tile's tokens read zeros.
+      if (kp0 + kTileN - 1 > se.base + qw0 || !live) {
 #pragma unroll
-    for (int i = 0; i < kTileN / 2; ++i) {
-      const float a = ex2(s[2 * i] - m_used), b = ex2(s[2 * i + 1] - m_used);
-      ps8[i & 7] += a + b;
-      pw[i] = bf16x2(a, b);
+        for (int i = 0; i < kTileN; ++i) {
+          if (live && kp0 + i > qpos) s[i] = -INFINITY;
+          if (!live) s[i] = 0.f;
+        }
+      }
+      float mx;
+      {  // eight independent chains instead of one 128-long dependency chain
+        float m8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = s[k];
+#pragma unroll
+        for (int i = 8; i < kTileN; ++i) m8[i & 7] = fmaxf(m8[i & 7], s[i]);
+        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      }
+      // The running max moves only when the row's max grows by more than 2^8.
+      const bool grow = mx > m_used + 8.f;
+      float corr = 1.f;
+      if (grow) {
+        corr = ex2(m_used - mx);  // 0 on the first tile
+        m_used = mx;
+      }
+      // ---- P_{j-1} V done: P_w and O_w are free ---------------------------------
+      // (waited before the exponentials so that P goes to shared memory as it
+      // is made, instead of 64 more registers a thread)
+      if (j > 0) {
+        if (!wait_warp(bar(kBarODone + w), (j - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // tcgen05.ld/st are warp-collective: a warp rescales O when any of its
+        // rows moved its max; the other rows scale by 1.
+        if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+          for (int c = 0; c < kHeadDim / 32; ++c) {
+            float v[32];
+            tmem_ld32(trow + o_col + 32 * c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= corr;
+            tmem_st32(trow + o_col + 32 * c, v);
+          }
+          tmem_wait_st();
+        }
+      }
+      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
+#pragma unroll
+      for (int u = 0; u < kTileN / 8; ++u) {  // tokens 0-63 in the first P tile, 64-127 in the second
+        uint32_t pw[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int i = 8 * u + 2 * k;
+          const float a = ex2(s[i] - m_used), b = ex2(s[i + 1] - m_used);
+          ps8[(4 * u + k) & 7] += a + b;
+          pw[k] = bf16x2(a, b);
+        }
+        *reinterpret_cast<uint4*>(prow + (u >> 3) * kTileBytes + swz(r, u & 7)) =
+            make_uint4(pw[0], pw[1], pw[2], pw[3]);
+      }
+      const float psum =
+          ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+      l_sum = fmaf(l_sum, corr, psum);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(bar(kBarPFull + w));
     }
-    const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
-    l_sum = fmaf(l_sum, corr, psum);
-    // ---- P·V_{j-1} done: P, O and V buffer (j-1)&1 are free ------------------
-    if (j > 0) {
-      const bool o_ok = bar_wait(bar_o, (j - 1) & 1);
-      if (!o_ok) fail = true;
-      if (warp == 0 && __all_sync(0xffffffffu, o_ok)) {
-        o_seen = j;
-        if (j + 1 < n_tiles) {
-          load_half(j + 1, true);
-          v_issued = j + 2;
+    // ---- epilogue: O / l to the output rows ------------------------------------
+    if (ok && ntw > 0) {
+      if (!wait_warp(bar(kBarODone + w), (ntw - 1) & 1)) {
+        ok = false;
+      } else {
+        tc_fence_after();
+        // every lane loads (warp-collective); live rows store
+        const float inv = 1.f / l_sum;
+        float* dst = p.out + (static_cast<size_t>(se.row_offset + qw0 + (live ? tq : 0)) * Hq +
+                              h * G + gq) * kHeadDim;
+#pragma unroll
+        for (int c = 0; c < kHeadDim / 32; ++c) {
+          float v[32];
+          tmem_ld32(trow + o_col + 32 * c, v);
+          tmem_wait_ld();
+          if (live) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(dst + 32 * c + i) =
+                  make_float4(v[i] * inv, v[i + 1] * inv, v[i + 2] * inv, v[i + 3] * inv);
+          }
         }
       }
     }
-    tc_fence_after();
-    // tcgen05.ld/st are warp-collective (.sync.aligned): a warp rescales O
-    // when any of its rows moved its max; the other rows scale by 1.
-    if (j > 0 && __any_sync(0xffffffffu, grow)) {
-#pragma unroll
-      for (int c = 0; c < kHeadDim / 32; ++c) {
-        float v[32];
-        tmem_ld32(tmem_row + kOCol + 32 * c, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= corr;
-        tmem_st32(tmem_row + kOCol + 32 * c, v);
+    if (!ok) raise_abort();
+  } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWsRegsProducer));
+    const int n_blocks = (n_kv + kBlockTokens - 1) / kBlockTokens;
+    if (warp == 8) {
+      // ================= loader =================
+      // K and V tile t -> stage t % 3: its 16-token blocks through the block
+      // table, one lane per block. Block ids of tiles [win, win+8) sit in
+      // registers (blk_cur: tiles win..win+3, lane l -> tile win + l/8, block
+      // l%8; blk_nxt: the next four), loaded four tiles before they are needed.
+      const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
+      const int layer_row0 = p.layer * p.g.num_blocks * Hkv;
+      auto fetch_window = [&](int first_tile) {
+        const int b = first_tile * (kTileN / kBlockTokens) + lane;
+        return b < n_blocks ? bt[b] : 0;
+      };
+      int win = 0;
+      int blk_cur = fetch_window(0), blk_nxt = fetch_window(4);
+      int k_issued = 0, v_issued = 0;
+      bool ok = true;
+      for (int t = 0; t < n_load; ++t) {
+        const int st = t % kWsStages;
+        while (t >= win + 4) {
+          blk_cur = blk_nxt;
+          win += 4;
+          blk_nxt = fetch_window(win + 4);
+        }
+        const int rel = t - win, sl = ((rel & 3) << 3) + (lane & 7);
+        const int a = __shfl_sync(0xffffffffu, blk_cur, sl), c = __shfl_sync(0xffffffffu, blk_nxt, sl);
+        int32_t blk = rel < 4 ? a : c;
+        const int nb = min(kTileN / kBlockTokens, n_blocks - t * (kTileN / kBlockTokens));
+        if (static_cast<uint32_t>(blk) >= static_cast<uint32_t>(p.g.num_blocks)) {
+          if (lane < nb) atomicOr(p.g.error, kErrBadBlock);
+          blk = 0;
+        }
+        const int y = (layer_row0 + blk * Hkv + h) * kBlockTokens;
+        const uint32_t off = static_cast<uint32_t>(st * kTileBytes + lane * kBlockTokens * 128);
+        const uint32_t bytes = static_cast<uint32_t>(nb) * kBlockTokens * kHeadDim * 2;
+        const uint32_t free_parity = static_cast<uint32_t>((t / kWsStages - 1) & 1);
+        if (t >= kWsStages && !wait_warp(bar(kBarKFree + st), free_parity)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) bar_expect_tx(bar(kBarKFull + st), bytes);
+        __syncwarp();
+        if (lane < nb) tma_rows(sbase + kWsOffK + off, &p.tmap_k, y, bar(kBarKFull + st));
+        __syncwarp();
+        k_issued = t + 1;
+        if (t >= kWsStages && !wait_warp(bar(kBarVFree + st), free_parity)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) bar_expect_tx(bar(kBarVFull + st), bytes);
+        __syncwarp();
+        if (lane < nb) tma_rows(sbase + kWsOffV + off, &p.tmap_v, y, bar(kBarVFull + st));
+        __syncwarp();
+        v_issued = t + 1;
       }
-      tmem_wait_st();
-    }
-    uint8_t* prow = sm + kOffP;
+      if (!ok) raise_abort();
+      // Every copy this warp issued lands before the CTA's shared memory is
+      // released, also when another role gave up and left it unread (a copy
+      // the MMA warp consumed has completed its phase: no wait).
+      for (int t = max(0, k_issued - kWsStages); t < k_issued; ++t)
+        bar_wait(bar(kBarKFull + t % kWsStages), (t / kWsStages) & 1);
+      for (int t = max(0, v_issued - kWsStages); t < v_issued; ++t)
+        bar_wait(bar(kBarVFull + t % kWsStages), (t / kWsStages) & 1);
+      __syncwarp();
+    } else if (warp == 9) {
+      // ================= MMA issue (lane 0; the warp waits together) =================
+      constexpr uint32_t kIdQK = idesc(kTileM, kTileN, false);
+      constexpr uint32_t kIdPV = idesc(kTileM, kHeadDim, true);
+      auto issue_s = [&](int w, int t) {  // S_w = Q_w K_t^T
+        if (lane == 0) {
+          const uint32_t kaddr = sbase + kWsOffK + (t % kWsStages) * kTileBytes;
+          const uint32_t qaddr = sbase + kWsOffQ + w * kTileBytes;
 #pragma unroll
-    for (int u = 0; u < kTileN / 8; ++u)  // tokens 0-63 in the first P tile, 64-127 in the second
-      *reinterpret_cast<uint4*>(prow + (u >> 3) * kTileBytes + swz(r, u & 7)) =
-          make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
-    const int valid = min(kTileN, n_kv - kp0);
-    if (valid < kTileN) {
-      // The last tile: P = 0 past the cache, but 0 times a non-finite stale
-      // value is not 0. Clear those V rows once the tile landed.
-      if (!bar_wait(bar_v0 + 8 * buf, (j >> 1) & 1)) fail = true;
-      uint8_t* vt = sm + kOffV + buf * kTileBytes;
-      // row t of a swizzled tile is the 128 bytes at t*128 (units permuted)
-      for (int i = valid * 8 + tid; i < kTileN * 8; i += 128)
-        *reinterpret_cast<uint4*>(vt + (i >> 3) * 128 + (i & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    tc_fence_before();
-    aborted = __syncthreads_or(fail) != 0;
-    tc_fence_after();
-    if (aborted) break;
-    // ---- O += P V ----------------------------------------------------------------
-    if (tid == 0) {
-      if (bar_wait(bar_v0 + 8 * buf, (j >> 1) & 1)) {
-        v_seen = j + 1;
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16(tmem + w * kTileN, sdesc(qaddr + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64),
+                    kIdQK, kk > 0);
+          mma_commit(bar(kBarSFull + w));
+        }
+      };
+      auto issue_pv = [&](int w, int t) {  // O_w += P_w V_t
+        if (lane == 0) {
+          const uint32_t vaddr = sbase + kWsOffV + (t % kWsStages) * kTileBytes;
+          const uint32_t paddr = sbase + kWsOffP + w * 2 * kTileBytes;
+#pragma unroll
+          for (int kk = 0; kk < kTileN / 16; ++kk)
+            mma_f16(tmem + kWsOCol + w * kHeadDim,
+                    sdesc(paddr + (kk >> 2) * kTileBytes + 32 * (kk & 3), 1, 64),
+                    sdesc(vaddr + 2048 * kk, kTileBytes >> 4, 64), kIdPV, (t > 0 || kk > 0) ? 1 : 0);
+          mma_commit(bar(kBarODone + w));
+        }
+      };
+      auto commit_to = [&](int b) {
+        if (lane == 0) mma_commit(bar(b));
+      };
+      // V_t landed; on the last tile, rows past the cache are cleared: P is 0
+      // there, but 0 times a non-finite stale value is not 0.
+      auto v_ready = [&](int t) {
+        if (!wait_warp(bar(kBarVFull + t % kWsStages), (t / kWsStages) & 1)) return false;
+        const int valid = n_kv - t * kTileN;
+        if (valid < kTileN) {
+          uint8_t* vt = sm + kWsOffV + (t % kWsStages) * kTileBytes;
+          // row t of a swizzled tile is the 128 bytes at t*128 (units permuted)
+          for (int i = valid * 8 + lane; i < kTileN * 8; i += 32)
+            *reinterpret_cast<uint4*>(vt + (i >> 3) * 128 + (i & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+        }
+        return true;
+      };
+      bool ok = wait_warp(bar(kBarQFull + 0), 0) && (nt1 == 0 || wait_warp(bar(kBarQFull + 1), 0)) &&
+                wait_warp(bar(kBarKFull + 0), 0);
+      if (ok) {
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kTileN / 16; ++kk)
-          mma_f16(tmem + kOCol,
-                  sdesc(sbase + kOffP + (kk >> 2) * kTileBytes + 32 * (kk & 3), 1, 64),
-                  sdesc(vaddr + 2048 * kk, kTileBytes >> 4, 64), kIdPV, (j > 0 || kk > 0) ? 1 : 0);
-        mma_commit(bar_o);
-        o_issued = j + 1;
-      } else {
-        fail = true;
+        issue_s(0, 0);
+        if (nt1 > 0) issue_s(1, 0);
+        commit_to(kBarKFree + 0);
       }
-    }
-  }
-
-  // ---- epilogue: O / l to the output rows --------------------------------------
-  tc_fence_before();
-  aborted = __syncthreads_or(fail) != 0;
-  tc_fence_after();
-  if (!aborted) {
-    if (!bar_wait(bar_o, (n_tiles - 1) & 1)) fail = true;
-    else if (tid == 0) o_seen = n_tiles;
-  }
-  tc_fence_before();
-  const bool abort = __syncthreads_or(fail) != 0;  // the same in every thread
-  tc_fence_after();
-  if (!abort) {
-    // every thread of the warp loads (warp-collective); live rows store
-    const float inv = 1.f / l_sum;
-    float* dst = p.out + (static_cast<size_t>(se.row_offset + q0 + (tq < nq ? tq : 0)) * Hq + h * G +
-                          gq) * kHeadDim;
-#pragma unroll
-    for (int c = 0; c < kHeadDim / 32; ++c) {
-      float v[32];
-      tmem_ld32(tmem_row + kOCol + 32 * c, v);
-      tmem_wait_ld();
-      if (tq < nq) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(dst + 32 * c + i) =
-              make_float4(v[i] * inv, v[i + 1] * inv, v[i + 2] * inv, v[i + 3] * inv);
+      for (int j = 0; ok && j < n_load; ++j) {
+        const int nx = j + 1;
+        if (nx < n_load) {
+          if (!wait_warp(bar(kBarKFull + nx % kWsStages), (nx / kWsStages) & 1)) {
+            ok = false;
+            break;
+          }
+          if (nx < nt0) {
+            if (!wait_warp(bar(kBarSFree + 0), j & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(0, nx);
+          }
+        }
+        bool have_v = false;
+        if (j < nt0) {
+          if (!wait_warp(bar(kBarPFull + 0), j & 1) || !v_ready(j)) {
+            ok = false;
+            break;
+          }
+          have_v = true;
+          tc_fence_after();
+          issue_pv(0, j);
+        }
+        if (nx < n_load) {
+          if (nx < nt1) {
+            if (!wait_warp(bar(kBarSFree + 1), j & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(1, nx);
+          }
+          commit_to(kBarKFree + nx % kWsStages);
+        }
+        if (j < nt1) {
+          if (!wait_warp(bar(kBarPFull + 1), j & 1) || (!have_v && !v_ready(j))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(1, j);
+        }
+        commit_to(kBarVFree + j % kWsStages);
       }
+      if (!ok) raise_abort();
+      // every MMA this warp issued completes before TMEM is released
+      commit_to(kBarDrain);
+      bar_wait(bar(kBarDrain), 0);
+      __syncwarp();
     }
-  } else if (tid == 0) {
-    atomicOr(p.g.error, kErrTimeout);
-    // Let this CTA's own MMAs and copies land (bounded) before its TMEM and
-    // shared memory are released.
-    if (s_issued > s_seen) bar_wait(bar_s, (s_issued - 1) & 1);
-    if (o_issued > o_seen) bar_wait(bar_o, (o_issued - 1) & 1);
-    for (int t = k_seen; t < k_issued; ++t) bar_wait(bar_k0 + 8 * (t & 1), (t >> 1) & 1);
-    for (int t = v_seen; t < v_issued; ++t) bar_wait(bar_v0 + 8 * (t & 1), (t >> 1) & 1);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+  if (warp == 9)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kWsTmemCols)
                  : "memory");
 }
 
@@ -533,7 +648,7 @@ bool prefill_tc_supported(const PrefillLaunch& p) {
 cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s) {
   if (p.n_seq <= 0 || p.max_count <= 0) return cudaSuccess;
   const int G = p.g.q_heads / p.g.kv_heads;
-  const int tq = kTileM / G;
+  const int tq = 2 * (kTileM / G);  // two query tiles per CTA
   const dim3 grid((p.max_count + tq - 1) / tq, p.n_seq, p.g.kv_heads);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -541,19 +656,24 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s) {
   static unsigned long long configured[4] = {};  // per G variant, one bit per device
   auto run = [&](auto kernel, int gi) {
     if (dev < 64 && !(configured[gi] & (1ull << dev))) {
-      const cudaError_t a =
-          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+      // setmaxnreg.inc waits until the CTA's launch registers cover the
+      // split; a build that launched with fewer would never get them.
+      cudaFuncAttributes fa{};
+      cudaError_t a = cudaFuncGetAttributes(&fa, kernel);
+      if (a != cudaSuccess) return a;
+      if (fa.numRegs < kWsRegsLaunch) return cudaErrorInvalidConfiguration;
+      a = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemWs);
       if (a != cudaSuccess) return a;
       configured[gi] |= (1ull << dev);
     }
-    kernel<<<grid, 128, kSmemTc, s>>>(p);
+    kernel<<<grid, kWsThreads, kSmemWs, s>>>(p);
     return cudaGetLastError();
   };
   switch (G) {
-    case 1: return run(prefill_tc_kernel<1>, 0);
-    case 2: return run(prefill_tc_kernel<2>, 1);
-    case 4: return run(prefill_tc_kernel<4>, 2);
-    case 8: return run(prefill_tc_kernel<8>, 3);
+    case 1: return run(prefill_ws_kernel<1>, 0);
+    case 2: return run(prefill_ws_kernel<2>, 1);
+    case 4: return run(prefill_ws_kernel<4>, 2);
+    case 8: return run(prefill_ws_kernel<8>, 3);
     default: return cudaErrorInvalidValue;
   }
 }
