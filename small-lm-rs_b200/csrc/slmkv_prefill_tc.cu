@@ -14,11 +14,11 @@
 //                    lane = row), exp2 domain, causal mask; the running max
 //                    moves only when a row's max grows by more than 2^8, then
 //                    O is rescaled in TMEM
-//   O += P V         M=128 N=64, P (bf16) from shared memory, V as an
-//                    MN-major operand, O in TMEM
+//   O += P V         M=128 N=64, P (bf16) from TMEM, V as an MN-major
+//                    operand from shared memory, O in TMEM
 // Q, K and V tiles are 128-byte-swizzled: K/V blocks arrive by TMA (16 rows
-// per block, block-table lookups), Q and P are written by the threads in the
-// same layout.
+// per block, block-table lookups), Q is written by the threads in the same
+// layout.
 #include <cstdint>
 
 #include "slmkv_internal.h"
@@ -97,6 +97,17 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b,
       "l"(a), "l"(b), "r"(id), "r"(accumulate)
       : "memory");
 }
+// The same with A read from TMEM (M rows in lanes, K along columns, two bf16
+// per 32-bit column, the lower k in the low half).
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t id,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(id), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    bar)
@@ -141,6 +152,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
       : "memory");
 }
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]),
+      "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]),
+      "r"(v[30]), "r"(v[31])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -174,7 +197,7 @@ __device__ __forceinline__ uint32_t swz(int r, int u) {
 //   q_full[w]         Q tile w written (4 warp arrivals)      softmax -> MMA
 //   s_full[w]         S_w of the next K tile is in TMEM       MMA -> softmax
 //   s_free[w]         S_w read out of TMEM (4 arrivals)       softmax -> MMA
-//   p_full[w]         P_w in shared memory, O_w rescaled      softmax -> MMA
+//   p_full[w]         P_w in TMEM, O_w rescaled               softmax -> MMA
 //   o_done[w]         P_w V done: P_w and O_w free            MMA -> softmax
 // Each completes once per K/V tile in order, so its phase parity is the
 // tile index's low bit. Registers are rebalanced with setmaxnreg: the
@@ -186,8 +209,11 @@ __device__ __forceinline__ uint32_t swz(int r, int u) {
 // the MMA warp for its own MMAs before TMEM is released.
 constexpr int kWsThreads = 384;
 constexpr int kWsStages = 3;
-constexpr int kWsTmemCols = 512;  // S_A [0,128), S_B [128,256), O_A [256,320), O_B [320,384)
+// TMEM columns: S_A [0,128), S_B [128,256), O_A [256,320), O_B [320,384),
+// P_A [384,448), P_B [448,512) (P: 128 bf16 a row, two a column)
+constexpr int kWsTmemCols = 512;
 constexpr int kWsOCol = 256;
+constexpr int kWsPCol = 384;
 constexpr int kWsRegsSoftmax = 224, kWsRegsProducer = 56, kWsRegsLaunch = 168;
 static_assert(128 * (2 * kWsRegsSoftmax + kWsRegsProducer) <= kWsThreads * kWsRegsLaunch,
               "the setmaxnreg split must fit the registers the CTA is launched with");
@@ -196,8 +222,7 @@ static_assert(kWsRegsLaunch == (65536 / kWsThreads) / 8 * 8, "launch registers o
 constexpr int kWsOffQ = 0;                                // Q_A, Q_B
 constexpr int kWsOffK = kWsOffQ + 2 * kTileBytes;          // kWsStages buffers
 constexpr int kWsOffV = kWsOffK + kWsStages * kTileBytes;  // kWsStages buffers
-constexpr int kWsOffP = kWsOffV + kWsStages * kTileBytes;  // P_A (two tiles), P_B (two tiles)
-constexpr int kWsOffBar = kWsOffP + 4 * kTileBytes;
+constexpr int kWsOffBar = kWsOffV + kWsStages * kTileBytes;
 enum : int {
   kBarKFull = 0,
   kBarVFull = kBarKFull + kWsStages,
@@ -218,16 +243,71 @@ static_assert(kSmemWs <= 227 * 1024, "shared memory of one CTA");
 __device__ __forceinline__ void bar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-// Bounded wait that also gives up as soon as another role raised the abort flag.
-__device__ __forceinline__ bool bar_wait_ab(uint32_t bar, uint32_t parity, const volatile uint32_t* abort) {
+__device__ __forceinline__ uint32_t ld_volatile_shared(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_volatile_shared(uint32_t addr, uint32_t v) {
+  asm volatile("st.volatile.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+// The value, hidden from the optimizer: addresses derived from it inside a
+// loop are recomputed there instead of being kept in registers across the
+// loop (the producer warps run with 56 registers).
+__device__ __forceinline__ uint32_t opaque(uint32_t x) {
+  asm volatile("" : "+r"(x));
+  return x;
+}
+// Bounded wait that also gives up as soon as another role raised the abort
+// flag (a shared-memory word at abort_addr).
+__device__ __forceinline__ bool bar_wait_ab(uint32_t bar, uint32_t parity, uint32_t abort_addr) {
   if (bar_try(bar, parity)) return true;
   const unsigned long long t0 = gtimer();
   for (int i = 0; i < kWaitSpinsMax; ++i) {
     if (bar_try(bar, parity)) return true;
-    if (*abort) return false;
+    if (ld_volatile_shared(abort_addr)) return false;
     if ((i & 255) == 255 && gtimer() - t0 > kWaitNs) return false;
   }
   return false;
+}
+
+// The CTA's share of the launch, derived from the block indices. Each role
+// derives it again after its setmaxnreg (the special-register reads are
+// volatile and the sequence entry is loaded again), so that nothing but the
+// shared-memory base stays live across the register reallocation, which
+// would otherwise move such values through local memory.
+struct CtaWork {
+  SeqEntry se;
+  int h, q0;
+  int nq0, nq1;  // query tile w: tokens [q0 + w*TQ, +nq_w)
+  int nt0, nt1;  // ... attends K/V tiles [0, nt_w)
+  int n_kv;      // keys the CTA reads
+  int n_load;    // K/V tiles the CTA loads: max(nt0, nt1) = (n_kv + 127) / 128
+};
+__device__ __forceinline__ int thread_index() {
+  uint32_t t;
+  asm volatile("mov.u32 %0, %%tid.x;" : "=r"(t));
+  return static_cast<int>(t);
+}
+template <int G>
+__device__ __forceinline__ CtaWork cta_work(const PrefillLaunch& p) {
+  uint32_t bx, by, bz, nbx;
+  asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(bx));
+  asm volatile("mov.u32 %0, %%ctaid.y;" : "=r"(by));
+  asm volatile("mov.u32 %0, %%ctaid.z;" : "=r"(bz));
+  asm volatile("mov.u32 %0, %%nctaid.x;" : "=r"(nbx));
+  constexpr int TQ = kTileM / G;
+  CtaWork c;
+  c.se = p.seqs[by];
+  c.h = static_cast<int>(bz);
+  c.q0 = (static_cast<int>(nbx) - 1 - static_cast<int>(bx)) * 2 * TQ;  // long tiles first
+  c.nq0 = min(TQ, c.se.count - c.q0);
+  c.nq1 = max(0, min(TQ, c.se.count - c.q0 - TQ));
+  c.nt0 = (c.se.base + c.q0 + c.nq0 - 1) / kTileN + 1;
+  c.nt1 = c.nq1 > 0 ? (c.se.base + c.q0 + TQ + c.nq1 - 1) / kTileN + 1 : 0;
+  c.n_kv = c.se.base + c.q0 + c.nq0 + c.nq1;
+  c.n_load = max(c.nt0, c.nt1);
+  return c;
 }
 
 template <int G>
@@ -239,23 +319,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     return;
   }
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int si = blockIdx.y, h = blockIdx.z;
   constexpr int TQ = kTileM / G;  // new tokens per query tile
-  const int tile = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // long tiles first
-  const SeqEntry se = p.seqs[si];
-  const int q0 = tile * 2 * TQ;
-  if (q0 >= se.count) return;
-  // Query tile w: tokens [q0 + w*TQ, +nq_w); it attends K/V tiles [0, nt_w).
-  const int nq0 = min(TQ, se.count - q0), nq1 = max(0, min(TQ, se.count - q0 - TQ));
-  const int nt0 = (se.base + q0 + nq0 - 1) / kTileN + 1;
-  const int nt1 = nq1 > 0 ? (se.base + q0 + TQ + nq1 - 1) / kTileN + 1 : 0;
-  const int n_kv = se.base + q0 + nq0 + nq1;  // keys the CTA reads
-  const int n_load = max(nt0, nt1);           // = (n_kv + 127) / 128
-  const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
+  {
+    const CtaWork c = cta_work<G>(p);
+    if (c.q0 >= c.se.count) return;  // uniform over the CTA
+  }
 
   auto bar = [&](int i) { return sbase + kWsOffBar + 8u * static_cast<uint32_t>(i); };
-  uint32_t* misc = reinterpret_cast<uint32_t*>(sm + kWsOffMisc);
-  volatile uint32_t* abort_flag = misc + 1;
+  const uint32_t abort_off = kWsOffMisc + 4;  // the abort flag's shared-memory offset
   if (tid == 0) {
     for (int s = 0; s < kWsStages; ++s) {
       bar_init(bar(kBarKFull + s), 1);
@@ -271,7 +342,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       bar_init(bar(kBarODone + w), 1);
     }
     bar_init(bar(kBarDrain), 1);
-    *abort_flag = 0u;
+    st_volatile_shared(sbase + abort_off, 0u);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 9) {
@@ -284,22 +355,26 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = misc[0];
   // One lane of a warp reports a failed (warp-uniform) wait.
   auto raise_abort = [&]() {
     if (lane == 0) {
-      *abort_flag = 1u;
+      st_volatile_shared(sbase + abort_off, 1u);
       atomicOr(p.g.error, kErrTimeout);
     }
   };
   auto wait_warp = [&](uint32_t b, uint32_t parity) {
-    const bool ok = bar_wait_ab(b, parity, abort_flag);
+    const bool ok = bar_wait_ab(b, parity, sbase + abort_off);
     return __all_sync(0xffffffffu, ok);
   };
 
   if (warp < 8) {
     // ================= softmax warpgroups =================
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWsRegsSoftmax));
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWsRegsSoftmax) : "memory");
+    const CtaWork cw = cta_work<G>(p);
+    const SeqEntry se = cw.se;
+    const int h = cw.h, q0 = cw.q0, nq0 = cw.nq0, nq1 = cw.nq1, nt0 = cw.nt0, nt1 = cw.nt1;
+    const int Hq = p.g.q_heads;
+    const uint32_t tmem = ld_volatile_shared(sbase + kWsOffMisc);
     const int w = warp >> 2;
     const int r = tid & 127;  // this thread's row = TMEM lane
     const int qw0 = q0 + w * TQ, nqw = w ? nq1 : nq0, ntw = w ? nt1 : nt0;
@@ -307,7 +382,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     const bool live = tq < nqw;
     const int qpos = se.base + qw0 + tq;
     const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const uint32_t s_col = static_cast<uint32_t>(w * kTileN), o_col = kWsOCol + w * kHeadDim;
+    const uint32_t s_col = static_cast<uint32_t>(w * kTileN), o_col = kWsOCol + w * kHeadDim,
+                   p_col = kWsPCol + w * (kTileN / 2);
     if (ntw > 0) {
       // Q rows: RoPE at the token's position, scaled into the exp2 domain,
       // bf16; rows past the tile's tokens are zero.
@@ -337,7 +413,6 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     }
     float m_used = -INFINITY, l_sum = 0.f;
     bool ok = true;  // warp-uniform
-    uint8_t* prow = sm + kWsOffP + w * 2 * kTileBytes;
     for (int j = 0; j < ntw; ++j) {
       // ---- S_j out of TMEM; the columns go back to the MMA warp at once ----
       if (!wait_warp(bar(kBarSFull + w), j & 1)) {
@@ -386,9 +461,18 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         corr = ex2(m_used - mx);  // 0 on the first tile
         m_used = mx;
       }
+      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
+      uint32_t pw[kTileN / 2];  // P row, bf16 pairs
+#pragma unroll
+      for (int i = 0; i < kTileN / 2; ++i) {
+        const float a = ex2(s[2 * i] - m_used), b = ex2(s[2 * i + 1] - m_used);
+        ps8[i & 7] += a + b;
+        pw[i] = bf16x2(a, b);
+      }
+      const float psum =
+          ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+      l_sum = fmaf(l_sum, corr, psum);
       // ---- P_{j-1} V done: P_w and O_w are free ---------------------------------
-      // (waited before the exponentials so that P goes to shared memory as it
-      // is made, instead of 64 more registers a thread)
       if (j > 0) {
         if (!wait_warp(bar(kBarODone + w), (j - 1) & 1)) {
           ok = false;
@@ -407,27 +491,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
             for (int i = 0; i < 32; ++i) v[i] *= corr;
             tmem_st32(trow + o_col + 32 * c, v);
           }
-          tmem_wait_st();
         }
       }
-      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
-#pragma unroll
-      for (int u = 0; u < kTileN / 8; ++u) {  // tokens 0-63 in the first P tile, 64-127 in the second
-        uint32_t pw[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int i = 8 * u + 2 * k;
-          const float a = ex2(s[i] - m_used), b = ex2(s[i + 1] - m_used);
-          ps8[(4 * u + k) & 7] += a + b;
-          pw[k] = bf16x2(a, b);
-        }
-        *reinterpret_cast<uint4*>(prow + (u >> 3) * kTileBytes + swz(r, u & 7)) =
-            make_uint4(pw[0], pw[1], pw[2], pw[3]);
-      }
-      const float psum =
-          ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
-      l_sum = fmaf(l_sum, corr, psum);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_st32u(trow + p_col, pw);
+      tmem_st32u(trow + p_col + 32, pw + 32);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) bar_arrive(bar(kBarPFull + w));
@@ -458,34 +526,46 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     }
     if (!ok) raise_abort();
   } else {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWsRegsProducer));
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWsRegsProducer) : "memory");
+    const CtaWork cw = cta_work<G>(p);
+    const int warp = thread_index() >> 5, lane = thread_index() & 31;  // read again, as cw
+    auto raise_abort = [&]() {
+      if (lane == 0) {
+        st_volatile_shared(sbase + abort_off, 1u);
+        atomicOr(p.g.error, kErrTimeout);
+      }
+    };
+    const int h = cw.h, nt0 = cw.nt0, nt1 = cw.nt1, n_kv = cw.n_kv, n_load = cw.n_load;
+    const int Hkv = p.g.kv_heads;
+    const uint32_t tmem = ld_volatile_shared(sbase + kWsOffMisc);
     const int n_blocks = (n_kv + kBlockTokens - 1) / kBlockTokens;
+    // Shared addresses are rederived from sb, made opaque once per tile, so
+    // that they are not all held in registers across the loops.
+    uint32_t sb = sbase;
+    auto pbar = [&](int i) { return sb + kWsOffBar + 8u * static_cast<uint32_t>(i); };
+    auto pwait = [&](uint32_t b, uint32_t parity) {
+      const bool ok = bar_wait_ab(b, parity, sb + abort_off);
+      return __all_sync(0xffffffffu, ok);
+    };
     if (warp == 8) {
       // ================= loader =================
       // K and V tile t -> stage t % 3: its 16-token blocks through the block
-      // table, one lane per block. Block ids of tiles [win, win+8) sit in
-      // registers (blk_cur: tiles win..win+3, lane l -> tile win + l/8, block
-      // l%8; blk_nxt: the next four), loaded four tiles before they are needed.
-      const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
+      // table, one lane per block (lanes 0-7); each lane loads the next tile's
+      // block id while the current one is copied.
+      const int32_t* bt = p.g.block_table + static_cast<size_t>(cw.se.slot) * p.g.max_blocks_per_seq;
       const int layer_row0 = p.layer * p.g.num_blocks * Hkv;
-      auto fetch_window = [&](int first_tile) {
-        const int b = first_tile * (kTileN / kBlockTokens) + lane;
-        return b < n_blocks ? bt[b] : 0;
+      auto block_id = [&](int t) {
+        const int b = t * (kTileN / kBlockTokens) + lane;
+        return (lane < kTileN / kBlockTokens && b < n_blocks) ? bt[b] : 0;
       };
-      int win = 0;
-      int blk_cur = fetch_window(0), blk_nxt = fetch_window(4);
+      int blk_next = block_id(0);
       int k_issued = 0, v_issued = 0;
       bool ok = true;
       for (int t = 0; t < n_load; ++t) {
+        sb = opaque(sb);
         const int st = t % kWsStages;
-        while (t >= win + 4) {
-          blk_cur = blk_nxt;
-          win += 4;
-          blk_nxt = fetch_window(win + 4);
-        }
-        const int rel = t - win, sl = ((rel & 3) << 3) + (lane & 7);
-        const int a = __shfl_sync(0xffffffffu, blk_cur, sl), c = __shfl_sync(0xffffffffu, blk_nxt, sl);
-        int32_t blk = rel < 4 ? a : c;
+        int32_t blk = blk_next;
+        blk_next = block_id(t + 1);
         const int nb = min(kTileN / kBlockTokens, n_blocks - t * (kTileN / kBlockTokens));
         if (static_cast<uint32_t>(blk) >= static_cast<uint32_t>(p.g.num_blocks)) {
           if (lane < nb) atomicOr(p.g.error, kErrBadBlock);
@@ -495,22 +575,22 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         const uint32_t off = static_cast<uint32_t>(st * kTileBytes + lane * kBlockTokens * 128);
         const uint32_t bytes = static_cast<uint32_t>(nb) * kBlockTokens * kHeadDim * 2;
         const uint32_t free_parity = static_cast<uint32_t>((t / kWsStages - 1) & 1);
-        if (t >= kWsStages && !wait_warp(bar(kBarKFree + st), free_parity)) {
+        if (t >= kWsStages && !pwait(pbar(kBarKFree + st), free_parity)) {
           ok = false;
           break;
         }
-        if (lane == 0) bar_expect_tx(bar(kBarKFull + st), bytes);
+        if (lane == 0) bar_expect_tx(pbar(kBarKFull + st), bytes);
         __syncwarp();
-        if (lane < nb) tma_rows(sbase + kWsOffK + off, &p.tmap_k, y, bar(kBarKFull + st));
+        if (lane < nb) tma_rows(sb + kWsOffK + off, &p.tmap_k, y, pbar(kBarKFull + st));
         __syncwarp();
         k_issued = t + 1;
-        if (t >= kWsStages && !wait_warp(bar(kBarVFree + st), free_parity)) {
+        if (t >= kWsStages && !pwait(pbar(kBarVFree + st), free_parity)) {
           ok = false;
           break;
         }
-        if (lane == 0) bar_expect_tx(bar(kBarVFull + st), bytes);
+        if (lane == 0) bar_expect_tx(pbar(kBarVFull + st), bytes);
         __syncwarp();
-        if (lane < nb) tma_rows(sbase + kWsOffV + off, &p.tmap_v, y, bar(kBarVFull + st));
+        if (lane < nb) tma_rows(sb + kWsOffV + off, &p.tmap_v, y, pbar(kBarVFull + st));
         __syncwarp();
         v_issued = t + 1;
       }
@@ -519,9 +599,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       // released, also when another role gave up and left it unread (a copy
       // the MMA warp consumed has completed its phase: no wait).
       for (int t = max(0, k_issued - kWsStages); t < k_issued; ++t)
-        bar_wait(bar(kBarKFull + t % kWsStages), (t / kWsStages) & 1);
+        bar_wait(pbar(kBarKFull + t % kWsStages), (t / kWsStages) & 1);
       for (int t = max(0, v_issued - kWsStages); t < v_issued; ++t)
-        bar_wait(bar(kBarVFull + t % kWsStages), (t / kWsStages) & 1);
+        bar_wait(pbar(kBarVFull + t % kWsStages), (t / kWsStages) & 1);
       __syncwarp();
     } else if (warp == 9) {
       // ================= MMA issue (lane 0; the warp waits together) =================
@@ -529,25 +609,23 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       constexpr uint32_t kIdPV = idesc(kTileM, kHeadDim, true);
       auto issue_s = [&](int w, int t) {  // S_w = Q_w K_t^T
         if (lane == 0) {
-          const uint32_t kaddr = sbase + kWsOffK + (t % kWsStages) * kTileBytes;
-          const uint32_t qaddr = sbase + kWsOffQ + w * kTileBytes;
+          const uint32_t kaddr = sb + kWsOffK + (t % kWsStages) * kTileBytes;
+          const uint32_t qaddr = sb + kWsOffQ + w * kTileBytes;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             mma_f16(tmem + w * kTileN, sdesc(qaddr + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64),
                     kIdQK, kk > 0);
-          mma_commit(bar(kBarSFull + w));
+          mma_commit(pbar(kBarSFull + w));
         }
       };
-      auto issue_pv = [&](int w, int t) {  // O_w += P_w V_t
+      auto issue_pv = [&](int w, int t) {  // O_w += P_w V_t, P_w from TMEM
         if (lane == 0) {
-          const uint32_t vaddr = sbase + kWsOffV + (t % kWsStages) * kTileBytes;
-          const uint32_t paddr = sbase + kWsOffP + w * 2 * kTileBytes;
+          const uint32_t vaddr = sb + kWsOffV + (t % kWsStages) * kTileBytes;
 #pragma unroll
-          for (int kk = 0; kk < kTileN / 16; ++kk)
-            mma_f16(tmem + kWsOCol + w * kHeadDim,
-                    sdesc(paddr + (kk >> 2) * kTileBytes + 32 * (kk & 3), 1, 64),
-                    sdesc(vaddr + 2048 * kk, kTileBytes >> 4, 64), kIdPV, (t > 0 || kk > 0) ? 1 : 0);
-          mma_commit(bar(kBarODone + w));
+          for (int kk = 0; kk < kTileN / 16; ++kk)  // 16 tokens = 8 P columns a step
+            mma_f16_ts(tmem + kWsOCol + w * kHeadDim, tmem + kWsPCol + w * (kTileN / 2) + 8 * kk,
+                       sdesc(vaddr + 2048 * kk, kTileBytes >> 4, 64), kIdPV, (t > 0 || kk > 0) ? 1 : 0);
+          mma_commit(pbar(kBarODone + w));
         }
       };
       auto commit_to = [&](int b) {
@@ -556,7 +634,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       // V_t landed; on the last tile, rows past the cache are cleared: P is 0
       // there, but 0 times a non-finite stale value is not 0.
       auto v_ready = [&](int t) {
-        if (!wait_warp(bar(kBarVFull + t % kWsStages), (t / kWsStages) & 1)) return false;
+        if (!pwait(pbar(kBarVFull + t % kWsStages), (t / kWsStages) & 1)) return false;
         const int valid = n_kv - t * kTileN;
         if (valid < kTileN) {
           uint8_t* vt = sm + kWsOffV + (t % kWsStages) * kTileBytes;
@@ -568,8 +646,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         }
         return true;
       };
-      bool ok = wait_warp(bar(kBarQFull + 0), 0) && (nt1 == 0 || wait_warp(bar(kBarQFull + 1), 0)) &&
-                wait_warp(bar(kBarKFull + 0), 0);
+      bool ok = pwait(pbar(kBarQFull + 0), 0) && (nt1 == 0 || pwait(pbar(kBarQFull + 1), 0)) &&
+                pwait(pbar(kBarKFull + 0), 0);
       if (ok) {
         tc_fence_after();
         issue_s(0, 0);
@@ -577,14 +655,15 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         commit_to(kBarKFree + 0);
       }
       for (int j = 0; ok && j < n_load; ++j) {
+        sb = opaque(sb);
         const int nx = j + 1;
         if (nx < n_load) {
-          if (!wait_warp(bar(kBarKFull + nx % kWsStages), (nx / kWsStages) & 1)) {
+          if (!pwait(pbar(kBarKFull + nx % kWsStages), (nx / kWsStages) & 1)) {
             ok = false;
             break;
           }
           if (nx < nt0) {
-            if (!wait_warp(bar(kBarSFree + 0), j & 1)) {
+            if (!pwait(pbar(kBarSFree + 0), j & 1)) {
               ok = false;
               break;
             }
@@ -594,7 +673,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         }
         bool have_v = false;
         if (j < nt0) {
-          if (!wait_warp(bar(kBarPFull + 0), j & 1) || !v_ready(j)) {
+          if (!pwait(pbar(kBarPFull + 0), j & 1) || !v_ready(j)) {
             ok = false;
             break;
           }
@@ -604,7 +683,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         }
         if (nx < n_load) {
           if (nx < nt1) {
-            if (!wait_warp(bar(kBarSFree + 1), j & 1)) {
+            if (!pwait(pbar(kBarSFree + 1), j & 1)) {
               ok = false;
               break;
             }
@@ -614,7 +693,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
           commit_to(kBarKFree + nx % kWsStages);
         }
         if (j < nt1) {
-          if (!wait_warp(bar(kBarPFull + 1), j & 1) || (!have_v && !v_ready(j))) {
+          if (!pwait(pbar(kBarPFull + 1), j & 1) || (!have_v && !v_ready(j))) {
             ok = false;
             break;
           }
@@ -626,7 +705,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       if (!ok) raise_abort();
       // every MMA this warp issued completes before TMEM is released
       commit_to(kBarDrain);
-      bar_wait(bar(kBarDrain), 0);
+      bar_wait(pbar(kBarDrain), 0);
       __syncwarp();
     }
   }
@@ -634,7 +713,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
   __syncthreads();
   tc_fence_after();
   if (warp == 9)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kWsTmemCols)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(
+                     ld_volatile_shared(sbase + kWsOffMisc)),
+                 "r"(kWsTmemCols)
                  : "memory");
 }
 
