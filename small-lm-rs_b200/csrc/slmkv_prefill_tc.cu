@@ -188,25 +188,26 @@ __device__ __forceinline__ uint32_t swz(int r, int u) {
 
 // 384 threads in three warpgroups. Warpgroups 0 and 1 each own a 128-row query
 // tile (A: the CTA's first 128/G tokens, B: the next 128/G) and run its
-// softmax; in warpgroup 2, warp 8 loads K/V tiles (3 stages each) and warp 9
-// issues the MMAs. TMEM holds S_A, S_B (128 columns each) and O_A, O_B (64
-// each), so the tensor cores compute one tile's scores while the other tile's
-// softmax runs. Every handoff is an mbarrier:
+// softmax; in warpgroup 2, warp 8 loads K/V tiles (3 stages each), warp 9
+// issues the S = Q K^T products and warp 10 the O += P V products. TMEM holds
+// S, O and P of both query tiles, so the tensor cores compute one tile's
+// scores while the other tile's softmax runs. Every handoff is an mbarrier:
 //   k_full/v_full[s]  copies landed (TMA transaction bytes)   loader -> MMA
 //   k_free/v_free[s]  the MMAs reading the stage are done     MMA -> loader
-//   q_full[w]         Q tile w written (4 warp arrivals)      softmax -> MMA
-//   s_full[w]         S_w of the next K tile is in TMEM       MMA -> softmax
-//   s_free[w]         S_w read out of TMEM (4 arrivals)       softmax -> MMA
-//   p_full[w]         P_w in TMEM, O_w rescaled               softmax -> MMA
-//   o_done[w]         P_w V done: P_w and O_w free            MMA -> softmax
+//   q_full[w]         Q tile w written (4 warp arrivals)      softmax -> S
+//   s_full[w]         S_w of the next K tile is in TMEM       S -> softmax
+//   s_free[w]         S_w read out of TMEM (4 arrivals)       softmax -> S
+//   p_full[w]         P_w in TMEM, O_w rescaled               softmax -> PV
+//   o_done[w]         P_w V done: P_w and O_w free            PV -> softmax
 // Each completes once per K/V tile in order, so its phase parity is the
-// tile index's low bit. Registers are rebalanced with setmaxnreg: the
+// tile index's low bit. The two issuers touch disjoint TMEM columns, and each
+// commits only its own MMAs. Registers are rebalanced with setmaxnreg: the
 // softmax warpgroups rise to 224 (a 128-score row stays in registers), the
 // producer warpgroup drops to 56; 128 * (2 * 224 + 56) = 384 * 168, the
 // registers the CTA is launched with (checked on the host before launch).
 // A wait that runs out (1 s) sets the CTA's abort flag, which ends every
 // other wait at once; the loader then waits (bounded) for its own copies and
-// the MMA warp for its own MMAs before TMEM is released.
+// each issuer for its own MMAs before TMEM is released.
 constexpr int kWsThreads = 384;
 constexpr int kWsStages = 3;
 // TMEM columns: S_A [0,128), S_B [128,256), O_A [256,320), O_B [320,384),
@@ -233,8 +234,8 @@ enum : int {
   kBarSFree = kBarSFull + 2,
   kBarPFull = kBarSFree + 2,
   kBarODone = kBarPFull + 2,
-  kBarDrain = kBarODone + 2,
-  kWsBars
+  kBarDrain = kBarODone + 2,  // one per MMA-issuing warp
+  kWsBars = kBarDrain + 2
 };
 constexpr int kWsOffMisc = kWsOffBar + 8 * kWsBars;  // TMEM base, abort flag
 constexpr int kSmemWs = kWsOffMisc + 16;
@@ -341,7 +342,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       bar_init(bar(kBarPFull + w), 4);
       bar_init(bar(kBarODone + w), 1);
     }
-    bar_init(bar(kBarDrain), 1);
+    bar_init(bar(kBarDrain + 0), 1);
+    bar_init(bar(kBarDrain + 1), 1);
     st_volatile_shared(sbase + abort_off, 0u);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -603,8 +605,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       for (int t = max(0, v_issued - kWsStages); t < v_issued; ++t)
         bar_wait(pbar(kBarVFull + t % kWsStages), (t / kWsStages) & 1);
       __syncwarp();
-    } else if (warp == 9) {
-      // ================= MMA issue (lane 0; the warp waits together) =================
+    } else if (warp == 9 || warp == 10) {
+      // ============ MMA issue: warp 9 the S products, warp 10 the P V products ============
+      // (lane 0 issues; the warp waits together). Two issuers, so that the
+      // next S of one query tile never queues behind the other tile's P V.
       constexpr uint32_t kIdQK = idesc(kTileM, kTileN, false);
       constexpr uint32_t kIdPV = idesc(kTileM, kHeadDim, true);
       auto issue_s = [&](int w, int t) {  // S_w = Q_w K_t^T
@@ -646,66 +650,62 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         }
         return true;
       };
-      bool ok = pwait(pbar(kBarQFull + 0), 0) && (nt1 == 0 || pwait(pbar(kBarQFull + 1), 0)) &&
-                pwait(pbar(kBarKFull + 0), 0);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        if (nt1 > 0) issue_s(1, 0);
-        commit_to(kBarKFree + 0);
-      }
-      for (int j = 0; ok && j < n_load; ++j) {
-        sb = opaque(sb);
-        const int nx = j + 1;
-        if (nx < n_load) {
-          if (!pwait(pbar(kBarKFull + nx % kWsStages), (nx / kWsStages) & 1)) {
+      bool ok = true;
+      if (warp == 9) {
+        ok = pwait(pbar(kBarQFull + 0), 0) && (nt1 == 0 || pwait(pbar(kBarQFull + 1), 0));
+        for (int j = 0; ok && j < n_load; ++j) {
+          sb = opaque(sb);
+          if (!pwait(pbar(kBarKFull + j % kWsStages), (j / kWsStages) & 1)) {
             ok = false;
             break;
           }
-          if (nx < nt0) {
-            if (!pwait(pbar(kBarSFree + 0), j & 1)) {
+          // S_w,j overwrites S_w,j-1: it goes once warpgroup w has read that
+          if (j < nt0) {
+            if (j > 0 && !pwait(pbar(kBarSFree + 0), (j - 1) & 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_s(0, nx);
+            issue_s(0, j);
           }
-        }
-        bool have_v = false;
-        if (j < nt0) {
-          if (!pwait(pbar(kBarPFull + 0), j & 1) || !v_ready(j)) {
-            ok = false;
-            break;
-          }
-          have_v = true;
-          tc_fence_after();
-          issue_pv(0, j);
-        }
-        if (nx < n_load) {
-          if (nx < nt1) {
-            if (!pwait(pbar(kBarSFree + 1), j & 1)) {
+          if (j < nt1) {
+            if (j > 0 && !pwait(pbar(kBarSFree + 1), (j - 1) & 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_s(1, nx);
+            issue_s(1, j);
           }
-          commit_to(kBarKFree + nx % kWsStages);
+          commit_to(kBarKFree + j % kWsStages);
         }
-        if (j < nt1) {
-          if (!pwait(pbar(kBarPFull + 1), j & 1) || (!have_v && !v_ready(j))) {
-            ok = false;
-            break;
+      } else {
+        for (int j = 0; ok && j < n_load; ++j) {
+          sb = opaque(sb);
+          bool have_v = false;
+          if (j < nt0) {
+            if (!pwait(pbar(kBarPFull + 0), j & 1) || !v_ready(j)) {
+              ok = false;
+              break;
+            }
+            have_v = true;
+            tc_fence_after();
+            issue_pv(0, j);
           }
-          tc_fence_after();
-          issue_pv(1, j);
+          if (j < nt1) {
+            if (!pwait(pbar(kBarPFull + 1), j & 1) || (!have_v && !v_ready(j))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(1, j);
+          }
+          commit_to(kBarVFree + j % kWsStages);
         }
-        commit_to(kBarVFree + j % kWsStages);
       }
       if (!ok) raise_abort();
       // every MMA this warp issued completes before TMEM is released
-      commit_to(kBarDrain);
-      bar_wait(pbar(kBarDrain), 0);
+      commit_to(kBarDrain + (warp - 9));
+      bar_wait(pbar(kBarDrain + (warp - 9)), 0);
       __syncwarp();
     }
   }
