@@ -388,26 +388,33 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
                    p_col = kWsPCol + w * (kTileN / 2);
     if (ntw > 0) {
       // Q rows: RoPE at the token's position, scaled into the exp2 domain,
-      // bf16; rows past the tile's tokens are zero.
+      // bf16; rows past the tile's tokens are zero. A warp writes its 32 TMEM
+      // rows one row per step: lane l holds elements 2l, 2l+1 (one RoPE pair),
+      // so each row is one coalesced 256-byte load (and one of the RoPE
+      // table), and the lanes' 4-byte results fill the row's swizzled line.
       uint8_t* qt = sm + kWsOffQ + w * kTileBytes;
-      const float2* src = reinterpret_cast<const float2*>(
-          p.q + (static_cast<size_t>(se.row_offset + qw0 + (live ? tq : 0)) * Hq + h * G + gq) *
-                    kHeadDim);
-      const float2* cs = p.g.rope + static_cast<size_t>(live ? qpos : 0) * (kHeadDim / 2);
+      const int r0 = (warp & 3) * 32;
+      float2 xv[32], cv[32];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        uint32_t hw[4];
+      for (int i = 0; i < 32; ++i) {  // all loads first
+        const int t = (r0 + i) / G, g = (r0 + i) % G;
+        const bool lv = t < nqw;
+        const size_t row = static_cast<size_t>(se.row_offset + qw0 + t) * Hq + h * G + g;
+        xv[i] = lv ? reinterpret_cast<const float2*>(p.q + row * kHeadDim)[lane] : make_float2(0.f, 0.f);
+        cv[i] = lv && p.rotate
+                    ? p.g.rope[static_cast<size_t>(se.base + qw0 + t) * (kHeadDim / 2) + lane]
+                    : make_float2(1.f, 0.f);
+      }
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          float2 x = live ? src[4 * u + k] : make_float2(0.f, 0.f);
-          if (live && p.rotate) {
-            const float2 c = cs[4 * u + k];
-            x = make_float2(__fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, c.y)),
-                            __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x)));
-          }
-          hw[k] = bf16x2(x.x * kScaleLog2Tc, x.y * kScaleLog2Tc);
+      for (int i = 0; i < 32; ++i) {
+        float2 x = xv[i];
+        if (p.rotate) {
+          const float2 c = cv[i];
+          x = make_float2(__fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, c.y)),
+                          __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x)));
         }
-        *reinterpret_cast<uint4*>(qt + swz(r, u)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint32_t*>(qt + swz(r0 + i, lane >> 2) + (lane & 3) * 4) =
+            bf16x2(x.x * kScaleLog2Tc, x.y * kScaleLog2Tc);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
