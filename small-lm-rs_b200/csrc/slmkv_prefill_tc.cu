@@ -186,12 +186,14 @@ __device__ __forceinline__ uint32_t swz(int r, int u) {
   return static_cast<uint32_t>(((r >> 3) << 10) + ((r & 7) << 7) + (((u ^ r) & 7) << 4));
 }
 
-// 384 threads in three warpgroups. Warpgroups 0 and 1 each own a 128-row query
-// tile (A: the CTA's first 128/G tokens, B: the next 128/G) and run its
-// softmax; in warpgroup 2, warp 8 loads K/V tiles (3 stages each), warp 9
-// issues the S = Q K^T products and warp 10 the O += P V products. TMEM holds
-// S, O and P of both query tiles, so the tensor cores compute one tile's
-// scores while the other tile's softmax runs. Every handoff is an mbarrier:
+// A CTA is QT softmax warpgroups and a producer warpgroup. Softmax warpgroup
+// w owns a 128-row query tile (w = 0: the CTA's first 128/G tokens, w = 1: the
+// next 128/G); in the producer warpgroup, the first warp loads K/V tiles (3
+// stages each), the second issues the S = Q K^T products and the third the
+// O += P V products. TMEM holds S, O and P of the CTA's query tiles; with
+// QT = 1 two CTAs share an SM, with QT = 2 the two tiles of one CTA do, so
+// either way the tensor cores compute one tile's scores while another
+// tile's softmax runs. Every handoff is an mbarrier:
 //   k_full/v_full[s]  copies landed (TMA transaction bytes)   loader -> MMA
 //   k_free/v_free[s]  the MMAs reading the stage are done     MMA -> loader
 //   q_full[w]         Q tile w written (4 warp arrivals)      softmax -> S
@@ -202,28 +204,38 @@ __device__ __forceinline__ uint32_t swz(int r, int u) {
 // Each completes once per K/V tile in order, so its phase parity is the
 // tile index's low bit. The two issuers touch disjoint TMEM columns, and each
 // commits only its own MMAs. Registers are rebalanced with setmaxnreg: the
-// softmax warpgroups rise to 224 (a 128-score row stays in registers), the
-// producer warpgroup drops to 56; 128 * (2 * 224 + 56) = 384 * 168, the
-// registers the CTA is launched with (checked on the host before launch).
+// softmax warpgroups rise (a 128-score row stays in registers), the
+// producer warpgroup drops, within the registers the CTA is launched with
+// (checked on the host before launch).
 // A wait that runs out (1 s) sets the CTA's abort flag, which ends every
 // other wait at once; the loader then waits (bounded) for its own copies and
 // each issuer for its own MMAs before TMEM is released.
-constexpr int kWsThreads = 384;
 constexpr int kWsStages = 3;
-// TMEM columns: S_A [0,128), S_B [128,256), O_A [256,320), O_B [320,384),
-// P_A [384,448), P_B [448,512) (P: 128 bf16 a row, two a column)
-constexpr int kWsTmemCols = 512;
-constexpr int kWsOCol = 256;
-constexpr int kWsPCol = 384;
-constexpr int kWsRegsSoftmax = 224, kWsRegsProducer = 56, kWsRegsLaunch = 168;
-static_assert(128 * (2 * kWsRegsSoftmax + kWsRegsProducer) <= kWsThreads * kWsRegsLaunch,
-              "the setmaxnreg split must fit the registers the CTA is launched with");
-static_assert(kWsRegsLaunch == (65536 / kWsThreads) / 8 * 8, "launch registers of a 384-thread CTA");
-
-constexpr int kWsOffQ = 0;                                // Q_A, Q_B
-constexpr int kWsOffK = kWsOffQ + 2 * kTileBytes;          // kWsStages buffers
-constexpr int kWsOffV = kWsOffK + kWsStages * kTileBytes;  // kWsStages buffers
-constexpr int kWsOffBar = kWsOffV + kWsStages * kTileBytes;
+constexpr int kPrefillQT = 1;  // query tiles per CTA (1: two CTAs per SM)
+// Launch shape for QT query tiles per CTA (128 threads each) plus the
+// producer warpgroup. QT = 2: one CTA per SM (384 threads at 168 registers,
+// 512 TMEM columns). QT = 1: two CTAs per SM (256 threads at 128 registers,
+// 256 TMEM columns, 112 KiB of shared memory each), so one CTA's start and
+// end overlap the other's steady state.
+// TMEM columns: S_w [128w, +128), O_w [128QT + 64w, +64), P_w [192QT + 64w,
+// +64) (P: 128 bf16 a row, two a column).
+template <int QT>
+struct WsCfg {
+  static constexpr int kThreads = 128 * (QT + 1);
+  static constexpr int kCtasPerSm = QT == 1 ? 2 : 1;
+  static constexpr int kTmemCols = 256 * QT;
+  static constexpr int kOCol = 128 * QT;
+  static constexpr int kPCol = 192 * QT;
+  static constexpr int kRegsLaunch = (65536 / (kThreads * kCtasPerSm)) / 8 * 8;
+  static constexpr int kRegsSoftmax = QT == 2 ? 224 : 216;
+  static constexpr int kRegsProducer = QT == 2 ? 56 : 40;
+  static_assert(128 * (QT * kRegsSoftmax + kRegsProducer) <= kThreads * kRegsLaunch,
+                "the setmaxnreg split must fit the registers the CTA is launched with");
+  static constexpr int kOffQ = 0;                                    // Q_w
+  static constexpr int kOffK = kOffQ + QT * kTileBytes;                // kWsStages buffers
+  static constexpr int kOffV = kOffK + kWsStages * kTileBytes;         // kWsStages buffers
+  static constexpr int kOffBar = kOffV + kWsStages * kTileBytes;
+};
 enum : int {
   kBarKFull = 0,
   kBarVFull = kBarKFull + kWsStages,
@@ -237,9 +249,14 @@ enum : int {
   kBarDrain = kBarODone + 2,  // one per MMA-issuing warp
   kWsBars = kBarDrain + 2
 };
-constexpr int kWsOffMisc = kWsOffBar + 8 * kWsBars;  // TMEM base, abort flag
-constexpr int kSmemWs = kWsOffMisc + 16;
-static_assert(kSmemWs <= 227 * 1024, "shared memory of one CTA");
+template <int QT>
+constexpr int ws_off_misc() {  // TMEM base, abort flag
+  return WsCfg<QT>::kOffBar + 8 * kWsBars;
+}
+template <int QT>
+constexpr int ws_smem() {
+  return ws_off_misc<QT>() + 16;
+}
 
 __device__ __forceinline__ void bar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
@@ -254,7 +271,7 @@ __device__ __forceinline__ void st_volatile_shared(uint32_t addr, uint32_t v) {
 }
 // The value, hidden from the optimizer: addresses derived from it inside a
 // loop are recomputed there instead of being kept in registers across the
-// loop (the producer warps run with 56 registers).
+// loop (the producer warps run with few registers).
 __device__ __forceinline__ uint32_t opaque(uint32_t x) {
   asm volatile("" : "+r"(x));
   return x;
@@ -290,7 +307,7 @@ __device__ __forceinline__ int thread_index() {
   asm volatile("mov.u32 %0, %%tid.x;" : "=r"(t));
   return static_cast<int>(t);
 }
-template <int G>
+template <int G, int QT>
 __device__ __forceinline__ CtaWork cta_work(const PrefillLaunch& p) {
   uint32_t bx, by, bz, nbx;
   asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(bx));
@@ -301,9 +318,9 @@ __device__ __forceinline__ CtaWork cta_work(const PrefillLaunch& p) {
   CtaWork c;
   c.se = p.seqs[by];
   c.h = static_cast<int>(bz);
-  c.q0 = (static_cast<int>(nbx) - 1 - static_cast<int>(bx)) * 2 * TQ;  // long tiles first
+  c.q0 = (static_cast<int>(nbx) - 1 - static_cast<int>(bx)) * QT * TQ;  // long tiles first
   c.nq0 = min(TQ, c.se.count - c.q0);
-  c.nq1 = max(0, min(TQ, c.se.count - c.q0 - TQ));
+  c.nq1 = QT == 2 ? max(0, min(TQ, c.se.count - c.q0 - TQ)) : 0;
   c.nt0 = (c.se.base + c.q0 + c.nq0 - 1) / kTileN + 1;
   c.nt1 = c.nq1 > 0 ? (c.se.base + c.q0 + TQ + c.nq1 - 1) / kTileN + 1 : 0;
   c.n_kv = c.se.base + c.q0 + c.nq0 + c.nq1;
@@ -311,8 +328,14 @@ __device__ __forceinline__ CtaWork cta_work(const PrefillLaunch& p) {
   return c;
 }
 
-template <int G>
-__global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_constant__ PrefillLaunch p) {
+template <int G, int QT>
+__global__ void __launch_bounds__(WsCfg<QT>::kThreads, WsCfg<QT>::kCtasPerSm)
+    prefill_ws_kernel(const __grid_constant__ PrefillLaunch p) {
+  using Cfg = WsCfg<QT>;
+  static_assert(ws_smem<QT>() <= 227 * 1024 &&
+                    Cfg::kCtasPerSm * (ws_smem<QT>() + 1024) <= 228 * 1024,
+                "the CTAs of an SM must fit its shared memory");
+  constexpr int kLoadWarp = 4 * QT, kSWarp = 4 * QT + 1, kPvWarp = 4 * QT + 2;
   extern __shared__ __align__(1024) uint8_t sm[];
   const uint32_t sbase = su32(sm);
   if (sbase & 1023u) {  // uniform over the CTA: report instead of misreading tiles
@@ -322,12 +345,12 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int TQ = kTileM / G;  // new tokens per query tile
   {
-    const CtaWork c = cta_work<G>(p);
+    const CtaWork c = cta_work<G, QT>(p);
     if (c.q0 >= c.se.count) return;  // uniform over the CTA
   }
 
-  auto bar = [&](int i) { return sbase + kWsOffBar + 8u * static_cast<uint32_t>(i); };
-  const uint32_t abort_off = kWsOffMisc + 4;  // the abort flag's shared-memory offset
+  auto bar = [&](int i) { return sbase + Cfg::kOffBar + 8u * static_cast<uint32_t>(i); };
+  const uint32_t abort_off = ws_off_misc<QT>() + 4;  // the abort flag's shared-memory offset
   if (tid == 0) {
     for (int s = 0; s < kWsStages; ++s) {
       bar_init(bar(kBarKFull + s), 1);
@@ -347,10 +370,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     st_volatile_shared(sbase + abort_off, 0u);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 9) {
+  if (warp == kSWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     sbase + kWsOffMisc),
-                 "r"(kWsTmemCols)
+                     sbase + ws_off_misc<QT>()),
+                 "r"(Cfg::kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -369,14 +392,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     return __all_sync(0xffffffffu, ok);
   };
 
-  if (warp < 8) {
+  if (warp < 4 * QT) {
     // ================= softmax warpgroups =================
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWsRegsSoftmax) : "memory");
-    const CtaWork cw = cta_work<G>(p);
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Cfg::kRegsSoftmax) : "memory");
+    const CtaWork cw = cta_work<G, QT>(p);
     const SeqEntry se = cw.se;
     const int h = cw.h, q0 = cw.q0, nq0 = cw.nq0, nq1 = cw.nq1, nt0 = cw.nt0, nt1 = cw.nt1;
     const int Hq = p.g.q_heads;
-    const uint32_t tmem = ld_volatile_shared(sbase + kWsOffMisc);
+    const uint32_t tmem = ld_volatile_shared(sbase + ws_off_misc<QT>());
     const int w = warp >> 2;
     const int r = tid & 127;  // this thread's row = TMEM lane
     const int qw0 = q0 + w * TQ, nqw = w ? nq1 : nq0, ntw = w ? nt1 : nt0;
@@ -384,15 +407,15 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     const bool live = tq < nqw;
     const int qpos = se.base + qw0 + tq;
     const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const uint32_t s_col = static_cast<uint32_t>(w * kTileN), o_col = kWsOCol + w * kHeadDim,
-                   p_col = kWsPCol + w * (kTileN / 2);
+    const uint32_t s_col = static_cast<uint32_t>(w * kTileN), o_col = Cfg::kOCol + w * kHeadDim,
+                   p_col = Cfg::kPCol + w * (kTileN / 2);
     if (ntw > 0) {
       // Q rows: RoPE at the token's position, scaled into the exp2 domain,
       // bf16; rows past the tile's tokens are zero. A warp writes its 32 TMEM
       // rows one row per step: lane l holds elements 2l, 2l+1 (one RoPE pair),
       // so each row is one coalesced 256-byte load (and one of the RoPE
       // table), and the lanes' 4-byte results fill the row's swizzled line.
-      uint8_t* qt = sm + kWsOffQ + w * kTileBytes;
+      uint8_t* qt = sm + Cfg::kOffQ + w * kTileBytes;
       const int r0 = (warp & 3) * 32;
       float2 xv[32], cv[32];
 #pragma unroll
@@ -535,8 +558,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     }
     if (!ok) raise_abort();
   } else {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWsRegsProducer) : "memory");
-    const CtaWork cw = cta_work<G>(p);
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Cfg::kRegsProducer) : "memory");
+    const CtaWork cw = cta_work<G, QT>(p);
     const int warp = thread_index() >> 5, lane = thread_index() & 31;  // read again, as cw
     auto raise_abort = [&]() {
       if (lane == 0) {
@@ -546,17 +569,17 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     };
     const int h = cw.h, nt0 = cw.nt0, nt1 = cw.nt1, n_kv = cw.n_kv, n_load = cw.n_load;
     const int Hkv = p.g.kv_heads;
-    const uint32_t tmem = ld_volatile_shared(sbase + kWsOffMisc);
+    const uint32_t tmem = ld_volatile_shared(sbase + ws_off_misc<QT>());
     const int n_blocks = (n_kv + kBlockTokens - 1) / kBlockTokens;
     // Shared addresses are rederived from sb, made opaque once per tile, so
     // that they are not all held in registers across the loops.
     uint32_t sb = sbase;
-    auto pbar = [&](int i) { return sb + kWsOffBar + 8u * static_cast<uint32_t>(i); };
+    auto pbar = [&](int i) { return sb + Cfg::kOffBar + 8u * static_cast<uint32_t>(i); };
     auto pwait = [&](uint32_t b, uint32_t parity) {
       const bool ok = bar_wait_ab(b, parity, sb + abort_off);
       return __all_sync(0xffffffffu, ok);
     };
-    if (warp == 8) {
+    if (warp == kLoadWarp) {
       // ================= loader =================
       // K and V tile t -> stage t % 3: its 16-token blocks through the block
       // table, one lane per block (lanes 0-7); each lane loads the next tile's
@@ -590,7 +613,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         }
         if (lane == 0) bar_expect_tx(pbar(kBarKFull + st), bytes);
         __syncwarp();
-        if (lane < nb) tma_rows(sb + kWsOffK + off, &p.tmap_k, y, pbar(kBarKFull + st));
+        if (lane < nb) tma_rows(sb + Cfg::kOffK + off, &p.tmap_k, y, pbar(kBarKFull + st));
         __syncwarp();
         k_issued = t + 1;
         if (t >= kWsStages && !pwait(pbar(kBarVFree + st), free_parity)) {
@@ -599,7 +622,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         }
         if (lane == 0) bar_expect_tx(pbar(kBarVFull + st), bytes);
         __syncwarp();
-        if (lane < nb) tma_rows(sb + kWsOffV + off, &p.tmap_v, y, pbar(kBarVFull + st));
+        if (lane < nb) tma_rows(sb + Cfg::kOffV + off, &p.tmap_v, y, pbar(kBarVFull + st));
         __syncwarp();
         v_issued = t + 1;
       }
@@ -612,7 +635,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       for (int t = max(0, v_issued - kWsStages); t < v_issued; ++t)
         bar_wait(pbar(kBarVFull + t % kWsStages), (t / kWsStages) & 1);
       __syncwarp();
-    } else if (warp == 9 || warp == 10) {
+    } else if (warp == kSWarp || warp == kPvWarp) {
       // ============ MMA issue: warp 9 the S products, warp 10 the P V products ============
       // (lane 0 issues; the warp waits together). Two issuers, so that the
       // next S of one query tile never queues behind the other tile's P V.
@@ -620,8 +643,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       constexpr uint32_t kIdPV = idesc(kTileM, kHeadDim, true);
       auto issue_s = [&](int w, int t) {  // S_w = Q_w K_t^T
         if (lane == 0) {
-          const uint32_t kaddr = sb + kWsOffK + (t % kWsStages) * kTileBytes;
-          const uint32_t qaddr = sb + kWsOffQ + w * kTileBytes;
+          const uint32_t kaddr = sb + Cfg::kOffK + (t % kWsStages) * kTileBytes;
+          const uint32_t qaddr = sb + Cfg::kOffQ + w * kTileBytes;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             mma_f16(tmem + w * kTileN, sdesc(qaddr + 32 * kk, 1, 64), sdesc(kaddr + 32 * kk, 1, 64),
@@ -631,10 +654,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       };
       auto issue_pv = [&](int w, int t) {  // O_w += P_w V_t, P_w from TMEM
         if (lane == 0) {
-          const uint32_t vaddr = sb + kWsOffV + (t % kWsStages) * kTileBytes;
+          const uint32_t vaddr = sb + Cfg::kOffV + (t % kWsStages) * kTileBytes;
 #pragma unroll
           for (int kk = 0; kk < kTileN / 16; ++kk)  // 16 tokens = 8 P columns a step
-            mma_f16_ts(tmem + kWsOCol + w * kHeadDim, tmem + kWsPCol + w * (kTileN / 2) + 8 * kk,
+            mma_f16_ts(tmem + Cfg::kOCol + w * kHeadDim, tmem + Cfg::kPCol + w * (kTileN / 2) + 8 * kk,
                        sdesc(vaddr + 2048 * kk, kTileBytes >> 4, 64), kIdPV, (t > 0 || kk > 0) ? 1 : 0);
           mma_commit(pbar(kBarODone + w));
         }
@@ -648,7 +671,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         if (!pwait(pbar(kBarVFull + t % kWsStages), (t / kWsStages) & 1)) return false;
         const int valid = n_kv - t * kTileN;
         if (valid < kTileN) {
-          uint8_t* vt = sm + kWsOffV + (t % kWsStages) * kTileBytes;
+          uint8_t* vt = sm + Cfg::kOffV + (t % kWsStages) * kTileBytes;
           // row t of a swizzled tile is the 128 bytes at t*128 (units permuted)
           for (int i = valid * 8 + lane; i < kTileN * 8; i += 32)
             *reinterpret_cast<uint4*>(vt + (i >> 3) * 128 + (i & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
@@ -658,7 +681,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
         return true;
       };
       bool ok = true;
-      if (warp == 9) {
+      if (warp == kSWarp) {
         ok = pwait(pbar(kBarQFull + 0), 0) && (nt1 == 0 || pwait(pbar(kBarQFull + 1), 0));
         for (int j = 0; ok && j < n_load; ++j) {
           sb = opaque(sb);
@@ -711,18 +734,18 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       }
       if (!ok) raise_abort();
       // every MMA this warp issued completes before TMEM is released
-      commit_to(kBarDrain + (warp - 9));
-      bar_wait(pbar(kBarDrain + (warp - 9)), 0);
+      commit_to(kBarDrain + (warp - kSWarp));
+      bar_wait(pbar(kBarDrain + (warp - kSWarp)), 0);
       __syncwarp();
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 9)
+  if (warp == kSWarp)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(
-                     ld_volatile_shared(sbase + kWsOffMisc)),
-                 "r"(kWsTmemCols)
+                     ld_volatile_shared(sbase + ws_off_misc<QT>())),
+                 "r"(Cfg::kTmemCols)
                  : "memory");
 }
 
@@ -735,8 +758,9 @@ bool prefill_tc_supported(const PrefillLaunch& p) {
 
 cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s) {
   if (p.n_seq <= 0 || p.max_count <= 0) return cudaSuccess;
+  using Cfg = WsCfg<kPrefillQT>;
   const int G = p.g.q_heads / p.g.kv_heads;
-  const int tq = 2 * (kTileM / G);  // two query tiles per CTA
+  const int tq = kPrefillQT * (kTileM / G);  // new tokens per CTA
   const dim3 grid((p.max_count + tq - 1) / tq, p.n_seq, p.g.kv_heads);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -749,19 +773,20 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s) {
       cudaFuncAttributes fa{};
       cudaError_t a = cudaFuncGetAttributes(&fa, kernel);
       if (a != cudaSuccess) return a;
-      if (fa.numRegs < kWsRegsLaunch) return cudaErrorInvalidConfiguration;
-      a = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemWs);
+      if (fa.numRegs < Cfg::kRegsLaunch) return cudaErrorInvalidConfiguration;
+      a = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               ws_smem<kPrefillQT>());
       if (a != cudaSuccess) return a;
       configured[gi] |= (1ull << dev);
     }
-    kernel<<<grid, kWsThreads, kSmemWs, s>>>(p);
+    kernel<<<grid, Cfg::kThreads, ws_smem<kPrefillQT>(), s>>>(p);
     return cudaGetLastError();
   };
   switch (G) {
-    case 1: return run(prefill_ws_kernel<1>, 0);
-    case 2: return run(prefill_ws_kernel<2>, 1);
-    case 4: return run(prefill_ws_kernel<4>, 2);
-    case 8: return run(prefill_ws_kernel<8>, 3);
+    case 1: return run(prefill_ws_kernel<1, kPrefillQT>, 0);
+    case 2: return run(prefill_ws_kernel<2, kPrefillQT>, 1);
+    case 4: return run(prefill_ws_kernel<4, kPrefillQT>, 2);
+    case 8: return run(prefill_ws_kernel<8, kPrefillQT>, 3);
     default: return cudaErrorInvalidValue;
   }
 }
