@@ -175,6 +175,26 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Three-input max (sm_100): fewer instructions for a row's max.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// Two f32 lanes in one 64-bit register, for the packed f32x2 arithmetic.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {  // two IEEE adds, rounded to nearest
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 // MMA operands (Q, P) to bf16, round to nearest even, one instruction per pair.
 __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
   uint32_t r;
@@ -477,14 +497,16 @@ __global__ void __launch_bounds__(WsCfg<QT>::kThreads, WsCfg<QT>::kCtasPerSm)
         }
       }
       float mx;
-      {  // eight independent chains instead of one 128-long dependency chain
+      {  // eight independent chains of three-input maxes (16 scores each)
         float m8[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) m8[k] = s[k];
+        for (int k = 0; k < 8; ++k) {
+          float m = fmax3(s[16 * k], s[16 * k + 1], s[16 * k + 2]);
 #pragma unroll
-        for (int i = 8; i < kTileN; ++i) m8[i & 7] = fmaxf(m8[i & 7], s[i]);
-        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+          for (int i = 3; i < 15; i += 2) m = fmax3(m, s[16 * k + i], s[16 * k + i + 1]);
+          m8[k] = fmaxf(m, s[16 * k + 15]);
+        }
+        mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       }
       // The running max moves only when the row's max grows by more than 2^8.
       const bool grow = mx > m_used + 8.f;
@@ -493,16 +515,24 @@ __global__ void __launch_bounds__(WsCfg<QT>::kThreads, WsCfg<QT>::kCtasPerSm)
         corr = ex2(m_used - mx);  // 0 on the first tile
         m_used = mx;
       }
-      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
+      // x - m and the row sum two lanes at a time (f32x2), four partial sums
+      const uint64_t neg_m = pack2(-m_used, -m_used);
+      uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};  // +0.0f in both lanes
       uint32_t pw[kTileN / 2];  // P row, bf16 pairs
 #pragma unroll
       for (int i = 0; i < kTileN / 2; ++i) {
-        const float a = ex2(s[2 * i] - m_used), b = ex2(s[2 * i + 1] - m_used);
-        ps8[i & 7] += a + b;
+        float xa, xb;
+        unpack2(add2(pack2(s[2 * i], s[2 * i + 1]), neg_m), xa, xb);
+        const float a = ex2(xa), b = ex2(xb);
+        ps2[i & 3] = add2(ps2[i & 3], pack2(a, b));
         pw[i] = bf16x2(a, b);
       }
-      const float psum =
-          ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+      float psum;
+      {
+        float l0, h0;
+        unpack2(add2(add2(ps2[0], ps2[1]), add2(ps2[2], ps2[3])), l0, h0);
+        psum = l0 + h0;
+      }
       l_sum = fmaf(l_sum, corr, psum);
       // ---- P_{j-1} V done: P_w and O_w are free ---------------------------------
       if (j > 0) {
