@@ -329,16 +329,19 @@ __device__ __forceinline__ int thread_index() {
 }
 template <int G, int QT>
 __device__ __forceinline__ CtaWork cta_work(const PrefillLaunch& p) {
-  uint32_t bx, by, bz, nbx;
+  // Grid (KV head, sequence, query-tile rank): blocks start in that linear
+  // order, so the query tiles furthest into the prompts (the most K/V tiles)
+  // of every sequence and head start first and the short ones fill the tail.
+  uint32_t bx, by, bz, nbz;
   asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(bx));
   asm volatile("mov.u32 %0, %%ctaid.y;" : "=r"(by));
   asm volatile("mov.u32 %0, %%ctaid.z;" : "=r"(bz));
-  asm volatile("mov.u32 %0, %%nctaid.x;" : "=r"(nbx));
+  asm volatile("mov.u32 %0, %%nctaid.z;" : "=r"(nbz));
   constexpr int TQ = kTileM / G;
   CtaWork c;
   c.se = p.seqs[by];
-  c.h = static_cast<int>(bz);
-  c.q0 = (static_cast<int>(nbx) - 1 - static_cast<int>(bx)) * QT * TQ;  // long tiles first
+  c.h = static_cast<int>(bx);
+  c.q0 = (static_cast<int>(nbz) - 1 - static_cast<int>(bz)) * QT * TQ;
   c.nq0 = min(TQ, c.se.count - c.q0);
   c.nq1 = QT == 2 ? max(0, min(TQ, c.se.count - c.q0 - TQ)) : 0;
   c.nt0 = (c.se.base + c.q0 + c.nq0 - 1) / kTileN + 1;
@@ -791,7 +794,9 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s) {
   using Cfg = WsCfg<kPrefillQT>;
   const int G = p.g.q_heads / p.g.kv_heads;
   const int tq = kPrefillQT * (kTileM / G);  // new tokens per CTA
-  const dim3 grid((p.max_count + tq - 1) / tq, p.n_seq, p.g.kv_heads);
+  const int n_tiles = (p.max_count + tq - 1) / tq;
+  if (n_tiles > 65535 || p.n_seq > 65535) return cudaErrorInvalidConfiguration;  // grid y/z limits
+  const dim3 grid(p.g.kv_heads, p.n_seq, n_tiles);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
