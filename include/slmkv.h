@@ -289,6 +289,52 @@ slm_status slm_decode_attention_noalloc(const float* d_key_pool, const float* d_
                                         int32_t n, const float* d_query, float* d_out,
                                         slm_stream stream);
 
+/* ---- full-model steps (SmallLMModel, model.rs) ------------------------------
+ * The decoder-only model around the KV path: token embedding, per layer
+ * RMSNorm -> q/k/v projections -> the batch's cache step -> output projection
+ * + residual -> RMSNorm -> SiTU-GLU -> residual, then the final RMSNorm and
+ * the tied fp32 vocabulary projection. Projections take bf16-rounded
+ * operands with fp32 accumulation (linear.rs:44-107); the vocabulary
+ * projection is fp32 (linear.rs:119-152). */
+typedef struct slm_model slm_model;
+typedef struct slm_model_config {
+  int32_t vocab_size;        /* ModelConfig::vocab_size */
+  int32_t hidden_size;       /* ModelConfig::hidden_size = num_query_heads * head_dimension */
+  int32_t intermediate_size; /* ModelConfig::intermediate_size */
+  float rms_norm_epsilon;    /* ModelConfig::rms_norm_epsilon */
+  float situ_beta_gate;      /* ModelConfig::situ_beta_gate */
+  float situ_beta_up;        /* ModelConfig::situ_beta_up */
+} slm_model_config;
+/* Layers, heads, head dimension and RoPE come from the context's config.
+ * `h_tensors` are host fp32 arrays in the reference layout ([out, in]
+ * matrices), 2 + 9 * num_layers of them in the order of weights.rs:347-375:
+ * token_embedding [vocab, hidden]; per layer attention_norm [hidden],
+ * q_proj [hidden, hidden], k_proj [kv, hidden], v_proj [kv, hidden],
+ * o_proj [hidden, hidden], ffn_norm [hidden], gate_proj [inter, hidden],
+ * up_proj [inter, hidden], down_proj [hidden, inter]; final_norm [hidden]
+ * (kv = num_key_value_heads * head_dimension). Projection matrices are stored
+ * on the device rounded to bf16 (the rounding linear.rs applies to them at
+ * every call); the embedding and the norms stay fp32. */
+slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config,
+                            const float* const* h_tensors, int32_t n_tensors, slm_model** out);
+slm_status slm_model_destroy(slm_model* model);
+/* One cached decode step (model.rs:342-397) for every sequence of an open
+ * batch whose token counts are all 1: d_token_ids [n] (device int32) are
+ * embedded and run through every layer (the batch's decode step per layer);
+ * d_logits [n, vocab] (device, may be NULL) and d_next_token [n] (device,
+ * the first maximal logit, greedy.rs; may be NULL). A token id outside the
+ * vocabulary or non-finite logits make the batch's end report
+ * SLM_ERR_INVALID_INPUT and roll the step back (model.rs:390-396). */
+slm_status slm_model_decode(slm_model* model, slm_batch* batch, const int32_t* d_token_ids,
+                            float* d_logits, int32_t* d_next_token);
+/* Prompt prefill (model.rs:297-330) for every sequence of an open batch:
+ * d_token_ids [sum(counts)] (device int32, the batch's tokens in batch order;
+ * token j of sequence i is at position base_i + j). Only each sequence's last
+ * position is projected to the vocabulary: d_logits [n, vocab] (may be NULL)
+ * and d_next_token [n] (may be NULL). */
+slm_status slm_model_prefill(slm_model* model, slm_batch* batch, const int32_t* d_token_ids,
+                             float* d_logits, int32_t* d_next_token);
+
 #ifdef __cplusplus
 }
 #endif

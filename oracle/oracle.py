@@ -3,7 +3,9 @@
 TEST INFRASTRUCTURE ONLY: a restatement of small-lm-rs's CPU arithmetic
 (``rust/engine/src/{kv_cache,rope,softmax,attention,linear}.rs``), used by the
 tests, the smoke check and the bench's CPU-baseline leg as the checker. The
-CUDA library and its Python mirror never import this module.
+CUDA library and its Python mirror never import this module. The model-level
+functions follow ``rmsnorm.rs``, ``situ_glu.rs``, ``embedding.rs``,
+``greedy.rs``, ``transformer.rs`` and ``model.rs``.
 
 Each method names the reference lines that the C function restates; see
 ``slm_oracle.c`` for the line-by-line restatement.
@@ -78,6 +80,18 @@ def lib() -> C.CDLL:
             "orc_linear": (C.c_int, [_f32p, i64, i64, _f32p, i64, _f32p, i32]),
             "orc_linear_fp32": (C.c_int, [_f32p, i64, i64, _f32p, i64, _f32p, i32]),
             "orc_max_threads": (i32, []),
+            "orc_rmsnorm_rows": (C.c_int, [_f32p, i64, i64, _f32p, C.c_float, _f32p]),
+            "orc_situ_gate_activation": (C.c_float, [C.c_float, C.c_float]),
+            "orc_situ_up_activation": (C.c_float, [C.c_float, C.c_float]),
+            "orc_situ_glu": (C.c_int, [_f32p, i64, i64, i64, _f32p, _f32p, _f32p, C.c_float,
+                                       C.c_float, _f32p, i32]),
+            "orc_embedding_lookup": (C.c_int, [C.POINTER(C.c_uint32), i64, _f32p, i64, i64,
+                                               _f32p]),
+            "orc_argmax_finite": (C.c_int, [_f32p, i64, C.POINTER(C.c_uint32)]),
+            "orc_model_tensor_count": (i32, [i32]),
+            "orc_model_prefill": (C.c_int, [vp, C.POINTER(_f32p), vp, C.POINTER(C.c_uint32),
+                                            i64, _f32p, i32]),
+            "orc_model_decode": (C.c_int, [vp, C.POINTER(_f32p), vp, C.c_uint32, _f32p, i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -341,3 +355,94 @@ def forward_cached_attention_batch(caches, layer, query, key, value, q_heads, in
                                                     _p(f32(inv_freq)), _p(out), threads),
            "forward_cached_attention_batch")
     return out
+
+
+# --- model level ------------------------------------------------------------
+
+def rmsnorm_rows(x, rows: int, hidden: int, weight, epsilon: float) -> np.ndarray:
+    """rmsnorm.rs:80-91"""
+    out = np.zeros(rows * hidden, np.float32)
+    _check(lib().orc_rmsnorm_rows(_p(f32(x)), rows, hidden, _p(f32(weight)), epsilon, _p(out)),
+           "rmsnorm")
+    return out
+
+
+def situ_gate_activation(v: float, beta_gate: float) -> float:
+    """situ_glu.rs:59-62 with the sigmoid of :131-138"""
+    return float(lib().orc_situ_gate_activation(float(v), float(beta_gate)))
+
+
+def situ_up_activation(v: float, beta_up: float) -> float:
+    """situ_glu.rs:64-67"""
+    return float(lib().orc_situ_up_activation(float(v), float(beta_up)))
+
+
+def situ_glu(x, rows, hidden, intermediate, gate_w, up_w, down_w, beta_gate, beta_up,
+             threads=1) -> np.ndarray:
+    """situ_glu.rs:80-128"""
+    out = np.zeros(rows * hidden, np.float32)
+    _check(lib().orc_situ_glu(_p(f32(x)), rows, hidden, intermediate, _p(f32(gate_w)),
+                              _p(f32(up_w)), _p(f32(down_w)), beta_gate, beta_up, _p(out),
+                              threads), "situ_glu")
+    return out
+
+
+def embedding_lookup(token_ids, table, vocab: int, hidden: int) -> np.ndarray:
+    """embedding.rs:15-56"""
+    ids = np.ascontiguousarray(np.asarray(token_ids, dtype=np.uint32))
+    out = np.zeros(ids.size * hidden, np.float32)
+    _check(lib().orc_embedding_lookup(ids.ctypes.data_as(C.POINTER(C.c_uint32)), ids.size,
+                                      _p(f32(table)), vocab, hidden, _p(out)), "embedding")
+    return out
+
+
+def argmax_finite(logits) -> int:
+    """greedy.rs argmax_finite: the first maximum; empty or non-finite fails."""
+    a = f32(logits)
+    out = C.c_uint32(0)
+    _check(lib().orc_argmax_finite(_p(a), a.size, C.byref(out)), "argmax")
+    return int(out.value)
+
+
+class _ModelConfig(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("vocab_size", "hidden_size", "intermediate_size",
+                                         "num_layers", "num_query_heads",
+                                         "num_key_value_heads", "head_dimension")] + \
+               [(n, C.c_float) for n in ("rms_norm_epsilon", "rope_theta", "situ_beta_gate",
+                                         "situ_beta_up")]
+
+
+class Model:
+    """The decoder-only model (model.rs) over fp32 tensors in the reference
+    layout, in the order of ``orc_model_tensor_count``: token_embedding; per
+    layer attention_norm, q, k, v, o, ffn_norm, gate, up, down; final_norm."""
+
+    def __init__(self, cfg: dict, tensors):
+        self.cfg = dict(cfg)
+        n = lib().orc_model_tensor_count(cfg["num_layers"])
+        if len(tensors) != n:
+            raise OracleError(ERR_INVALID_INPUT, f"model wants {n} tensors")
+        self._keep = [f32(t) for t in tensors]
+        self._arr = (_f32p * n)(*[_p(t) for t in self._keep])
+        self._c = _ModelConfig(**{k: cfg[k] for k, _ in _ModelConfig._fields_})
+
+    def new_cache(self, max_sequence_length: int, quantize_bf16=False) -> DenseCache:
+        c = self.cfg
+        return DenseCache(c["num_layers"], max_sequence_length, c["num_key_value_heads"],
+                          c["head_dimension"], quantize_bf16)
+
+    def prefill(self, cache: DenseCache, token_ids, threads=1) -> np.ndarray:
+        """model.rs:297-330: logits [T, vocab]"""
+        ids = np.ascontiguousarray(np.asarray(token_ids, dtype=np.uint32))
+        out = np.zeros(ids.size * self.cfg["vocab_size"], np.float32)
+        _check(lib().orc_model_prefill(C.byref(self._c), self._arr, cache.handle,
+                                       ids.ctypes.data_as(C.POINTER(C.c_uint32)), ids.size,
+                                       _p(out), threads), "model_prefill")
+        return out.reshape(ids.size, self.cfg["vocab_size"])
+
+    def decode(self, cache: DenseCache, token_id: int, threads=1) -> np.ndarray:
+        """model.rs:342-397: logits [vocab]"""
+        out = np.zeros(self.cfg["vocab_size"], np.float32)
+        _check(lib().orc_model_decode(C.byref(self._c), self._arr, cache.handle,
+                                      int(token_id), _p(out), threads), "model_decode")
+        return out

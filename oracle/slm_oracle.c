@@ -542,3 +542,208 @@ int32_t orc_max_threads(void) {
   return 1;
 #endif
 }
+
+/* ---- model-level functions -------------------------------------------- */
+
+/* rmsnorm.rs:80-91 */
+int orc_rmsnorm_rows(const float* input, int64_t rows, int64_t hidden,
+                     const float* weight, float epsilon, float* out) {
+  if (rows <= 0 || hidden <= 0) return ORC_ERR_INVALID_INPUT;
+  const float width = (float)hidden;
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* x = input + r * hidden;
+    float square_sum = 0.0f;
+    for (int64_t i = 0; i < hidden; ++i) square_sum = fmaf(x[i], x[i], square_sum);
+    const float inverse_rms = 1.0f / sqrtf(square_sum / width + epsilon);
+    for (int64_t i = 0; i < hidden; ++i) out[r * hidden + i] = x[i] * inverse_rms * weight[i];
+  }
+  return ORC_OK;
+}
+
+/* situ_glu.rs:131-138 */
+static float orc_sigmoid(float value) {
+  if (value >= 0.0f) return 1.0f / (1.0f + expf(-value));
+  const float e = expf(value);
+  return e / (1.0f + e);
+}
+/* situ_glu.rs:59-62 */
+float orc_situ_gate_activation(float value, float beta_gate) {
+  return beta_gate * tanhf(value / beta_gate) * orc_sigmoid(value);
+}
+/* situ_glu.rs:64-67 */
+float orc_situ_up_activation(float value, float beta_up) {
+  return beta_up * tanhf(value / beta_up);
+}
+
+/* situ_glu.rs:80-128 */
+int orc_situ_glu(const float* input, int64_t rows, int64_t hidden,
+                 int64_t intermediate, const float* gate_weight,
+                 const float* up_weight, const float* down_weight,
+                 float beta_gate, float beta_up, float* out, int32_t threads) {
+  if (rows <= 0 || hidden <= 0 || intermediate <= 0) return ORC_ERR_INVALID_INPUT;
+  const size_t n = (size_t)(rows * intermediate);
+  float* gate = (float*)malloc(n * sizeof(float));
+  float* up = (float*)malloc(n * sizeof(float));
+  int rc = (gate && up) ? ORC_OK : ORC_ERR_INVALID_INPUT;
+  if (rc == ORC_OK) rc = orc_linear(input, rows, hidden, gate_weight, intermediate, gate, threads);
+  if (rc == ORC_OK) rc = orc_linear(input, rows, hidden, up_weight, intermediate, up, threads);
+  if (rc == ORC_OK) {
+    for (size_t i = 0; i < n; ++i)
+      gate[i] = orc_situ_gate_activation(gate[i], beta_gate) * orc_situ_up_activation(up[i], beta_up);
+    rc = orc_linear(gate, rows, intermediate, down_weight, hidden, out, threads);
+  }
+  free(gate);
+  free(up);
+  return rc;
+}
+
+/* embedding.rs:15-56 */
+int orc_embedding_lookup(const uint32_t* token_ids, int64_t n, const float* table,
+                         int64_t vocab, int64_t hidden, float* out) {
+  if (n <= 0 || vocab <= 0 || hidden <= 0) return ORC_ERR_INVALID_INPUT;
+  for (int64_t t = 0; t < n; ++t) {
+    if ((int64_t)token_ids[t] >= vocab) return ORC_ERR_INVALID_INPUT;
+    memcpy(out + t * hidden, table + (int64_t)token_ids[t] * hidden, (size_t)hidden * sizeof(float));
+  }
+  return ORC_OK;
+}
+
+/* greedy.rs: argmax_finite */
+int orc_argmax_finite(const float* logits, int64_t n, uint32_t* out) {
+  if (n <= 0) return ORC_ERR_INVALID_INPUT;
+  for (int64_t i = 0; i < n; ++i)
+    if (!isfinite(logits[i])) return ORC_ERR_INVALID_INPUT;
+  int64_t best = 0;
+  float best_value = logits[0];
+  for (int64_t i = 1; i < n; ++i)
+    if (logits[i] > best_value) {
+      best = i;
+      best_value = logits[i];
+    }
+  *out = (uint32_t)best;
+  return ORC_OK;
+}
+
+int32_t orc_model_tensor_count(int32_t num_layers) { return 2 + 9 * num_layers; }
+
+/* transformer.rs:183-204 (ffn_residual) and :296-311 (add_residual_in_place):
+ * x += down(situ(norm(x))). */
+static int orc_ffn_residual(const orc_model_config* cfg, const float* const* lt, float* x,
+                            int64_t rows, float* scratch_norm, float* scratch_out,
+                            int32_t threads) {
+  const int64_t H = cfg->hidden_size;
+  int rc = orc_rmsnorm_rows(x, rows, H, lt[5], cfg->rms_norm_epsilon, scratch_norm);
+  if (rc == ORC_OK)
+    rc = orc_situ_glu(scratch_norm, rows, H, cfg->intermediate_size, lt[6], lt[7], lt[8],
+                      cfg->situ_beta_gate, cfg->situ_beta_up, scratch_out, threads);
+  if (rc == ORC_OK)
+    for (int64_t i = 0; i < rows * H; ++i) x[i] += scratch_out[i];
+  return rc;
+}
+
+/* model.rs:206-227 (final norm) and :193-205 (tied fp32 vocabulary projection) */
+static int orc_final_logits(const orc_model_config* cfg, const float* const* tensors,
+                            const float* x, int64_t rows, float* scratch, float* logits,
+                            int32_t threads) {
+  const int64_t H = cfg->hidden_size;
+  int rc = orc_rmsnorm_rows(x, rows, H, tensors[1 + 9 * cfg->num_layers], cfg->rms_norm_epsilon,
+                            scratch);
+  if (rc == ORC_OK) rc = orc_linear_fp32(scratch, rows, H, tensors[0], cfg->vocab_size, logits, threads);
+  return rc;
+}
+
+int orc_model_prefill(const orc_model_config* cfg, const float* const* tensors,
+                      orc_cache* cache, const uint32_t* token_ids, int64_t tokens,
+                      float* logits, int32_t threads) {
+  if (!cfg || !tensors || !cache || tokens <= 0) return ORC_ERR_INVALID_INPUT;
+  if (!orc_cache_is_empty(cache)) return ORC_ERR_INVALID_INPUT;  /* model.rs:304-309 */
+  const int64_t H = cfg->hidden_size, KV = (int64_t)cfg->num_key_value_heads * cfg->head_dimension;
+  const int64_t I = cfg->intermediate_size, T = tokens;
+  const int32_t hq = cfg->num_query_heads, hkv = cfg->num_key_value_heads, d = cfg->head_dimension;
+  float inv_freq[256];
+  if (d > 512) return ORC_ERR_INVALID_INPUT;
+  int rc = orc_rope_inverse_frequencies(d, cfg->rope_theta, inv_freq);
+  float* x = (float*)malloc((size_t)(T * H) * sizeof(float));
+  float* xn = (float*)malloc((size_t)(T * H) * sizeof(float));
+  float* q = (float*)malloc((size_t)(T * H) * sizeof(float));
+  float* k = (float*)malloc((size_t)(T * KV) * sizeof(float));
+  float* v = (float*)malloc((size_t)(T * KV) * sizeof(float));
+  float* att = (float*)malloc((size_t)(T * H) * sizeof(float));
+  float* o = (float*)malloc((size_t)(T * (H > I ? H : I)) * sizeof(float));
+  float* probs = (float*)malloc((size_t)((int64_t)hq * T * T) * sizeof(float));
+  if (!x || !xn || !q || !k || !v || !att || !o || !probs) rc = ORC_ERR_INVALID_INPUT;
+  if (rc == ORC_OK) rc = orc_embedding_lookup(token_ids, T, tensors[0], cfg->vocab_size, H, x);
+  for (int32_t l = 0; rc == ORC_OK && l < cfg->num_layers; ++l) {
+    const float* const* lt = tensors + 1 + 9 * l;
+    rc = orc_rmsnorm_rows(x, T, H, lt[0], cfg->rms_norm_epsilon, xn);
+    if (rc == ORC_OK) rc = orc_linear(xn, T, H, lt[1], H, q, threads);
+    if (rc == ORC_OK) rc = orc_linear(xn, T, H, lt[2], KV, k, threads);
+    if (rc == ORC_OK) rc = orc_linear(xn, T, H, lt[3], KV, v, threads);
+    if (rc == ORC_OK) rc = orc_apply_rotary_with_offset(q, k, T, hq, hkv, d, inv_freq, 0);
+    if (rc == ORC_OK) rc = orc_causal_probabilities(q, k, T, hq, hkv, d, probs);
+    if (rc == ORC_OK) rc = orc_attend_values(probs, v, T, hq, hkv, d, att);
+    if (rc == ORC_OK) rc = orc_linear(att, T, H, lt[4], H, o, threads);
+    if (rc == ORC_OK) rc = orc_cache_append_layer(cache, l, k, v, T);  /* attention.rs:863-868 */
+    if (rc == ORC_OK)
+      for (int64_t i = 0; i < T * H; ++i) x[i] += o[i];
+    if (rc == ORC_OK) rc = orc_ffn_residual(cfg, lt, x, T, xn, o, threads);
+  }
+  if (rc == ORC_OK) rc = orc_final_logits(cfg, tensors, x, T, xn, logits, threads);
+  if (rc != ORC_OK) orc_cache_clear(cache);
+  free(x);
+  free(xn);
+  free(q);
+  free(k);
+  free(v);
+  free(att);
+  free(o);
+  free(probs);
+  return rc;
+}
+
+int orc_model_decode(const orc_model_config* cfg, const float* const* tensors,
+                     orc_cache* cache, uint32_t token_id, float* logits, int32_t threads) {
+  if (!cfg || !tensors || !cache) return ORC_ERR_INVALID_INPUT;
+  /* model.rs:344-364 */
+  if (!orc_cache_is_synchronized(cache) || orc_cache_sequence_length(cache) == 0 ||
+      orc_cache_remaining_capacity(cache) == 0)
+    return ORC_ERR_INVALID_INPUT;
+  const int64_t previous = orc_cache_sequence_length(cache);
+  const int64_t H = cfg->hidden_size, KV = (int64_t)cfg->num_key_value_heads * cfg->head_dimension;
+  const int64_t I = cfg->intermediate_size;
+  float inv_freq[256];
+  if (cfg->head_dimension > 512) return ORC_ERR_INVALID_INPUT;
+  int rc = orc_rope_inverse_frequencies(cfg->head_dimension, cfg->rope_theta, inv_freq);
+  float* x = (float*)malloc((size_t)H * sizeof(float));
+  float* xn = (float*)malloc((size_t)H * sizeof(float));
+  float* q = (float*)malloc((size_t)H * sizeof(float));
+  float* k = (float*)malloc((size_t)KV * sizeof(float));
+  float* v = (float*)malloc((size_t)KV * sizeof(float));
+  float* att = (float*)malloc((size_t)H * sizeof(float));
+  float* o = (float*)malloc((size_t)(H > I ? H : I) * sizeof(float));
+  if (!x || !xn || !q || !k || !v || !att || !o) rc = ORC_ERR_INVALID_INPUT;
+  if (rc == ORC_OK) rc = orc_embedding_lookup(&token_id, 1, tensors[0], cfg->vocab_size, H, x);
+  for (int32_t l = 0; rc == ORC_OK && l < cfg->num_layers; ++l) {
+    const float* const* lt = tensors + 1 + 9 * l;
+    rc = orc_rmsnorm_rows(x, 1, H, lt[0], cfg->rms_norm_epsilon, xn);
+    if (rc == ORC_OK) rc = orc_linear(xn, 1, H, lt[1], H, q, threads);
+    if (rc == ORC_OK) rc = orc_linear(xn, 1, H, lt[2], KV, k, threads);
+    if (rc == ORC_OK) rc = orc_linear(xn, 1, H, lt[3], KV, v, threads);
+    if (rc == ORC_OK)
+      rc = orc_forward_cached_attention(cache, l, q, k, v, cfg->num_query_heads, inv_freq, att);
+    if (rc == ORC_OK) rc = orc_linear(att, 1, H, lt[4], H, o, threads);
+    if (rc == ORC_OK)
+      for (int64_t i = 0; i < H; ++i) x[i] += o[i];
+    if (rc == ORC_OK) rc = orc_ffn_residual(cfg, lt, x, 1, xn, o, threads);
+  }
+  if (rc == ORC_OK) rc = orc_final_logits(cfg, tensors, x, 1, xn, logits, threads);
+  if (rc != ORC_OK) orc_cache_truncate_all(cache, previous);
+  free(x);
+  free(xn);
+  free(q);
+  free(k);
+  free(v);
+  free(att);
+  free(o);
+  return rc;
+}

@@ -127,6 +127,50 @@ int orc_linear_fp32(const float* input, int64_t rows, int64_t in_features,
 
 int32_t orc_max_threads(void);
 
+/* rmsnorm.rs:80-91: per row, square sum by fma fold, inv = 1/sqrt(s/w + eps),
+ * out = value * inv * scale (left to right). */
+int orc_rmsnorm_rows(const float* input, int64_t rows, int64_t hidden,
+                     const float* weight, float epsilon, float* out);
+/* situ_glu.rs:59-70 and the sign-branched sigmoid of :131-138 */
+float orc_situ_gate_activation(float value, float beta_gate);
+float orc_situ_up_activation(float value, float beta_up);
+/* situ_glu.rs:80-128: down(gate_act(gate(x)) * up_act(up(x))), bf16 linears */
+int orc_situ_glu(const float* input, int64_t rows, int64_t hidden,
+                 int64_t intermediate, const float* gate_weight,
+                 const float* up_weight, const float* down_weight,
+                 float beta_gate, float beta_up, float* out, int32_t threads);
+/* embedding.rs:15-56 */
+int orc_embedding_lookup(const uint32_t* token_ids, int64_t n,
+                         const float* table, int64_t vocab, int64_t hidden,
+                         float* out);
+/* greedy.rs: argmax_finite (first maximum wins; empty or non-finite fails) */
+int orc_argmax_finite(const float* logits, int64_t n, uint32_t* out);
+
+/* The decoder-only model (model.rs, transformer.rs). `tensors` are fp32
+ * arrays in the reference layout ([out, in] matrices), in this order:
+ * token_embedding [vocab, hidden]; per layer: attention_norm [hidden],
+ * q_proj [hidden, hidden], k_proj [kv, hidden], v_proj [kv, hidden],
+ * o_proj [hidden, hidden], ffn_norm [hidden], gate_proj [inter, hidden],
+ * up_proj [inter, hidden], down_proj [hidden, inter]; final_norm [hidden]
+ * (kv = kv_heads * head_dim; names as weights.rs:347-375). */
+typedef struct orc_model_config {
+  int32_t vocab_size, hidden_size, intermediate_size, num_layers;
+  int32_t num_query_heads, num_key_value_heads, head_dimension;
+  float rms_norm_epsilon, rope_theta, situ_beta_gate, situ_beta_up;
+} orc_model_config;
+int32_t orc_model_tensor_count(int32_t num_layers);
+/* model.rs:297-330 with transformer.rs:221-258 and attention.rs:835-870:
+ * prompt prefill into an empty cache; logits [tokens, vocab]. The cache is
+ * cleared on failure (model.rs:323-328). */
+int orc_model_prefill(const orc_model_config* cfg, const float* const* tensors,
+                      orc_cache* cache, const uint32_t* token_ids,
+                      int64_t tokens, float* logits, int32_t threads);
+/* model.rs:342-397 with transformer.rs:259-292 and attention.rs:772-825:
+ * one cached token; logits [vocab]. Rolled back on failure (model.rs:390-396). */
+int orc_model_decode(const orc_model_config* cfg, const float* const* tensors,
+                     orc_cache* cache, uint32_t token_id, float* logits,
+                     int32_t threads);
+
 #ifdef __cplusplus
 }
 #endif

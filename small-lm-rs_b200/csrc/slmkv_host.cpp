@@ -691,6 +691,12 @@ slm_status check_device_error(slm_ctx* c) {
       return fail(c, SLM_ERR_DEVICE_TIMEOUT, "device wait timed out (error word 0x%x)", e);
     if (e & kErrLayout)
       return fail(c, SLM_ERR_CUDA, "CUDA error: a kernel found its shared memory misaligned (0x%x)", e);
+    if (e & kErrBadToken)
+      return fail(c, SLM_ERR_INVALID_INPUT,
+                  "invalid input for embedding lookup: token id outside the vocabulary (0x%x)", e);
+    if (e & kErrLogits)
+      return fail(c, SLM_ERR_INVALID_INPUT,
+                  "invalid input for greedy decoding: final-position logits are not finite (0x%x)", e);
     return fail(c, SLM_ERR_INVALID_INPUT,
                 "invalid input for KV cache: block table held an out-of-pool id (0x%x)", e);
   }
@@ -783,6 +789,16 @@ namespace slmkv {
 // Records the message of a failed call made without a context; read back by
 // slm_last_error(NULL).
 void set_contextless_error(const std::string& message) { g_create_error = message; }
+
+BatchRows batch_rows(const slm_batch* b) {
+  return BatchRows{b->stream, static_cast<int32_t>(b->seq_ids.size()), b->total_tokens,
+                   b->counts.data(), b->dev.seqs};
+}
+slm_ctx* batch_ctx(const slm_batch* b) { return b->ctx; }
+int32_t* ctx_error_word(slm_ctx* c) { return c->d_error; }
+void ctx_count_launches(slm_ctx* c, int32_t n) { c->launches += n; }
+slm_status ctx_need_device(slm_ctx* c) { return need_device(c); }
+slm_status ctx_fail(slm_ctx* c, slm_status code, const char* msg) { return fail(c, code, "%s", msg); }
 }  // namespace slmkv
 
 // =============================================================================
@@ -1484,6 +1500,12 @@ void resolve_oldest(slm_ctx* ctx) {
     } else if (w & kErrLayout) {
       dev = SLM_ERR_CUDA;
       snprintf(buf, sizeof buf, "CUDA error: a kernel found its shared memory misaligned (0x%x)", w);
+    } else if (w & kErrBadToken) {
+      dev = SLM_ERR_INVALID_INPUT;  // embedding.rs:36-43
+      snprintf(buf, sizeof buf, "invalid input for embedding lookup: token id outside the vocabulary (0x%x)", w);
+    } else if (w & kErrLogits) {
+      dev = SLM_ERR_INVALID_INPUT;  // greedy.rs argmax_finite
+      snprintf(buf, sizeof buf, "invalid input for greedy decoding: final-position logits are not finite (0x%x)", w);
     } else {
       dev = SLM_ERR_INVALID_INPUT;
       snprintf(buf, sizeof buf,

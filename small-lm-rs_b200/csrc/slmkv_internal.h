@@ -7,6 +7,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "slmkv.h"
+
 namespace slmkv {
 
 constexpr int kBlockTokens = 16;  // tokens per physical block
@@ -69,7 +71,7 @@ struct CopyJob {
 enum : int32_t { kStatusNonFinite = 1 };
 // Device error word bits: a bounded wait expired; a block table held an id
 // outside the pool; a kernel found its shared-memory layout misaligned.
-enum : int32_t { kErrTimeout = 1, kErrBadBlock = 2, kErrLayout = 4 };
+enum : int32_t { kErrTimeout = 1, kErrBadBlock = 2, kErrLayout = 4, kErrBadToken = 8, kErrLogits = 16 };
 
 struct PoolGeom {
   void* k;                   // pool base (layer 0)
@@ -161,5 +163,22 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s);
 
 cudaError_t launch_apply_updates(const PoolGeom& g, const TableUpdate* updates, int32_t n_updates,
                                  const CopyJob* copies, int32_t n_copies, cudaStream_t s);
+
+// ---- the model step's view of a context and an open batch (slmkv_host.cpp) ----
+struct BatchRows {
+  cudaStream_t stream;
+  int32_t n_seq;
+  int32_t total_tokens;
+  const int32_t* counts;  // [n_seq], host
+  const SeqEntry* d_seqs; // [n_seq], device: row_offset, count, base per sequence
+};
+BatchRows batch_rows(const slm_batch* b);
+slm_ctx* batch_ctx(const slm_batch* b);
+int32_t* ctx_error_word(slm_ctx* c);
+void ctx_count_launches(slm_ctx* c, int32_t n);
+// Selects the context's device; SLM_ERR_NO_DEVICE for a host-only context.
+slm_status ctx_need_device(slm_ctx* c);
+// Sets the context's last error message and returns code.
+slm_status ctx_fail(slm_ctx* c, slm_status code, const char* msg);
 
 }  // namespace slmkv

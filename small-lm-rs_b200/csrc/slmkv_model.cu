@@ -1,0 +1,509 @@
+// Full-model steps around the KV path: SmallLMModel's cached decode
+// (model.rs:342-397) and prompt prefill (model.rs:297-330) with the
+// transformer block of transformer.rs:221-292, on the device.
+//
+// Per layer: RMSNorm (rmsnorm.rs:80-91) into bf16 rows -> q/k/v projections
+// -> the batch's cache step (RoPE, append, attention: slmkv_kernels.cu) ->
+// output projection accumulated onto the residual -> RMSNorm -> gate/up
+// projections (one GEMM over the concatenated [gate; up] matrix) -> SiTU-GLU
+// activations (situ_glu.rs:59-70) into bf16 rows -> down projection
+// accumulated onto the residual. Then the final RMSNorm and the tied fp32
+// vocabulary projection (model.rs:193-227), and the first maximal logit
+// (greedy.rs argmax_finite).
+//
+// Projections follow linear.rs:44-107: both operands rounded to bf16 (the
+// weights once, at upload; the activations by the kernel that produces them,
+// round-to-nearest-even as linear.rs:14-23), products exact in fp32, fp32
+// accumulation. They are plain GEMMs and run in cuBLAS (bf16 inputs,
+// CUBLAS_COMPUTE_32F); the residual add is the GEMM's beta = 1, one rounding
+// of (x + dot) as the reference's `hidden += update`. The vocabulary
+// projection is an fp32 SGEMM (no TF32: the handle keeps the default math
+// mode), as linear.rs:119-152. Accumulation order differs from the
+// reference's sequential folds, which the 1e-4 logits tolerance covers.
+#include <cublas_v2.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "slmkv.h"
+#include "slmkv_internal.h"
+
+namespace slmkv {
+namespace {
+
+// embedding.rs:15-56: row r <- table[ids[r]]; an id outside the vocabulary
+// sets the context's error bit and reads row 0 (the step then fails).
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ table,
+                             int32_t vocab, int32_t hidden, float* __restrict__ x,
+                             int32_t* __restrict__ err) {
+  const int r = blockIdx.x;
+  int32_t id = ids[r];
+  if (static_cast<uint32_t>(id) >= static_cast<uint32_t>(vocab)) {
+    if (threadIdx.x == 0) atomicOr(err, kErrBadToken);
+    id = 0;
+  }
+  const float4* src = reinterpret_cast<const float4*>(table + static_cast<size_t>(id) * hidden);
+  float4* dst = reinterpret_cast<float4*>(x + static_cast<size_t>(r) * hidden);
+  for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// rmsnorm.rs:80-91, one warp per row: square sum (fma), inverse RMS
+// 1 / sqrt(s / width + eps), out = x * inv * scale (two products, in that
+// order). Output rows are bf16 (the next projection's rounded operand) or
+// fp32 (the vocabulary projection's). With `seqs`, output row i normalises
+// the last token row of sequence i (the prefill's final positions).
+__global__ void rmsnorm_kernel(const float* __restrict__ x, int32_t rows, int32_t hidden,
+                               const float* __restrict__ w, float eps,
+                               uint32_t* __restrict__ out_bf16, float* __restrict__ out_f32,
+                               const SeqEntry* __restrict__ seqs) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int src_row = seqs ? seqs[warp].row_offset + seqs[warp].count - 1 : warp;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(src_row) * hidden);
+  const int n4 = hidden / 4;
+  float s = 0.f;
+  for (int i = lane; i < n4; i += 32) {
+    const float4 v = xr[i];
+    s = fmaf(v.x, v.x, s);
+    s = fmaf(v.y, v.y, s);
+    s = fmaf(v.z, v.z, s);
+    s = fmaf(v.w, v.w, s);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float inv = 1.f / sqrtf(__fdiv_rn(s, static_cast<float>(hidden)) + eps);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  for (int i = lane; i < n4; i += 32) {
+    const float4 v = xr[i], g = wr[i];
+    const float a = __fmul_rn(__fmul_rn(v.x, inv), g.x), b = __fmul_rn(__fmul_rn(v.y, inv), g.y);
+    const float c = __fmul_rn(__fmul_rn(v.z, inv), g.z), d = __fmul_rn(__fmul_rn(v.w, inv), g.w);
+    if (out_bf16) {
+      reinterpret_cast<uint2*>(out_bf16 + static_cast<size_t>(warp) * (hidden / 2))[i] =
+          make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
+    } else {
+      reinterpret_cast<float4*>(out_f32 + static_cast<size_t>(warp) * hidden)[i] = make_float4(a, b, c, d);
+    }
+  }
+}
+
+// fp32 rows -> bf16 rows (round to nearest even), 4 values a thread.
+__global__ void round_bf16_kernel(const float4* __restrict__ in, size_t n4, uint2* __restrict__ out) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float4 v = in[i];
+    out[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
+}
+
+// situ_glu.rs:131-138
+__device__ __forceinline__ float situ_sigmoid(float v) {
+  if (v >= 0.f) return __fdiv_rn(1.f, 1.f + expf(-v));
+  const float e = expf(v);
+  return __fdiv_rn(e, 1.f + e);
+}
+// situ_glu.rs:59-70 and :101-107: h = gate_act(gate) * up_act(up), as bf16
+// (the down projection's rounded operand). gu rows are [gate | up].
+__global__ void situ_kernel(const float* __restrict__ gu, int32_t rows, int32_t inter, float beta_gate,
+                            float beta_up, uint32_t* __restrict__ h) {
+  const size_t pairs = static_cast<size_t>(rows) * (inter / 2);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < pairs;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t r = i / (inter / 2), c = 2 * (i % (inter / 2));
+    const float* row = gu + r * 2 * inter;
+    float out[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float g = row[c + k], u = row[inter + c + k];
+      const float ga = __fmul_rn(__fmul_rn(beta_gate, tanhf(__fdiv_rn(g, beta_gate))), situ_sigmoid(g));
+      const float ua = __fmul_rn(beta_up, tanhf(__fdiv_rn(u, beta_up)));
+      out[k] = __fmul_rn(ga, ua);
+    }
+    h[r * (inter / 2) + c / 2] = pack_bf16x2(out[0], out[1]);
+  }
+}
+
+// greedy.rs argmax_finite, one CTA per row: the first maximal logit; a
+// non-finite logit sets the context's error bit (the step then fails).
+constexpr int kArgmaxThreads = 256;
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits,
+                                                                int32_t vocab, int32_t* __restrict__ next,
+                                                                int32_t* __restrict__ err) {
+  const float* row = logits + static_cast<size_t>(blockIdx.x) * vocab;
+  float best = -INFINITY;
+  int32_t idx = 0x7fffffff;
+  bool bad = false;
+  for (int i = threadIdx.x; i < vocab; i += kArgmaxThreads) {
+    const float v = row[i];
+    if (!isfinite(v)) bad = true;
+    if (idx == 0x7fffffff || v > best) {  // strictly greater: the earlier index stays
+      best = v;
+      idx = i;
+    }
+  }
+  // (value, index) pairs: larger value wins, then the smaller index
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int32_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ob > best || (ob == best && oi < idx)) {
+      best = ob;
+      idx = oi;
+    }
+  }
+  __shared__ float sb[kArgmaxThreads / 32];
+  __shared__ int32_t si[kArgmaxThreads / 32];
+  const bool any_bad = __syncthreads_or(bad);
+  if ((threadIdx.x & 31) == 0) {
+    sb[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < kArgmaxThreads / 32; ++k)
+      if (sb[k] > best || (sb[k] == best && si[k] < idx)) {
+        best = sb[k];
+        idx = si[k];
+      }
+    if (any_bad) {
+      atomicOr(err, kErrLogits);
+      idx = 0;
+    }
+    next[blockIdx.x] = idx;
+  }
+}
+
+}  // namespace
+}  // namespace slmkv
+
+struct slm_model {
+  slm_ctx* ctx = nullptr;
+  int32_t V = 0, H = 0, I = 0, L = 0, KV = 0;
+  float eps = 0.f, beta_gate = 0.f, beta_up = 0.f;
+  cublasHandle_t blas = nullptr;
+  void* weights = nullptr;  // one device allocation for every tensor
+  const float* emb = nullptr;         // [V, H] fp32: lookup table and tied vocabulary projection
+  const float* final_norm = nullptr;  // [H]
+  struct Layer {
+    const float *attn_norm, *ffn_norm;                        // [H]
+    const __nv_bfloat16 *wq, *wk, *wv, *wo, *wgu, *wd;        // bf16, [out, in]; wgu = [gate; up]
+  };
+  std::vector<Layer> layers;
+  // scratch, grown on demand: rows for token rows, out rows for projected rows
+  int32_t rows_cap = 0, out_cap = 0;
+  float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *gu = nullptr;
+  uint32_t* xb = nullptr;  // bf16 pairs, [rows, max(H, I) / 2]
+  float *xf = nullptr, *logits = nullptr;
+};
+
+namespace slmkv {
+namespace {
+
+// linear.rs:14-23 on the bits (non-finite values keep their leading bits).
+uint16_t bf16_bits(float f) {
+  uint32_t b;
+  std::memcpy(&b, &f, 4);
+  if ((b & 0x7f800000u) == 0x7f800000u) return static_cast<uint16_t>((b & 0x007fffffu) ? 0x7fc0u : (b >> 16));
+  b += 0x7fffu + ((b >> 16) & 1u);
+  return static_cast<uint16_t>(b >> 16);
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+slm_status cuda_fail(slm_ctx* c, const char* what, cudaError_t e) {
+  std::string m = std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e);
+  return ctx_fail(c, SLM_ERR_CUDA, m.c_str());
+}
+slm_status blas_fail(slm_ctx* c, const char* what, cublasStatus_t e) {
+  std::string m = std::string("CUDA error in ") + what + ": cuBLAS status " + std::to_string(static_cast<int>(e));
+  return ctx_fail(c, SLM_ERR_CUDA, m.c_str());
+}
+
+void free_scratch(slm_model* m) {
+  for (void* p : {static_cast<void*>(m->x), static_cast<void*>(m->q), static_cast<void*>(m->k),
+                  static_cast<void*>(m->v), static_cast<void*>(m->att), static_cast<void*>(m->gu),
+                  static_cast<void*>(m->xb), static_cast<void*>(m->xf), static_cast<void*>(m->logits)})
+    if (p) cudaFree(p);
+  m->x = m->q = m->k = m->v = m->att = m->gu = m->xf = m->logits = nullptr;
+  m->xb = nullptr;
+  m->rows_cap = m->out_cap = 0;
+}
+
+// Scratch for `rows` token rows and `out_rows` projected rows (the stream
+// is synchronized before buffers are replaced).
+slm_status ensure_scratch(slm_model* m, int32_t rows, int32_t out_rows, cudaStream_t s) {
+  if (rows <= m->rows_cap && out_rows <= m->out_cap) return SLM_OK;
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(m->ctx, "slm_model step", e);
+  const int32_t r = std::max(rows, m->rows_cap), o = std::max(out_rows, m->out_cap);
+  free_scratch(m);
+  const size_t R = static_cast<size_t>(r), O = static_cast<size_t>(o);
+  const size_t wide = static_cast<size_t>(std::max(m->H, m->I));
+  struct A {
+    void** p;
+    size_t bytes;
+  } allocs[] = {{reinterpret_cast<void**>(&m->x), R * m->H * 4},
+                {reinterpret_cast<void**>(&m->q), R * m->H * 4},
+                {reinterpret_cast<void**>(&m->k), R * m->KV * 4},
+                {reinterpret_cast<void**>(&m->v), R * m->KV * 4},
+                {reinterpret_cast<void**>(&m->att), R * m->H * 4},
+                {reinterpret_cast<void**>(&m->gu), R * 2 * m->I * 4},
+                {reinterpret_cast<void**>(&m->xb), R * wide * 2},
+                {reinterpret_cast<void**>(&m->xf), O * m->H * 4},
+                {reinterpret_cast<void**>(&m->logits), O * m->V * 4}};
+  for (const A& a : allocs) {
+    e = cudaMalloc(a.p, a.bytes);
+    if (e != cudaSuccess) {
+      free_scratch(m);
+      return cuda_fail(m->ctx, "slm_model scratch allocation", e);
+    }
+  }
+  m->rows_cap = r;
+  m->out_cap = o;
+  return SLM_OK;
+}
+
+// y[rows, N] (+)= x[rows, K] . w[N, K]^T, bf16 operands, fp32 accumulation.
+cublasStatus_t gemm_bf16(cublasHandle_t h, const uint32_t* x, int32_t rows, int32_t K,
+                         const __nv_bfloat16* w, int32_t N, float* y, float beta) {
+  const float alpha = 1.f;
+  return cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, N, rows, K, &alpha, w, CUDA_R_16BF, K, x,
+                      CUDA_R_16BF, K, &beta, y, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+}
+
+int32_t grid_for(size_t work, int32_t threads) {
+  const size_t g = (work + threads - 1) / threads;
+  return static_cast<int32_t>(std::min<size_t>(std::max<size_t>(g, 1), 148 * 16));
+}
+
+// The layers and the vocabulary projection for `rows` token rows of the
+// open batch; `prefill` selects the append + prefill-attention cache step
+// and projects only each sequence's last row.
+slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32_t* ids, int32_t rows,
+                    bool prefill, float* logits, int32_t* next) {
+  const int32_t out_rows = prefill ? br.n_seq : rows;
+  slm_status rc = ensure_scratch(m, rows, out_rows, br.stream);
+  if (rc) return rc;
+  cudaStream_t s = br.stream;
+  cublasStatus_t bs = cublasSetStream(m->blas, s);
+  if (bs != CUBLAS_STATUS_SUCCESS) return blas_fail(m->ctx, "slm_model step", bs);
+  int32_t* err = ctx_error_word(m->ctx);
+  int32_t launches = 0;
+  const int32_t H = m->H, I = m->I, KV = m->KV;
+  const int32_t norm_grid = (rows + 3) / 4;  // 4 warps (rows) a CTA
+  embed_kernel<<<rows, 64, 0, s>>>(ids, m->emb, m->V, H, m->x, err);
+  ++launches;
+  for (int32_t l = 0; l < m->L; ++l) {
+    const slm_model::Layer& Ly = m->layers[l];
+    rmsnorm_kernel<<<norm_grid, 128, 0, s>>>(m->x, rows, H, Ly.attn_norm, m->eps, m->xb, nullptr, nullptr);
+    ++launches;
+    if ((bs = gemm_bf16(m->blas, m->xb, rows, H, Ly.wq, H, m->q, 0.f)) != CUBLAS_STATUS_SUCCESS ||
+        (bs = gemm_bf16(m->blas, m->xb, rows, H, Ly.wk, KV, m->k, 0.f)) != CUBLAS_STATUS_SUCCESS ||
+        (bs = gemm_bf16(m->blas, m->xb, rows, H, Ly.wv, KV, m->v, 0.f)) != CUBLAS_STATUS_SUCCESS)
+      return blas_fail(m->ctx, "slm_model q/k/v projection", bs);
+    if (prefill) {
+      rc = slm_batch_append_layer(b, l, m->k, m->v, 1);
+      if (!rc) rc = slm_batch_prefill_attention(b, l, m->q, 1, m->att);
+    } else {
+      rc = slm_batch_decode_layer(b, l, m->q, m->k, m->v, m->att);
+    }
+    if (rc) return rc;
+    const size_t n4 = static_cast<size_t>(rows) * H / 4;
+    round_bf16_kernel<<<grid_for(n4, 256), 256, 0, s>>>(reinterpret_cast<const float4*>(m->att), n4,
+                                                         reinterpret_cast<uint2*>(m->xb));
+    ++launches;
+    if ((bs = gemm_bf16(m->blas, m->xb, rows, H, Ly.wo, H, m->x, 1.f)) != CUBLAS_STATUS_SUCCESS)
+      return blas_fail(m->ctx, "slm_model output projection", bs);
+    rmsnorm_kernel<<<norm_grid, 128, 0, s>>>(m->x, rows, H, Ly.ffn_norm, m->eps, m->xb, nullptr, nullptr);
+    ++launches;
+    if ((bs = gemm_bf16(m->blas, m->xb, rows, H, Ly.wgu, 2 * I, m->gu, 0.f)) != CUBLAS_STATUS_SUCCESS)
+      return blas_fail(m->ctx, "slm_model gate/up projection", bs);
+    const size_t pairs = static_cast<size_t>(rows) * (I / 2);
+    situ_kernel<<<grid_for(pairs, 256), 256, 0, s>>>(m->gu, rows, I, m->beta_gate, m->beta_up, m->xb);
+    ++launches;
+    if ((bs = gemm_bf16(m->blas, m->xb, rows, I, Ly.wd, H, m->x, 1.f)) != CUBLAS_STATUS_SUCCESS)
+      return blas_fail(m->ctx, "slm_model down projection", bs);
+  }
+  if (logits || next) {
+    rmsnorm_kernel<<<(out_rows + 3) / 4, 128, 0, s>>>(m->x, out_rows, H, m->final_norm, m->eps, nullptr,
+                                                      m->xf, prefill ? br.d_seqs : nullptr);
+    ++launches;
+    float* lg = logits ? logits : m->logits;
+    const float one = 1.f, zero = 0.f;
+    bs = cublasSgemm(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, m->V, out_rows, H, &one, m->emb, H, m->xf, H, &zero,
+                     lg, m->V);
+    if (bs != CUBLAS_STATUS_SUCCESS) return blas_fail(m->ctx, "slm_model vocabulary projection", bs);
+    if (next) {
+      argmax_kernel<<<out_rows, kArgmaxThreads, 0, s>>>(lg, m->V, next, err);
+      ++launches;
+    }
+  }
+  ctx_count_launches(m->ctx, launches);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(m->ctx, "slm_model step", e);
+  return SLM_OK;
+}
+
+}  // namespace
+}  // namespace slmkv
+
+using namespace slmkv;
+
+extern "C" {
+
+slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const float* const* h_tensors,
+                            int32_t n_tensors, slm_model** out) {
+  if (!ctx || !config || !h_tensors || !out) return SLM_ERR_INVALID_INPUT;
+  *out = nullptr;
+  slm_config c{};
+  slm_status rc = slm_ctx_config(ctx, &c);
+  if (rc) return rc;
+  if ((rc = ctx_need_device(ctx))) return rc;
+  const int32_t V = config->vocab_size, H = config->hidden_size, I = config->intermediate_size;
+  const int32_t L = c.num_layers, KV = c.num_key_value_heads * c.head_dimension;
+  // config.rs:91-198 (the parts the device path relies on)
+  if (V <= 0 || H != c.num_query_heads * c.head_dimension || I <= 0 || I % 8 != 0)
+    return ctx_fail(ctx, SLM_ERR_INVALID_CONFIGURATION,
+                    "invalid model configuration: vocab > 0, hidden = query heads x head dimension, "
+                    "intermediate a positive multiple of 8");
+  if (!(config->rms_norm_epsilon > 0.f) || !std::isfinite(config->rms_norm_epsilon) ||
+      !std::isfinite(config->situ_beta_gate) || !std::isfinite(config->situ_beta_up) ||
+      config->situ_beta_gate == 0.f || config->situ_beta_up == 0.f)
+    return ctx_fail(ctx, SLM_ERR_INVALID_CONFIGURATION,
+                    "invalid model configuration: rms_norm_epsilon finite and > 0, SiTU betas finite "
+                    "and non-zero");
+  if (n_tensors != 2 + 9 * L)
+    return ctx_fail(ctx, SLM_ERR_INVALID_INPUT, "invalid input for model weights: 2 + 9 * layers tensors");
+  for (int32_t i = 0; i < n_tensors; ++i)
+    if (!h_tensors[i]) return ctx_fail(ctx, SLM_ERR_INVALID_INPUT, "invalid input for model weights: null tensor");
+
+  // One host image of the device allocation: fp32 embedding and norms,
+  // bf16 projection matrices ([gate; up] concatenated), 256-byte aligned.
+  const size_t HH = static_cast<size_t>(H) * H, KH = static_cast<size_t>(KV) * H,
+               IH = static_cast<size_t>(I) * H;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t o_emb = take(static_cast<size_t>(V) * H * 4), o_final = take(static_cast<size_t>(H) * 4);
+  struct LayerOff {
+    size_t an, fn, q, k, v, o, gu, d;
+  };
+  std::vector<LayerOff> lo(static_cast<size_t>(L));
+  for (auto& x : lo) {
+    x.an = take(static_cast<size_t>(H) * 4);
+    x.fn = take(static_cast<size_t>(H) * 4);
+    x.q = take(HH * 2);
+    x.k = take(KH * 2);
+    x.v = take(KH * 2);
+    x.o = take(HH * 2);
+    x.gu = take(2 * IH * 2);
+    x.d = take(IH * 2);
+  }
+  std::vector<uint8_t> img(off);
+  auto put_f32 = [&](size_t o, const float* src, size_t n) { std::memcpy(img.data() + o, src, n * 4); };
+  auto put_bf16 = [&](size_t o, const float* src, size_t n) {
+    uint16_t* d = reinterpret_cast<uint16_t*>(img.data() + o);
+    for (size_t i = 0; i < n; ++i) d[i] = bf16_bits(src[i]);
+  };
+  put_f32(o_emb, h_tensors[0], static_cast<size_t>(V) * H);
+  put_f32(o_final, h_tensors[1 + 9 * L], static_cast<size_t>(H));
+  for (int32_t l = 0; l < L; ++l) {
+    const float* const* t = h_tensors + 1 + 9 * l;
+    const LayerOff& x = lo[static_cast<size_t>(l)];
+    put_f32(x.an, t[0], static_cast<size_t>(H));
+    put_bf16(x.q, t[1], HH);
+    put_bf16(x.k, t[2], KH);
+    put_bf16(x.v, t[3], KH);
+    put_bf16(x.o, t[4], HH);
+    put_f32(x.fn, t[5], static_cast<size_t>(H));
+    put_bf16(x.gu, t[6], IH);           // gate rows first
+    put_bf16(x.gu + IH * 2, t[7], IH);  // then up
+    put_bf16(x.d, t[8], IH);
+  }
+  auto m = new slm_model();
+  m->ctx = ctx;
+  m->V = V;
+  m->H = H;
+  m->I = I;
+  m->L = L;
+  m->KV = KV;
+  m->eps = config->rms_norm_epsilon;
+  m->beta_gate = config->situ_beta_gate;
+  m->beta_up = config->situ_beta_up;
+  cudaError_t e = cudaMalloc(&m->weights, off);
+  if (e == cudaSuccess) e = cudaMemcpy(m->weights, img.data(), off, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    slm_model_destroy(m);
+    return cuda_fail(ctx, "slm_model_create", e);
+  }
+  const cublasStatus_t bs = cublasCreate(&m->blas);
+  if (bs != CUBLAS_STATUS_SUCCESS) {
+    m->blas = nullptr;
+    slm_model_destroy(m);
+    return blas_fail(ctx, "slm_model_create", bs);
+  }
+  cublasSetMathMode(m->blas, CUBLAS_DEFAULT_MATH);  // fp32 SGEMM without TF32
+  const uint8_t* base = static_cast<const uint8_t*>(m->weights);
+  m->emb = reinterpret_cast<const float*>(base + o_emb);
+  m->final_norm = reinterpret_cast<const float*>(base + o_final);
+  for (const LayerOff& x : lo) {
+    auto bf = [&](size_t o) { return reinterpret_cast<const __nv_bfloat16*>(base + o); };
+    m->layers.push_back(slm_model::Layer{reinterpret_cast<const float*>(base + x.an),
+                                         reinterpret_cast<const float*>(base + x.fn), bf(x.q), bf(x.k),
+                                         bf(x.v), bf(x.o), bf(x.gu), bf(x.d)});
+  }
+  *out = m;
+  return SLM_OK;
+}
+
+slm_status slm_model_destroy(slm_model* m) {
+  if (!m) return SLM_ERR_INVALID_INPUT;
+  free_scratch(m);
+  if (m->weights) cudaFree(m->weights);
+  if (m->blas) cublasDestroy(m->blas);
+  delete m;
+  return SLM_OK;
+}
+
+slm_status slm_model_decode(slm_model* m, slm_batch* b, const int32_t* d_token_ids, float* d_logits,
+                            int32_t* d_next_token) {
+  if (!m || !b || !d_token_ids) return SLM_ERR_INVALID_INPUT;
+  if (batch_ctx(b) != m->ctx)
+    return ctx_fail(m->ctx, SLM_ERR_INVALID_INPUT, "invalid input for model step: batch of another context");
+  slm_status rc = ctx_need_device(m->ctx);
+  if (rc) return rc;
+  const BatchRows br = batch_rows(b);
+  for (int32_t i = 0; i < br.n_seq; ++i)
+    if (br.counts[i] != 1)
+      return ctx_fail(m->ctx, SLM_ERR_INVALID_INPUT,
+                      "invalid input for model cached decode: one token per sequence (model.rs:342)");
+  if (br.n_seq == 0) return SLM_OK;
+  return run_step(m, b, br, d_token_ids, br.n_seq, false, d_logits, d_next_token);
+}
+
+slm_status slm_model_prefill(slm_model* m, slm_batch* b, const int32_t* d_token_ids, float* d_logits,
+                             int32_t* d_next_token) {
+  if (!m || !b || !d_token_ids) return SLM_ERR_INVALID_INPUT;
+  if (batch_ctx(b) != m->ctx)
+    return ctx_fail(m->ctx, SLM_ERR_INVALID_INPUT, "invalid input for model step: batch of another context");
+  slm_status rc = ctx_need_device(m->ctx);
+  if (rc) return rc;
+  const BatchRows br = batch_rows(b);
+  if (br.n_seq == 0 || br.total_tokens == 0) return SLM_OK;
+  return run_step(m, b, br, d_token_ids, br.total_tokens, true, d_logits, d_next_token);
+}
+
+}  // extern "C"

@@ -93,6 +93,14 @@ class SchedConfig(C.Structure):
     _fields_ = [("max_running", C.c_int32), ("max_prefill_tokens", C.c_int32)]
 
 
+class ModelConfig(C.Structure):
+    """slm_model_config: the model-only fields of ModelConfig (config.rs);
+    layers, heads, head dimension and RoPE come from the pool."""
+    _fields_ = [("vocab_size", C.c_int32), ("hidden_size", C.c_int32),
+                ("intermediate_size", C.c_int32), ("rms_norm_epsilon", C.c_float),
+                ("situ_beta_gate", C.c_float), ("situ_beta_up", C.c_float)]
+
+
 # Every symbol include/slmkv.h declares, with its ctypes signature.
 _i32, _i64, _u64, _vp = C.c_int32, C.c_int64, C.c_uint64, C.c_void_p
 _pi32 = C.POINTER(C.c_int32)
@@ -139,6 +147,11 @@ SIGNATURES = {
     "slm_sched_counts": (C.c_int, [_vp, _pi32, _pi32, C.POINTER(_i64), C.POINTER(_i64)]),
     "slm_decode_attention_noalloc": (
         C.c_int, [_vp, _vp, _i32, _i32, _i32, _pi32, _i32, _pi32, _i32, _vp, _vp, _vp]),
+    "slm_model_create": (C.c_int, [_vp, C.POINTER(ModelConfig), C.POINTER(_vp), _i32,
+                                   C.POINTER(_vp)]),
+    "slm_model_destroy": (C.c_int, [_vp]),
+    "slm_model_decode": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "slm_model_prefill": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
 }
 
 _lib = None
@@ -668,6 +681,88 @@ def decode_attention_noalloc(key_pool, value_pool, block_table, lengths, query, 
     if rc != OK:
         msg = (lib().slm_last_error(None) or b"").decode()
         raise _error_class(rc)(rc, msg)
+    return out
+
+
+def _ptr_i32(t) -> C.c_void_p:
+    """Device pointer of a contiguous CUDA int32 tensor (None -> NULL)."""
+    if t is None:
+        return C.c_void_p(0)
+    import torch
+
+    if not isinstance(t, torch.Tensor) or t.dtype != torch.int32 or not t.is_cuda \
+            or not t.is_contiguous():
+        raise InvalidInput(ERR_INVALID_INPUT,
+                           "invalid input for slmkv: token ids must be a contiguous CUDA int32 tensor")
+    return C.c_void_p(t.data_ptr())
+
+
+class Model:
+    """SmallLMModel (model.rs) on one pool's device: its cached decode step
+    and prompt prefill run through an open ``Batch`` of that pool.
+
+    ``tensors``: fp32 host arrays in the reference layout and order
+    (``MODEL_TENSOR_ORDER``): token_embedding; per layer attention_norm, q, k,
+    v, o, ffn_norm, gate, up, down; final_norm."""
+
+    def __init__(self, pool: KvPool, *, vocab_size: int, intermediate_size: int,
+                 tensors, rms_norm_epsilon: float = 1e-5, situ_beta_gate: float = 4.0,
+                 situ_beta_up: float = 25.0):
+        import numpy as np
+
+        self.pool = pool
+        self.vocab_size = vocab_size
+        cfg = ModelConfig(vocab_size, pool.q_heads * pool.head_dim, intermediate_size,
+                          rms_norm_epsilon, situ_beta_gate, situ_beta_up)
+        keep = [np.ascontiguousarray(np.asarray(t, dtype=np.float32)) for t in tensors]
+        arr = (_vp * len(keep))(*[C.c_void_p(a.ctypes.data) for a in keep])
+        h = _vp()
+        pool.check(lib().slm_model_create(pool.handle, C.byref(cfg), arr, len(keep), C.byref(h)))
+        self._h = h
+
+    def decode(self, batch: "Batch", token_ids, logits=None, next_tokens=None) -> None:
+        """model.rs:342-397 for every sequence of ``batch`` (counts 1):
+        token_ids [n] CUDA int32; logits [n, vocab] CUDA float32 and
+        next_tokens [n] CUDA int32 are optional outputs."""
+        self.pool.check(lib().slm_model_decode(self._h, batch._h, _ptr_i32(token_ids),
+                                               _ptr(logits), _ptr_i32(next_tokens)))
+
+    def prefill(self, batch: "Batch", token_ids, logits=None, next_tokens=None) -> None:
+        """model.rs:297-330 for every sequence of ``batch``: token_ids
+        [sum(counts)] in batch order; logits / next token of each sequence's
+        last position ([n, vocab], [n])."""
+        self.pool.check(lib().slm_model_prefill(self._h, batch._h, _ptr_i32(token_ids),
+                                                _ptr(logits), _ptr_i32(next_tokens)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None:
+            lib().slm_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+MODEL_TENSOR_ORDER = ("attention_norm", "q_proj", "k_proj", "v_proj", "o_proj", "ffn_norm",
+                      "gate_proj", "up_proj", "down_proj")
+
+
+def model_tensor_shapes(*, vocab_size: int, hidden_size: int, intermediate_size: int,
+                        num_layers: int, kv_width: int):
+    """Names and shapes in the order the model takes them (weights.rs:347-375)."""
+    out = [("token_embedding.weight", (vocab_size, hidden_size))]
+    for layer in range(num_layers):
+        shapes = {"attention_norm": (hidden_size,), "q_proj": (hidden_size, hidden_size),
+                  "k_proj": (kv_width, hidden_size), "v_proj": (kv_width, hidden_size),
+                  "o_proj": (hidden_size, hidden_size), "ffn_norm": (hidden_size,),
+                  "gate_proj": (intermediate_size, hidden_size),
+                  "up_proj": (intermediate_size, hidden_size),
+                  "down_proj": (hidden_size, intermediate_size)}
+        out += [(f"layers.{layer}.{n}.weight", shapes[n]) for n in MODEL_TENSOR_ORDER]
+    out.append(("final_norm.weight", (hidden_size,)))
     return out
 
 

@@ -1,0 +1,137 @@
+"""Full-model steps (slm_model_prefill / slm_model_decode) against the
+oracle's model (model.rs:297-397): a seeded random model in the reference
+layout, prompts of several lengths prefilled in one batch, then greedy decode
+steps for all of them in one batch per step.
+
+Logits are held to the reference's own GPU-versus-CPU logit parity
+thresholds (parity/runner.rs:33-43: max abs 0.1, mean abs 0.01, RMS 0.02,
+cosine >= 0.9999, top-1 agreement 1.0, the final next token exact), and
+every greedy token must be the oracle's. A tighter bound is not a property of
+this arithmetic: every projection rounds its input to bf16 (linear.rs), so a
+1-ulp fp32 difference upstream (another accumulation order in a GEMM, the
+RMSNorm reduction or the split-K attention, whose own outputs stay within
+1e-4) can move a bf16 operand by one bf16 ulp, which moves a logit by ~1e-3.
+Also: a token outside the vocabulary fails the step and rolls it back."""
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+slmkv = pytest.importorskip("slmkv")
+
+
+def random_model(seed, vocab, hidden, hkv, inter, layers, d=64):
+    rng = np.random.default_rng(seed)
+    kv = hkv * d
+    shapes = [(vocab, hidden)]
+    for _ in range(layers):
+        shapes += [(hidden,), (hidden, hidden), (kv, hidden), (kv, hidden), (hidden, hidden),
+                   (hidden,), (inter, hidden), (inter, hidden), (hidden, inter)]
+    shapes.append((hidden,))
+    # norms near 1, matrices N(0, 0.05^2) so the logits spread out
+    return [(1.0 + 0.05 * rng.standard_normal(s)).astype(np.float32) if len(s) == 1
+            else (0.05 * rng.standard_normal(s)).astype(np.float32) for s in shapes]
+
+
+def _run(kv_dtype, prompts, steps=4, seed=7):
+    vocab, hq, hkv, d, inter, layers = 1024, 4, 2, 64, 704, 2
+    hidden = hq * d
+    tensors = random_model(seed, vocab, hidden, hkv, inter, layers)
+    ocfg = dict(vocab_size=vocab, hidden_size=hidden, intermediate_size=inter, num_layers=layers,
+                num_query_heads=hq, num_key_value_heads=hkv, head_dimension=d,
+                rms_norm_epsilon=1e-5, rope_theta=10000.0, situ_beta_gate=4.0, situ_beta_up=25.0)
+    omodel = O.Model(ocfg, tensors)
+    ctx = 128
+    pool = slmkv.KvPool(num_layers=layers, num_query_heads=hq, num_key_value_heads=hkv,
+                        head_dimension=d, context_length=ctx, rope_theta=10000.0,
+                        num_blocks=len(prompts) * (ctx // 16) + 4, max_sequences=len(prompts),
+                        kv_dtype=kv_dtype, device=0)
+    pool.shuffle(seed)
+    model = slmkv.Model(pool, vocab_size=vocab, intermediate_size=inter, tensors=tensors)
+    caches = [pool.allocate_kv_cache(ctx) for _ in prompts]
+    ocaches = [omodel.new_cache(ctx, quantize_bf16=(kv_dtype == slmkv.KV_BF16)) for _ in prompts]
+    n = len(prompts)
+    ids = torch.tensor(np.concatenate(prompts), dtype=torch.int32, device="cuda:0")
+    logits = torch.empty((n, vocab), dtype=torch.float32, device="cuda:0")
+    nxt = torch.empty(n, dtype=torch.int32, device="cuda:0")
+    with pool.begin(caches, [len(p) for p in prompts]) as b:
+        model.prefill(b, ids, logits, nxt)
+    got_all, ref_all = [], []
+    ref = np.stack([omodel.prefill(oc, p)[-1] for oc, p in zip(ocaches, prompts)])
+    got_all.append(logits.cpu().numpy())
+    ref_all.append(ref)
+    tokens = nxt.cpu().numpy()
+    assert tokens.tolist() == [int(np.argmax(r)) for r in ref]
+    for _ in range(steps):
+        cur = torch.tensor(tokens, dtype=torch.int32, device="cuda:0")
+        with pool.begin(caches, 1) as b:
+            model.decode(b, cur, logits, nxt)
+        ref = np.stack([omodel.decode(oc, int(t)) for oc, t in zip(ocaches, tokens)])
+        got_all.append(logits.cpu().numpy())
+        ref_all.append(ref)
+        tokens = nxt.cpu().numpy()
+        assert tokens.tolist() == [int(np.argmax(r)) for r in ref]
+    assert [c.sequence_length() for c in caches] == [len(p) + steps for p in prompts]
+    model.close()
+    return parity_metrics(np.concatenate(got_all), np.concatenate(ref_all))
+
+
+def parity_metrics(got, ref):
+    """parity/metrics.rs: scalar errors, flattened cosine, per-row top-1."""
+    d = (got.astype(np.float64) - ref.astype(np.float64))
+    g, r = got.astype(np.float64).ravel(), ref.astype(np.float64).ravel()
+    return dict(max_abs=float(np.abs(d).max()), mean_abs=float(np.abs(d).mean()),
+                rms=float(np.sqrt((d * d).mean())),
+                cosine=float(g @ r / (np.linalg.norm(g) * np.linalg.norm(r))),
+                top1=float(np.mean(np.argmax(got, 1) == np.argmax(ref, 1))))
+
+
+def check_thresholds(m):
+    # parity/runner.rs:33-43 defaults
+    assert m["max_abs"] <= 0.1 and m["mean_abs"] <= 0.01 and m["rms"] <= 0.02, m
+    assert m["cosine"] >= 0.9999 and m["top1"] == 1.0, m
+
+
+PROMPTS = [np.array(p, np.uint32) for p in ([5, 900, 17, 3, 3], list(range(100, 117)),
+                                             [int(x) for x in np.arange(33) * 31 % 1024])]
+
+
+def test_model_prefill_and_decode_match_the_oracle_f32():
+    m = _run(slmkv.KV_F32, PROMPTS)
+    check_thresholds(m)
+    print("f32 KV logits vs oracle:", m)
+
+
+def test_model_prefill_and_decode_match_the_oracle_bf16():
+    m = _run(slmkv.KV_BF16, PROMPTS)
+    check_thresholds(m)
+    print("bf16 KV logits vs oracle:", m)
+
+
+def test_out_of_vocabulary_token_fails_and_rolls_back():
+    vocab, hq, hkv, d, inter, layers = 256, 4, 2, 64, 64, 1
+    tensors = random_model(3, vocab, hq * d, hkv, inter, layers)
+    pool = slmkv.KvPool(num_layers=layers, num_query_heads=hq, num_key_value_heads=hkv,
+                        head_dimension=d, context_length=64, num_blocks=16, max_sequences=2,
+                        device=0)
+    model = slmkv.Model(pool, vocab_size=vocab, intermediate_size=inter, tensors=tensors)
+    caches = [pool.allocate_kv_cache(64) for _ in range(2)]
+    with pool.begin(caches, [3, 4]) as b:
+        model.prefill(b, torch.tensor([1, 2, 3, 4, 5, 6, 7], dtype=torch.int32, device="cuda:0"))
+    b = pool.begin(caches, 1)
+    model.decode(b, torch.tensor([9, vocab], dtype=torch.int32, device="cuda:0"))
+    with pytest.raises(slmkv.InvalidInput) as e:
+        b.end()
+    assert "vocabulary" in str(e.value)
+    assert [c.sequence_length() for c in caches] == [3, 4]
+    # the context is still usable
+    nxt = torch.empty(2, dtype=torch.int32, device="cuda:0")
+    with pool.begin(caches, 1) as b:
+        model.decode(b, torch.tensor([9, 10], dtype=torch.int32, device="cuda:0"), None, nxt)
+    assert [c.sequence_length() for c in caches] == [4, 5]
+    assert all(0 <= t < vocab for t in nxt.cpu().tolist())
+    model.close()
