@@ -57,7 +57,12 @@ WORKLOADS = {
     "serve": dict(B=512, LEN_LO=8, LEN_HI=256, LAYERS=8, HQ=4, HKV=2, D=64, CTX=512, BF16=False),
     # prefix reuse: 64 requests, a shared 384-token prefix + 32 own tokens each
     "prefix": dict(B=64, LEN_LO=384, LEN_HI=32, LAYERS=8, HQ=4, HKV=2, D=64, CTX=512, BF16=False),
+    # the 8M model end to end: batch 1, a 64-token prompt, 448 greedy decode steps
+    "model": dict(B=1, LEN_LO=64, LEN_HI=448, LAYERS=8, HQ=4, HKV=2, D=64, CTX=512, BF16=False),
 }
+# the 8M model (artifacts/small-lm-8m/config.json): vocab 8192, hidden 256,
+# SiTU-GLU FFN 704, RMSNorm eps 1e-5, SiTU betas 4 / 25, tied embeddings
+MODEL_VOCAB, MODEL_INTER = 8192, 704
 PREFIX_DECODE_STEPS = 96
 # "serve": 4096 requests in total (shared by the ranks), Poisson arrivals at
 # SERVE_RATE requests/s (seeded), prompts U[8,256], outputs U[16,256], at
@@ -794,10 +799,166 @@ def run_prefix(args):
     pool.close()
 
 
+def model_tensors(seed: int):
+    """Random-init weights of the 8M model in the reference layout and order:
+    matrices and the embedding N(0, 0.02^2) (seeded), norms 1."""
+    import numpy as np
+
+    import slmkv
+
+    rng = np.random.default_rng(seed)
+    out = []
+    for _, shape in slmkv.model_tensor_shapes(vocab_size=MODEL_VOCAB, hidden_size=HQ * D,
+                                              intermediate_size=MODEL_INTER, num_layers=LAYERS,
+                                              kv_width=HKV * D):
+        out.append(np.ones(shape, np.float32) if len(shape) == 1
+                   else (0.02 * rng.standard_normal(shape)).astype(np.float32))
+    return out
+
+
+def model_cpu_baseline(tensors, prompt, threads: int, budget_s: float = 10.0):
+    """The oracle's model decode on the host cores: prefill the prompt, then
+    time greedy decode steps until about budget_s."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    cfg = dict(vocab_size=MODEL_VOCAB, hidden_size=HQ * D, intermediate_size=MODEL_INTER,
+               num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV, head_dimension=D,
+               rms_norm_epsilon=1e-5, rope_theta=10000.0, situ_beta_gate=4.0, situ_beta_up=25.0)
+    m = O.Model(cfg, tensors)
+    cache = m.new_cache(CTX)
+    tok = O.argmax_finite(m.prefill(cache, prompt, threads)[-1])
+    toks = []
+    n, t0 = 0, time.perf_counter()
+    while n < LEN_HI and (time.perf_counter() - t0) < budget_s:
+        toks.append(tok)
+        tok = O.argmax_finite(m.decode(cache, tok, threads))
+        n += 1
+    dt = time.perf_counter() - t0
+    return n / dt, n, toks
+
+
+def run_model(args):
+    """The 8M model end to end on one GPU: prefill a 64-token random prompt,
+    then greedy decode (one token per step, batch 1) through slm_model_decode;
+    each step's next token stays on the device and feeds the next step's
+    embedding. `value` is the decode steps per second with two steps in
+    flight; `e2e` copies each step's token from pinned host memory and reads
+    the chosen token back before the next step (a streaming server's loop)."""
+    import numpy as np
+    import torch
+
+    import slmkv
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    rng = np.random.default_rng(args.seed)
+    prompt = [int(x) for x in rng.integers(0, MODEL_VOCAB, size=LEN_LO)]
+    steps = min(max(args.steps, 1), LEN_HI)
+    tensors = model_tensors(args.seed)
+    pool = slmkv.KvPool(num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV,
+                        head_dimension=D, context_length=CTX, num_blocks=4 * (CTX // BLOCK) + 8,
+                        max_sequences=2, device=local)
+    model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=MODEL_INTER,
+                        tensors=tensors)
+    stream = torch.cuda.current_stream()
+    ids = torch.tensor(prompt, dtype=torch.int32, device=dev)
+    tok = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(2)]
+
+    def generate(n_steps, e2e=False):
+        cache = pool.allocate_kv_cache(CTX)
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        e[0].record(stream)
+        with pool.begin([cache], [LEN_LO]) as b:
+            model.prefill(b, ids, None, tok[0])
+        e[1].record(stream)
+        plan = pool.step_plan([cache], 1)
+        h_tok = torch.zeros(1, dtype=torch.int32).pin_memory()
+        out = []
+        if e2e:  # the prompt's own next token, streamed before the first step
+            h_tok.copy_(tok[0], non_blocking=True)
+            stream.synchronize()
+            out.append(int(h_tok[0]))
+        inflight = []
+        t_host = time.perf_counter()
+        for i in range(n_steps):
+            cur, nxt = tok[i % 2], tok[(i + 1) % 2]
+            if e2e:
+                cur.copy_(h_tok, non_blocking=True)
+            b = plan.begin()
+            model.decode(b, cur, None, nxt)
+            if e2e:
+                if b.end(raise_on_error=False) != [0]:
+                    raise RuntimeError("decode step failed")
+                h_tok.copy_(nxt, non_blocking=True)
+                stream.synchronize()
+                out.append(int(h_tok[0]))
+            else:
+                inflight.append(b.submit())
+                while len(inflight) > 1:
+                    if any(inflight.pop(0).wait(raise_on_error=False)):
+                        raise RuntimeError("decode step failed")
+        for b in inflight:
+            if any(b.wait(raise_on_error=False)):
+                raise RuntimeError("decode step failed")
+        e[2].record(stream)
+        torch.cuda.synchronize()
+        host_s = time.perf_counter() - t_host
+        if cache.sequence_length() != LEN_LO + n_steps:
+            raise RuntimeError(f"unexpected length {cache.sequence_length()}")
+        cache.free()
+        return e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2]), host_s, out
+
+    for _ in range(max(args.warmup, 3)):
+        generate(min(steps, 16))
+    l0 = pool.launch_count()
+    prefill_ms, decode_ms, _, _ = generate(steps)
+    launches = pool.launch_count() - l0
+    _, _, e2e_s, toks = generate(steps, e2e=True)
+    value = steps / (decode_ms / 1e3)
+    result = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": 1, "steps": steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": decode_ms / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": (f"8M model end to end: batch 1, {LEN_LO}-token random prompt, "
+                                f"{steps} greedy decode steps; {LAYERS} layers, hidden {HQ * D}, "
+                                f"FFN {MODEL_INTER} SiTU-GLU, Hq={HQ}, Hkv={HKV}, d={D}, "
+                                f"vocab {MODEL_VOCAB}, f32 KV, random N(0, 0.02^2) weights "
+                                f"(seed {args.seed})"), "name": "model", "seed": args.seed},
+        "prefill_ms": prefill_ms,
+        "e2e": {"value": steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4,
+                "loop": "pinned H2D of the step's token, decode, D2H of the chosen token, "
+                        "host synchronizes every step"},
+        "gpu_launches": launches,
+        "projections": "cuBLAS bf16 GEMM (fp32 accumulate) and fp32 SGEMM for the tied head; "
+                       "embedding, RMSNorm, SiTU, argmax and the KV step are this library's kernels",
+        "generated_head": toks[:8],
+    }
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle as O
+
+        threads = O.max_threads()
+        tps, n, cpu_toks = model_cpu_baseline(tensors, prompt, threads)
+        # both lists start with the prompt's own next token
+        result["greedy_tokens_match_cpu"] = cpu_toks[:n] == toks[:n]
+        result["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port",
+                                  "sample": f"{n} greedy decode steps of the same model and "
+                                            f"prompt (oracle, OpenMP projections, serial "
+                                            f"attention as the reference)"}
+    print(json.dumps(result), flush=True)
+    model.close()
+    pool.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif WORKLOAD_NAME == "model":
+        run_model(args)
     elif WORKLOAD_NAME == "serve":
         run_serve(args)
     elif WORKLOAD_NAME == "prefix":
