@@ -12,14 +12,17 @@
 // (greedy.rs argmax_finite).
 //
 // Projections follow linear.rs:44-107: both operands rounded to bf16 (the
-// weights once, at upload; the activations by the kernel that produces them,
-// round-to-nearest-even as linear.rs:14-23), products exact in fp32, fp32
-// accumulation. They are plain GEMMs and run in cuBLAS (bf16 inputs,
-// CUBLAS_COMPUTE_32F); the residual add is the GEMM's beta = 1, one rounding
-// of (x + dot) as the reference's `hidden += update`. The vocabulary
-// projection is an fp32 SGEMM (no TF32: the handle keeps the default math
-// mode), as linear.rs:119-152. Accumulation order differs from the
-// reference's sequential folds, which the 1e-4 logits tolerance covers.
+// weights once, at upload; the activations where they are produced or
+// staged, round-to-nearest-even as linear.rs:14-23), products exact in fp32,
+// fp32 accumulation. Up to kFusedRows token rows (decode steps, short
+// prompts) they are this file's fused kernels, whose every output is the
+// reference's own in-order fold, with the RMSNorm, the attention output's
+// rounding, SiTU-GLU and the residual add fused in (5 launches a layer with
+// the cache step). Beyond that (long prefills) they are tensor-core GEMMs in
+// cuBLAS (bf16 inputs, CUBLAS_COMPUTE_32F; the residual add as beta = 1),
+// whose accumulation order differs. The vocabulary projection is an fp32
+// SGEMM (no TF32: the handle keeps the default math mode), as
+// linear.rs:119-152.
 #include <cublas_v2.h>
 #include <cuda_bf16.h>
 
@@ -133,6 +136,224 @@ __global__ void situ_kernel(const float* __restrict__ gu, int32_t rows, int32_t 
   }
 }
 
+// ---- fused projections for up to kFusedRows token rows ------------------------
+// Each output is the reference's own fold: sum = fma(x_k, w_k, sum) from 0
+// over k in order (linear.rs:98-103), on bf16-rounded operands. A CTA stages
+// kProjRows input rows, already in their rounded form, in shared memory;
+// its 64 threads own 128 adjacent output columns (two each) and fold them for
+// all staged rows (2 x kProjRows independent chains). The weights ([in][out]
+// bf16 rows) stream through shared memory in 64-row chunks by cp.async, 128
+// KiB in flight a CTA, so the folds never wait on one global load at a time.
+//   kProjQKV   RMSNorm (attention_norm) fused in; writes q, k, v
+//   kProjO     the attention output rounded here; adds onto the residual
+//   kProjGU    RMSNorm (ffn_norm) fused in; gate and up columns j and I + j,
+//              SiTU-GLU applied, h written as bf16 (the down projection's operand)
+//   kProjDown  h as staged; adds onto the residual
+// The RMSNorm square sum is the reference's sequential fma fold as well (one
+// thread per staged row), so for f32 inputs the staged operands, and with
+// them the projections, reproduce the reference bit for bit.
+enum : int { kProjQKV = 0, kProjO = 1, kProjGU = 2, kProjDown = 3 };
+constexpr int kProjThreads = 64;   // two output columns each
+constexpr int kProjCols = 2 * kProjThreads;
+constexpr int kProjRows = 4;       // token rows a CTA
+constexpr int kProjChunk = 64;     // weight rows a stage
+constexpr int kFusedRows = 1024;   // above this, tensor-core GEMMs (cuBLAS)
+
+struct ProjArgs {
+  const float* x;               // QKV, GU: residual stream; O: attention output  [rows, K] fp32
+  const __nv_bfloat16* xh;      // Down: h  [rows, K] bf16
+  const float* norm_w;          // QKV, GU: RMSNorm scale [K]
+  float eps;
+  int32_t rows, K;
+  int32_t ncols;                // output columns this launch computes (QKV: H + 2KV; O, Down: H; GU: I)
+  const __nv_bfloat16* w;       // [K][ld] bf16
+  int32_t ld;
+  float* y0;                    // QKV: q; O, Down: residual (accumulated)
+  float* y1;                    // QKV: k
+  float* y2;                    // QKV: v
+  __nv_bfloat16* h;             // GU: [rows, I]
+  int32_t H, KV, I;
+  float beta_gate, beta_up;
+};
+
+template <int MODE>
+constexpr int proj_mats() {
+  return MODE == kProjGU ? 2 : 1;  // gate and up slices
+}
+// weight chunks in flight: 128 KiB of weights a CTA either way
+template <int MODE>
+constexpr int proj_stages() {
+  return proj_mats<MODE>() == 2 ? 4 : 8;
+}
+template <int MODE>
+size_t proj_smem(int32_t K) {  // enough for either row blocking
+  return static_cast<size_t>(kProjRows) * K * sizeof(float) +
+         static_cast<size_t>(proj_stages<MODE>()) * proj_mats<MODE>() * kProjChunk * kProjCols * 2;
+}
+
+__device__ __forceinline__ float situ_gate(float g, float beta_gate) {
+  return __fmul_rn(__fmul_rn(beta_gate, tanhf(__fdiv_rn(g, beta_gate))), situ_sigmoid(g));
+}
+__device__ __forceinline__ float situ_up(float u, float beta_up) {
+  return __fmul_rn(beta_up, tanhf(__fdiv_rn(u, beta_up)));
+}
+__device__ __forceinline__ float round_bf16(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// NR: token rows a CTA (1 for a single-row step, else kProjRows; the last
+// CTA may hold fewer).
+template <int MODE, int NR>
+__global__ void __launch_bounds__(kProjThreads) proj_kernel(const ProjArgs a) {
+  constexpr int NM = proj_mats<MODE>();
+  constexpr int S = proj_stages<MODE>();
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* xs = reinterpret_cast<float*>(smem);  // [kProjRows][K]
+  const int K = a.K;
+  __nv_bfloat16* wbuf = reinterpret_cast<__nv_bfloat16*>(smem + static_cast<size_t>(kProjRows) * K * 4);
+  __shared__ float inv_s[NR];
+  const int tid = threadIdx.x;
+  const int r0 = blockIdx.y * NR;
+  const int nr = min(NR, a.rows - r0);
+  const int c0 = blockIdx.x * kProjCols;  // first output column of the CTA
+  const int nchunks = (K + kProjChunk - 1) / kProjChunk;
+  // weight rows [k0, k0 + kProjChunk) x columns [c0, c0 + 128) (and the up
+  // columns I + c0 ...) into stage st, 16-byte copies; columns past ncols skip
+  static_assert(kProjCols / 8 == 16, "16 segments of 8 columns a weight row");
+  auto load_chunk = [&](int ch, int st) {
+    const int k0 = ch * kProjChunk, nk = min(kProjChunk, K - k0);
+#pragma unroll
+    for (int m = 0; m < NM; ++m) {
+      for (int i = tid; i < nk * 16; i += kProjThreads) {
+        const int kr = i >> 4, seg = i & 15;
+        const int col = c0 + 8 * seg;
+        if (col < a.ncols)
+          cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(
+                         wbuf + ((st * NM + m) * kProjChunk + kr) * kProjCols + 8 * seg)),
+                     a.w + static_cast<size_t>(k0 + kr) * a.ld + (m ? a.I : 0) + col);
+      }
+    }
+    cp_async_commit();
+  };
+  for (int ch = 0; ch < S && ch < nchunks; ++ch) load_chunk(ch, ch);
+  // the rows as they arrive (coalesced), then, for the normed modes, the
+  // reference's in-order square-sum fold over shared memory by one thread a
+  // row (rmsnorm.rs:80-91) and the scaling and bf16 rounding in place
+  for (int r = 0; r < nr; ++r) {
+    const size_t row = static_cast<size_t>(r0 + r) * K;
+    for (int k = tid; k < K; k += kProjThreads)
+      xs[r * K + k] = MODE == kProjDown ? __bfloat162float(a.xh[row + k]) : a.x[row + k];
+  }
+  if (MODE == kProjQKV || MODE == kProjGU) {
+    __syncthreads();
+    if (tid < nr) {
+      const float* xr = xs + tid * K;
+      float s = 0.f;
+#pragma unroll 8
+      for (int k = 0; k < K; ++k) s = fmaf(xr[k], xr[k], s);
+      inv_s[tid] = 1.f / sqrtf(__fdiv_rn(s, static_cast<float>(K)) + a.eps);
+    }
+    __syncthreads();
+    for (int r = 0; r < nr; ++r)
+      for (int k = tid; k < K; k += kProjThreads)
+        xs[r * K + k] = round_bf16(__fmul_rn(__fmul_rn(xs[r * K + k], inv_s[r]), a.norm_w[k]));
+  } else if (MODE == kProjO) {
+    for (int r = 0; r < nr; ++r)
+      for (int k = tid; k < K; k += kProjThreads) xs[r * K + k] = round_bf16(xs[r * K + k]);
+  }
+  const int c = c0 + 2 * tid;  // this thread's two columns
+  float acc[NR][2], acc_up[NR][2];
+#pragma unroll
+  for (int r = 0; r < NR; ++r) acc[r][0] = acc[r][1] = acc_up[r][0] = acc_up[r][1] = 0.f;
+  for (int ch = 0; ch < nchunks; ++ch) {
+    const int st = ch % S;
+    // chunk ch is complete once at most the S-1 groups issued after it are
+    // pending; near the end fewer follow, so wait for all
+    if (ch + S - 1 <= nchunks - 1) cp_async_wait<S - 1>();
+    else cp_async_wait<0>();
+    __syncthreads();  // chunk ch (and, the first time, the staged rows) visible
+    const int k0 = ch * kProjChunk, nk = min(kProjChunk, K - k0);
+    const uint32_t* wg = reinterpret_cast<const uint32_t*>(
+        wbuf + (static_cast<size_t>(st) * NM) * kProjChunk * kProjCols) + tid;  // bf16 pairs
+    const uint32_t* wu = wg + (NM > 1 ? kProjChunk * kProjCols / 2 : 0);
+    if (c < a.ncols) {
+      // groups of 8 k: every load of the group first, then the FMAs in k
+      // order (nk is a multiple of 8: K and the chunk are)
+      for (int kb = 0; kb < nk; kb += 8) {
+        uint32_t wv[8], wuv[8];
+        float xv[NR][8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          wv[j] = wg[(kb + j) * (kProjCols / 2)];
+          if (MODE == kProjGU) wuv[j] = wu[(kb + j) * (kProjCols / 2)];
+        }
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          if (NR == 1 || r < nr) {
+            const float4* xp = reinterpret_cast<const float4*>(xs + r * K + k0 + kb);
+            const float4 lo = xp[0], hi = xp[1];
+            xv[r][0] = lo.x, xv[r][1] = lo.y, xv[r][2] = lo.z, xv[r][3] = lo.w;
+            xv[r][4] = hi.x, xv[r][5] = hi.y, xv[r][6] = hi.z, xv[r][7] = hi.w;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float w0 = __uint_as_float(wv[j] << 16), w1 = __uint_as_float(wv[j] & 0xffff0000u);
+          float u0 = 0.f, u1 = 0.f;
+          if (MODE == kProjGU) {
+            u0 = __uint_as_float(wuv[j] << 16);
+            u1 = __uint_as_float(wuv[j] & 0xffff0000u);
+          }
+#pragma unroll
+          for (int r = 0; r < NR; ++r) {
+            if (NR == 1 || r < nr) {
+              acc[r][0] = fmaf(xv[r][j], w0, acc[r][0]);
+              acc[r][1] = fmaf(xv[r][j], w1, acc[r][1]);
+              if (MODE == kProjGU) {
+                acc_up[r][0] = fmaf(xv[r][j], u0, acc_up[r][0]);
+                acc_up[r][1] = fmaf(xv[r][j], u1, acc_up[r][1]);
+              }
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();  // stage st is read: chunk ch + S may overwrite it
+    if (ch + S < nchunks) load_chunk(ch + S, st);
+  }
+  if (c >= a.ncols) return;
+#pragma unroll
+  for (int r = 0; r < NR; ++r) {
+    if (r >= nr) break;
+    const size_t row = static_cast<size_t>(r0 + r);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int col = c + e;
+      if (MODE == kProjQKV) {
+        if (col < a.H) a.y0[row * a.H + col] = acc[r][e];
+        else if (col < a.H + a.KV) a.y1[row * a.KV + col - a.H] = acc[r][e];
+        else a.y2[row * a.KV + col - a.H - a.KV] = acc[r][e];
+      } else if (MODE == kProjGU) {
+        // situ_glu.rs:101-107
+        const float hv = __fmul_rn(situ_gate(acc[r][e], a.beta_gate), situ_up(acc_up[r][e], a.beta_up));
+        a.h[row * a.I + col] = __float2bfloat16_rn(hv);
+      } else {
+        // transformer.rs add_residual_in_place: hidden += update
+        float* y = a.y0 + row * a.ncols + col;
+        *y = __fadd_rn(*y, acc[r][e]);
+      }
+    }
+  }
+}
+
 // greedy.rs argmax_finite, one CTA per row: the first maximal logit; a
 // non-finite logit sets the context's error bit (the step then fails).
 constexpr int kArgmaxThreads = 256;
@@ -194,9 +415,11 @@ struct slm_model {
   void* weights = nullptr;  // one device allocation for every tensor
   const float* emb = nullptr;         // [V, H] fp32: lookup table and tied vocabulary projection
   const float* final_norm = nullptr;  // [H]
+  // Projection matrices bf16 and transposed ([in][out] rows): wqkv [H][H+2KV]
+  // (columns q | k | v), wo [H][H], wgu [H][2I] (columns gate | up), wd [I][H].
   struct Layer {
-    const float *attn_norm, *ffn_norm;                        // [H]
-    const __nv_bfloat16 *wq, *wk, *wv, *wo, *wgu, *wd;        // bf16, [out, in]; wgu = [gate; up]
+    const float *attn_norm, *ffn_norm;  // [H]
+    const __nv_bfloat16 *wqkv, *wo, *wgu, *wd;
   };
   std::vector<Layer> layers;
   // scratch, grown on demand: rows for token rows, out rows for projected rows
@@ -273,12 +496,13 @@ slm_status ensure_scratch(slm_model* m, int32_t rows, int32_t out_rows, cudaStre
   return SLM_OK;
 }
 
-// y[rows, N] (+)= x[rows, K] . w[N, K]^T, bf16 operands, fp32 accumulation.
-cublasStatus_t gemm_bf16(cublasHandle_t h, const uint32_t* x, int32_t rows, int32_t K,
-                         const __nv_bfloat16* w, int32_t N, float* y, float beta) {
+// y[rows, N] (+)= x[rows, K] . wT[K, col0 : col0 + N] (transposed bf16 weights
+// with row length ld, passed at col0), bf16 operands, fp32 accumulation.
+cublasStatus_t gemm_t(cublasHandle_t h, const void* x, int32_t rows, int32_t K, const __nv_bfloat16* wT,
+                      int32_t ld, int32_t N, float* y, float beta) {
   const float alpha = 1.f;
-  return cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, N, rows, K, &alpha, w, CUDA_R_16BF, K, x,
-                      CUDA_R_16BF, K, &beta, y, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+  return cublasGemmEx(h, CUBLAS_OP_N, CUBLAS_OP_N, N, rows, K, &alpha, wT, CUDA_R_16BF, ld, x, CUDA_R_16BF,
+                      K, &beta, y, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
 }
 
 int32_t grid_for(size_t work, int32_t threads) {
@@ -286,9 +510,21 @@ int32_t grid_for(size_t work, int32_t threads) {
   return static_cast<int32_t>(std::min<size_t>(std::max<size_t>(g, 1), 148 * 16));
 }
 
+template <int MODE>
+void launch_proj(const ProjArgs& a, cudaStream_t s) {
+  const int gx = (a.ncols + kProjCols - 1) / kProjCols;
+  if (a.rows == 1)
+    proj_kernel<MODE, 1><<<dim3(gx, 1), kProjThreads, proj_smem<MODE>(a.K), s>>>(a);
+  else
+    proj_kernel<MODE, kProjRows><<<dim3(gx, (a.rows + kProjRows - 1) / kProjRows), kProjThreads,
+                                   proj_smem<MODE>(a.K), s>>>(a);
+}
+
 // The layers and the vocabulary projection for `rows` token rows of the
 // open batch; `prefill` selects the append + prefill-attention cache step
-// and projects only each sequence's last row.
+// and projects only each sequence's last row. Up to kFusedRows rows the
+// projections are the fused kernels above (5 launches a layer with the cache
+// step); beyond, tensor-core GEMMs with separate norm / rounding / SiTU.
 slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32_t* ids, int32_t rows,
                     bool prefill, float* logits, int32_t* next) {
   const int32_t out_rows = prefill ? br.n_seq : rows;
@@ -300,38 +536,69 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
   int32_t* err = ctx_error_word(m->ctx);
   int32_t launches = 0;
   const int32_t H = m->H, I = m->I, KV = m->KV;
-  const int32_t norm_grid = (rows + 3) / 4;  // 4 warps (rows) a CTA
+  const bool fused = rows <= kFusedRows;
+  __nv_bfloat16* hb = reinterpret_cast<__nv_bfloat16*>(m->xb);
   embed_kernel<<<rows, 64, 0, s>>>(ids, m->emb, m->V, H, m->x, err);
   ++launches;
+  auto cache_step = [&](int32_t l) {
+    if (prefill) {
+      slm_status r = slm_batch_append_layer(b, l, m->k, m->v, 1);
+      return r ? r : slm_batch_prefill_attention(b, l, m->q, 1, m->att);
+    }
+    return slm_batch_decode_layer(b, l, m->q, m->k, m->v, m->att);
+  };
   for (int32_t l = 0; l < m->L; ++l) {
     const slm_model::Layer& Ly = m->layers[l];
+    if (fused) {
+      ProjArgs a{};
+      a.eps = m->eps;
+      a.rows = rows;
+      a.H = H;
+      a.KV = KV;
+      a.I = I;
+      a.beta_gate = m->beta_gate;
+      a.beta_up = m->beta_up;
+      ProjArgs q = a;  // q, k, v with the attention RMSNorm
+      q.x = m->x, q.norm_w = Ly.attn_norm, q.K = H, q.ncols = H + 2 * KV, q.w = Ly.wqkv, q.ld = H + 2 * KV;
+      q.y0 = m->q, q.y1 = m->k, q.y2 = m->v;
+      launch_proj<kProjQKV>(q, s);
+      if ((rc = cache_step(l))) return rc;
+      ProjArgs o = a;  // output projection onto the residual
+      o.x = m->att, o.K = H, o.ncols = H, o.w = Ly.wo, o.ld = H, o.y0 = m->x;
+      launch_proj<kProjO>(o, s);
+      ProjArgs g = a;  // gate / up with the FFN RMSNorm, SiTU-GLU
+      g.x = m->x, g.norm_w = Ly.ffn_norm, g.K = H, g.ncols = I, g.w = Ly.wgu, g.ld = 2 * I, g.h = hb;
+      launch_proj<kProjGU>(g, s);
+      ProjArgs d = a;  // down projection onto the residual
+      d.xh = hb, d.K = I, d.ncols = H, d.w = Ly.wd, d.ld = H, d.y0 = m->x;
+      launch_proj<kProjDown>(d, s);
+      launches += 4;
+      continue;
+    }
+    const int32_t norm_grid = (rows + 3) / 4;  // 4 warps (rows) a CTA
+    const int32_t nqkv = H + 2 * KV;
     rmsnorm_kernel<<<norm_grid, 128, 0, s>>>(m->x, rows, H, Ly.attn_norm, m->eps, m->xb, nullptr, nullptr);
     ++launches;
-    if ((bs = gemm_bf16(m->blas, m->xb, rows, H, Ly.wq, H, m->q, 0.f)) != CUBLAS_STATUS_SUCCESS ||
-        (bs = gemm_bf16(m->blas, m->xb, rows, H, Ly.wk, KV, m->k, 0.f)) != CUBLAS_STATUS_SUCCESS ||
-        (bs = gemm_bf16(m->blas, m->xb, rows, H, Ly.wv, KV, m->v, 0.f)) != CUBLAS_STATUS_SUCCESS)
+    if ((bs = gemm_t(m->blas, m->xb, rows, H, Ly.wqkv, nqkv, H, m->q, 0.f)) != CUBLAS_STATUS_SUCCESS ||
+        (bs = gemm_t(m->blas, m->xb, rows, H, Ly.wqkv + H, nqkv, KV, m->k, 0.f)) != CUBLAS_STATUS_SUCCESS ||
+        (bs = gemm_t(m->blas, m->xb, rows, H, Ly.wqkv + H + KV, nqkv, KV, m->v, 0.f)) !=
+            CUBLAS_STATUS_SUCCESS)
       return blas_fail(m->ctx, "slm_model q/k/v projection", bs);
-    if (prefill) {
-      rc = slm_batch_append_layer(b, l, m->k, m->v, 1);
-      if (!rc) rc = slm_batch_prefill_attention(b, l, m->q, 1, m->att);
-    } else {
-      rc = slm_batch_decode_layer(b, l, m->q, m->k, m->v, m->att);
-    }
-    if (rc) return rc;
+    if ((rc = cache_step(l))) return rc;
     const size_t n4 = static_cast<size_t>(rows) * H / 4;
     round_bf16_kernel<<<grid_for(n4, 256), 256, 0, s>>>(reinterpret_cast<const float4*>(m->att), n4,
                                                          reinterpret_cast<uint2*>(m->xb));
     ++launches;
-    if ((bs = gemm_bf16(m->blas, m->xb, rows, H, Ly.wo, H, m->x, 1.f)) != CUBLAS_STATUS_SUCCESS)
+    if ((bs = gemm_t(m->blas, m->xb, rows, H, Ly.wo, H, H, m->x, 1.f)) != CUBLAS_STATUS_SUCCESS)
       return blas_fail(m->ctx, "slm_model output projection", bs);
     rmsnorm_kernel<<<norm_grid, 128, 0, s>>>(m->x, rows, H, Ly.ffn_norm, m->eps, m->xb, nullptr, nullptr);
     ++launches;
-    if ((bs = gemm_bf16(m->blas, m->xb, rows, H, Ly.wgu, 2 * I, m->gu, 0.f)) != CUBLAS_STATUS_SUCCESS)
+    if ((bs = gemm_t(m->blas, m->xb, rows, H, Ly.wgu, 2 * I, 2 * I, m->gu, 0.f)) != CUBLAS_STATUS_SUCCESS)
       return blas_fail(m->ctx, "slm_model gate/up projection", bs);
     const size_t pairs = static_cast<size_t>(rows) * (I / 2);
     situ_kernel<<<grid_for(pairs, 256), 256, 0, s>>>(m->gu, rows, I, m->beta_gate, m->beta_up, m->xb);
     ++launches;
-    if ((bs = gemm_bf16(m->blas, m->xb, rows, I, Ly.wd, H, m->x, 1.f)) != CUBLAS_STATUS_SUCCESS)
+    if ((bs = gemm_t(m->blas, m->xb, rows, I, Ly.wd, H, H, m->x, 1.f)) != CUBLAS_STATUS_SUCCESS)
       return blas_fail(m->ctx, "slm_model down projection", bs);
   }
   if (logits || next) {
@@ -399,39 +666,43 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
   };
   const size_t o_emb = take(static_cast<size_t>(V) * H * 4), o_final = take(static_cast<size_t>(H) * 4);
   struct LayerOff {
-    size_t an, fn, q, k, v, o, gu, d;
+    size_t an, fn, qkv, o, gu, d;
   };
   std::vector<LayerOff> lo(static_cast<size_t>(L));
   for (auto& x : lo) {
     x.an = take(static_cast<size_t>(H) * 4);
     x.fn = take(static_cast<size_t>(H) * 4);
-    x.q = take(HH * 2);
-    x.k = take(KH * 2);
-    x.v = take(KH * 2);
+    x.qkv = take((HH + 2 * KH) * 2);
     x.o = take(HH * 2);
     x.gu = take(2 * IH * 2);
     x.d = take(IH * 2);
   }
   std::vector<uint8_t> img(off);
   auto put_f32 = [&](size_t o, const float* src, size_t n) { std::memcpy(img.data() + o, src, n * 4); };
-  auto put_bf16 = [&](size_t o, const float* src, size_t n) {
+  // src [rows][cols] (the reference's [out][in]) into columns [col0, col0 +
+  // rows) of a transposed [cols][ld] bf16 matrix at byte offset o
+  auto put_bf16_t = [&](size_t o, const float* src, int32_t rows, int32_t cols, int32_t ld,
+                        int32_t col0) {
     uint16_t* d = reinterpret_cast<uint16_t*>(img.data() + o);
-    for (size_t i = 0; i < n; ++i) d[i] = bf16_bits(src[i]);
+    for (int32_t r = 0; r < rows; ++r)
+      for (int32_t c2 = 0; c2 < cols; ++c2)
+        d[static_cast<size_t>(c2) * ld + col0 + r] = bf16_bits(src[static_cast<size_t>(r) * cols + c2]);
   };
   put_f32(o_emb, h_tensors[0], static_cast<size_t>(V) * H);
   put_f32(o_final, h_tensors[1 + 9 * L], static_cast<size_t>(H));
   for (int32_t l = 0; l < L; ++l) {
     const float* const* t = h_tensors + 1 + 9 * l;
     const LayerOff& x = lo[static_cast<size_t>(l)];
+    const int32_t nqkv = H + 2 * KV;
     put_f32(x.an, t[0], static_cast<size_t>(H));
-    put_bf16(x.q, t[1], HH);
-    put_bf16(x.k, t[2], KH);
-    put_bf16(x.v, t[3], KH);
-    put_bf16(x.o, t[4], HH);
+    put_bf16_t(x.qkv, t[1], H, H, nqkv, 0);
+    put_bf16_t(x.qkv, t[2], KV, H, nqkv, H);
+    put_bf16_t(x.qkv, t[3], KV, H, nqkv, H + KV);
+    put_bf16_t(x.o, t[4], H, H, H, 0);
     put_f32(x.fn, t[5], static_cast<size_t>(H));
-    put_bf16(x.gu, t[6], IH);           // gate rows first
-    put_bf16(x.gu + IH * 2, t[7], IH);  // then up
-    put_bf16(x.d, t[8], IH);
+    put_bf16_t(x.gu, t[6], I, H, 2 * I, 0);  // gate columns first
+    put_bf16_t(x.gu, t[7], I, H, 2 * I, I);  // then up
+    put_bf16_t(x.d, t[8], H, I, H, 0);
   }
   auto m = new slm_model();
   m->ctx = ctx;
@@ -456,14 +727,34 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
     return blas_fail(ctx, "slm_model_create", bs);
   }
   cublasSetMathMode(m->blas, CUBLAS_DEFAULT_MATH);  // fp32 SGEMM without TF32
+  // the fused projections stage kProjRows input rows and two weight chunks
+  {
+    auto attr = [&](auto kernel, size_t bytes) {
+      return bytes > 48 * 1024 ? cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      static_cast<int>(bytes))
+                               : cudaSuccess;
+    };
+    cudaError_t a = attr(proj_kernel<kProjQKV, 1>, proj_smem<kProjQKV>(H));
+    if (a == cudaSuccess) a = attr(proj_kernel<kProjO, 1>, proj_smem<kProjO>(H));
+    if (a == cudaSuccess) a = attr(proj_kernel<kProjGU, 1>, proj_smem<kProjGU>(H));
+    if (a == cudaSuccess) a = attr(proj_kernel<kProjDown, 1>, proj_smem<kProjDown>(I));
+    if (a == cudaSuccess) a = attr(proj_kernel<kProjQKV, kProjRows>, proj_smem<kProjQKV>(H));
+    if (a == cudaSuccess) a = attr(proj_kernel<kProjO, kProjRows>, proj_smem<kProjO>(H));
+    if (a == cudaSuccess) a = attr(proj_kernel<kProjGU, kProjRows>, proj_smem<kProjGU>(H));
+    if (a == cudaSuccess) a = attr(proj_kernel<kProjDown, kProjRows>, proj_smem<kProjDown>(I));
+    if (a != cudaSuccess) {
+      slm_model_destroy(m);
+      return cuda_fail(ctx, "slm_model_create", a);
+    }
+  }
   const uint8_t* base = static_cast<const uint8_t*>(m->weights);
   m->emb = reinterpret_cast<const float*>(base + o_emb);
   m->final_norm = reinterpret_cast<const float*>(base + o_final);
   for (const LayerOff& x : lo) {
     auto bf = [&](size_t o) { return reinterpret_cast<const __nv_bfloat16*>(base + o); };
     m->layers.push_back(slm_model::Layer{reinterpret_cast<const float*>(base + x.an),
-                                         reinterpret_cast<const float*>(base + x.fn), bf(x.q), bf(x.k),
-                                         bf(x.v), bf(x.o), bf(x.gu), bf(x.d)});
+                                         reinterpret_cast<const float*>(base + x.fn), bf(x.qkv), bf(x.o),
+                                         bf(x.gu), bf(x.d)});
   }
   *out = m;
   return SLM_OK;

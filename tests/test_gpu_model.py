@@ -37,7 +37,7 @@ def random_model(seed, vocab, hidden, hkv, inter, layers, d=64):
             else (0.05 * rng.standard_normal(s)).astype(np.float32) for s in shapes]
 
 
-def _run(kv_dtype, prompts, steps=4, seed=7):
+def _run(kv_dtype, prompts, steps=4, seed=7, ctx=128):
     vocab, hq, hkv, d, inter, layers = 1024, 4, 2, 64, 704, 2
     hidden = hq * d
     tensors = random_model(seed, vocab, hidden, hkv, inter, layers)
@@ -45,7 +45,6 @@ def _run(kv_dtype, prompts, steps=4, seed=7):
                 num_query_heads=hq, num_key_value_heads=hkv, head_dimension=d,
                 rms_norm_epsilon=1e-5, rope_theta=10000.0, situ_beta_gate=4.0, situ_beta_up=25.0)
     omodel = O.Model(ocfg, tensors)
-    ctx = 128
     pool = slmkv.KvPool(num_layers=layers, num_query_heads=hq, num_key_value_heads=hkv,
                         head_dimension=d, context_length=ctx, rope_theta=10000.0,
                         num_blocks=len(prompts) * (ctx // 16) + 4, max_sequences=len(prompts),
@@ -110,6 +109,16 @@ def test_model_prefill_and_decode_match_the_oracle_bf16():
     m = _run(slmkv.KV_BF16, PROMPTS)
     check_thresholds(m)
     print("bf16 KV logits vs oracle:", m)
+
+
+def test_long_prefill_on_the_tensor_core_path():
+    # 3 x 400 prompt rows > 1024: the prefill's projections run as tensor-core
+    # GEMMs (another accumulation order), the decode steps as the fused kernels
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, 1024, 400).astype(np.uint32) for _ in range(3)]
+    m = _run(slmkv.KV_F32, prompts, steps=2, ctx=512)
+    check_thresholds(m)
+    print("long prefill, f32 KV logits vs oracle:", m)
 
 
 def test_out_of_vocabulary_token_fails_and_rolls_back():
