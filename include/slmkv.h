@@ -334,6 +334,19 @@ slm_status slm_model_decode(slm_model* model, slm_batch* batch, const int32_t* d
  * and d_next_token [n] (may be NULL). */
 slm_status slm_model_prefill(slm_model* model, slm_batch* batch, const int32_t* d_token_ids,
                              float* d_logits, int32_t* d_next_token);
+/* ModelWeights::load (weights.rs:117-190) into a device model: a SafeTensors
+ * file whose tensors are exactly the expected set for this config and the
+ * context's layers and heads (names and shapes of weights.rs:344-378), every
+ * one F32 (little-endian); `expected_parameter_count` (0: not checked) must
+ * equal their total (ModelConfig::expected_parameter_count). A malformed file
+ * or any mismatch fails with SLM_ERR_INVALID_INPUT ("invalid weights: ..."). */
+slm_status slm_model_load_safetensors(slm_ctx* ctx, const slm_model_config* config, const char* path,
+                                      int64_t expected_parameter_count, slm_model** out);
+/* The same checks without a device (layers, KV heads and head dimension
+ * given); reports the parameter count. Errors: slm_last_error(NULL). */
+slm_status slm_safetensors_check(const slm_model_config* config, int32_t num_layers,
+                                 int32_t num_key_value_heads, int32_t head_dimension, const char* path,
+                                 int64_t expected_parameter_count, int64_t* parameter_count);
 
 #ifdef __cplusplus
 }

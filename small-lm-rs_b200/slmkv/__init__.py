@@ -152,6 +152,10 @@ SIGNATURES = {
     "slm_model_destroy": (C.c_int, [_vp]),
     "slm_model_decode": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "slm_model_prefill": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "slm_model_load_safetensors": (C.c_int, [_vp, C.POINTER(ModelConfig), C.c_char_p, _i64,
+                                             C.POINTER(_vp)]),
+    "slm_safetensors_check": (C.c_int, [C.POINTER(ModelConfig), _i32, _i32, _i32, C.c_char_p,
+                                        _i64, C.POINTER(_i64)]),
 }
 
 _lib = None
@@ -706,12 +710,15 @@ class Model:
     v, o, ffn_norm, gate, up, down; final_norm."""
 
     def __init__(self, pool: KvPool, *, vocab_size: int, intermediate_size: int,
-                 tensors, rms_norm_epsilon: float = 1e-5, situ_beta_gate: float = 4.0,
-                 situ_beta_up: float = 25.0):
+                 tensors=None, rms_norm_epsilon: float = 1e-5, situ_beta_gate: float = 4.0,
+                 situ_beta_up: float = 25.0, _handle=None):
         import numpy as np
 
         self.pool = pool
         self.vocab_size = vocab_size
+        if _handle is not None:
+            self._h = _handle
+            return
         cfg = ModelConfig(vocab_size, pool.q_heads * pool.head_dim, intermediate_size,
                           rms_norm_epsilon, situ_beta_gate, situ_beta_up)
         keep = [np.ascontiguousarray(np.asarray(t, dtype=np.float32)) for t in tensors]
@@ -719,6 +726,19 @@ class Model:
         h = _vp()
         pool.check(lib().slm_model_create(pool.handle, C.byref(cfg), arr, len(keep), C.byref(h)))
         self._h = h
+
+    @classmethod
+    def from_safetensors(cls, pool: KvPool, path, *, vocab_size: int, intermediate_size: int,
+                         expected_parameter_count: int = 0, rms_norm_epsilon: float = 1e-5,
+                         situ_beta_gate: float = 4.0, situ_beta_up: float = 25.0) -> "Model":
+        """ModelWeights::load (weights.rs:117-190) straight into the device model."""
+        cfg = ModelConfig(vocab_size, pool.q_heads * pool.head_dim, intermediate_size,
+                          rms_norm_epsilon, situ_beta_gate, situ_beta_up)
+        h = _vp()
+        pool.check(lib().slm_model_load_safetensors(pool.handle, C.byref(cfg),
+                                                    str(path).encode(), expected_parameter_count,
+                                                    C.byref(h)))
+        return cls(pool, vocab_size=vocab_size, intermediate_size=intermediate_size, _handle=h)
 
     def decode(self, batch: "Batch", token_ids, logits=None, next_tokens=None) -> None:
         """model.rs:342-397 for every sequence of ``batch`` (counts 1):
@@ -744,6 +764,21 @@ class Model:
             self.close()
         except Exception:
             pass
+
+
+def check_safetensors(path, *, vocab_size: int, hidden_size: int, intermediate_size: int,
+                      num_layers: int, num_key_value_heads: int, head_dimension: int = 64,
+                      expected_parameter_count: int = 0) -> int:
+    """The checks of ModelWeights::load (weights.rs:117-190) without a device;
+    returns the parameter count, raises InvalidInput with the reason."""
+    cfg = ModelConfig(vocab_size, hidden_size, intermediate_size, 1e-5, 4.0, 25.0)
+    n = _i64()
+    rc = lib().slm_safetensors_check(C.byref(cfg), num_layers, num_key_value_heads,
+                                     head_dimension, str(path).encode(), expected_parameter_count,
+                                     C.byref(n))
+    if rc != OK:
+        raise _error_class(rc)(rc, (lib().slm_last_error(None) or b"").decode())
+    return int(n.value)
 
 
 MODEL_TENSOR_ORDER = ("attention_norm", "q_proj", "k_proj", "v_proj", "o_proj", "ffn_norm",

@@ -144,3 +144,40 @@ def test_out_of_vocabulary_token_fails_and_rolls_back():
     assert [c.sequence_length() for c in caches] == [4, 5]
     assert all(0 <= t < vocab for t in nxt.cpu().tolist())
     model.close()
+
+
+def test_model_loaded_from_safetensors_equals_the_array_model(tmp_path):
+    # the same weights through slm_model_load_safetensors (weights.rs:117-190)
+    # give bit-identical logits: names, shapes and little-endian values land
+    # where slm_model_create puts them
+    from test_weights_safetensors import write_safetensors
+
+    vocab, hq, hkv, d, inter, layers = 512, 4, 2, 64, 128, 2
+    tensors = random_model(5, vocab, hq * d, hkv, inter, layers)
+    names = [n for n, _ in slmkv.model_tensor_shapes(vocab_size=vocab, hidden_size=hq * d,
+                                                      intermediate_size=inter, num_layers=layers,
+                                                      kv_width=hkv * d)]
+    path = tmp_path / "w.safetensors"
+    write_safetensors(path, dict(zip(names, tensors)), order=names[::-1])
+    outs = []
+    for build in ("arrays", "file"):
+        pool = slmkv.KvPool(num_layers=layers, num_query_heads=hq, num_key_value_heads=hkv,
+                            head_dimension=d, context_length=64, num_blocks=16, max_sequences=1,
+                            device=0)
+        if build == "arrays":
+            model = slmkv.Model(pool, vocab_size=vocab, intermediate_size=inter, tensors=tensors)
+        else:
+            model = slmkv.Model.from_safetensors(pool, path, vocab_size=vocab,
+                                                 intermediate_size=inter,
+                                                 expected_parameter_count=sum(t.size for t in tensors))
+        cache = pool.allocate_kv_cache(64)
+        logits = torch.empty((1, vocab), dtype=torch.float32, device="cuda:0")
+        with pool.begin([cache], [5]) as b:
+            model.prefill(b, torch.tensor([3, 1, 4, 1, 5], dtype=torch.int32, device="cuda:0"), logits)
+        first = logits.cpu().numpy().copy()
+        with pool.begin([cache], 1) as b:
+            model.decode(b, torch.tensor([9], dtype=torch.int32, device="cuda:0"), logits)
+        outs.append((first, logits.cpu().numpy().copy()))
+        model.close()
+        pool.close()
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
