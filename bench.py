@@ -578,11 +578,15 @@ def serve_trace(seed: int):
 
 
 def run_serve(args):
-    """Continuous batching of the request trace: every step the scheduler plans
-    a decode batch and a prefill batch, their KV work runs for all layers with
-    synthetic projections (the model's matmuls are outside this path), and the
-    statuses are committed. Requests arrive on the host clock. Throughput =
-    output tokens of all ranks / slowest rank's device time."""
+    """Continuous batching of the request trace on the 8M model: every step the
+    scheduler plans a decode batch and a prefill batch (prompt chunks within a
+    token budget); the decode batch runs slm_model_decode, the prefill batch
+    slm_model_prefill, and their statuses are committed. Each request's tokens
+    (its random prompt, then the greedy tokens the model chose) live in a
+    device history indexed by request and position: a step gathers its input
+    tokens from it and writes the chosen tokens back, so a preempted request
+    recomputes from its own tokens. Requests arrive on the host clock.
+    Throughput = output tokens of all ranks / slowest rank's device time."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -605,43 +609,80 @@ def run_serve(args):
                         head_dimension=D, context_length=CTX, num_blocks=B * (CTX // BLOCK),
                         max_sequences=B, device=local)
     pool.shuffle(args.seed + 1)
+    model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=MODEL_INTER,
+                        tensors=model_tensors(args.seed))
     sched = slmkv.Scheduler(pool, max_running=B, max_prefill_tokens=SERVE_PREFILL_TOKENS)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(args.seed + 3)
-    nd_max, np_max = B, SERVE_PREFILL_TOKENS
-    dq = torch.randn((LAYERS, nd_max, HQ, D), generator=gen, device=dev)
-    dk = torch.randn((LAYERS, nd_max, HKV, D), generator=gen, device=dev)
-    dout = torch.empty((LAYERS, nd_max, HQ, D), device=dev)
-    pq = torch.randn((LAYERS, np_max, HQ, D), generator=gen, device=dev)
-    pk = torch.randn((LAYERS, np_max, HKV, D), generator=gen, device=dev)
-    pout = torch.empty((LAYERS, np_max, HQ, D), device=dev)
-    dptr = [(dq[l].data_ptr(), dk[l].data_ptr(), dk[l].data_ptr(), dout[l].data_ptr())
-            for l in range(LAYERS)]
+    # token history: row per request of this rank, prompt tokens first
+    row_of = {rid: k for k, rid in enumerate(mine)}
+    W = CTX + 1
+    rng = np.random.default_rng(args.seed + 11)
+    h_hist = np.zeros((max(1, len(mine)), W), np.int32)
+    for rid, k in row_of.items():
+        h_hist[k, :prompts[rid]] = rng.integers(0, MODEL_VOCAB, size=int(prompts[rid]))
+    hist = torch.from_numpy(h_hist).to(dev).view(-1)
+    first_done = set()
     stream = torch.cuda.current_stream()
     ones = slmkv._i32_array([1] * B)
+    # staging for the per-step gather / scatter indices (pinned, copied async)
+    h_idx = torch.zeros(B + SERVE_PREFILL_TOKENS + B, dtype=torch.int64).pin_memory()
+    d_idx = torch.zeros_like(h_idx, device=dev)
+    nxt_dec = torch.zeros(B, dtype=torch.int32, device=dev)
+    nxt_pre = torch.zeros(B, dtype=torch.int32, device=dev)
 
     def run_step():
         # the decode batch is submitted and the prefill batch queued behind it:
         # one wait per step
         nd, npf = sched.plan()
+        dec_req, pre_req = sched.plan_requests()
+        counts = list(sched._pcnt[:npf])
+        rows = sum(counts)
+        # indices: decode inputs [0, nd), prefill inputs [nd, nd + rows),
+        # first-token writes after them
+        hv = h_idx.numpy()
+        for i, (rid, pos) in enumerate(dec_req):
+            hv[i] = row_of[rid] * W + pos
+        at = nd
+        firsts = []
+        for i, ((rid, pos), c) in enumerate(zip(pre_req, counts)):
+            base = row_of[rid] * W + pos
+            hv[at:at + c] = np.arange(base, base + c)
+            at += c
+            if pos + c == prompts[rid] and rid not in first_done:
+                firsts.append((i, base + c))
+                first_done.add(rid)
+        for j, (_, dst) in enumerate(firsts):
+            hv[at + j] = dst
+        n_idx = at + len(firsts)
+        if n_idx:
+            d_idx[:n_idx].copy_(h_idx[:n_idx], non_blocking=True)
         dst = pst = None
         dec = None
         if nd:
             dec = slmkv.Batch.for_sequences(pool, nd, sched._dseq, ones, stream)
-            for l in range(LAYERS):
-                dec.decode_layer_ptr(l, *dptr[l])
+            model.decode(dec, hist.index_select(0, d_idx[:nd]).to(torch.int32), None, nxt_dec[:nd])
+            hist.index_copy_(0, d_idx[:nd] + 1, nxt_dec[:nd])
             dec.submit()
         if npf:
-            counts = list(sched._pcnt[:npf])
-            rows = sum(counts)
             b = slmkv.Batch.for_sequences(pool, npf, sched._pseq, sched._pcnt, stream)
-            for l in range(LAYERS):
-                b.append_layer(l, pk[l, :rows], pk[l, :rows], rotate_keys=True)
-                b.prefill_attention(l, pq[l, :rows], pout[l, :rows], rotate_query=True)
+            model.prefill(b, hist.index_select(0, d_idx[nd:nd + rows]).to(torch.int32), None,
+                          nxt_pre[:npf])
+            if firsts:
+                sel = torch.tensor([i for i, _ in firsts], dtype=torch.int64, device=dev)
+                hist.index_copy_(0, d_idx[nd + rows:n_idx], nxt_pre.index_select(0, sel))
             pst = b.end(raise_on_error=False)
         if dec is not None:
             dst = dec.wait(raise_on_error=False)
         return nd, npf, sched.commit(dst, pst)
+
+    # warm-up on throwaway sequences (both projection paths and a decode step)
+    warm = [pool.allocate_kv_cache(CTX) for _ in range(3)]
+    wid = torch.ones(1200, dtype=torch.int32, device=dev)
+    with pool.begin(warm, [400, 400, 400]) as b:
+        model.prefill(b, wid)
+    with pool.begin(warm, 1) as b:
+        model.decode(b, wid[:3])
+    for c in warm:
+        c.free()
 
     order = sorted(mine, key=lambda i: arrivals[i])
     t_start = torch.cuda.Event(enable_timing=True)
@@ -682,8 +723,10 @@ def run_serve(args):
         "config": {"workload": (f"continuous batching: {SERVE_REQUESTS} requests, Poisson "
                                 f"arrivals {SERVE_RATE:.0f}/s, prompts U[{LEN_LO},{LEN_HI}], "
                                 f"outputs U[{SERVE_OUT_LO},{SERVE_OUT_HI}], <= {B} running per "
-                                f"GPU, {LAYERS} layers, Hq={HQ}, Hkv={HKV}, d={D}, f32 KV; "
-                                "synthetic Q/K/V per step"),
+                                f"GPU; the 8M model ({LAYERS} layers, hidden {HQ * D}, FFN "
+                                f"{MODEL_INTER}, Hq={HQ}, Hkv={HKV}, d={D}, vocab {MODEL_VOCAB}, "
+                                "f32 KV, random N(0, 0.02^2) weights), random prompt ids, "
+                                "greedy decoding"),
                    "name": "serve", "requests_per_rank": len(order), "seed": args.seed},
         "output_tokens": int(tokens.item()), "preemptions": counts["preemptions"],
         "gpu_launches": pool.launch_count(),
@@ -691,18 +734,19 @@ def run_serve(args):
     if rank == 0:
         print(json.dumps(result), flush=True)
     sched.close()
+    model.close()
     pool.close()
     if world > 1:
         dist.destroy_process_group()
 
 
 def run_prefix(args):
-    """Prefix reuse: request 0 prefills the shared prefix and publishes its
-    full blocks; the other requests attach them through the block table and
-    prefill only their own suffix over the attached cache; then every request
-    decodes PREFIX_DECODE_STEPS tokens in batched steps. Reports the prefill
-    tokens the reuse saved and the decode throughput (synthetic Q/K/V: the
-    model's projections are outside this path)."""
+    """Prefix reuse on the 8M model: request 0 prefills the shared prefix and
+    publishes its full blocks; the other requests attach them through the
+    block table and prefill only their own suffix over the attached cache;
+    then every request decodes PREFIX_DECODE_STEPS greedy tokens in batched
+    steps, each step's tokens staying on the device. Reports the prefill
+    tokens the reuse saved and the decode throughput."""
     import numpy as np
     import torch
 
@@ -713,66 +757,66 @@ def run_prefix(args):
     dev = torch.device(f"cuda:{local}")
     prefix_len, suffix_len = LEN_LO, LEN_HI
     rng = np.random.default_rng(args.seed + 77)
-    prefix_ids = [int(x) for x in rng.integers(0, 8192, size=prefix_len)]
-    suffix_ids = [[int(x) for x in rng.integers(0, 8192, size=suffix_len)] for _ in range(B)]
+    prefix_ids = [int(x) for x in rng.integers(0, MODEL_VOCAB, size=prefix_len)]
+    suffix_ids = [[int(x) for x in rng.integers(0, MODEL_VOCAB, size=suffix_len)] for _ in range(B)]
     total_len = prefix_len + suffix_len + PREFIX_DECODE_STEPS
     pool = slmkv.KvPool(num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV,
                         head_dimension=D, context_length=CTX,
-                        num_blocks=B * ((total_len + BLOCK - 1) // BLOCK) + 64, max_sequences=B,
+                        num_blocks=B * ((total_len + BLOCK - 1) // BLOCK) + 160, max_sequences=B,
                         device=local)
     pool.shuffle(args.seed + 1)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(args.seed + 5)
+    model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=MODEL_INTER,
+                        tensors=model_tensors(args.seed))
 
-    def qkv(rows):
-        return [(torch.randn((rows, HQ, D), generator=gen, device=dev),
-                 torch.randn((rows, HKV, D), generator=gen, device=dev),
-                 torch.randn((rows, HKV, D), generator=gen, device=dev)) for _ in range(LAYERS)]
+    def ids(tokens):
+        return torch.tensor(tokens, dtype=torch.int32, device=dev)
 
-    def prefill(caches, counts, inputs):
-        rows = sum(counts)
-        out = torch.empty((rows, HQ, D), device=dev)
-        with pool.begin(caches, counts) as b:
-            for l, (q, k, v) in enumerate(inputs):
-                b.append_layer(l, k, v, rotate_keys=True)
-                b.prefill_attention(l, q, out, rotate_query=True)
+    # warm-up on throwaway sequences: both projection paths (fused up to 1024
+    # rows, tensor-core GEMMs beyond) and a decode step, so that one-time
+    # library and module loading stays out of the timed prefill
+    warm = [pool.allocate_kv_cache(CTX) for _ in range(3)]
+    with pool.begin(warm, [400, 400, 400]) as b:
+        model.prefill(b, ids([1] * 1200))
+    with pool.begin(warm[:1], [32]) as b:
+        model.prefill(b, ids([2] * 32))
+    with pool.begin(warm, 1) as b:
+        model.decode(b, ids([3, 4, 5]))
+    for c in warm:
+        c.free()
 
     caches = [pool.allocate_kv_cache(total_len) for _ in range(B)]
     stream = torch.cuda.current_stream()
     e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    pre_in = qkv(prefix_len)
-    suf_in = qkv(suffix_len * (B - 1))
-    first_suffix = qkv(suffix_len)
+    tok = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(2)]
+    pre_ids, first_suffix = ids(prefix_ids), ids(suffix_ids[0])
+    rest_ids = ids([t for sfx in suffix_ids[1:] for t in sfx])
     torch.cuda.synchronize()
     e[0].record(stream)
     # request 0: the prefix, published, then its own suffix
-    prefill([caches[0]], [prefix_len], pre_in)
+    with pool.begin([caches[0]], [prefix_len]) as b:
+        model.prefill(b, pre_ids)
     indexed = caches[0].publish_prefix(prefix_ids)
-    prefill([caches[0]], [suffix_len], first_suffix)
+    with pool.begin([caches[0]], [suffix_len]) as b:
+        model.prefill(b, first_suffix, None, tok[0][:1])
     # the others: attach the prefix blocks, prefill only the suffix
     reused = [c.attach_prefix(prefix_ids + suffix_ids[i]) for i, c in enumerate(caches[1:], 1)]
-    prefill(caches[1:], [suffix_len] * (B - 1), suf_in)
+    with pool.begin(caches[1:], [suffix_len] * (B - 1)) as b:
+        model.prefill(b, rest_ids, None, tok[0][1:])
     e[1].record(stream)
-    # batched decode of every request
-    dq = torch.randn((LAYERS, B, HQ, D), generator=gen, device=dev)
-    dk = torch.randn((LAYERS, B, HKV, D), generator=gen, device=dev)
-    dout = torch.empty((LAYERS, B, HQ, D), device=dev)
-    ptrs = [(dq[l].data_ptr(), dk[l].data_ptr(), dk[l].data_ptr(), dout[l].data_ptr())
-            for l in range(LAYERS)]
+    # batched greedy decode of every request
     plan = pool.step_plan(caches, 1)
     inflight = []
     e[2].record(stream)
-    for _ in range(PREFIX_DECODE_STEPS):
+    for i in range(PREFIX_DECODE_STEPS):
         b = plan.begin()
-        for l in range(LAYERS):
-            b.decode_layer_ptr(l, *ptrs[l])
+        model.decode(b, tok[i % 2], None, tok[(i + 1) % 2])
         inflight.append(b.submit())
         while len(inflight) > 1:
-            if any(inflight.pop(0).wait()):
+            if any(inflight.pop(0).wait(raise_on_error=False)):
                 raise RuntimeError("decode step failed")
     e[3].record(stream)
     for b in inflight:
-        if any(b.wait()):
+        if any(b.wait(raise_on_error=False)):
             raise RuntimeError("decode step failed")
     torch.cuda.synchronize()
     lengths = [c.sequence_length() for c in caches]
@@ -787,15 +831,18 @@ def run_prefix(args):
         "steps": PREFIX_DECODE_STEPS, "warmup": 0, "ms_per_step": decode_ms / PREFIX_DECODE_STEPS,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": (f"prefix reuse: {B} requests share a {prefix_len}-token prefix "
-                                f"and add {suffix_len} own tokens, then {PREFIX_DECODE_STEPS} "
-                                f"decode steps each; {LAYERS} layers, Hq={HQ}, Hkv={HKV}, d={D}, "
-                                "f32 KV; synthetic Q/K/V"), "name": "prefix", "seed": args.seed},
+        "config": {"workload": (f"prefix reuse on the 8M model: {B} requests share a "
+                                f"{prefix_len}-token random prefix and add {suffix_len} own "
+                                f"tokens, then {PREFIX_DECODE_STEPS} greedy decode steps each; "
+                                f"{LAYERS} layers, hidden {HQ * D}, Hq={HQ}, Hkv={HKV}, d={D}, "
+                                "f32 KV, random N(0, 0.02^2) weights"), "name": "prefix",
+                   "seed": args.seed},
         "prefill_tokens_computed": computed, "prefill_tokens_without_reuse": without,
         "prefill_tokens_saved": without - computed, "prefix_blocks_indexed": indexed,
         "prefill_ms": prefill_ms, "gpu_launches": pool.launch_count(),
     }
     print(json.dumps(result), flush=True)
+    model.close()
     pool.close()
 
 

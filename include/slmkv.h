@@ -246,6 +246,14 @@ slm_status slm_sched_submit(slm_sched* sched, int64_t request_id, int32_t prompt
  * nothing to do returns 0 and 0. */
 slm_status slm_sched_plan(slm_sched* sched, int32_t* n_decode, int32_t* decode_seq,
                           int32_t* n_prefill, int32_t* prefill_seq, int32_t* prefill_count);
+/* The requests behind the last plan, in plan order: their ids and the cache
+ * position each entry starts at (a decode entry feeds the token at that
+ * position; a prefill entry feeds positions pos .. pos + count - 1, its
+ * prompt, or after a preemption its prompt and generated tokens again). Any
+ * array may be NULL. */
+slm_status slm_sched_plan_requests(const slm_sched* sched, int64_t* decode_request,
+                                   int32_t* decode_pos, int64_t* prefill_request,
+                                   int32_t* prefill_pos);
 /* Commits the last plan: the per-sequence statuses its batches reported (in
  * plan order; NULL when that part was empty). Requests whose sequence failed
  * are finished with that status. Fills the requests finished by this step

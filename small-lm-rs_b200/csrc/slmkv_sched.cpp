@@ -173,6 +173,20 @@ slm_status slm_sched_plan(slm_sched* s, int32_t* n_decode, int32_t* decode_seq,
   return SLM_OK;
 }
 
+slm_status slm_sched_plan_requests(const slm_sched* s, int64_t* decode_request, int32_t* decode_pos,
+                                   int64_t* prefill_request, int32_t* prefill_pos) {
+  if (!s || !s->planned) return SLM_ERR_INVALID_INPUT;
+  for (size_t i = 0; i < s->plan_decode.size(); ++i) {
+    if (decode_request) decode_request[i] = s->plan_decode[i]->id;
+    if (decode_pos) decode_pos[i] = s->plan_decode[i]->cached;
+  }
+  for (size_t i = 0; i < s->plan_prefill.size(); ++i) {
+    if (prefill_request) prefill_request[i] = s->plan_prefill[i]->id;
+    if (prefill_pos) prefill_pos[i] = s->plan_prefill[i]->cached;
+  }
+  return SLM_OK;
+}
+
 slm_status slm_sched_commit(slm_sched* s, const int32_t* decode_status,
                             const int32_t* prefill_status, int32_t* n_finished,
                             int64_t* finished_id, int32_t* finished_status, int32_t* h_generated) {

@@ -145,6 +145,7 @@ SIGNATURES = {
     "slm_sched_plan": (C.c_int, [_vp, _pi32, _pi32, _pi32, _pi32, _pi32]),
     "slm_sched_commit": (C.c_int, [_vp, _pi32, _pi32, _pi32, C.POINTER(_i64), _pi32, _pi32]),
     "slm_sched_counts": (C.c_int, [_vp, _pi32, _pi32, C.POINTER(_i64), C.POINTER(_i64)]),
+    "slm_sched_plan_requests": (C.c_int, [_vp, C.POINTER(_i64), _pi32, C.POINTER(_i64), _pi32]),
     "slm_decode_attention_noalloc": (
         C.c_int, [_vp, _vp, _i32, _i32, _i32, _pi32, _i32, _pi32, _i32, _vp, _vp, _vp]),
     "slm_model_create": (C.c_int, [_vp, C.POINTER(ModelConfig), C.POINTER(_vp), _i32,
@@ -818,6 +819,8 @@ class Scheduler:
         n = max(1, self.max_running)
         self._dseq, self._pseq, self._pcnt = (C.c_int32 * n)(), (C.c_int32 * n)(), (C.c_int32 * n)()
         self._fid, self._fst, self._fgen = (C.c_int64 * n)(), (C.c_int32 * n)(), (C.c_int32 * n)()
+        self._dreq, self._preq = (C.c_int64 * n)(), (C.c_int64 * n)()
+        self._dpos, self._ppos = (C.c_int32 * n)(), (C.c_int32 * n)()
         self._nd, self._np, self._nf = C.c_int32(), C.c_int32(), C.c_int32()
 
     def close(self) -> None:
@@ -847,6 +850,16 @@ class Scheduler:
 
     def prefill_seqs(self) -> list[tuple[int, int]]:
         return list(zip(self._pseq[: self._np.value], self._pcnt[: self._np.value]))
+
+    def plan_requests(self):
+        """The requests behind the last plan: (decode [(request, pos)],
+        prefill [(request, pos)]); a decode entry feeds the token at `pos`, a
+        prefill entry positions pos .. pos + count - 1."""
+        self.pool.check(lib().slm_sched_plan_requests(self._h, self._dreq, self._dpos,
+                                                      self._preq, self._ppos))
+        nd, np_ = self._nd.value, self._np.value
+        return (list(zip(self._dreq[:nd], self._dpos[:nd])),
+                list(zip(self._preq[:np_], self._ppos[:np_])))
 
     def commit(self, decode_status=None, prefill_status=None) -> list[tuple[int, int, int]]:
         """Commits the last plan; returns the finished requests as

@@ -123,3 +123,20 @@ def test_failed_sequence_finishes_with_its_status():
     assert done[1][0] == slmkv.ERR_NON_FINITE
     assert done[2] == (0, 5) or done[2][0] == slmkv.ERR_NON_FINITE
     assert s.counts()["running"] == 0
+
+
+def test_plan_requests_report_ids_and_positions():
+    pool = _pool()
+    s = slmkv.Scheduler(pool, max_running=3, max_prefill_tokens=16)
+    s.submit(10, 20, 3)
+    s.submit(11, 5, 2)
+    s.plan()
+    assert s.plan_requests() == ([], [(10, 0)])  # 16 of request 10's 20 prompt tokens
+    s.commit(None, [0])
+    s.plan()
+    # request 10 continues at position 16; request 11 starts at 0
+    assert s.plan_requests() == ([], [(10, 16), (11, 0)])
+    s.commit(None, [0, 0])
+    s.plan()
+    # both prompts are cached: each decode step feeds the token at its length
+    assert s.plan_requests() == ([(10, 20), (11, 5)], [])
