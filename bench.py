@@ -59,10 +59,16 @@ WORKLOADS = {
     "prefix": dict(B=64, LEN_LO=384, LEN_HI=32, LAYERS=8, HQ=4, HKV=2, D=64, CTX=512, BF16=False),
     # the 8M model end to end: batch 1, a 64-token prompt, 448 greedy decode steps
     "model": dict(B=1, LEN_LO=64, LEN_HI=448, LAYERS=8, HQ=4, HKV=2, D=64, CTX=512, BF16=False),
+    # the scaled GQA model end to end: 16 sequences a GPU, prompts of
+    # U[1024, 8192 - 256] random tokens, then 256 greedy decode steps
+    "gqa-model": dict(B=16, LEN_LO=1024, LEN_HI=8192 - 256, LAYERS=8, HQ=32, HKV=8, D=64,
+                      CTX=8192, BF16=True),
 }
 # the 8M model (artifacts/small-lm-8m/config.json): vocab 8192, hidden 256,
 # SiTU-GLU FFN 704, RMSNorm eps 1e-5, SiTU betas 4 / 25, tied embeddings
 MODEL_VOCAB, MODEL_INTER = 8192, 704
+# the scaled GQA model: hidden 2048 (32 x 64), FFN 5632, same vocabulary
+GQA_MODEL_INTER, GQA_MODEL_STEPS = 5632, 256
 PREFIX_DECODE_STEPS = 96
 # "serve": 4096 requests in total (shared by the ranks), Poisson arrivals at
 # SERVE_RATE requests/s (seeded), prompts U[8,256], outputs U[16,256], at
@@ -98,6 +104,10 @@ def parse():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="microbench")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU instead of the workload's (smaller cases for profiling)")
+    ap.add_argument("--exact-rows", type=int, default=None,
+                    help="model workloads: steps of up to this many token rows project in the "
+                         "reference's accumulation order, larger ones on tensor-core GEMMs "
+                         "(default: the library's 1024; the scaled GQA model: 0)")
     args = ap.parse_args()
     select_workload(args.workload, args.batch)
     return args
@@ -611,6 +621,8 @@ def run_serve(args):
     pool.shuffle(args.seed + 1)
     model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=MODEL_INTER,
                         tensors=model_tensors(args.seed))
+    if args.exact_rows is not None:
+        model.set_exact_rows(args.exact_rows)
     sched = slmkv.Scheduler(pool, max_running=B, max_prefill_tokens=SERVE_PREFILL_TOKENS)
     # token history: row per request of this rank, prompt tokens first
     row_of = {rid: k for k, rid in enumerate(mine)}
@@ -727,7 +739,8 @@ def run_serve(args):
                                 f"{MODEL_INTER}, Hq={HQ}, Hkv={HKV}, d={D}, vocab {MODEL_VOCAB}, "
                                 "f32 KV, random N(0, 0.02^2) weights), random prompt ids, "
                                 "greedy decoding"),
-                   "name": "serve", "requests_per_rank": len(order), "seed": args.seed},
+                   "name": "serve", "requests_per_rank": len(order), "seed": args.seed,
+                   "exact_rows": 1024 if args.exact_rows is None else args.exact_rows},
         "output_tokens": int(tokens.item()), "preemptions": counts["preemptions"],
         "gpu_launches": pool.launch_count(),
     }
@@ -767,27 +780,33 @@ def run_prefix(args):
     pool.shuffle(args.seed + 1)
     model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=MODEL_INTER,
                         tensors=model_tensors(args.seed))
+    if args.exact_rows is not None:
+        model.set_exact_rows(args.exact_rows)
 
     def ids(tokens):
         return torch.tensor(tokens, dtype=torch.int32, device=dev)
 
-    # warm-up on throwaway sequences: both projection paths (fused up to 1024
-    # rows, tensor-core GEMMs beyond) and a decode step, so that one-time
-    # library and module loading stays out of the timed prefill
-    warm = [pool.allocate_kv_cache(CTX) for _ in range(3)]
-    with pool.begin(warm, [400, 400, 400]) as b:
-        model.prefill(b, ids([1] * 1200))
-    with pool.begin(warm[:1], [32]) as b:
-        model.prefill(b, ids([2] * 32))
+    # warm-up on throwaway sequences with the timed phase's shapes (the
+    # prefix, one suffix, the other requests' suffixes in one batch, a decode
+    # step of all), so that one-time library and module loading, GEMM
+    # selection and scratch growth stay out of the timed prefill
+    tok = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(2)]
+    warm = [pool.allocate_kv_cache(CTX) for _ in range(B - 1)]
+    wtok = torch.zeros(B, dtype=torch.int32, device=dev)
+    with pool.begin(warm[:1], [prefix_len]) as b:
+        model.prefill(b, ids([1] * prefix_len))
+    with pool.begin(warm[:1], [suffix_len]) as b:
+        model.prefill(b, ids([2] * suffix_len), None, wtok[:1])
+    with pool.begin(warm, [suffix_len] * (B - 1)) as b:
+        model.prefill(b, ids([3] * (suffix_len * (B - 1))), None, wtok[:B - 1])
     with pool.begin(warm, 1) as b:
-        model.decode(b, ids([3, 4, 5]))
+        model.decode(b, wtok[:B - 1], None, tok[1][:B - 1])
     for c in warm:
         c.free()
 
     caches = [pool.allocate_kv_cache(total_len) for _ in range(B)]
     stream = torch.cuda.current_stream()
     e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    tok = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(2)]
     pre_ids, first_suffix = ids(prefix_ids), ids(suffix_ids[0])
     rest_ids = ids([t for sfx in suffix_ids[1:] for t in sfx])
     torch.cuda.synchronize()
@@ -836,6 +855,7 @@ def run_prefix(args):
                                 f"tokens, then {PREFIX_DECODE_STEPS} greedy decode steps each; "
                                 f"{LAYERS} layers, hidden {HQ * D}, Hq={HQ}, Hkv={HKV}, d={D}, "
                                 "f32 KV, random N(0, 0.02^2) weights"), "name": "prefix",
+                   "exact_rows": 1024 if args.exact_rows is None else args.exact_rows,
                    "seed": args.seed},
         "prefill_tokens_computed": computed, "prefill_tokens_without_reuse": without,
         "prefill_tokens_saved": without - computed, "prefix_blocks_indexed": indexed,
@@ -846,9 +866,9 @@ def run_prefix(args):
     pool.close()
 
 
-def model_tensors(seed: int):
-    """Random-init weights of the 8M model in the reference layout and order:
-    matrices and the embedding N(0, 0.02^2) (seeded), norms 1."""
+def model_tensors(seed: int, intermediate_size: int = MODEL_INTER):
+    """Random-init weights of the workload's model in the reference layout and
+    order: matrices and the embedding N(0, 0.02^2) (seeded), norms 1."""
     import numpy as np
 
     import slmkv
@@ -856,8 +876,8 @@ def model_tensors(seed: int):
     rng = np.random.default_rng(seed)
     out = []
     for _, shape in slmkv.model_tensor_shapes(vocab_size=MODEL_VOCAB, hidden_size=HQ * D,
-                                              intermediate_size=MODEL_INTER, num_layers=LAYERS,
-                                              kv_width=HKV * D):
+                                              intermediate_size=intermediate_size,
+                                              num_layers=LAYERS, kv_width=HKV * D):
         out.append(np.ones(shape, np.float32) if len(shape) == 1
                    else (0.02 * rng.standard_normal(shape)).astype(np.float32))
     return out
@@ -909,6 +929,8 @@ def run_model(args):
                         max_sequences=2, device=local)
     model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=MODEL_INTER,
                         tensors=tensors)
+    if args.exact_rows is not None:
+        model.set_exact_rows(args.exact_rows)
     stream = torch.cuda.current_stream()
     ids = torch.tensor(prompt, dtype=torch.int32, device=dev)
     tok = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(2)]
@@ -972,15 +994,16 @@ def run_model(args):
                                 f"{steps} greedy decode steps; {LAYERS} layers, hidden {HQ * D}, "
                                 f"FFN {MODEL_INTER} SiTU-GLU, Hq={HQ}, Hkv={HKV}, d={D}, "
                                 f"vocab {MODEL_VOCAB}, f32 KV, random N(0, 0.02^2) weights "
-                                f"(seed {args.seed})"), "name": "model", "seed": args.seed},
+                                f"(seed {args.seed})"), "name": "model", "seed": args.seed,
+                   "exact_rows": 1024 if args.exact_rows is None else args.exact_rows},
         "prefill_ms": prefill_ms,
         "e2e": {"value": steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4,
                 "loop": "pinned H2D of the step's token, decode, D2H of the chosen token, "
                         "host synchronizes every step"},
         "gpu_launches": launches,
-        "projections": "cuBLAS bf16 GEMM (fp32 accumulate) and fp32 SGEMM for the tied head; "
-                       "embedding, RMSNorm, SiTU, argmax and the KV step are this library's kernels",
+        "projections": "this library's fused exact-order projection kernels (bf16 operands, "
+                       "the reference's fp32 fold order); cuBLAS fp32 SGEMM for the tied head",
         "generated_head": toks[:8],
     }
     if not args.no_cpu_baseline:
@@ -1000,12 +1023,226 @@ def run_model(args):
     pool.close()
 
 
+def gqa_model_step_bytes(lengths) -> int:
+    """Algorithmic HBM bytes of one decode step of the scaled model for a
+    batch whose caches hold `lengths` entries: every bf16 projection matrix
+    once, the fp32 tied embedding once (the vocabulary projection), and the
+    KV path's bytes for every layer. Activations (a few MB) are left out."""
+    H, KV, I = HQ * D, HKV * D, GQA_MODEL_INTER
+    weights = LAYERS * 2 * (H * (H + 2 * KV) + H * H + 2 * H * I + I * H)
+    head = 4 * MODEL_VOCAB * H
+    return weights + head + LAYERS * algorithmic_bytes(lengths)
+
+
+def gqa_model_cpu_baseline(tensors, length: int, seed: int, threads: int, budget_s: float = 20.0):
+    """The oracle's model decode of ONE sequence at the scaled shape (the
+    reference engine serves one request at a time): its cache is filled with
+    `length` random bf16-rounded K/V entries per layer, then greedy decode
+    steps are timed (projections on all threads, attention serial)."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    cfg = dict(vocab_size=MODEL_VOCAB, hidden_size=HQ * D, intermediate_size=GQA_MODEL_INTER,
+               num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV, head_dimension=D,
+               rms_norm_epsilon=1e-5, rope_theta=10000.0, situ_beta_gate=4.0, situ_beta_up=25.0)
+    m = O.Model(cfg, tensors)
+    cache = m.new_cache(CTX, quantize_bf16=True)
+    rng = np.random.default_rng(seed + 5)
+    for layer in range(LAYERS):
+        kv = rng.standard_normal((2, length, HKV, D)).astype(np.float32)
+        cache.append_layer(layer, kv[0], kv[1], length)
+    tok, n = 1, 0
+    t0 = time.perf_counter()
+    while n < 2 or (n < 8 and time.perf_counter() - t0 < budget_s):
+        tok = O.argmax_finite(m.decode(cache, tok, threads))
+        n += 1
+    return n / (time.perf_counter() - t0), n
+
+
+def run_gqa_model(args):
+    """The scaled GQA model end to end on every GPU (weak scaling, no
+    collective on the data path): B sequences a GPU with random prompts,
+    prefilled in one batch, then greedy decode steps for all of them in one
+    batch per step, two steps in flight, the chosen tokens staying on the
+    device. Projections run as tensor-core GEMMs (cuBLAS bf16, fp32
+    accumulate). value = decode tokens of all ranks / the slowest rank's
+    device time; e2e copies each step's tokens from pinned host memory and
+    reads the chosen tokens back before the next step."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import slmkv
+    from slmkv.shard import max_over_ranks
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    steps = min(max(args.steps, 1), GQA_MODEL_STEPS)
+    warm = max(args.warmup, 3)
+    # B lengths per rank from one seeded draw, so rank r's share is the same
+    # at every world size
+    all_lens = np.random.default_rng(args.seed).integers(LEN_LO, LEN_HI + 1, size=B * max(world, 8))
+    lens = [int(x) for x in all_lens[rank * B:(rank + 1) * B]]
+    prng = np.random.default_rng(args.seed + 1 + rank)
+    prompts = [prng.integers(0, MODEL_VOCAB, size=L).astype(np.int32) for L in lens]
+    tensors = model_tensors(args.seed, GQA_MODEL_INTER)
+    blocks = sum(-(-(L + GQA_MODEL_STEPS) // BLOCK) for L in lens) + 8
+    pool = slmkv.KvPool(num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV,
+                        head_dimension=D, context_length=CTX, num_blocks=blocks, max_sequences=B,
+                        kv_dtype=slmkv.KV_BF16, device=local)
+    pool.shuffle(args.seed + 1)
+    model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=GQA_MODEL_INTER,
+                        tensors=tensors)
+    model.set_exact_rows(0 if args.exact_rows is None else args.exact_rows)
+    caches = [pool.allocate_kv_cache(CTX) for _ in lens]
+    stream = torch.cuda.current_stream()
+    ids = torch.from_numpy(np.concatenate(prompts)).to(dev)
+    tok = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(2)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    ev[0].record(stream)
+    with pool.begin(caches, lens) as b:
+        model.prefill(b, ids, None, tok[0])
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    first = tok[0].clone()
+    h_tok = torch.zeros(B, dtype=torch.int32).pin_memory()
+    plan = pool.step_plan(caches, 1)
+    lens_arr = plan.lengths(lens)
+
+    def decode(n, e2e=False):
+        tok[0].copy_(first)
+        if e2e:
+            h_tok.copy_(first)
+        inflight = []
+        for i in range(n):
+            cur, nxt = tok[i % 2], tok[(i + 1) % 2]
+            if e2e:
+                cur.copy_(h_tok, non_blocking=True)
+            b = plan.begin()
+            model.decode(b, cur, None, nxt)
+            if e2e:
+                if any(b.end(raise_on_error=False)):
+                    raise RuntimeError("decode step failed")
+                h_tok.copy_(nxt, non_blocking=True)
+                stream.synchronize()
+            else:
+                inflight.append(b.submit())
+                while len(inflight) > 1:
+                    if any(inflight.pop(0).wait(raise_on_error=False)):
+                        raise RuntimeError("decode step failed")
+        for b in inflight:
+            if any(b.wait(raise_on_error=False)):
+                raise RuntimeError("decode step failed")
+
+    def rewind():
+        torch.cuda.synchronize()
+        if [c.sequence_length() for c in caches] != [L + done[0] for L in lens]:
+            raise RuntimeError("unexpected cache lengths")
+        plan.truncate_all(lens_arr)
+
+    done = [warm]
+    decode(warm)
+    rewind()
+    clocks = ClockSampler(local)
+    clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0 = pool.launch_count()
+    ev[2].record(stream)
+    decode(steps)
+    ev[3].record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = pool.launch_count() - l0
+    (ms,) = max_over_ranks([ev[2].elapsed_time(ev[3])], device=dev)
+    done[0] = steps
+    rewind()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev[4].record(stream)
+    decode(steps, e2e=True)
+    ev[5].record(stream)
+    torch.cuda.synchronize()
+    (e2e_ms,) = max_over_ranks([ev[4].elapsed_time(ev[5])], device=dev)
+    rewind()
+    (prefill_ms,) = max_over_ranks([prefill_ms], device=dev)
+    step_bytes = sum(gqa_model_step_bytes([L + i for L in lens]) for i in range(steps))
+    peaks, kind = measured_peaks()
+    achieved = step_bytes / (ms / 1e3) / 1e9
+    tokens = world * B * steps
+    result = {
+        "metric": METRIC, "value": tokens / (ms / 1e3), "unit": "tok/s", "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": ms / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": (f"scaled GQA model end to end: {B} sequences per GPU, random "
+                                f"prompts of U[{LEN_LO},{LEN_HI}] tokens prefilled in one batch, "
+                                f"then {steps} greedy decode steps of all {B} per step; "
+                                f"{LAYERS} layers, hidden {HQ * D}, FFN {GQA_MODEL_INTER} "
+                                f"SiTU-GLU, Hq={HQ}, Hkv={HKV}, d={D}, vocab {MODEL_VOCAB}, "
+                                f"context {CTX}, bf16 KV, {BLOCK}-token shuffled blocks, random "
+                                f"N(0, 0.02^2) weights (seed {args.seed})"),
+                   "name": "gqa-model", "seed": args.seed,
+                   "exact_rows": 0 if args.exact_rows is None else args.exact_rows,
+                   "l2": "no flush: a step reads ~2 GB (weights and K/V), far above the 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "peak_kind": kind,
+                     "kernel": "the whole decode step: algorithmic bytes (bf16 projection "
+                               "matrices, fp32 tied embedding, the KV path per layer) / step "
+                               "time"},
+        "prefill_ms": prefill_ms,
+        "prefill_tok_s": world * sum(lens) / (prefill_ms / 1e3),
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                "d2h_bytes_per_step": 4 * B,
+                "loop": "pinned H2D of the step's tokens, decode, D2H of the chosen tokens, host "
+                        "synchronizes every step"},
+        "gpu_launches": launches,
+        "clocks": clk,
+        "projections": "cuBLAS bf16 GEMMs (fp32 accumulate); fp32 SGEMM for the tied head; "
+                       "embedding, RMSNorm, rounding, SiTU, argmax and the KV step are this "
+                       "library's kernels",
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle as O
+
+        threads = O.max_threads()
+        at = int(np.mean(lens)) + steps // 2
+        tps, n = gqa_model_cpu_baseline(tensors, at, args.seed, threads)
+        result["cpu_baseline"] = {
+            "value": tps, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": (f"{n} greedy decode steps of one sequence of the same model whose cache "
+                       f"holds {at} entries (this GPU's mean prompt + half the steps); oracle, "
+                       "OpenMP projections, serial attention as the reference, which serves one "
+                       "request at a time")}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    model.close()
+    pool.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif WORKLOAD_NAME == "model":
         run_model(args)
+    elif WORKLOAD_NAME == "gqa-model":
+        run_gqa_model(args)
     elif WORKLOAD_NAME == "serve":
         run_serve(args)
     elif WORKLOAD_NAME == "prefix":

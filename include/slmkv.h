@@ -326,6 +326,14 @@ typedef struct slm_model_config {
 slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config,
                             const float* const* h_tensors, int32_t n_tensors, slm_model** out);
 slm_status slm_model_destroy(slm_model* model);
+/* Steps of up to `max_rows` token rows (0..1024; default 1024, or 0 when the
+ * model's rows do not fit the kernels' shared memory) compute every projection
+ * output as linear.rs:98-103 does: one fp32 fma fold over the input features in
+ * order, so f32-KV logits match the CPU engine to ~1e-6. Larger steps, and
+ * every step when 0, use tensor-core GEMMs: another accumulation order, within
+ * the reference's GPU-vs-CPU logit thresholds (parity/runner.rs:33-43) and
+ * faster on wide models. Not an engine method: a B200 execution choice. */
+slm_status slm_model_set_exact_rows(slm_model* model, int32_t max_rows);
 /* One cached decode step (model.rs:342-397) for every sequence of an open
  * batch whose token counts are all 1: d_token_ids [n] (device int32) are
  * embedded and run through every layer (the batch's decode step per layer);

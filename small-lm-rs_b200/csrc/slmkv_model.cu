@@ -39,11 +39,41 @@
 namespace slmkv {
 namespace {
 
+// Programmatic dependent launch. The single-row steps are chains of short
+// kernels; launched with programmatic stream serialization, a kernel's CTAs
+// start while the previous kernel finishes and run what depends on no
+// earlier kernel (the immutable weights' first copies). Every such kernel
+// calls this before it reads or writes anything another kernel of the
+// stream touches: it returns once the previous kernel has completed and its
+// memory is visible, and only then lets the next kernel launch. Without the
+// launch attribute both instructions are no-ops.
+__device__ __forceinline__ void wait_previous_kernel() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... Params, typename... Args>
+cudaError_t launch_chained(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                           Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // embedding.rs:15-56: row r <- table[ids[r]]; an id outside the vocabulary
 // sets the context's error bit and reads row 0 (the step then fails).
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ table,
                              int32_t vocab, int32_t hidden, float* __restrict__ x,
                              int32_t* __restrict__ err) {
+  wait_previous_kernel();
   const int r = blockIdx.x;
   int32_t id = ids[r];
   if (static_cast<uint32_t>(id) >= static_cast<uint32_t>(vocab)) {
@@ -70,6 +100,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, int32_t rows, int32_
                                const float* __restrict__ w, float eps,
                                uint32_t* __restrict__ out_bf16, float* __restrict__ out_f32,
                                const SeqEntry* __restrict__ seqs) {
+  wait_previous_kernel();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const int src_row = seqs ? seqs[warp].row_offset + seqs[warp].count - 1 : warp;
@@ -244,6 +275,7 @@ __global__ void __launch_bounds__(kProjThreads) proj_kernel(const ProjArgs a) {
     cp_async_commit();
   };
   for (int ch = 0; ch < S && ch < nchunks; ++ch) load_chunk(ch, ch);
+  wait_previous_kernel();  // the rows come from the previous kernels
   // the rows as they arrive (coalesced), then, for the normed modes, the
   // reference's in-order square-sum fold over shared memory by one thread a
   // row (rmsnorm.rs:80-91) and the scaling and bf16 rounding in place
@@ -360,6 +392,7 @@ constexpr int kArgmaxThreads = 256;
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits,
                                                                 int32_t vocab, int32_t* __restrict__ next,
                                                                 int32_t* __restrict__ err) {
+  wait_previous_kernel();
   const float* row = logits + static_cast<size_t>(blockIdx.x) * vocab;
   float best = -INFINITY;
   int32_t idx = 0x7fffffff;
@@ -411,6 +444,10 @@ struct slm_model {
   slm_ctx* ctx = nullptr;
   int32_t V = 0, H = 0, I = 0, L = 0, KV = 0;
   float eps = 0.f, beta_gate = 0.f, beta_up = 0.f;
+  // steps of up to this many token rows run the fused exact-order
+  // projections; 0 when their shared memory does not fit this model
+  int32_t exact_rows = 0;
+  bool exact_fits = false;
   cublasHandle_t blas = nullptr;
   void* weights = nullptr;  // one device allocation for every tensor
   const float* emb = nullptr;         // [V, H] fp32: lookup table and tied vocabulary projection
@@ -511,13 +548,12 @@ int32_t grid_for(size_t work, int32_t threads) {
 }
 
 template <int MODE>
-void launch_proj(const ProjArgs& a, cudaStream_t s) {
+cudaError_t launch_proj(const ProjArgs& a, cudaStream_t s) {
   const int gx = (a.ncols + kProjCols - 1) / kProjCols;
   if (a.rows == 1)
-    proj_kernel<MODE, 1><<<dim3(gx, 1), kProjThreads, proj_smem<MODE>(a.K), s>>>(a);
-  else
-    proj_kernel<MODE, kProjRows><<<dim3(gx, (a.rows + kProjRows - 1) / kProjRows), kProjThreads,
-                                   proj_smem<MODE>(a.K), s>>>(a);
+    return launch_chained(proj_kernel<MODE, 1>, dim3(gx, 1), dim3(kProjThreads), proj_smem<MODE>(a.K), s, a);
+  return launch_chained(proj_kernel<MODE, kProjRows>, dim3(gx, (a.rows + kProjRows - 1) / kProjRows),
+                        dim3(kProjThreads), proj_smem<MODE>(a.K), s, a);
 }
 
 // The layers and the vocabulary projection for `rows` token rows of the
@@ -536,10 +572,15 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
   int32_t* err = ctx_error_word(m->ctx);
   int32_t launches = 0;
   const int32_t H = m->H, I = m->I, KV = m->KV;
-  const bool fused = rows <= kFusedRows;
+  const bool fused = rows <= m->exact_rows;
   __nv_bfloat16* hb = reinterpret_cast<__nv_bfloat16*>(m->xb);
-  embed_kernel<<<rows, 64, 0, s>>>(ids, m->emb, m->V, H, m->x, err);
+  // the fused path's kernels are chained (programmatic dependent launch)
+  cudaError_t le = fused ? launch_chained(embed_kernel, dim3(rows), dim3(64), 0, s, ids, m->emb, m->V, H, m->x, err)
+                         : (embed_kernel<<<rows, 64, 0, s>>>(ids, m->emb, m->V, H, m->x, err), cudaSuccess);
   ++launches;
+  auto launched = [&](cudaError_t e2) {
+    if (le == cudaSuccess) le = e2;
+  };
   auto cache_step = [&](int32_t l) {
     if (prefill) {
       slm_status r = slm_batch_append_layer(b, l, m->k, m->v, 1);
@@ -561,17 +602,17 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       ProjArgs q = a;  // q, k, v with the attention RMSNorm
       q.x = m->x, q.norm_w = Ly.attn_norm, q.K = H, q.ncols = H + 2 * KV, q.w = Ly.wqkv, q.ld = H + 2 * KV;
       q.y0 = m->q, q.y1 = m->k, q.y2 = m->v;
-      launch_proj<kProjQKV>(q, s);
+      launched(launch_proj<kProjQKV>(q, s));
       if ((rc = cache_step(l))) return rc;
       ProjArgs o = a;  // output projection onto the residual
       o.x = m->att, o.K = H, o.ncols = H, o.w = Ly.wo, o.ld = H, o.y0 = m->x;
-      launch_proj<kProjO>(o, s);
+      launched(launch_proj<kProjO>(o, s));
       ProjArgs g = a;  // gate / up with the FFN RMSNorm, SiTU-GLU
       g.x = m->x, g.norm_w = Ly.ffn_norm, g.K = H, g.ncols = I, g.w = Ly.wgu, g.ld = 2 * I, g.h = hb;
-      launch_proj<kProjGU>(g, s);
+      launched(launch_proj<kProjGU>(g, s));
       ProjArgs d = a;  // down projection onto the residual
       d.xh = hb, d.K = I, d.ncols = H, d.w = Ly.wd, d.ld = H, d.y0 = m->x;
-      launch_proj<kProjDown>(d, s);
+      launched(launch_proj<kProjDown>(d, s));
       launches += 4;
       continue;
     }
@@ -602,8 +643,13 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       return blas_fail(m->ctx, "slm_model down projection", bs);
   }
   if (logits || next) {
-    rmsnorm_kernel<<<(out_rows + 3) / 4, 128, 0, s>>>(m->x, out_rows, H, m->final_norm, m->eps, nullptr,
-                                                      m->xf, prefill ? br.d_seqs : nullptr);
+    const SeqEntry* last_rows = prefill ? br.d_seqs : nullptr;
+    if (fused)
+      launched(launch_chained(rmsnorm_kernel, dim3((out_rows + 3) / 4), dim3(128), 0, s, m->x, out_rows, H,
+                              m->final_norm, m->eps, static_cast<uint32_t*>(nullptr), m->xf, last_rows));
+    else
+      rmsnorm_kernel<<<(out_rows + 3) / 4, 128, 0, s>>>(m->x, out_rows, H, m->final_norm, m->eps, nullptr,
+                                                        m->xf, last_rows);
     ++launches;
     float* lg = logits ? logits : m->logits;
     const float one = 1.f, zero = 0.f;
@@ -611,12 +657,13 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
                      lg, m->V);
     if (bs != CUBLAS_STATUS_SUCCESS) return blas_fail(m->ctx, "slm_model vocabulary projection", bs);
     if (next) {
-      argmax_kernel<<<out_rows, kArgmaxThreads, 0, s>>>(lg, m->V, next, err);
+      launched(launch_chained(argmax_kernel, dim3(out_rows), dim3(kArgmaxThreads), 0, s,
+                              static_cast<const float*>(lg), m->V, next, err));
       ++launches;
     }
   }
   ctx_count_launches(m->ctx, launches);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = le != cudaSuccess ? le : cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(m->ctx, "slm_model step", e);
   return SLM_OK;
 }
@@ -727,8 +774,19 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
     return blas_fail(ctx, "slm_model_create", bs);
   }
   cublasSetMathMode(m->blas, CUBLAS_DEFAULT_MATH);  // fp32 SGEMM without TF32
-  // the fused projections stage kProjRows input rows and two weight chunks
-  {
+  // the fused projections stage kProjRows input rows and the weight ring;
+  // a model whose rows do not fit runs every step on the GEMM path
+  int dev = 0, optin = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) {
+    slm_model_destroy(m);
+    return cuda_fail(ctx, "slm_model_create", e);
+  }
+  m->exact_fits = std::max({proj_smem<kProjQKV>(H), proj_smem<kProjO>(H), proj_smem<kProjGU>(H),
+                            proj_smem<kProjDown>(I)}) <= static_cast<size_t>(optin);
+  m->exact_rows = m->exact_fits ? kFusedRows : 0;
+  if (m->exact_fits) {
     auto attr = [&](auto kernel, size_t bytes) {
       return bytes > 48 * 1024 ? cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                       static_cast<int>(bytes))
@@ -757,6 +815,19 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
                                          bf(x.gu), bf(x.d)});
   }
   *out = m;
+  return SLM_OK;
+}
+
+slm_status slm_model_set_exact_rows(slm_model* m, int32_t max_rows) {
+  if (!m) return SLM_ERR_INVALID_INPUT;
+  if (max_rows < 0 || max_rows > kFusedRows)
+    return ctx_fail(m->ctx, SLM_ERR_INVALID_INPUT,
+                    "invalid input for model projections: exact-order rows must be in [0, 1024]");
+  if (max_rows > 0 && !m->exact_fits)
+    return ctx_fail(m->ctx, SLM_ERR_INVALID_INPUT,
+                    "invalid input for model projections: this model's rows do not fit the exact-order "
+                    "kernels' shared memory");
+  m->exact_rows = max_rows;
   return SLM_OK;
 }
 

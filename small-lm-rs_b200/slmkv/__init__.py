@@ -151,6 +151,7 @@ SIGNATURES = {
     "slm_model_create": (C.c_int, [_vp, C.POINTER(ModelConfig), C.POINTER(_vp), _i32,
                                    C.POINTER(_vp)]),
     "slm_model_destroy": (C.c_int, [_vp]),
+    "slm_model_set_exact_rows": (C.c_int, [_vp, _i32]),
     "slm_model_decode": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "slm_model_prefill": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "slm_model_load_safetensors": (C.c_int, [_vp, C.POINTER(ModelConfig), C.c_char_p, _i64,
@@ -740,6 +741,12 @@ class Model:
                                                     str(path).encode(), expected_parameter_count,
                                                     C.byref(h)))
         return cls(pool, vocab_size=vocab_size, intermediate_size=intermediate_size, _handle=h)
+
+    def set_exact_rows(self, max_rows: int) -> None:
+        """Steps of up to ``max_rows`` token rows (0..1024) project in the
+        reference's accumulation order (linear.rs:98-103); larger steps, or
+        all when 0, on tensor-core GEMMs."""
+        self.pool.check(lib().slm_model_set_exact_rows(self._h, int(max_rows)))
 
     def decode(self, batch: "Batch", token_ids, logits=None, next_tokens=None) -> None:
         """model.rs:342-397 for every sequence of ``batch`` (counts 1):

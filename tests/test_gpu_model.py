@@ -24,7 +24,7 @@ torch = pytest.importorskip("torch")
 slmkv = pytest.importorskip("slmkv")
 
 
-def random_model(seed, vocab, hidden, hkv, inter, layers, d=64):
+def random_model(seed, vocab, hidden, hkv, inter, layers, d=64, scale=0.05):
     rng = np.random.default_rng(seed)
     kv = hkv * d
     shapes = [(vocab, hidden)]
@@ -32,15 +32,18 @@ def random_model(seed, vocab, hidden, hkv, inter, layers, d=64):
         shapes += [(hidden,), (hidden, hidden), (kv, hidden), (kv, hidden), (hidden, hidden),
                    (hidden,), (inter, hidden), (inter, hidden), (hidden, inter)]
     shapes.append((hidden,))
-    # norms near 1, matrices N(0, 0.05^2) so the logits spread out
+    # norms near 1, matrices N(0, scale^2) so the logits spread out
     return [(1.0 + 0.05 * rng.standard_normal(s)).astype(np.float32) if len(s) == 1
-            else (0.05 * rng.standard_normal(s)).astype(np.float32) for s in shapes]
+            else (scale * rng.standard_normal(s)).astype(np.float32) for s in shapes]
 
 
-def _run(kv_dtype, prompts, steps=4, seed=7, ctx=128):
-    vocab, hq, hkv, d, inter, layers = 1024, 4, 2, 64, 704, 2
+def _run(kv_dtype, prompts, steps=4, seed=7, ctx=128, exact_rows=None,
+         dims=(1024, 4, 2, 64, 704, 2)):
+    vocab, hq, hkv, d, inter, layers = dims
     hidden = hq * d
-    tensors = random_model(seed, vocab, hidden, hkv, inter, layers)
+    threads = O.max_threads()
+    # matrices scaled with the width so activations stay as at hidden 256
+    tensors = random_model(seed, vocab, hidden, hkv, inter, layers, scale=0.8 / np.sqrt(hidden))
     ocfg = dict(vocab_size=vocab, hidden_size=hidden, intermediate_size=inter, num_layers=layers,
                 num_query_heads=hq, num_key_value_heads=hkv, head_dimension=d,
                 rms_norm_epsilon=1e-5, rope_theta=10000.0, situ_beta_gate=4.0, situ_beta_up=25.0)
@@ -51,6 +54,8 @@ def _run(kv_dtype, prompts, steps=4, seed=7, ctx=128):
                         kv_dtype=kv_dtype, device=0)
     pool.shuffle(seed)
     model = slmkv.Model(pool, vocab_size=vocab, intermediate_size=inter, tensors=tensors)
+    if exact_rows is not None:
+        model.set_exact_rows(exact_rows)
     caches = [pool.allocate_kv_cache(ctx) for _ in prompts]
     ocaches = [omodel.new_cache(ctx, quantize_bf16=(kv_dtype == slmkv.KV_BF16)) for _ in prompts]
     n = len(prompts)
@@ -60,7 +65,7 @@ def _run(kv_dtype, prompts, steps=4, seed=7, ctx=128):
     with pool.begin(caches, [len(p) for p in prompts]) as b:
         model.prefill(b, ids, logits, nxt)
     got_all, ref_all = [], []
-    ref = np.stack([omodel.prefill(oc, p)[-1] for oc, p in zip(ocaches, prompts)])
+    ref = np.stack([omodel.prefill(oc, p, threads)[-1] for oc, p in zip(ocaches, prompts)])
     got_all.append(logits.cpu().numpy())
     ref_all.append(ref)
     tokens = nxt.cpu().numpy()
@@ -69,7 +74,7 @@ def _run(kv_dtype, prompts, steps=4, seed=7, ctx=128):
         cur = torch.tensor(tokens, dtype=torch.int32, device="cuda:0")
         with pool.begin(caches, 1) as b:
             model.decode(b, cur, logits, nxt)
-        ref = np.stack([omodel.decode(oc, int(t)) for oc, t in zip(ocaches, tokens)])
+        ref = np.stack([omodel.decode(oc, int(t), threads) for oc, t in zip(ocaches, tokens)])
         got_all.append(logits.cpu().numpy())
         ref_all.append(ref)
         tokens = nxt.cpu().numpy()
@@ -119,6 +124,40 @@ def test_long_prefill_on_the_tensor_core_path():
     m = _run(slmkv.KV_F32, prompts, steps=2, ctx=512)
     check_thresholds(m)
     print("long prefill, f32 KV logits vs oracle:", m)
+
+
+def test_every_step_on_the_tensor_core_path():
+    # exact-order rows 0: prefill and decode projections all as GEMMs
+    m = _run(slmkv.KV_F32, PROMPTS, exact_rows=0)
+    check_thresholds(m)
+    print("GEMM projections, f32 KV logits vs oracle:", m)
+
+
+@pytest.mark.parametrize("exact_rows", [None, 0])
+def test_scaled_gqa_shape_bf16(exact_rows):
+    # the scaled GQA model's widths (hidden 2048 = 32 x 64, 8 KV heads, FFN
+    # 5632, bf16 KV) on two layers and a small vocabulary: the exact-order
+    # kernels at their widest staging (5632 down-projection inputs) and the
+    # tensor-core GEMMs
+    prompts = [np.array(p, np.uint32) for p in ([7, 1000, 3], list(range(200, 213)), [5] * 6)]
+    m = _run(slmkv.KV_BF16, prompts, steps=3, exact_rows=exact_rows,
+             dims=(1024, 32, 8, 64, 5632, 2))
+    check_thresholds(m)
+    print(f"scaled GQA shape, exact rows {exact_rows}, bf16 KV logits vs oracle:", m)
+
+
+def test_exact_rows_range_is_checked():
+    pool = slmkv.KvPool(num_layers=1, num_query_heads=4, num_key_value_heads=2, head_dimension=64,
+                        context_length=64, num_blocks=8, max_sequences=1, device=0)
+    model = slmkv.Model(pool, vocab_size=64, intermediate_size=64,
+                        tensors=random_model(1, 64, 256, 2, 64, 1))
+    for bad in (-1, 1025):
+        with pytest.raises(slmkv.InvalidInput):
+            model.set_exact_rows(bad)
+    model.set_exact_rows(0)
+    model.set_exact_rows(1024)
+    model.close()
+    pool.close()
 
 
 def test_out_of_vocabulary_token_fails_and_rolls_back():
