@@ -91,43 +91,62 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
-// rmsnorm.rs:80-91, one warp per row: square sum (fma), inverse RMS
-// 1 / sqrt(s / width + eps), out = x * inv * scale (two products, in that
-// order). Output rows are bf16 (the next projection's rounded operand) or
-// fp32 (the vocabulary projection's). With `seqs`, output row i normalises
-// the last token row of sequence i (the prefill's final positions).
-__global__ void rmsnorm_kernel(const float* __restrict__ x, int32_t rows, int32_t hidden,
-                               const float* __restrict__ w, float eps,
-                               uint32_t* __restrict__ out_bf16, float* __restrict__ out_f32,
-                               const SeqEntry* __restrict__ seqs) {
+// rmsnorm.rs:80-91, one CTA per row: square sum (fma; per thread, then a
+// warp and a CTA tree in fixed order), inverse RMS 1 / sqrt(s / width + eps),
+// out = x * inv * scale (two products, in that order). The row stays in
+// registers (all its loads in flight at once). Output rows are bf16 (the
+// next projection's rounded operand) or fp32 (the vocabulary projection's).
+// With `seqs`, output row i normalises the last token row of sequence i (the
+// prefill's final positions).
+constexpr int kNormThreads = 256;
+constexpr int kNormVec = 8;  // float4s a thread holds: rows up to 8192 wide
+constexpr int kNormMaxWidth = kNormThreads * 4 * kNormVec;
+__global__ void __launch_bounds__(kNormThreads)
+    rmsnorm_kernel(const float* __restrict__ x, int32_t rows, int32_t hidden, const float* __restrict__ w,
+                   float eps, uint32_t* __restrict__ out_bf16, float* __restrict__ out_f32,
+                   const SeqEntry* __restrict__ seqs) {
   wait_previous_kernel();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= rows) return;
-  const int src_row = seqs ? seqs[warp].row_offset + seqs[warp].count - 1 : warp;
+  const int row = blockIdx.x, tid = threadIdx.x;
+  if (row >= rows) return;
+  const int src_row = seqs ? seqs[row].row_offset + seqs[row].count - 1 : row;
   const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(src_row) * hidden);
   const int n4 = hidden / 4;
+  float4 v[kNormVec];
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = tid + j * kNormThreads;
+    v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   float s = 0.f;
-  for (int i = lane; i < n4; i += 32) {
-    const float4 v = xr[i];
-    s = fmaf(v.x, v.x, s);
-    s = fmaf(v.y, v.y, s);
-    s = fmaf(v.z, v.z, s);
-    s = fmaf(v.w, v.w, s);
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    s = fmaf(v[j].x, v[j].x, s);
+    s = fmaf(v[j].y, v[j].y, s);
+    s = fmaf(v[j].z, v[j].z, s);
+    s = fmaf(v[j].w, v[j].w, s);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  __shared__ float part[kNormThreads / 32];
+  if ((tid & 31) == 0) part[tid >> 5] = s;
+  __syncthreads();
+  s = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormThreads / 32; ++k) s += part[k];
   const float inv = 1.f / sqrtf(__fdiv_rn(s, static_cast<float>(hidden)) + eps);
   const float4* wr = reinterpret_cast<const float4*>(w);
-  for (int i = lane; i < n4; i += 32) {
-    const float4 v = xr[i], g = wr[i];
-    const float a = __fmul_rn(__fmul_rn(v.x, inv), g.x), b = __fmul_rn(__fmul_rn(v.y, inv), g.y);
-    const float c = __fmul_rn(__fmul_rn(v.z, inv), g.z), d = __fmul_rn(__fmul_rn(v.w, inv), g.w);
-    if (out_bf16) {
-      reinterpret_cast<uint2*>(out_bf16 + static_cast<size_t>(warp) * (hidden / 2))[i] =
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = tid + j * kNormThreads;
+    if (i >= n4) break;
+    const float4 g = wr[i];
+    const float a = __fmul_rn(__fmul_rn(v[j].x, inv), g.x), b = __fmul_rn(__fmul_rn(v[j].y, inv), g.y);
+    const float c = __fmul_rn(__fmul_rn(v[j].z, inv), g.z), d = __fmul_rn(__fmul_rn(v[j].w, inv), g.w);
+    if (out_bf16)
+      reinterpret_cast<uint2*>(out_bf16 + static_cast<size_t>(row) * (hidden / 2))[i] =
           make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
-    } else {
-      reinterpret_cast<float4*>(out_f32 + static_cast<size_t>(warp) * hidden)[i] = make_float4(a, b, c, d);
-    }
+    else
+      reinterpret_cast<float4*>(out_f32 + static_cast<size_t>(row) * hidden)[i] = make_float4(a, b, c, d);
   }
 }
 
@@ -616,9 +635,8 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       launches += 4;
       continue;
     }
-    const int32_t norm_grid = (rows + 3) / 4;  // 4 warps (rows) a CTA
     const int32_t nqkv = H + 2 * KV;
-    rmsnorm_kernel<<<norm_grid, 128, 0, s>>>(m->x, rows, H, Ly.attn_norm, m->eps, m->xb, nullptr, nullptr);
+    rmsnorm_kernel<<<rows, kNormThreads, 0, s>>>(m->x, rows, H, Ly.attn_norm, m->eps, m->xb, nullptr, nullptr);
     ++launches;
     if ((bs = gemm_t(m->blas, m->xb, rows, H, Ly.wqkv, nqkv, H, m->q, 0.f)) != CUBLAS_STATUS_SUCCESS ||
         (bs = gemm_t(m->blas, m->xb, rows, H, Ly.wqkv + H, nqkv, KV, m->k, 0.f)) != CUBLAS_STATUS_SUCCESS ||
@@ -632,7 +650,7 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
     ++launches;
     if ((bs = gemm_t(m->blas, m->xb, rows, H, Ly.wo, H, H, m->x, 1.f)) != CUBLAS_STATUS_SUCCESS)
       return blas_fail(m->ctx, "slm_model output projection", bs);
-    rmsnorm_kernel<<<norm_grid, 128, 0, s>>>(m->x, rows, H, Ly.ffn_norm, m->eps, m->xb, nullptr, nullptr);
+    rmsnorm_kernel<<<rows, kNormThreads, 0, s>>>(m->x, rows, H, Ly.ffn_norm, m->eps, m->xb, nullptr, nullptr);
     ++launches;
     if ((bs = gemm_t(m->blas, m->xb, rows, H, Ly.wgu, 2 * I, 2 * I, m->gu, 0.f)) != CUBLAS_STATUS_SUCCESS)
       return blas_fail(m->ctx, "slm_model gate/up projection", bs);
@@ -645,11 +663,11 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
   if (logits || next) {
     const SeqEntry* last_rows = prefill ? br.d_seqs : nullptr;
     if (fused)
-      launched(launch_chained(rmsnorm_kernel, dim3((out_rows + 3) / 4), dim3(128), 0, s, m->x, out_rows, H,
+      launched(launch_chained(rmsnorm_kernel, dim3(out_rows), dim3(kNormThreads), 0, s, m->x, out_rows, H,
                               m->final_norm, m->eps, static_cast<uint32_t*>(nullptr), m->xf, last_rows));
     else
-      rmsnorm_kernel<<<(out_rows + 3) / 4, 128, 0, s>>>(m->x, out_rows, H, m->final_norm, m->eps, nullptr,
-                                                        m->xf, last_rows);
+      rmsnorm_kernel<<<out_rows, kNormThreads, 0, s>>>(m->x, out_rows, H, m->final_norm, m->eps, nullptr,
+                                                       m->xf, last_rows);
     ++launches;
     float* lg = logits ? logits : m->logits;
     const float one = 1.f, zero = 0.f;
@@ -686,10 +704,10 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
   const int32_t V = config->vocab_size, H = config->hidden_size, I = config->intermediate_size;
   const int32_t L = c.num_layers, KV = c.num_key_value_heads * c.head_dimension;
   // config.rs:91-198 (the parts the device path relies on)
-  if (V <= 0 || H != c.num_query_heads * c.head_dimension || I <= 0 || I % 8 != 0)
+  if (V <= 0 || H != c.num_query_heads * c.head_dimension || H > kNormMaxWidth || I <= 0 || I % 8 != 0)
     return ctx_fail(ctx, SLM_ERR_INVALID_CONFIGURATION,
-                    "invalid model configuration: vocab > 0, hidden = query heads x head dimension, "
-                    "intermediate a positive multiple of 8");
+                    "invalid model configuration: vocab > 0, hidden = query heads x head dimension "
+                    "(at most 8192), intermediate a positive multiple of 8");
   if (!(config->rms_norm_epsilon > 0.f) || !std::isfinite(config->rms_norm_epsilon) ||
       !std::isfinite(config->situ_beta_gate) || !std::isfinite(config->situ_beta_up) ||
       config->situ_beta_gate == 0.f || config->situ_beta_up == 0.f)
