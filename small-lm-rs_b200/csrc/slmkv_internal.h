@@ -164,6 +164,31 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s);
 cudaError_t launch_apply_updates(const PoolGeom& g, const TableUpdate* updates, int32_t n_updates,
                                  const CopyJob* copies, int32_t n_copies, cudaStream_t s);
 
+// ---- few-row projections on the tensor cores (slmkv_rowgemm.cu) ----
+enum : int { kRowQKV = 0, kRowO = 1, kRowGU = 2, kRowDown = 3 };
+struct RowGemmLaunch {
+  CUtensorMap tmap_w;  // weights [K][ld] bf16, 64 x 64 boxes, 128-byte swizzle
+  CUtensorMap tmap_x;  // rows [rows][K] bf16 (encoded by launch_row_gemm)
+  const void* x;
+  int32_t rows, K;
+  int32_t ncols;  // output columns (QKV: H + 2 KV; O, Down: H; GU: I)
+  int32_t H, KV, I;
+  int32_t nchunks, chunks_per_split;  // filled by launch_row_gemm
+  float* y0;     // QKV: q; O, Down: the residual stream (accumulated)
+  float* y1;     // QKV: k
+  float* y2;     // QKV: v
+  void* h;       // GU: [rows][I] bf16
+  float beta_gate, beta_up;
+  int32_t* err;
+};
+struct RowGemmPlan {
+  int32_t rt, row_tiles, col_tiles, nchunks, chunks_per_split, splits;
+};
+RowGemmPlan plan_row_gemm(int mode, int32_t rows, int32_t K, int32_t ncols, int32_t sms);
+cudaError_t encode_row_gemm_map(CUtensorMap* map, const void* base, int32_t inner, int32_t outer,
+                                int32_t box_inner, int32_t box_outer);
+cudaError_t launch_row_gemm(int mode, RowGemmLaunch p, const RowGemmPlan& q, cudaStream_t s);
+
 // ---- the model step's view of a context and an open batch (slmkv_host.cpp) ----
 struct BatchRows {
   cudaStream_t stream;

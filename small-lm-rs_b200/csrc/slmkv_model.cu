@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(kNormThreads)
 
 // fp32 rows -> bf16 rows (round to nearest even), 4 values a thread.
 __global__ void round_bf16_kernel(const float4* __restrict__ in, size_t n4, uint2* __restrict__ out) {
+  wait_previous_kernel();
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const float4 v = in[i];
@@ -207,7 +208,8 @@ constexpr int kProjThreads = 64;   // two output columns each
 constexpr int kProjCols = 2 * kProjThreads;
 constexpr int kProjRows = 4;       // token rows a CTA
 constexpr int kProjChunk = 64;     // weight rows a stage
-constexpr int kFusedRows = 1024;   // above this, tensor-core GEMMs (cuBLAS)
+constexpr int kFusedRows = 1024;   // above this, tensor-core GEMMs
+constexpr int kRowGemmRows = 512;  // up to this, this library's row GEMMs; beyond, cuBLAS
 
 struct ProjArgs {
   const float* x;               // QKV, GU: residual stream; O: attention output  [rows, K] fp32
@@ -476,12 +478,15 @@ struct slm_model {
   struct Layer {
     const float *attn_norm, *ffn_norm;  // [H]
     const __nv_bfloat16 *wqkv, *wo, *wgu, *wd;
+    CUtensorMap tm_qkv, tm_o, tm_gu, tm_d;  // the same matrices for the tensor-core row GEMMs
   };
   std::vector<Layer> layers;
+  int32_t sms = 148;
   // scratch, grown on demand: rows for token rows, out rows for projected rows
   int32_t rows_cap = 0, out_cap = 0;
   float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *gu = nullptr;
   uint32_t* xb = nullptr;  // bf16 pairs, [rows, max(H, I) / 2]
+  uint32_t* hb = nullptr;  // bf16 pairs, [rows, I / 2]: the row GEMMs' SiTU-GLU output
   float *xf = nullptr, *logits = nullptr;
 };
 
@@ -511,10 +516,11 @@ slm_status blas_fail(slm_ctx* c, const char* what, cublasStatus_t e) {
 void free_scratch(slm_model* m) {
   for (void* p : {static_cast<void*>(m->x), static_cast<void*>(m->q), static_cast<void*>(m->k),
                   static_cast<void*>(m->v), static_cast<void*>(m->att), static_cast<void*>(m->gu),
-                  static_cast<void*>(m->xb), static_cast<void*>(m->xf), static_cast<void*>(m->logits)})
+                  static_cast<void*>(m->xb), static_cast<void*>(m->hb), static_cast<void*>(m->xf),
+                  static_cast<void*>(m->logits)})
     if (p) cudaFree(p);
   m->x = m->q = m->k = m->v = m->att = m->gu = m->xf = m->logits = nullptr;
-  m->xb = nullptr;
+  m->xb = m->hb = nullptr;
   m->rows_cap = m->out_cap = 0;
 }
 
@@ -538,6 +544,7 @@ slm_status ensure_scratch(slm_model* m, int32_t rows, int32_t out_rows, cudaStre
                 {reinterpret_cast<void**>(&m->att), R * m->H * 4},
                 {reinterpret_cast<void**>(&m->gu), R * 2 * m->I * 4},
                 {reinterpret_cast<void**>(&m->xb), R * wide * 2},
+                {reinterpret_cast<void**>(&m->hb), R * m->I * 2},
                 {reinterpret_cast<void**>(&m->xf), O * m->H * 4},
                 {reinterpret_cast<void**>(&m->logits), O * m->V * 4}};
   for (const A& a : allocs) {
@@ -592,6 +599,8 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
   int32_t launches = 0;
   const int32_t H = m->H, I = m->I, KV = m->KV;
   const bool fused = rows <= m->exact_rows;
+  // otherwise: few rows on the tensor-core row GEMMs, many on cuBLAS
+  const bool row_gemms = !fused && rows <= kRowGemmRows;
   __nv_bfloat16* hb = reinterpret_cast<__nv_bfloat16*>(m->xb);
   // the fused path's kernels are chained (programmatic dependent launch)
   cudaError_t le = fused ? launch_chained(embed_kernel, dim3(rows), dim3(64), 0, s, ids, m->emb, m->V, H, m->x, err)
@@ -636,6 +645,50 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       continue;
     }
     const int32_t nqkv = H + 2 * KV;
+    if (row_gemms) {
+      // tensor-core row GEMMs (slmkv_rowgemm.cu), every kernel chained
+      RowGemmLaunch a{};
+      a.rows = rows;
+      a.H = H;
+      a.KV = KV;
+      a.I = I;
+      a.beta_gate = m->beta_gate;
+      a.beta_up = m->beta_up;
+      a.err = err;
+      auto gemm = [&](int mode, const CUtensorMap& tw, const void* x, int32_t K, int32_t ncols) -> slm_status {
+        const RowGemmPlan q = plan_row_gemm(mode, rows, K, ncols, m->sms);
+        RowGemmLaunch g = a;
+        g.tmap_w = tw;
+        g.x = x;
+        g.K = K;
+        g.ncols = ncols;
+        const cudaError_t e2 = launch_row_gemm(mode, g, q, s);
+        if (e2 != cudaSuccess) return cuda_fail(m->ctx, "slm_model row GEMM", e2);
+        ++launches;
+        return SLM_OK;
+      };
+      launched(launch_chained(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, s,
+                              static_cast<const float*>(m->x), rows, H, Ly.attn_norm, m->eps, m->xb,
+                              static_cast<float*>(nullptr), static_cast<const SeqEntry*>(nullptr)));
+      ++launches;
+      a.y0 = m->q, a.y1 = m->k, a.y2 = m->v;
+      if ((rc = gemm(kRowQKV, Ly.tm_qkv, m->xb, H, nqkv))) return rc;
+      if ((rc = cache_step(l))) return rc;
+      const size_t n4 = static_cast<size_t>(rows) * H / 4;
+      launched(launch_chained(round_bf16_kernel, dim3(grid_for(n4, 256)), dim3(256), 0, s,
+                              reinterpret_cast<const float4*>(m->att), n4, reinterpret_cast<uint2*>(m->xb)));
+      ++launches;
+      a.y0 = m->x, a.y1 = a.y2 = nullptr;
+      if ((rc = gemm(kRowO, Ly.tm_o, m->xb, H, H))) return rc;
+      launched(launch_chained(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, s,
+                              static_cast<const float*>(m->x), rows, H, Ly.ffn_norm, m->eps, m->xb,
+                              static_cast<float*>(nullptr), static_cast<const SeqEntry*>(nullptr)));
+      ++launches;
+      a.h = m->hb;
+      if ((rc = gemm(kRowGU, Ly.tm_gu, m->xb, H, I))) return rc;
+      if ((rc = gemm(kRowDown, Ly.tm_d, m->hb, I, H))) return rc;
+      continue;
+    }
     rmsnorm_kernel<<<rows, kNormThreads, 0, s>>>(m->x, rows, H, Ly.attn_norm, m->eps, m->xb, nullptr, nullptr);
     ++launches;
     if ((bs = gemm_t(m->blas, m->xb, rows, H, Ly.wqkv, nqkv, H, m->q, 0.f)) != CUBLAS_STATUS_SUCCESS ||
@@ -826,11 +879,33 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
   const uint8_t* base = static_cast<const uint8_t*>(m->weights);
   m->emb = reinterpret_cast<const float*>(base + o_emb);
   m->final_norm = reinterpret_cast<const float*>(base + o_final);
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) {
+    slm_model_destroy(m);
+    return cuda_fail(ctx, "slm_model_create", e);
+  }
+  m->sms = sms;
   for (const LayerOff& x : lo) {
     auto bf = [&](size_t o) { return reinterpret_cast<const __nv_bfloat16*>(base + o); };
-    m->layers.push_back(slm_model::Layer{reinterpret_cast<const float*>(base + x.an),
-                                         reinterpret_cast<const float*>(base + x.fn), bf(x.qkv), bf(x.o),
-                                         bf(x.gu), bf(x.d)});
+    slm_model::Layer Ly{};
+    Ly.attn_norm = reinterpret_cast<const float*>(base + x.an);
+    Ly.ffn_norm = reinterpret_cast<const float*>(base + x.fn);
+    Ly.wqkv = bf(x.qkv);
+    Ly.wo = bf(x.o);
+    Ly.wgu = bf(x.gu);
+    Ly.wd = bf(x.d);
+    // [K rows][columns] bf16, 64 x 64 boxes
+    const int32_t nqkv = H + 2 * KV;
+    e = encode_row_gemm_map(&Ly.tm_qkv, Ly.wqkv, nqkv, H, 64, 64);
+    if (e == cudaSuccess) e = encode_row_gemm_map(&Ly.tm_o, Ly.wo, H, H, 64, 64);
+    if (e == cudaSuccess) e = encode_row_gemm_map(&Ly.tm_gu, Ly.wgu, 2 * I, H, 64, 64);
+    if (e == cudaSuccess) e = encode_row_gemm_map(&Ly.tm_d, Ly.wd, H, I, 64, 64);
+    if (e != cudaSuccess) {
+      slm_model_destroy(m);
+      return cuda_fail(ctx, "slm_model_create (weight tensor maps)", e);
+    }
+    m->layers.push_back(Ly);
   }
   *out = m;
   return SLM_OK;
