@@ -107,7 +107,8 @@ def parse():
     ap.add_argument("--exact-rows", type=int, default=None,
                     help="model workloads: steps of up to this many token rows project in the "
                          "reference's accumulation order, larger ones on tensor-core GEMMs "
-                         "(default: the library's 1024; the scaled GQA model: 0)")
+                         "(default: the 8M model at batch 1: 1024; serve and prefix: 1; the scaled "
+                         "GQA model: 0)")
     args = ap.parse_args()
     select_workload(args.workload, args.batch)
     return args
@@ -621,8 +622,9 @@ def run_serve(args):
     pool.shuffle(args.seed + 1)
     model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=MODEL_INTER,
                         tensors=model_tensors(args.seed))
-    if args.exact_rows is not None:
-        model.set_exact_rows(args.exact_rows)
+    # batched steps on the tensor cores (another accumulation order, within
+    # the reference's logit parity thresholds); single-row steps exact
+    model.set_exact_rows(1 if args.exact_rows is None else args.exact_rows)
     sched = slmkv.Scheduler(pool, max_running=B, max_prefill_tokens=SERVE_PREFILL_TOKENS)
     # token history: row per request of this rank, prompt tokens first
     row_of = {rid: k for k, rid in enumerate(mine)}
@@ -740,7 +742,7 @@ def run_serve(args):
                                 "f32 KV, random N(0, 0.02^2) weights), random prompt ids, "
                                 "greedy decoding"),
                    "name": "serve", "requests_per_rank": len(order), "seed": args.seed,
-                   "exact_rows": 1024 if args.exact_rows is None else args.exact_rows},
+                   "exact_rows": 1 if args.exact_rows is None else args.exact_rows},
         "output_tokens": int(tokens.item()), "preemptions": counts["preemptions"],
         "gpu_launches": pool.launch_count(),
     }
@@ -780,8 +782,7 @@ def run_prefix(args):
     pool.shuffle(args.seed + 1)
     model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=MODEL_INTER,
                         tensors=model_tensors(args.seed))
-    if args.exact_rows is not None:
-        model.set_exact_rows(args.exact_rows)
+    model.set_exact_rows(1 if args.exact_rows is None else args.exact_rows)
 
     def ids(tokens):
         return torch.tensor(tokens, dtype=torch.int32, device=dev)
@@ -855,7 +856,7 @@ def run_prefix(args):
                                 f"tokens, then {PREFIX_DECODE_STEPS} greedy decode steps each; "
                                 f"{LAYERS} layers, hidden {HQ * D}, Hq={HQ}, Hkv={HKV}, d={D}, "
                                 "f32 KV, random N(0, 0.02^2) weights"), "name": "prefix",
-                   "exact_rows": 1024 if args.exact_rows is None else args.exact_rows,
+                   "exact_rows": 1 if args.exact_rows is None else args.exact_rows,
                    "seed": args.seed},
         "prefill_tokens_computed": computed, "prefill_tokens_without_reuse": without,
         "prefill_tokens_saved": without - computed, "prefix_blocks_indexed": indexed,
