@@ -1211,8 +1211,9 @@ def run_gqa_model(args):
                         "synchronizes every step"},
         "gpu_launches": launches,
         "clocks": clk,
-        "projections": "cuBLAS bf16 GEMMs (fp32 accumulate); fp32 SGEMM for the tied head; "
-                       "embedding, RMSNorm, rounding, SiTU, argmax and the KV step are this "
+        "projections": "this library's tcgen05 row GEMMs (bf16 operands, fp32 accumulate; "
+                       "cuBLAS beyond 512 rows: the prefill); cuBLAS fp32 SGEMM for the tied "
+                       "head; embedding, RMSNorm, rounding, argmax and the KV step are this "
                        "library's kernels",
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
