@@ -279,20 +279,21 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
     if (sp < splits) asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(part_addr), "r"(sp));
     peer[sp] = a;
   }
-  // row r, tile column c summed over the splits in split order
+  // row r, tile column c summed over the splits in split order: every
+  // split's value is requested first (the loads depend only on the addresses
+  // mapped after the barrier), then added in order
   auto reduced = [&](int r, int c) {
-    float t = 0.f;
+    float x[kRgMaxSplits];
 #pragma unroll
     for (int sp = 0; sp < kRgMaxSplits; ++sp) {
-      if (sp < splits) {
-        float x;
-        asm volatile("ld.shared::cluster.f32 %0, [%1];"
-                     : "=f"(x)
-                     : "r"(peer[sp] + 4u * static_cast<uint32_t>(r * kRgTileM + c))
-                     : "memory");
-        t += x;
-      }
+      x[sp] = 0.f;
+      if (sp < splits)
+        asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(x[sp]) : "r"(peer[sp] + 4u * static_cast<uint32_t>(r * kRgTileM + c)));
     }
+    float t = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < kRgMaxSplits; ++sp)
+      if (sp < splits) t += x[sp];
     return t;
   };
   if (run) {
