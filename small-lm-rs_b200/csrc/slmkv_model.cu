@@ -407,6 +407,89 @@ __global__ void __launch_bounds__(kProjThreads) proj_kernel(const ProjArgs a) {
   }
 }
 
+// linear.rs:119-152, the tied vocabulary projection (fp32, unrounded), for
+// up to 64 rows: logits[r][v] = sum_k x[r][k] emb[v][k]. A CTA stages 8 rows
+// in shared memory (small enough for two CTAs an SM, so that enough
+// embedding loads are in flight); a warp takes 4 vocabulary entries at a
+// time, its lanes 4 features apart (coalesced 16-byte loads of the embedding
+// rows, the next step's issued before this step's FMAs), 32 sums a lane,
+// then a reduce-scatter across the lanes (5 exchange
+// steps, each halving the sums a lane holds: lane l ends with row l / 4,
+// entry l % 4). CTAs of the other row groups read the same embedding rows at
+// the same time (from L2).
+constexpr int kHeadThreads = 256;
+constexpr int kHeadRows = 8;       // rows a CTA
+constexpr int kHeadEntries = 64;   // vocabulary entries a CTA: 8 warps x 4, two rounds
+constexpr int kHeadMaxRows = 64;
+constexpr int kHeadMaxWidth = 4096;  // 8 rows x 16 KiB of shared memory
+template <int N>
+__device__ __forceinline__ void head_halve(float (&a)[32], int lane, int o) {
+  const bool upper = (lane & o) != 0;
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    const float send = upper ? a[i] : a[i + N / 2];
+    const float keep = upper ? a[i + N / 2] : a[i];
+    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+  }
+}
+__global__ void __launch_bounds__(kHeadThreads, 2) head_kernel(const float* __restrict__ x, int32_t rows, int32_t H,
+                                                            const float* __restrict__ emb, int32_t V,
+                                                            float* __restrict__ logits) {
+  wait_previous_kernel();
+  extern __shared__ float4 head_x[];  // [kHeadRows][H / 4]
+  const int n4 = H / 4;
+  const int r0 = blockIdx.y * kHeadRows, nr = min(kHeadRows, rows - r0);
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  for (int r = 0; r < kHeadRows; ++r)
+    for (int k = threadIdx.x; k < n4; k += kHeadThreads)
+      head_x[r * n4 + k] = r < nr ? x4[static_cast<size_t>(r0 + r) * n4 + k] : make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float4* e4 = reinterpret_cast<const float4*>(emb);
+#pragma unroll 1
+  for (int round = 0; round < kHeadEntries / 32; ++round) {
+    const int v0 = blockIdx.x * kHeadEntries + round * 32 + warp * 4;
+    if (v0 >= V) break;  // warp-uniform
+    float a[32];  // a[4 r + j]: row r, entry v0 + j
+#pragma unroll
+    for (int i = 0; i < 32; ++i) a[i] = 0.f;
+    const float4* ev[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ev[j] = e4 + static_cast<size_t>(min(v0 + j, V - 1)) * n4;
+    // the next step's embedding loads are issued before this step's FMAs
+    float4 e[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) e[j] = lane < n4 ? __ldcg(ev[j] + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = lane; k < n4; k += 32) {
+      float4 en[4];
+      const bool more = k + 32 < n4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) en[j] = more ? __ldcg(ev[j] + k + 32) : e[j];
+#pragma unroll
+      for (int r = 0; r < kHeadRows; ++r) {
+        const float4 xv = head_x[r * n4 + k];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float t = a[4 * r + j];
+          t = fmaf(xv.x, e[j].x, t);
+          t = fmaf(xv.y, e[j].y, t);
+          t = fmaf(xv.z, e[j].z, t);
+          a[4 * r + j] = fmaf(xv.w, e[j].w, t);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) e[j] = en[j];
+    }
+    head_halve<32>(a, lane, 16);
+    head_halve<16>(a, lane, 8);
+    head_halve<8>(a, lane, 4);
+    head_halve<4>(a, lane, 2);
+    head_halve<2>(a, lane, 1);
+    const int r = lane >> 2, j = lane & 3;  // a[0] is sum `lane`
+    if (r < nr && v0 + j < V) logits[static_cast<size_t>(r0 + r) * V + v0 + j] = a[0];
+  }
+}
+
 // greedy.rs argmax_finite, one CTA per row: the first maximal logit; a
 // non-finite logit sets the context's error bit (the step then fails).
 constexpr int kArgmaxThreads = 256;
@@ -469,6 +552,7 @@ struct slm_model {
   // projections; 0 when their shared memory does not fit this model
   int32_t exact_rows = 0;
   bool exact_fits = false;
+  bool head_kernel_ok = false;  // rows up to 64 on head_kernel (hidden <= 4096)
   cublasHandle_t blas = nullptr;
   void* weights = nullptr;  // one device allocation for every tensor
   const float* emb = nullptr;         // [V, H] fp32: lookup table and tied vocabulary projection
@@ -723,10 +807,17 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
                                                        m->xf, last_rows);
     ++launches;
     float* lg = logits ? logits : m->logits;
-    const float one = 1.f, zero = 0.f;
-    bs = cublasSgemm(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, m->V, out_rows, H, &one, m->emb, H, m->xf, H, &zero,
-                     lg, m->V);
-    if (bs != CUBLAS_STATUS_SUCCESS) return blas_fail(m->ctx, "slm_model vocabulary projection", bs);
+    if (out_rows > 1 && out_rows <= kHeadMaxRows && m->head_kernel_ok) {
+      const dim3 grid((m->V + kHeadEntries - 1) / kHeadEntries, (out_rows + kHeadRows - 1) / kHeadRows);
+      launched(launch_chained(head_kernel, grid, dim3(kHeadThreads), static_cast<size_t>(kHeadRows) * H * 4, s,
+                              static_cast<const float*>(m->xf), out_rows, H, m->emb, m->V, lg));
+      ++launches;
+    } else {
+      const float one = 1.f, zero = 0.f;
+      bs = cublasSgemm(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, m->V, out_rows, H, &one, m->emb, H, m->xf, H, &zero,
+                       lg, m->V);
+      if (bs != CUBLAS_STATUS_SUCCESS) return blas_fail(m->ctx, "slm_model vocabulary projection", bs);
+    }
     if (next) {
       launched(launch_chained(argmax_kernel, dim3(out_rows), dim3(kArgmaxThreads), 0, s,
                               static_cast<const float*>(lg), m->V, next, err));
@@ -879,6 +970,14 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
   const uint8_t* base = static_cast<const uint8_t*>(m->weights);
   m->emb = reinterpret_cast<const float*>(base + o_emb);
   m->final_norm = reinterpret_cast<const float*>(base + o_final);
+  if (H <= kHeadMaxWidth) {
+    e = cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadRows * H * 4);
+    if (e != cudaSuccess) {
+      slm_model_destroy(m);
+      return cuda_fail(ctx, "slm_model_create", e);
+    }
+    m->head_kernel_ok = true;
+  }
   int sms = 0;
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) {
