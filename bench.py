@@ -640,6 +640,11 @@ def run_serve(args):
     # staging for the per-step gather / scatter indices (pinned, copied async)
     h_idx = torch.zeros(B + SERVE_PREFILL_TOKENS + B, dtype=torch.int64).pin_memory()
     d_idx = torch.zeros_like(h_idx, device=dev)
+    sel_h = torch.zeros(B, dtype=torch.int64).pin_memory()  # prefill rows whose first token is due
+    sel_d = torch.zeros_like(sel_h, device=dev)
+    row_arr = np.full(len(prompts), -1, np.int64)  # request id -> history row
+    for rid, k in row_of.items():
+        row_arr[rid] = k
     nxt_dec = torch.zeros(B, dtype=torch.int32, device=dev)
     nxt_pre = torch.zeros(B, dtype=torch.int32, device=dev)
 
@@ -647,28 +652,31 @@ def run_serve(args):
         # the decode batch is submitted and the prefill batch queued behind it:
         # one wait per step
         nd, npf = sched.plan()
-        dec_req, pre_req = sched.plan_requests()
-        counts = list(sched._pcnt[:npf])
-        rows = sum(counts)
+        dreq, dpos, preq, ppos = sched.plan_request_arrays()
+        counts = np.ctypeslib.as_array(sched._pcnt)[:npf]
+        rows = int(counts.sum())
         # indices: decode inputs [0, nd), prefill inputs [nd, nd + rows),
         # first-token writes after them
         hv = h_idx.numpy()
-        for i, (rid, pos) in enumerate(dec_req):
-            hv[i] = row_of[rid] * W + pos
+        hv[:nd] = row_arr[dreq] * W + dpos
         at = nd
         firsts = []
-        for i, ((rid, pos), c) in enumerate(zip(pre_req, counts)):
-            base = row_of[rid] * W + pos
+        for i in range(npf):
+            rid, pos, c = int(preq[i]), int(ppos[i]), int(counts[i])
+            base = int(row_arr[rid]) * W + pos
             hv[at:at + c] = np.arange(base, base + c)
             at += c
             if pos + c == prompts[rid] and rid not in first_done:
                 firsts.append((i, base + c))
                 first_done.add(rid)
-        for j, (_, dst) in enumerate(firsts):
+        for j, (i, dst) in enumerate(firsts):
             hv[at + j] = dst
+            sel_h.numpy()[j] = i
         n_idx = at + len(firsts)
         if n_idx:
             d_idx[:n_idx].copy_(h_idx[:n_idx], non_blocking=True)
+        if firsts:
+            sel_d[:len(firsts)].copy_(sel_h[:len(firsts)], non_blocking=True)
         dst = pst = None
         dec = None
         if nd:
@@ -681,8 +689,7 @@ def run_serve(args):
             model.prefill(b, hist.index_select(0, d_idx[nd:nd + rows]).to(torch.int32), None,
                           nxt_pre[:npf])
             if firsts:
-                sel = torch.tensor([i for i, _ in firsts], dtype=torch.int64, device=dev)
-                hist.index_copy_(0, d_idx[nd + rows:n_idx], nxt_pre.index_select(0, sel))
+                hist.index_copy_(0, d_idx[nd + rows:n_idx], nxt_pre.index_select(0, sel_d[:len(firsts)]))
             pst = b.end(raise_on_error=False)
         if dec is not None:
             dst = dec.wait(raise_on_error=False)

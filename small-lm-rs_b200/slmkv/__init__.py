@@ -868,6 +868,17 @@ class Scheduler:
         return (list(zip(self._dreq[:nd], self._dpos[:nd])),
                 list(zip(self._preq[:np_], self._ppos[:np_])))
 
+    def plan_request_arrays(self):
+        """plan_requests as numpy views (valid until the next plan): decode
+        request ids and positions, prefill request ids and first positions."""
+        import numpy as np
+
+        self.pool.check(lib().slm_sched_plan_requests(self._h, self._dreq, self._dpos,
+                                                      self._preq, self._ppos))
+        nd, np_ = self._nd.value, self._np.value
+        return (np.ctypeslib.as_array(self._dreq)[:nd], np.ctypeslib.as_array(self._dpos)[:nd],
+                np.ctypeslib.as_array(self._preq)[:np_], np.ctypeslib.as_array(self._ppos)[:np_])
+
     def commit(self, decode_status=None, prefill_status=None) -> list[tuple[int, int, int]]:
         """Commits the last plan; returns the finished requests as
         (request_id, status, output tokens)."""

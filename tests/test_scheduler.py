@@ -140,3 +140,6 @@ def test_plan_requests_report_ids_and_positions():
     s.plan()
     # both prompts are cached: each decode step feeds the token at its length
     assert s.plan_requests() == ([(10, 20), (11, 5)], [])
+    dreq, dpos, preq, ppos = s.plan_request_arrays()  # the same as numpy views
+    assert dreq.tolist() == [10, 11] and dpos.tolist() == [20, 5]
+    assert preq.tolist() == [] and ppos.tolist() == []
