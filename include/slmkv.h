@@ -40,7 +40,8 @@ enum {
   SLM_ERR_INVALID_CONFIGURATION = -1, /* EngineError::InvalidConfiguration */
   SLM_ERR_INVALID_INPUT = -2,         /* EngineError::InvalidInput (shape, index, state) */
   SLM_ERR_CAPACITY = -3,              /* InvalidInput: sequence would exceed its capacity */
-  SLM_ERR_NON_FINITE = -4,            /* InvalidInput: appended K/V not finite */
+  SLM_ERR_NON_FINITE = -4,            /* InvalidInput: appended K/V, or an attention
+                                         score (softmax.rs:17-22), not finite */
   SLM_ERR_POOL_EXHAUSTED = -5,        /* no free physical block (paged pool only) */
   SLM_ERR_CUDA = -6,                  /* a CUDA runtime call failed */
   SLM_ERR_DEVICE_TIMEOUT = -7,        /* a kernel's bounded wait expired */
@@ -138,7 +139,10 @@ slm_status slm_append_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, const f
 slm_status slm_gather_layer(slm_ctx* ctx, int32_t seq_id, int32_t layer, float* d_keys,
                             float* d_values, slm_stream stream);
 /* GroupedQueryAttention::attend_cached_query (attention.rs:677-759) for one
- * sequence: query [q_heads, head_dim] already rotated, out [q_heads*head_dim]. */
+ * sequence: query [q_heads, head_dim] already rotated, out [q_heads*head_dim].
+ * Waits for `stream`: a score that is not finite (a non-finite query, or an
+ * overflowing dot product) fails the call with SLM_ERR_NON_FINITE, as
+ * softmax_rows fails the reference's call (attention.rs:731, softmax.rs:17-22). */
 slm_status slm_attend_cached_query(slm_ctx* ctx, int32_t seq_id, int32_t layer,
                                    const float* d_query, float* d_out, slm_stream stream);
 
@@ -173,8 +177,11 @@ slm_status slm_batch_prefill_attention(slm_batch* batch, int32_t layer, const fl
                                        int32_t rotate_query, float* d_out);
 /* Closes the step: waits for its stream, and reports per sequence (h_status
  * may be NULL) 0 or SLM_ERR_NON_FINITE. A sequence whose appends were not
- * finite, or whose layers did not all advance by its count, is rolled back to
- * its length at slm_batch_begin (model.rs:390-396). Returns the first failure. */
+ * finite, whose attention met a score that is not finite (softmax.rs:17-22,
+ * in decode as attention.rs:731,814-815, in prefill as causal_probabilities),
+ * or whose layers did not all advance by its count, is rolled back to its
+ * length at slm_batch_begin (model.rs:390-396). Returns the first failure.
+ * The pool never holds a non-finite value: a failed append stores zeros. */
 slm_status slm_batch_end(slm_batch* batch, int32_t* h_status);
 /* Abandons the step: every sequence goes back to its begin length. */
 slm_status slm_batch_rollback(slm_batch* batch);
@@ -269,10 +276,9 @@ slm_status slm_sched_counts(const slm_sched* sched, int32_t* waiting, int32_t* r
 
 /* ---- allocation-free decode attention ------------------------------------
  * No counterpart in the reference. For callers that cannot allocate device
- * memory: code that runs while a CUDA graph is captured on its stream,
- * engines that hand out all device memory from one arena of their own, and
- * plugins loaded into hosts that forbid new device allocations after
- * start-up. It computes GroupedQueryAttention::attend_cached_query
+ * memory: engines that hand out all device memory from one arena of their
+ * own, and plugins loaded into hosts that forbid new device allocations
+ * after start-up. It computes GroupedQueryAttention::attend_cached_query
  * (attention.rs:677-759) for n sequences of a paged KV cache the caller owns,
  * with the library's decode kernel, and allocates nothing: the plan, split-K
  * partials, merge counters and error word live in one 2 MiB file-scope device
@@ -284,12 +290,14 @@ slm_status slm_sched_counts(const slm_sched* sched, int32_t* waiting, int32_t* r
  *   d_out                     [n][q_heads][64]
  * Limits (SLM_ERR_INVALID_INPUT beyond them): n * kv_heads <= 4096 and
  * sum(ceil(len/16)) * kv_heads <= 131072 blocks; q_heads / kv_heads in
- * {1, 2, 4, 8}. Runs on the calling thread's current device and returns after
- * the result is in d_out (it synchronizes `stream`). The first call on a
- * device looks up the array's device address (cudaGetSymbolAddress); make
- * that first call before any stream capture. All calls share the array and
- * clear what must start at zero; calls that overlap on the GPU (other
- * streams or threads) race on it. Errors: slm_last_error(NULL). */
+ * {1, 2, 4, 8}; num_blocks * kv_heads <= INT32_MAX. Runs on the calling
+ * thread's current device and returns after the result is in d_out (it
+ * synchronizes `stream`). The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call before any
+ * stream capture. All calls share the array and clear what must start at
+ * zero; calls that overlap on the GPU (other streams or threads) race on it.
+ * A score that is not finite fails the call with SLM_ERR_NON_FINITE
+ * (softmax.rs:17-22). Errors: slm_last_error(NULL). */
 slm_status slm_decode_attention_noalloc(const float* d_key_pool, const float* d_value_pool,
                                         int32_t num_blocks, int32_t num_query_heads,
                                         int32_t num_key_value_heads, const int32_t* h_block_table,

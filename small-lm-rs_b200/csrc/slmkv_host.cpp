@@ -1216,6 +1216,13 @@ slm_status slm_attend_cached_query(slm_ctx* ctx, int32_t seq_id, int32_t layer,
   ctx->prev_decode_layer = -1;
   CU(ctx, launch_decode(p, s));
   ++ctx->launches;
+  // softmax_rows (attention.rs:731) fails on a non-finite score: the call
+  // waits for the kernel and reports it as the reference's InvalidInput.
+  int32_t status = 0;
+  rc = finish_single(ctx, s, dev.status, &status);
+  if (rc) return rc;
+  if (status & kStatusNonFiniteScore)
+    return input_error(ctx, SLM_ERR_NON_FINITE, "softmax", "all input values must be finite");
   return SLM_OK;
 }
 
@@ -1429,6 +1436,7 @@ slm_status slm_batch_prefill_attention(slm_batch* b, int32_t layer, const float*
   p.rotate = rotate_query != 0;
   p.out = d_out;
   p.max_count = b->max_count;
+  p.status = b->dev.status;
   p.tmap_k = ctx->tmap_k;
   p.tmap_v = ctx->tmap_v;
   ctx->prev_decode_layer = -1;
@@ -1514,15 +1522,19 @@ void resolve_oldest(slm_ctx* ctx) {
     dev_msg = buf;
   }
   b->codes.assign(n, SLM_OK);
+  int32_t first_bits = 0;  // status bits of the first sequence that failed
   for (size_t i = 0; i < n; ++i) {
     const int32_t st = (dev == SLM_OK) ? rb[2 + i] : 0;
     int32_t code = SLM_OK;
     if (dev != SLM_OK) code = dev;
     else if (b->poison_base[i] >= 0) code = b->poison_code[i];
-    else if (st & kStatusNonFinite) code = SLM_ERR_NON_FINITE;
+    else if (st & (kStatusNonFinite | kStatusNonFiniteScore)) code = SLM_ERR_NON_FINITE;
     else if (!b->complete[i]) code = SLM_ERR_INVALID_INPUT;
     b->codes[i] = code;
-    if (code != SLM_OK && b->first == SLM_OK) b->first = code;
+    if (code != SLM_OK && b->first == SLM_OK) {
+      b->first = code;
+      first_bits = st;
+    }
   }
   for (size_t i = 0; i < n; ++i) {
     const int32_t id = b->seq_ids[i];
@@ -1533,7 +1545,10 @@ void resolve_oldest(slm_ctx* ctx) {
       roll_back_seq(ctx, b, id, target, b->codes[i]);
     }
   }
-  if (b->first == SLM_ERR_NON_FINITE)
+  if (b->first == SLM_ERR_NON_FINITE && !(first_bits & kStatusNonFinite) &&
+      (first_bits & kStatusNonFiniteScore))  // softmax.rs:17-22 through attention.rs:731
+    b->msg = "invalid input for softmax: all input values must be finite";
+  else if (b->first == SLM_ERR_NON_FINITE)
     b->msg = "invalid input for KV cache: all appended key/value values must be finite";
   else if (dev != SLM_OK)
     b->msg = dev_msg;

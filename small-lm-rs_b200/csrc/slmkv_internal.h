@@ -68,7 +68,9 @@ struct CopyJob {
 };
 
 // Device status words (per batch sequence, and one per context).
-enum : int32_t { kStatusNonFinite = 1 };
+// kStatusNonFinite: appended K/V not finite (kv_cache.rs:192-197);
+// kStatusNonFiniteScore: an attention score not finite (softmax.rs:17-22).
+enum : int32_t { kStatusNonFinite = 1, kStatusNonFiniteScore = 2 };
 // Device error word bits: a bounded wait expired; a block table held an id
 // outside the pool; a kernel found its shared-memory layout misaligned.
 enum : int32_t { kErrTimeout = 1, kErrBadBlock = 2, kErrLayout = 4, kErrBadToken = 8, kErrLogits = 16 };
@@ -154,6 +156,7 @@ struct PrefillLaunch {
   int32_t rotate;
   float* out;
   int32_t max_count;  // largest per-sequence token count
+  int32_t* status;    // [n_seq]: kStatusNonFiniteScore when a score is not finite
   CUtensorMap tmap_k, tmap_v;  // bf16 pools: the decode kernel's pool maps
 };
 cudaError_t launch_prefill(const PrefillLaunch& p, cudaStream_t s);

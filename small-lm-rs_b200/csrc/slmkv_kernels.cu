@@ -126,8 +126,21 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 __device__ __forceinline__ bool finite2(float2 v) { return isfinite(v.x) && isfinite(v.y); }
+// softmax.rs:17-22: a score row with a non-finite entry is rejected. True when
+// one of this lane's G scores is not finite and its token is a real one.
+template <int G>
+__device__ __forceinline__ bool scores_bad(const float (&sc)[G], bool valid) {
+  bool bad = false;
+#pragma unroll
+  for (int g = 0; g < G; ++g) bad |= !isfinite(sc[g]);
+  return valid && bad;
+}
 __device__ __forceinline__ bool finite4(float4 v) {
   return isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+}
+// Both halves of a bf16 pair finite (a finite f32 near FLT_MAX rounds to inf).
+__device__ __forceinline__ bool finite_bf16x2(uint32_t w) {
+  return (w & 0x7f80u) != 0x7f80u && (w & 0x7f800000u) != 0x7f800000u;
 }
 
 // Q rows live in shared memory as 16 four-float units per head; unit u is
@@ -352,7 +365,7 @@ __device__ __forceinline__ void load_q_frags(const float* qs, int lane, uint32_t
 // rows must be finite: the caller zeroes them).
 __device__ __forceinline__ void block_mma_bf16(uint32_t kaddr, uint32_t vaddr, int lane, int nvalid,
                                                const uint32_t (&qa)[4][4], float& m_row,
-                                               float& l_row, float (&o)[8][4]) {
+                                               float& l_row, float (&o)[8][4], bool& bad) {
   const int r = lane & 7, mtx = lane >> 3, t = lane & 3;
   float c[2][4];
 #pragma unroll
@@ -374,7 +387,9 @@ __device__ __forceinline__ void block_mma_bf16(uint32_t kaddr, uint32_t vaddr, i
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int tok = 8 * j + 2 * t + e;
-      sc[j][e] = (tok < nvalid) ? c[j][e] + c[j][2 + e] : -INFINITY;
+      const float v = c[j][e] + c[j][2 + e];
+      bad |= (tok < nvalid) && !isfinite(v);  // softmax.rs:17-22
+      sc[j][e] = (tok < nvalid) ? v : -INFINITY;
       mx = fmaxf(mx, sc[j][e]);
     }
   mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
@@ -707,6 +722,10 @@ __global__ void __launch_bounds__(W * 32, 1)
   float2 cs = make_float2(1.f, 0.f), kn = cs, vn = cs;
   int seg_end = min(g1, cur.blk_begin + cur.nblk);
   bool seg_start = true;
+  // A score of this segment that is not finite (a non-finite or overflowing
+  // query, softmax.rs:17-22): the pair's sequence is flagged at the segment's
+  // end and its step fails as attention.rs:731,814-815 does.
+  bool bad = false;
 
   // Cross-CTA pairs finished after the warp's last block (at most two).
   int npend = 0;
@@ -769,12 +788,16 @@ __global__ void __launch_bounds__(W * 32, 1)
       // The append: rotate the new key at position L-1, store K/V (rounded
       // to the pool's type) into the staged block and into the pool.
       const int slot = (cur.L - 1) - tok0;
-      const bool fin = finite2(kn) && finite2(vn);
-      const float2 kx = rope_pair(kn, cs);
+      bool fin = finite2(kn) && finite2(vn);
+      float2 kx = rope_pair(kn, cs);
       const size_t dst =
           layer_elems + (static_cast<size_t>(stage_chunk[stage]) * kBlockTokens + slot) * D;
+      // Non-finite K/V are stored as zeros: the pool never holds a non-finite
+      // value (the step fails and the slot stays past the length).
       if constexpr (BF16) {
-        const uint32_t kq = pack_bf16x2(kx.x, kx.y), vq = pack_bf16x2(vn.x, vn.y);
+        uint32_t kq = pack_bf16x2(kx.x, kx.y), vq = pack_bf16x2(vn.x, vn.y);
+        fin = fin && finite_bf16x2(kq) && finite_bf16x2(vq);
+        if (!fin) kq = vq = 0u;
         // lane's word: unit lane/4 of the swizzled row `slot`
         const uint32_t off = sw128(0u, slot, lane >> 2) + ((lane & 3) << 2);
         *reinterpret_cast<uint32_t*>(kb + off) = kq;
@@ -782,10 +805,12 @@ __global__ void __launch_bounds__(W * 32, 1)
         reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.k) + dst)[lane] = kq;
         reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.g.v) + dst)[lane] = vq;
       } else {
+        const float2 vx = fin ? vn : make_float2(0.f, 0.f);
+        if (!fin) kx = make_float2(0.f, 0.f);
         reinterpret_cast<float2*>(kb)[slot * (D / 2) + lane] = kx;
-        reinterpret_cast<float2*>(vb)[slot * (D / 2) + lane] = vn;
+        reinterpret_cast<float2*>(vb)[slot * (D / 2) + lane] = vx;
         reinterpret_cast<float2*>(static_cast<float*>(p.g.k) + dst)[lane] = kx;
-        reinterpret_cast<float2*>(static_cast<float*>(p.g.v) + dst)[lane] = vn;
+        reinterpret_cast<float2*>(static_cast<float*>(p.g.v) + dst)[lane] = vx;
       }
       if (!__all_sync(kFull, fin) && lane == 0) atomicOr(&p.status[cur.seq], kStatusNonFinite);
       __syncwarp();
@@ -799,11 +824,12 @@ __global__ void __launch_bounds__(W * 32, 1)
               make_uint4(0u, 0u, 0u, 0u);
         __syncwarp();
       }
-      block_mma_bf16(smem_u32(kb), smem_u32(vb), lane, nvalid, qa, m_row, l_row, o);
+      block_mma_bf16(smem_u32(kb), smem_u32(vb), lane, nvalid, qa, m_row, l_row, o, bad);
       __syncwarp();
     } else {
       float sc[G];
       block_scores_f32<G>(reinterpret_cast<const float*>(kb), qs, lane, sc);
+      bad |= scores_bad<G>(sc, (lane & 15) < nvalid);
       block_softmax_pv<G, false>(vb, pbuf, lane, nvalid, sc, m, l, acc);
     }
     if (pg < g1) {
@@ -816,6 +842,10 @@ __global__ void __launch_bounds__(W * 32, 1)
 
     if (g != seg_end - 1) continue;
     // ---- end of this warp's segment of pair `pc` ---------------------------------
+    if (__any_sync(kFull, bad)) {
+      if (lane == 0 && p.status) atomicOr(&p.status[cur.seq], kStatusNonFiniteScore);
+      bad = false;
+    }
     if constexpr (BF16) {
       // Back to one float2 per lane and head (dims 2*lane, 2*lane+1): the
       // layout the merges below use. qs is free: Q lives in qa.
@@ -1071,16 +1101,24 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendLaunch p) {
     }
     const size_t dst = static_cast<size_t>(p.layer) * p.g.layer_elems +
                        ((static_cast<size_t>(blk) * Hkv + h) * kBlockTokens + pos % kBlockTokens) * D;
+    // The pool never holds a non-finite value: a failed append stores zeros
+    // (the step is rolled back, the slot stays past the length), so that stale
+    // slots a later tile stages are finite and P = 0 times them is 0.
     if constexpr (BF16) {
-      reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.g.k) + dst)[l16] =
-          make_uint2(pack_bf16x2(k.x, k.y), pack_bf16x2(k.z, k.w));
-      reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.g.v) + dst)[l16] =
-          make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+      uint2 kq = make_uint2(pack_bf16x2(k.x, k.y), pack_bf16x2(k.z, k.w));
+      uint2 vq = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+      const bool fq = fin && finite_bf16x2(kq.x) && finite_bf16x2(kq.y) &&
+                      finite_bf16x2(vq.x) && finite_bf16x2(vq.y);
+      if (!fq) kq = vq = make_uint2(0u, 0u);
+      reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.g.k) + dst)[l16] = kq;
+      reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.g.v) + dst)[l16] = vq;
+      if (!fq) atomicOr(&p.status[si], kStatusNonFinite);
     } else {
-      reinterpret_cast<float4*>(static_cast<float*>(p.g.k) + dst)[l16] = k;
-      reinterpret_cast<float4*>(static_cast<float*>(p.g.v) + dst)[l16] = v;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      reinterpret_cast<float4*>(static_cast<float*>(p.g.k) + dst)[l16] = fin ? k : z;
+      reinterpret_cast<float4*>(static_cast<float*>(p.g.v) + dst)[l16] = fin ? v : z;
+      if (!fin) atomicOr(&p.status[si], kStatusNonFinite);
     }
-    if (!fin) atomicOr(&p.status[si], kStatusNonFinite);
   }
 }
 
@@ -1156,6 +1194,7 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillLaunch p) {
       acc[r][g] = make_float2(0.f, 0.f);
     }
 
+  bool bad = false;  // a real score of this tile is not finite (softmax.rs:17-22)
   const int last_pos = se.base + q0 + nq - 1;
   const int nblk = last_pos / kBlockTokens + 1;
   const size_t layer_off = static_cast<size_t>(p.layer) * p.g.layer_elems;
@@ -1189,9 +1228,12 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillLaunch p) {
       if (nvalid <= 0) continue;
       float sc[G];
       block_scores_f32<G>(kbuf, qs + jq * G * D, lane, sc);
+      bad |= scores_bad<G>(sc, (lane & 15) < nvalid);
       block_softmax_pv<G, false>(vbuf, pbufs[warp], lane, nvalid, sc, m[r], l[r], acc[r]);
     }
   }
+  if (__any_sync(kFull, bad) && lane == 0 && p.status)
+    atomicOr(&p.status[si], kStatusNonFiniteScore);
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int jq = warp + 4 * r;

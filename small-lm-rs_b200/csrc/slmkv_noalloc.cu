@@ -1,23 +1,26 @@
 // Allocation-free decode attention: slm_decode_attention_noalloc.
 //
-// Some callers cannot call cudaMalloc at all: code running while a CUDA
-// graph is being captured on its stream, engines whose device memory is one
-// arena they own and hand out themselves, and plugins loaded into a host
-// that forbids new device allocations after start-up. For them this entry
-// point runs the library's decode attention kernel (the same split-K kernel
-// as slm_attend_cached_query) over a paged KV cache the caller owns, and
-// keeps everything the kernel needs besides the caller's inputs and outputs
-// (the step plan, split-K partials and merge counters, an error word) in one
-// fixed file-scope device array below. Nothing is allocated per call.
+// Some callers cannot call cudaMalloc at all: engines whose device memory is
+// one arena they own and hand out themselves, and plugins loaded into a host
+// that forbids new device allocations after start-up (an allocation there
+// can fail, or break the host's own accounting of device memory). For them
+// this entry point runs the library's decode attention kernel (the same
+// split-K kernel as slm_attend_cached_query) over a paged KV cache the caller
+// owns, and keeps everything the kernel needs besides the caller's inputs and
+// outputs (the step plan, split-K partials and merge counters, per-sequence
+// status words, an error word) in one fixed file-scope device array below.
+// Nothing is allocated per call.
 //
 // The array is kNoAllocScratchBytes (2 MiB). Every GPU that loads this
 // library holds it until the process exits. It is shared by every call on
 // that GPU and keeps the last call's contents; each call clears the parts
-// that must start at zero (merge counters, error word). Calls whose work
-// overlaps on the GPU (other streams, other host threads) race on it.
+// that must start at zero (merge counters, status and error words). Calls
+// whose work overlaps on the GPU (other streams, other host threads) race on
+// it. A call waits for its stream before it returns.
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -53,7 +56,8 @@ constexpr size_t kOffPartAcc = align256(kOffWarpStart + sizeof(int4) * 2 * kMaxW
 constexpr size_t kOffPartMl =
     align256(kOffPartAcc + sizeof(float) * kMaxSlots * kMaxGroup * kHeadDim);
 constexpr size_t kOffCounters = align256(kOffPartMl + sizeof(float2) * kMaxSlots * kMaxGroup);
-constexpr size_t kOffError = align256(kOffCounters + sizeof(int32_t) * kMaxPairs);
+constexpr size_t kOffStatus = align256(kOffCounters + sizeof(int32_t) * kMaxPairs);
+constexpr size_t kOffError = align256(kOffStatus + sizeof(int32_t) * kMaxPairs);
 constexpr size_t kPlanBytes = kOffPartAcc;  // pairs + chunks + warp starts: uploaded per call
 constexpr size_t kNoAllocScratchBytes = 2u << 20;
 static_assert(kOffError + 256 <= kNoAllocScratchBytes, "scratch layout exceeds 2 MiB");
@@ -72,6 +76,7 @@ int g_sms[kMaxDevices] = {};
 alignas(16) unsigned char g_plan_host[kPlanBytes];
 int32_t g_bounds[kMaxWarps + 1];
 int32_t g_ctx_len[kMaxPairs];
+int32_t g_status_host[kMaxPairs];  // sequences <= pairs
 int32_t g_error_host;
 
 slm_status fail(slm_status code, const char* fmt, ...) {
@@ -132,6 +137,11 @@ extern "C" slm_status slm_decode_attention_noalloc(
   if (G != 1 && G != 2 && G != 4 && G != 8)
     return fail(SLM_ERR_INVALID_INPUT,
                 "invalid input for %s: query heads per KV head must be 1, 2, 4 or 8", who);
+  // The plan names a chunk as block * kv_heads + head in an int32.
+  if (static_cast<int64_t>(num_blocks) * num_key_value_heads > INT32_MAX)
+    return fail(SLM_ERR_INVALID_INPUT,
+                "invalid input for %s: %d blocks x %d KV heads exceed the int32 chunk index", who,
+                num_blocks, num_key_value_heads);
   if (static_cast<int64_t>(n) * num_key_value_heads > kMaxPairs)
     return fail(SLM_ERR_INVALID_INPUT,
                 "invalid input for %s: %lld (sequence, KV head) pairs exceed the %d its fixed "
@@ -189,9 +199,11 @@ extern "C" slm_status slm_decode_attention_noalloc(
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(dev + kOffWarpStart, wstart, sizeof(int4) * 2 * sz.n_warps,
                         cudaMemcpyHostToDevice, s);
-  // What must start at zero: the merge counters and the error word.
+  // What must start at zero: the merge counters, the status words and the
+  // error word.
   if (e == cudaSuccess)
     e = cudaMemsetAsync(dev + kOffCounters, 0, sizeof(int32_t) * sz.n_pairs, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dev + kOffStatus, 0, sizeof(int32_t) * n, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(dev + kOffError, 0, sizeof(int32_t), s);
   if (e != cudaSuccess)
     return fail(SLM_ERR_CUDA, "CUDA error in %s (plan upload): %s", who, cudaGetErrorString(e));
@@ -224,11 +236,14 @@ extern "C" slm_status slm_decode_attention_noalloc(
   p.part_acc = reinterpret_cast<float*>(dev + kOffPartAcc);
   p.part_ml = reinterpret_cast<float2*>(dev + kOffPartMl);
   p.counters = reinterpret_cast<int32_t*>(dev + kOffCounters);
-  p.status = nullptr;  // written only when appending
+  p.status = reinterpret_cast<int32_t*>(dev + kOffStatus);
   p.fused = 0;
   e = launch_decode(p, s);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(&g_error_host, dev + kOffError, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(g_status_host, dev + kOffStatus, sizeof(int32_t) * n,
+                        cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess)
     return fail(SLM_ERR_CUDA, "CUDA error in %s: %s", who, cudaGetErrorString(e));
@@ -236,5 +251,9 @@ extern "C" slm_status slm_decode_attention_noalloc(
     return fail(SLM_ERR_DEVICE_TIMEOUT, "%s: a device wait timed out", who);
   if (g_error_host)
     return fail(SLM_ERR_INVALID_INPUT, "invalid input for %s: out-of-pool block id", who);
+  for (int32_t i = 0; i < n; ++i)
+    if (g_status_host[i] & kStatusNonFiniteScore)  // softmax.rs:17-22
+      return fail(SLM_ERR_NON_FINITE,
+                  "invalid input for softmax: all input values must be finite (sequence %d)", i);
   return SLM_OK;
 }

@@ -19,6 +19,7 @@
 // Q, K and V tiles are 128-byte-swizzled: K/V blocks arrive by TMA (16 rows
 // per block, block-table lookups), Q is written by the threads in the same
 // layout.
+#include <cfloat>
 #include <cstdint>
 
 #include "slmkv_internal.h"
@@ -175,10 +176,15 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// Three-input max (sm_100): fewer instructions for a row's max.
+// Three-input max and min (sm_100): fewer instructions for a row's max.
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
 // Two f32 lanes in one 64-bit register, for the packed f32x2 arithmetic.
@@ -193,6 +199,11 @@ __device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
 __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {  // two IEEE adds, rounded to nearest
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {  // a * b + c, twice
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
 // MMA operands (Q, P) to bf16, round to nearest even, one instruction per pair.
@@ -466,7 +477,10 @@ __global__ void __launch_bounds__(WsCfg<QT>::kThreads, WsCfg<QT>::kCtasPerSm)
       __syncwarp();
       if (lane == 0) bar_arrive(bar(kBarQFull + w));
     }
+    // fin2: +0 in both halves while every score of the row (masked ones are
+    // finite) has been finite; a NaN from the first non-finite one on.
     float m_used = -INFINITY, l_sum = 0.f;
+    uint64_t fin2 = 0ull;
     bool ok = true;  // warp-uniform
     for (int j = 0; j < ntw; ++j) {
       // ---- S_j out of TMEM; the columns go back to the MMA warp at once ----
@@ -489,13 +503,14 @@ __global__ void __launch_bounds__(WsCfg<QT>::kThreads, WsCfg<QT>::kCtasPerSm)
       if (lane == 0) bar_arrive(bar(kBarSFree + w));
       // ---- softmax of this thread's row ---------------------------------------
       const int kp0 = j * kTileN;
-      // causal (attention.rs:207): key position <= query position. Only tiles
-      // reaching past the tile's first query position need the mask; rows
-      // past the tile's tokens read zeros.
+      // causal (attention.rs:207): key position <= query position; a masked
+      // score is f32::MIN, finite as in the reference, and its ex2 is 0. Only
+      // tiles reaching past the tile's first query position need the mask;
+      // rows past the tile's tokens read zeros.
       if (kp0 + kTileN - 1 > se.base + qw0 || !live) {
 #pragma unroll
         for (int i = 0; i < kTileN; ++i) {
-          if (live && kp0 + i > qpos) s[i] = -INFINITY;
+          if (live && kp0 + i > qpos) s[i] = -FLT_MAX;
           if (!live) s[i] = 0.f;
         }
       }
@@ -525,7 +540,9 @@ __global__ void __launch_bounds__(WsCfg<QT>::kThreads, WsCfg<QT>::kCtasPerSm)
 #pragma unroll
       for (int i = 0; i < kTileN / 2; ++i) {
         float xa, xb;
-        unpack2(add2(pack2(s[2 * i], s[2 * i + 1]), neg_m), xa, xb);
+        const uint64_t s2 = pack2(s[2 * i], s[2 * i + 1]);
+        unpack2(add2(s2, neg_m), xa, xb);
+        fin2 = fma2(s2, 0ull, fin2);  // +0 per finite score, NaN per non-finite one
         const float a = ex2(xa), b = ex2(xb);
         ps2[i & 3] = add2(ps2[i & 3], pack2(a, b));
         pw[i] = bf16x2(a, b);
@@ -567,6 +584,16 @@ __global__ void __launch_bounds__(WsCfg<QT>::kThreads, WsCfg<QT>::kCtasPerSm)
     }
     // ---- epilogue: O / l to the output rows ------------------------------------
     if (ok && ntw > 0) {
+      // softmax.rs:17-22,35-40: a non-finite score or row sum fails the
+      // sequence's step (its batch rolls it back).
+      float f0, f1;
+      unpack2(fin2, f0, f1);
+      const bool bad = live && !(f0 == 0.f && f1 == 0.f && isfinite(l_sum) && l_sum > 0.f);
+      if (__any_sync(0xffffffffu, bad) && lane == 0 && p.status) {
+        uint32_t si;  // the grid's y index is the sequence's batch row
+        asm volatile("mov.u32 %0, %%ctaid.y;" : "=r"(si));
+        atomicOr(&p.status[si], kStatusNonFiniteScore);
+      }
       if (!wait_warp(bar(kBarODone + w), (ntw - 1) & 1)) {
         ok = false;
       } else {
@@ -616,12 +643,15 @@ __global__ void __launch_bounds__(WsCfg<QT>::kThreads, WsCfg<QT>::kCtasPerSm)
       // ================= loader =================
       // K and V tile t -> stage t % 3: its 16-token blocks through the block
       // table, one lane per block (lanes 0-7); each lane loads the next tile's
-      // block id while the current one is copied.
+      // block id while the current one is copied. A tile is always loaded
+      // whole: slots past the sequence's last block take that block again, so
+      // every staged V row is a pool row, which is finite (the pool never
+      // holds a non-finite value), and a masked P = 0 times it is 0.
       const int32_t* bt = p.g.block_table + static_cast<size_t>(cw.se.slot) * p.g.max_blocks_per_seq;
       const int layer_row0 = p.layer * p.g.num_blocks * Hkv;
       auto block_id = [&](int t) {
-        const int b = t * (kTileN / kBlockTokens) + lane;
-        return (lane < kTileN / kBlockTokens && b < n_blocks) ? bt[b] : 0;
+        const int b = min(t * (kTileN / kBlockTokens) + lane, n_blocks - 1);
+        return (lane < kTileN / kBlockTokens) ? bt[b] : 0;
       };
       int blk_next = block_id(0);
       int k_issued = 0, v_issued = 0;
@@ -631,7 +661,7 @@ __global__ void __launch_bounds__(WsCfg<QT>::kThreads, WsCfg<QT>::kCtasPerSm)
         const int st = t % kWsStages;
         int32_t blk = blk_next;
         blk_next = block_id(t + 1);
-        const int nb = min(kTileN / kBlockTokens, n_blocks - t * (kTileN / kBlockTokens));
+        constexpr int nb = kTileN / kBlockTokens;
         if (static_cast<uint32_t>(blk) >= static_cast<uint32_t>(p.g.num_blocks)) {
           if (lane < nb) atomicOr(p.g.error, kErrBadBlock);
           blk = 0;

@@ -665,8 +665,8 @@ def decode_attention_noalloc(key_pool, value_pool, block_table, lengths, query, 
                              stream=None):
     """slm_decode_attention_noalloc: attend_cached_query (attention.rs:677-759)
     for n sequences of a caller-owned paged f32 cache, without any device
-    allocation by the library (for callers that cannot allocate: graph
-    capture, arena-managed memory, hosts that forbid new allocations).
+    allocation by the library (for engines that own all device memory as one
+    arena, and plugins in hosts that forbid new device allocations).
 
     key_pool/value_pool: CUDA [num_blocks, kv_heads, 16, 64]; block_table:
     host int32 [n, max_blocks]; lengths: host int32 [n]; query: CUDA
@@ -674,12 +674,32 @@ def decode_attention_noalloc(key_pool, value_pool, block_table, lengths, query, 
     import numpy as np
     import torch
 
-    nb, hkv = int(key_pool.shape[0]), int(key_pool.shape[1])
-    n, hq = int(query.shape[0]), int(query.shape[1])
+    def bad(msg):
+        return InvalidInput(ERR_INVALID_INPUT,
+                            f"invalid input for slm_decode_attention_noalloc: {msg}")
+
     table = np.ascontiguousarray(block_table, dtype=np.int32)
     lens = np.ascontiguousarray(lengths, dtype=np.int32)
+    if key_pool.dim() != 4 or tuple(key_pool.shape[2:]) != (BLOCK_TOKENS, 64):
+        raise bad("key pool must be [num_blocks, kv_heads, 16, 64]")
+    if tuple(value_pool.shape) != tuple(key_pool.shape):
+        raise bad("value pool must have the key pool's shape")
+    if query.dim() != 3 or int(query.shape[2]) != 64:
+        raise bad("query must be [n, q_heads, 64]")
+    nb, hkv = int(key_pool.shape[0]), int(key_pool.shape[1])
+    n, hq = int(query.shape[0]), int(query.shape[1])
+    if table.ndim != 2 or table.shape[0] != n or lens.shape != (n,):
+        raise bad(f"block table must be [{n}, max_blocks] and lengths [{n}]")
     if out is None:
         out = torch.empty_like(query)
+    if tuple(out.shape) != tuple(query.shape):
+        raise bad("out must have the query's shape")
+    dev = torch.cuda.current_device()
+    for name, t in (("key pool", key_pool), ("value pool", value_pool), ("query", query),
+                    ("out", out)):
+        if not t.is_cuda or t.device.index != dev or t.dtype != torch.float32 \
+                or not t.is_contiguous():
+            raise bad(f"{name} must be a contiguous f32 tensor on the current device")
     rc = lib().slm_decode_attention_noalloc(
         _ptr(key_pool), _ptr(value_pool), nb, hq, hkv,
         table.ctypes.data_as(_pi32), int(table.shape[1]), lens.ctypes.data_as(_pi32), n,

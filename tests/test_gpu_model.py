@@ -3,14 +3,18 @@ oracle's model (model.rs:297-397): a seeded random model in the reference
 layout, prompts of several lengths prefilled in one batch, then greedy decode
 steps for all of them in one batch per step.
 
-Logits are held to the reference's own GPU-versus-CPU logit parity
-thresholds (parity/runner.rs:33-43: max abs 0.1, mean abs 0.01, RMS 0.02,
-cosine >= 0.9999, top-1 agreement 1.0, the final next token exact), and
-every greedy token must be the oracle's. A tighter bound is not a property of
-this arithmetic: every projection rounds its input to bf16 (linear.rs), so a
-1-ulp fp32 difference upstream (another accumulation order in a GEMM, the
-RMSNorm reduction or the split-K attention, whose own outputs stay within
-1e-4) can move a bf16 operand by one bf16 ulp, which moves a logit by ~1e-3.
+Bars: every greedy token must be the oracle's, and the logits must meet
+  - max abs <= 1e-4 with an f32 pool on the exact-order projections (the
+    default up to 1024 rows: each output is the reference's own fma fold over
+    bf16-rounded operands, linear.rs:98-103);
+  - max abs <= 2e-2 with a bf16 pool (the oracle's bf16 cache stores the same
+    values rounded; the reference's prefill attends its unrounded K/V);
+and, on top, the reference's own GPU-versus-CPU logit thresholds
+(parity/runner.rs:33-43: max abs 0.1, mean abs 0.01, RMS 0.02, cosine >=
+0.9999, top-1 agreement 1.0). The tensor-core projection path (another
+accumulation order: a 1-ulp fp32 difference can flip a bf16 operand rounding,
+which moves a logit by ~1e-3) is an option outside the fp32 parity claim and
+is held to the reference's thresholds only.
 Also: a token outside the vocabulary fails the step and rolls it back."""
 
 import numpy as np
@@ -100,25 +104,48 @@ def check_thresholds(m):
     assert m["cosine"] >= 0.9999 and m["top1"] == 1.0, m
 
 
+F32_BAR, BF16_BAR = 1e-4, 2e-2  # logits max abs: fp32 KV, bf16 KV
+
+
+def check_f32(m):
+    check_thresholds(m)
+    assert m["max_abs"] <= F32_BAR, m
+
+
+def check_bf16(m):
+    check_thresholds(m)
+    assert m["max_abs"] <= BF16_BAR, m
+
+
 PROMPTS = [np.array(p, np.uint32) for p in ([5, 900, 17, 3, 3], list(range(100, 117)),
                                              [int(x) for x in np.arange(33) * 31 % 1024])]
 
 
 def test_model_prefill_and_decode_match_the_oracle_f32():
     m = _run(slmkv.KV_F32, PROMPTS)
-    check_thresholds(m)
+    check_f32(m)
     print("f32 KV logits vs oracle:", m)
 
 
 def test_model_prefill_and_decode_match_the_oracle_bf16():
     m = _run(slmkv.KV_BF16, PROMPTS)
-    check_thresholds(m)
+    check_bf16(m)
     print("bf16 KV logits vs oracle:", m)
+
+
+def test_batched_prefill_of_1024_rows_stays_exact():
+    # 4 x 256 prompt rows = 1024: the largest step the exact-order kernels take
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, 1024, 256).astype(np.uint32) for _ in range(4)]
+    m = _run(slmkv.KV_F32, prompts, steps=2, ctx=512)
+    check_f32(m)
+    print("1024-row prefill, f32 KV logits vs oracle:", m)
 
 
 def test_long_prefill_on_the_tensor_core_path():
     # 3 x 400 prompt rows > 1024: the prefill's projections run as tensor-core
-    # GEMMs (another accumulation order), the decode steps as the fused kernels
+    # GEMMs (another accumulation order, outside the fp32 bar), the decode
+    # steps as the exact-order kernels
     rng = np.random.default_rng(11)
     prompts = [rng.integers(0, 1024, 400).astype(np.uint32) for _ in range(3)]
     m = _run(slmkv.KV_F32, prompts, steps=2, ctx=512)
@@ -127,7 +154,8 @@ def test_long_prefill_on_the_tensor_core_path():
 
 
 def test_every_step_on_the_tensor_core_path():
-    # exact-order rows 0: prefill and decode projections all as GEMMs
+    # exact-order rows 0: prefill and decode projections all as GEMMs (an
+    # option outside the fp32 bar)
     m = _run(slmkv.KV_F32, PROMPTS, exact_rows=0)
     check_thresholds(m)
     print("GEMM projections, f32 KV logits vs oracle:", m)
@@ -142,7 +170,10 @@ def test_scaled_gqa_shape_bf16(exact_rows):
     prompts = [np.array(p, np.uint32) for p in ([7, 1000, 3], list(range(200, 213)), [5] * 6)]
     m = _run(slmkv.KV_BF16, prompts, steps=3, exact_rows=exact_rows,
              dims=(1024, 32, 8, 64, 5632, 2))
-    check_thresholds(m)
+    if exact_rows is None:
+        check_bf16(m)
+    else:
+        check_thresholds(m)
     print(f"scaled GQA shape, exact rows {exact_rows}, bf16 KV logits vs oracle:", m)
 
 
