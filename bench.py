@@ -12,11 +12,20 @@ every step does the same work. One step reads ~544 MB of K/V, far more than
 the 126 MB L2, so no flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload microbench|gqa-bf16]
+                  [--workload microbench|gqa-bf16|model|prefix|serve|gqa-model]
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own 256
 sequences (weak scaling, no collective on the data path); the timed region is
 bracketed by barriers and the slowest rank's time is reported.
+
+The default run (no --workload) then runs the benchmark's other
+configurations, each in a process of its own per GPU, and attaches their
+result lines under "configs": the 8M model end to end (batch 1, 64-token
+prompt, 448 greedy steps), prefix reuse (64 requests sharing a 384-token
+prefix, 96 greedy steps), continuous batching (4096 Poisson requests over the
+GPUs) and the scaled GQA model (16 sequences of 1-8k tokens per GPU, 256
+greedy steps). Each line has its own value, e2e, and at one GPU its CPU
+baseline and greedy-token parity against the oracle.
 
 `--impl reference` times the reference's CPU path for the same workload: the
 oracle restatement of rust/engine (the Rust engine cannot be built here), all
@@ -74,7 +83,7 @@ PREFIX_DECODE_STEPS = 96
 # SERVE_RATE requests/s (seeded), prompts U[8,256], outputs U[16,256], at
 # most 512 running per GPU, the 8M model's KV shape.
 SERVE_REQUESTS, SERVE_RATE, SERVE_OUT_LO, SERVE_OUT_HI = 4096, 50000.0, 16, 256
-SERVE_PREFILL_TOKENS = 4096
+SERVE_PREFILL_TOKENS = 1024  # prompt tokens a step: the exact-order projections' row limit
 
 
 def select_workload(name: str, batch: int | None = None) -> None:
@@ -101,6 +110,10 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="headline workload only: skip the other configurations' runs")
+    ap.add_argument("--pg-timeout", type=int, default=300,
+                    help="process-group timeout in seconds (multi-GPU)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="microbench")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU instead of the workload's (smaller cases for profiling)")
@@ -112,6 +125,114 @@ def parse():
     args = ap.parse_args()
     select_workload(args.workload, args.batch)
     return args
+
+
+def dist_env():
+    """(rank, world size, local rank) from the torchrun environment."""
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def init_dist(world: int, dev, seconds: int) -> None:
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=seconds),
+                                device_id=dev)
+
+
+def close_dist(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def host_threads() -> int:
+    """Host cores this process may run on (torchrun sets OMP_NUM_THREADS=1,
+    so the oracle is always given this count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def sum_over_ranks(value: float, device) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+# The other configurations of the benchmark, each run by `python bench.py`
+# (no --workload) in a process of its own after the headline microbench, on
+# the same GPUs, and attached to the headline line under "configs":
+#   model     the 8M model end to end, batch 1: 64-token prompt, 448 greedy
+#             steps (each GPU its own replica: weak scaling)
+#   prefix    prefix reuse: 64 requests sharing a 384-token prefix + 32 own
+#             tokens, 96 greedy steps (64 requests per GPU: weak scaling)
+#   serve     continuous batching of 4096 Poisson requests over the GPUs
+#             (strong scaling)
+#   gqa_model the scaled GQA model, 16 sequences per GPU, 256 greedy steps
+CONFIG_RUNS = [
+    ("model", "model", ["--steps", "448"]),
+    ("prefix", "prefix", []),
+    ("serve", "serve", []),
+    ("gqa_model", "gqa-model", ["--steps", "256"]),
+]
+CONFIGS_BUDGET_S = 700.0  # all configuration runs of one bench.py invocation
+
+
+def last_json_line(text: str):
+    for line in reversed(text.splitlines()):
+        line = line.strip()
+        if line.startswith("{"):
+            try:
+                return json.loads(line)
+            except ValueError:
+                continue
+    return None
+
+
+def run_configs(args, world: int) -> dict:
+    """Runs CONFIG_RUNS one after another, each as a child process per rank
+    (a fresh CUDA context and, with several GPUs, a process group of its own
+    on its own port). Returns rank 0's result line of each, or its error."""
+    env = dict(os.environ)
+    # the children host their own rendezvous store (rank 0 child)
+    env.pop("TORCHELASTIC_USE_AGENT_STORE", None)
+    base_port = int(env.get("MASTER_PORT", "29500"))
+    out, t_begin = {}, time.time()
+    for k, (key, workload, extra) in enumerate(CONFIG_RUNS):
+        left = CONFIGS_BUDGET_S - (time.time() - t_begin)
+        if left < 30:
+            out[key] = {"error": "skipped: the configurations' time budget is spent"}
+            continue
+        env["MASTER_PORT"] = str(base_port + 1 + k)
+        cmd = [sys.executable, str(ROOT / "bench.py"), "--workload", workload, "--warmup", "3",
+               "--gpus", str(world), "--seed", str(args.seed), "--pg-timeout", "180", *extra]
+        if args.no_cpu_baseline:
+            cmd.append("--no-cpu-baseline")
+        t0 = time.time()
+        try:
+            p = subprocess.run(cmd, env=env, capture_output=True, text=True,
+                               timeout=min(400.0, left))
+            line = last_json_line(p.stdout)
+            if p.returncode != 0 or (line is None and int(env.get("RANK", "0")) == 0):
+                tail = (p.stderr or p.stdout or "").strip().splitlines()[-3:]
+                line = {"error": f"exit {p.returncode}: " + " | ".join(tail)}
+        except subprocess.TimeoutExpired:
+            line = {"error": f"timed out after {min(400.0, left):.0f} s"}
+        if line is not None:
+            line["wall_s"] = round(time.time() - t0, 1)
+        out[key] = line
+    return out
 
 
 def draw_lengths(seed: int):
@@ -258,7 +379,7 @@ def run_reference(args):
     import oracle as O
 
     lengths = draw_lengths(args.seed)
-    threads = O.max_threads()
+    threads = host_threads()
     rng = np.random.default_rng(args.seed + 7)
     inv = O.rope_inverse_frequencies(D, 10000.0)
     sample = [int(x) for x in lengths[:REF_SAMPLE]]
@@ -310,16 +431,10 @@ def run_ours(args):
     import slmkv
     from slmkv.shard import max_over_ranks
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=dev)
+    init_dist(world, dev, args.pg_timeout)
 
     def barrier():
         if world > 1:
@@ -570,11 +685,9 @@ def run_ours(args):
             "sample": (f"{min(REF_SAMPLE, B)} of the {B} seeded sequences x {LAYERS} layers per step, "
                        f"{reps} steps in {el:.1f} s, single thread (the reference's decode "
                        "attention is serial per sequence)")}
-    if rank == 0:
-        print(json.dumps(result), flush=True)
     pool.close()
-    if world > 1:
-        dist.destroy_process_group()
+    close_dist(world)
+    return result if rank == 0 else None
 
 
 def serve_trace(seed: int):
@@ -588,6 +701,26 @@ def serve_trace(seed: int):
     return arrivals, prompts, outputs
 
 
+def oracle_generate_check(tensors, prompt, generated, threads):
+    """The oracle model (model.rs:297-397 restated) prefills `prompt` and then
+    decodes the GPU's `generated` tokens one by one (the reference has no
+    prefix cache or batching: every request alone, from scratch); returns
+    (every greedy choice equal to the GPU's next token, seconds)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    cfg = dict(vocab_size=MODEL_VOCAB, hidden_size=HQ * D, intermediate_size=MODEL_INTER,
+               num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV, head_dimension=D,
+               rms_norm_epsilon=1e-5, rope_theta=10000.0, situ_beta_gate=4.0, situ_beta_up=25.0)
+    m = O.Model(cfg, tensors)
+    cache = m.new_cache(CTX)
+    t0 = time.perf_counter()
+    ok = O.argmax_finite(m.prefill(cache, [int(t) for t in prompt], threads)[-1]) == generated[0]
+    for j in range(len(generated) - 1):
+        ok = ok and O.argmax_finite(m.decode(cache, int(generated[j]), threads)) == generated[j + 1]
+    return ok, time.perf_counter() - t0
+
+
 def run_serve(args):
     """Continuous batching of the request trace on the 8M model: every step the
     scheduler plans a decode batch and a prefill batch (prompt chunks within a
@@ -597,7 +730,12 @@ def run_serve(args):
     device history indexed by request and position: a step gathers its input
     tokens from it and writes the chosen tokens back, so a preempted request
     recomputes from its own tokens. Requests arrive on the host clock.
-    Throughput = output tokens of all ranks / slowest rank's device time."""
+    Throughput = output tokens of all ranks / slowest rank's device time.
+    Every step stays on the exact-order projections (steps of at most 1024
+    rows: a 512-row decode batch and a 1024-token prefill budget). The e2e
+    run copies each request's prompt in from pinned host memory when it
+    arrives and each step's chosen tokens out. At one GPU the oracle replays
+    sampled requests from their prompts: every greedy token must agree."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -605,27 +743,21 @@ def run_serve(args):
     import slmkv
     from slmkv.shard import max_over_ranks, rank_share
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    init_dist(world, dev, args.pg_timeout)
     arrivals, prompts, outputs = serve_trace(args.seed)
     mine = rank_share([int(p + o) for p, o in zip(prompts, outputs)], world, rank)
     pool = slmkv.KvPool(num_layers=LAYERS, num_query_heads=HQ, num_key_value_heads=HKV,
                         head_dimension=D, context_length=CTX, num_blocks=B * (CTX // BLOCK),
                         max_sequences=B, device=local)
     pool.shuffle(args.seed + 1)
+    tensors = model_tensors(args.seed)
     model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=MODEL_INTER,
-                        tensors=model_tensors(args.seed))
-    # batched steps on the tensor cores (another accumulation order, within
-    # the reference's logit parity thresholds); single-row steps exact
-    model.set_exact_rows(1 if args.exact_rows is None else args.exact_rows)
-    sched = slmkv.Scheduler(pool, max_running=B, max_prefill_tokens=SERVE_PREFILL_TOKENS)
+                        tensors=tensors)
+    exact_rows = 1024 if args.exact_rows is None else args.exact_rows
+    model.set_exact_rows(exact_rows)
     # token history: row per request of this rank, prompt tokens first
     row_of = {rid: k for k, rid in enumerate(mine)}
     W = CTX + 1
@@ -633,8 +765,8 @@ def run_serve(args):
     h_hist = np.zeros((max(1, len(mine)), W), np.int32)
     for rid, k in row_of.items():
         h_hist[k, :prompts[rid]] = rng.integers(0, MODEL_VOCAB, size=int(prompts[rid]))
-    hist = torch.from_numpy(h_hist).to(dev).view(-1)
-    first_done = set()
+    p_hist = torch.from_numpy(h_hist).pin_memory()  # the prompts, on the host
+    hist = torch.zeros(h_hist.size, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
     ones = slmkv._i32_array([1] * B)
     # staging for the per-step gather / scatter indices (pinned, copied async)
@@ -647,8 +779,10 @@ def run_serve(args):
         row_arr[rid] = k
     nxt_dec = torch.zeros(B, dtype=torch.int32, device=dev)
     nxt_pre = torch.zeros(B, dtype=torch.int32, device=dev)
+    h_out = torch.zeros(2 * B, dtype=torch.int32).pin_memory()  # a step's chosen tokens
+    copied = {"h2d": 0, "d2h": 0}
 
-    def run_step():
+    def run_step(sched, first_done, e2e):
         # the decode batch is submitted and the prefill batch queued behind it:
         # one wait per step
         nd, npf = sched.plan()
@@ -683,100 +817,163 @@ def run_serve(args):
             dec = slmkv.Batch.for_sequences(pool, nd, sched._dseq, ones, stream)
             model.decode(dec, hist.index_select(0, d_idx[:nd]).to(torch.int32), None, nxt_dec[:nd])
             hist.index_copy_(0, d_idx[:nd] + 1, nxt_dec[:nd])
+            if e2e:
+                h_out[:nd].copy_(nxt_dec[:nd], non_blocking=True)
+                copied["d2h"] += 4 * nd
             dec.submit()
         if npf:
             b = slmkv.Batch.for_sequences(pool, npf, sched._pseq, sched._pcnt, stream)
             model.prefill(b, hist.index_select(0, d_idx[nd:nd + rows]).to(torch.int32), None,
                           nxt_pre[:npf])
             if firsts:
-                hist.index_copy_(0, d_idx[nd + rows:n_idx], nxt_pre.index_select(0, sel_d[:len(firsts)]))
+                firsts_tok = nxt_pre.index_select(0, sel_d[:len(firsts)])
+                hist.index_copy_(0, d_idx[nd + rows:n_idx], firsts_tok)
+                if e2e:
+                    h_out[B:B + len(firsts)].copy_(firsts_tok, non_blocking=True)
+                    copied["d2h"] += 4 * len(firsts)
             pst = b.end(raise_on_error=False)
         if dec is not None:
             dst = dec.wait(raise_on_error=False)
+        if e2e:
+            stream.synchronize()  # the chosen tokens are on the host
         return nd, npf, sched.commit(dst, pst)
 
-    # warm-up on throwaway sequences (both projection paths and a decode step)
-    warm = [pool.allocate_kv_cache(CTX) for _ in range(3)]
-    wid = torch.ones(1200, dtype=torch.int32, device=dev)
-    with pool.begin(warm, [400, 400, 400]) as b:
+    def serve_once(e2e):
+        """The whole trace once; returns (device ms, steps, output tokens,
+        preemptions, launches)."""
+        sched = slmkv.Scheduler(pool, max_running=B, max_prefill_tokens=SERVE_PREFILL_TOKENS)
+        first_done = set()
+        if not e2e:  # the prompts are resident before the timed region
+            hist.copy_(p_hist.view(-1))
+        else:
+            hist.zero_()
+        order = sorted(mine, key=lambda i: arrivals[i])
+        l0 = pool.launch_count()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_stop = torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t_start.record(stream)
+        t0 = time.perf_counter()
+        nxt, finished, failed, steps = 0, 0, 0, 0
+        while finished < len(order):
+            now = time.perf_counter() - t0
+            while nxt < len(order) and arrivals[order[nxt]] <= now:
+                i = order[nxt]
+                if e2e:  # the request's prompt arrives from the host
+                    k, P = row_of[i], int(prompts[i])
+                    hist[k * W:k * W + P].copy_(p_hist[k, :P], non_blocking=True)
+                    copied["h2d"] += 4 * P
+                sched.submit(i, int(prompts[i]), int(outputs[i]))
+                nxt += 1
+            nd, npf, fin = run_step(sched, first_done, e2e)
+            steps += 1
+            finished += len(fin)
+            failed += sum(1 for _, st, _ in fin if st != 0)
+            if nd == 0 and npf == 0 and nxt < len(order):
+                time.sleep(max(0.0, arrivals[order[nxt]] - (time.perf_counter() - t0)))
+        t_stop.record(stream)
+        torch.cuda.synchronize()
+        if failed:
+            raise RuntimeError(f"{failed} requests failed")
+        c = sched.counts()
+        sched.close()
+        return (t_start.elapsed_time(t_stop), steps, c["generated_tokens"], c["preemptions"],
+                pool.launch_count() - l0)
+
+    # warm-up on throwaway sequences (both batch kinds at the timed shapes)
+    warm = [pool.allocate_kv_cache(CTX) for _ in range(4)]
+    wid = torch.ones(SERVE_PREFILL_TOKENS, dtype=torch.int32, device=dev)
+    with pool.begin(warm, [SERVE_PREFILL_TOKENS // 4] * 4) as b:
         model.prefill(b, wid)
     with pool.begin(warm, 1) as b:
-        model.decode(b, wid[:3])
+        model.decode(b, wid[:4])
     for c in warm:
         c.free()
 
-    order = sorted(mine, key=lambda i: arrivals[i])
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_stop = torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t_start.record(stream)
-    t0 = time.perf_counter()
-    nxt, finished, failed, steps = 0, 0, 0, 0
-    while finished < len(order):
-        now = time.perf_counter() - t0
-        while nxt < len(order) and arrivals[order[nxt]] <= now:
-            i = order[nxt]
-            sched.submit(i, int(prompts[i]), int(outputs[i]))
-            nxt += 1
-        nd, npf, fin = run_step()
-        steps += 1
-        finished += len(fin)
-        failed += sum(1 for _, st, _ in fin if st != 0)
-        if nd == 0 and npf == 0 and nxt < len(order):
-            time.sleep(max(0.0, arrivals[order[nxt]] - (time.perf_counter() - t0)))
-    t_stop.record(stream)
-    torch.cuda.synchronize()
-    counts = sched.counts()
-    ms = t_start.elapsed_time(t_stop)
-    (ms,) = max_over_ranks([ms], device=dev)
-    tokens = torch.tensor([float(counts["generated_tokens"])], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(tokens)
-    if failed:
-        raise RuntimeError(f"{failed} requests failed")
+    ms, steps, generated, preemptions, launches = serve_once(False)
+    hist_done = hist.view(-1, W).cpu().numpy().copy()
+    copied["h2d"] = copied["d2h"] = 0
+    e2e_ms, e2e_steps, _, _, _ = serve_once(True)
+    if not np.array_equal(hist.view(-1, W).cpu().numpy(), hist_done):
+        raise RuntimeError("the e2e run generated other tokens than the device-resident run")
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], device=dev)
+    tokens = sum_over_ranks(generated, dev)
     result = {
-        "metric": METRIC, "value": float(tokens.item()) / (ms / 1e3), "unit": "tok/s",
+        "metric": METRIC, "value": tokens / (ms / 1e3), "unit": "tok/s",
         "n_gpus": world, "steps": steps, "warmup": 0, "ms_per_step": ms / max(1, steps),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": (f"continuous batching: {SERVE_REQUESTS} requests, Poisson "
-                                f"arrivals {SERVE_RATE:.0f}/s, prompts U[{LEN_LO},{LEN_HI}], "
-                                f"outputs U[{SERVE_OUT_LO},{SERVE_OUT_HI}], <= {B} running per "
-                                f"GPU; the 8M model ({LAYERS} layers, hidden {HQ * D}, FFN "
+        "config": {"workload": (f"continuous batching: {SERVE_REQUESTS} requests shared by the "
+                                f"GPUs, Poisson arrivals {SERVE_RATE:.0f}/s, prompts "
+                                f"U[{LEN_LO},{LEN_HI}], outputs U[{SERVE_OUT_LO},{SERVE_OUT_HI}], "
+                                f"<= {B} running per GPU, {SERVE_PREFILL_TOKENS} prompt tokens "
+                                f"per step; the 8M model ({LAYERS} layers, hidden {HQ * D}, FFN "
                                 f"{MODEL_INTER}, Hq={HQ}, Hkv={HKV}, d={D}, vocab {MODEL_VOCAB}, "
                                 "f32 KV, random N(0, 0.02^2) weights), random prompt ids, "
                                 "greedy decoding"),
-                   "name": "serve", "requests_per_rank": len(order), "seed": args.seed,
-                   "exact_rows": 1 if args.exact_rows is None else args.exact_rows},
-        "output_tokens": int(tokens.item()), "preemptions": counts["preemptions"],
-        "gpu_launches": pool.launch_count(),
+                   "name": "serve", "requests_per_rank": len(mine), "seed": args.seed,
+                   "exact_rows": exact_rows},
+        "output_tokens": int(tokens), "preemptions": preemptions,
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": copied["h2d"] // max(1, e2e_steps),
+                "d2h_bytes_per_step": copied["d2h"] // max(1, e2e_steps),
+                "loop": "each request's prompt ids copied in from pinned host memory on "
+                        "arrival, each step's chosen tokens copied out and synchronized "
+                        "(plus the step's gather indices, as in the device-resident run)"},
+        "gpu_launches": launches,
+        "projections": ("this library's fused exact-order projection kernels (bf16 operands, "
+                        "the reference's fp32 fold order) for every step" if exact_rows >= 1024
+                        else f"exact order up to {exact_rows} rows, tensor-core GEMMs beyond "
+                             "(outside the fp32 parity bar)"),
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # the three cheapest requests of this rank, replayed by the oracle
+        sample = sorted(mine, key=lambda i: int(prompts[i] + outputs[i]))[:3]
+        ok, secs, toks = True, 0.0, 0
+        for rid in sample:
+            k, P, Ou = row_of[rid], int(prompts[rid]), int(outputs[rid])
+            good, t = oracle_generate_check(tensors, hist_done[k, :P], list(hist_done[k, P:P + Ou]),
+                                            host_threads())
+            ok, secs, toks = ok and good, secs + t, toks + Ou
+        result["parity"] = {"greedy_tokens_match_cpu": ok, "requests_checked": len(sample),
+                            "tokens_checked": toks,
+                            "oracle": "oracle model replaying each request alone from its prompt"}
+        result["cpu_baseline"] = {
+            "value": toks / secs, "unit": "tok/s", "cores": host_threads(), "kind": "port",
+            "sample": (f"{len(sample)} requests ({toks} output tokens) served one at a time as the "
+                       "reference server does (worker.rs:87-98): oracle prefill of the prompt, "
+                       "then greedy decode; OpenMP projections, serial attention")}
     if rank == 0:
         print(json.dumps(result), flush=True)
-    sched.close()
     model.close()
     pool.close()
-    if world > 1:
-        dist.destroy_process_group()
+    close_dist(world)
 
 
 def run_prefix(args):
     """Prefix reuse on the 8M model: request 0 prefills the shared prefix and
     publishes its full blocks; the other requests attach them through the
-    block table and prefill only their own suffix over the attached cache;
-    then every request decodes PREFIX_DECODE_STEPS greedy tokens in batched
-    steps, each step's tokens staying on the device. Reports the prefill
-    tokens the reuse saved and the decode throughput."""
+    block table and prefill only their own suffix over the attached cache (in
+    batches of at most 1024 rows, the exact-order projections' limit); then
+    every request decodes PREFIX_DECODE_STEPS greedy tokens in batched steps,
+    each step's tokens staying on the device. Each GPU serves its own 64
+    requests (weak scaling). Reports the prefill tokens the reuse saved and
+    the decode throughput; the e2e run copies the prompts in from pinned host
+    memory and every step's chosen tokens out. At one GPU the oracle
+    generates two requests alone, from their whole prompts (the reference has
+    no prefix cache): every greedy token must agree."""
     import numpy as np
     import torch
 
     import slmkv
+    from slmkv.shard import max_over_ranks
 
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
+    init_dist(world, dev, args.pg_timeout)
     prefix_len, suffix_len = LEN_LO, LEN_HI
     rng = np.random.default_rng(args.seed + 77)
     prefix_ids = [int(x) for x in rng.integers(0, MODEL_VOCAB, size=prefix_len)]
@@ -787,91 +984,140 @@ def run_prefix(args):
                         num_blocks=B * ((total_len + BLOCK - 1) // BLOCK) + 160, max_sequences=B,
                         device=local)
     pool.shuffle(args.seed + 1)
+    tensors = model_tensors(args.seed)
     model = slmkv.Model(pool, vocab_size=MODEL_VOCAB, intermediate_size=MODEL_INTER,
-                        tensors=model_tensors(args.seed))
-    model.set_exact_rows(1 if args.exact_rows is None else args.exact_rows)
-
-    def ids(tokens):
-        return torch.tensor(tokens, dtype=torch.int32, device=dev)
-
-    # warm-up on throwaway sequences with the timed phase's shapes (the
-    # prefix, one suffix, the other requests' suffixes in one batch, a decode
-    # step of all), so that one-time library and module loading, GEMM
-    # selection and scratch growth stay out of the timed prefill
-    tok = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(2)]
-    warm = [pool.allocate_kv_cache(CTX) for _ in range(B - 1)]
-    wtok = torch.zeros(B, dtype=torch.int32, device=dev)
-    with pool.begin(warm[:1], [prefix_len]) as b:
-        model.prefill(b, ids([1] * prefix_len))
-    with pool.begin(warm[:1], [suffix_len]) as b:
-        model.prefill(b, ids([2] * suffix_len), None, wtok[:1])
-    with pool.begin(warm, [suffix_len] * (B - 1)) as b:
-        model.prefill(b, ids([3] * (suffix_len * (B - 1))), None, wtok[:B - 1])
-    with pool.begin(warm, 1) as b:
-        model.decode(b, wtok[:B - 1], None, tok[1][:B - 1])
-    for c in warm:
-        c.free()
-
-    caches = [pool.allocate_kv_cache(total_len) for _ in range(B)]
+                        tensors=tensors)
+    exact_rows = 1024 if args.exact_rows is None else args.exact_rows
+    model.set_exact_rows(exact_rows)
+    # the other requests' suffixes, in prefill batches of at most 1024 rows
+    per_batch = max(1, 1024 // suffix_len)
+    groups = [list(range(i, min(B, i + per_batch))) for i in range(1, B, per_batch)]
     stream = torch.cuda.current_stream()
-    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    pre_ids, first_suffix = ids(prefix_ids), ids(suffix_ids[0])
-    rest_ids = ids([t for sfx in suffix_ids[1:] for t in sfx])
-    torch.cuda.synchronize()
-    e[0].record(stream)
-    # request 0: the prefix, published, then its own suffix
-    with pool.begin([caches[0]], [prefix_len]) as b:
-        model.prefill(b, pre_ids)
-    indexed = caches[0].publish_prefix(prefix_ids)
-    with pool.begin([caches[0]], [suffix_len]) as b:
-        model.prefill(b, first_suffix, None, tok[0][:1])
-    # the others: attach the prefix blocks, prefill only the suffix
-    reused = [c.attach_prefix(prefix_ids + suffix_ids[i]) for i, c in enumerate(caches[1:], 1)]
-    with pool.begin(caches[1:], [suffix_len] * (B - 1)) as b:
-        model.prefill(b, rest_ids, None, tok[0][1:])
-    e[1].record(stream)
-    # batched greedy decode of every request
-    plan = pool.step_plan(caches, 1)
-    inflight = []
-    e[2].record(stream)
-    for i in range(PREFIX_DECODE_STEPS):
-        b = plan.begin()
-        model.decode(b, tok[i % 2], None, tok[(i + 1) % 2])
-        inflight.append(b.submit())
-        while len(inflight) > 1:
-            if any(inflight.pop(0).wait(raise_on_error=False)):
+    # all prompt tokens on the host (pinned): prefix, then every suffix
+    h_ids = torch.tensor(prefix_ids + [t for sfx in suffix_ids for t in sfx],
+                         dtype=torch.int32).pin_memory()
+    d_ids = torch.zeros_like(h_ids, device=dev)
+    tok = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(2)]
+    gen = torch.zeros((PREFIX_DECODE_STEPS + 1, B), dtype=torch.int32, device=dev)
+    h_gen = torch.zeros(B, dtype=torch.int32).pin_memory()
+
+    def suffix(i):  # request i's suffix tokens in d_ids
+        return d_ids[prefix_len + i * suffix_len:prefix_len + (i + 1) * suffix_len]
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def run_once(e2e):
+        caches = [pool.allocate_kv_cache(total_len) for _ in range(B)]
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        barrier()
+        torch.cuda.synchronize()
+        e[0].record(stream)
+        if e2e:
+            d_ids.copy_(h_ids, non_blocking=True)
+        # request 0: the prefix, published, then its own suffix
+        with pool.begin([caches[0]], [prefix_len]) as b:
+            model.prefill(b, d_ids[:prefix_len])
+        indexed = caches[0].publish_prefix(prefix_ids)
+        with pool.begin([caches[0]], [suffix_len]) as b:
+            model.prefill(b, suffix(0), None, tok[0][:1])
+        # the others: attach the prefix blocks, prefill only the suffix
+        reused = [c.attach_prefix(prefix_ids + suffix_ids[i]) for i, c in enumerate(caches[1:], 1)]
+        for g in groups:
+            lo, hi = g[0], g[-1] + 1
+            with pool.begin(caches[lo:hi], [suffix_len] * len(g)) as b:
+                model.prefill(b, d_ids[prefix_len + lo * suffix_len:prefix_len + hi * suffix_len],
+                              None, tok[0][lo:hi])
+        e[1].record(stream)
+        gen[0].copy_(tok[0])
+        # batched greedy decode of every request
+        plan = pool.step_plan(caches, 1)
+        inflight = []
+        e[2].record(stream)
+        for i in range(PREFIX_DECODE_STEPS):
+            b = plan.begin()
+            model.decode(b, tok[i % 2], None, tok[(i + 1) % 2])
+            if e2e:
+                h_gen.copy_(tok[(i + 1) % 2], non_blocking=True)
+                if any(b.end(raise_on_error=False)):
+                    raise RuntimeError("decode step failed")
+                stream.synchronize()
+            else:
+                gen[i + 1].copy_(tok[(i + 1) % 2])
+                inflight.append(b.submit())
+                while len(inflight) > 1:
+                    if any(inflight.pop(0).wait(raise_on_error=False)):
+                        raise RuntimeError("decode step failed")
+        e[3].record(stream)
+        for b in inflight:
+            if any(b.wait(raise_on_error=False)):
                 raise RuntimeError("decode step failed")
-    e[3].record(stream)
-    for b in inflight:
-        if any(b.wait(raise_on_error=False)):
-            raise RuntimeError("decode step failed")
-    torch.cuda.synchronize()
-    lengths = [c.sequence_length() for c in caches]
-    if lengths != [total_len] * B or any(r != prefix_len for r in reused):
-        raise RuntimeError(f"unexpected lengths {set(lengths)} or reuse {set(reused)}")
-    prefill_ms, decode_ms = e[0].elapsed_time(e[1]), e[2].elapsed_time(e[3])
+        torch.cuda.synchronize()
+        lengths = [c.sequence_length() for c in caches]
+        if lengths != [total_len] * B or any(r != prefix_len for r in reused):
+            raise RuntimeError(f"unexpected lengths {set(lengths)} or reuse {set(reused)}")
+        for c in caches:  # the prefix index keeps its blocks; a later run attaches to them
+            c.free()
+        return e[0].elapsed_time(e[1]), e[2].elapsed_time(e[3]), e[0].elapsed_time(e[3]), indexed
+
+    d_ids.copy_(h_ids)
+    run_once(False)  # warm-up with the timed shapes
+    l0 = pool.launch_count()
+    prefill_ms, decode_ms, _, indexed = run_once(False)
+    launches = pool.launch_count() - l0
+    gen_h = gen.cpu().numpy().T.copy()  # [B, steps + 1]
+    _, e2e_decode_ms, _, _ = run_once(True)
+    prefill_ms, decode_ms, e2e_decode_ms = max_over_ranks([prefill_ms, decode_ms, e2e_decode_ms],
+                                                          device=dev)
     computed = prefix_len + B * suffix_len
     without = B * (prefix_len + suffix_len)
-    tokens = B * PREFIX_DECODE_STEPS
+    tokens = world * B * PREFIX_DECODE_STEPS
     result = {
-        "metric": METRIC, "value": tokens / (decode_ms / 1e3), "unit": "tok/s", "n_gpus": 1,
-        "steps": PREFIX_DECODE_STEPS, "warmup": 0, "ms_per_step": decode_ms / PREFIX_DECODE_STEPS,
+        "metric": METRIC, "value": tokens / (decode_ms / 1e3), "unit": "tok/s", "n_gpus": world,
+        "steps": PREFIX_DECODE_STEPS, "warmup": 1, "ms_per_step": decode_ms / PREFIX_DECODE_STEPS,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": (f"prefix reuse on the 8M model: {B} requests share a "
+        "config": {"workload": (f"prefix reuse on the 8M model: {B} requests per GPU share a "
                                 f"{prefix_len}-token random prefix and add {suffix_len} own "
                                 f"tokens, then {PREFIX_DECODE_STEPS} greedy decode steps each; "
                                 f"{LAYERS} layers, hidden {HQ * D}, Hq={HQ}, Hkv={HKV}, d={D}, "
                                 "f32 KV, random N(0, 0.02^2) weights"), "name": "prefix",
-                   "exact_rows": 1 if args.exact_rows is None else args.exact_rows,
-                   "seed": args.seed},
+                   "exact_rows": exact_rows, "seed": args.seed},
         "prefill_tokens_computed": computed, "prefill_tokens_without_reuse": without,
         "prefill_tokens_saved": without - computed, "prefix_blocks_indexed": indexed,
-        "prefill_ms": prefill_ms, "gpu_launches": pool.launch_count(),
+        "prefill_ms": prefill_ms,
+        "e2e": {"value": tokens / (e2e_decode_ms / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B,
+                "loop": "decode steps with every step's chosen tokens copied to pinned host memory "
+                        "and synchronized (the prompts copied in from pinned host memory before "
+                        "the prefill)"},
+        "gpu_launches": launches,
+        "projections": "this library's fused exact-order projection kernels for every step"
+                       if exact_rows >= 1024 else
+                       f"exact order up to {exact_rows} rows, tensor-core GEMMs beyond",
     }
-    print(json.dumps(result), flush=True)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ok, secs = True, 0.0
+        for i in (0, 1):  # request 0 prefilled the prefix; request 1 attached it
+            good, t = oracle_generate_check(tensors, prefix_ids + suffix_ids[i],
+                                            [int(x) for x in gen_h[i]], host_threads())
+            ok, secs = ok and good, secs + t
+        result["parity"] = {"greedy_tokens_match_cpu": ok, "requests_checked": 2,
+                            "tokens_checked": 2 * (PREFIX_DECODE_STEPS + 1),
+                            "oracle": "oracle model generating each request alone from its "
+                                      "whole prompt"}
+        result["cpu_baseline"] = {
+            "value": 2 * PREFIX_DECODE_STEPS / secs, "unit": "tok/s", "cores": host_threads(),
+            "kind": "port",
+            "sample": (f"2 requests one at a time: oracle prefill of all {prefix_len + suffix_len} "
+                       f"prompt tokens (no prefix cache in the reference), then "
+                       f"{PREFIX_DECODE_STEPS} greedy steps; decode tokens / total seconds")}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
     model.close()
     pool.close()
+    close_dist(world)
 
 
 def model_tensors(seed: int, intermediate_size: int = MODEL_INTER):
@@ -910,24 +1156,30 @@ def model_cpu_baseline(tensors, prompt, threads: int, budget_s: float = 10.0):
         tok = O.argmax_finite(m.decode(cache, tok, threads))
         n += 1
     dt = time.perf_counter() - t0
+    toks.append(tok)  # n steps choose n tokens after the prompt's own
     return n / dt, n, toks
 
 
 def run_model(args):
-    """The 8M model end to end on one GPU: prefill a 64-token random prompt,
-    then greedy decode (one token per step, batch 1) through slm_model_decode;
-    each step's next token stays on the device and feeds the next step's
-    embedding. `value` is the decode steps per second with two steps in
-    flight; `e2e` copies each step's token from pinned host memory and reads
-    the chosen token back before the next step (a streaming server's loop)."""
+    """The 8M model end to end: prefill a 64-token random prompt, then greedy
+    decode (one token per step, batch 1) through slm_model_decode; each step's
+    next token stays on the device and feeds the next step's embedding.
+    `value` is the decode steps per second with two steps in flight, summed
+    over the GPUs (each runs its own replica of the request: weak scaling);
+    `e2e` copies each step's token from pinned host memory and reads the
+    chosen token back before the next step (a streaming server's loop). At one
+    GPU the oracle generates from the same prompt on the host cores: every
+    greedy token must agree (the CPU baseline)."""
     import numpy as np
     import torch
 
     import slmkv
+    from slmkv.shard import max_over_ranks
 
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
+    init_dist(world, dev, args.pg_timeout)
     rng = np.random.default_rng(args.seed)
     prompt = [int(x) for x in rng.integers(0, MODEL_VOCAB, size=LEN_LO)]
     steps = min(max(args.steps, 1), LEN_HI)
@@ -942,14 +1194,21 @@ def run_model(args):
     stream = torch.cuda.current_stream()
     ids = torch.tensor(prompt, dtype=torch.int32, device=dev)
     tok = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(2)]
+    gen = torch.zeros(LEN_HI + 1, dtype=torch.int32, device=dev)
 
-    def generate(n_steps, e2e=False):
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def generate(n_steps, e2e=False, record=False):
         cache = pool.allocate_kv_cache(CTX)
         e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         e[0].record(stream)
         with pool.begin([cache], [LEN_LO]) as b:
             model.prefill(b, ids, None, tok[0])
         e[1].record(stream)
+        if record:
+            gen[0:1].copy_(tok[0])
         plan = pool.step_plan([cache], 1)
         h_tok = torch.zeros(1, dtype=torch.int32).pin_memory()
         out = []
@@ -965,6 +1224,8 @@ def run_model(args):
                 cur.copy_(h_tok, non_blocking=True)
             b = plan.begin()
             model.decode(b, cur, None, nxt)
+            if record:
+                gen[i + 1:i + 2].copy_(nxt)
             if e2e:
                 if b.end(raise_on_error=False) != [0]:
                     raise RuntimeError("decode step failed")
@@ -989,46 +1250,57 @@ def run_model(args):
 
     for _ in range(max(args.warmup, 3)):
         generate(min(steps, 16))
+    barrier()
     l0 = pool.launch_count()
     prefill_ms, decode_ms, _, _ = generate(steps)
     launches = pool.launch_count() - l0
+    barrier()
     _, _, e2e_s, toks = generate(steps, e2e=True)
-    value = steps / (decode_ms / 1e3)
+    _, _, _, _ = generate(steps, record=True)  # the generated tokens, for the parity check
+    decode_ms, e2e_ms, prefill_ms = max_over_ranks([decode_ms, e2e_s * 1e3, prefill_ms], device=dev)
+    gen_h = gen[:steps + 1].cpu().tolist()
+    if gen_h != toks:
+        raise RuntimeError("the e2e run chose other tokens than the device-resident run")
+    value = world * steps / (decode_ms / 1e3)
     result = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": 1, "steps": steps,
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
         "warmup": max(args.warmup, 3), "ms_per_step": decode_ms / steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": (f"8M model end to end: batch 1, {LEN_LO}-token random prompt, "
-                                f"{steps} greedy decode steps; {LAYERS} layers, hidden {HQ * D}, "
-                                f"FFN {MODEL_INTER} SiTU-GLU, Hq={HQ}, Hkv={HKV}, d={D}, "
+        "config": {"workload": (f"8M model end to end: batch 1 per GPU, {LEN_LO}-token random "
+                                f"prompt, {steps} greedy decode steps; {LAYERS} layers, hidden "
+                                f"{HQ * D}, FFN {MODEL_INTER} SiTU-GLU, Hq={HQ}, Hkv={HKV}, d={D}, "
                                 f"vocab {MODEL_VOCAB}, f32 KV, random N(0, 0.02^2) weights "
                                 f"(seed {args.seed})"), "name": "model", "seed": args.seed,
                    "exact_rows": 1024 if args.exact_rows is None else args.exact_rows},
         "prefill_ms": prefill_ms,
-        "e2e": {"value": steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
-                "d2h_bytes_per_step": 4,
+        "e2e": {"value": world * steps / (e2e_ms / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                 "loop": "pinned H2D of the step's token, decode, D2H of the chosen token, "
                         "host synchronizes every step"},
         "gpu_launches": launches,
         "projections": "this library's fused exact-order projection kernels (bf16 operands, "
-                       "the reference's fp32 fold order); cuBLAS fp32 SGEMM for the tied head",
+                       "the reference's fp32 fold order); cuBLAS fp32 SGEMV for the tied head "
+                       "of one row",
         "generated_head": toks[:8],
     }
-    if not args.no_cpu_baseline:
-        sys.path.insert(0, str(ROOT / "oracle"))
-        import oracle as O
-
-        threads = O.max_threads()
-        tps, n, cpu_toks = model_cpu_baseline(tensors, prompt, threads)
-        # both lists start with the prompt's own next token
-        result["greedy_tokens_match_cpu"] = cpu_toks[:n] == toks[:n]
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        tps, n, cpu_toks = model_cpu_baseline(tensors, prompt, threads, budget_s=1e9)
+        # every greedy token of the run, the prompt's own next token first
+        match = cpu_toks == toks[:len(cpu_toks)]
+        result["parity"] = {"greedy_tokens_match_cpu": match, "tokens_checked": len(cpu_toks),
+                            "oracle": "oracle model (model.rs:342-397 restated), same weights "
+                                      "and prompt"}
+        result["greedy_tokens_match_cpu"] = match
         result["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port",
                                   "sample": f"{n} greedy decode steps of the same model and "
                                             f"prompt (oracle, OpenMP projections, serial "
                                             f"attention as the reference)"}
-    print(json.dumps(result), flush=True)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
     model.close()
     pool.close()
+    close_dist(world)
 
 
 def gqa_model_step_bytes(lengths) -> int:
@@ -1077,7 +1349,10 @@ def run_gqa_model(args):
     device. Projections run as tensor-core GEMMs (cuBLAS bf16, fp32
     accumulate). value = decode tokens of all ranks / the slowest rank's
     device time; e2e copies each step's tokens from pinned host memory and
-    reads the chosen tokens back before the next step."""
+    reads the chosen tokens back before the next step. Parity of this shape
+    (bf16 KV, 2e-2) is checked by the GPU tests on two of its layers; the
+    oracle's CPU prefill of 16 prompts of thousands of tokens would take
+    hours."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -1085,15 +1360,10 @@ def run_gqa_model(args):
     import slmkv
     from slmkv.shard import max_over_ranks
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    init_dist(world, dev, args.pg_timeout)
     steps = min(max(args.steps, 1), GQA_MODEL_STEPS)
     warm = max(args.warmup, 3)
     # B lengths per rank from one seeded draw, so rank r's share is the same
@@ -1227,7 +1497,7 @@ def run_gqa_model(args):
         sys.path.insert(0, str(ROOT / "oracle"))
         import oracle as O
 
-        threads = O.max_threads()
+        threads = host_threads()
         at = int(np.mean(lens)) + steps // 2
         tps, n = gqa_model_cpu_baseline(tensors, at, args.seed, threads)
         result["cpu_baseline"] = {
@@ -1240,8 +1510,7 @@ def run_gqa_model(args):
         print(json.dumps(result), flush=True)
     model.close()
     pool.close()
-    if world > 1:
-        dist.destroy_process_group()
+    close_dist(world)
 
 
 def main():
@@ -1257,7 +1526,13 @@ def main():
     elif WORKLOAD_NAME == "prefix":
         run_prefix(args)
     else:
-        run_ours(args)
+        result = run_ours(args)
+        if WORKLOAD_NAME == "microbench" and not args.no_configs and args.batch is None:
+            configs = run_configs(args, dist_env()[1])
+            if result is not None:
+                result["configs"] = configs
+        if result is not None:
+            print(json.dumps(result), flush=True)
 
 
 if __name__ == "__main__":

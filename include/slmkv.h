@@ -175,6 +175,20 @@ slm_status slm_batch_append_layer(slm_batch* batch, int32_t layer, const float* 
  * q: [sum(counts), q_heads, d] (unrotated if rotate_query), out likewise. */
 slm_status slm_batch_prefill_attention(slm_batch* batch, int32_t layer, const float* d_query,
                                        int32_t rotate_query, float* d_out);
+/* The attention of slm_batch_prefill_attention (and, for a batch whose token
+ * counts are all 1, the attention half of slm_batch_decode_layer, after
+ * slm_batch_append_layer with rotate_keys) computed in the reference's own
+ * operation order, bit for bit with its CPU path: scaled_causal_scores,
+ * causal_probabilities and attend_values (attention.rs:195-399) for a prompt,
+ * attend_cached_query (attention.rs:677-759) for a decoded token; each score
+ * an in-order fma fold, softmax_in_place's sequential sum and glibc's expf
+ * (softmax.rs:26-44), each output an in-order fma fold over the positions.
+ * f32 pools only; rows of up to 57344 positions. Slower than the split-K
+ * kernels (one warp per token row and query head, a sequential sum); the
+ * model step uses it on its exact-order path. Same arguments as
+ * slm_batch_prefill_attention. */
+slm_status slm_batch_attention_exact(slm_batch* batch, int32_t layer, const float* d_query,
+                                     int32_t rotate_query, float* d_out);
 /* Closes the step: waits for its stream, and reports per sequence (h_status
  * may be NULL) 0 or SLM_ERR_NON_FINITE. A sequence whose appends were not
  * finite, whose attention met a score that is not finite (softmax.rs:17-22,

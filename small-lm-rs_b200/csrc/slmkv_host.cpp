@@ -1445,6 +1445,46 @@ slm_status slm_batch_prefill_attention(slm_batch* b, int32_t layer, const float*
   return SLM_OK;
 }
 
+slm_status slm_batch_attention_exact(slm_batch* b, int32_t layer, const float* d_query,
+                                     int32_t rotate_query, float* d_out) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_ctx* ctx = b->ctx;
+  slm_status rc = batch_layer_check(b, layer);
+  if (rc) return rc;
+  if (!b->layer_done[layer])
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention",
+                       "layer %d must be appended before its attention", layer);
+  if (ctx->cfg.kv_dtype != SLM_KV_F32)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention",
+                       "exact-order attention needs an f32 pool");
+  if (!d_query || !d_out) return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "null tensor");
+  int32_t max_ctx = 0;
+  for (size_t i = 0; i < b->seq_ids.size(); ++i)
+    max_ctx = std::max(max_ctx, b->base[i] + b->counts[i]);
+  if (max_ctx > kExactMaxCtx)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention",
+                       "exact-order attention takes at most %d positions, the batch reaches %d",
+                       kExactMaxCtx, max_ctx);
+  rc = flush_excess(ctx, b->stream, 0, 0);  // the kernel reads the device block table
+  if (rc) return rc;
+  PrefillLaunch p{};
+  p.g = ctx->geom();
+  p.layer = layer;
+  p.seqs = b->dev.seqs;
+  p.n_seq = static_cast<int32_t>(b->seq_ids.size());
+  p.total_tokens = b->total_tokens;
+  p.q = d_query;
+  p.rotate = rotate_query != 0;
+  p.out = d_out;
+  p.max_count = b->max_count;
+  p.status = b->dev.status;
+  p.max_ctx = max_ctx;
+  ctx->prev_decode_layer = -1;
+  CU(ctx, launch_exact_attention(p, b->stream));
+  ++ctx->launches;
+  return SLM_OK;
+}
+
 namespace {
 // Rolls sequence `id` back to at most `target` tokens in every layer and
 // forces the same rollback on every later batch (submitted or open) that

@@ -157,9 +157,15 @@ struct PrefillLaunch {
   float* out;
   int32_t max_count;  // largest per-sequence token count
   int32_t* status;    // [n_seq]: kStatusNonFiniteScore when a score is not finite
+  int32_t max_ctx;    // exact-order attention: the longest row (positions attended)
   CUtensorMap tmap_k, tmap_v;  // bf16 pools: the decode kernel's pool maps
 };
 cudaError_t launch_prefill(const PrefillLaunch& p, cudaStream_t s);
+// Attention in the reference's operation order, bit for bit (f32 pools);
+// its shared memory per launch, and the longest row a launch can take.
+cudaError_t launch_exact_attention(const PrefillLaunch& p, cudaStream_t s);
+size_t exact_attention_smem(int32_t max_ctx, int warps);
+constexpr int32_t kExactMaxCtx = 56 * 1024;
 // bf16 pools on the tensor cores (tcgen05): slmkv_prefill_tc.cu.
 bool prefill_tc_supported(const PrefillLaunch& p);
 cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s);

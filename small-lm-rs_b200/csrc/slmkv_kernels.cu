@@ -20,6 +20,7 @@
 #include <cstdint>
 
 #include "slmkv_internal.h"
+#include "slmkv_libm.h"
 
 namespace slmkv {
 namespace {
@@ -1248,6 +1249,131 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillLaunch p) {
 }
 
 // ---------------------------------------------------------------------------
+// Attention in the reference's operation order (f32 pools), bit for bit.
+// One warp per (token row, query head): the row's query at position qpos
+// attends positions 0..qpos of its sequence's cache, as
+// scaled_causal_scores / causal_probabilities / attend_values do for a prompt
+// (attention.rs:195-399; masked positions hold f32::MIN, whose exp is 0 and
+// which add nothing) and attend_cached_query does for a decoded token
+// (attention.rs:677-759):
+//   score_j = fold_i fma(q_i, k_j,i) from 0, times (d as f32).sqrt().recip()
+//   m = max_j score_j; p_j = exp(score_j - m) (glibc's expf, restated);
+//   sum = p_0 + p_1 + ... in order; p_j /= sum           (softmax.rs:26-44)
+//   out_d = fold_j fma(v_j,d, p_j, out_d) from 0           (attention.rs:751-756)
+// Scores and probabilities of the row live in this warp's shared memory;
+// the sum is one lane's sequential fold. A non-finite score or sum flags
+// the sequence (softmax.rs:17-22,35-40).
+// ---------------------------------------------------------------------------
+constexpr float kScaleExact = 0.125f;  // (64 as f32).sqrt().recip(), exact
+
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) exact_attention_kernel(const PrefillLaunch p) {
+  extern __shared__ __align__(16) float sm_exact[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int Hq = p.g.q_heads, Hkv = p.g.kv_heads;
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * WARPS + warp;
+  if (item >= static_cast<int64_t>(p.total_tokens) * Hq) return;  // no CTA barrier below
+  const int r = static_cast<int>(item / Hq), h = static_cast<int>(item - static_cast<int64_t>(r) * Hq);
+  const int si = warp_find_seq(p.seqs, p.n_seq, r, lane);
+  const SeqEntry se = p.seqs[si];
+  const int qpos = se.base + (r - se.row_offset);
+  const int L = qpos + 1;
+  float* qs = sm_exact + static_cast<size_t>(warp) * (D + p.max_ctx);
+  float* ps = qs + D;
+  float2 x = reinterpret_cast<const float2*>(p.q + (static_cast<size_t>(r) * Hq + h) * D)[lane];
+  if (p.rotate) x = rope_pair(x, p.g.rope[static_cast<size_t>(qpos) * (D / 2) + lane]);
+  reinterpret_cast<float2*>(qs)[lane] = x;
+  __syncwarp();
+  const int kvh = h / (Hq / Hkv);
+  const size_t layer_off = static_cast<size_t>(p.layer) * p.g.layer_elems;
+  const float* kb = static_cast<const float*>(p.g.k) + layer_off;
+  const float* vb = static_cast<const float*>(p.g.v) + layer_off;
+  const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
+  auto row_of = [&](const float* base, int j) {
+    const int32_t blk = checked_block(p.g, bt[j >> 4]);
+    return base + ((static_cast<size_t>(blk) * Hkv + kvh) * kBlockTokens + (j & 15)) * D;
+  };
+  bool bad = false;
+  // scores: lane l takes positions l, l+32, ...; two rows at a time
+  for (int j0 = lane; j0 < L; j0 += 64) {
+    const int j1 = j0 + 32;
+    const bool two = j1 < L;
+    const float4* k0 = reinterpret_cast<const float4*>(row_of(kb, j0));
+    const float4* k1 = reinterpret_cast<const float4*>(row_of(kb, two ? j1 : j0));
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int c = 0; c < D / 4; ++c) {
+      const float4 q4 = reinterpret_cast<const float4*>(qs)[c];
+      const float4 x0 = k0[c], x1 = k1[c];
+      a0 = fmaf(q4.x, x0.x, a0);
+      a1 = fmaf(q4.x, x1.x, a1);
+      a0 = fmaf(q4.y, x0.y, a0);
+      a1 = fmaf(q4.y, x1.y, a1);
+      a0 = fmaf(q4.z, x0.z, a0);
+      a1 = fmaf(q4.z, x1.z, a1);
+      a0 = fmaf(q4.w, x0.w, a0);
+      a1 = fmaf(q4.w, x1.w, a1);
+    }
+    const float s0 = __fmul_rn(a0, kScaleExact), s1 = __fmul_rn(a1, kScaleExact);
+    bad |= !isfinite(s0);
+    ps[j0] = s0;
+    if (two) {
+      bad |= !isfinite(s1);
+      ps[j1] = s1;
+    }
+  }
+  __syncwarp();
+  float m = -INFINITY;
+  for (int j = lane; j < L; j += 32) m = fmaxf(m, ps[j]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
+  for (int j = lane; j < L; j += 32) ps[j] = libm::slm_expf(__fsub_rn(ps[j], m));
+  __syncwarp();
+  float sum = 0.f;
+  if (lane == 0) {
+    int j = 0;
+    for (; j + 4 <= L; j += 4) {  // ps is 16-byte aligned (D floats in)
+      const float4 v = *reinterpret_cast<const float4*>(ps + j);
+      sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, v.x), v.y), v.z), v.w);
+    }
+    for (; j < L; ++j) sum = __fadd_rn(sum, ps[j]);
+  }
+  sum = __shfl_sync(kFull, sum, 0);
+  bad |= !(isfinite(sum) && sum > 0.f);
+  for (int j = lane; j < L; j += 32) ps[j] = __fdiv_rn(ps[j], sum);
+  __syncwarp();
+  // values: lane owns dims 2l, 2l+1; one 16-token block of V rows in flight
+  // while the previous block's fma chain runs
+  float2 o = make_float2(0.f, 0.f);
+  float2 cur[kBlockTokens], nxt[kBlockTokens];
+  auto load_block = [&](float2 (&dst)[kBlockTokens], int j0) {
+    const float2* vr = reinterpret_cast<const float2*>(row_of(vb, j0));
+    const int n = min(kBlockTokens, L - j0);
+#pragma unroll
+    for (int t = 0; t < kBlockTokens; ++t)
+      dst[t] = (t < n) ? vr[t * (D / 2) + lane] : make_float2(0.f, 0.f);
+  };
+  load_block(cur, 0);
+  for (int j0 = 0; j0 < L; j0 += kBlockTokens) {
+    if (j0 + kBlockTokens < L) load_block(nxt, j0 + kBlockTokens);
+    const int n = min(kBlockTokens, L - j0);
+#pragma unroll
+    for (int t = 0; t < kBlockTokens; ++t) {
+      if (t < n) {
+        const float pj = ps[j0 + t];
+        o.x = fmaf(cur[t].x, pj, o.x);
+        o.y = fmaf(cur[t].y, pj, o.y);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kBlockTokens; ++t) cur[t] = nxt[t];
+  }
+  reinterpret_cast<float2*>(p.out + (static_cast<size_t>(r) * Hq + h) * D)[lane] = o;
+  if (__any_sync(kFull, bad) && lane == 0 && p.status)
+    atomicOr(&p.status[si], kStatusNonFiniteScore);
+}
+
+// ---------------------------------------------------------------------------
 // Block-table writes, then copy-on-write block copies (all layers, K and V).
 // ---------------------------------------------------------------------------
 __global__ void apply_updates_kernel(const PoolGeom g, const TableUpdate* __restrict__ up,
@@ -1305,6 +1431,36 @@ cudaError_t launch_append(const AppendLaunch& p, cudaStream_t s) {
   const int64_t blocks = (rows + kAppendRows - 1) / kAppendRows;
   if (p.g.bf16) append_kernel<1><<<static_cast<unsigned>(blocks), 256, 0, s>>>(p);
   else append_kernel<0><<<static_cast<unsigned>(blocks), 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+size_t exact_attention_smem(int32_t max_ctx, int warps) {
+  return static_cast<size_t>(warps) * (D + ((max_ctx + 3) & ~3)) * sizeof(float);
+}
+
+cudaError_t launch_exact_attention(const PrefillLaunch& p0, cudaStream_t s) {
+  if (p0.n_seq <= 0 || p0.total_tokens <= 0) return cudaSuccess;
+  if (p0.g.bf16) return cudaErrorInvalidValue;
+  PrefillLaunch p = p0;
+  p.max_ctx = (p.max_ctx + 3) & ~3;  // keeps every warp's rows 16-byte aligned
+  const int64_t items = static_cast<int64_t>(p.total_tokens) * p.g.q_heads;
+  constexpr size_t kSmemLimit = 200 * 1024;
+  if (exact_attention_smem(p.max_ctx, 4) <= kSmemLimit) {
+    const size_t smem = exact_attention_smem(p.max_ctx, 4);
+    cudaError_t e = cudaFuncSetAttribute(exact_attention_kernel<4>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    exact_attention_kernel<4><<<static_cast<unsigned>((items + 3) / 4), 128, smem, s>>>(p);
+  } else {
+    const size_t smem = exact_attention_smem(p.max_ctx, 1);
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(exact_attention_kernel<1>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    exact_attention_kernel<1><<<static_cast<unsigned>(items), 32, smem, s>>>(p);
+  }
   return cudaGetLastError();
 }
 

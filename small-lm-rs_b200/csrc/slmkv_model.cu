@@ -35,6 +35,7 @@
 
 #include "slmkv.h"
 #include "slmkv_internal.h"
+#include "slmkv_libm.h"
 
 namespace slmkv {
 namespace {
@@ -162,9 +163,9 @@ __global__ void round_bf16_kernel(const float4* __restrict__ in, size_t n4, uint
 
 // situ_glu.rs:131-138
 __device__ __forceinline__ float situ_sigmoid(float v) {
-  if (v >= 0.f) return __fdiv_rn(1.f, 1.f + expf(-v));
-  const float e = expf(v);
-  return __fdiv_rn(e, 1.f + e);
+  if (v >= 0.f) return __fdiv_rn(1.f, __fadd_rn(1.f, libm::slm_expf(-v)));
+  const float e = libm::slm_expf(v);
+  return __fdiv_rn(e, __fadd_rn(1.f, e));
 }
 // situ_glu.rs:59-70 and :101-107: h = gate_act(gate) * up_act(up), as bf16
 // (the down projection's rounded operand). gu rows are [gate | up].
@@ -179,8 +180,8 @@ __global__ void situ_kernel(const float* __restrict__ gu, int32_t rows, int32_t 
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const float g = row[c + k], u = row[inter + c + k];
-      const float ga = __fmul_rn(__fmul_rn(beta_gate, tanhf(__fdiv_rn(g, beta_gate))), situ_sigmoid(g));
-      const float ua = __fmul_rn(beta_up, tanhf(__fdiv_rn(u, beta_up)));
+      const float ga = __fmul_rn(__fmul_rn(beta_gate, libm::slm_tanhf(__fdiv_rn(g, beta_gate))), situ_sigmoid(g));
+      const float ua = __fmul_rn(beta_up, libm::slm_tanhf(__fdiv_rn(u, beta_up)));
       out[k] = __fmul_rn(ga, ua);
     }
     h[r * (inter / 2) + c / 2] = pack_bf16x2(out[0], out[1]);
@@ -244,10 +245,10 @@ size_t proj_smem(int32_t K) {  // enough for either row blocking
 }
 
 __device__ __forceinline__ float situ_gate(float g, float beta_gate) {
-  return __fmul_rn(__fmul_rn(beta_gate, tanhf(__fdiv_rn(g, beta_gate))), situ_sigmoid(g));
+  return __fmul_rn(__fmul_rn(beta_gate, libm::slm_tanhf(__fdiv_rn(g, beta_gate))), situ_sigmoid(g));
 }
 __device__ __forceinline__ float situ_up(float u, float beta_up) {
-  return __fmul_rn(beta_up, tanhf(__fdiv_rn(u, beta_up)));
+  return __fmul_rn(beta_up, libm::slm_tanhf(__fdiv_rn(u, beta_up)));
 }
 __device__ __forceinline__ float round_bf16(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
@@ -552,6 +553,9 @@ struct slm_model {
   // projections; 0 when their shared memory does not fit this model
   int32_t exact_rows = 0;
   bool exact_fits = false;
+  // f32 pool: the exact-order steps also attend in the reference's order
+  // (slm_batch_attention_exact), so that their logits are the CPU path's
+  bool f32_pool = false;
   bool head_kernel_ok = false;  // rows up to 64 on head_kernel (hidden <= 4096)
   cublasHandle_t blas = nullptr;
   void* weights = nullptr;  // one device allocation for every tensor
@@ -693,10 +697,17 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
   auto launched = [&](cudaError_t e2) {
     if (le == cudaSuccess) le = e2;
   };
+  // The exact-order path on an f32 pool appends, then attends in the
+  // reference's operation order (every score, the softmax sum and every
+  // output fold as the CPU path computes them); otherwise the split-K decode
+  // kernel or the prefill kernels.
+  const bool exact_attention = fused && m->f32_pool;
   auto cache_step = [&](int32_t l) {
-    if (prefill) {
+    if (prefill || exact_attention) {
       slm_status r = slm_batch_append_layer(b, l, m->k, m->v, 1);
-      return r ? r : slm_batch_prefill_attention(b, l, m->q, 1, m->att);
+      if (r) return r;
+      return exact_attention ? slm_batch_attention_exact(b, l, m->q, 1, m->att)
+                             : slm_batch_prefill_attention(b, l, m->q, 1, m->att);
     }
     return slm_batch_decode_layer(b, l, m->q, m->k, m->v, m->att);
   };
@@ -915,6 +926,7 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
   }
   auto m = new slm_model();
   m->ctx = ctx;
+  m->f32_pool = c.kv_dtype == SLM_KV_F32;
   m->V = V;
   m->H = H;
   m->I = I;

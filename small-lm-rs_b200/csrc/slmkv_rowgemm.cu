@@ -34,6 +34,7 @@
 #include <cstdint>
 
 #include "slmkv_internal.h"
+#include "slmkv_libm.h"
 
 namespace slmkv {
 namespace {
@@ -133,9 +134,9 @@ __device__ __forceinline__ void rg_cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 __device__ __forceinline__ float rg_situ_sigmoid(float v) {  // situ_glu.rs:131-138
-  if (v >= 0.f) return __fdiv_rn(1.f, 1.f + expf(-v));
-  const float e = expf(v);
-  return __fdiv_rn(e, 1.f + e);
+  if (v >= 0.f) return __fdiv_rn(1.f, __fadd_rn(1.f, libm::slm_expf(-v)));
+  const float e = libm::slm_expf(v);
+  return __fdiv_rn(e, __fadd_rn(1.f, e));
 }
 
 template <int MODE, int RT>
@@ -303,8 +304,8 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
         for (int r = split; r < nr; r += splits) {
           const float gv = reduced(r, m), u = reduced(r, m + 64);
           const float ga =
-              __fmul_rn(__fmul_rn(p.beta_gate, tanhf(__fdiv_rn(gv, p.beta_gate))), rg_situ_sigmoid(gv));
-          const float ua = __fmul_rn(p.beta_up, tanhf(__fdiv_rn(u, p.beta_up)));
+              __fmul_rn(__fmul_rn(p.beta_gate, libm::slm_tanhf(__fdiv_rn(gv, p.beta_gate))), rg_situ_sigmoid(gv));
+          const float ua = __fmul_rn(p.beta_up, libm::slm_tanhf(__fdiv_rn(u, p.beta_up)));
           static_cast<__nv_bfloat16*>(p.h)[static_cast<size_t>(r0 + r) * p.I + col] =
               __float2bfloat16_rn(__fmul_rn(ga, ua));
         }

@@ -130,6 +130,7 @@ SIGNATURES = {
     "slm_batch_decode_layer": (C.c_int, [_vp, _i32, _vp, _vp, _vp, _vp]),
     "slm_batch_append_layer": (C.c_int, [_vp, _i32, _vp, _vp, _i32]),
     "slm_batch_prefill_attention": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
+    "slm_batch_attention_exact": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
     "slm_batch_end": (C.c_int, [_vp, _pi32]),
     "slm_batch_rollback": (C.c_int, [_vp]),
     "slm_batch_submit": (C.c_int, [_vp]),
@@ -563,6 +564,12 @@ class Batch:
     def prefill_attention(self, layer: int, query, out, rotate_query: bool = True) -> None:
         self.pool.check(lib().slm_batch_prefill_attention(self._h, int(layer), _ptr(query),
                                                           int(bool(rotate_query)), _ptr(out)))
+
+    def attention_exact(self, layer: int, query, out, rotate_query: bool = True) -> None:
+        """slm_batch_attention_exact: the batch's attention in the reference's
+        operation order (attention.rs:195-399, 677-759), bit for bit; f32 pools."""
+        self.pool.check(lib().slm_batch_attention_exact(self._h, int(layer), _ptr(query),
+                                                        int(bool(rotate_query)), _ptr(out)))
 
     def end(self, raise_on_error: bool = True) -> list[int]:
         if self._h is None:
