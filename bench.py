@@ -714,11 +714,12 @@ def oracle_generate_check(tensors, prompt, generated, threads):
                rms_norm_epsilon=1e-5, rope_theta=10000.0, situ_beta_gate=4.0, situ_beta_up=25.0)
     m = O.Model(cfg, tensors)
     cache = m.new_cache(CTX)
+    generated = [int(t) for t in generated]
     t0 = time.perf_counter()
     ok = O.argmax_finite(m.prefill(cache, [int(t) for t in prompt], threads)[-1]) == generated[0]
     for j in range(len(generated) - 1):
-        ok = ok and O.argmax_finite(m.decode(cache, int(generated[j]), threads)) == generated[j + 1]
-    return ok, time.perf_counter() - t0
+        ok = ok and O.argmax_finite(m.decode(cache, generated[j], threads)) == generated[j + 1]
+    return bool(ok), time.perf_counter() - t0
 
 
 def run_serve(args):

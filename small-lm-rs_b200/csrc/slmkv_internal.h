@@ -164,8 +164,7 @@ cudaError_t launch_prefill(const PrefillLaunch& p, cudaStream_t s);
 // Attention in the reference's operation order, bit for bit (f32 pools);
 // its shared memory per launch, and the longest row a launch can take.
 cudaError_t launch_exact_attention(const PrefillLaunch& p, cudaStream_t s);
-size_t exact_attention_smem(int32_t max_ctx, int warps);
-constexpr int32_t kExactMaxCtx = 56 * 1024;
+constexpr int32_t kExactMaxCtx = 48 * 1024;
 // bf16 pools on the tensor cores (tcgen05): slmkv_prefill_tc.cu.
 bool prefill_tc_supported(const PrefillLaunch& p);
 cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s);

@@ -49,6 +49,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                "r"(bytes)
                : "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 // Global -> shared bulk copy completing on `bar`; 16-byte aligned addresses,
 // size a multiple of 16 (every chunk here is 2 or 4 KiB at chunk offsets).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
@@ -1250,8 +1253,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillLaunch p) {
 
 // ---------------------------------------------------------------------------
 // Attention in the reference's operation order (f32 pools), bit for bit.
-// One warp per (token row, query head): the row's query at position qpos
-// attends positions 0..qpos of its sequence's cache, as
+// One CTA of 128 threads per (token row, query head): the row's query at
+// position qpos attends positions 0..qpos of its sequence's cache, as
 // scaled_causal_scores / causal_probabilities / attend_values do for a prompt
 // (attention.rs:195-399; masked positions hold f32::MIN, whose exp is 0 and
 // which add nothing) and attend_cached_query does for a decoded token
@@ -1260,46 +1263,100 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillLaunch p) {
 //   m = max_j score_j; p_j = exp(score_j - m) (glibc's expf, restated);
 //   sum = p_0 + p_1 + ... in order; p_j /= sum           (softmax.rs:26-44)
 //   out_d = fold_j fma(v_j,d, p_j, out_d) from 0           (attention.rs:751-756)
-// Scores and probabilities of the row live in this warp's shared memory;
-// the sum is one lane's sequential fold. A non-finite score or sum flags
-// the sequence (softmax.rs:17-22,35-40).
+// Every thread scores positions (tid, tid + 128, ...); the probabilities live
+// in shared memory; thread 0 folds the sum; threads 0-63 each fold one output
+// dimension. The value folds are one dependent fma per position, so their
+// rows must already be in shared memory: thread 64 starts bulk copies of the
+// first kExactStages 16-token V blocks when the CTA starts (they land while
+// the scores and the softmax run) and refills each stage once both folding
+// warps have read it. A non-finite score or sum flags the sequence
+// (softmax.rs:17-22,35-40). Every wait is bounded; on expiry the CTA records
+// the timeout, waits (bounded) for its own copies and returns.
 // ---------------------------------------------------------------------------
 constexpr float kScaleExact = 0.125f;  // (64 as f32).sqrt().recip(), exact
+constexpr int kExactThreads = 128;
+constexpr int kExactChunk = kBlockTokens * D * 4;  // one 16-token block of V, one head
 
-template <int WARPS>
-__global__ void __launch_bounds__(WARPS * 32) exact_attention_kernel(const PrefillLaunch p) {
-  extern __shared__ __align__(16) float sm_exact[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+struct ExactSmem {  // byte offsets in dynamic shared memory
+  int stages, ring, full, empty, q, red, ps, total;
+};
+__host__ __device__ inline ExactSmem exact_smem_layout(int max_ctx, int stages) {
+  ExactSmem l;
+  l.stages = stages;
+  l.ring = 0;                                  // stages x 4 KiB, 16-byte aligned
+  l.full = stages * kExactChunk;               // mbarriers
+  l.empty = l.full + 8 * stages;
+  l.q = l.empty + 8 * stages;                  // 64 floats
+  l.red = l.q + D * 4;                         // 8 floats + flags
+  l.ps = l.red + 64;                           // max_ctx floats
+  l.total = l.ps + ((max_ctx + 3) & ~3) * 4;
+  return l;
+}
+
+__global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const PrefillLaunch p,
+                                                                        int stages) {
+  extern __shared__ __align__(128) uint8_t sm_exact[];
+  const ExactSmem lay = exact_smem_layout(p.max_ctx, stages);
+  uint8_t* ring = sm_exact + lay.ring;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm_exact + lay.full);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(sm_exact + lay.empty);
+  float* qs = reinterpret_cast<float*>(sm_exact + lay.q);
+  float* red = reinterpret_cast<float*>(sm_exact + lay.red);
+  int* flags = reinterpret_cast<int*>(red + 8);  // [0] bad, [1] abort
+  float* ps = reinterpret_cast<float*>(sm_exact + lay.ps);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int Hq = p.g.q_heads, Hkv = p.g.kv_heads;
-  const int64_t item = static_cast<int64_t>(blockIdx.x) * WARPS + warp;
-  if (item >= static_cast<int64_t>(p.total_tokens) * Hq) return;  // no CTA barrier below
-  const int r = static_cast<int>(item / Hq), h = static_cast<int>(item - static_cast<int64_t>(r) * Hq);
-  const int si = warp_find_seq(p.seqs, p.n_seq, r, lane);
+  const int r = static_cast<int>(blockIdx.x / Hq), h = static_cast<int>(blockIdx.x % Hq);
+  int si = 0;
+  if (warp == 0) si = warp_find_seq(p.seqs, p.n_seq, r, lane);
+  if (tid == 0) {
+    for (int st = 0; st < stages; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 2);  // one arrival per folding warp
+    }
+    fence_mbar_init();
+    flags[0] = flags[1] = 0;
+    reinterpret_cast<int*>(red)[0] = si;
+  }
+  __syncthreads();
+  si = reinterpret_cast<const int*>(red)[0];
   const SeqEntry se = p.seqs[si];
   const int qpos = se.base + (r - se.row_offset);
   const int L = qpos + 1;
-  float* qs = sm_exact + static_cast<size_t>(warp) * (D + p.max_ctx);
-  float* ps = qs + D;
-  float2 x = reinterpret_cast<const float2*>(p.q + (static_cast<size_t>(r) * Hq + h) * D)[lane];
-  if (p.rotate) x = rope_pair(x, p.g.rope[static_cast<size_t>(qpos) * (D / 2) + lane]);
-  reinterpret_cast<float2*>(qs)[lane] = x;
-  __syncwarp();
+  const int nblk = (L + kBlockTokens - 1) / kBlockTokens;
   const int kvh = h / (Hq / Hkv);
   const size_t layer_off = static_cast<size_t>(p.layer) * p.g.layer_elems;
   const float* kb = static_cast<const float*>(p.g.k) + layer_off;
   const float* vb = static_cast<const float*>(p.g.v) + layer_off;
   const int32_t* bt = p.g.block_table + static_cast<size_t>(se.slot) * p.g.max_blocks_per_seq;
-  auto row_of = [&](const float* base, int j) {
-    const int32_t blk = checked_block(p.g, bt[j >> 4]);
-    return base + ((static_cast<size_t>(blk) * Hkv + kvh) * kBlockTokens + (j & 15)) * D;
+  auto chunk_of = [&](const float* base, int b) {
+    const int32_t blk = checked_block(p.g, bt[b]);
+    return base + (static_cast<size_t>(blk) * Hkv + kvh) * (kBlockTokens * D);
   };
+  // thread 64: the V ring's producer
+  int issued = 0;
+  if (tid == 64) {
+    for (; issued < min(stages, nblk); ++issued) {
+      mbar_arrive_expect_tx(&full[issued], kExactChunk);
+      bulk_load(ring + issued * kExactChunk, chunk_of(vb, issued), kExactChunk, &full[issued]);
+    }
+  }
+  if (warp == 0) {
+    float2 x = reinterpret_cast<const float2*>(p.q + (static_cast<size_t>(r) * Hq + h) * D)[lane];
+    if (p.rotate) x = rope_pair(x, p.g.rope[static_cast<size_t>(qpos) * (D / 2) + lane]);
+    reinterpret_cast<float2*>(qs)[lane] = x;
+  }
+  __syncthreads();
+  // ---- scores, two positions per thread at a time ----------------------------
   bool bad = false;
-  // scores: lane l takes positions l, l+32, ...; two rows at a time
-  for (int j0 = lane; j0 < L; j0 += 64) {
-    const int j1 = j0 + 32;
+  float mloc = -INFINITY;
+  for (int j0 = tid; j0 < L; j0 += 2 * kExactThreads) {
+    const int j1 = j0 + kExactThreads;
     const bool two = j1 < L;
-    const float4* k0 = reinterpret_cast<const float4*>(row_of(kb, j0));
-    const float4* k1 = reinterpret_cast<const float4*>(row_of(kb, two ? j1 : j0));
+    const float4* k0 =
+        reinterpret_cast<const float4*>(chunk_of(kb, j0 >> 4) + (j0 & 15) * D);
+    const float4* k1 = reinterpret_cast<const float4*>(
+        chunk_of(kb, (two ? j1 : j0) >> 4) + ((two ? j1 : j0) & 15) * D);
     float a0 = 0.f, a1 = 0.f;
 #pragma unroll
     for (int c = 0; c < D / 4; ++c) {
@@ -1317,60 +1374,78 @@ __global__ void __launch_bounds__(WARPS * 32) exact_attention_kernel(const Prefi
     const float s0 = __fmul_rn(a0, kScaleExact), s1 = __fmul_rn(a1, kScaleExact);
     bad |= !isfinite(s0);
     ps[j0] = s0;
+    mloc = fmaxf(mloc, s0);
     if (two) {
       bad |= !isfinite(s1);
       ps[j1] = s1;
+      mloc = fmaxf(mloc, s1);
     }
   }
-  __syncwarp();
-  float m = -INFINITY;
-  for (int j = lane; j < L; j += 32) m = fmaxf(m, ps[j]);
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
-  for (int j = lane; j < L; j += 32) ps[j] = libm::slm_expf(__fsub_rn(ps[j], m));
-  __syncwarp();
-  float sum = 0.f;
-  if (lane == 0) {
+  for (int off = 16; off > 0; off >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(kFull, mloc, off));
+  if (lane == 0) red[warp] = mloc;
+  __syncthreads();
+  const float m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  for (int j = tid; j < L; j += kExactThreads) ps[j] = libm::slm_expf(__fsub_rn(ps[j], m));
+  __syncthreads();
+  if (tid == 0) {
+    float sum = 0.f;
     int j = 0;
-    for (; j + 4 <= L; j += 4) {  // ps is 16-byte aligned (D floats in)
+    for (; j + 4 <= L; j += 4) {  // ps is 16-byte aligned
       const float4 v = *reinterpret_cast<const float4*>(ps + j);
       sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, v.x), v.y), v.z), v.w);
     }
     for (; j < L; ++j) sum = __fadd_rn(sum, ps[j]);
+    red[4] = sum;
   }
-  sum = __shfl_sync(kFull, sum, 0);
+  __syncthreads();
+  const float sum = red[4];
   bad |= !(isfinite(sum) && sum > 0.f);
-  for (int j = lane; j < L; j += 32) ps[j] = __fdiv_rn(ps[j], sum);
-  __syncwarp();
-  // values: lane owns dims 2l, 2l+1; one 16-token block of V rows in flight
-  // while the previous block's fma chain runs
-  float2 o = make_float2(0.f, 0.f);
-  float2 cur[kBlockTokens], nxt[kBlockTokens];
-  auto load_block = [&](float2 (&dst)[kBlockTokens], int j0) {
-    const float2* vr = reinterpret_cast<const float2*>(row_of(vb, j0));
-    const int n = min(kBlockTokens, L - j0);
-#pragma unroll
-    for (int t = 0; t < kBlockTokens; ++t)
-      dst[t] = (t < n) ? vr[t * (D / 2) + lane] : make_float2(0.f, 0.f);
-  };
-  load_block(cur, 0);
-  for (int j0 = 0; j0 < L; j0 += kBlockTokens) {
-    if (j0 + kBlockTokens < L) load_block(nxt, j0 + kBlockTokens);
-    const int n = min(kBlockTokens, L - j0);
-#pragma unroll
-    for (int t = 0; t < kBlockTokens; ++t) {
-      if (t < n) {
-        const float pj = ps[j0 + t];
-        o.x = fmaf(cur[t].x, pj, o.x);
-        o.y = fmaf(cur[t].y, pj, o.y);
+  for (int j = tid; j < L; j += kExactThreads) ps[j] = __fdiv_rn(ps[j], sum);
+  if (bad) flags[0] = 1;
+  __syncthreads();
+  // ---- values: threads 0-63 fold one dimension each; thread 64 refills -------
+  if (tid < D) {
+    float o = 0.f;
+    for (int b = 0; b < nblk; ++b) {
+      const int st = b % stages;
+      if (!mbar_wait_bounded(&full[st], static_cast<uint32_t>(b / stages) & 1u)) {
+        flags[1] = 1;
+        atomicOr(p.g.error, kErrTimeout);
+        break;
       }
-    }
+      if (flags[1]) break;
+      const float* vr = reinterpret_cast<const float*>(ring + st * kExactChunk) + tid;
+      const int n = min(kBlockTokens, L - b * kBlockTokens);
+      const float* pb = ps + b * kBlockTokens;
+      if (n == kBlockTokens) {
 #pragma unroll
-    for (int t = 0; t < kBlockTokens; ++t) cur[t] = nxt[t];
+        for (int t = 0; t < kBlockTokens; ++t) o = fmaf(vr[t * D], pb[t], o);
+      } else {
+        for (int t = 0; t < n; ++t) o = fmaf(vr[t * D], pb[t], o);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    p.out[(static_cast<size_t>(r) * Hq + h) * D + tid] = o;
+  } else if (tid == 64) {
+    for (; issued < nblk; ++issued) {
+      const int st = issued % stages;
+      if (flags[1] ||
+          !mbar_wait_bounded(&empty[st], static_cast<uint32_t>(issued / stages - 1) & 1u)) {
+        flags[1] = 1;
+        atomicOr(p.g.error, kErrTimeout);
+        break;
+      }
+      mbar_arrive_expect_tx(&full[st], kExactChunk);
+      bulk_load(ring + st * kExactChunk, chunk_of(vb, issued), kExactChunk, &full[st]);
+    }
+    // every copy issued lands before the CTA's shared memory is released
+    for (int b = max(0, issued - stages); b < issued; ++b)
+      mbar_wait_bounded(&full[b % stages], static_cast<uint32_t>(b / stages) & 1u);
   }
-  reinterpret_cast<float2*>(p.out + (static_cast<size_t>(r) * Hq + h) * D)[lane] = o;
-  if (__any_sync(kFull, bad) && lane == 0 && p.status)
-    atomicOr(&p.status[si], kStatusNonFiniteScore);
+  __syncthreads();
+  if (tid == 0 && flags[0] && p.status) atomicOr(&p.status[si], kStatusNonFiniteScore);
 }
 
 // ---------------------------------------------------------------------------
@@ -1434,33 +1509,25 @@ cudaError_t launch_append(const AppendLaunch& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-size_t exact_attention_smem(int32_t max_ctx, int warps) {
-  return static_cast<size_t>(warps) * (D + ((max_ctx + 3) & ~3)) * sizeof(float);
+int exact_attention_stages(int32_t max_ctx) {
+  for (int st = 16; st >= 2; --st)
+    if (exact_smem_layout(max_ctx, st).total <= 227 * 1024) return st;
+  return 0;
 }
 
 cudaError_t launch_exact_attention(const PrefillLaunch& p0, cudaStream_t s) {
   if (p0.n_seq <= 0 || p0.total_tokens <= 0) return cudaSuccess;
   if (p0.g.bf16) return cudaErrorInvalidValue;
   PrefillLaunch p = p0;
-  p.max_ctx = (p.max_ctx + 3) & ~3;  // keeps every warp's rows 16-byte aligned
+  p.max_ctx = (p.max_ctx + 3) & ~3;
+  const int stages = exact_attention_stages(p.max_ctx);
+  if (stages == 0) return cudaErrorInvalidValue;
+  const int smem = exact_smem_layout(p.max_ctx, stages).total;
+  cudaError_t e = cudaFuncSetAttribute(exact_attention_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
   const int64_t items = static_cast<int64_t>(p.total_tokens) * p.g.q_heads;
-  constexpr size_t kSmemLimit = 200 * 1024;
-  if (exact_attention_smem(p.max_ctx, 4) <= kSmemLimit) {
-    const size_t smem = exact_attention_smem(p.max_ctx, 4);
-    cudaError_t e = cudaFuncSetAttribute(exact_attention_kernel<4>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    exact_attention_kernel<4><<<static_cast<unsigned>((items + 3) / 4), 128, smem, s>>>(p);
-  } else {
-    const size_t smem = exact_attention_smem(p.max_ctx, 1);
-    if (smem > 227 * 1024) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(exact_attention_kernel<1>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    exact_attention_kernel<1><<<static_cast<unsigned>(items), 32, smem, s>>>(p);
-  }
+  exact_attention_kernel<<<static_cast<unsigned>(items), kExactThreads, smem, s>>>(p, stages);
   return cudaGetLastError();
 }
 
