@@ -150,6 +150,22 @@ def close_dist(world: int) -> None:
         dist.destroy_process_group()
 
 
+def pin_rank_cores(local: int, local_world: int) -> list[int]:
+    """Binds this rank's process to its own share of the host cores it may
+    use (rank r of n takes the r-th of n equal slices), so that the ranks'
+    host loops do not migrate across one another's cores. Returns them."""
+    try:
+        cores = sorted(os.sched_getaffinity(0))
+    except AttributeError:
+        return []
+    if local_world <= 1 or len(cores) < local_world:
+        return cores
+    k = len(cores) // local_world
+    mine = cores[local * k:(local + 1) * k]
+    os.sched_setaffinity(0, mine)
+    return mine
+
+
 def host_threads() -> int:
     """Host cores this process may run on (torchrun sets OMP_NUM_THREADS=1,
     so the oracle is always given this count explicitly)."""
@@ -263,19 +279,26 @@ def measured_peaks():
 
 
 def ncu_traffic_per_launch():
-    """dram bytes (read + write) per decode launch from the committed ncu
-    summary, if one has been captured for this workload."""
+    """(dram bytes read + written per decode launch, where they come from)
+    from the committed ncu summary of this workload's decode kernel: a figure
+    of one capture of the kernel version the summary names, not a counter of
+    this run. (None, None) without one."""
     name = "microbench" if WORKLOAD_NAME == "microbench" else "gqa_bf16"
     p = ROOT / "profiles" / f"decode_kernel_{name}.md"
     if not p.exists():
-        return None
+        return None, None
+    traffic, version = None, None
     for line in p.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
+        key, _, val = line.strip().partition(":")
+        if key == "traffic_bytes_per_launch":
             try:
-                return int(float(line.split(":", 1)[1].strip()))
+                traffic = int(float(val.strip()))
             except ValueError:
-                return None
-    return None
+                return None, None
+        elif key == "traffic_kernel_version":
+            version = val.strip()
+    src = f"profiles/{p.name}" + (f", kernel version {version}" if version else "")
+    return traffic, src
 
 
 class ClockSampler:
@@ -432,6 +455,7 @@ def run_ours(args):
     from slmkv.shard import max_over_ranks
 
     rank, world, local = dist_env()
+    pinned = pin_rank_cores(local, int(os.environ.get("LOCAL_WORLD_SIZE", str(world))))
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
     init_dist(world, dev, args.pg_timeout)
@@ -525,15 +549,22 @@ def run_ours(args):
             if any(st):
                 raise RuntimeError(f"decode step failed: {st}")
 
+    host_s = [0.0, 0.0]  # seconds in begin..submit, and waiting in collect
+
     def step(timed_index=None, layer_ptrs=ptrs):
+        t0 = time.perf_counter()
         batch = plan.begin()
         for layer in range(LAYERS):
             batch.decode_layer_ptr(layer, *layer_ptrs[layer])
             if timed_index is not None and layer in (0, LAYERS - 1):
                 ev[timed_index][0 if layer == 0 else 1].record(stream)
         inflight.append(batch.submit())
+        t1 = time.perf_counter()
         collect(1)
         plan.truncate_all(base_arr)
+        if timed_index is not None:
+            host_s[0] += t1 - t0
+            host_s[1] += time.perf_counter() - t1
 
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
@@ -558,6 +589,14 @@ def run_ours(args):
     ms = t_start.elapsed_time(t_stop)
     kern_ms = [a.elapsed_time(b) / (LAYERS - 1) for a, b in ev]
     kern_avg_ms = sum(kern_ms) / len(kern_ms)
+    # every rank's own step time and host time per step, for the line
+    mine = torch.tensor([ms / args.steps, kern_avg_ms, host_s[0] / args.steps * 1e3,
+                         host_s[1] / args.steps * 1e3], dtype=torch.float64, device=dev)
+    per_rank = [mine]
+    if world > 1:
+        per_rank = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(per_rank, mine)
+    per_rank = [[round(float(x), 4) for x in t.tolist()] for t in per_rank]
     ms, kern_avg_ms = max_over_ranks([ms, kern_avg_ms], device=dev)
 
     # End to end through the public API with host buffers: every step copies
@@ -637,7 +676,7 @@ def run_ours(args):
     peaks, peak_kind = measured_peaks()
     alg = algorithmic_bytes(lengths)
     achieved = alg / (kern_avg_ms / 1e3) / 1e9
-    traffic = ncu_traffic_per_launch()
+    traffic, traffic_src = ncu_traffic_per_launch()
     result = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -651,7 +690,7 @@ def run_ours(args):
         "kv_attn_hbm_frac": achieved / peaks["hbm_gbs"],
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                     "traffic": traffic, "peak_source": peak_kind,
+                     "traffic": traffic, "traffic_source": traffic_src, "peak_source": peak_kind,
                      "kernel": "decode_kernel (fused RoPE + paged append + split-K GQA attention)",
                      "algorithmic_bytes_per_launch": alg, "avg_launch_ms": kern_avg_ms},
         "e2e": {"value": e2e_value, "unit": "tok/s",
@@ -675,6 +714,9 @@ def run_ours(args):
         "gpu_launches": launches,
         "kernel_timing": ("CUDA events at the completion of layer 0's and layer 7's decode "
                           "kernel in every timed step; interval / 7"),
+        "per_rank": {"fields": ["ms_per_step", "decode_kernel_ms", "host_submit_ms_per_step",
+                                "host_wait_ms_per_step"], "values": per_rank,
+                     "host_cores_per_rank": len(pinned)},
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

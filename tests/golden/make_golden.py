@@ -230,13 +230,14 @@ def numpy_reference_vectors(ref_root: Path) -> dict:
 
 
 def main() -> None:
-    ref_root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <small-lm-rs checkout>")
+    ref_root = Path(sys.argv[1])
+    if not (ref_root / "src" / "smalllm" / "reference.py").exists():
+        sys.exit(f"{ref_root}: not a small-lm-rs checkout (src/smalllm/reference.py missing)")
     (HERE / "known_answers.json").write_text(json.dumps(known_answers(), indent=1) + "\n")
-    if (ref_root / "src" / "smalllm" / "reference.py").exists():
-        vec = numpy_reference_vectors(ref_root)
-        (HERE / "numpy_reference_vectors.json").write_text(json.dumps(vec) + "\n")
-    else:
-        print("reference checkout not found; numpy vectors left unchanged")
+    vec = numpy_reference_vectors(ref_root)
+    (HERE / "numpy_reference_vectors.json").write_text(json.dumps(vec) + "\n")
 
 
 if __name__ == "__main__":
