@@ -618,16 +618,23 @@ def run_ours(args):
     computed = [torch.cuda.Event() for _ in range(2)]
     read_back = [torch.cuda.Event() for _ in range(2)]
     e2e_i = [0]
+    # copy timing: events at the start and end of every step's H2D and D2H
+    # copies, on their own streams (averaged over the timed steps)
+    cev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)]
+           for _ in range(args.steps + 3)]
 
     def e2e_step():
         j = e2e_i[0] % 2
+        ce = cev[e2e_i[0]]
         e2e_i[0] += 1
         bq, bk, bv, bo = dbuf[j]
         with torch.cuda.stream(h2d):
             h2d.wait_event(computed[j])  # the step that last read these inputs
+            ce[0].record(h2d)
             bq.copy_(hq_, non_blocking=True)
             bk.copy_(hk_, non_blocking=True)
             bv.copy_(hv_, non_blocking=True)
+            ce[1].record(h2d)
             in_ready[j].record(h2d)
         stream.wait_event(in_ready[j])
         stream.wait_event(read_back[j])  # the outputs last written here were read
@@ -637,7 +644,9 @@ def run_ours(args):
         computed[j].record(stream)
         with torch.cuda.stream(d2h):
             d2h.wait_event(computed[j])
+            ce[2].record(d2h)
             ho_[j].copy_(bo, non_blocking=True)
+            ce[3].record(d2h)
             read_back[j].record(d2h)
         inflight.append(batch.submit())
         collect(1)
@@ -659,6 +668,9 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
+    timed = cev[3:3 + args.steps]
+    h2d_ms = sum(c[0].elapsed_time(c[1]) for c in timed) / len(timed)
+    d2h_ms = sum(c[2].elapsed_time(c[3]) for c in timed) / len(timed)
     (e2e_ms,) = max_over_ranks([e2e_ms], device=dev)
     ref_out = out.cpu()
     if not all(torch.equal(h, ref_out) for h in ho_):
@@ -696,7 +708,11 @@ def run_ours(args):
         "e2e": {"value": e2e_value, "unit": "tok/s",
                 "h2d_bytes_per_step": int(q.numel() + kn.numel() + vn.numel()) * 4,
                 "copies": "own H2D and D2H streams, double-buffered, overlapping compute",
-                "d2h_bytes_per_step": int(out.numel()) * 4},
+                "d2h_bytes_per_step": int(out.numel()) * 4,
+                "ms_per_step": e2e_ms / args.steps,
+                "h2d_copy_ms_per_step": h2d_ms, "d2h_copy_ms_per_step": d2h_ms,
+                "h2d_gbs": (q.numel() + kn.numel() + vn.numel()) * 4 / (h2d_ms / 1e3) / 1e9,
+                "d2h_gbs": out.numel() * 4 / (d2h_ms / 1e3) / 1e9},
         "append_kernel": {"achieved": append_bytes / (append_ms / 1e3) / 1e9, "unit": "GB/s",
                           "frac": append_bytes / (append_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
                           "avg_launch_ms": append_ms, "bytes_per_launch": append_bytes,
