@@ -203,7 +203,7 @@ slm_status slm_batch_rollback(slm_batch* batch);
  * at a time, worker.rs:87-98). slm_batch_submit closes the step without
  * waiting for the GPU: the per-sequence status is copied back on the batch's
  * stream and the next step may begin at once, planned on the advanced
- * lengths. At most 2 submitted batches may be pending. slm_batch_wait waits
+ * lengths. At most 8 submitted batches may be pending. slm_batch_wait waits
  * for a submitted batch and reports like slm_batch_end; batches resolve in
  * submission order (waiting for a later one resolves the earlier ones, whose
  * own wait then returns at once), and every submitted batch must be waited

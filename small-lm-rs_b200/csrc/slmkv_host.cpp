@@ -29,10 +29,13 @@ using namespace slmkv;
 
 namespace {
 
-constexpr int kUploadSlots = 2;
-// Batches that may be submitted and not yet resolved at once, and readback
+// Batches that may be submitted and not yet resolved at once (the host may
+// plan and queue that many steps ahead of the GPU, so that a stall of the
+// host thread of up to that many steps leaves the GPU busy), and readback
 // slots (one more, for slm_batch_end while that many are in flight).
-constexpr int kMaxInFlight = 2;
+constexpr int kMaxInFlight = 8;
+// Descriptor slots: every submitted batch and the open one hold their own.
+constexpr int kUploadSlots = kMaxInFlight + 1;
 constexpr int kReadbackSlots = kMaxInFlight + 1;
 
 struct Seq {
@@ -52,18 +55,17 @@ struct BlockMeta {
   std::array<uint32_t, kBlockTokens> tokens{};
 };
 
-// Pinned staging (ring of two) feeding one device region.
-// Pinned staging (ring of two) feeding device memory. A single device region
+// Pinned staging (a ring of kUploadSlots) feeding device memory. A single device region
 // is written on the caller's stream; a dual one (the batch descriptors) has a
 // device buffer per slot, written on the context's copy stream while the
 // previous step's kernels run, once the kernels that last read that buffer
 // are done (`consumed`), with the caller's stream waiting for the copy.
 struct Upload {
-  uint8_t* h[kUploadSlots] = {nullptr, nullptr};
-  cudaEvent_t ev[kUploadSlots] = {nullptr, nullptr};        // copy of slot k done
-  cudaEvent_t consumed[kUploadSlots] = {nullptr, nullptr};  // kernels reading slot k done
-  uint8_t* d = nullptr;                                     // single
-  uint8_t* dd[kUploadSlots] = {nullptr, nullptr};           // dual
+  uint8_t* h[kUploadSlots] = {};
+  cudaEvent_t ev[kUploadSlots] = {};        // copy of slot k done
+  cudaEvent_t consumed[kUploadSlots] = {};  // kernels reading slot k done
+  uint8_t* d = nullptr;                     // single
+  uint8_t* dd[kUploadSlots] = {};           // dual
   bool dual = false;
   size_t cap = 0;
   int next = 0, last = 0;

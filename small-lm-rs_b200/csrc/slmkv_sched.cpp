@@ -58,13 +58,15 @@ int32_t held_blocks(const slm_sched* s) {
 }
 
 // Frees the newest running request's sequence and puts it back at the front
-// of the queue, to prefill what it had cached again.
+// of the queue, to prefill what it had cached again: its prompt and the
+// tokens it generated (a request preempted inside its prompt keeps the
+// whole prompt as its target).
 void preempt_newest(slm_sched* s) {
   std::unique_ptr<Request> r = std::move(s->running.back());
   s->running.pop_back();
   slm_seq_free(s->ctx, r->seq);
   r->seq = -1;
-  r->target = r->cached;
+  r->target = std::max(r->target, r->cached);
   r->cached = 0;
   r->first_from_prefill = (r->generated == 0);
   s->waiting.push_front(std::move(r));

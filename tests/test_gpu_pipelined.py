@@ -142,22 +142,23 @@ def test_in_flight_limit_and_sync_end_alongside():
     layers, hq, hkv = 1, 4, 2
     lengths = [5, 40]
     n = len(lengths)
-    pool = _pool(layers, hq, hkv, n, lengths, 4)
+    in_flight = 8  # the library's limit on submitted, unresolved batches
+    pool = _pool(layers, hq, hkv, n, lengths, in_flight + 2)
     inv = O.rope_inverse_frequencies(D, 10000.0)
     caches = [pool.allocate_kv_cache(128) for _ in range(n)]
     ocs = [O.DenseCache(layers, 128, hkv, D) for _ in range(n)]
     fill_history(caches, ocs, lengths, layers, rng, inv, hkv, D)
     subs = []
-    for _ in range(2):
+    for _ in range(in_flight):
         b = pool.begin(caches, 1)
         _launch(b, _step_inputs(rng, n, layers, hq, hkv), n, hq)
         subs.append(b.submit())
-    b3 = pool.begin(caches, 1)
-    _launch(b3, _step_inputs(rng, n, layers, hq, hkv), n, hq)
+    b_extra = pool.begin(caches, 1)
+    _launch(b_extra, _step_inputs(rng, n, layers, hq, hkv), n, hq)
     with pytest.raises(slmkv.InvalidInput) as e:
-        b3.submit()
-    assert "at most 2" in str(e.value)
+        b_extra.submit()
+    assert f"at most {in_flight}" in str(e.value)
     # the refused step stays open; a synchronous end still has a readback slot
-    assert b3.end() == [0, 0]
-    assert [b.wait() for b in subs] == [[0, 0], [0, 0]]
-    assert [c.sequence_length() for c in caches] == [L + 3 for L in lengths]
+    assert b_extra.end() == [0, 0]
+    assert [b.wait() for b in subs] == [[0, 0]] * in_flight
+    assert [c.sequence_length() for c in caches] == [L + in_flight + 1 for L in lengths]

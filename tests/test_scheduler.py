@@ -143,3 +143,48 @@ def test_plan_requests_report_ids_and_positions():
     dreq, dpos, preq, ppos = s.plan_request_arrays()  # the same as numpy views
     assert dreq.tolist() == [10, 11] and dpos.tolist() == [20, 5]
     assert preq.tolist() == [] and ppos.tolist() == []
+
+
+def test_a_request_preempted_inside_its_prompt_prefills_the_whole_prompt_again():
+    # A small prompt budget spreads prompts over several steps and a small
+    # pool preempts requests inside their prompts. Replaying the plans'
+    # positions: no request decodes before its whole prompt is cached (a
+    # decode entry feeds position >= prompt length), a prefill entry always
+    # starts where the request's cache ends, and the first token comes only
+    # from the prompt's last position.
+    rng = random.Random(11)
+    pool = _pool(num_blocks=12, seqs=8, ctx=128)
+    s = slmkv.Scheduler(pool, max_running=6, max_prefill_tokens=24)
+    prompts, outs = {}, {}
+    for rid in range(12):
+        prompts[rid], outs[rid] = rng.randint(20, 60), rng.randint(4, 20)
+        s.submit(rid, prompts[rid], outs[rid])
+    cached = {rid: 0 for rid in prompts}
+    generated = {rid: 0 for rid in prompts}
+    mid_prompt_preemptions = 0
+    for _ in range(5000):
+        nd, np_ = s.plan()
+        if nd == 0 and np_ == 0:
+            break
+        dreq, dpos, preq, ppos = s.plan_request_arrays()
+        counts = [c for _, c in s.prefill_seqs()]
+        for r, p in zip(dreq, dpos):
+            r, p = int(r), int(p)
+            assert p >= prompts[r], (r, p, prompts[r])
+        for r, p, c in zip(preq, ppos, counts):
+            r, p = int(r), int(p)
+            if p == 0 and cached[r] > 0:  # recomputation after a preemption
+                if cached[r] < prompts[r]:
+                    mid_prompt_preemptions += 1
+                cached[r] = 0
+            assert p == cached[r], (r, p, cached[r])
+            cached[r] += c
+            if cached[r] == prompts[r] and generated[r] == 0:
+                generated[r] = 1
+        for r, p in zip(dreq, dpos):
+            cached[int(r)] += 1
+            generated[int(r)] += 1
+        s.commit([0] * nd, [0] * np_)
+    assert s.counts()["waiting"] == 0 and s.counts()["running"] == 0
+    assert s.counts()["generated_tokens"] == sum(outs.values())
+    assert mid_prompt_preemptions > 0
