@@ -189,6 +189,14 @@ slm_status slm_batch_prefill_attention(slm_batch* batch, int32_t layer, const fl
  * slm_batch_prefill_attention. */
 slm_status slm_batch_attention_exact(slm_batch* batch, int32_t layer, const float* d_query,
                                      int32_t rotate_query, float* d_out);
+/* slm_batch_decode_layer in the reference's operation order, bit for bit
+ * (f32 pools): forward_cached_token's cache part (attention.rs:794-810) --
+ * RoPE on Q and K at the pre-append position, the append (a non-finite K/V
+ * fails the sequence, kv_cache.rs:192-197), then attend_cached_query
+ * (attention.rs:677-759) as slm_batch_attention_exact computes it -- in one
+ * kernel per layer. Same arguments as slm_batch_decode_layer. */
+slm_status slm_batch_decode_layer_exact(slm_batch* batch, int32_t layer, const float* d_query,
+                                        const float* d_keys, const float* d_values, float* d_out);
 /* Closes the step: waits for its stream, and reports per sequence (h_status
  * may be NULL) 0 or SLM_ERR_NON_FINITE. A sequence whose appends were not
  * finite, whose attention met a score that is not finite (softmax.rs:17-22,

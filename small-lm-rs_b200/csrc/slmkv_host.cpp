@@ -1447,6 +1447,58 @@ slm_status slm_batch_prefill_attention(slm_batch* b, int32_t layer, const float*
   return SLM_OK;
 }
 
+slm_status slm_batch_decode_layer_exact(slm_batch* b, int32_t layer, const float* d_query,
+                                        const float* d_keys, const float* d_values, float* d_out) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_ctx* ctx = b->ctx;
+  slm_status rc = batch_layer_check(b, layer);
+  if (rc) return rc;
+  if (b->max_count != 1)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
+                       "decode layers need exactly one new token per sequence");
+  if (b->layer_done[layer])
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "layer %d was already appended", layer);
+  if (ctx->cfg.kv_dtype != SLM_KV_F32)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention",
+                       "exact-order attention needs an f32 pool");
+  if (!d_query || !d_keys || !d_values || !d_out)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch", "null tensor");
+  if (!aligned16(d_query) || !aligned16(d_keys) || !aligned16(d_values) || !aligned16(d_out))
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
+                       "query, key, value and output buffers must be 16-byte aligned");
+  int32_t max_ctx = 0;
+  for (size_t i = 0; i < b->seq_ids.size(); ++i)
+    max_ctx = std::max(max_ctx, b->base[i] + b->counts[i]);
+  if (max_ctx > kExactMaxCtx)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "cached attention",
+                       "exact-order attention takes at most %d positions, the batch reaches %d",
+                       kExactMaxCtx, max_ctx);
+  rc = flush_excess(ctx, b->stream, 0, 0);  // the kernel reads the device block table
+  if (rc) return rc;
+  PrefillLaunch p{};
+  p.g = ctx->geom();
+  p.layer = layer;
+  p.seqs = b->dev.seqs;
+  p.n_seq = static_cast<int32_t>(b->seq_ids.size());
+  p.total_tokens = b->total_tokens;
+  p.q = d_query;
+  p.rotate = 1;
+  p.out = d_out;
+  p.max_count = 1;
+  p.status = b->dev.status;
+  p.max_ctx = max_ctx;
+  p.k_new = d_keys;
+  p.v_new = d_values;
+  p.fused = 1;
+  ctx->prev_decode_layer = -1;
+  CU(ctx, launch_exact_attention(p, b->stream));
+  ++ctx->launches;
+  b->layer_done[layer] = 1;
+  for (size_t i = 0; i < b->seq_ids.size(); ++i)
+    ctx->seqs[b->seq_ids[i]].layer_len[layer] = b->base[i] + b->counts[i];
+  return SLM_OK;
+}
+
 slm_status slm_batch_attention_exact(slm_batch* b, int32_t layer, const float* d_query,
                                      int32_t rotate_query, float* d_out) {
   if (!b) return SLM_ERR_INVALID_INPUT;

@@ -158,6 +158,11 @@ struct PrefillLaunch {
   int32_t max_count;  // largest per-sequence token count
   int32_t* status;    // [n_seq]: kStatusNonFiniteScore when a score is not finite
   int32_t max_ctx;    // exact-order attention: the longest row (positions attended)
+  // exact-order decode (token counts 1): the new K (unrotated) and V rows
+  // [n, kv_heads, d], appended by the attention kernel itself
+  const float* k_new;
+  const float* v_new;
+  int32_t fused;
   CUtensorMap tmap_k, tmap_v;  // bf16 pools: the decode kernel's pool maps
 };
 cudaError_t launch_prefill(const PrefillLaunch& p, cudaStream_t s);

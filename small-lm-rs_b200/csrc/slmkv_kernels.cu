@@ -1258,7 +1258,13 @@ __global__ void __launch_bounds__(128) prefill_kernel(const PrefillLaunch p) {
 // scaled_causal_scores / causal_probabilities / attend_values do for a prompt
 // (attention.rs:195-399; masked positions hold f32::MIN, whose exp is 0 and
 // which add nothing) and attend_cached_query does for a decoded token
-// (attention.rs:677-759):
+// (attention.rs:677-759). In the fused decode form (every token count 1,
+// p.fused) the kernel also does forward_cached_token's append
+// (attention.rs:794-810): the new K row rotated at position qpos and the new
+// V row come from k_new / v_new, the first query head of each KV group
+// stores them into the pool (zeros and kStatusNonFinite when not finite,
+// kv_cache.rs:192-197), and every head reads the new row from its inputs,
+// never from the pool (another CTA may be writing it):
 //   score_j = fold_i fma(q_i, k_j,i) from 0, times (d as f32).sqrt().recip()
 //   m = max_j score_j; p_j = exp(score_j - m) (glibc's expf, restated);
 //   sum = p_0 + p_1 + ... in order; p_j /= sum           (softmax.rs:26-44)
@@ -1278,7 +1284,7 @@ constexpr int kExactThreads = 128;
 constexpr int kExactChunk = kBlockTokens * D * 4;  // one 16-token block of V, one head
 
 struct ExactSmem {  // byte offsets in dynamic shared memory
-  int stages, ring, full, empty, q, red, ps, total;
+  int stages, ring, full, empty, q, kn, vn, red, ps, total;
 };
 __host__ __device__ inline ExactSmem exact_smem_layout(int max_ctx, int stages) {
   ExactSmem l;
@@ -1287,7 +1293,9 @@ __host__ __device__ inline ExactSmem exact_smem_layout(int max_ctx, int stages) 
   l.full = stages * kExactChunk;               // mbarriers
   l.empty = l.full + 8 * stages;
   l.q = l.empty + 8 * stages;                  // 64 floats
-  l.red = l.q + D * 4;                         // 8 floats + flags
+  l.kn = l.q + D * 4;                          // the new K row (rotated), fused decode
+  l.vn = l.kn + D * 4;                         // the new V row
+  l.red = l.vn + D * 4;                        // 8 floats + flags
   l.ps = l.red + 64;                           // max_ctx floats
   l.total = l.ps + ((max_ctx + 3) & ~3) * 4;
   return l;
@@ -1301,6 +1309,8 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
   uint64_t* full = reinterpret_cast<uint64_t*>(sm_exact + lay.full);
   uint64_t* empty = reinterpret_cast<uint64_t*>(sm_exact + lay.empty);
   float* qs = reinterpret_cast<float*>(sm_exact + lay.q);
+  float* kns = reinterpret_cast<float*>(sm_exact + lay.kn);
+  float* vns = reinterpret_cast<float*>(sm_exact + lay.vn);
   float* red = reinterpret_cast<float*>(sm_exact + lay.red);
   int* flags = reinterpret_cast<int*>(red + 8);  // [0] bad, [1] abort
   float* ps = reinterpret_cast<float*>(sm_exact + lay.ps);
@@ -1333,18 +1343,49 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
     const int32_t blk = checked_block(p.g, bt[b]);
     return base + (static_cast<size_t>(blk) * Hkv + kvh) * (kBlockTokens * D);
   };
-  // thread 64: the V ring's producer
+  // Fused decode: the new row is the last block's row n_last - 1; a block
+  // holding nothing but the new row is not staged at all.
+  const int n_last = L - (nblk - 1) * kBlockTokens;
+  const int nload = (p.fused && n_last == 1) ? nblk - 1 : nblk;
+  // thread 64: the V ring's producer. In the fused decode form the staged
+  // rows are older than this step (and the previous kernel of the stream
+  // writes none of the pool), so the first copies go out before the wait.
   int issued = 0;
-  if (tid == 64) {
-    for (; issued < min(stages, nblk); ++issued) {
+  auto first_copies = [&]() {
+    for (; issued < min(stages, nload); ++issued) {
       mbar_arrive_expect_tx(&full[issued], kExactChunk);
       bulk_load(ring + issued * kExactChunk, chunk_of(vb, issued), kExactChunk, &full[issued]);
     }
-  }
+  };
+  if (tid == 64 && p.fused) first_copies();
+  // Launched with programmatic stream serialization in the fused form: the
+  // inputs (q, new K/V) are the previous kernel's outputs.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (tid == 64 && !p.fused) first_copies();
   if (warp == 0) {
     float2 x = reinterpret_cast<const float2*>(p.q + (static_cast<size_t>(r) * Hq + h) * D)[lane];
     if (p.rotate) x = rope_pair(x, p.g.rope[static_cast<size_t>(qpos) * (D / 2) + lane]);
     reinterpret_cast<float2*>(qs)[lane] = x;
+  } else if (warp == 1 && p.fused) {
+    // forward_cached_token's append (attention.rs:794-810, kv_cache.rs:182-230)
+    const size_t row = (static_cast<size_t>(r) * Hkv + kvh) * D;
+    const float2 kx = reinterpret_cast<const float2*>(p.k_new + row)[lane];
+    const float2 vx = reinterpret_cast<const float2*>(p.v_new + row)[lane];
+    const float2 kr = rope_pair(kx, p.g.rope[static_cast<size_t>(qpos) * (D / 2) + lane]);
+    const bool fin = finite2(kx) && finite2(vx);
+    reinterpret_cast<float2*>(kns)[lane] = kr;
+    reinterpret_cast<float2*>(vns)[lane] = vx;
+    if (h % (Hq / Hkv) == 0) {  // one writer per KV head
+      const int32_t blk = checked_block(p.g, bt[qpos >> 4]);
+      const size_t dst = layer_off + ((static_cast<size_t>(blk) * Hkv + kvh) * kBlockTokens +
+                                      (qpos & 15)) * D;
+      const float2 z = make_float2(0.f, 0.f);
+      reinterpret_cast<float2*>(static_cast<float*>(p.g.k) + dst)[lane] = fin ? kr : z;
+      reinterpret_cast<float2*>(static_cast<float*>(p.g.v) + dst)[lane] = fin ? vx : z;
+      if (!__all_sync(kFull, fin) && lane == 0 && p.status)
+        atomicOr(&p.status[si], kStatusNonFinite);
+    }
   }
   __syncthreads();
   // ---- scores, two positions per thread at a time ----------------------------
@@ -1353,10 +1394,13 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
   for (int j0 = tid; j0 < L; j0 += 2 * kExactThreads) {
     const int j1 = j0 + kExactThreads;
     const bool two = j1 < L;
-    const float4* k0 =
-        reinterpret_cast<const float4*>(chunk_of(kb, j0 >> 4) + (j0 & 15) * D);
-    const float4* k1 = reinterpret_cast<const float4*>(
-        chunk_of(kb, (two ? j1 : j0) >> 4) + ((two ? j1 : j0) & 15) * D);
+    const int jj1 = two ? j1 : j0;
+    const float4* k0 = (p.fused && j0 == qpos)
+                           ? reinterpret_cast<const float4*>(kns)
+                           : reinterpret_cast<const float4*>(chunk_of(kb, j0 >> 4) + (j0 & 15) * D);
+    const float4* k1 = (p.fused && jj1 == qpos)
+                           ? reinterpret_cast<const float4*>(kns)
+                           : reinterpret_cast<const float4*>(chunk_of(kb, jj1 >> 4) + (jj1 & 15) * D);
     float a0 = 0.f, a1 = 0.f;
 #pragma unroll
     for (int c = 0; c < D / 4; ++c) {
@@ -1407,7 +1451,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
   // ---- values: threads 0-63 fold one dimension each; thread 64 refills -------
   if (tid < D) {
     float o = 0.f;
-    for (int b = 0; b < nblk; ++b) {
+    for (int b = 0; b < nload; ++b) {
       const int st = b % stages;
       if (!mbar_wait_bounded(&full[st], static_cast<uint32_t>(b / stages) & 1u)) {
         flags[1] = 1;
@@ -1416,7 +1460,8 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
       }
       if (flags[1]) break;
       const float* vr = reinterpret_cast<const float*>(ring + st * kExactChunk) + tid;
-      const int n = min(kBlockTokens, L - b * kBlockTokens);
+      // the fused form's new row comes from its input, not from the pool
+      const int n = min(kBlockTokens, L - b * kBlockTokens) - ((p.fused && b == nblk - 1) ? 1 : 0);
       const float* pb = ps + b * kBlockTokens;
       if (n == kBlockTokens) {
 #pragma unroll
@@ -1427,9 +1472,10 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
+    if (p.fused && !flags[1]) o = fmaf(vns[tid], ps[qpos], o);
     p.out[(static_cast<size_t>(r) * Hq + h) * D + tid] = o;
   } else if (tid == 64) {
-    for (; issued < nblk; ++issued) {
+    for (; issued < nload; ++issued) {
       const int st = issued % stages;
       if (flags[1] ||
           !mbar_wait_bounded(&empty[st], static_cast<uint32_t>(issued / stages - 1) & 1u)) {
@@ -1527,8 +1573,17 @@ cudaError_t launch_exact_attention(const PrefillLaunch& p0, cudaStream_t s) {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   const int64_t items = static_cast<int64_t>(p.total_tokens) * p.g.q_heads;
-  exact_attention_kernel<<<static_cast<unsigned>(items), kExactThreads, smem, s>>>(p, stages);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(items));
+  cfg.blockDim = dim3(kExactThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.fused ? 1 : 0;  // the fused decode chains onto the q/k/v kernel
+  return cudaLaunchKernelEx(&cfg, exact_attention_kernel, p, stages);
 }
 
 cudaError_t launch_gather(const GatherLaunch& p, cudaStream_t s) {

@@ -703,13 +703,14 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
   // kernel or the prefill kernels.
   const bool exact_attention = fused && m->f32_pool;
   auto cache_step = [&](int32_t l) {
-    if (prefill || exact_attention) {
+    if (prefill) {
       slm_status r = slm_batch_append_layer(b, l, m->k, m->v, 1);
       if (r) return r;
       return exact_attention ? slm_batch_attention_exact(b, l, m->q, 1, m->att)
                              : slm_batch_prefill_attention(b, l, m->q, 1, m->att);
     }
-    return slm_batch_decode_layer(b, l, m->q, m->k, m->v, m->att);
+    return exact_attention ? slm_batch_decode_layer_exact(b, l, m->q, m->k, m->v, m->att)
+                           : slm_batch_decode_layer(b, l, m->q, m->k, m->v, m->att);
   };
   for (int32_t l = 0; l < m->L; ++l) {
     const slm_model::Layer& Ly = m->layers[l];

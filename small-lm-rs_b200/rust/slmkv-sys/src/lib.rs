@@ -106,6 +106,7 @@ extern "C" {
     pub fn slm_batch_append_layer(batch: *mut SlmBatch, layer: i32, d_keys: *const f32, d_values: *const f32, rotate_keys: i32) -> i32;
     pub fn slm_batch_prefill_attention(batch: *mut SlmBatch, layer: i32, d_query: *const f32, rotate_query: i32, d_out: *mut f32) -> i32;
     pub fn slm_batch_attention_exact(batch: *mut SlmBatch, layer: i32, d_query: *const f32, rotate_query: i32, d_out: *mut f32) -> i32;
+    pub fn slm_batch_decode_layer_exact(batch: *mut SlmBatch, layer: i32, d_query: *const f32, d_keys: *const f32, d_values: *const f32, d_out: *mut f32) -> i32;
     pub fn slm_batch_end(batch: *mut SlmBatch, h_status: *mut i32) -> i32;
     pub fn slm_batch_rollback(batch: *mut SlmBatch) -> i32;
     pub fn slm_batch_submit(batch: *mut SlmBatch) -> i32;

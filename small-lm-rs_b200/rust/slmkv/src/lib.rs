@@ -410,6 +410,16 @@ impl<'c> Batch<'c> {
               unsafe { sys::slm_batch_decode_layer(b, layer, q.c(), k.c(), v.c(), out.m()) })
     }
 
+    /// `decode_layer` in the reference's operation order, bit for bit with
+    /// its CPU path (f32 pools).
+    pub fn decode_layer_exact(&mut self, layer: i32, q: DevicePtr<f32>, k: DevicePtr<f32>,
+                              v: DevicePtr<f32>, out: DevicePtr<f32>) -> Result<()> {
+        let b = self.open_raw()?;
+        check(self.ctx.raw, unsafe {
+            sys::slm_batch_decode_layer_exact(b, layer, q.c(), k.c(), v.c(), out.m())
+        })
+    }
+
     /// Appends the batch's tokens of one layer (prompt prefill).
     pub fn append_layer(&mut self, layer: i32, k: DevicePtr<f32>, v: DevicePtr<f32>,
                         rotate_keys: bool) -> Result<()> {

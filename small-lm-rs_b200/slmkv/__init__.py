@@ -131,6 +131,7 @@ SIGNATURES = {
     "slm_batch_append_layer": (C.c_int, [_vp, _i32, _vp, _vp, _i32]),
     "slm_batch_prefill_attention": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
     "slm_batch_attention_exact": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
+    "slm_batch_decode_layer_exact": (C.c_int, [_vp, _i32, _vp, _vp, _vp, _vp]),
     "slm_batch_end": (C.c_int, [_vp, _pi32]),
     "slm_batch_rollback": (C.c_int, [_vp]),
     "slm_batch_submit": (C.c_int, [_vp]),
@@ -564,6 +565,12 @@ class Batch:
     def prefill_attention(self, layer: int, query, out, rotate_query: bool = True) -> None:
         self.pool.check(lib().slm_batch_prefill_attention(self._h, int(layer), _ptr(query),
                                                           int(bool(rotate_query)), _ptr(out)))
+
+    def decode_layer_exact(self, layer: int, query, keys, values, out) -> None:
+        """slm_batch_decode_layer_exact: decode_layer in the reference's
+        operation order (attention.rs:794-810, 677-759), bit for bit; f32 pools."""
+        self.pool.check(lib().slm_batch_decode_layer_exact(self._h, int(layer), _ptr(query),
+                                                           _ptr(keys), _ptr(values), _ptr(out)))
 
     def attention_exact(self, layer: int, query, out, rotate_query: bool = True) -> None:
         """slm_batch_attention_exact: the batch's attention in the reference's

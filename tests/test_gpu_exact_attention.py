@@ -93,10 +93,12 @@ def test_prefill_after_history_is_bit_exact():
         row += t
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("hq,hkv", [(4, 2), (8, 2)])
-def test_decode_steps_are_bit_exact(hq, hkv):
+def test_decode_steps_are_bit_exact(hq, hkv, fused):
     # append at the pre-append length, then attend the grown cache
-    # (attention.rs:794-810); three steps over ragged shuffled caches
+    # (attention.rs:794-810); three steps over ragged shuffled caches, as
+    # append + attention_exact and as the one-kernel decode_layer_exact
     rng = np.random.default_rng(70 + hq)
     lengths = [1, 15, 16, 17, 100, 300, 511 - 3]
     n = len(lengths)
@@ -112,11 +114,39 @@ def test_decode_steps_are_bit_exact(hq, hkv):
                 k = rng.standard_normal((n, hkv, D)).astype(np.float32)
                 v = rng.standard_normal((n, hkv, D)).astype(np.float32)
                 out = torch.empty((n, hq, D), dtype=torch.float32, device="cuda:0")
-                b.append_layer(layer, to_dev(k), to_dev(v), rotate_keys=True)
-                b.attention_exact(layer, to_dev(q), out, rotate_query=True)
+                if fused:
+                    b.decode_layer_exact(layer, to_dev(q), to_dev(k), to_dev(v), out)
+                else:
+                    b.append_layer(layer, to_dev(k), to_dev(v), rotate_keys=True)
+                    b.attention_exact(layer, to_dev(q), out, rotate_query=True)
                 ref = O.forward_cached_attention_batch(ocs, layer, q, k, v, hq, inv, threads=8)
                 assert np.array_equal(bits(out).reshape(n, -1), bits(ref).reshape(n, -1))
     assert [c.sequence_length() for c in caches] == [L + 3 for L in lengths]
+    for c, oc in zip(caches, ocs):  # the appended rows, bit for bit
+        for layer in range(2):
+            assert np.array_equal(bits(c.layer_keys(layer)), bits(oc.layer_keys(layer)))
+            assert np.array_equal(bits(c.layer_values(layer)), bits(oc.layer_values(layer)))
+
+
+def test_fused_exact_decode_rolls_back_non_finite_kv():
+    rng = np.random.default_rng(75)
+    pool = _pool(4, 2, layers=1, seqs=3)
+    inv = O.rope_inverse_frequencies(D, 10000.0)
+    caches = [pool.allocate_kv_cache(64) for _ in range(3)]
+    ocs = [O.DenseCache(1, 64, 2, D) for _ in range(3)]
+    fill_history(caches, ocs, [15, 16, 3], 1, rng, inv, 2, D)
+    q = rng.standard_normal((3, 4, D)).astype(np.float32)
+    k = rng.standard_normal((3, 2, D)).astype(np.float32)
+    v = rng.standard_normal((3, 2, D)).astype(np.float32)
+    v[1, 1, 5] = np.inf
+    out = torch.empty((3, 4, D), dtype=torch.float32, device="cuda:0")
+    b = pool.begin(caches, 1)
+    b.decode_layer_exact(0, to_dev(q), to_dev(k), to_dev(v), out)
+    with pytest.raises(slmkv.InvalidInput) as e:
+        b.end()
+    assert "key/value" in str(e.value)
+    assert b.statuses == [0, slmkv.ERR_NON_FINITE, 0]
+    assert [c.sequence_length() for c in caches] == [16, 16, 4]
 
 
 def test_exact_attention_flags_a_non_finite_query_and_needs_f32():
