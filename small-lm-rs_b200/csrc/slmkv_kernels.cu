@@ -1555,8 +1555,13 @@ cudaError_t launch_append(const AppendLaunch& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-int exact_attention_stages(int32_t max_ctx) {
-  for (int st = 16; st >= 2; --st)
+// V ring depth: a few rows (batch-1 decode) run one CTA per SM or less, and
+// each CTA's value fold waits on its own copies, so the ring is deep (16
+// blocks in flight from the CTA's start); many rows keep several CTAs per SM
+// busy, which hides the copies, so the ring is shallow and more CTAs fit.
+int exact_attention_stages(int32_t max_ctx, int64_t items) {
+  const int want = items <= 2 * 148 ? 16 : 4;
+  for (int st = want; st >= 2; --st)
     if (exact_smem_layout(max_ctx, st).total <= 227 * 1024) return st;
   return 0;
 }
@@ -1566,13 +1571,13 @@ cudaError_t launch_exact_attention(const PrefillLaunch& p0, cudaStream_t s) {
   if (p0.g.bf16) return cudaErrorInvalidValue;
   PrefillLaunch p = p0;
   p.max_ctx = (p.max_ctx + 3) & ~3;
-  const int stages = exact_attention_stages(p.max_ctx);
+  const int64_t items = static_cast<int64_t>(p.total_tokens) * p.g.q_heads;
+  const int stages = exact_attention_stages(p.max_ctx, items);
   if (stages == 0) return cudaErrorInvalidValue;
   const int smem = exact_smem_layout(p.max_ctx, stages).total;
   cudaError_t e = cudaFuncSetAttribute(exact_attention_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  const int64_t items = static_cast<int64_t>(p.total_tokens) * p.g.q_heads;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(items));
   cfg.blockDim = dim3(kExactThreads);

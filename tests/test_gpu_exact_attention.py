@@ -128,6 +128,28 @@ def test_decode_steps_are_bit_exact(hq, hkv, fused):
             assert np.array_equal(bits(c.layer_values(layer)), bits(oc.layer_values(layer)))
 
 
+def test_fused_exact_decode_of_many_sequences_is_bit_exact():
+    # 100 sequences x 4 heads: more rows than the deep-ring shape takes, so
+    # the shallow V ring with several CTAs per SM runs
+    rng = np.random.default_rng(77)
+    hq, hkv = 4, 2
+    lengths = [int(x) for x in rng.integers(1, 300, size=100)]
+    n = len(lengths)
+    pool = _pool(hq, hkv, layers=1, seqs=n, blocks=sum(L // 16 + 2 for L in lengths) + 8)
+    inv = O.rope_inverse_frequencies(D, 10000.0)
+    caches = [pool.allocate_kv_cache(512) for _ in lengths]
+    ocs = [O.DenseCache(1, 512, hkv, D) for _ in lengths]
+    fill_history(caches, ocs, lengths, 1, rng, inv, hkv, D)
+    q = rng.standard_normal((n, hq, D)).astype(np.float32)
+    k = rng.standard_normal((n, hkv, D)).astype(np.float32)
+    v = rng.standard_normal((n, hkv, D)).astype(np.float32)
+    out = torch.empty((n, hq, D), dtype=torch.float32, device="cuda:0")
+    with pool.begin(caches, 1) as b:
+        b.decode_layer_exact(0, to_dev(q), to_dev(k), to_dev(v), out)
+    ref = O.forward_cached_attention_batch(ocs, 0, q, k, v, hq, inv, threads=8)
+    assert np.array_equal(bits(out).reshape(n, -1), bits(ref).reshape(n, -1))
+
+
 def test_fused_exact_decode_rolls_back_non_finite_kv():
     rng = np.random.default_rng(75)
     pool = _pool(4, 2, layers=1, seqs=3)
