@@ -458,8 +458,8 @@ struct StreamShape {
   static constexpr int kOffQ = kOffSide + W * R * kSide;
   static constexpr int kOffP = kOffQ + W * G * D * 4;
   static constexpr int kOffSlots = kOffP + W * G * kBlockTokens * 4;
-  static constexpr int kOffBars = kOffSlots + 2 * W * kSlot;  // K then V mbarrier per stage
-  static constexpr int kOffChunk = kOffBars + W * R * 16;
+  static constexpr int kOffBars = kOffSlots + 2 * W * kSlot;
+  static constexpr int kOffChunk = kOffBars + W * R * 8;
   static constexpr int kOffCnt = kOffChunk + W * R * 4;
   static constexpr int kOffPend = (kOffCnt + 2 * W * 4 + 15) / 16 * 16;
   static constexpr int kSmem = kOffPend + W * R * 16 + (BF16 ? 1024 : 0);  // + alignment slack
@@ -575,11 +575,7 @@ __global__ void __launch_bounds__(W * 32, 1)
   float* qs = reinterpret_cast<float*>(smem + Sh::kOffQ) + warp * G * D;
   float* pbuf = reinterpret_cast<float*>(smem + Sh::kOffP) + warp * G * kBlockTokens;
   uint8_t* slots = smem + Sh::kOffSlots;
-  // kbar[s]: the stage's K chunk (and, for a pair's first block, its side
-  // inputs); vbar[s]: its V chunk. f32 stages refill K as soon as a block's
-  // scores are done, while its P.V runs, and V after the P.V.
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sh::kOffBars) + warp * 2 * R;
-  uint64_t* vbars = bars + R;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sh::kOffBars) + warp * R;
   int* stage_chunk = reinterpret_cast<int*>(smem + Sh::kOffChunk) + warp * R;
   int* cta_cnt = reinterpret_cast<int*>(smem + Sh::kOffCnt);
   int4* side_pend = reinterpret_cast<int4*>(smem + Sh::kOffPend) + warp * R;
@@ -615,10 +611,7 @@ __global__ void __launch_bounds__(W * 32, 1)
   };
   if (active) load_window(r0.x);
   if (active && lane == 0) {
-    for (int s = 0; s < R; ++s) {
-      mbar_init(&bars[s], 1);
-      mbar_init(&vbars[s], 1);
-    }
+    for (int s = 0; s < R; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
   const int cta_w0 = blockIdx.x * W;
@@ -649,11 +642,10 @@ __global__ void __launch_bounds__(W * 32, 1)
       bulk_load(sd + Sh::kSideVn, p.v_new + row, D * 4, &bars[stage]);
     }
   };
-  // Arms the next stage's K barrier and copies its K chunk (and side
-  // inputs); with defer_side the side copies are recorded in side_pend and
-  // issued later on the same barrier (its expected byte count already
-  // includes them). issue_v then copies the same block's V chunk.
-  auto issue_k = [&](int stage, bool defer_side) {
+  // Arms the next stage and copies its K/V chunks; with defer_side the side
+  // copies are recorded in side_pend and issued later on the same barrier
+  // (its expected byte count already includes them).
+  auto issue = [&](int stage, bool defer_side) {
     if (pg == pp_end) {  // the producer enters the next pair
       ++pp;
       if (pp - pwin >= 32) load_window(pc);
@@ -678,14 +670,17 @@ __global__ void __launch_bounds__(W * 32, 1)
       uint8_t* st = stages + stage * Sh::kStage;
       const bool first = (pg == pp_first);
       const bool appends = p.fused && first && (pp_end - 1 < g1);
-      uint32_t tx = Sh::kChunk;
+      uint32_t tx = Sh::kStage;
       if (first) tx += G * D * 4 + (p.fused ? (D / 2) * 8 : 0) + (appends ? 2 * D * 4 : 0);
       mbar_arrive_expect_tx(&bars[stage], tx);
       if constexpr (BF16) {
         const int y = (p.layer * static_cast<int>(max_chunk) + static_cast<int>(chunk)) * kBlockTokens;
         tma_load_rows(st, &p.tmap_k, y, &bars[stage]);
+        tma_load_rows(st + Sh::kChunk, &p.tmap_v, y, &bars[stage]);
       } else {
         bulk_load(st, kbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk, &bars[stage]);
+        bulk_load(st + Sh::kChunk, vbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk,
+                  &bars[stage]);
       }
       if (defer_side)
         side_pend[stage] = first ? make_int4(pp_seq, pp_head, pp_L, appends ? 1 : 0)
@@ -694,23 +689,6 @@ __global__ void __launch_bounds__(W * 32, 1)
         issue_side(stage, pp_seq, pp_head, pp_L, appends);
     }
     ++pg;
-  };
-  auto issue_v = [&](int stage) {  // lane 0: the V chunk of the block issue_k staged last
-    if (lane == 0) {
-      const uint32_t chunk = static_cast<uint32_t>(stage_chunk[stage]);
-      uint8_t* st = stages + stage * Sh::kStage + Sh::kChunk;
-      mbar_arrive_expect_tx(&vbars[stage], Sh::kChunk);
-      if constexpr (BF16) {
-        const int y = (p.layer * static_cast<int>(max_chunk) + static_cast<int>(chunk)) * kBlockTokens;
-        tma_load_rows(st, &p.tmap_v, y, &vbars[stage]);
-      } else {
-        bulk_load(st, vbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk, &vbars[stage]);
-      }
-    }
-  };
-  auto issue = [&](int stage, bool defer_side) {
-    issue_k(stage, defer_side);
-    issue_v(stage);
   };
 
   // The first stages' K/V may be fetched before waiting on the previous
@@ -757,34 +735,19 @@ __global__ void __launch_bounds__(W * 32, 1)
   int npend = 0;
   int4 pend0 = make_int4(0, 0, 0, 0), pend1 = pend0;  // {pair, global slot base, n CTA segs, row}
 
-  // A copy that did not land within the limit: record it, give the copies
-  // still in flight a bounded chance to land (from stream index `from` on;
-  // V of `from` itself when only its V wait failed), and stop this warp.
-  auto give_up = [&](int from_k, int from_v) {
-    if (lane == 0) {
-      atomicOr(p.g.error, kErrTimeout);
-      for (int c = from_k; c < pg - g0; ++c)
-        mbar_wait_bounded(&bars[c % R], static_cast<uint32_t>(c / R) & 1u);
-      for (int c = from_v; c < pg - g0; ++c)
-        mbar_wait_bounded(&vbars[c % R], static_cast<uint32_t>(c / R) & 1u);
-    }
-    __syncwarp();
-  };
   for (int g = g0, cnt = 0; g < g1; ++g, ++cnt) {
     const int stage = cnt % R;
     const uint32_t parity = static_cast<uint32_t>(cnt / R) & 1u;
     if (!mbar_wait_bounded(&bars[stage], parity)) {
-      give_up(cnt + 1, cnt);
-      return;
-    }
-    // bf16 blocks (and any block that appends) need V before their first step
-    bool v_ready = false;
-    if (BF16 || (p.fused && g - cur.blk_begin == cur.nblk - 1)) {
-      if (!mbar_wait_bounded(&vbars[stage], parity)) {
-        give_up(cnt + 1, cnt);
-        return;
+      // A copy did not land within the limit: record it, give the copies
+      // still in flight a bounded chance to land, and stop this warp.
+      if (lane == 0) {
+        atomicOr(p.g.error, kErrTimeout);
+        for (int c = cnt + 1; c < pg - g0; ++c)
+          mbar_wait_bounded(&bars[c % R], static_cast<uint32_t>(c / R) & 1u);
       }
-      v_ready = true;
+      __syncwarp();
+      return;
     }
     uint8_t* kb = stages + stage * Sh::kStage;
     uint8_t* vb = kb + Sh::kChunk;
@@ -871,28 +834,12 @@ __global__ void __launch_bounds__(W * 32, 1)
       float sc[G];
       block_scores_f32<G>(reinterpret_cast<const float*>(kb), qs, lane, sc);
       bad |= scores_bad<G>(sc, (lane & 15) < nvalid);
-      // K (and the side buffer) are read: refill them with the next block
-      // while this block's P.V runs.
-      const bool refill = pg < g1;
-      if (refill) {
-        __syncwarp();
-        if (append_here) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        issue_k(stage, false);
-      }
-      if (!v_ready && !mbar_wait_bounded(&vbars[stage], parity)) {
-        give_up(cnt + 1, cnt);
-        return;
-      }
       block_softmax_pv<G, false>(vb, pbuf, lane, nvalid, sc, m, l, acc);
-      if (refill) {
-        if (append_here) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        issue_v(stage);
-      }
     }
-    if (BF16 && pg < g1) {
+    if (pg < g1) {
       // The stage (and its side buffer) were read, maybe written, through
       // the generic proxy; order that before the async-proxy refill.
-      if (append_here || nvalid < kBlockTokens)
+      if (append_here || (BF16 && nvalid < kBlockTokens))
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(stage, false);
     }
