@@ -227,6 +227,7 @@ struct ProjArgs {
   __nv_bfloat16* h;             // GU: [rows, I]
   int32_t H, KV, I;
   float beta_gate, beta_up;
+  int32_t cols;                 // one-row kernel: output columns a CTA (a multiple of 8)
 };
 
 template <int MODE>
@@ -557,6 +558,8 @@ struct slm_model {
   // (slm_batch_attention_exact), so that their logits are the CPU path's
   bool f32_pool = false;
   bool head_kernel_ok = false;  // rows up to 64 on head_kernel (hidden <= 4096)
+  // one-row steps: columns a CTA of proj1_kernel per mode (0: proj_kernel)
+  int32_t p1_cols[4] = {0, 0, 0, 0};
   cublasHandle_t blas = nullptr;
   void* weights = nullptr;  // one device allocation for every tensor
   const float* emb = nullptr;         // [V, H] fp32: lookup table and tied vocabulary projection
@@ -661,8 +664,115 @@ int32_t grid_for(size_t work, int32_t threads) {
   return static_cast<int32_t>(std::min<size_t>(std::max<size_t>(g, 1), 148 * 16));
 }
 
+// ---- one token row (batch-1 decode) ----------------------------------------------
+// The fold of one output column is K dependent fmas in k order and cannot be
+// split, so a one-row projection is a few hundred independent folds; the
+// kernel above packs 128 columns (two a thread, four for gate/up) into each
+// of 64 threads and issues them from a handful of CTAs, and each warp's
+// long dependent instruction stream sets the time. Here every thread folds one
+// column (gate/up: the first `cols` threads the gate columns, the next the
+// up columns), a CTA takes `cols` columns, and the projection spreads over
+// ncols / cols small CTAs. The CTA's whole weight tile (K rows x cols
+// columns, bf16) is requested by cp.async before waiting on the previous
+// kernel (weights are immutable), so it lands while that kernel finishes.
+// Same operands, folds, norm and epilogues as proj_kernel: the same bits.
+constexpr int kProj1MaxSmem = 200 * 1024;
+template <int MODE>
+size_t proj1_smem(int32_t K, int32_t cols) {
+  return static_cast<size_t>(K) * 4 + static_cast<size_t>(proj_mats<MODE>()) * K * cols * 2;
+}
+// Columns a CTA: 32 (gate/up and down: more CTAs for the larger matrices) or
+// 64, halved while the tile does not fit; 0 when not even 8 fit.
+template <int MODE>
+int32_t proj1_cols(int32_t K) {
+  int32_t c = (MODE == kProjQKV || MODE == kProjO) ? 64 : 32;
+  while (c >= 8 && proj1_smem<MODE>(K, c) > static_cast<size_t>(kProj1MaxSmem)) c /= 2;
+  return c >= 8 ? c : 0;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(128) proj1_kernel(const ProjArgs a) {
+  constexpr int NM = proj_mats<MODE>();
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int K = a.K, C = a.cols, NT = NM * C;
+  float* xs = reinterpret_cast<float*>(smem);  // [K]
+  __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(smem + static_cast<size_t>(K) * 4);  // [NM][K][C]
+  __shared__ float inv_s;
+  __shared__ float up_s[64];
+  const int tid = threadIdx.x;
+  const int c0 = blockIdx.x * C;
+  const int seg = C / 8;  // 16-byte segments of a weight row
+  for (int i = tid; i < NM * K * seg; i += NT) {
+    const int m = i / (K * seg), rem = i - m * K * seg;
+    const int k = rem / seg, sg = rem - k * seg;
+    const int col = c0 + 8 * sg;
+    if (col < a.ncols)
+      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(ws + (static_cast<size_t>(m) * K + k) * C + 8 * sg)),
+                 a.w + static_cast<size_t>(k) * a.ld + (m ? a.I : 0) + col);
+  }
+  cp_async_commit();
+  wait_previous_kernel();  // the row comes from the previous kernels
+  for (int k = tid; k < K; k += NT) xs[k] = MODE == kProjDown ? __bfloat162float(a.xh[k]) : a.x[k];
+  __syncthreads();
+  if (MODE == kProjQKV || MODE == kProjGU) {
+    if (tid == 0) {  // rmsnorm.rs:80-91, the in-order square-sum fold
+      float sum = 0.f;
+#pragma unroll 8
+      for (int k = 0; k < K; ++k) sum = fmaf(xs[k], xs[k], sum);
+      inv_s = 1.f / sqrtf(__fdiv_rn(sum, static_cast<float>(K)) + a.eps);
+    }
+    __syncthreads();
+    for (int k = tid; k < K; k += NT) xs[k] = round_bf16(__fmul_rn(__fmul_rn(xs[k], inv_s), a.norm_w[k]));
+  } else if (MODE == kProjO) {
+    for (int k = tid; k < K; k += NT) xs[k] = round_bf16(xs[k]);
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  const int m = (NM > 1 && tid >= C) ? 1 : 0;
+  const int cl = tid - m * C, col = c0 + cl;
+  float acc = 0.f;
+  if (col < a.ncols) {
+    const uint16_t* wc = reinterpret_cast<const uint16_t*>(ws) + static_cast<size_t>(m) * K * C + cl;
+    for (int k = 0; k < K; k += 8) {  // K is a multiple of 8; loads first, then the fmas in order
+      const float4 x0 = *reinterpret_cast<const float4*>(xs + k);
+      const float4 x1 = *reinterpret_cast<const float4*>(xs + k + 4);
+      uint32_t w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = wc[static_cast<size_t>(k + j) * C];
+      acc = fmaf(x0.x, __uint_as_float(w[0] << 16), acc);
+      acc = fmaf(x0.y, __uint_as_float(w[1] << 16), acc);
+      acc = fmaf(x0.z, __uint_as_float(w[2] << 16), acc);
+      acc = fmaf(x0.w, __uint_as_float(w[3] << 16), acc);
+      acc = fmaf(x1.x, __uint_as_float(w[4] << 16), acc);
+      acc = fmaf(x1.y, __uint_as_float(w[5] << 16), acc);
+      acc = fmaf(x1.z, __uint_as_float(w[6] << 16), acc);
+      acc = fmaf(x1.w, __uint_as_float(w[7] << 16), acc);
+    }
+  }
+  if (MODE == kProjGU) {
+    if (m == 1) up_s[cl] = acc;
+    __syncthreads();
+    if (m == 0 && col < a.ncols)  // situ_glu.rs:101-107
+      a.h[col] = __float2bfloat16_rn(__fmul_rn(situ_gate(acc, a.beta_gate), situ_up(up_s[cl], a.beta_up)));
+    return;
+  }
+  if (col >= a.ncols) return;
+  if (MODE == kProjQKV) {
+    if (col < a.H) a.y0[col] = acc;
+    else if (col < a.H + a.KV) a.y1[col - a.H] = acc;
+    else a.y2[col - a.H - a.KV] = acc;
+  } else {  // transformer.rs add_residual_in_place: hidden += update
+    a.y0[col] = __fadd_rn(a.y0[col], acc);
+  }
+}
+
 template <int MODE>
 cudaError_t launch_proj(const ProjArgs& a, cudaStream_t s) {
+  if (a.rows == 1 && a.cols > 0) {
+    ProjArgs b = a;
+    return launch_chained(proj1_kernel<MODE>, dim3((a.ncols + a.cols - 1) / a.cols),
+                          dim3(proj_mats<MODE>() * a.cols), proj1_smem<MODE>(a.K, a.cols), s, b);
+  }
   const int gx = (a.ncols + kProjCols - 1) / kProjCols;
   if (a.rows == 1)
     return launch_chained(proj_kernel<MODE, 1>, dim3(gx, 1), dim3(kProjThreads), proj_smem<MODE>(a.K), s, a);
@@ -725,17 +835,21 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       a.beta_up = m->beta_up;
       ProjArgs q = a;  // q, k, v with the attention RMSNorm
       q.x = m->x, q.norm_w = Ly.attn_norm, q.K = H, q.ncols = H + 2 * KV, q.w = Ly.wqkv, q.ld = H + 2 * KV;
+      q.cols = m->p1_cols[kProjQKV];
       q.y0 = m->q, q.y1 = m->k, q.y2 = m->v;
       launched(launch_proj<kProjQKV>(q, s));
       if ((rc = cache_step(l))) return rc;
       ProjArgs o = a;  // output projection onto the residual
       o.x = m->att, o.K = H, o.ncols = H, o.w = Ly.wo, o.ld = H, o.y0 = m->x;
+      o.cols = m->p1_cols[kProjO];
       launched(launch_proj<kProjO>(o, s));
       ProjArgs g = a;  // gate / up with the FFN RMSNorm, SiTU-GLU
       g.x = m->x, g.norm_w = Ly.ffn_norm, g.K = H, g.ncols = I, g.w = Ly.wgu, g.ld = 2 * I, g.h = hb;
+      g.cols = m->p1_cols[kProjGU];
       launched(launch_proj<kProjGU>(g, s));
       ProjArgs d = a;  // down projection onto the residual
       d.xh = hb, d.K = I, d.ncols = H, d.w = Ly.wd, d.ld = H, d.y0 = m->x;
+      d.cols = m->p1_cols[kProjDown];
       launched(launch_proj<kProjDown>(d, s));
       launches += 4;
       continue;
@@ -979,6 +1093,14 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
       slm_model_destroy(m);
       return cuda_fail(ctx, "slm_model_create", a);
     }
+    auto one_row = [&](auto kernel, int32_t cols, size_t bytes, int mode) {
+      if (cols > 0 && attr(kernel, bytes) == cudaSuccess) m->p1_cols[mode] = cols;
+    };
+    one_row(proj1_kernel<kProjQKV>, proj1_cols<kProjQKV>(H), proj1_smem<kProjQKV>(H, proj1_cols<kProjQKV>(H)), kProjQKV);
+    one_row(proj1_kernel<kProjO>, proj1_cols<kProjO>(H), proj1_smem<kProjO>(H, proj1_cols<kProjO>(H)), kProjO);
+    one_row(proj1_kernel<kProjGU>, proj1_cols<kProjGU>(H), proj1_smem<kProjGU>(H, proj1_cols<kProjGU>(H)), kProjGU);
+    one_row(proj1_kernel<kProjDown>, proj1_cols<kProjDown>(I), proj1_smem<kProjDown>(I, proj1_cols<kProjDown>(I)),
+            kProjDown);
   }
   const uint8_t* base = static_cast<const uint8_t*>(m->weights);
   m->emb = reinterpret_cast<const float*>(base + o_emb);
