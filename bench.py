@@ -5,8 +5,11 @@ Workload (the batched KV-cached decode microbench): B=256 sequences per GPU,
 cached lengths uniform in [1, 511] (seeded), 4 query / 2 KV heads, head_dim
 64, f32 KV, 16-token paged blocks handed out from a shuffled free list, 8
 layers. One step = one decode token for every sequence through all 8 layers:
-`slm_batch_begin`, 8 x `slm_batch_decode_layer` (RoPE on Q and K, paged
-append, split-K attention over the grown cache), `slm_batch_end`. After each
+`slm_batch_begin`, `slm_batch_decode_layers` over the 8 layers (RoPE on Q and
+K, paged append, split-K attention over the grown cache; one launch runs all
+8, since every layer's inputs are given), `slm_batch_submit`. The same step
+with one `slm_batch_decode_layer` launch per layer, as a model step issues
+them, is timed beside it ("one_layer_launches"). After each
 step the sequences return to their drawn lengths (host bookkeeping only), so
 every step does the same work. One step reads ~544 MB of K/V, far more than
 the 126 MB L2, so no flush is needed between steps.
@@ -534,13 +537,13 @@ def run_ours(args):
     base_arr = plan.lengths(base)
     ptrs = [(q[l].data_ptr(), kn[l].data_ptr(), vn[l].data_ptr(), out[l].data_ptr())
             for l in range(LAYERS)]
-    # Decode-kernel timing, live in every timed step: one CUDA event when
-    # layer 0's kernel completes and one when layer 7's completes; the host
-    # queues launches faster than the GPU runs them, so the interval divided
-    # by LAYERS-1 is the kernels' average duration back to back (launches
-    # overlap their prologue with the previous kernel's tail).
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
+    io = slmkv.layer_io_array(ptrs)
+    # Decode-kernel timing, live in every timed step: a step's layers go out
+    # as one launch (slm_batch_decode_layers) and a CUDA event records its
+    # completion; the host queues steps ahead of the GPU, so the interval
+    # between consecutive steps' completions is the launch's duration back to
+    # back (each launch's prologue overlaps the previous one's tail).
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
 
     # Steps are pipelined (slm_batch_submit / slm_batch_wait): a step is
     # submitted without waiting for the GPU, the next one is planned and
@@ -556,13 +559,12 @@ def run_ours(args):
 
     host_s = [0.0, 0.0]  # seconds in begin..submit, and waiting in collect
 
-    def step(timed_index=None, layer_ptrs=ptrs):
+    def step(timed_index=None, layer_io=io):
         t0 = time.perf_counter()
         batch = plan.begin()
-        for layer in range(LAYERS):
-            batch.decode_layer_ptr(layer, *layer_ptrs[layer])
-            if timed_index is not None and layer in (0, LAYERS - 1):
-                ev[timed_index][0 if layer == 0 else 1].record(stream)
+        batch.decode_layers_array(0, LAYERS, layer_io)
+        if timed_index is not None:
+            ev[timed_index].record(stream)
         inflight.append(batch.submit())
         t1 = time.perf_counter()
         collect(DEPTH - 1)
@@ -592,8 +594,26 @@ def run_ours(args):
     launches = pool.launch_count() - launches0
     clocks = sampler.stop() if sampler else None
     ms = t_start.elapsed_time(t_stop)
-    kern_ms = [a.elapsed_time(b) / (LAYERS - 1) for a, b in ev]
-    kern_avg_ms = sum(kern_ms) / len(kern_ms)
+    kern_avg_ms = ev[0].elapsed_time(ev[-1]) / max(1, args.steps - 1)
+
+    # The same step with one launch per layer (slm_batch_decode_layer), as a
+    # model step issues them between its projections: completion of layer 0's
+    # and of the last layer's kernel, interval / (LAYERS - 1).
+    chain_steps = min(args.steps, 50)
+    cev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(chain_steps)]
+    for i in range(3 + chain_steps):
+        batch = plan.begin()
+        for layer in range(LAYERS):
+            batch.decode_layer_ptr(layer, *ptrs[layer])
+            if i >= 3 and layer in (0, LAYERS - 1):
+                cev[i - 3][0 if layer == 0 else 1].record(stream)
+        inflight.append(batch.submit())
+        collect(DEPTH - 1)
+        plan.truncate_all(base_arr)
+    collect(0)
+    torch.cuda.synchronize()
+    chain_ms = sum(a.elapsed_time(b) for a, b in cev) / (chain_steps * (LAYERS - 1))
     # every rank's own step time and host time per step, for the line
     mine = torch.tensor([ms / args.steps, kern_avg_ms, host_s[0] / args.steps * 1e3,
                          host_s[1] / args.steps * 1e3], dtype=torch.float64, device=dev)
@@ -602,7 +622,7 @@ def run_ours(args):
         per_rank = [torch.zeros_like(mine) for _ in range(world)]
         dist.all_gather(per_rank, mine)
     per_rank = [[round(float(x), 4) for x in t.tolist()] for t in per_rank]
-    ms, kern_avg_ms = max_over_ranks([ms, kern_avg_ms], device=dev)
+    ms, kern_avg_ms, chain_ms = max_over_ranks([ms, kern_avg_ms, chain_ms], device=dev)
 
     # End to end through the public API with host buffers: every step copies
     # its inputs in from pinned host memory and its outputs back out. The
@@ -610,14 +630,22 @@ def run_ours(args):
     # later steps' inputs cross PCIe while step i computes and earlier steps'
     # outputs come back; the compute stream waits for its inputs, and a
     # buffer is rewritten only after the step that used it is done with it.
-    hq_ = q.cpu().pin_memory()
-    hk_ = kn.cpu().pin_memory()
-    hv_ = vn.cpu().pin_memory()
+    # A step's inputs sit in one pinned host buffer (Q, new K, new V of every
+    # layer, back to back) and cross PCIe as one copy; its outputs as one.
+    n_in = q.numel() + kn.numel() + vn.numel()
+    h_in = torch.cat([q.reshape(-1), kn.reshape(-1), vn.reshape(-1)]).cpu().pin_memory()
     ho_ = [torch.empty_like(out, device="cpu").pin_memory() for _ in range(DEPTH)]
-    dbuf = [(torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn), torch.empty_like(out))
-            for _ in range(DEPTH)]
-    dptrs = [[(bq[l].data_ptr(), bk[l].data_ptr(), bv[l].data_ptr(), bo[l].data_ptr())
-              for l in range(LAYERS)] for bq, bk, bv, bo in dbuf]
+
+    def split_in(buf):
+        a, b_ = q.numel(), q.numel() + kn.numel()
+        return (buf[:a].view_as(q), buf[a:b_].view_as(kn), buf[b_:].view_as(vn))
+
+    dbuf = [(torch.empty(n_in, device=dev), torch.empty_like(out)) for _ in range(DEPTH)]
+    dio = []
+    for bin_, bo in dbuf:
+        bq, bk, bv = split_in(bin_)
+        dio.append(slmkv.layer_io_array([(bq[l].data_ptr(), bk[l].data_ptr(), bv[l].data_ptr(),
+                                          bo[l].data_ptr()) for l in range(LAYERS)]))
     h2d, d2h = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
     in_ready = [torch.cuda.Event() for _ in range(DEPTH)]
     computed = [torch.cuda.Event() for _ in range(DEPTH)]
@@ -632,20 +660,17 @@ def run_ours(args):
         j = e2e_i[0] % DEPTH
         ce = cev[e2e_i[0]]
         e2e_i[0] += 1
-        bq, bk, bv, bo = dbuf[j]
+        bin_, bo = dbuf[j]
         with torch.cuda.stream(h2d):
             h2d.wait_event(computed[j])  # the step that last read these inputs
             ce[0].record(h2d)
-            bq.copy_(hq_, non_blocking=True)
-            bk.copy_(hk_, non_blocking=True)
-            bv.copy_(hv_, non_blocking=True)
+            bin_.copy_(h_in, non_blocking=True)
             ce[1].record(h2d)
             in_ready[j].record(h2d)
         stream.wait_event(in_ready[j])
         stream.wait_event(read_back[j])  # the outputs last written here were read
         batch = plan.begin()
-        for layer in range(LAYERS):
-            batch.decode_layer_ptr(layer, *dptrs[j][layer])
+        batch.decode_layers_array(0, LAYERS, dio[j])
         computed[j].record(stream)
         with torch.cuda.stream(d2h):
             d2h.wait_event(computed[j])
@@ -692,8 +717,9 @@ def run_ours(args):
     value = tokens / (ms / 1e3)
     e2e_value = tokens / (e2e_ms / 1e3)
     peaks, peak_kind = measured_peaks()
-    alg = algorithmic_bytes(lengths)
-    achieved = alg / (kern_avg_ms / 1e3) / 1e9
+    alg = algorithmic_bytes(lengths)  # one layer
+    achieved = LAYERS * alg / (kern_avg_ms / 1e3) / 1e9  # a launch runs every layer
+    chain_achieved = alg / (chain_ms / 1e3) / 1e9
     traffic, traffic_src = ncu_traffic_per_launch()
     result = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
@@ -709,15 +735,27 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "traffic": traffic, "traffic_source": traffic_src, "peak_source": peak_kind,
-                     "kernel": "decode_kernel (fused RoPE + paged append + split-K GQA attention)",
-                     "algorithmic_bytes_per_launch": alg, "avg_launch_ms": kern_avg_ms},
+                     "kernel": ("decode_stream_kernel (fused RoPE + paged append + split-K GQA "
+                                f"attention), all {LAYERS} layers of a step in one launch "
+                                "(slm_batch_decode_layers)"),
+                     "algorithmic_bytes_per_launch": LAYERS * alg, "avg_launch_ms": kern_avg_ms,
+                     "timing": ("CUDA events at each timed step's launch completion; mean "
+                                "interval between consecutive steps' completions")},
+        "one_layer_launches": {
+            "what": ("the same step as one slm_batch_decode_layer launch per layer, as a model "
+                     "step issues them between its projections"),
+            "avg_launch_ms": chain_ms, "algorithmic_bytes_per_launch": alg,
+            "achieved": chain_achieved, "unit": "GB/s", "frac": chain_achieved / peaks["hbm_gbs"],
+            "timing": (f"completion of layer 0's to layer {LAYERS - 1}'s kernel, "
+                       f"/ {LAYERS - 1}, over {chain_steps} steps")},
         "e2e": {"value": e2e_value, "unit": "tok/s",
-                "h2d_bytes_per_step": int(q.numel() + kn.numel() + vn.numel()) * 4,
-                "copies": f"own H2D and D2H streams, {DEPTH} buffer sets, overlapping compute",
+                "h2d_bytes_per_step": int(n_in) * 4,
+                "copies": (f"one H2D and one D2H copy a step on their own streams, {DEPTH} "
+                           "buffer sets, overlapping compute"),
                 "d2h_bytes_per_step": int(out.numel()) * 4,
                 "ms_per_step": e2e_ms / args.steps,
                 "h2d_copy_ms_per_step": h2d_ms, "d2h_copy_ms_per_step": d2h_ms,
-                "h2d_gbs": (q.numel() + kn.numel() + vn.numel()) * 4 / (h2d_ms / 1e3) / 1e9,
+                "h2d_gbs": n_in * 4 / (h2d_ms / 1e3) / 1e9,
                 "d2h_gbs": out.numel() * 4 / (d2h_ms / 1e3) / 1e9},
         "append_kernel": {"achieved": append_bytes / (append_ms / 1e3) / 1e9, "unit": "GB/s",
                           "frac": append_bytes / (append_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
@@ -734,8 +772,8 @@ def run_ours(args):
                          f"({total} tokens), Hq={HQ}, Hkv={HKV}, causal, bf16 KV, tcgen05")}}
            if BF16 else {}),
         "gpu_launches": launches,
-        "kernel_timing": ("CUDA events at the completion of layer 0's and layer 7's decode "
-                          "kernel in every timed step; interval / 7"),
+        "kernel_timing": ("CUDA events at the completion of every timed step's decode launch "
+                          "(all layers); mean interval between consecutive completions"),
         "per_rank": {"fields": ["ms_per_step", "decode_kernel_ms", "host_submit_ms_per_step",
                                 "host_wait_ms_per_step"], "values": per_rank,
                      "host_cores_per_rank": len(pinned)},

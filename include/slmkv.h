@@ -163,6 +163,23 @@ slm_status slm_batch_begin(slm_ctx* ctx, int32_t n, const int32_t* h_seq_ids,
  * q: [n, q_heads, d], k/v: [n, kv_heads, d] (unrotated), out: [n, q_heads, d]. */
 slm_status slm_batch_decode_layer(slm_batch* batch, int32_t layer, const float* d_query,
                                   const float* d_keys, const float* d_values, float* d_out);
+/* One decode layer's device buffers, as slm_batch_decode_layer takes them. */
+typedef struct slm_layer_io {
+  const float* query;   /* [n, q_heads, d] */
+  const float* keys;    /* [n, kv_heads, d], unrotated */
+  const float* values;  /* [n, kv_heads, d] */
+  float* out;           /* [n, q_heads, d] */
+} slm_layer_io;
+/* slm_batch_decode_layer for layers first_layer .. first_layer + n_layers - 1,
+ * io[i] for layer first_layer + i, when the inputs of all of them are ready
+ * (forward_cached_token's cache part, attention.rs:794-810, per layer). The
+ * layers share the batch's plan, so up to 8 of them run as one launch: each
+ * warp of the grid takes its slice of the step's blocks in every layer in
+ * turn, keeping its copies in flight across the layer boundaries. Results
+ * equal the one-layer calls'. Every layer is checked before anything is
+ * launched; a layer's output may not overlap another layer's buffers. */
+slm_status slm_batch_decode_layers(slm_batch* batch, int32_t first_layer, int32_t n_layers,
+                                   const slm_layer_io* io);
 /* Append-only form (prompt prefill, attention.rs:863-868): keys/values are the
  * batch's tokens concatenated in batch order, [sum(counts), kv_heads, d]. */
 slm_status slm_batch_append_layer(slm_batch* batch, int32_t layer, const float* d_keys,

@@ -79,6 +79,10 @@ struct StreamPlan {
   // 2 per warp: {first pair, seq, head, ctx_len}, {first pair's end, g0, g1, 0}
   std::vector<int4> warp_start;
   std::vector<int32_t> bounds;  // warp boundaries in the stream (scratch)
+  // A launch that runs several layers keeps each warp's chunk ids and pair
+  // entries in one 32-entry window: true when every warp's slice has at most
+  // 32 blocks and touches at most 32 pairs.
+  bool fits_window = false;
   std::vector<int32_t> bucket_top, bucket_next, heads_left;  // pair packing (scratch)
 };
 
@@ -133,6 +137,7 @@ struct slm_ctx {
   int32_t group = 1;
   int32_t n_warps = 0;     // decode grid: SMs x decode_warps()
   int32_t max_pairs = 0;   // max_sequences x Hkv
+  int32_t launch_layers = 1;  // layers one decode launch may run (split-K scratch copies)
   int64_t max_chunks = 0;  // max_sequences x blocks per sequence x Hkv
   int64_t device_bytes = 0;
   int64_t launches = 0;  // kernels launched by this context
@@ -140,7 +145,11 @@ struct slm_ctx {
   // decode of another layer right after it may fetch its first K/V stages
   // before waiting on it (nothing else has written the pool since).
   int32_t prev_decode_layer = -1;
+  int32_t prev_decode_last = -1;  // with it, the last layer that launch ran
   std::string err;
+  size_t counter_bytes() const {
+    return sizeof(int32_t) * static_cast<size_t>(max_pairs) * launch_layers;
+  }
 
   // device memory
   void* k_pool = nullptr;
@@ -569,13 +578,17 @@ void build_stream_plan(const slm_ctx* c, const std::vector<SeqEntry>& entries, i
     if (n_cta > 1) part += n_cta;
   }
   plan.warp_start.resize(static_cast<size_t>(2 * NW));
-  size_t pc = 0;
+  plan.fits_window = true;
+  size_t pc = 0, pl = 0;  // first and last pair of warp w's slice
   for (int32_t w = 0; w < NW; ++w) {
     const int32_t b = bounds[w];
     while (plan.pairs[pc].blk_begin + plan.pairs[pc].nblk <= b) ++pc;
     const PairEntry& pe = plan.pairs[pc];
     plan.warp_start[2 * w] = make_int4(static_cast<int32_t>(pc), pe.seq, pe.head, pe.ctx_len);
     plan.warp_start[2 * w + 1] = make_int4(pe.blk_begin + pe.nblk, b, bounds[w + 1], 0);
+    if (pl < pc) pl = pc;
+    while (plan.pairs[pl].blk_begin + plan.pairs[pl].nblk < bounds[w + 1]) ++pl;
+    if (bounds[w + 1] - b > 32 || pl - pc + 1 > 32) plan.fits_window = false;
   }
 }
 
@@ -675,9 +688,12 @@ StreamDecodeLaunch decode_launch(slm_ctx* c, int32_t layer, const StepDev& dev,
   p.total_blocks = static_cast<int32_t>(plan.chunks.size());
   p.warp_start = dev.wfp;
   p.n_warps = static_cast<int32_t>(plan.warp_start.size() / 2);
+  p.n_layers = 1;
   p.part_acc = c->d_part_acc;
   p.part_ml = c->d_part_ml;
+  p.part_stride = c->max_pairs + c->n_warps;
   p.counters = c->d_counters;
+  p.counter_stride = c->max_pairs;
   p.status = dev.status;
   return p;
 }
@@ -688,7 +704,7 @@ slm_status check_device_error(slm_ctx* c) {
   CU(c, cudaMemcpy(&e, c->d_error, sizeof e, cudaMemcpyDeviceToHost));
   if (e) {
     CU(c, cudaMemset(c->d_error, 0, sizeof(int32_t)));
-    CU(c, cudaMemset(c->d_counters, 0, sizeof(int32_t) * c->max_pairs));
+    CU(c, cudaMemset(c->d_counters, 0, c->counter_bytes()));
     if (e & kErrTimeout)
       return fail(c, SLM_ERR_DEVICE_TIMEOUT, "device wait timed out (error word 0x%x)", e);
     if (e & kErrLayout)
@@ -824,6 +840,7 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
   c->group = G;
   c->max_blocks_per_seq = blocks_for(k.context_length);
   c->max_pairs = k.max_sequences * k.num_key_value_heads;
+  c->launch_layers = std::min(k.num_layers, kMaxLaunchLayers);
   c->max_chunks = static_cast<int64_t>(c->max_pairs) * c->max_blocks_per_seq;
   c->seqs.resize(k.max_sequences);
   for (int32_t i = k.max_sequences - 1; i >= 0; --i) c->free_slots.push_back(i);
@@ -862,10 +879,12 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
     step(dev_alloc(cp, &cp->d_rope, rope.size() * sizeof(float2), "RoPE table"));
     // A pair split over s warps takes s partial slots; at most one extra
     // slot per warp boundary: pairs + warps bounds the total.
-    const size_t parts = (static_cast<size_t>(cp->max_pairs) + cp->n_warps) * G;
+    // One copy of the partials and counters per layer a launch may run.
+    const size_t parts =
+        (static_cast<size_t>(cp->max_pairs) + cp->n_warps) * G * cp->launch_layers;
     step(dev_alloc(cp, &cp->d_part_acc, parts * kHeadDim * sizeof(float), "split-K partials"));
     step(dev_alloc(cp, &cp->d_part_ml, parts * sizeof(float2), "split-K partials"));
-    step(dev_alloc(cp, &cp->d_counters, sizeof(int32_t) * cp->max_pairs, "split-K counters"));
+    step(dev_alloc(cp, &cp->d_counters, cp->counter_bytes(), "split-K counters"));
     step(dev_alloc(cp, &cp->d_error, sizeof(int32_t), "error word"));
     if (rc == SLM_OK) {
       e = cudaMallocHost(reinterpret_cast<void**>(&cp->h_readback),
@@ -895,7 +914,7 @@ slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
       if ((e = cudaMemset(cp->k_pool, 0, pool_bytes)) != cudaSuccess ||
           (e = cudaMemset(cp->v_pool, 0, pool_bytes)) != cudaSuccess ||
           (e = cudaMemset(cp->d_block_table, 0, bt_bytes)) != cudaSuccess ||
-          (e = cudaMemset(cp->d_counters, 0, sizeof(int32_t) * cp->max_pairs)) != cudaSuccess ||
+          (e = cudaMemset(cp->d_counters, 0, cp->counter_bytes())) != cudaSuccess ||
           (e = cudaMemset(cp->d_error, 0, sizeof(int32_t))) != cudaSuccess ||
           (e = cudaMemcpy(cp->d_rope, rope.data(), rope.size() * sizeof(float2),
                           cudaMemcpyHostToDevice)) != cudaSuccess ||
@@ -1212,8 +1231,8 @@ slm_status slm_attend_cached_query(slm_ctx* ctx, int32_t seq_id, int32_t layer,
   rc = upload_step(ctx, ctx->up_aux, s, e, &plan, &dev);
   if (rc) return rc;
   StreamDecodeLaunch p = decode_launch(ctx, layer, dev, plan);
-  p.q = d_query;
-  p.out = d_out;
+  p.q[0] = d_query;
+  p.out[0] = d_out;
   p.fused = 0;
   ctx->prev_decode_layer = -1;
   CU(ctx, launch_decode(p, s));
@@ -1349,9 +1368,11 @@ slm_status batch_layer_check(slm_batch* b, int32_t layer) {
 }
 }  // namespace
 
-slm_status slm_batch_decode_layer(slm_batch* b, int32_t layer, const float* d_query,
-                                  const float* d_keys, const float* d_values, float* d_out) {
-  if (!b) return SLM_ERR_INVALID_INPUT;
+namespace {
+// Checks one decode layer's arguments (the batch open, every count 1, the
+// layer not yet appended, the buffers non-null and 16-byte aligned).
+slm_status decode_layer_check(slm_batch* b, int32_t layer, const float* d_query,
+                              const float* d_keys, const float* d_values, const float* d_out) {
   slm_ctx* ctx = b->ctx;
   slm_status rc = batch_layer_check(b, layer);
   if (rc) return rc;
@@ -1365,19 +1386,93 @@ slm_status slm_batch_decode_layer(slm_batch* b, int32_t layer, const float* d_qu
   if (!aligned16(d_query) || !aligned16(d_keys) || !aligned16(d_values) || !aligned16(d_out))
     return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
                        "query, key, value and output buffers must be 16-byte aligned");
-  StreamDecodeLaunch p = decode_launch(ctx, layer, b->dev, ctx->plan);
-  p.q = d_query;
-  p.k_new = d_keys;
-  p.v_new = d_values;
-  p.out = d_out;
+  return SLM_OK;
+}
+
+// Launches the decode of layers first .. first + nl - 1 (io[i] for layer
+// first + i) as one kernel, then advances those layers' lengths.
+slm_status decode_launch_layers(slm_batch* b, int32_t first, int32_t nl, const slm_layer_io* io) {
+  slm_ctx* ctx = b->ctx;
+  StreamDecodeLaunch p = decode_launch(ctx, first, b->dev, ctx->plan);
+  p.n_layers = nl;
+  for (int32_t i = 0; i < nl; ++i) {
+    p.q[i] = io[i].query;
+    p.k_new[i] = io[i].keys;
+    p.v_new[i] = io[i].values;
+    p.out[i] = io[i].out;
+  }
   p.fused = 1;
-  p.early_kv = (ctx->prev_decode_layer >= 0 && ctx->prev_decode_layer != layer) ? 1 : 0;
-  ctx->prev_decode_layer = layer;
+  // The first stages may be fetched early when the previous launch was a
+  // decode of other layers only.
+  const int32_t last = first + nl - 1;
+  p.early_kv = (ctx->prev_decode_layer >= 0 &&
+                (last < ctx->prev_decode_layer || first > ctx->prev_decode_last)) ? 1 : 0;
+  ctx->prev_decode_layer = first;
+  ctx->prev_decode_last = last;
   CU(ctx, launch_decode(p, b->stream));
   ++ctx->launches;
-  b->layer_done[layer] = 1;
-  for (size_t i = 0; i < b->seq_ids.size(); ++i)
-    ctx->seqs[b->seq_ids[i]].layer_len[layer] = b->base[i] + b->counts[i];
+  for (int32_t layer = first; layer <= last; ++layer) {
+    b->layer_done[layer] = 1;
+    for (size_t i = 0; i < b->seq_ids.size(); ++i)
+      ctx->seqs[b->seq_ids[i]].layer_len[layer] = b->base[i] + b->counts[i];
+  }
+  return SLM_OK;
+}
+
+bool ranges_overlap(const void* a, size_t na, const void* b, size_t nb) {
+  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return x < y + nb && y < x + na;
+}
+}  // namespace
+
+slm_status slm_batch_decode_layer(slm_batch* b, int32_t layer, const float* d_query,
+                                  const float* d_keys, const float* d_values, float* d_out) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_status rc = decode_layer_check(b, layer, d_query, d_keys, d_values, d_out);
+  if (rc) return rc;
+  const slm_layer_io io{d_query, d_keys, d_values, d_out};
+  return decode_launch_layers(b, layer, 1, &io);
+}
+
+slm_status slm_batch_decode_layers(slm_batch* b, int32_t first_layer, int32_t n_layers,
+                                   const slm_layer_io* io) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_ctx* ctx = b->ctx;
+  if (n_layers <= 0 || !io)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
+                       "a layer count of at least 1 and its buffers are required");
+  if (first_layer < 0 || n_layers > ctx->cfg.num_layers - first_layer)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache",
+                       "layers %d..%d are outside 0..%d", first_layer,
+                       first_layer + n_layers - 1, ctx->cfg.num_layers);
+  // Everything is checked before the first launch.
+  for (int32_t i = 0; i < n_layers; ++i) {
+    const slm_status rc = decode_layer_check(b, first_layer + i, io[i].query, io[i].keys,
+                                             io[i].values, io[i].out);
+    if (rc) return rc;
+  }
+  // The layers of one launch run at the same time: a layer's output may not
+  // overlap another layer's inputs or output.
+  const size_t n = b->seq_ids.size();
+  const size_t qb = n * ctx->cfg.num_query_heads * kHeadDim * sizeof(float);
+  const size_t kvb = n * ctx->cfg.num_key_value_heads * kHeadDim * sizeof(float);
+  for (int32_t i = 0; i < n_layers; ++i)
+    for (int32_t j = 0; j < n_layers; ++j) {
+      if (i == j) continue;
+      const void* o = io[i].out;
+      if (ranges_overlap(o, qb, io[j].query, qb) || ranges_overlap(o, qb, io[j].keys, kvb) ||
+          ranges_overlap(o, qb, io[j].values, kvb) || ranges_overlap(o, qb, io[j].out, qb))
+        return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
+                           "layer %d's output overlaps layer %d's buffers", first_layer + i,
+                           first_layer + j);
+    }
+  // One launch runs up to kMaxLaunchLayers layers when every warp's slice
+  // fits its 32-entry windows; otherwise one launch per layer.
+  const int32_t per = ctx->plan.fits_window ? ctx->launch_layers : 1;
+  for (int32_t i = 0; i < n_layers; i += per) {
+    const slm_status rc = decode_launch_layers(b, first_layer + i, std::min(per, n_layers - i), io + i);
+    if (rc) return rc;
+  }
   return SLM_OK;
 }
 
@@ -1594,7 +1689,7 @@ void resolve_oldest(slm_ctx* ctx) {
   } else if (rb[0]) {
     const int32_t w = rb[0];
     cudaMemsetAsync(ctx->d_error, 0, sizeof(int32_t), b->stream);
-    cudaMemsetAsync(ctx->d_counters, 0, sizeof(int32_t) * ctx->max_pairs, b->stream);
+    cudaMemsetAsync(ctx->d_counters, 0, ctx->counter_bytes(), b->stream);
     char buf[160];
     if (w & kErrTimeout) {
       dev = SLM_ERR_DEVICE_TIMEOUT;

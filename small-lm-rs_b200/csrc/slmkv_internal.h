@@ -93,9 +93,13 @@ struct PoolGeom {
 
 
 // ---- kernel launchers (slmkv_kernels.cu) ----------------------------------
+// Layers one decode launch may run (consecutive layers, one plan).
+constexpr int kMaxLaunchLayers = 8;
+
 struct StreamDecodeLaunch {
   PoolGeom g;
-  int32_t layer;
+  int32_t layer;     // first layer of the launch
+  int32_t n_layers;  // layers layer .. layer + n_layers - 1, 1..kMaxLaunchLayers
   const PairEntry* pairs;
   int32_t n_pairs;
   const int32_t* chunks;          // [total_blocks]
@@ -103,13 +107,16 @@ struct StreamDecodeLaunch {
   const int4* warp_start;         // [2 * n_warps]: {first pair, seq, head,
                                   //  ctx_len}, {first pair's end, g0, g1, 0}
   int32_t n_warps;                // grid = ceil(n_warps / decode_warps()) CTAs
-  const float* q;      // [n, Hq, d]
-  const float* k_new;  // [n, Hkv, d] (fused mode) or null
-  const float* v_new;
-  float* out;          // [n, Hq, d]
-  float* part_acc;     // [slots][G][d]
-  float2* part_ml;     // [slots][G]  (running max in the exp2 domain, sum)
-  int32_t* counters;   // [n_pairs], zero between launches
+  // per layer of the launch:
+  const float* q[kMaxLaunchLayers];      // [n, Hq, d]
+  const float* k_new[kMaxLaunchLayers];  // [n, Hkv, d] (fused mode) or null
+  const float* v_new[kMaxLaunchLayers];
+  float* out[kMaxLaunchLayers];          // [n, Hq, d]
+  float* part_acc;        // [layer of the launch][part_stride slots][G][d]
+  float2* part_ml;        // [layer][part_stride][G] (running max in the exp2 domain, sum)
+  int32_t part_stride;    // split-K partial slots per layer of the launch
+  int32_t* counters;      // [layer][counter_stride], zero between launches
+  int32_t counter_stride;
   int32_t* status;     // [n]
   int32_t fused;       // 1: rope(q,k) + append + attend; 0: attend (q rotated)
   // 1: this layer's pool region was last written by a launch that completed

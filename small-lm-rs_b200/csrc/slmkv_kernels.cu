@@ -460,8 +460,8 @@ struct StreamShape {
   static constexpr int kOffSlots = kOffP + W * G * kBlockTokens * 4;
   static constexpr int kOffBars = kOffSlots + 2 * W * kSlot;
   static constexpr int kOffChunk = kOffBars + W * R * 8;
-  static constexpr int kOffCnt = kOffChunk + W * R * 4;
-  static constexpr int kOffPend = (kOffCnt + 2 * W * 4 + 15) / 16 * 16;
+  static constexpr int kOffCnt = kOffChunk + W * R * 4;  // 3 x 2W merge-slot counters
+  static constexpr int kOffPend = (kOffCnt + 6 * W * 4 + 15) / 16 * 16;
   static constexpr int kSmem = kOffPend + W * R * 16 + (BF16 ? 1024 : 0);  // + alignment slack
   static_assert(kSmem <= 227 * 1024, "decode staging exceeds shared memory");
   static_assert(kChunk % 16 == 0 && kSide % 16 == 0 && kSlot % 16 == 0, "16-byte alignment");
@@ -577,24 +577,32 @@ __global__ void __launch_bounds__(W * 32, 1)
   uint8_t* slots = smem + Sh::kOffSlots;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sh::kOffBars) + warp * R;
   int* stage_chunk = reinterpret_cast<int*>(smem + Sh::kOffChunk) + warp * R;
+  // In-CTA merge bookkeeping, per slot: arrivals (at the pair's first slot),
+  // partials written into the slot, and partials read out of it by a merge.
   int* cta_cnt = reinterpret_cast<int*>(smem + Sh::kOffCnt);
+  int* slot_wr = cta_cnt + 2 * W;
+  int* slot_rd = cta_cnt + 4 * W;
   int4* side_pend = reinterpret_cast<int4*>(smem + Sh::kOffPend) + warp * R;
 
-  if (threadIdx.x < 2 * W) cta_cnt[threadIdx.x] = 0;
+  if (threadIdx.x < 6 * W) cta_cnt[threadIdx.x] = 0;
   const int gw = blockIdx.x * W + warp;
   const bool active = gw < p.n_warps;
 
   // Start record: {first pair, seq, head, ctx_len}, {first pair's end in the
-  // stream, g0, g1, -}; the warp owns stream blocks [g0, g1) (never empty).
-  // The step plan (start records, chunk stream, pair entries) is written only
-  // by host-to-device copies ordered before the previous kernel of the stream,
-  // never by a kernel, so it is read before the wait below.
+  // stream, g0, g1, -}; the warp owns stream blocks [g0, g1) (never empty) of
+  // every layer of the launch. The step plan (start records, chunk stream,
+  // pair entries) is written only by host-to-device copies ordered before the
+  // previous kernel of the stream, never by a kernel, so it is read before
+  // the wait below.
   int4 r0 = make_int4(0, 0, 0, 0), r1 = r0;
   if (active) {
     r0 = p.warp_start[2 * gw];
     r1 = p.warp_start[2 * gw + 1];
   }
   const int g0 = r1.y, g1 = r1.z;
+  // The warp's blocks over the launch: its slice of layer 0, then the same
+  // slice of layer 1, and so on (the plan is the same for every layer).
+  const int total = p.n_layers * (g1 - g0);
   int cwin = g0;
   int cval = (g0 + lane < g1) ? p.chunks[g0 + lane] : 0;
 
@@ -618,35 +626,49 @@ __global__ void __launch_bounds__(W * 32, 1)
   const int cta_w1 = min(cta_w0 + W, p.n_warps) - 1;
 
   const int Hkv = p.g.kv_heads, Hq = p.g.q_heads;
-  const size_t layer_elems = static_cast<size_t>(p.layer) * p.g.layer_elems;
-  const uint8_t* kbase = static_cast<const uint8_t*>(p.g.k) + layer_elems * Sh::kEsz;
-  const uint8_t* vbase = static_cast<const uint8_t*>(p.g.v) + layer_elems * Sh::kEsz;
+  const size_t layer_bytes = static_cast<size_t>(p.g.layer_elems) * Sh::kEsz;
+  const uint8_t* kbase = static_cast<const uint8_t*>(p.g.k) + p.layer * layer_bytes;
+  const uint8_t* vbase = static_cast<const uint8_t*>(p.g.v) + p.layer * layer_bytes;
   const uint32_t max_chunk = static_cast<uint32_t>(p.g.num_blocks) * Hkv;
 
   // ---- producer: lane 0 keeps R stages in flight ahead of the consumer ------
-  int pg = g0;  // next stream block to issue
+  int pg = g0, pl = 0, pv = 0;  // next stream block to issue, its layer, blocks issued
   int pp = r0.x, pp_seq = r0.y, pp_head = r0.z, pp_L = r0.w, pp_end = r1.x;
   int pp_first = g0;  // first block of pair pp in this warp
   int pc = r0.x;      // the consumer's pair; the window never moves past it
   // Side copies of a stage that starts a pair (lane 0): the pair's Q rows,
   // its RoPE row and, when this warp ends the pair, the new K/V rows.
-  auto issue_side = [&](int stage, int seq, int head, int L, bool appends) {
+  auto issue_side = [&](int stage, int seq, int head, int L, bool appends, int layer) {
     uint8_t* sd = sides + stage * Sh::kSide;
-    bulk_load(sd, p.q + (static_cast<size_t>(seq) * Hq + head * G) * D, G * D * 4, &bars[stage]);
+    bulk_load(sd, p.q[layer] + (static_cast<size_t>(seq) * Hq + head * G) * D, G * D * 4,
+              &bars[stage]);
     if (p.fused)
       bulk_load(sd + Sh::kSideCs, p.g.rope + static_cast<size_t>(L - 1) * (D / 2), (D / 2) * 8,
                 &bars[stage]);
     if (appends) {
       const size_t row = (static_cast<size_t>(seq) * Hkv + head) * D;
-      bulk_load(sd + Sh::kSideKn, p.k_new + row, D * 4, &bars[stage]);
-      bulk_load(sd + Sh::kSideVn, p.v_new + row, D * 4, &bars[stage]);
+      bulk_load(sd + Sh::kSideKn, p.k_new[layer] + row, D * 4, &bars[stage]);
+      bulk_load(sd + Sh::kSideVn, p.v_new[layer] + row, D * 4, &bars[stage]);
     }
   };
   // Arms the next stage and copies its K/V chunks; with defer_side the side
   // copies are recorded in side_pend and issued later on the same barrier
   // (its expected byte count already includes them).
   auto issue = [&](int stage, bool defer_side) {
-    if (pg == pp_end) {  // the producer enters the next pair
+    if (pg == g1) {  // the producer enters the next layer: the slice again
+      ++pl;
+      pg = g0;
+      pp = r0.x;
+      pp_seq = r0.y;
+      pp_head = r0.z;
+      pp_L = r0.w;
+      pp_end = r1.x;
+      pp_first = g0;
+      if (cwin != g0) {  // the chunk window is the producer's alone
+        cwin = g0;
+        cval = (g0 + lane < g1) ? p.chunks[g0 + lane] : 0;
+      }
+    } else if (pg == pp_end) {  // the producer enters the next pair
       ++pp;
       if (pp - pwin >= 32) load_window(pc);
       const PairFields f = pair_from_window(pa, pb, pp - pwin);
@@ -674,28 +696,30 @@ __global__ void __launch_bounds__(W * 32, 1)
       if (first) tx += G * D * 4 + (p.fused ? (D / 2) * 8 : 0) + (appends ? 2 * D * 4 : 0);
       mbar_arrive_expect_tx(&bars[stage], tx);
       if constexpr (BF16) {
-        const int y = (p.layer * static_cast<int>(max_chunk) + static_cast<int>(chunk)) * kBlockTokens;
+        const int y = ((p.layer + pl) * static_cast<int>(max_chunk) + static_cast<int>(chunk)) *
+                      kBlockTokens;
         tma_load_rows(st, &p.tmap_k, y, &bars[stage]);
         tma_load_rows(st + Sh::kChunk, &p.tmap_v, y, &bars[stage]);
       } else {
-        bulk_load(st, kbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk, &bars[stage]);
-        bulk_load(st + Sh::kChunk, vbase + static_cast<size_t>(chunk) * Sh::kChunk, Sh::kChunk,
-                  &bars[stage]);
+        const size_t off = pl * layer_bytes + static_cast<size_t>(chunk) * Sh::kChunk;
+        bulk_load(st, kbase + off, Sh::kChunk, &bars[stage]);
+        bulk_load(st + Sh::kChunk, vbase + off, Sh::kChunk, &bars[stage]);
       }
       if (defer_side)
-        side_pend[stage] = first ? make_int4(pp_seq, pp_head, pp_L, appends ? 1 : 0)
+        side_pend[stage] = first ? make_int4(pp_seq, pp_head, pp_L, (pl << 1) | (appends ? 1 : 0))
                                  : make_int4(0, 0, 0, -1);
       else if (first)
-        issue_side(stage, pp_seq, pp_head, pp_L, appends);
+        issue_side(stage, pp_seq, pp_head, pp_L, appends, pl);
     }
     ++pg;
+    ++pv;
   };
 
   // The first stages' K/V may be fetched before waiting on the previous
   // kernel when the host says this layer's pool region was complete before
   // that kernel started (the previous kernel is a decode of another layer).
   if (active && p.early_kv)
-    for (int s = 0; s < R && pg < g1; ++s) issue(s, true);
+    for (int s = 0; s < R && pv < total; ++s) issue(s, true);
 
   // Launched with programmatic stream serialization: everything above ran
   // while the previous kernel of the stream was finishing; wait for it (and
@@ -709,12 +733,12 @@ __global__ void __launch_bounds__(W * 32, 1)
   if (!active) return;
   if (p.early_kv) {
     if (lane == 0)
-      for (int s = 0; s < pg - g0; ++s) {
+      for (int s = 0; s < pv; ++s) {
         const int4 e = side_pend[s];
-        if (e.w >= 0) issue_side(s, e.x, e.y, e.z, e.w != 0);
+        if (e.w >= 0) issue_side(s, e.x, e.y, e.z, (e.w & 1) != 0, e.w >> 1);
       }
   } else {
-    for (int s = 0; s < R && pg < g1; ++s) issue(s, false);
+    for (int s = 0; s < R && pv < total; ++s) issue(s, false);
   }
   // ---- consumer --------------------------------------------------------------
   PairFields cur = pair_from_window(pa, pb, pc - pwin);
@@ -730,20 +754,21 @@ __global__ void __launch_bounds__(W * 32, 1)
   // query, softmax.rs:17-22): the pair's sequence is flagged at the segment's
   // end and its step fails as attention.rs:731,814-815 does.
   bool bad = false;
+  int cl = 0;  // the consumer's layer (of the launch)
 
-  // Cross-CTA pairs finished after the warp's last block (at most two).
+  // Cross-CTA pairs of the current layer, merged after its last block (at most two).
   int npend = 0;
   int4 pend0 = make_int4(0, 0, 0, 0), pend1 = pend0;  // {pair, global slot base, n CTA segs, row}
 
-  for (int g = g0, cnt = 0; g < g1; ++g, ++cnt) {
-    const int stage = cnt % R;
-    const uint32_t parity = static_cast<uint32_t>(cnt / R) & 1u;
+  for (int v = 0, g = g0; v < total; ++v) {
+    const int stage = v % R;
+    const uint32_t parity = static_cast<uint32_t>(v / R) & 1u;
     if (!mbar_wait_bounded(&bars[stage], parity)) {
       // A copy did not land within the limit: record it, give the copies
       // still in flight a bounded chance to land, and stop this warp.
       if (lane == 0) {
         atomicOr(p.g.error, kErrTimeout);
-        for (int c = cnt + 1; c < pg - g0; ++c)
+        for (int c = v + 1; c < pv; ++c)
           mbar_wait_bounded(&bars[c % R], static_cast<uint32_t>(c / R) & 1u);
       }
       __syncwarp();
@@ -794,8 +819,8 @@ __global__ void __launch_bounds__(W * 32, 1)
       const int slot = (cur.L - 1) - tok0;
       bool fin = finite2(kn) && finite2(vn);
       float2 kx = rope_pair(kn, cs);
-      const size_t dst =
-          layer_elems + (static_cast<size_t>(stage_chunk[stage]) * kBlockTokens + slot) * D;
+      const size_t dst = static_cast<size_t>(p.layer + cl) * p.g.layer_elems +
+                         (static_cast<size_t>(stage_chunk[stage]) * kBlockTokens + slot) * D;
       // Non-finite K/V are stored as zeros: the pool never holds a non-finite
       // value (the step fails and the slot stays past the length).
       if constexpr (BF16) {
@@ -836,7 +861,7 @@ __global__ void __launch_bounds__(W * 32, 1)
       bad |= scores_bad<G>(sc, (lane & 15) < nvalid);
       block_softmax_pv<G, false>(vb, pbuf, lane, nvalid, sc, m, l, acc);
     }
-    if (pg < g1) {
+    if (pv < total) {
       // The stage (and its side buffer) were read, maybe written, through
       // the generic proxy; order that before the async-proxy refill.
       if (append_here || (BF16 && nvalid < kBlockTokens))
@@ -844,163 +869,212 @@ __global__ void __launch_bounds__(W * 32, 1)
       issue(stage, false);
     }
 
-    if (g != seg_end - 1) continue;
-    // ---- end of this warp's segment of pair `pc` ---------------------------------
-    if (__any_sync(kFull, bad)) {
-      if (lane == 0 && p.status) atomicOr(&p.status[cur.seq], kStatusNonFiniteScore);
-      bad = false;
-    }
-    if constexpr (BF16) {
-      // Back to one float2 per lane and head (dims 2*lane, 2*lane+1): the
-      // layout the merges below use. qs is free: Q lives in qa.
-      const int gl = lane >> 2, tl = lane & 3;
-      if (gl < G) {
-#pragma unroll
-        for (int n = 0; n < 8; ++n)
-          *reinterpret_cast<float2*>(qs + gl * D + 8 * n + 2 * tl) =
-              make_float2(o[n][0] + o[n][2], o[n][1] + o[n][3]);
+    if (g == seg_end - 1) {
+      // ---- end of this warp's segment of pair `pc` -------------------------------
+      if (__any_sync(kFull, bad)) {
+        if (lane == 0 && p.status) atomicOr(&p.status[cur.seq], kStatusNonFiniteScore);
+        bad = false;
       }
-      __syncwarp();
+      if constexpr (BF16) {
+        // Back to one float2 per lane and head (dims 2*lane, 2*lane+1): the
+        // layout the merges below use. qs is free: Q lives in qa.
+        const int gl = lane >> 2, tl = lane & 3;
+        if (gl < G) {
 #pragma unroll
-      for (int g2 = 0; g2 < G; ++g2) {
-        acc[g2] = reinterpret_cast<const float2*>(qs + g2 * D)[lane];
-        m[g2] = __shfl_sync(kFull, m_row, 4 * g2);
-        l[g2] = __shfl_sync(kFull, l_row, 4 * g2);
-      }
-      __syncwarp();
-    }
-    const size_t orow = static_cast<size_t>(cur.seq) * Hq + cur.head * G;
-    if (cur.nseg == 1) {
-#pragma unroll
-      for (int g2 = 0; g2 < G; ++g2) {
-        const float inv = 1.0f / l[g2];
-        reinterpret_cast<float2*>(p.out + (orow + g2) * D)[lane] =
-            make_float2(acc[g2].x * inv, acc[g2].y * inv);
-      }
-    } else {
-      // Warps [ka, kb] of this CTA hold the pair's segments here; they merge
-      // in shared memory, the last one to arrive does the merge.
-      const int last_warp = cur.first_warp + cur.nseg - 1;
-      const int ka = max(cur.first_warp, cta_w0), kbw = min(last_warp, cta_w1);
-      const bool whole_in_cta = (cur.first_warp >= cta_w0) && (last_warp <= cta_w1);
-      const int n_in = kbw - ka + 1;
-      // A segment sits in slot 2k+0 when it is warp k's first segment: true
-      // for every warp after ka (the pair started before them); for ka it
-      // depends on where the pair starts.
-      const int ka_off = (cur.first_warp < cta_w0 || cur.at_warp_start) ? 0 : 1;
-      auto seg_slot = [&](int w) { return 2 * (w - cta_w0) + ((w == ka) ? ka_off : 0); };
-      float2 A[G];
-      float Mo[G], Lo[G];
-      bool merged = false;
-      if (n_in == 1) {
-#pragma unroll
-        for (int g2 = 0; g2 < G; ++g2) {
-          A[g2] = acc[g2];
-          Mo[g2] = m[g2];
-          Lo[g2] = l[g2];
+          for (int n = 0; n < 8; ++n)
+            *reinterpret_cast<float2*>(qs + gl * D + 8 * n + 2 * tl) =
+                make_float2(o[n][0] + o[n][2], o[n][1] + o[n][3]);
         }
-        merged = true;
-      } else {
-        uint8_t* mine = slots + seg_slot(gw) * Sh::kSlot;
-#pragma unroll
-        for (int g2 = 0; g2 < G; ++g2) {
-          reinterpret_cast<float2*>(mine)[g2 * (D / 2) + lane] = acc[g2];
-          if (lane == 0)
-            reinterpret_cast<float2*>(mine + G * D * 4)[g2] = make_float2(m[g2], l[g2]);
-        }
-        __threadfence_block();
         __syncwarp();
-        int last = 0;
-        if (lane == 0) last = (atomicAdd(&cta_cnt[seg_slot(ka)], 1) == n_in - 1);
-        last = __shfl_sync(kFull, last, 0);
-        if (last) {
-          __threadfence_block();
-          auto acc_at = [&](int s, int g2) {
-            const uint8_t* sl = slots + seg_slot(ka + s) * Sh::kSlot;
-            return reinterpret_cast<const float2*>(sl)[g2 * (D / 2) + lane];
-          };
-          auto ml_at = [&](int s, int g2) {
-            const uint8_t* sl = slots + seg_slot(ka + s) * Sh::kSlot;
-            return reinterpret_cast<const float2*>(sl + G * D * 4)[g2];
-          };
-          merge_partials<G>(n_in, lane, acc_at, ml_at, A, Mo, Lo);
+#pragma unroll
+        for (int g2 = 0; g2 < G; ++g2) {
+          acc[g2] = reinterpret_cast<const float2*>(qs + g2 * D)[lane];
+          m[g2] = __shfl_sync(kFull, m_row, 4 * g2);
+          l[g2] = __shfl_sync(kFull, l_row, 4 * g2);
+        }
+        __syncwarp();
+      }
+      float* out = p.out[cl];
+      const size_t orow = static_cast<size_t>(cur.seq) * Hq + cur.head * G;
+      if (cur.nseg == 1) {
+#pragma unroll
+        for (int g2 = 0; g2 < G; ++g2) {
+          const float inv = 1.0f / l[g2];
+          reinterpret_cast<float2*>(out + (orow + g2) * D)[lane] =
+              make_float2(acc[g2].x * inv, acc[g2].y * inv);
+        }
+      } else {
+        // Warps [ka, kb] of this CTA hold the pair's segments here; they merge
+        // in shared memory, the last one to arrive does the merge.
+        const int last_warp = cur.first_warp + cur.nseg - 1;
+        const int ka = max(cur.first_warp, cta_w0), kbw = min(last_warp, cta_w1);
+        const bool whole_in_cta = (cur.first_warp >= cta_w0) && (last_warp <= cta_w1);
+        const int n_in = kbw - ka + 1;
+        // A segment sits in slot 2k+0 when it is warp k's first segment: true
+        // for every warp after ka (the pair started before them); for ka it
+        // depends on where the pair starts.
+        const int ka_off = (cur.first_warp < cta_w0 || cur.at_warp_start) ? 0 : 1;
+        auto seg_slot = [&](int w) { return 2 * (w - cta_w0) + ((w == ka) ? ka_off : 0); };
+        float2 A[G];
+        float Mo[G], Lo[G];
+        bool merged = false;
+        if (n_in == 1) {
+#pragma unroll
+          for (int g2 = 0; g2 < G; ++g2) {
+            A[g2] = acc[g2];
+            Mo[g2] = m[g2];
+            Lo[g2] = l[g2];
+          }
           merged = true;
+        } else {
+          const int my = seg_slot(gw);
+          uint8_t* mine = slots + my * Sh::kSlot;
+          // A slot is written again (the same pair in a later layer of the
+          // launch) only after the merge that read its last partial is done.
+          if (lane == 0) {
+            const int written = slot_wr[my];
+            const uint64_t t0 = globaltimer_ns();
+            for (uint32_t i = 0; *reinterpret_cast<volatile int*>(&slot_rd[my]) != written; ++i)
+              if ((i & 31u) == 31u && globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(p.g.error, kErrTimeout);
+                break;
+              }
+            __threadfence_block();
+          }
+          __syncwarp();
+#pragma unroll
+          for (int g2 = 0; g2 < G; ++g2) {
+            reinterpret_cast<float2*>(mine)[g2 * (D / 2) + lane] = acc[g2];
+            if (lane == 0)
+              reinterpret_cast<float2*>(mine + G * D * 4)[g2] = make_float2(m[g2], l[g2]);
+          }
+          __threadfence_block();
+          __syncwarp();
+          int last = 0;
+          if (lane == 0) {
+            slot_wr[my] += 1;
+            last = (atomicAdd(&cta_cnt[seg_slot(ka)], 1) == n_in - 1);
+          }
+          last = __shfl_sync(kFull, last, 0);
+          if (last) {
+            __threadfence_block();
+            auto acc_at = [&](int s, int g2) {
+              const uint8_t* sl = slots + seg_slot(ka + s) * Sh::kSlot;
+              return reinterpret_cast<const float2*>(sl)[g2 * (D / 2) + lane];
+            };
+            auto ml_at = [&](int s, int g2) {
+              const uint8_t* sl = slots + seg_slot(ka + s) * Sh::kSlot;
+              return reinterpret_cast<const float2*>(sl + G * D * 4)[g2];
+            };
+            merge_partials<G>(n_in, lane, acc_at, ml_at, A, Mo, Lo);
+            // Every read of the slots is done: reset the arrivals, release them.
+            __threadfence_block();
+            __syncwarp();
+            if (lane == 0) {
+              cta_cnt[seg_slot(ka)] = 0;
+              __threadfence_block();
+              for (int s = 0; s < n_in; ++s) atomicAdd(&slot_rd[seg_slot(ka + s)], 1);
+            }
+            merged = true;
+          }
+        }
+        if (merged) {
+          if (whole_in_cta) {
+#pragma unroll
+            for (int g2 = 0; g2 < G; ++g2) {
+              const float inv = 1.0f / Lo[g2];
+              reinterpret_cast<float2*>(out + (orow + g2) * D)[lane] =
+                  make_float2(A[g2].x * inv, A[g2].y * inv);
+            }
+          } else {
+            // This CTA's share of a pair that spans CTAs: one global partial
+            // (each layer of the launch has its own slots and counters).
+            const int first_cta = cur.first_warp / W;
+            const int n_cta = last_warp / W - first_cta + 1;
+            const size_t gslot = static_cast<size_t>(cl) * p.part_stride + cur.part_base +
+                                 (blockIdx.x - first_cta);
+#pragma unroll
+            for (int g2 = 0; g2 < G; ++g2) {
+              reinterpret_cast<float2*>(p.part_acc + (gslot * G + g2) * D)[lane] = A[g2];
+              if (lane == 0) p.part_ml[gslot * G + g2] = make_float2(Mo[g2], Lo[g2]);
+            }
+            const int4 e = make_int4(pc, cur.part_base, n_cta, static_cast<int>(orow));
+            if (npend == 0) pend0 = e;
+            else pend1 = e;
+            ++npend;
+          }
         }
       }
-      if (merged) {
-        if (whole_in_cta) {
-#pragma unroll
-          for (int g2 = 0; g2 < G; ++g2) {
-            const float inv = 1.0f / Lo[g2];
-            reinterpret_cast<float2*>(p.out + (orow + g2) * D)[lane] =
-                make_float2(A[g2].x * inv, A[g2].y * inv);
-          }
-        } else {
-          // This CTA's share of a pair that spans CTAs: one global partial.
-          const int first_cta = cur.first_warp / W;
-          const int n_cta = last_warp / W - first_cta + 1;
-          const size_t gslot = static_cast<size_t>(cur.part_base) + (blockIdx.x - first_cta);
-#pragma unroll
-          for (int g2 = 0; g2 < G; ++g2) {
-            reinterpret_cast<float2*>(p.part_acc + (gslot * G + g2) * D)[lane] = A[g2];
-            if (lane == 0) p.part_ml[gslot * G + g2] = make_float2(Mo[g2], Lo[g2]);
-          }
-          const int4 e = make_int4(pc, cur.part_base, n_cta, static_cast<int>(orow));
-          if (npend == 0) pend0 = e;
-          else pend1 = e;
-          ++npend;
-        }
+      if (g + 1 < g1) {
+        ++pc;
+        if (pc - pwin >= 32) load_window(pc);
+        cur = pair_from_window(pa, pb, pc - pwin);
+        seg_end = min(g1, cur.blk_begin + cur.nblk);
+        seg_start = true;
       }
     }
     if (g + 1 < g1) {
-      ++pc;
-      if (pc - pwin >= 32) load_window(pc);
+      ++g;
+      continue;
+    }
+
+    // ---- end of this layer's slice: pairs that span CTAs ----------------------
+    // The last CTA to arrive merges the partials. Release this warp's
+    // partials, then arrive on each pair's counter (both arrivals in flight
+    // together); the next layer's first copies are already in flight.
+    if (npend > 0) {
+      int* counters = p.counters + static_cast<size_t>(cl) * p.counter_stride;
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      __syncwarp();
+      int lastmask = 0;
+      if (lane == 0) {
+        const int prev0 = atomicAdd(&counters[pend0.x], 1);
+        const int prev1 = (npend > 1) ? atomicAdd(&counters[pend1.x], 1) : 0;
+        if (prev0 == pend0.z - 1) {
+          lastmask |= 1;
+          atomicExch(&counters[pend0.x], 0);  // ready for the next launch
+        }
+        if (npend > 1 && prev1 == pend1.z - 1) {
+          lastmask |= 2;
+          atomicExch(&counters[pend1.x], 0);
+        }
+      }
+      lastmask = __shfl_sync(kFull, lastmask, 0);
+      if (lastmask != 0) {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        float* out = p.out[cl];
+        const size_t pbase = static_cast<size_t>(cl) * p.part_stride;
+        for (int k = 0; k < npend; ++k) {
+          if (!((lastmask >> k) & 1)) continue;
+          const int4 e = (k == 0) ? pend0 : pend1;
+          auto acc_at = [&](int s, int g2) {
+            return __ldcg(reinterpret_cast<const float2*>(
+                              p.part_acc + ((pbase + e.y + s) * G + g2) * D) + lane);
+          };
+          auto ml_at = [&](int s, int g2) {
+            return __ldcg(&p.part_ml[(pbase + e.y + s) * G + g2]);
+          };
+          float2 A[G];
+          float Mo[G], Lo[G];
+          merge_partials<G>(e.z, lane, acc_at, ml_at, A, Mo, Lo);
+#pragma unroll
+          for (int g2 = 0; g2 < G; ++g2) {
+            const float inv = 1.0f / Lo[g2];
+            reinterpret_cast<float2*>(out + (static_cast<size_t>(e.w) + g2) * D)[lane] =
+                make_float2(A[g2].x * inv, A[g2].y * inv);
+          }
+        }
+      }
+      npend = 0;
+    }
+    if (v + 1 < total) {  // the consumer enters the next layer: the slice again
+      ++cl;
+      g = g0;
+      pc = r0.x;
+      if (pc < pwin || pc - pwin >= 32) load_window(pc);
       cur = pair_from_window(pa, pb, pc - pwin);
       seg_end = min(g1, cur.blk_begin + cur.nblk);
       seg_start = true;
-    }
-  }
-
-  // ---- pairs that span CTAs: the last CTA to arrive merges the partials -----
-  if (npend == 0) return;
-  // Release this warp's partials, then arrive on each pair's counter (both
-  // arrivals in flight together); the last CTA to arrive acquires and merges.
-  asm volatile("fence.acq_rel.gpu;" ::: "memory");
-  __syncwarp();
-  int lastmask = 0;
-  if (lane == 0) {
-    const int prev0 = atomicAdd(&p.counters[pend0.x], 1);
-    const int prev1 = (npend > 1) ? atomicAdd(&p.counters[pend1.x], 1) : 0;
-    if (prev0 == pend0.z - 1) {
-      lastmask |= 1;
-      atomicExch(&p.counters[pend0.x], 0);  // ready for the next launch
-    }
-    if (npend > 1 && prev1 == pend1.z - 1) {
-      lastmask |= 2;
-      atomicExch(&p.counters[pend1.x], 0);
-    }
-  }
-  lastmask = __shfl_sync(kFull, lastmask, 0);
-  if (lastmask == 0) return;
-  asm volatile("fence.acq_rel.gpu;" ::: "memory");
-  for (int k = 0; k < npend; ++k) {
-    if (!((lastmask >> k) & 1)) continue;
-    const int4 e = (k == 0) ? pend0 : pend1;
-    auto acc_at = [&](int s, int g2) {
-      return __ldcg(reinterpret_cast<const float2*>(
-                        p.part_acc + ((static_cast<size_t>(e.y) + s) * G + g2) * D) + lane);
-    };
-    auto ml_at = [&](int s, int g2) {
-      return __ldcg(&p.part_ml[(static_cast<size_t>(e.y) + s) * G + g2]);
-    };
-    float2 A[G];
-    float Mo[G], Lo[G];
-    merge_partials<G>(e.z, lane, acc_at, ml_at, A, Mo, Lo);
-#pragma unroll
-    for (int g2 = 0; g2 < G; ++g2) {
-      const float inv = 1.0f / Lo[g2];
-      reinterpret_cast<float2*>(p.out + (static_cast<size_t>(e.w) + g2) * D)[lane] =
-          make_float2(A[g2].x * inv, A[g2].y * inv);
     }
   }
 }

@@ -223,16 +223,15 @@ extern "C" slm_status slm_decode_attention_noalloc(
   p.g.context_length = max_blocks_per_sequence * kBlockTokens;
   p.g.error = reinterpret_cast<int32_t*>(dev + kOffError);
   p.layer = 0;
+  p.n_layers = 1;
   p.pairs = reinterpret_cast<const PairEntry*>(dev + kOffPairs);
   p.n_pairs = static_cast<int32_t>(sz.n_pairs);
   p.chunks = reinterpret_cast<const int32_t*>(dev + kOffChunks);
   p.total_blocks = static_cast<int32_t>(sz.n_chunks);
   p.warp_start = reinterpret_cast<const int4*>(dev + kOffWarpStart);
   p.n_warps = sz.n_warps;
-  p.q = d_query;
-  p.k_new = nullptr;
-  p.v_new = nullptr;
-  p.out = d_out;
+  p.q[0] = d_query;
+  p.out[0] = d_out;
   p.part_acc = reinterpret_cast<float*>(dev + kOffPartAcc);
   p.part_ml = reinterpret_cast<float2*>(dev + kOffPartMl);
   p.counters = reinterpret_cast<int32_t*>(dev + kOffCounters);

@@ -42,6 +42,16 @@ pub struct SlmConfig {
     pub kv_dtype: i32,
 }
 
+/// `slm_layer_io`: one decode layer's device buffers (`slm_batch_decode_layers`).
+#[repr(C)]
+#[derive(Clone, Copy, Debug)]
+pub struct SlmLayerIo {
+    pub query: *const f32,
+    pub keys: *const f32,
+    pub values: *const f32,
+    pub out: *mut f32,
+}
+
 /// `slm_sched_config`.
 #[repr(C)]
 #[derive(Clone, Copy, Debug, Default, PartialEq, Eq)]
@@ -103,6 +113,7 @@ extern "C" {
     pub fn slm_attend_cached_query(ctx: *mut SlmCtx, seq_id: i32, layer: i32, d_query: *const f32, d_out: *mut f32, stream: *mut c_void) -> i32;
     pub fn slm_batch_begin(ctx: *mut SlmCtx, n: i32, h_seq_ids: *const i32, h_token_counts: *const i32, stream: *mut c_void, out: *mut *mut SlmBatch) -> i32;
     pub fn slm_batch_decode_layer(batch: *mut SlmBatch, layer: i32, d_query: *const f32, d_keys: *const f32, d_values: *const f32, d_out: *mut f32) -> i32;
+    pub fn slm_batch_decode_layers(batch: *mut SlmBatch, first_layer: i32, n_layers: i32, io: *const SlmLayerIo) -> i32;
     pub fn slm_batch_append_layer(batch: *mut SlmBatch, layer: i32, d_keys: *const f32, d_values: *const f32, rotate_keys: i32) -> i32;
     pub fn slm_batch_prefill_attention(batch: *mut SlmBatch, layer: i32, d_query: *const f32, rotate_query: i32, d_out: *mut f32) -> i32;
     pub fn slm_batch_attention_exact(batch: *mut SlmBatch, layer: i32, d_query: *const f32, rotate_query: i32, d_out: *mut f32) -> i32;

@@ -410,6 +410,23 @@ impl<'c> Batch<'c> {
               unsafe { sys::slm_batch_decode_layer(b, layer, q.c(), k.c(), v.c(), out.m()) })
     }
 
+    /// `decode_layer` for layers `first_layer ..` in order, one
+    /// `(q, k, v, out)` per layer, when all of their inputs are ready: up to
+    /// eight layers run as one launch. A layer's output may not overlap
+    /// another layer's buffers.
+    pub fn decode_layers(&mut self, first_layer: i32,
+                         layers: &[(DevicePtr<f32>, DevicePtr<f32>, DevicePtr<f32>, DevicePtr<f32>)])
+                         -> Result<()> {
+        let b = self.open_raw()?;
+        let io: Vec<sys::SlmLayerIo> = layers
+            .iter()
+            .map(|(q, k, v, out)| sys::SlmLayerIo { query: q.c(), keys: k.c(), values: v.c(), out: out.m() })
+            .collect();
+        check(self.ctx.raw, unsafe {
+            sys::slm_batch_decode_layers(b, first_layer, io.len() as i32, io.as_ptr())
+        })
+    }
+
     /// `decode_layer` in the reference's operation order, bit for bit with
     /// its CPU path (f32 pools).
     pub fn decode_layer_exact(&mut self, layer: i32, q: DevicePtr<f32>, k: DevicePtr<f32>,

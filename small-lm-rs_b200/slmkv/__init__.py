@@ -89,6 +89,22 @@ class SlmConfig(C.Structure):
     ]
 
 
+class LayerIo(C.Structure):
+    """slm_layer_io: one decode layer's device buffers."""
+    _fields_ = [("query", C.c_void_p), ("keys", C.c_void_p), ("values", C.c_void_p),
+                ("out", C.c_void_p)]
+
+
+def layer_io_array(layers):
+    """A ctypes array of LayerIo for slm_batch_decode_layers from (query,
+    keys, values, out) tuples of device addresses (ints), built once for a
+    loop that reuses its buffers."""
+    arr = (LayerIo * len(layers))()
+    for i, (q, k, v, o) in enumerate(layers):
+        arr[i] = LayerIo(q, k, v, o)
+    return arr
+
+
 class SchedConfig(C.Structure):
     _fields_ = [("max_running", C.c_int32), ("max_prefill_tokens", C.c_int32)]
 
@@ -128,6 +144,7 @@ SIGNATURES = {
     "slm_attend_cached_query": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp]),
     "slm_batch_begin": (C.c_int, [_vp, _i32, _pi32, _pi32, _vp, C.POINTER(_vp)]),
     "slm_batch_decode_layer": (C.c_int, [_vp, _i32, _vp, _vp, _vp, _vp]),
+    "slm_batch_decode_layers": (C.c_int, [_vp, _i32, _i32, _vp]),
     "slm_batch_append_layer": (C.c_int, [_vp, _i32, _vp, _vp, _i32]),
     "slm_batch_prefill_attention": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
     "slm_batch_attention_exact": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
@@ -486,6 +503,7 @@ class _Fast:
         L = lib()
         self.begin = L.slm_batch_begin
         self.decode = L.slm_batch_decode_layer
+        self.decode_many = L.slm_batch_decode_layers
         self.end = L.slm_batch_end
         self.submit = L.slm_batch_submit
         self.wait = L.slm_batch_wait
@@ -555,6 +573,19 @@ class Batch:
         """decode_layer with raw device addresses (for callers that checked
         their tensors once, e.g. a serving loop's persistent buffers)."""
         rc = _fast.decode(self._h, layer, query, keys, values, out)
+        if rc:
+            self.pool.check(rc)
+
+    def decode_layers(self, first_layer: int, layers) -> None:
+        """slm_batch_decode_layers: decode_layer for layers first_layer, ...
+        with one (query, keys, values, out) tuple of tensors per layer, all
+        inputs ready; up to eight layers run as one launch."""
+        arr = layer_io_array([tuple(_ptr(t).value for t in io) for io in layers])
+        self.decode_layers_array(first_layer, len(layers), arr)
+
+    def decode_layers_array(self, first_layer: int, n_layers: int, arr) -> None:
+        """decode_layers with a prebuilt layer_io_array of device addresses."""
+        rc = _fast.decode_many(self._h, first_layer, n_layers, arr)
         if rc:
             self.pool.check(rc)
 

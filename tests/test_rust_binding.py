@@ -38,6 +38,7 @@ C_TO_RUST = {
     "const slm_model_config*": "*const SlmModelConfig",
     "const slm_sched_config*": "*const SlmSchedConfig",
     "slm_status": "i32",
+    "const slm_layer_io*": "*const SlmLayerIo",
 }
 
 
@@ -98,6 +99,18 @@ def _rust_struct(name):
 def test_repr_c_structs_match_the_header(c_name, rust_name):
     assert _c_struct(c_name) == _rust_struct(rust_name)
     assert "#[repr(C)]" in SYS.read_text().split(f"pub struct {rust_name}")[0][-120:]
+
+
+def test_layer_io_struct_matches_the_header():
+    src = _strip_c_comments(HEADER.read_text())
+    body = re.search(r"typedef struct slm_layer_io \{([^{}]*)\}\s*slm_layer_io;", src).group(1)
+    c_fields = [(C_TO_RUST[re.sub(r"\s*\*", "*", t.strip())], n)
+                for t, n in re.findall(r"([\w ]+\*)\s*(\w+);", body)]
+    rs = SYS.read_text()
+    rs_body = re.search(r"pub struct SlmLayerIo \{(.*?)\}", rs, flags=re.S).group(1)
+    rs_fields = [(t.strip(), n) for n, t in re.findall(r"pub (\w+): ([^,]+),", rs_body)]
+    assert c_fields == rs_fields
+    assert "#[repr(C)]" in rs.split("pub struct SlmLayerIo")[0][-120:]
 
 
 def test_constants_match_the_header():
