@@ -173,11 +173,12 @@ typedef struct slm_layer_io {
 /* slm_batch_decode_layer for layers first_layer .. first_layer + n_layers - 1,
  * io[i] for layer first_layer + i, when the inputs of all of them are ready
  * (forward_cached_token's cache part, attention.rs:794-810, per layer). The
- * layers share the batch's plan, so up to 8 of them run as one launch: each
- * warp of the grid takes its slice of the step's blocks in every layer in
- * turn, keeping its copies in flight across the layer boundaries. Results
- * equal the one-layer calls'. Every layer is checked before anything is
- * launched; a layer's output may not overlap another layer's buffers. */
+ * layers share the batch's plan, so with an f32 pool up to 8 of them run as
+ * one launch: each warp of the grid takes its slice of the step's blocks in
+ * every layer in turn, keeping its copies in flight across the layer
+ * boundaries (bf16 pools: one launch per layer). Results equal the one-layer
+ * calls'. Every layer is checked before anything is launched; a layer's
+ * output may not overlap another layer's buffers. */
 slm_status slm_batch_decode_layers(slm_batch* batch, int32_t first_layer, int32_t n_layers,
                                    const slm_layer_io* io);
 /* Append-only form (prompt prefill, attention.rs:863-868): keys/values are the

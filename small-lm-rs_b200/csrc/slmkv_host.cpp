@@ -1466,9 +1466,10 @@ slm_status slm_batch_decode_layers(slm_batch* b, int32_t first_layer, int32_t n_
                            "layer %d's output overlaps layer %d's buffers", first_layer + i,
                            first_layer + j);
     }
-  // One launch runs up to kMaxLaunchLayers layers when every warp's slice
-  // fits its 32-entry windows; otherwise one launch per layer.
-  const int32_t per = ctx->plan.fits_window ? ctx->launch_layers : 1;
+  // One launch runs up to kMaxLaunchLayers layers of an f32 pool when every
+  // warp's slice fits its 32-entry windows; otherwise one launch per layer.
+  const int32_t per =
+      (ctx->plan.fits_window && ctx->cfg.kv_dtype == SLM_KV_F32) ? ctx->launch_layers : 1;
   for (int32_t i = 0; i < n_layers; i += per) {
     const slm_status rc = decode_launch_layers(b, first_layer + i, std::min(per, n_layers - i), io + i);
     if (rc) return rc;

@@ -45,7 +45,9 @@ static_assert(sizeof(PairEntry) == 32, "PairEntry is read as two int4");
 // memory (each stage holds one 16-token block of K and V plus side inputs).
 // Twelve warps per SM hide the per-block latency best where they fit in
 // shared memory (measured on the batched decode microbench for f32 with at
-// most two query heads per KV head, 12 x 1 against 10 x 2 and 16 x 1; and on
+// most two query heads per KV head, 12 x 1 against 10 x 2 and 16 x 1, and
+// again with a step's 8 layers in one launch: 12 x 1 against 10 x 2, 11 x 2
+// and 8 x 2; and on
 // the scaled GQA shape for bf16 with four, 12 x 2 against 8 x 4, 8 x 2 and
 // 16 x 1). Larger query groups need more shared memory per warp.
 constexpr int decode_warps(int bf16, int group) {
@@ -93,7 +95,9 @@ struct PoolGeom {
 
 
 // ---- kernel launchers (slmkv_kernels.cu) ----------------------------------
-// Layers one decode launch may run (consecutive layers, one plan).
+// Layers one decode launch may run (consecutive layers, one plan; f32
+// pools: on the scaled GQA shape a bf16 launch of several layers measured
+// slower than one launch per layer, 36.7 against 34.4 us a layer).
 constexpr int kMaxLaunchLayers = 8;
 
 struct StreamDecodeLaunch {

@@ -462,7 +462,10 @@ struct StreamShape {
   static constexpr int kOffChunk = kOffBars + W * R * 8;
   static constexpr int kOffCnt = kOffChunk + W * R * 4;  // 3 x 2W merge-slot counters
   static constexpr int kOffPend = (kOffCnt + 6 * W * 4 + 15) / 16 * 16;
-  static constexpr int kSmem = kOffPend + W * R * 16 + (BF16 ? 1024 : 0);  // + alignment slack
+  // Per warp: its start record (2 x int4) and the cross-CTA pairs it has
+  // pending in the current layer (2 x int4), kept out of registers.
+  static constexpr int kOffRec = kOffPend + W * R * 16;
+  static constexpr int kSmem = kOffRec + W * 64 + (BF16 ? 1024 : 0);  // + alignment slack
   static_assert(kSmem <= 227 * 1024, "decode staging exceeds shared memory");
   static_assert(kChunk % 16 == 0 && kSide % 16 == 0 && kSlot % 16 == 0, "16-byte alignment");
 };
@@ -562,7 +565,7 @@ __device__ __forceinline__ void merge_partials(int n, int lane, Acc acc_at, Ml m
   }
 }
 
-template <int BF16, int G, int W, int R>
+template <int BF16, int G, int W, int R, bool ML>
 __global__ void __launch_bounds__(W * 32, 1)
     decode_stream_kernel(const __grid_constant__ StreamDecodeLaunch p) {
   using Sh = StreamShape<BF16, G, W, R>;
@@ -583,6 +586,7 @@ __global__ void __launch_bounds__(W * 32, 1)
   int* slot_wr = cta_cnt + 2 * W;
   int* slot_rd = cta_cnt + 4 * W;
   int4* side_pend = reinterpret_cast<int4*>(smem + Sh::kOffPend) + warp * R;
+  int4* rec = reinterpret_cast<int4*>(smem + Sh::kOffRec) + warp * 4;
 
   if (threadIdx.x < 6 * W) cta_cnt[threadIdx.x] = 0;
   const int gw = blockIdx.x * W + warp;
@@ -600,9 +604,13 @@ __global__ void __launch_bounds__(W * 32, 1)
     r1 = p.warp_start[2 * gw + 1];
   }
   const int g0 = r1.y, g1 = r1.z;
+  if (lane == 0) {  // read back at the layer boundaries
+    rec[0] = r0;
+    rec[1] = r1;
+  }
   // The warp's blocks over the launch: its slice of layer 0, then the same
   // slice of layer 1, and so on (the plan is the same for every layer).
-  const int total = p.n_layers * (g1 - g0);
+  const int total = ML ? p.n_layers * (g1 - g0) : g1 - g0;
   int cwin = g0;
   int cval = (g0 + lane < g1) ? p.chunks[g0 + lane] : 0;
 
@@ -640,29 +648,30 @@ __global__ void __launch_bounds__(W * 32, 1)
   // its RoPE row and, when this warp ends the pair, the new K/V rows.
   auto issue_side = [&](int stage, int seq, int head, int L, bool appends, int layer) {
     uint8_t* sd = sides + stage * Sh::kSide;
-    bulk_load(sd, p.q[layer] + (static_cast<size_t>(seq) * Hq + head * G) * D, G * D * 4,
+    bulk_load(sd, p.q[ML ? layer : 0] + (static_cast<size_t>(seq) * Hq + head * G) * D, G * D * 4,
               &bars[stage]);
     if (p.fused)
       bulk_load(sd + Sh::kSideCs, p.g.rope + static_cast<size_t>(L - 1) * (D / 2), (D / 2) * 8,
                 &bars[stage]);
     if (appends) {
       const size_t row = (static_cast<size_t>(seq) * Hkv + head) * D;
-      bulk_load(sd + Sh::kSideKn, p.k_new[layer] + row, D * 4, &bars[stage]);
-      bulk_load(sd + Sh::kSideVn, p.v_new[layer] + row, D * 4, &bars[stage]);
+      bulk_load(sd + Sh::kSideKn, p.k_new[ML ? layer : 0] + row, D * 4, &bars[stage]);
+      bulk_load(sd + Sh::kSideVn, p.v_new[ML ? layer : 0] + row, D * 4, &bars[stage]);
     }
   };
   // Arms the next stage and copies its K/V chunks; with defer_side the side
   // copies are recorded in side_pend and issued later on the same barrier
   // (its expected byte count already includes them).
   auto issue = [&](int stage, bool defer_side) {
-    if (pg == g1) {  // the producer enters the next layer: the slice again
+    if (ML && pg == g1) {  // the producer enters the next layer: the slice again
       ++pl;
       pg = g0;
-      pp = r0.x;
-      pp_seq = r0.y;
-      pp_head = r0.z;
-      pp_L = r0.w;
-      pp_end = r1.x;
+      const int4 a = rec[0];
+      pp = a.x;
+      pp_seq = a.y;
+      pp_head = a.z;
+      pp_L = a.w;
+      pp_end = rec[1].x;
       pp_first = g0;
       if (cwin != g0) {  // the chunk window is the producer's alone
         cwin = g0;
@@ -757,8 +766,8 @@ __global__ void __launch_bounds__(W * 32, 1)
   int cl = 0;  // the consumer's layer (of the launch)
 
   // Cross-CTA pairs of the current layer, merged after its last block (at most two).
+  // rec[2 + k]: {pair, global slot base, n CTA segs, row} of pending pair k.
   int npend = 0;
-  int4 pend0 = make_int4(0, 0, 0, 0), pend1 = pend0;  // {pair, global slot base, n CTA segs, row}
 
   for (int v = 0, g = g0; v < total; ++v) {
     const int stage = v % R;
@@ -894,7 +903,7 @@ __global__ void __launch_bounds__(W * 32, 1)
         }
         __syncwarp();
       }
-      float* out = p.out[cl];
+      float* out = p.out[ML ? cl : 0];
       const size_t orow = static_cast<size_t>(cur.seq) * Hq + cur.head * G;
       if (cur.nseg == 1) {
 #pragma unroll
@@ -931,7 +940,7 @@ __global__ void __launch_bounds__(W * 32, 1)
           uint8_t* mine = slots + my * Sh::kSlot;
           // A slot is written again (the same pair in a later layer of the
           // launch) only after the merge that read its last partial is done.
-          if (lane == 0) {
+          if (ML && lane == 0) {
             const int written = slot_wr[my];
             const uint64_t t0 = globaltimer_ns();
             for (uint32_t i = 0; *reinterpret_cast<volatile int*>(&slot_rd[my]) != written; ++i)
@@ -952,7 +961,7 @@ __global__ void __launch_bounds__(W * 32, 1)
           __syncwarp();
           int last = 0;
           if (lane == 0) {
-            slot_wr[my] += 1;
+            if (ML) slot_wr[my] += 1;
             last = (atomicAdd(&cta_cnt[seg_slot(ka)], 1) == n_in - 1);
           }
           last = __shfl_sync(kFull, last, 0);
@@ -970,7 +979,7 @@ __global__ void __launch_bounds__(W * 32, 1)
             // Every read of the slots is done: reset the arrivals, release them.
             __threadfence_block();
             __syncwarp();
-            if (lane == 0) {
+            if (ML && lane == 0) {
               cta_cnt[seg_slot(ka)] = 0;
               __threadfence_block();
               for (int s = 0; s < n_in; ++s) atomicAdd(&slot_rd[seg_slot(ka + s)], 1);
@@ -999,8 +1008,7 @@ __global__ void __launch_bounds__(W * 32, 1)
               if (lane == 0) p.part_ml[gslot * G + g2] = make_float2(Mo[g2], Lo[g2]);
             }
             const int4 e = make_int4(pc, cur.part_base, n_cta, static_cast<int>(orow));
-            if (npend == 0) pend0 = e;
-            else pend1 = e;
+            if (lane == 0) rec[2 + npend] = e;
             ++npend;
           }
         }
@@ -1026,6 +1034,7 @@ __global__ void __launch_bounds__(W * 32, 1)
       int* counters = p.counters + static_cast<size_t>(cl) * p.counter_stride;
       asm volatile("fence.acq_rel.gpu;" ::: "memory");
       __syncwarp();
+      const int4 pend0 = rec[2], pend1 = rec[3];
       int lastmask = 0;
       if (lane == 0) {
         const int prev0 = atomicAdd(&counters[pend0.x], 1);
@@ -1042,7 +1051,7 @@ __global__ void __launch_bounds__(W * 32, 1)
       lastmask = __shfl_sync(kFull, lastmask, 0);
       if (lastmask != 0) {
         asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        float* out = p.out[cl];
+        float* out = p.out[ML ? cl : 0];
         const size_t pbase = static_cast<size_t>(cl) * p.part_stride;
         for (int k = 0; k < npend; ++k) {
           if (!((lastmask >> k) & 1)) continue;
@@ -1067,10 +1076,10 @@ __global__ void __launch_bounds__(W * 32, 1)
       }
       npend = 0;
     }
-    if (v + 1 < total) {  // the consumer enters the next layer: the slice again
+    if (ML && v + 1 < total) {  // the consumer enters the next layer: the slice again
       ++cl;
       g = g0;
-      pc = r0.x;
+      pc = rec[0].x;
       if (pc < pwin || pc - pwin >= 32) load_window(pc);
       cur = pair_from_window(pa, pb, pc - pwin);
       seg_end = min(g1, cur.blk_begin + cur.nblk);
@@ -1090,8 +1099,12 @@ cudaError_t launch_decode_t(const StreamDecodeLaunch& p, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   static unsigned long long configured = 0;  // one bit per device
   if (dev < 64 && !(configured & (1ull << dev))) {
-    e = cudaFuncSetAttribute(decode_stream_kernel<BF16, G, W, R>,
+    e = cudaFuncSetAttribute(decode_stream_kernel<BF16, G, W, R, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::kSmem);
+    if constexpr (!BF16)
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(decode_stream_kernel<BF16, G, W, R, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::kSmem);
     if (e != cudaSuccess) return e;
     configured |= (1ull << dev);
   }
@@ -1105,7 +1118,13 @@ cudaError_t launch_decode_t(const StreamDecodeLaunch& p, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_stream_kernel<BF16, G, W, R>, p);
+  if constexpr (!BF16) {
+    if (p.n_layers > 1)
+      return cudaLaunchKernelEx(&cfg, decode_stream_kernel<BF16, G, W, R, true>, p);
+  } else {
+    if (p.n_layers > 1) return cudaErrorInvalidValue;  // f32 pools only
+  }
+  return cudaLaunchKernelEx(&cfg, decode_stream_kernel<BF16, G, W, R, false>, p);
 }
 
 // ---------------------------------------------------------------------------
