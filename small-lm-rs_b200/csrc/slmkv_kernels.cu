@@ -304,6 +304,74 @@ __device__ __forceinline__ void block_softmax_pv(const void* __restrict__ vb, fl
   __syncwarp();  // pbuf is rewritten by the next block
 }
 
+// Maximum of v over the warp in one instruction (sm_100a).
+__device__ __forceinline__ float warp_max(float v) {
+  float r;
+  asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off);
+  return v;
+}
+
+// block_softmax_pv for f32 V as the decode kernel runs it: the block's
+// maximum in one warp reduction, and the row sum l kept per lane (lane t < 16
+// holds its tokens' share, lanes 16-31 hold 0) so that no block waits on a
+// sum reduction; warp_sum(l) at the end of the segment gives the total.
+template <int G>
+__device__ __forceinline__ void block_softmax_pv_lanesum(const float* __restrict__ vb, float* pbuf,
+                                                         int lane, int nvalid, const float (&sc)[G],
+                                                         float (&m)[G], float (&l)[G],
+                                                         float2 (&acc)[G]) {
+  const int t = lane & 15;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float s = (t < nvalid) ? sc[g] * kScaleLog2 : -INFINITY;
+    const float mnew = fmaxf(m[g], warp_max(s));  // finite: nvalid >= 1
+    const float corr = fast_exp2(m[g] - mnew);
+    const float p = fast_exp2(s - mnew);
+    if (lane < 16) pbuf[g * 16 + t] = p;
+    l[g] = fmaf(l[g], corr, (lane < 16) ? p : 0.f);
+    acc[g].x *= corr;
+    acc[g].y *= corr;
+    m[g] = mnew;
+  }
+  __syncwarp();
+  const float2* v2 = reinterpret_cast<const float2*>(vb);
+  if (nvalid == kBlockTokens) {
+#pragma unroll
+    for (int t4 = 0; t4 < kBlockTokens; t4 += 4) {
+      const float2 v0 = v2[t4 * (D / 2) + lane], v1 = v2[(t4 + 1) * (D / 2) + lane];
+      const float2 w2 = v2[(t4 + 2) * (D / 2) + lane], w3 = v2[(t4 + 3) * (D / 2) + lane];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float4 p4 = *reinterpret_cast<const float4*>(pbuf + g * 16 + t4);
+        acc[g].x = fmaf(p4.x, v0.x, acc[g].x);
+        acc[g].y = fmaf(p4.x, v0.y, acc[g].y);
+        acc[g].x = fmaf(p4.y, v1.x, acc[g].x);
+        acc[g].y = fmaf(p4.y, v1.y, acc[g].y);
+        acc[g].x = fmaf(p4.z, w2.x, acc[g].x);
+        acc[g].y = fmaf(p4.z, w2.y, acc[g].y);
+        acc[g].x = fmaf(p4.w, w3.x, acc[g].x);
+        acc[g].y = fmaf(p4.w, w3.y, acc[g].y);
+      }
+    }
+  } else {
+    for (int tt = 0; tt < nvalid; ++tt) {
+      const float2 vv = v2[tt * (D / 2) + lane];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pt = pbuf[g * 16 + tt];
+        acc[g].x = fmaf(pt, vv.x, acc[g].x);
+        acc[g].y = fmaf(pt, vv.y, acc[g].y);
+      }
+    }
+  }
+  __syncwarp();  // pbuf is rewritten by the next block
+}
+
 // ---------------------------------------------------------------------------
 // bf16 K/V blocks on the tensor cores (warp-level mma.m16n8k16, f32
 // accumulate). The block's K and V chunks are staged by TMA with the 128-byte
@@ -868,7 +936,8 @@ __global__ void __launch_bounds__(W * 32, 1)
       float sc[G];
       block_scores_f32<G>(reinterpret_cast<const float*>(kb), qs, lane, sc);
       bad |= scores_bad<G>(sc, (lane & 15) < nvalid);
-      block_softmax_pv<G, false>(vb, pbuf, lane, nvalid, sc, m, l, acc);
+      block_softmax_pv_lanesum<G>(reinterpret_cast<const float*>(vb), pbuf, lane, nvalid, sc, m,
+                                  l, acc);
     }
     if (pv < total) {
       // The stage (and its side buffer) were read, maybe written, through
@@ -883,6 +952,10 @@ __global__ void __launch_bounds__(W * 32, 1)
       if (__any_sync(kFull, bad)) {
         if (lane == 0 && p.status) atomicOr(&p.status[cur.seq], kStatusNonFiniteScore);
         bad = false;
+      }
+      if constexpr (!BF16) {
+#pragma unroll
+        for (int g2 = 0; g2 < G; ++g2) l[g2] = warp_sum(l[g2]);  // the lanes' shares
       }
       if constexpr (BF16) {
         // Back to one float2 per lane and head (dims 2*lane, 2*lane+1): the
