@@ -434,7 +434,8 @@ __device__ __forceinline__ void load_q_frags(const float* qs, int lane, uint32_t
 // One block: scores on the tensor cores, the online-softmax update for this
 // lane's head, then P·V on the tensor cores. kaddr/vaddr: shared addresses of
 // the swizzled K and V chunks; tokens at or past nvalid are masked (their V
-// rows must be finite: the caller zeroes them).
+// rows must be finite: the caller zeroes them). l_row accumulates this lane's
+// share of the row sum: the caller adds the quad's shares at the segment end.
 __device__ __forceinline__ void block_mma_bf16(uint32_t kaddr, uint32_t vaddr, int lane, int nvalid,
                                                const uint32_t (&qa)[4][4], float& m_row,
                                                float& l_row, float (&o)[8][4], bool& bad) {
@@ -476,9 +477,7 @@ __device__ __forceinline__ void block_mma_bf16(uint32_t kaddr, uint32_t vaddr, i
       pr[j][e] = fast_exp2(sc[j][e] - mnew);
       ps += pr[j][e];
     }
-  ps += __shfl_xor_sync(kFull, ps, 1);
-  ps += __shfl_xor_sync(kFull, ps, 2);
-  l_row = fmaf(l_row, corr, ps);
+  l_row = fmaf(l_row, corr, ps);  // this lane's share; the quad's sum at the segment's end
   m_row = mnew;
   uint32_t pa0, pa1, pa2, pa3;
   split_bf16x2(pr[0][0], pr[0][1], pa0, pa1);
@@ -968,6 +967,8 @@ __global__ void __launch_bounds__(W * 32, 1)
                 make_float2(o[n][0] + o[n][2], o[n][1] + o[n][3]);
         }
         __syncwarp();
+        l_row += __shfl_xor_sync(kFull, l_row, 1);  // the quad's shares of its row sum
+        l_row += __shfl_xor_sync(kFull, l_row, 2);
 #pragma unroll
         for (int g2 = 0; g2 < G; ++g2) {
           acc[g2] = reinterpret_cast<const float2*>(qs + g2 * D)[lane];
