@@ -822,6 +822,21 @@ slm_status ctx_fail(slm_ctx* c, slm_status code, const char* msg) { return fail(
 // =============================================================================
 // C ABI
 // =============================================================================
+#ifdef SLMKV_TIMELINE
+// Profiling builds only (not in the public header): points every instrumented
+// kernel at a device buffer of `cap` TimelineRec records and a device counter
+// (null buffer: off).
+extern "C" int slmkv_timeline_set(void* d_buf, void* d_count, uint32_t cap) {
+  auto* b = static_cast<slmkv::TimelineRec*>(d_buf);
+  auto* n = static_cast<unsigned*>(d_count);
+  cudaError_t e = slmkv::timeline_set_kernels(b, n, cap);
+  if (e == cudaSuccess) e = slmkv::timeline_set_model(b, n, cap);
+  if (e == cudaSuccess) e = slmkv::timeline_set_rowgemm(b, n, cap);
+  if (e == cudaSuccess) e = slmkv::timeline_set_prefill_tc(b, n, cap);
+  return static_cast<int>(e);
+}
+#endif
+
 extern "C" {
 
 slm_status slm_create(const slm_config* config, int32_t device, slm_ctx** out) {
@@ -1391,10 +1406,12 @@ slm_status decode_layer_check(slm_batch* b, int32_t layer, const float* d_query,
 
 // Launches the decode of layers first .. first + nl - 1 (io[i] for layer
 // first + i) as one kernel, then advances those layers' lengths.
-slm_status decode_launch_layers(slm_batch* b, int32_t first, int32_t nl, const slm_layer_io* io) {
+slm_status decode_launch_layers(slm_batch* b, int32_t first, int32_t nl, const slm_layer_io* io,
+                                uint32_t* out_bf16 = nullptr) {
   slm_ctx* ctx = b->ctx;
   StreamDecodeLaunch p = decode_launch(ctx, first, b->dev, ctx->plan);
   p.n_layers = nl;
+  p.out_bf16 = nl == 1 ? out_bf16 : nullptr;
   for (int32_t i = 0; i < nl; ++i) {
     p.q[i] = io[i].query;
     p.k_new[i] = io[i].keys;
@@ -1432,6 +1449,20 @@ slm_status slm_batch_decode_layer(slm_batch* b, int32_t layer, const float* d_qu
   if (rc) return rc;
   const slm_layer_io io{d_query, d_keys, d_values, d_out};
   return decode_launch_layers(b, layer, 1, &io);
+}
+
+extern "C++" {
+namespace slmkv {
+slm_status batch_decode_layer_bf16(slm_batch* b, int32_t layer, const float* d_query,
+                                   const float* d_keys, const float* d_values, float* d_out,
+                                   uint32_t* d_out_bf16) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_status rc = decode_layer_check(b, layer, d_query, d_keys, d_values, d_out);
+  if (rc) return rc;
+  const slm_layer_io io{d_query, d_keys, d_values, d_out};
+  return decode_launch_layers(b, layer, 1, &io, d_out_bf16);
+}
+}  // namespace slmkv
 }
 
 slm_status slm_batch_decode_layers(slm_batch* b, int32_t first_layer, int32_t n_layers,

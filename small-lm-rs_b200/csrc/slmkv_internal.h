@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include "slmkv.h"
+#include "slmkv_timeline.h"
 
 namespace slmkv {
 
@@ -116,6 +117,7 @@ struct StreamDecodeLaunch {
   const float* k_new[kMaxLaunchLayers];  // [n, Hkv, d] (fused mode) or null
   const float* v_new[kMaxLaunchLayers];
   float* out[kMaxLaunchLayers];          // [n, Hq, d]
+  uint32_t* out_bf16;  // one-layer launches: out rounded to bf16 as well (or null)
   float* part_acc;        // [layer of the launch][part_stride slots][G][d]
   float2* part_ml;        // [layer][part_stride][G] (running max in the exp2 domain, sum)
   int32_t part_stride;    // split-K partial slots per layer of the launch
@@ -222,6 +224,11 @@ struct BatchRows {
   const SeqEntry* d_seqs; // [n_seq], device: row_offset, count, base per sequence
 };
 BatchRows batch_rows(const slm_batch* b);
+// slm_batch_decode_layer that also writes its output rounded to bf16
+// (d_out_bf16: [n, q_heads * d / 2] bf16 pairs), for the next projection.
+slm_status batch_decode_layer_bf16(slm_batch* b, int32_t layer, const float* d_query,
+                                   const float* d_keys, const float* d_values, float* d_out,
+                                   uint32_t* d_out_bf16);
 slm_ctx* batch_ctx(const slm_batch* b);
 int32_t* ctx_error_word(slm_ctx* c);
 void ctx_count_launches(slm_ctx* c, int32_t n);

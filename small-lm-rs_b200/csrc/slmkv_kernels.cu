@@ -635,6 +635,7 @@ __device__ __forceinline__ void merge_partials(int n, int lane, Acc acc_at, Ml m
 template <int BF16, int G, int W, int R, bool ML>
 __global__ void __launch_bounds__(W * 32, 1)
     decode_stream_kernel(const __grid_constant__ StreamDecodeLaunch p) {
+  SLMKV_TL(ML ? kTlDecodeLayers : kTlDecode);
   using Sh = StreamShape<BF16, G, W, R>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // bf16 stages are TMA boxes with the 128-byte swizzle: 1024-byte aligned.
@@ -816,6 +817,13 @@ __global__ void __launch_bounds__(W * 32, 1)
   } else {
     for (int s = 0; s < R && pv < total; ++s) issue(s, false);
   }
+  // An output row (one query head of one sequence): f32, and for a one-layer
+  // launch that asks for it also as bf16 (linear.rs:14-23 rounding), the next
+  // projection's operand.
+  auto store_out = [&](float* out, size_t row, float2 v) {
+    reinterpret_cast<float2*>(out + row * D)[lane] = v;
+    if (!ML && p.out_bf16) p.out_bf16[row * (D / 2) + lane] = pack_bf16x2(v.x, v.y);
+  };
   // ---- consumer --------------------------------------------------------------
   PairFields cur = pair_from_window(pa, pb, pc - pwin);
   float m[G], l[G];
@@ -983,8 +991,7 @@ __global__ void __launch_bounds__(W * 32, 1)
 #pragma unroll
         for (int g2 = 0; g2 < G; ++g2) {
           const float inv = 1.0f / l[g2];
-          reinterpret_cast<float2*>(out + (orow + g2) * D)[lane] =
-              make_float2(acc[g2].x * inv, acc[g2].y * inv);
+          store_out(out, orow + g2, make_float2(acc[g2].x * inv, acc[g2].y * inv));
         }
       } else {
         // Warps [ka, kb] of this CTA hold the pair's segments here; they merge
@@ -1066,8 +1073,7 @@ __global__ void __launch_bounds__(W * 32, 1)
 #pragma unroll
             for (int g2 = 0; g2 < G; ++g2) {
               const float inv = 1.0f / Lo[g2];
-              reinterpret_cast<float2*>(out + (orow + g2) * D)[lane] =
-                  make_float2(A[g2].x * inv, A[g2].y * inv);
+              store_out(out, orow + g2, make_float2(A[g2].x * inv, A[g2].y * inv));
             }
           } else {
             // This CTA's share of a pair that spans CTAs: one global partial
@@ -1143,8 +1149,7 @@ __global__ void __launch_bounds__(W * 32, 1)
 #pragma unroll
           for (int g2 = 0; g2 < G; ++g2) {
             const float inv = 1.0f / Lo[g2];
-            reinterpret_cast<float2*>(out + (static_cast<size_t>(e.w) + g2) * D)[lane] =
-                make_float2(A[g2].x * inv, A[g2].y * inv);
+            store_out(out, static_cast<size_t>(e.w) + g2, make_float2(A[g2].x * inv, A[g2].y * inv));
           }
         }
       }
@@ -1233,6 +1238,7 @@ constexpr int kAppendRows = 16 * kAppendRowsPerGroup;  // 256 threads = 16 group
 
 template <int BF16>
 __global__ void __launch_bounds__(256) append_kernel(const AppendLaunch p) {
+  SLMKV_TL(kTlAppend);
   const int Hkv = p.g.kv_heads;
   const int64_t n_rows = static_cast<int64_t>(p.total_tokens) * Hkv;
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kAppendRows;
@@ -1299,6 +1305,7 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendLaunch p) {
 // ---------------------------------------------------------------------------
 template <int BF16>
 __global__ void __launch_bounds__(256) gather_kernel(const GatherLaunch p) {
+  SLMKV_TL(kTlGather);
   const int Hkv = p.g.kv_heads;
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
   const int l16 = threadIdx.x & 15;
@@ -1330,6 +1337,7 @@ __global__ void __launch_bounds__(256) gather_kernel(const GatherLaunch p) {
 // ---------------------------------------------------------------------------
 template <int BF16, int G>
 __global__ void __launch_bounds__(128) prefill_kernel(const PrefillLaunch p) {
+  SLMKV_TL(kTlPrefill);
   __shared__ __align__(16) float qs[kBlockTokens * G * D];
   __shared__ __align__(16) float kbuf[kBlockTokens * D];
   __shared__ __align__(16) float vbuf[kBlockTokens * D];
@@ -1470,6 +1478,7 @@ __host__ __device__ inline ExactSmem exact_smem_layout(int max_ctx, int stages) 
 
 __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const PrefillLaunch p,
                                                                         int stages) {
+  SLMKV_TL(kTlExact);
   extern __shared__ __align__(128) uint8_t sm_exact[];
   const ExactSmem lay = exact_smem_layout(p.max_ctx, stages);
   uint8_t* ring = sm_exact + lay.ring;
@@ -1666,6 +1675,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
 // ---------------------------------------------------------------------------
 __global__ void apply_updates_kernel(const PoolGeom g, const TableUpdate* __restrict__ up,
                                      int32_t nu, const CopyJob* __restrict__ cp, int32_t nc) {
+  SLMKV_TL(kTlApply);
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = tid; i < nu; i += stride) {
@@ -1808,5 +1818,7 @@ cudaError_t launch_apply_updates(const PoolGeom& g, const TableUpdate* updates, 
                                                                           copies, n_copies);
   return cudaGetLastError();
 }
+
+SLMKV_TL_SETTER(timeline_set_kernels)
 
 }  // namespace slmkv

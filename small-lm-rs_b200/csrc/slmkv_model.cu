@@ -74,6 +74,7 @@ cudaError_t launch_chained(void (*kernel)(Params...), dim3 grid, dim3 block, siz
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ table,
                              int32_t vocab, int32_t hidden, float* __restrict__ x,
                              int32_t* __restrict__ err) {
+  SLMKV_TL(kTlEmbed);
   wait_previous_kernel();
   const int r = blockIdx.x;
   int32_t id = ids[r];
@@ -106,8 +107,20 @@ __global__ void __launch_bounds__(kNormThreads)
     rmsnorm_kernel(const float* __restrict__ x, int32_t rows, int32_t hidden, const float* __restrict__ w,
                    float eps, uint32_t* __restrict__ out_bf16, float* __restrict__ out_f32,
                    const SeqEntry* __restrict__ seqs) {
-  wait_previous_kernel();
+  SLMKV_TL(kTlNorm);
   const int row = blockIdx.x, tid = threadIdx.x;
+  // The scale vector is a weight (no kernel writes it): fetched while the
+  // previous kernel finishes, before the next kernel's weight copies queue
+  // up in front of it.
+  const int n4w = hidden / 4;
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  float4 g4[kNormVec];
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = tid + j * kNormThreads;
+    g4[j] = i < n4w ? wr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  wait_previous_kernel();
   if (row >= rows) return;
   const int src_row = seqs ? seqs[row].row_offset + seqs[row].count - 1 : row;
   const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(src_row) * hidden);
@@ -135,12 +148,11 @@ __global__ void __launch_bounds__(kNormThreads)
 #pragma unroll
   for (int k = 0; k < kNormThreads / 32; ++k) s += part[k];
   const float inv = 1.f / sqrtf(__fdiv_rn(s, static_cast<float>(hidden)) + eps);
-  const float4* wr = reinterpret_cast<const float4*>(w);
 #pragma unroll
   for (int j = 0; j < kNormVec; ++j) {
     const int i = tid + j * kNormThreads;
     if (i >= n4) break;
-    const float4 g = wr[i];
+    const float4 g = g4[j];
     const float a = __fmul_rn(__fmul_rn(v[j].x, inv), g.x), b = __fmul_rn(__fmul_rn(v[j].y, inv), g.y);
     const float c = __fmul_rn(__fmul_rn(v[j].z, inv), g.z), d = __fmul_rn(__fmul_rn(v[j].w, inv), g.w);
     if (out_bf16)
@@ -153,6 +165,7 @@ __global__ void __launch_bounds__(kNormThreads)
 
 // fp32 rows -> bf16 rows (round to nearest even), 4 values a thread.
 __global__ void round_bf16_kernel(const float4* __restrict__ in, size_t n4, uint2* __restrict__ out) {
+  SLMKV_TL(kTlRound);
   wait_previous_kernel();
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -171,6 +184,7 @@ __device__ __forceinline__ float situ_sigmoid(float v) {
 // (the down projection's rounded operand). gu rows are [gate | up].
 __global__ void situ_kernel(const float* __restrict__ gu, int32_t rows, int32_t inter, float beta_gate,
                             float beta_up, uint32_t* __restrict__ h) {
+  SLMKV_TL(kTlSitu);
   const size_t pairs = static_cast<size_t>(rows) * (inter / 2);
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < pairs;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -267,6 +281,7 @@ __device__ __forceinline__ void cp_async_wait() {
 // CTA may hold fewer).
 template <int MODE, int NR>
 __global__ void __launch_bounds__(kProjThreads) proj_kernel(const ProjArgs a) {
+  SLMKV_TL(kTlProj);
   constexpr int NM = proj_mats<MODE>();
   constexpr int S = proj_stages<MODE>();
   extern __shared__ __align__(16) uint8_t smem[];
@@ -437,6 +452,7 @@ __device__ __forceinline__ void head_halve(float (&a)[32], int lane, int o) {
 __global__ void __launch_bounds__(kHeadThreads, 2) head_kernel(const float* __restrict__ x, int32_t rows, int32_t H,
                                                             const float* __restrict__ emb, int32_t V,
                                                             float* __restrict__ logits) {
+  SLMKV_TL(kTlHead);
   wait_previous_kernel();
   extern __shared__ float4 head_x[];  // [kHeadRows][H / 4]
   const int n4 = H / 4;
@@ -498,6 +514,7 @@ constexpr int kArgmaxThreads = 256;
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits,
                                                                 int32_t vocab, int32_t* __restrict__ next,
                                                                 int32_t* __restrict__ err) {
+  SLMKV_TL(kTlArgmax);
   wait_previous_kernel();
   const float* row = logits + static_cast<size_t>(blockIdx.x) * vocab;
   float best = -INFINITY;
@@ -578,6 +595,7 @@ struct slm_model {
   float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *gu = nullptr;
   uint32_t* xb = nullptr;  // bf16 pairs, [rows, max(H, I) / 2]
   uint32_t* hb = nullptr;  // bf16 pairs, [rows, I / 2]: the row GEMMs' SiTU-GLU output
+
   float *xf = nullptr, *logits = nullptr;
 };
 
@@ -692,6 +710,7 @@ int32_t proj1_cols(int32_t K) {
 
 template <int MODE>
 __global__ void __launch_bounds__(128) proj1_kernel(const ProjArgs a) {
+  SLMKV_TL(kTlProj1);
   constexpr int NM = proj_mats<MODE>();
   extern __shared__ __align__(16) uint8_t smem[];
   const int K = a.K, C = a.cols, NT = NM * C;
@@ -883,11 +902,20 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       ++launches;
       a.y0 = m->q, a.y1 = m->k, a.y2 = m->v;
       if ((rc = gemm(kRowQKV, Ly.tm_qkv, m->xb, H, nqkv))) return rc;
-      if ((rc = cache_step(l))) return rc;
-      const size_t n4 = static_cast<size_t>(rows) * H / 4;
-      launched(launch_chained(round_bf16_kernel, dim3(grid_for(n4, 256)), dim3(256), 0, s,
-                              reinterpret_cast<const float4*>(m->att), n4, reinterpret_cast<uint2*>(m->xb)));
-      ++launches;
+      if (!prefill && !exact_attention) {
+        // the decode kernel also writes the attention rows rounded to bf16,
+        // the output projection's operand (no separate rounding launch)
+        if ((rc = batch_decode_layer_bf16(b, l, m->q, m->k, m->v, m->att,
+                                          reinterpret_cast<uint32_t*>(m->xb))))
+          return rc;
+      } else {
+        if ((rc = cache_step(l))) return rc;
+        const size_t n4 = static_cast<size_t>(rows) * H / 4;
+        launched(launch_chained(round_bf16_kernel, dim3(grid_for(n4, 256)), dim3(256), 0, s,
+                                reinterpret_cast<const float4*>(m->att), n4,
+                                reinterpret_cast<uint2*>(m->xb)));
+        ++launches;
+      }
       a.y0 = m->x, a.y1 = a.y2 = nullptr;
       if ((rc = gemm(kRowO, Ly.tm_o, m->xb, H, H))) return rc;
       launched(launch_chained(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, s,
@@ -957,6 +985,8 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
 }
 
 }  // namespace
+SLMKV_TL_SETTER(timeline_set_model)
+
 }  // namespace slmkv
 
 using namespace slmkv;

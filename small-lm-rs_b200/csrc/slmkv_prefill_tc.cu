@@ -360,6 +360,7 @@ __device__ __forceinline__ CtaWork cta_work(const PrefillLaunch& p) {
 template <int G, int QT>
 __global__ void __launch_bounds__(WsCfg<QT>::kThreads, WsCfg<QT>::kCtasPerSm)
     prefill_ws_kernel(const __grid_constant__ PrefillLaunch p) {
+  SLMKV_TL(kTlPrefillTc);
   using Cfg = WsCfg<QT>;
   static_assert(ws_smem<QT>() <= 227 * 1024 &&
                     Cfg::kCtasPerSm * (ws_smem<QT>() + 1024) <= 228 * 1024,
@@ -850,5 +851,7 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& p, cudaStream_t s) {
     default: return cudaErrorInvalidValue;
   }
 }
+
+SLMKV_TL_SETTER(timeline_set_prefill_tc)
 
 }  // namespace slmkv

@@ -141,6 +141,7 @@ __device__ __forceinline__ float rg_situ_sigmoid(float v) {  // situ_glu.rs:131-
 
 template <int MODE, int RT>
 __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_constant__ RowGemmLaunch p) {
+  SLMKV_TL(kTlRowGemm + MODE);
   using Cfg = RgCfg<RT>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t rg_smem_raw[];
@@ -196,6 +197,7 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
         rg_tma(stage_a(i) + kRgABytes / 2, &p.tmap_w, xa1, ky, fb);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
+      SLMKV_TL_MARK(kTlRowGemmWaited + MODE);
       for (int i = 0; i < pre; ++i) rg_tma(stage_b(i), &p.tmap_x, (ch0 + i) * kRgChunk, yb, full0 + 8 * i);
       int issued = pre;
       for (int i = pre; i < nch; ++i) {
@@ -253,6 +255,7 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
   if (lane == 0) ok = rg_wait(done, 0);
   ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
   if (!ok && lane == 0) raise_abort();
+  if (warp == 0) SLMKV_TL_MARK(kTlRowGemmMmaDone + MODE);
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   __syncthreads();
   const bool run = *reinterpret_cast<volatile int32_t*>(&aborted) == 0;  // CTA-uniform
@@ -299,10 +302,13 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
   };
   if (run) {
     if (MODE == kRowGU) {
-      const int col = kRgChunk * col_tile + m;
-      if (m < 64 && col < p.I) {
-        for (int r = split; r < nr; r += splits) {
-          const float gv = reduced(r, m), u = reduced(r, m + 64);
+      // every thread: tile column c (gate c, up c + 64) for every other of
+      // this CTA's rows, so all 128 threads share the SiTU-GLU work
+      const int c = m & 63, half = m >> 6;
+      const int col = kRgChunk * col_tile + c;
+      if (col < p.I) {
+        for (int r = split + half * splits; r < nr; r += 2 * splits) {
+          const float gv = reduced(r, c), u = reduced(r, c + 64);
           const float ga =
               __fmul_rn(__fmul_rn(p.beta_gate, libm::slm_tanhf(__fdiv_rn(gv, p.beta_gate))), rg_situ_sigmoid(gv));
           const float ua = __fmul_rn(p.beta_up, libm::slm_tanhf(__fdiv_rn(u, p.beta_up)));
@@ -431,5 +437,7 @@ cudaError_t launch_row_gemm(int mode, RowGemmLaunch p, const RowGemmPlan& q, cud
     default: return launch_mode<kRowDown>(p, q.rt, grid, s);
   }
 }
+
+SLMKV_TL_SETTER(timeline_set_rowgemm)
 
 }  // namespace slmkv
