@@ -808,6 +808,7 @@ __global__ void __launch_bounds__(W * 32, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();  // the only CTA-wide barrier; the warps are independent after it
   if (!active) return;
+  SLMKV_TL_MARK(kTlDecodeWaited);
   if (p.early_kv) {
     if (lane == 0)
       for (int s = 0; s < pv; ++s) {
@@ -1107,6 +1108,7 @@ __global__ void __launch_bounds__(W * 32, 1)
     }
 
     // ---- end of this layer's slice: pairs that span CTAs ----------------------
+    SLMKV_TL_MARK(kTlDecodeSliceDone);
     // The last CTA to arrive merges the partials. Release this warp's
     // partials, then arrive on each pair's counter (both arrivals in flight
     // together); the next layer's first copies are already in flight.
