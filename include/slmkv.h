@@ -181,6 +181,21 @@ typedef struct slm_layer_io {
  * output may not overlap another layer's buffers. */
 slm_status slm_batch_decode_layers(slm_batch* batch, int32_t first_layer, int32_t n_layers,
                                    const slm_layer_io* io);
+/* slm_batch_decode_layers for a caller whose step inputs and outputs are in
+ * host memory (an engine's host tensors, as forward_cached_token holds them,
+ * attention.rs:772-779): h_query [n_layers][n][q_heads][d], h_keys and
+ * h_values [n_layers][n][kv_heads][d] (unrotated), h_out
+ * [n_layers][n][q_heads][d]. The inputs are copied into the context's own
+ * device staging (allocated at the first call, grown when a call needs more),
+ * the layers run as slm_batch_decode_layers, and the outputs are copied back
+ * ahead of the step's statuses: h_out is complete when slm_batch_end or
+ * slm_batch_wait returns for this batch, and the host buffers must stay valid
+ * until then. Host buffers should be pinned (cudaHostAlloc, cudaHostRegister)
+ * for the copies to overlap the GPU's work; up to 8 submitted steps keep
+ * their own staging. */
+slm_status slm_batch_decode_layers_host(slm_batch* batch, int32_t first_layer, int32_t n_layers,
+                                        const float* h_query, const float* h_keys,
+                                        const float* h_values, float* h_out);
 /* Append-only form (prompt prefill, attention.rs:863-868): keys/values are the
  * batch's tokens concatenated in batch order, [sum(counts), kv_heads, d]. */
 slm_status slm_batch_append_layer(slm_batch* batch, int32_t layer, const float* d_keys,

@@ -173,6 +173,20 @@ struct slm_ctx {
   // hold up the next step's descriptor behind it).
   cudaStream_t copy_stream = nullptr, readback_stream = nullptr;
   Upload up_batch, up_aux;
+  // slm_batch_decode_layers_host: device staging of a step's inputs and
+  // outputs, one set per descriptor slot (the batch's up_slot), grown on
+  // demand. Inputs go in on io_h2d (not copy_stream, so that the next step's
+  // descriptor does not queue behind them), outputs come back on
+  // readback_stream ahead of the step's statuses.
+  struct HostIo {
+    float* d_in[kUploadSlots] = {};
+    float* d_out[kUploadSlots] = {};
+    size_t in_cap = 0, out_cap = 0;  // floats a slot
+    cudaEvent_t in_done[kUploadSlots] = {};  // the slot's inputs are on the device
+    cudaEvent_t used[kUploadSlots] = {};     // the slot's kernels are done with it
+    cudaEvent_t read[kUploadSlots] = {};     // the slot's outputs are on the host
+    cudaStream_t h2d = nullptr;
+  } io;
   size_t upd_cap = 0, copy_cap = 0;
 
   // host state
@@ -755,6 +769,13 @@ void destroy_device(slm_ctx* c) {
     if (ev) cudaEventDestroy(ev);
   upload_free(c->up_batch);
   upload_free(c->up_aux);
+  for (int k = 0; k < kUploadSlots; ++k) {
+    if (c->io.d_in[k]) cudaFree(c->io.d_in[k]);
+    if (c->io.d_out[k]) cudaFree(c->io.d_out[k]);
+    for (cudaEvent_t ev : {c->io.in_done[k], c->io.used[k], c->io.read[k]})
+      if (ev) cudaEventDestroy(ev);
+  }
+  if (c->io.h2d) cudaStreamDestroy(c->io.h2d);
   if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
   if (c->readback_stream) cudaStreamDestroy(c->readback_stream);
 }
@@ -1505,6 +1526,88 @@ slm_status slm_batch_decode_layers(slm_batch* b, int32_t first_layer, int32_t n_
     const slm_status rc = decode_launch_layers(b, first_layer + i, std::min(per, n_layers - i), io + i);
     if (rc) return rc;
   }
+  return SLM_OK;
+}
+
+namespace {
+// Grows the host-IO staging to `in` / `out` floats a slot (waits for the
+// device first: a slot may be in use).
+slm_status host_io_reserve(slm_ctx* c, size_t in, size_t out) {
+  slm_ctx::HostIo& io = c->io;
+  if (!io.h2d) {
+    CU(c, cudaStreamCreateWithFlags(&io.h2d, cudaStreamNonBlocking));
+    for (int k = 0; k < kUploadSlots; ++k)
+      for (cudaEvent_t* ev : {&io.in_done[k], &io.used[k], &io.read[k]})
+        CU(c, cudaEventCreateWithFlags(ev, cudaEventDisableTiming));
+  }
+  if (in <= io.in_cap && out <= io.out_cap) return SLM_OK;
+  CU(c, cudaDeviceSynchronize());
+  for (int k = 0; k < kUploadSlots; ++k) {
+    if (io.d_in[k]) cudaFree(io.d_in[k]);
+    if (io.d_out[k]) cudaFree(io.d_out[k]);
+    io.d_in[k] = io.d_out[k] = nullptr;
+  }
+  c->device_bytes -= static_cast<int64_t>((io.in_cap + io.out_cap) * sizeof(float)) * kUploadSlots;
+  io.in_cap = io.out_cap = 0;
+  for (int k = 0; k < kUploadSlots; ++k) {
+    CU(c, cudaMalloc(reinterpret_cast<void**>(&io.d_in[k]), in * sizeof(float)));
+    CU(c, cudaMalloc(reinterpret_cast<void**>(&io.d_out[k]), out * sizeof(float)));
+  }
+  io.in_cap = in;
+  io.out_cap = out;
+  c->device_bytes += static_cast<int64_t>((in + out) * sizeof(float)) * kUploadSlots;
+  return SLM_OK;
+}
+}  // namespace
+
+slm_status slm_batch_decode_layers_host(slm_batch* b, int32_t first_layer, int32_t n_layers,
+                                        const float* h_query, const float* h_keys,
+                                        const float* h_values, float* h_out) {
+  if (!b) return SLM_ERR_INVALID_INPUT;
+  slm_ctx* ctx = b->ctx;
+  if (n_layers <= 0 || n_layers > ctx->cfg.num_layers || !h_query || !h_keys || !h_values || !h_out)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "batch",
+                       "a layer count of at least 1 and host buffers are required");
+  slm_status rc = batch_layer_check(b, first_layer);
+  if (rc) return rc;
+  if (first_layer + n_layers > ctx->cfg.num_layers)
+    return input_error(ctx, SLM_ERR_INVALID_INPUT, "KV cache", "layers %d..%d are outside 0..%d",
+                       first_layer, first_layer + n_layers - 1, ctx->cfg.num_layers);
+  const size_t n = b->seq_ids.size();
+  const size_t qn = n * ctx->cfg.num_query_heads * kHeadDim;
+  const size_t kvn = n * ctx->cfg.num_key_value_heads * kHeadDim;
+  const size_t L = static_cast<size_t>(n_layers);
+  if ((rc = host_io_reserve(ctx, L * (qn + 2 * kvn), L * qn))) return rc;
+  slm_ctx::HostIo& io = ctx->io;
+  const int k = b->up_slot;
+  float* dq = io.d_in[k];
+  float* dk = dq + L * qn;
+  float* dv = dk + L * kvn;
+  float* dout = io.d_out[k];
+  std::vector<slm_layer_io> lio(L);
+  for (size_t i = 0; i < L; ++i) lio[i] = slm_layer_io{dq + i * qn, dk + i * kvn, dv + i * kvn, dout + i * qn};
+  // every layer's arguments checked before anything is queued
+  for (int32_t i = 0; i < n_layers; ++i)
+    if ((rc = decode_layer_check(b, first_layer + i, lio[i].query, lio[i].keys, lio[i].values,
+                                 lio[i].out)))
+      return rc;
+  // inputs in, after the kernels that last read this slot
+  CU(ctx, cudaStreamWaitEvent(io.h2d, io.used[k], 0));
+  CU(ctx, cudaMemcpyAsync(dq, h_query, L * qn * sizeof(float), cudaMemcpyHostToDevice, io.h2d));
+  CU(ctx, cudaMemcpyAsync(dk, h_keys, L * kvn * sizeof(float), cudaMemcpyHostToDevice, io.h2d));
+  CU(ctx, cudaMemcpyAsync(dv, h_values, L * kvn * sizeof(float), cudaMemcpyHostToDevice, io.h2d));
+  CU(ctx, cudaEventRecord(io.in_done[k], io.h2d));
+  // the step's kernels, after its inputs and after this slot's last outputs left
+  CU(ctx, cudaStreamWaitEvent(b->stream, io.in_done[k], 0));
+  CU(ctx, cudaStreamWaitEvent(b->stream, io.read[k], 0));
+  if ((rc = slm_batch_decode_layers(b, first_layer, n_layers, lio.data()))) return rc;
+  CU(ctx, cudaEventRecord(io.used[k], b->stream));
+  // outputs out on the readback stream, ahead of the step's statuses, so the
+  // batch's end / wait returns after they are on the host
+  CU(ctx, cudaStreamWaitEvent(ctx->readback_stream, io.used[k], 0));
+  CU(ctx, cudaMemcpyAsync(h_out, dout, L * qn * sizeof(float), cudaMemcpyDeviceToHost,
+                          ctx->readback_stream));
+  CU(ctx, cudaEventRecord(io.read[k], ctx->readback_stream));
   return SLM_OK;
 }
 

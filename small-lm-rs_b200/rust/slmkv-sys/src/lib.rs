@@ -114,6 +114,7 @@ extern "C" {
     pub fn slm_batch_begin(ctx: *mut SlmCtx, n: i32, h_seq_ids: *const i32, h_token_counts: *const i32, stream: *mut c_void, out: *mut *mut SlmBatch) -> i32;
     pub fn slm_batch_decode_layer(batch: *mut SlmBatch, layer: i32, d_query: *const f32, d_keys: *const f32, d_values: *const f32, d_out: *mut f32) -> i32;
     pub fn slm_batch_decode_layers(batch: *mut SlmBatch, first_layer: i32, n_layers: i32, io: *const SlmLayerIo) -> i32;
+    pub fn slm_batch_decode_layers_host(batch: *mut SlmBatch, first_layer: i32, n_layers: i32, h_query: *const f32, h_keys: *const f32, h_values: *const f32, h_out: *mut f32) -> i32;
     pub fn slm_batch_append_layer(batch: *mut SlmBatch, layer: i32, d_keys: *const f32, d_values: *const f32, rotate_keys: i32) -> i32;
     pub fn slm_batch_prefill_attention(batch: *mut SlmBatch, layer: i32, d_query: *const f32, rotate_query: i32, d_out: *mut f32) -> i32;
     pub fn slm_batch_attention_exact(batch: *mut SlmBatch, layer: i32, d_query: *const f32, rotate_query: i32, d_out: *mut f32) -> i32;

@@ -427,6 +427,28 @@ impl<'c> Batch<'c> {
         })
     }
 
+    /// `decode_layers` with the step's inputs and outputs in host memory
+    /// (`[n_layers][n][heads][64]` each; pinned for the copies to overlap):
+    /// `out` is complete once this batch's `end` / `wait` has returned.
+    pub fn decode_layers_host(&mut self, first_layer: i32, n_layers: i32, q: &[f32], k: &[f32],
+                              v: &[f32], out: &mut [f32]) -> Result<()> {
+        let b = self.open_raw()?;
+        let mut cfg = sys::SlmConfig::default();
+        check(self.ctx.raw, unsafe { sys::slm_ctx_config(self.ctx.raw, &mut cfg) })?;
+        let (hq, hkv) = (cfg.num_query_heads as usize, cfg.num_key_value_heads as usize);
+        let per = self.n * 64 * n_layers.max(0) as usize;
+        if q.len() < per * hq || k.len() < per * hkv || v.len() < per * hkv || out.len() < per * hq {
+            return Err(Error::InvalidInput {
+                code: sys::SLM_ERR_INVALID_INPUT,
+                message: "invalid input for batch: host buffers shorter than the layers need".into(),
+            });
+        }
+        check(self.ctx.raw, unsafe {
+            sys::slm_batch_decode_layers_host(b, first_layer, n_layers, q.as_ptr(), k.as_ptr(),
+                                              v.as_ptr(), out.as_mut_ptr())
+        })
+    }
+
     /// `decode_layer` in the reference's operation order, bit for bit with
     /// its CPU path (f32 pools).
     pub fn decode_layer_exact(&mut self, layer: i32, q: DevicePtr<f32>, k: DevicePtr<f32>,

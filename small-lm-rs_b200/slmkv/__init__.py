@@ -145,6 +145,7 @@ SIGNATURES = {
     "slm_batch_begin": (C.c_int, [_vp, _i32, _pi32, _pi32, _vp, C.POINTER(_vp)]),
     "slm_batch_decode_layer": (C.c_int, [_vp, _i32, _vp, _vp, _vp, _vp]),
     "slm_batch_decode_layers": (C.c_int, [_vp, _i32, _i32, _vp]),
+    "slm_batch_decode_layers_host": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp]),
     "slm_batch_append_layer": (C.c_int, [_vp, _i32, _vp, _vp, _i32]),
     "slm_batch_prefill_attention": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
     "slm_batch_attention_exact": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
@@ -504,6 +505,7 @@ class _Fast:
         self.begin = L.slm_batch_begin
         self.decode = L.slm_batch_decode_layer
         self.decode_many = L.slm_batch_decode_layers
+        self.decode_host = L.slm_batch_decode_layers_host
         self.end = L.slm_batch_end
         self.submit = L.slm_batch_submit
         self.wait = L.slm_batch_wait
@@ -586,6 +588,27 @@ class Batch:
     def decode_layers_array(self, first_layer: int, n_layers: int, arr) -> None:
         """decode_layers with a prebuilt layer_io_array of device addresses."""
         rc = _fast.decode_many(self._h, first_layer, n_layers, arr)
+        if rc:
+            self.pool.check(rc)
+
+    def decode_layers_host(self, first_layer: int, n_layers: int, query, keys, values, out) -> None:
+        """slm_batch_decode_layers_host: the step's inputs and outputs in host
+        memory (contiguous CPU float32 tensors, pinned for the copies to
+        overlap; query/out [n_layers, n, q_heads, 64], keys/values [n_layers,
+        n, kv_heads, 64]). `out` is complete once this batch's end() / wait()
+        has returned; the tensors must live until then."""
+        ptrs = []
+        for t in (query, keys, values, out):
+            if t.is_cuda or not t.is_contiguous() or str(t.dtype) != "torch.float32":
+                raise InvalidInput(ERR_INVALID_INPUT, "invalid input for slmkv: host buffers must "
+                                   "be contiguous CPU float32 tensors")
+            ptrs.append(C.c_void_p(t.data_ptr()))
+        self.decode_layers_host_ptr(first_layer, n_layers, *ptrs)
+
+    def decode_layers_host_ptr(self, first_layer: int, n_layers: int, query, keys, values,
+                               out) -> None:
+        """decode_layers_host with raw host addresses."""
+        rc = _fast.decode_host(self._h, first_layer, n_layers, query, keys, values, out)
         if rc:
             self.pool.check(rc)
 

@@ -158,3 +158,41 @@ def test_rejects_overlapping_layer_buffers_before_launching():
     assert pool.launch_count() == launches0
     b.rollback()
     assert [c.sequence_length() for c in caches] == lengths
+
+
+def test_host_buffers_equal_the_device_call_with_steps_in_flight():
+    """slm_batch_decode_layers_host: inputs copied in from pinned host memory,
+    outputs copied back before the batch's wait returns; three steps
+    submitted before any is waited for (each its own staging and host
+    buffers), every output equal to the device-buffer call's bit for bit."""
+    lengths = [0, 3, 16, 17, 200, 505, 45, 130]
+    layers, hq, hkv = 8, 4, 2
+    pool, caches, ocs, inv, qs, ks, vs = _setup(slmkv.KV_F32, lengths, layers, hq, hkv, 37)
+    base = [c.sequence_length() for c in caches]
+    rng = np.random.default_rng(38)
+    steps = 3
+    hq_ = [torch.from_numpy(rng.standard_normal(qs.shape).astype(np.float32)).pin_memory()
+           for _ in range(steps)]
+    hk_ = [torch.from_numpy(rng.standard_normal(ks.shape).astype(np.float32)).pin_memory()
+           for _ in range(steps)]
+    hv_ = [torch.from_numpy(rng.standard_normal(vs.shape).astype(np.float32)).pin_memory()
+           for _ in range(steps)]
+    hout = [torch.full(qs.shape, float("nan")).pin_memory() for _ in range(steps)]
+    inflight = []
+    for i in range(steps):
+        b = pool.begin(caches, 1)
+        b.decode_layers_host(0, layers, hq_[i], hk_[i], hv_[i], hout[i])
+        inflight.append(b.submit())
+    for b in inflight:
+        assert b.wait() == [0] * len(lengths)
+    got = [h.clone() for h in hout]
+    # the same three steps from device buffers
+    for c, L in zip(caches, base):
+        c.truncate_all(L)
+    for i in range(steps):
+        dq, dk, dv = hq_[i].cuda(), hk_[i].cuda(), hv_[i].cuda()
+        out = torch.empty_like(dq)
+        with pool.begin(caches, 1) as b:
+            b.decode_layers(0, [(dq[l], dk[l], dv[l], out[l]) for l in range(layers)])
+        assert np.array_equal(bits(got[i]), bits(out))
+    assert [c.sequence_length() for c in caches] == [L + steps for L in base]
