@@ -1593,9 +1593,14 @@ slm_status slm_batch_decode_layers_host(slm_batch* b, int32_t first_layer, int32
       return rc;
   // inputs in, after the kernels that last read this slot
   CU(ctx, cudaStreamWaitEvent(io.h2d, io.used[k], 0));
-  CU(ctx, cudaMemcpyAsync(dq, h_query, L * qn * sizeof(float), cudaMemcpyHostToDevice, io.h2d));
-  CU(ctx, cudaMemcpyAsync(dk, h_keys, L * kvn * sizeof(float), cudaMemcpyHostToDevice, io.h2d));
-  CU(ctx, cudaMemcpyAsync(dv, h_values, L * kvn * sizeof(float), cudaMemcpyHostToDevice, io.h2d));
+  if (h_keys == h_query + L * qn && h_values == h_keys + L * kvn) {  // one host block: one copy
+    CU(ctx, cudaMemcpyAsync(dq, h_query, L * (qn + 2 * kvn) * sizeof(float), cudaMemcpyHostToDevice,
+                            io.h2d));
+  } else {
+    CU(ctx, cudaMemcpyAsync(dq, h_query, L * qn * sizeof(float), cudaMemcpyHostToDevice, io.h2d));
+    CU(ctx, cudaMemcpyAsync(dk, h_keys, L * kvn * sizeof(float), cudaMemcpyHostToDevice, io.h2d));
+    CU(ctx, cudaMemcpyAsync(dv, h_values, L * kvn * sizeof(float), cudaMemcpyHostToDevice, io.h2d));
+  }
   CU(ctx, cudaEventRecord(io.in_done[k], io.h2d));
   // the step's kernels, after its inputs and after this slot's last outputs left
   CU(ctx, cudaStreamWaitEvent(b->stream, io.in_done[k], 0));

@@ -178,6 +178,12 @@ def test_host_buffers_equal_the_device_call_with_steps_in_flight():
     hv_ = [torch.from_numpy(rng.standard_normal(vs.shape).astype(np.float32)).pin_memory()
            for _ in range(steps)]
     hout = [torch.full(qs.shape, float("nan")).pin_memory() for _ in range(steps)]
+    # step 0's inputs as one pinned block (Q, K, V back to back: one copy in)
+    blk = torch.cat([hq_[0].reshape(-1), hk_[0].reshape(-1), hv_[0].reshape(-1)]).pin_memory()
+    nq, nk = hq_[0].numel(), hk_[0].numel()
+    hq_[0] = blk[:nq].view(qs.shape)
+    hk_[0] = blk[nq:nq + nk].view(ks.shape)
+    hv_[0] = blk[nq + nk:].view(vs.shape)
     inflight = []
     for i in range(steps):
         b = pool.begin(caches, 1)
