@@ -102,6 +102,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity);
 }
 
+// Counter arrival with release and acquire at gpu scope, and the relaxed
+// store that resets a counter for the next launch.
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void st_relaxed(int* p, int v) {
+  asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // 2^x on the MUFU unit (scores live in the exp2 domain); ex2(-inf) = +0.
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -1114,25 +1125,27 @@ __global__ void __launch_bounds__(W * 32, 1)
     // together); the next layer's first copies are already in flight.
     if (npend > 0) {
       int* counters = p.counters + static_cast<size_t>(cl) * p.counter_stride;
-      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      // The warp barrier orders every lane's partial writes before lane 0's
+      // arrival, whose release (gpu scope, cumulative) publishes them; the
+      // arrival's acquire, passed on by the shuffle, orders the last CTA's
+      // reads of the other partials after every earlier arrival.
       __syncwarp();
       const int4 pend0 = rec[2], pend1 = rec[3];
       int lastmask = 0;
       if (lane == 0) {
-        const int prev0 = atomicAdd(&counters[pend0.x], 1);
-        const int prev1 = (npend > 1) ? atomicAdd(&counters[pend1.x], 1) : 0;
+        const int prev0 = atom_add_acq_rel(&counters[pend0.x], 1);
+        const int prev1 = (npend > 1) ? atom_add_acq_rel(&counters[pend1.x], 1) : 0;
         if (prev0 == pend0.z - 1) {
           lastmask |= 1;
-          atomicExch(&counters[pend0.x], 0);  // ready for the next launch
+          st_relaxed(&counters[pend0.x], 0);  // ready for the next launch
         }
         if (npend > 1 && prev1 == pend1.z - 1) {
           lastmask |= 2;
-          atomicExch(&counters[pend1.x], 0);
+          st_relaxed(&counters[pend1.x], 0);
         }
       }
       lastmask = __shfl_sync(kFull, lastmask, 0);
       if (lastmask != 0) {
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         float* out = p.out[ML ? cl : 0];
         const size_t pbase = static_cast<size_t>(cl) * p.part_stride;
         for (int k = 0; k < npend; ++k) {
