@@ -8,7 +8,7 @@ every kernel record its kernel kind, SM and %globaltimer at entry and exit;
 this module runs the scaled GQA model's decode steps on it and prints, per
 kernel, where a step's time goes:
 
-    python -m slmkv.timeline [--steps 6] [--batch 16]
+    python -m slmkv.timeline [--workload gqa-model|model] [--steps 6] [--batch 16]
 
 (run from the repository root with small-lm-rs_b200 on sys.path, as the
 tests do). The numbers are of the timeline build, whose records cost a few
@@ -28,7 +28,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parents[1]
 
 RECORD = np.dtype([("kind", "<u2"), ("sm", "<u2"), ("block", "<u4"), ("t0", "<u8"), ("t1", "<u8")])
-NAMES = {1: "decode", 2: "decode (layers)", 3: "append", 5: "prefill", 6: "exact", 7: "apply",
+NAMES = {1: "decode", 2: "decode (layers)", 3: "append", 5: "prefill", 6: "exact attention", 7: "apply",
          8: "embed", 9: "rmsnorm", 10: "round", 11: "situ", 12: "proj", 13: "head", 14: "argmax",
          15: "proj1", 16: "prefill_tc", 32: "gemm_qkv", 33: "gemm_o", 34: "gemm_gu",
          35: "gemm_down"}
@@ -49,8 +49,10 @@ def launches(rec):
     return runs
 
 
-def run_gqa_steps(steps: int, batch: int):
-    """The scaled GQA model (bench.py's gqa-model workload, one GPU): prefill,
+def run_steps(workload: str, steps: int, batch: int):
+    """bench.py's gqa-model workload (the scaled GQA model, 16 sequences of
+    1-8 k tokens, row-GEMM projections) or model workload (the 8M model,
+    batch 1, a 64-token prompt, exact-order projections), one GPU: prefill,
     10 untimed decode steps, then `steps` recorded ones. Returns the records
     sorted by entry time."""
     import torch
@@ -63,22 +65,28 @@ def run_gqa_steps(steps: int, batch: int):
     sys.path.insert(0, str(ROOT))
     import bench
 
-    bench.select_workload("gqa-model", batch)
+    gqa = workload == "gqa-model"
+    bench.select_workload(workload, batch)
     B = bench.B
     dev = torch.device("cuda:0")
-    lens = [int(x) for x in np.random.default_rng(0).integers(bench.LEN_LO, bench.LEN_HI + 1,
-                                                             size=B * 8)[:B]]
+    if gqa:
+        lens = [int(x) for x in np.random.default_rng(0).integers(bench.LEN_LO, bench.LEN_HI + 1,
+                                                                 size=B * 8)[:B]]
+    else:
+        lens = [bench.LEN_LO] * B
     prng = np.random.default_rng(1)
     prompts = [prng.integers(0, bench.MODEL_VOCAB, size=L).astype(np.int32) for L in lens]
     pool = slmkv.KvPool(num_layers=bench.LAYERS, num_query_heads=bench.HQ,
                         num_key_value_heads=bench.HKV, head_dimension=bench.D,
                         context_length=bench.CTX,
                         num_blocks=sum(-(-(L + 256) // 16) for L in lens) + 8, max_sequences=B,
-                        kv_dtype=slmkv.KV_BF16, device=0)
+                        kv_dtype=slmkv.KV_BF16 if gqa else slmkv.KV_F32, device=0)
     pool.shuffle(1)
-    model = slmkv.Model(pool, vocab_size=bench.MODEL_VOCAB, intermediate_size=bench.GQA_MODEL_INTER,
-                        tensors=bench.model_tensors(0, bench.GQA_MODEL_INTER))
-    model.set_exact_rows(0)
+    inter = bench.GQA_MODEL_INTER if gqa else bench.MODEL_INTER
+    model = slmkv.Model(pool, vocab_size=bench.MODEL_VOCAB, intermediate_size=inter,
+                        tensors=bench.model_tensors(0, inter))
+    if gqa:
+        model.set_exact_rows(0)
     caches = [pool.allocate_kv_cache(bench.CTX) for _ in lens]
     tok = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(2)]
     with pool.begin(caches, lens) as b:
@@ -149,7 +157,7 @@ def report(rec):
     st = full[len(full) // 2]
     base = st[0]["t0"]
     print("one step's first layer (entry / exit, us from the step's start):")
-    for g in st[:10]:
+    for g in st[:12]:
         print(f"  {NAMES.get(g['kind'], g['kind']):16s} {(g['t0'] - base) / 1e3:8.2f} "
               f"{(g['t1'] - base) / 1e3:8.2f}")
     dec = [g for s in full for g in s if g["kind"] == 1]
@@ -167,10 +175,11 @@ def report(rec):
 
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", choices=["gqa-model", "model"], default="gqa-model")
     ap.add_argument("--steps", type=int, default=6)
     ap.add_argument("--batch", type=int, default=None)
     a = ap.parse_args()
-    report(run_gqa_steps(a.steps, a.batch))
+    report(run_steps(a.workload, a.steps, a.batch))
 
 
 if __name__ == "__main__":
