@@ -577,6 +577,7 @@ struct slm_model {
   bool head_kernel_ok = false;  // rows up to 64 on head_kernel (hidden <= 4096)
   // one-row steps: columns a CTA of proj1_kernel per mode (0: proj_kernel)
   int32_t p1_cols[4] = {0, 0, 0, 0};
+  bool mlp1_ok = false;  // one-row steps: output .. down projection as one cluster launch
   cublasHandle_t blas = nullptr;
   void* weights = nullptr;  // one device allocation for every tensor
   const float* emb = nullptr;         // [V, H] fp32: lookup table and tied vocabulary projection
@@ -785,6 +786,171 @@ __global__ void __launch_bounds__(128) proj1_kernel(const ProjArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// One-row steps: a layer's output projection, FFN RMSNorm, gate/up with
+// SiTU-GLU and down projection in one launch of one thread-block cluster
+// (transformer.rs:221-292 after the attention). Each of the kMlpCluster CTAs
+// holds its slice of the three weight matrices in shared memory (requested
+// before waiting on the attention kernel) and computes its slice of the
+// output columns, each the reference's in-order fma fold (linear.rs:98-103)
+// as proj1_kernel does; the new residual row and the SiTU-GLU outputs are
+// written into every CTA's shared memory (distributed shared memory) and a
+// cluster barrier stands where two kernel boundaries stood.
+constexpr int kMlpCluster = 8;
+constexpr int kMlpThreads = 192;
+struct MlpArgs {
+  const float* att;          // attention output row [H]
+  float* x;                  // residual row [H]: + output projection, + down projection
+  const __nv_bfloat16* wo;   // [H][H]
+  const __nv_bfloat16* wgu;  // [H][2I]: gate | up
+  const __nv_bfloat16* wd;   // [I][H]
+  const float* ffn_norm;     // [H]
+  float eps, beta_gate, beta_up;
+  int32_t H, I;
+};
+size_t mlp1_smem(int32_t H, int32_t I) {
+  const size_t co = H / kMlpCluster, ci = I / kMlpCluster;
+  return 2 * (static_cast<size_t>(H) * co + 2 * static_cast<size_t>(H) * ci + static_cast<size_t>(I) * co) +
+         4 * (3 * static_cast<size_t>(H) + I + ci);
+}
+bool mlp1_fits(int32_t H, int32_t I) {
+  return H % (8 * kMlpCluster) == 0 && I % (8 * kMlpCluster) == 0 && H % 8 == 0 &&
+         2 * (I / kMlpCluster) <= kMlpThreads && H / kMlpCluster <= kMlpThreads &&
+         mlp1_smem(H, I) <= 227 * 1024;
+}
+// acc = fold over k of x[k] * w[k * stride] (bf16 w), in order; K % 8 == 0
+__device__ __forceinline__ float fold_row(const uint16_t* w, int stride, const float* x, int K) {
+  float acc = 0.f;
+  for (int k = 0; k < K; k += 8) {
+    const float4 x0 = *reinterpret_cast<const float4*>(x + k);
+    const float4 x1 = *reinterpret_cast<const float4*>(x + k + 4);
+    uint32_t v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = w[static_cast<size_t>(k + j) * stride];
+    acc = fmaf(x0.x, __uint_as_float(v[0] << 16), acc);
+    acc = fmaf(x0.y, __uint_as_float(v[1] << 16), acc);
+    acc = fmaf(x0.z, __uint_as_float(v[2] << 16), acc);
+    acc = fmaf(x0.w, __uint_as_float(v[3] << 16), acc);
+    acc = fmaf(x1.x, __uint_as_float(v[4] << 16), acc);
+    acc = fmaf(x1.y, __uint_as_float(v[5] << 16), acc);
+    acc = fmaf(x1.z, __uint_as_float(v[6] << 16), acc);
+    acc = fmaf(x1.w, __uint_as_float(v[7] << 16), acc);
+  }
+  return acc;
+}
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// v into element i of array `arr` (shared memory) of every CTA of the cluster
+__device__ __forceinline__ void store_to_cluster(float* arr, int i, float v) {
+  const uint32_t local = static_cast<uint32_t>(__cvta_generic_to_shared(arr + i));
+#pragma unroll
+  for (int r = 0; r < kMlpCluster; ++r) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(r));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+  }
+}
+
+__global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
+  SLMKV_TL(kTlMlp1);
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int tid = threadIdx.x, H = a.H, I = a.I;
+  const int CO = H / kMlpCluster, CI = I / kMlpCluster;
+  uint32_t rank;
+  asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const int o0 = static_cast<int>(rank) * CO, i0 = static_cast<int>(rank) * CI;
+  // [H][CO] output, [H][CI] gate, [H][CI] up, [I][CO] down slices (bf16), then
+  // the f32 rows: rounded attention row, new residual row, normalised row,
+  // SiTU-GLU outputs, this CTA's up columns
+  __nv_bfloat16* wo_s = reinterpret_cast<__nv_bfloat16*>(smem);
+  __nv_bfloat16* wg_s = wo_s + static_cast<size_t>(H) * CO;
+  __nv_bfloat16* wu_s = wg_s + static_cast<size_t>(H) * CI;
+  __nv_bfloat16* wd_s = wu_s + static_cast<size_t>(H) * CI;
+  float* xo = reinterpret_cast<float*>(wd_s + static_cast<size_t>(I) * CO);
+  float* hid = xo + H;
+  float* xg = hid + H;
+  float* hb = xg + H;
+  float* up_s = hb + I;
+  __shared__ float inv_s;
+  auto smem_u32 = [](const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); };
+  // the weights (no kernel writes them) are requested before the wait
+  const int so = CO / 8, si = CI / 8;
+  for (int i = tid; i < H * so; i += kMlpThreads) {
+    const int k = i / so, sg = i - k * so;
+    cp_async16(smem_u32(wo_s + k * CO + 8 * sg), a.wo + static_cast<size_t>(k) * H + o0 + 8 * sg);
+  }
+  for (int i = tid; i < H * si; i += kMlpThreads) {
+    const int k = i / si, sg = i - k * si;
+    const __nv_bfloat16* src = a.wgu + static_cast<size_t>(k) * 2 * I + i0 + 8 * sg;
+    cp_async16(smem_u32(wg_s + k * CI + 8 * sg), src);
+    cp_async16(smem_u32(wu_s + k * CI + 8 * sg), src + I);
+  }
+  for (int i = tid; i < I * so; i += kMlpThreads) {
+    const int k = i / so, sg = i - k * so;
+    cp_async16(smem_u32(wd_s + k * CO + 8 * sg), a.wd + static_cast<size_t>(k) * H + o0 + 8 * sg);
+  }
+  cp_async_commit();
+  wait_previous_kernel();  // the attention row comes from the previous kernel
+  for (int k = tid; k < H; k += kMlpThreads) xo[k] = round_bf16(a.att[k]);  // the projection's operand
+  cp_async_wait<0>();
+  __syncthreads();
+  // output projection, onto the residual (transformer.rs add_residual_in_place);
+  // every CTA receives the new residual row
+  if (tid < CO) {
+    const float acc = fold_row(reinterpret_cast<const uint16_t*>(wo_s) + tid, CO, xo, H);
+    store_to_cluster(hid, o0 + tid, __fadd_rn(a.x[o0 + tid], acc));
+  }
+  cluster_barrier();
+  // FFN RMSNorm (rmsnorm.rs:80-91): the in-order square-sum fold
+  if (tid == 0) {
+    float sum = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < H; ++k) sum = fmaf(hid[k], hid[k], sum);
+    inv_s = 1.f / sqrtf(__fdiv_rn(sum, static_cast<float>(H)) + a.eps);
+  }
+  __syncthreads();
+  for (int k = tid; k < H; k += kMlpThreads)
+    xg[k] = round_bf16(__fmul_rn(__fmul_rn(hid[k], inv_s), a.ffn_norm[k]));
+  __syncthreads();
+  // gate and up columns i0 .. i0 + CI, SiTU-GLU (situ_glu.rs:101-107) as bf16;
+  // every CTA receives h
+  float g = 0.f;
+  if (tid < 2 * CI) {
+    const int up = tid >= CI ? 1 : 0, cl = tid - up * CI;
+    g = fold_row(reinterpret_cast<const uint16_t*>(up ? wu_s : wg_s) + cl, CI, xg, H);
+    if (up) up_s[cl] = g;
+  }
+  __syncthreads();
+  if (tid < CI)
+    store_to_cluster(hb, i0 + tid,
+                     round_bf16(__fmul_rn(situ_gate(g, a.beta_gate), situ_up(up_s[tid], a.beta_up))));
+  cluster_barrier();
+  // down projection, onto the residual
+  if (tid < CO) {
+    const float acc = fold_row(reinterpret_cast<const uint16_t*>(wd_s) + tid, CO, hb, I);
+    a.x[o0 + tid] = __fadd_rn(hid[o0 + tid], acc);
+  }
+}
+
+cudaError_t launch_mlp1(const MlpArgs& a, cudaStream_t s) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(kMlpCluster);
+  cfg.blockDim = dim3(kMlpThreads);
+  cfg.dynamicSmemBytes = mlp1_smem(a.H, a.I);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = kMlpCluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, mlp1_kernel, a);
+}
+
 template <int MODE>
 cudaError_t launch_proj(const ProjArgs& a, cudaStream_t s) {
   if (a.rows == 1 && a.cols > 0) {
@@ -858,6 +1024,13 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       q.y0 = m->q, q.y1 = m->k, q.y2 = m->v;
       launched(launch_proj<kProjQKV>(q, s));
       if ((rc = cache_step(l))) return rc;
+      if (rows == 1 && m->mlp1_ok) {  // output, FFN norm, gate/up, down: one cluster launch
+        const MlpArgs ma{m->att, m->x, Ly.wo, Ly.wgu, Ly.wd, Ly.ffn_norm, m->eps,
+                         m->beta_gate, m->beta_up, H, I};
+        launched(launch_mlp1(ma, s));
+        launches += 2;
+        continue;
+      }
       ProjArgs o = a;  // output projection onto the residual
       o.x = m->att, o.K = H, o.ncols = H, o.w = Ly.wo, o.ld = H, o.y0 = m->x;
       o.cols = m->p1_cols[kProjO];
@@ -1131,6 +1304,7 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
     one_row(proj1_kernel<kProjGU>, proj1_cols<kProjGU>(H), proj1_smem<kProjGU>(H, proj1_cols<kProjGU>(H)), kProjGU);
     one_row(proj1_kernel<kProjDown>, proj1_cols<kProjDown>(I), proj1_smem<kProjDown>(I, proj1_cols<kProjDown>(I)),
             kProjDown);
+    m->mlp1_ok = mlp1_fits(H, I) && attr(mlp1_kernel, mlp1_smem(H, I)) == cudaSuccess;
   }
   const uint8_t* base = static_cast<const uint8_t*>(m->weights);
   m->emb = reinterpret_cast<const float*>(base + o_emb);

@@ -25,6 +25,7 @@ static_assert(sizeof(TimelineRec) == 24, "timeline record layout");
 enum TimelineKind : uint16_t {
   kTlDecode = 1, kTlDecodeLayers, kTlAppend, kTlGather, kTlPrefill, kTlExact, kTlApply,
   kTlEmbed, kTlNorm, kTlRound, kTlSitu, kTlProj, kTlHead, kTlArgmax, kTlProj1, kTlPrefillTc,
+  kTlMlp1,
   kTlDecodeWaited = 24,    // a decode warp passed its wait on the previous kernel
   kTlDecodeSliceDone = 25, // a decode warp's slice streamed, its in-CTA merges done
   kTlRowGemm = 32,      // + the row GEMM's mode
