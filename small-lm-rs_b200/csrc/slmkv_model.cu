@@ -578,6 +578,7 @@ struct slm_model {
   // one-row steps: columns a CTA of proj1_kernel per mode (0: proj_kernel)
   int32_t p1_cols[4] = {0, 0, 0, 0};
   bool mlp1_ok = false;  // one-row steps: output .. down projection as one cluster launch
+  bool mlp1_qkv_ok = false;  // ... and the next layer's norm and q/k/v too
   cublasHandle_t blas = nullptr;
   void* weights = nullptr;  // one device allocation for every tensor
   const float* emb = nullptr;         // [V, H] fp32: lookup table and tied vocabulary projection
@@ -807,16 +808,25 @@ struct MlpArgs {
   const float* ffn_norm;     // [H]
   float eps, beta_gate, beta_up;
   int32_t H, I;
+  // with wqkv set: the next layer's attention RMSNorm and q/k/v projection too
+  const __nv_bfloat16* wqkv;  // [H][H + 2 KV]
+  const float* attn_norm;     // [H]
+  float *q, *k, *v;           // [H], [KV], [KV]
+  int32_t KV;
 };
-size_t mlp1_smem(int32_t H, int32_t I) {
+size_t mlp1_smem(int32_t H, int32_t I, int32_t KV) {  // KV = 0: without the next q/k/v
   const size_t co = H / kMlpCluster, ci = I / kMlpCluster;
-  return 2 * (static_cast<size_t>(H) * co + 2 * static_cast<size_t>(H) * ci + static_cast<size_t>(I) * co) +
+  const size_t cq = KV ? (H + 2 * KV) / kMlpCluster : 0;
+  return 2 * (static_cast<size_t>(H) * co + 2 * static_cast<size_t>(H) * ci + static_cast<size_t>(I) * co +
+              static_cast<size_t>(H) * cq) +
          4 * (3 * static_cast<size_t>(H) + I + ci);
 }
-bool mlp1_fits(int32_t H, int32_t I) {
+bool mlp1_fits(int32_t H, int32_t I, int32_t KV) {
   return H % (8 * kMlpCluster) == 0 && I % (8 * kMlpCluster) == 0 && H % 8 == 0 &&
          2 * (I / kMlpCluster) <= kMlpThreads && H / kMlpCluster <= kMlpThreads &&
-         mlp1_smem(H, I) <= 227 * 1024;
+         (KV == 0 || ((H + 2 * KV) % (8 * kMlpCluster) == 0 &&
+                      (H + 2 * KV) / kMlpCluster <= kMlpThreads)) &&
+         mlp1_smem(H, I, KV) <= 227 * 1024;
 }
 // acc = fold over k of x[k] * w[k * stride] (bf16 w), in order; K % 8 == 0
 __device__ __forceinline__ float fold_row(const uint16_t* w, int stride, const float* x, int K) {
@@ -867,7 +877,9 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   __nv_bfloat16* wg_s = wo_s + static_cast<size_t>(H) * CO;
   __nv_bfloat16* wu_s = wg_s + static_cast<size_t>(H) * CI;
   __nv_bfloat16* wd_s = wu_s + static_cast<size_t>(H) * CI;
-  float* xo = reinterpret_cast<float*>(wd_s + static_cast<size_t>(I) * CO);
+  const int CQ = a.wqkv ? (H + 2 * a.KV) / kMlpCluster : 0, q0 = static_cast<int>(rank) * CQ;
+  __nv_bfloat16* wq_s = wd_s + static_cast<size_t>(I) * CO;  // [H][CQ] next q/k/v slice
+  float* xo = reinterpret_cast<float*>(wq_s + static_cast<size_t>(H) * CQ);
   float* hid = xo + H;
   float* xg = hid + H;
   float* hb = xg + H;
@@ -889,6 +901,11 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   for (int i = tid; i < I * so; i += kMlpThreads) {
     const int k = i / so, sg = i - k * so;
     cp_async16(smem_u32(wd_s + k * CO + 8 * sg), a.wd + static_cast<size_t>(k) * H + o0 + 8 * sg);
+  }
+  const int sq = CQ / 8, ldq = H + 2 * a.KV;
+  for (int i = tid; i < H * sq; i += kMlpThreads) {
+    const int k = i / sq, sg = i - k * sq;
+    cp_async16(smem_u32(wq_s + k * CQ + 8 * sg), a.wqkv + static_cast<size_t>(k) * ldq + q0 + 8 * sg);
   }
   cp_async_commit();
   wait_previous_kernel();  // the attention row comes from the previous kernel
@@ -929,7 +946,29 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   // down projection, onto the residual
   if (tid < CO) {
     const float acc = fold_row(reinterpret_cast<const uint16_t*>(wd_s) + tid, CO, hb, I);
-    a.x[o0 + tid] = __fadd_rn(hid[o0 + tid], acc);
+    const float nx = __fadd_rn(hid[o0 + tid], acc);
+    a.x[o0 + tid] = nx;
+    if (a.wqkv) store_to_cluster(xo, o0 + tid, nx);  // xo is free: the next layer's row
+  }
+  if (!a.wqkv) return;
+  cluster_barrier();
+  // the next layer's attention RMSNorm and q/k/v columns q0 .. q0 + CQ
+  if (tid == 0) {
+    float sum = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < H; ++k) sum = fmaf(xo[k], xo[k], sum);
+    inv_s = 1.f / sqrtf(__fdiv_rn(sum, static_cast<float>(H)) + a.eps);
+  }
+  __syncthreads();
+  for (int k = tid; k < H; k += kMlpThreads)
+    xg[k] = round_bf16(__fmul_rn(__fmul_rn(xo[k], inv_s), a.attn_norm[k]));
+  __syncthreads();
+  if (tid < CQ) {
+    const int col = q0 + tid;
+    const float acc = fold_row(reinterpret_cast<const uint16_t*>(wq_s) + tid, CQ, xg, H);
+    if (col < H) a.q[col] = acc;
+    else if (col < H + a.KV) a.k[col - H] = acc;
+    else a.v[col - H - a.KV] = acc;
   }
 }
 
@@ -937,7 +976,7 @@ cudaError_t launch_mlp1(const MlpArgs& a, cudaStream_t s) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(kMlpCluster);
   cfg.blockDim = dim3(kMlpThreads);
-  cfg.dynamicSmemBytes = mlp1_smem(a.H, a.I);
+  cfg.dynamicSmemBytes = mlp1_smem(a.H, a.I, a.wqkv ? a.KV : 0);
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1007,6 +1046,7 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
     return exact_attention ? slm_batch_decode_layer_exact(b, l, m->q, m->k, m->v, m->att)
                            : slm_batch_decode_layer(b, l, m->q, m->k, m->v, m->att);
   };
+  bool qkv_done = false;  // the previous layer's cluster launch made this layer's q/k/v
   for (int32_t l = 0; l < m->L; ++l) {
     const slm_model::Layer& Ly = m->layers[l];
     if (fused) {
@@ -1022,13 +1062,28 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       q.x = m->x, q.norm_w = Ly.attn_norm, q.K = H, q.ncols = H + 2 * KV, q.w = Ly.wqkv, q.ld = H + 2 * KV;
       q.cols = m->p1_cols[kProjQKV];
       q.y0 = m->q, q.y1 = m->k, q.y2 = m->v;
-      launched(launch_proj<kProjQKV>(q, s));
+      if (!qkv_done) {
+        launched(launch_proj<kProjQKV>(q, s));
+        ++launches;
+      }
+      qkv_done = false;
       if ((rc = cache_step(l))) return rc;
-      if (rows == 1 && m->mlp1_ok) {  // output, FFN norm, gate/up, down: one cluster launch
-        const MlpArgs ma{m->att, m->x, Ly.wo, Ly.wgu, Ly.wd, Ly.ffn_norm, m->eps,
-                         m->beta_gate, m->beta_up, H, I};
+      if (rows == 1 && m->mlp1_ok) {
+        // output, FFN norm, gate/up, down (and the next layer's norm and
+        // q/k/v): one cluster launch
+        MlpArgs ma{m->att, m->x, Ly.wo, Ly.wgu, Ly.wd, Ly.ffn_norm, m->eps,
+                   m->beta_gate, m->beta_up, H, I};
+        if (l + 1 < m->L && m->mlp1_qkv_ok) {
+          ma.wqkv = m->layers[l + 1].wqkv;
+          ma.attn_norm = m->layers[l + 1].attn_norm;
+          ma.q = m->q;
+          ma.k = m->k;
+          ma.v = m->v;
+          ma.KV = KV;
+          qkv_done = true;
+        }
         launched(launch_mlp1(ma, s));
-        launches += 2;
+        ++launches;
         continue;
       }
       ProjArgs o = a;  // output projection onto the residual
@@ -1043,7 +1098,7 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       d.xh = hb, d.K = I, d.ncols = H, d.w = Ly.wd, d.ld = H, d.y0 = m->x;
       d.cols = m->p1_cols[kProjDown];
       launched(launch_proj<kProjDown>(d, s));
-      launches += 4;
+      launches += 3;
       continue;
     }
     const int32_t nqkv = H + 2 * KV;
@@ -1304,7 +1359,9 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
     one_row(proj1_kernel<kProjGU>, proj1_cols<kProjGU>(H), proj1_smem<kProjGU>(H, proj1_cols<kProjGU>(H)), kProjGU);
     one_row(proj1_kernel<kProjDown>, proj1_cols<kProjDown>(I), proj1_smem<kProjDown>(I, proj1_cols<kProjDown>(I)),
             kProjDown);
-    m->mlp1_ok = mlp1_fits(H, I) && attr(mlp1_kernel, mlp1_smem(H, I)) == cudaSuccess;
+    m->mlp1_qkv_ok = mlp1_fits(H, I, KV) && attr(mlp1_kernel, mlp1_smem(H, I, KV)) == cudaSuccess;
+    m->mlp1_ok = m->mlp1_qkv_ok ||
+                 (mlp1_fits(H, I, 0) && attr(mlp1_kernel, mlp1_smem(H, I, 0)) == cudaSuccess);
   }
   const uint8_t* base = static_cast<const uint8_t*>(m->weights);
   m->emb = reinterpret_cast<const float*>(base + o_emb);
