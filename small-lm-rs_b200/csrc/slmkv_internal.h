@@ -206,6 +206,17 @@ struct RowGemmLaunch {
   void* h;       // GU: [rows][I] bf16
   float beta_gate, beta_up;
   int32_t* err;
+  // The RMSNorm in front of q/k/v and gate/up, applied across the GEMM:
+  // O and Down with norm_next set also write the next projection's operand
+  // bf16(x * norm_next) into xg [rows][H] and each row's sum of squares over
+  // their 128-column tile into ssq [rows][ssq_ld]; QKV and GU with ssq_in set
+  // scale each row's reduced sums by 1 / sqrt(sum over the tiles / H + eps).
+  const float* norm_next;
+  void* xg;
+  float* ssq;
+  const float* ssq_in;
+  int32_t ssq_ld;
+  float eps;
 };
 struct RowGemmPlan {
   int32_t rt, row_tiles, col_tiles, nchunks, chunks_per_split, splits;

@@ -1553,6 +1553,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
   // inputs (q, new K/V) are the previous kernel's outputs.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  SLMKV_TL_MARK(kTlExactWaited);
   if (tid == 64 && !p.fused) first_copies();
   if (warp == 0) {
     float2 x = reinterpret_cast<const float2*>(p.q + (static_cast<size_t>(r) * Hq + h) * D)[lane];
@@ -1639,6 +1640,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
   for (int j = tid; j < L; j += kExactThreads) ps[j] = __fdiv_rn(ps[j], sum);
   if (bad) flags[0] = 1;
   __syncthreads();
+  SLMKV_TL_MARK(kTlExactSoftmax);
   // ---- values: threads 0-63 fold one dimension each; thread 64 refills -------
   if (tid < D) {
     float o = 0.f;

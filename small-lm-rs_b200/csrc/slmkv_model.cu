@@ -597,6 +597,10 @@ struct slm_model {
   float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *gu = nullptr;
   uint32_t* xb = nullptr;  // bf16 pairs, [rows, max(H, I) / 2]
   uint32_t* hb = nullptr;  // bf16 pairs, [rows, I / 2]: the row GEMMs' SiTU-GLU output
+  // the row GEMMs' RMSNorm across the projections: bf16(x * g) [rows, H] and
+  // each row's square sums over the 128-column tiles [rows, ceil(H / 128)]
+  __nv_bfloat16* xg = nullptr;
+  float* ssq = nullptr;
 
   float *xf = nullptr, *logits = nullptr;
 };
@@ -628,12 +632,16 @@ void free_scratch(slm_model* m) {
   for (void* p : {static_cast<void*>(m->x), static_cast<void*>(m->q), static_cast<void*>(m->k),
                   static_cast<void*>(m->v), static_cast<void*>(m->att), static_cast<void*>(m->gu),
                   static_cast<void*>(m->xb), static_cast<void*>(m->hb), static_cast<void*>(m->xf),
-                  static_cast<void*>(m->logits)})
+                  static_cast<void*>(m->logits), static_cast<void*>(m->xg), static_cast<void*>(m->ssq)})
     if (p) cudaFree(p);
-  m->x = m->q = m->k = m->v = m->att = m->gu = m->xf = m->logits = nullptr;
+  m->x = m->q = m->k = m->v = m->att = m->gu = m->xf = m->logits = m->ssq = nullptr;
   m->xb = m->hb = nullptr;
+  m->xg = nullptr;
   m->rows_cap = m->out_cap = 0;
 }
+
+// the row GEMMs' 128-column output tiles across the hidden width
+int32_t ssq_tiles(int32_t H) { return (H + 127) / 128; }
 
 // Scratch for `rows` token rows and `out_rows` projected rows (the stream
 // is synchronized before buffers are replaced).
@@ -656,6 +664,8 @@ slm_status ensure_scratch(slm_model* m, int32_t rows, int32_t out_rows, cudaStre
                 {reinterpret_cast<void**>(&m->gu), R * 2 * m->I * 4},
                 {reinterpret_cast<void**>(&m->xb), R * wide * 2},
                 {reinterpret_cast<void**>(&m->hb), R * m->I * 2},
+                {reinterpret_cast<void**>(&m->xg), R * m->H * 2},
+                {reinterpret_cast<void**>(&m->ssq), R * ssq_tiles(m->H) * 4},
                 {reinterpret_cast<void**>(&m->xf), O * m->H * 4},
                 {reinterpret_cast<void**>(&m->logits), O * m->V * 4}};
   for (const A& a : allocs) {
@@ -909,9 +919,11 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   }
   cp_async_commit();
   wait_previous_kernel();  // the attention row comes from the previous kernel
+  SLMKV_TL_MARK(kTlMlpPhase + 0);
   for (int k = tid; k < H; k += kMlpThreads) xo[k] = round_bf16(a.att[k]);  // the projection's operand
   cp_async_wait<0>();
   __syncthreads();
+  SLMKV_TL_MARK(kTlMlpPhase + 1);
   // output projection, onto the residual (transformer.rs add_residual_in_place);
   // every CTA receives the new residual row
   if (tid < CO) {
@@ -919,6 +931,7 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
     store_to_cluster(hid, o0 + tid, __fadd_rn(a.x[o0 + tid], acc));
   }
   cluster_barrier();
+  SLMKV_TL_MARK(kTlMlpPhase + 2);
   // FFN RMSNorm (rmsnorm.rs:80-91): the in-order square-sum fold
   if (tid == 0) {
     float sum = 0.f;
@@ -930,6 +943,7 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   for (int k = tid; k < H; k += kMlpThreads)
     xg[k] = round_bf16(__fmul_rn(__fmul_rn(hid[k], inv_s), a.ffn_norm[k]));
   __syncthreads();
+  SLMKV_TL_MARK(kTlMlpPhase + 3);
   // gate and up columns i0 .. i0 + CI, SiTU-GLU (situ_glu.rs:101-107) as bf16;
   // every CTA receives h
   float g = 0.f;
@@ -943,6 +957,7 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
     store_to_cluster(hb, i0 + tid,
                      round_bf16(__fmul_rn(situ_gate(g, a.beta_gate), situ_up(up_s[tid], a.beta_up))));
   cluster_barrier();
+  SLMKV_TL_MARK(kTlMlpPhase + 4);
   // down projection, onto the residual
   if (tid < CO) {
     const float acc = fold_row(reinterpret_cast<const uint16_t*>(wd_s) + tid, CO, hb, I);
@@ -952,6 +967,7 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   }
   if (!a.wqkv) return;
   cluster_barrier();
+  SLMKV_TL_MARK(kTlMlpPhase + 5);
   // the next layer's attention RMSNorm and q/k/v columns q0 .. q0 + CQ
   if (tid == 0) {
     float sum = 0.f;
@@ -963,6 +979,7 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   for (int k = tid; k < H; k += kMlpThreads)
     xg[k] = round_bf16(__fmul_rn(__fmul_rn(xo[k], inv_s), a.attn_norm[k]));
   __syncthreads();
+  SLMKV_TL_MARK(kTlMlpPhase + 6);
   if (tid < CQ) {
     const int col = q0 + tid;
     const float acc = fold_row(reinterpret_cast<const uint16_t*>(wq_s) + tid, CQ, xg, H);
@@ -1124,12 +1141,25 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
         ++launches;
         return SLM_OK;
       };
-      launched(launch_chained(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, s,
-                              static_cast<const float*>(m->x), rows, H, Ly.attn_norm, m->eps, m->xb,
-                              static_cast<float*>(nullptr), static_cast<const SeqEntry*>(nullptr)));
-      ++launches;
+      // The RMSNorms run across the projections (slmkv_rowgemm.cu): the
+      // previous residual update wrote bf16(x * g) and its square sums,
+      // q/k/v and gate/up scale by 1 / rms. The first layer's attention
+      // norm, after the embedding, is a kernel of its own.
+      a.ssq_ld = ssq_tiles(H);
+      a.eps = m->eps;
       a.y0 = m->q, a.y1 = m->k, a.y2 = m->v;
-      if ((rc = gemm(kRowQKV, Ly.tm_qkv, m->xb, H, nqkv))) return rc;
+      if (l == 0) {
+        launched(launch_chained(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, s,
+                                static_cast<const float*>(m->x), rows, H, Ly.attn_norm, m->eps, m->xb,
+                                static_cast<float*>(nullptr), static_cast<const SeqEntry*>(nullptr)));
+        ++launches;
+        if ((rc = gemm(kRowQKV, Ly.tm_qkv, m->xb, H, nqkv))) return rc;
+      } else {
+        a.ssq_in = m->ssq;
+        rc = gemm(kRowQKV, Ly.tm_qkv, m->xg, H, nqkv);
+        a.ssq_in = nullptr;
+        if (rc) return rc;
+      }
       if (!prefill && !exact_attention) {
         // the decode kernel also writes the attention rows rounded to bf16,
         // the output projection's operand (no separate rounding launch)
@@ -1145,13 +1175,15 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
         ++launches;
       }
       a.y0 = m->x, a.y1 = a.y2 = nullptr;
+      a.xg = m->xg, a.ssq = m->ssq;
+      a.norm_next = Ly.ffn_norm;
       if ((rc = gemm(kRowO, Ly.tm_o, m->xb, H, H))) return rc;
-      launched(launch_chained(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, s,
-                              static_cast<const float*>(m->x), rows, H, Ly.ffn_norm, m->eps, m->xb,
-                              static_cast<float*>(nullptr), static_cast<const SeqEntry*>(nullptr)));
-      ++launches;
+      a.norm_next = nullptr;
       a.h = m->hb;
-      if ((rc = gemm(kRowGU, Ly.tm_gu, m->xb, H, I))) return rc;
+      a.ssq_in = m->ssq;
+      if ((rc = gemm(kRowGU, Ly.tm_gu, m->xg, H, I))) return rc;
+      a.ssq_in = nullptr;
+      a.norm_next = l + 1 < m->L ? m->layers[l + 1].attn_norm : nullptr;
       if ((rc = gemm(kRowDown, Ly.tm_d, m->hb, I, H))) return rc;
       continue;
     }

@@ -17,8 +17,14 @@
 //   QKV   q | k | v columns to their three outputs
 //   O     onto the residual stream (transformer.rs add_residual_in_place)
 //   GU    gate and up tiles side by side (lanes 0-63 gate, 64-127 up of the
-//         same 64 columns), SiTU-GLU (situ_glu.rs:101-107), h as bf16
+//         same 64 columns), SiTU-GLU (situ_glu.rs:101-107,131-138:
+//         b_g tanh(g / b_g) sigmoid(g) * b_u tanh(u / b_u)), h as bf16
 //   Down  onto the residual stream
+// The RMSNorm between a residual update and the next projection
+// (rmsnorm.rs:80-91: x * inv_rms * g) needs no kernel of its own: O and Down
+// also write bf16(x * g) and each row's square sum over their tile, and QKV
+// and GU multiply each row's reduced sums by inv_rms, which they compute from
+// those square sums (the same product up to where the bf16 rounding falls).
 // Operands are bf16 with fp32 accumulation (linear.rs:44-107 up to the
 // accumulation order). Launched with programmatic stream serialization: the
 // first stages' weight boxes are requested before the previous kernel
@@ -34,7 +40,6 @@
 #include <cstdint>
 
 #include "slmkv_internal.h"
-#include "slmkv_libm.h"
 
 namespace slmkv {
 namespace {
@@ -133,11 +138,6 @@ __device__ __forceinline__ void rg_ld16(uint32_t taddr, float* v) {
 __device__ __forceinline__ void rg_cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float rg_situ_sigmoid(float v) {  // situ_glu.rs:131-138
-  if (v >= 0.f) return __fdiv_rn(1.f, __fadd_rn(1.f, libm::slm_expf(-v)));
-  const float e = libm::slm_expf(v);
-  return __fdiv_rn(e, __fadd_rn(1.f, e));
-}
 
 template <int MODE, int RT>
 __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_constant__ RowGemmLaunch p) {
@@ -149,6 +149,9 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
   __shared__ uint32_t tmem_slot;
   __shared__ int32_t aborted;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // The next kernel may be scheduled as soon as every CTA of this grid is
+  // resident: before its own wait it only requests weights, and it waits for
+  // this grid's completion before it touches activations.
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rg_smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = rg_su32(sm);
   const uint32_t full0 = rg_su32(&bars[0]), empty0 = rg_su32(&bars[S]), done = rg_su32(&bars[2 * S]);
@@ -249,8 +252,40 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
   // after a cluster barrier CTA c reduces rows c, c + S, ... of the tile,
   // reading every split's partial from its shared memory (DSMEM) and adding
   // them in split order, and writes those rows. One split: the same, S = 1.
+  const int m = warp * 32 + lane;
+  const int r0 = row_tile * RT, nr = min(RT, p.rows - r0);
+  constexpr bool kResidual = MODE == kRowO || MODE == kRowDown;
+  constexpr bool kNormed = MODE == kRowQKV || MODE == kRowGU;
+  __shared__ float inv_s[kNormed ? RT : 1];         // the deferred RMSNorm's 1 / rms per row
+  __shared__ float red_s[kResidual ? 4 : 1][RT];    // per-warp square sums per row
+  float gn = 0.f;  // the next norm's scale for this thread's column (a weight)
+  if (kResidual && p.norm_next != nullptr && kRgTileM * col_tile + m < p.ncols)
+    gn = p.norm_next[kRgTileM * col_tile + m];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (kResidual && warp >= 2) {
+    // the residual rows this CTA updates (rows split, split + S, ...; 128
+    // columns = four 128-byte lines a row) into L1 while the MMAs run
+    const int splits = gridDim.z;
+    const int nrow = nr > split ? (nr - split + splits - 1) / splits : 0;
+    for (int i = tid - 64; i < 4 * nrow; i += 64) {
+      const int r = split + (i >> 2) * splits;
+      const int c = kRgTileM * col_tile + 32 * (i & 3);
+      if (c < p.ncols)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(p.y0 + static_cast<size_t>(r0 + r) * p.ncols + c));
+    }
+  }
+  if (kNormed && p.ssq_in != nullptr && warp >= 2) {
+    // rmsnorm.rs:80-91's 1 / sqrt(mean square + eps), the square sum from
+    // the previous projection's tiles; the MMAs may still be running
+    for (int r = tid - 64; r < nr; r += 64) {
+      const float* sr = p.ssq_in + static_cast<size_t>(r0 + r) * p.ssq_ld;
+      float t = 0.f;
+#pragma unroll 4
+      for (int i = 0; i < p.ssq_ld; ++i) t += sr[i];
+      inv_s[r] = 1.f / sqrtf(__fdiv_rn(t, static_cast<float>(p.H)) + p.eps);
+    }
+  }
   bool ok = true;
   if (lane == 0) ok = rg_wait(done, 0);
   ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -259,7 +294,6 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   __syncthreads();
   const bool run = *reinterpret_cast<volatile int32_t*>(&aborted) == 0;  // CTA-uniform
-  const int m = warp * 32 + lane;
   float* part = reinterpret_cast<float*>(sm);  // [RT][128]: the stages are idle, every MMA completed
   if (run) {
     const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
@@ -273,8 +307,8 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
     }
   }
   rg_cluster_sync();  // every CTA of the cluster arrives, an aborted one too
+  if (warp == 0) SLMKV_TL_MARK(kTlRowGemmPartials + MODE);
   const int splits = gridDim.z;
-  const int r0 = row_tile * RT, nr = min(RT, p.rows - r0);
   const uint32_t part_addr = rg_su32(part);
   uint32_t peer[kRgMaxSplits];
 #pragma unroll
@@ -308,32 +342,66 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
       const int col = kRgChunk * col_tile + c;
       if (col < p.I) {
         for (int r = split + half * splits; r < nr; r += 2 * splits) {
-          const float gv = reduced(r, c), u = reduced(r, c + 64);
-          const float ga =
-              __fmul_rn(__fmul_rn(p.beta_gate, libm::slm_tanhf(__fdiv_rn(gv, p.beta_gate))), rg_situ_sigmoid(gv));
-          const float ua = __fmul_rn(p.beta_up, libm::slm_tanhf(__fdiv_rn(u, p.beta_up)));
+          float gv = reduced(r, c), u = reduced(r, c + 64);
+          if (p.ssq_in != nullptr) {
+            gv = __fmul_rn(gv, inv_s[r]);
+            u = __fmul_rn(u, inv_s[r]);
+          }
+          // CUDA's tanhf and exp: this path is held to a tolerance (its
+          // accumulation order is the tensor cores'), and glibc's branchy
+          // expm1f-based tanhf restated (the exact-order kernels' form)
+          // diverges across the lanes and took 3 us more a launch
+          const float ga = p.beta_gate * tanhf(gv * (1.f / p.beta_gate)) * __fdividef(1.f, 1.f + __expf(-gv));
+          const float ua = p.beta_up * tanhf(u * (1.f / p.beta_up));
           static_cast<__nv_bfloat16*>(p.h)[static_cast<size_t>(r0 + r) * p.I + col] =
               __float2bfloat16_rn(__fmul_rn(ga, ua));
         }
       }
-    } else {
+    } else if (MODE == kRowQKV) {
       const int col = kRgTileM * col_tile + m;
       if (col < p.ncols) {
         for (int r = split; r < nr; r += splits) {
-          const float v = reduced(r, m);
+          float v = reduced(r, m);
+          if (p.ssq_in != nullptr) v = __fmul_rn(v, inv_s[r]);
           const size_t row = static_cast<size_t>(r0 + r);
-          if (MODE == kRowQKV) {
-            if (col < p.H) p.y0[row * p.H + col] = v;
-            else if (col < p.H + p.KV) p.y1[row * p.KV + col - p.H] = v;
-            else p.y2[row * p.KV + col - p.H - p.KV] = v;
-          } else {
-            float* y = p.y0 + row * p.ncols + col;
-            *y = __fadd_rn(*y, v);
-          }
+          if (col < p.H) p.y0[row * p.H + col] = v;
+          else if (col < p.H + p.KV) p.y1[row * p.KV + col - p.H] = v;
+          else p.y2[row * p.KV + col - p.H - p.KV] = v;
         }
+      }
+    } else {
+      // onto the residual stream; with norm_next, also the next projection's
+      // operand and the tile's square sum of each row (every thread takes
+      // part in the per-row reductions)
+      const int col = kRgTileM * col_tile + m;
+      const bool has = col < p.ncols, norm = p.norm_next != nullptr;
+      int it = 0;
+      for (int r = split; r < nr; r += splits, ++it) {
+        float y = 0.f;
+        const size_t row = static_cast<size_t>(r0 + r);
+        if (has) {
+          float* yp = p.y0 + row * p.ncols + col;
+          y = __fadd_rn(*yp, reduced(r, m));
+          *yp = y;
+          if (norm)
+            static_cast<__nv_bfloat16*>(p.xg)[row * p.ncols + col] = __float2bfloat16_rn(__fmul_rn(y, gn));
+        }
+        if (norm) {
+          float sq = __fmul_rn(y, y);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+          if (lane == 0) red_s[warp][it] = sq;
+        }
+      }
+      if (norm) {
+        __syncthreads();
+        for (int i = tid; i < it; i += kRgThreads)
+          p.ssq[static_cast<size_t>(r0 + split + i * splits) * p.ssq_ld + col_tile] =
+              ((red_s[0][i] + red_s[1][i]) + red_s[2][i]) + red_s[3][i];
       }
     }
   }
+  if (warp == 0) SLMKV_TL_MARK(kTlRowGemmStored + MODE);
   rg_cluster_sync();  // no CTA leaves (with its shared memory) while another may read it
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();

@@ -28,9 +28,14 @@ enum TimelineKind : uint16_t {
   kTlMlp1,
   kTlDecodeWaited = 24,    // a decode warp passed its wait on the previous kernel
   kTlDecodeSliceDone = 25, // a decode warp's slice streamed, its in-CTA merges done
+  kTlExactWaited = 26,     // exact attention: past the wait on the previous kernel
+  kTlExactSoftmax = 27,    // exact attention: probabilities ready, value folds start
   kTlRowGemm = 32,      // + the row GEMM's mode
   kTlRowGemmMmaDone = 40,  // + mode: a CTA's MMAs complete (its epilogue starts)
   kTlRowGemmWaited = 48,   // + mode: the producer passed the wait on the previous kernel
+  kTlMlpPhase = 56,        // + 0..6: a one-row cluster launch's phase boundaries
+  kTlRowGemmPartials = 64, // + mode: the cluster's partial sums in shared memory
+  kTlRowGemmStored = 72,   // + mode: a CTA's epilogue stores issued
 };
 
 #ifdef SLMKV_TIMELINE

@@ -33,6 +33,13 @@ NAMES = {1: "decode", 2: "decode (layers)", 3: "append", 5: "prefill", 6: "exact
          15: "proj1", 16: "prefill_tc", 17: "mlp1 (cluster)", 32: "gemm_qkv", 33: "gemm_o", 34: "gemm_gu",
          35: "gemm_down"}
 MARK_WAITED, MARK_SLICE_DONE = 24, 25  # decode warps (slmkv_timeline.h)
+EXACT_MARKS = {26: "past the wait", 27: "softmax done"}
+MLP_MARKS = {56: "past the wait", 57: "weights in", 58: "O + barrier", 59: "FFN norm",
+             60: "gate/up + barrier", 61: "down + barrier", 62: "attn norm"}
+
+
+def is_mark(kind):
+    return ((kind >= 24) & (kind < 32)) | (kind >= 40)
 
 
 def launches(rec):
@@ -129,9 +136,9 @@ def pct(a, ps=(0, 0.1, 0.5, 0.9, 0.99, 1.0)):
 
 
 def report(rec):
-    marks = rec[(rec["kind"] == MARK_WAITED) | (rec["kind"] == MARK_SLICE_DONE) | (rec["kind"] >= 40)]
-    runs = launches(rec[((rec["kind"] < 40) & (rec["kind"] != MARK_WAITED) &
-                         (rec["kind"] != MARK_SLICE_DONE))])
+    mk = is_mark(rec["kind"])
+    marks = rec[mk]
+    runs = launches(rec[~mk])
     steps = []
     for g in runs:
         if g["kind"] == 8:  # embed opens a step
@@ -160,6 +167,26 @@ def report(rec):
     for g in st[:12]:
         print(f"  {NAMES.get(g['kind'], g['kind']):16s} {(g['t0'] - base) / 1e3:8.2f} "
               f"{(g['t1'] - base) / 1e3:8.2f}")
+    gemm_marks = [(32 + md, {48 + md: "producer past the wait", 40 + md: "MMAs done",
+                                64 + md: "partials", 72 + md: "stored"}) for md in range(4)]
+    for kind, names in [(6, EXACT_MARKS), (17, MLP_MARKS)] + gemm_marks:
+        gs = [g for s in full for g in s if g["kind"] == kind]
+        if not gs:
+            continue
+        print(f"{NAMES[kind]}: phases, median over launches of the first / last warp's time "
+              "from the launch's first entry (us)")
+        row = []
+        for k, nm in names.items():
+            ts = []
+            for g in gs:
+                t = marks[(marks["kind"] == k) & (marks["t0"] >= g["t0"]) & (marks["t0"] <= g["t1"])]["t0"]
+                if len(t):
+                    ts.append(((int(t.min()) - g["t0"]) / 1e3, (int(t.max()) - g["t0"]) / 1e3))
+            if ts:
+                ts = np.array(ts)
+                row.append(f"{nm} {np.median(ts[:, 0]):.2f} / {np.median(ts[:, 1]):.2f}")
+        row.append(f"exit {np.median([(g['t1'] - g['t0']) / 1e3 for g in gs]):.2f}")
+        print("  " + "; ".join(row))
     dec = [g for s in full for g in s if g["kind"] == 1]
     if dec:
         print("decode launches, warps' times from the launch's first entry (p0 / 10 / 50 / 90 / "
