@@ -589,6 +589,11 @@ struct slm_model {
     const float *attn_norm, *ffn_norm;  // [H]
     const __nv_bfloat16 *wqkv, *wo, *wgu, *wd;
     CUtensorMap tm_qkv, tm_o, tm_gu, tm_d;  // the same matrices for the tensor-core row GEMMs
+    // Models whose one-row steps run as one cluster launch a layer: the same
+    // matrices bf16 in the reference's [out][in] layout (each output's
+    // weights one contiguous row): wqkv_r [H+2KV][H], wo_r [H][H],
+    // wgu_r [2I][H] (gate rows, then up), wd_r [H][I]; null otherwise.
+    const __nv_bfloat16 *wqkv_r, *wo_r, *wgu_r, *wd_r;
   };
   std::vector<Layer> layers;
   int32_t sms = 148;
@@ -806,30 +811,36 @@ __global__ void __launch_bounds__(128) proj1_kernel(const ProjArgs a) {
 // output columns, each the reference's in-order fma fold (linear.rs:98-103)
 // as proj1_kernel does; the new residual row and the SiTU-GLU outputs are
 // written into every CTA's shared memory (distributed shared memory) and a
-// cluster barrier stands where two kernel boundaries stood.
+// cluster barrier stands where two kernel boundaries stood. The slices are
+// the matrices' [out][in] copies, one padded row an output column, so a fold
+// reads 8 weights with one 16-byte shared load.
 constexpr int kMlpCluster = 8;
 constexpr int kMlpThreads = 192;
 struct MlpArgs {
   const float* att;          // attention output row [H]
   float* x;                  // residual row [H]: + output projection, + down projection
-  const __nv_bfloat16* wo;   // [H][H]
-  const __nv_bfloat16* wgu;  // [H][2I]: gate | up
-  const __nv_bfloat16* wd;   // [I][H]
+  const __nv_bfloat16* wo;   // [H out][H in]
+  const __nv_bfloat16* wgu;  // [2I out][H in]: gate rows, then up rows
+  const __nv_bfloat16* wd;   // [H out][I in]
   const float* ffn_norm;     // [H]
   float eps, beta_gate, beta_up;
   int32_t H, I;
   // with wqkv set: the next layer's attention RMSNorm and q/k/v projection too
-  const __nv_bfloat16* wqkv;  // [H][H + 2 KV]
+  const __nv_bfloat16* wqkv;  // [H + 2 KV out][H in]
   const float* attn_norm;     // [H]
   float *q, *k, *v;           // [H], [KV], [KV]
   int32_t KV;
 };
-size_t mlp1_smem(int32_t H, int32_t I, int32_t KV) {  // KV = 0: without the next q/k/v
+// Shared memory of one CTA (KV = 0: without the next q/k/v): the bf16 slices
+// [CO][H + 8] output, [CI][H + 8] gate and up, [CO][I + 8] down, [CQ][H + 8]
+// q/k/v, then the f32 rows (rounded attention row, residual, normalised row,
+// SiTU-GLU outputs, this CTA's up columns, the FFN and attention norm scales)
+size_t mlp1_smem(int32_t H, int32_t I, int32_t KV) {
   const size_t co = H / kMlpCluster, ci = I / kMlpCluster;
   const size_t cq = KV ? (H + 2 * KV) / kMlpCluster : 0;
-  return 2 * (static_cast<size_t>(H) * co + 2 * static_cast<size_t>(H) * ci + static_cast<size_t>(I) * co +
-              static_cast<size_t>(H) * cq) +
-         4 * (3 * static_cast<size_t>(H) + I + ci);
+  const size_t hp = static_cast<size_t>(H) + 8, ip = static_cast<size_t>(I) + 8;
+  return 2 * (co * hp + 2 * ci * hp + co * ip + cq * hp) +
+         4 * (4 * static_cast<size_t>(H) + I + ci + (KV ? H : 0));
 }
 bool mlp1_fits(int32_t H, int32_t I, int32_t KV) {
   return H % (8 * kMlpCluster) == 0 && I % (8 * kMlpCluster) == 0 && H % 8 == 0 &&
@@ -838,25 +849,39 @@ bool mlp1_fits(int32_t H, int32_t I, int32_t KV) {
                       (H + 2 * KV) / kMlpCluster <= kMlpThreads)) &&
          mlp1_smem(H, I, KV) <= 227 * 1024;
 }
-// acc = fold over k of x[k] * w[k * stride] (bf16 w), in order; K % 8 == 0
-__device__ __forceinline__ float fold_row(const uint16_t* w, int stride, const float* x, int K) {
+// acc = fold over k of x[k] * w[k] (bf16 row w, 16-byte aligned), in order;
+// K % 8 == 0
+__device__ __forceinline__ float fold_row(const uint16_t* w, const float* x, int K) {
   float acc = 0.f;
+#pragma unroll 4
   for (int k = 0; k < K; k += 8) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + k);
     const float4 x0 = *reinterpret_cast<const float4*>(x + k);
     const float4 x1 = *reinterpret_cast<const float4*>(x + k + 4);
-    uint32_t v[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = w[static_cast<size_t>(k + j) * stride];
-    acc = fmaf(x0.x, __uint_as_float(v[0] << 16), acc);
-    acc = fmaf(x0.y, __uint_as_float(v[1] << 16), acc);
-    acc = fmaf(x0.z, __uint_as_float(v[2] << 16), acc);
-    acc = fmaf(x0.w, __uint_as_float(v[3] << 16), acc);
-    acc = fmaf(x1.x, __uint_as_float(v[4] << 16), acc);
-    acc = fmaf(x1.y, __uint_as_float(v[5] << 16), acc);
-    acc = fmaf(x1.z, __uint_as_float(v[6] << 16), acc);
-    acc = fmaf(x1.w, __uint_as_float(v[7] << 16), acc);
+    acc = fmaf(x0.x, __uint_as_float(wv.x << 16), acc);
+    acc = fmaf(x0.y, __uint_as_float(wv.x & 0xffff0000u), acc);
+    acc = fmaf(x0.z, __uint_as_float(wv.y << 16), acc);
+    acc = fmaf(x0.w, __uint_as_float(wv.y & 0xffff0000u), acc);
+    acc = fmaf(x1.x, __uint_as_float(wv.z << 16), acc);
+    acc = fmaf(x1.y, __uint_as_float(wv.z & 0xffff0000u), acc);
+    acc = fmaf(x1.z, __uint_as_float(wv.w << 16), acc);
+    acc = fmaf(x1.w, __uint_as_float(wv.w & 0xffff0000u), acc);
   }
   return acc;
+}
+// rmsnorm.rs:80-91's in-order square-sum fold and 1 / sqrt(mean + eps)
+__device__ __forceinline__ float inv_rms(const float* x, int H, float eps) {
+  float sum = 0.f;
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll 4
+  for (int k = 0; k < H / 4; ++k) {
+    const float4 v = x4[k];
+    sum = fmaf(v.x, v.x, sum);
+    sum = fmaf(v.y, v.y, sum);
+    sum = fmaf(v.z, v.z, sum);
+    sum = fmaf(v.w, v.w, sum);
+  }
+  return 1.f / sqrtf(__fdiv_rn(sum, static_cast<float>(H)) + eps);
 }
 __device__ __forceinline__ void cluster_barrier() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -877,71 +902,74 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int tid = threadIdx.x, H = a.H, I = a.I;
   const int CO = H / kMlpCluster, CI = I / kMlpCluster;
+  const int HP = H + 8, IP = I + 8;  // padded row lengths (bank-conflict-free 16-byte loads)
   uint32_t rank;
   asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
   const int o0 = static_cast<int>(rank) * CO, i0 = static_cast<int>(rank) * CI;
-  // [H][CO] output, [H][CI] gate, [H][CI] up, [I][CO] down slices (bf16), then
-  // the f32 rows: rounded attention row, new residual row, normalised row,
-  // SiTU-GLU outputs, this CTA's up columns
-  __nv_bfloat16* wo_s = reinterpret_cast<__nv_bfloat16*>(smem);
-  __nv_bfloat16* wg_s = wo_s + static_cast<size_t>(H) * CO;
-  __nv_bfloat16* wu_s = wg_s + static_cast<size_t>(H) * CI;
-  __nv_bfloat16* wd_s = wu_s + static_cast<size_t>(H) * CI;
   const int CQ = a.wqkv ? (H + 2 * a.KV) / kMlpCluster : 0, q0 = static_cast<int>(rank) * CQ;
-  __nv_bfloat16* wq_s = wd_s + static_cast<size_t>(I) * CO;  // [H][CQ] next q/k/v slice
-  float* xo = reinterpret_cast<float*>(wq_s + static_cast<size_t>(H) * CQ);
+  uint16_t* wo_s = reinterpret_cast<uint16_t*>(smem);
+  uint16_t* wg_s = wo_s + static_cast<size_t>(CO) * HP;
+  uint16_t* wu_s = wg_s + static_cast<size_t>(CI) * HP;
+  uint16_t* wd_s = wu_s + static_cast<size_t>(CI) * HP;
+  uint16_t* wq_s = wd_s + static_cast<size_t>(CO) * IP;
+  float* xo = reinterpret_cast<float*>(wq_s + static_cast<size_t>(CQ) * HP);
   float* hid = xo + H;
   float* xg = hid + H;
   float* hb = xg + H;
   float* up_s = hb + I;
+  float* gf = up_s + CI;  // FFN norm scale
+  float* ga = gf + H;     // the next layer's attention norm scale (with wqkv)
   __shared__ float inv_s;
   auto smem_u32 = [](const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); };
-  // the weights (no kernel writes them) are requested before the wait
-  const int so = CO / 8, si = CI / 8;
-  for (int i = tid; i < H * so; i += kMlpThreads) {
-    const int k = i / so, sg = i - k * so;
-    cp_async16(smem_u32(wo_s + k * CO + 8 * sg), a.wo + static_cast<size_t>(k) * H + o0 + 8 * sg);
+  // the weights and norm scales (no kernel writes them) are requested before
+  // the wait, 16 bytes a copy along each output's row
+  const int h8 = H / 8, i8 = I / 8;
+  const uint16_t* wo = reinterpret_cast<const uint16_t*>(a.wo);
+  const uint16_t* wgu = reinterpret_cast<const uint16_t*>(a.wgu);
+  const uint16_t* wd = reinterpret_cast<const uint16_t*>(a.wd);
+  const uint16_t* wq = reinterpret_cast<const uint16_t*>(a.wqkv);
+  for (int i = tid; i < CO * h8; i += kMlpThreads) {
+    const int j = i / h8, c = i - j * h8;
+    cp_async16(smem_u32(wo_s + j * HP + 8 * c), wo + static_cast<size_t>(o0 + j) * H + 8 * c);
   }
-  for (int i = tid; i < H * si; i += kMlpThreads) {
-    const int k = i / si, sg = i - k * si;
-    const __nv_bfloat16* src = a.wgu + static_cast<size_t>(k) * 2 * I + i0 + 8 * sg;
-    cp_async16(smem_u32(wg_s + k * CI + 8 * sg), src);
-    cp_async16(smem_u32(wu_s + k * CI + 8 * sg), src + I);
+  for (int i = tid; i < CI * h8; i += kMlpThreads) {
+    const int j = i / h8, c = i - j * h8;
+    cp_async16(smem_u32(wg_s + j * HP + 8 * c), wgu + static_cast<size_t>(i0 + j) * H + 8 * c);
+    cp_async16(smem_u32(wu_s + j * HP + 8 * c), wgu + static_cast<size_t>(I + i0 + j) * H + 8 * c);
   }
-  for (int i = tid; i < I * so; i += kMlpThreads) {
-    const int k = i / so, sg = i - k * so;
-    cp_async16(smem_u32(wd_s + k * CO + 8 * sg), a.wd + static_cast<size_t>(k) * H + o0 + 8 * sg);
+  for (int i = tid; i < CO * i8; i += kMlpThreads) {
+    const int j = i / i8, c = i - j * i8;
+    cp_async16(smem_u32(wd_s + j * IP + 8 * c), wd + static_cast<size_t>(o0 + j) * I + 8 * c);
   }
-  const int sq = CQ / 8, ldq = H + 2 * a.KV;
-  for (int i = tid; i < H * sq; i += kMlpThreads) {
-    const int k = i / sq, sg = i - k * sq;
-    cp_async16(smem_u32(wq_s + k * CQ + 8 * sg), a.wqkv + static_cast<size_t>(k) * ldq + q0 + 8 * sg);
+  for (int i = tid; i < CQ * h8; i += kMlpThreads) {
+    const int j = i / h8, c = i - j * h8;
+    cp_async16(smem_u32(wq_s + j * HP + 8 * c), wq + static_cast<size_t>(q0 + j) * H + 8 * c);
+  }
+  for (int i = tid; i < H / 4; i += kMlpThreads) {
+    cp_async16(smem_u32(gf + 4 * i), a.ffn_norm + 4 * i);
+    if (a.wqkv) cp_async16(smem_u32(ga + 4 * i), a.attn_norm + 4 * i);
   }
   cp_async_commit();
   wait_previous_kernel();  // the attention row comes from the previous kernel
   SLMKV_TL_MARK(kTlMlpPhase + 0);
   for (int k = tid; k < H; k += kMlpThreads) xo[k] = round_bf16(a.att[k]);  // the projection's operand
+  float xres = 0.f;  // this thread's residual element
+  if (tid < CO) xres = a.x[o0 + tid];
   cp_async_wait<0>();
   __syncthreads();
   SLMKV_TL_MARK(kTlMlpPhase + 1);
   // output projection, onto the residual (transformer.rs add_residual_in_place);
   // every CTA receives the new residual row
   if (tid < CO) {
-    const float acc = fold_row(reinterpret_cast<const uint16_t*>(wo_s) + tid, CO, xo, H);
-    store_to_cluster(hid, o0 + tid, __fadd_rn(a.x[o0 + tid], acc));
+    const float acc = fold_row(wo_s + tid * HP, xo, H);
+    store_to_cluster(hid, o0 + tid, __fadd_rn(xres, acc));
   }
   cluster_barrier();
   SLMKV_TL_MARK(kTlMlpPhase + 2);
-  // FFN RMSNorm (rmsnorm.rs:80-91): the in-order square-sum fold
-  if (tid == 0) {
-    float sum = 0.f;
-#pragma unroll 8
-    for (int k = 0; k < H; ++k) sum = fmaf(hid[k], hid[k], sum);
-    inv_s = 1.f / sqrtf(__fdiv_rn(sum, static_cast<float>(H)) + a.eps);
-  }
+  // FFN RMSNorm (rmsnorm.rs:80-91)
+  if (tid == 0) inv_s = inv_rms(hid, H, a.eps);
   __syncthreads();
-  for (int k = tid; k < H; k += kMlpThreads)
-    xg[k] = round_bf16(__fmul_rn(__fmul_rn(hid[k], inv_s), a.ffn_norm[k]));
+  for (int k = tid; k < H; k += kMlpThreads) xg[k] = round_bf16(__fmul_rn(__fmul_rn(hid[k], inv_s), gf[k]));
   __syncthreads();
   SLMKV_TL_MARK(kTlMlpPhase + 3);
   // gate and up columns i0 .. i0 + CI, SiTU-GLU (situ_glu.rs:101-107) as bf16;
@@ -949,7 +977,7 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   float g = 0.f;
   if (tid < 2 * CI) {
     const int up = tid >= CI ? 1 : 0, cl = tid - up * CI;
-    g = fold_row(reinterpret_cast<const uint16_t*>(up ? wu_s : wg_s) + cl, CI, xg, H);
+    g = fold_row((up ? wu_s : wg_s) + cl * HP, xg, H);
     if (up) up_s[cl] = g;
   }
   __syncthreads();
@@ -960,7 +988,7 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   SLMKV_TL_MARK(kTlMlpPhase + 4);
   // down projection, onto the residual
   if (tid < CO) {
-    const float acc = fold_row(reinterpret_cast<const uint16_t*>(wd_s) + tid, CO, hb, I);
+    const float acc = fold_row(wd_s + tid * IP, hb, I);
     const float nx = __fadd_rn(hid[o0 + tid], acc);
     a.x[o0 + tid] = nx;
     if (a.wqkv) store_to_cluster(xo, o0 + tid, nx);  // xo is free: the next layer's row
@@ -969,20 +997,14 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
   cluster_barrier();
   SLMKV_TL_MARK(kTlMlpPhase + 5);
   // the next layer's attention RMSNorm and q/k/v columns q0 .. q0 + CQ
-  if (tid == 0) {
-    float sum = 0.f;
-#pragma unroll 8
-    for (int k = 0; k < H; ++k) sum = fmaf(xo[k], xo[k], sum);
-    inv_s = 1.f / sqrtf(__fdiv_rn(sum, static_cast<float>(H)) + a.eps);
-  }
+  if (tid == 0) inv_s = inv_rms(xo, H, a.eps);
   __syncthreads();
-  for (int k = tid; k < H; k += kMlpThreads)
-    xg[k] = round_bf16(__fmul_rn(__fmul_rn(xo[k], inv_s), a.attn_norm[k]));
+  for (int k = tid; k < H; k += kMlpThreads) xg[k] = round_bf16(__fmul_rn(__fmul_rn(xo[k], inv_s), ga[k]));
   __syncthreads();
   SLMKV_TL_MARK(kTlMlpPhase + 6);
   if (tid < CQ) {
     const int col = q0 + tid;
-    const float acc = fold_row(reinterpret_cast<const uint16_t*>(wq_s) + tid, CQ, xg, H);
+    const float acc = fold_row(wq_s + tid * HP, xg, H);
     if (col < H) a.q[col] = acc;
     else if (col < H + a.KV) a.k[col - H] = acc;
     else a.v[col - H - a.KV] = acc;
@@ -1088,10 +1110,10 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       if (rows == 1 && m->mlp1_ok) {
         // output, FFN norm, gate/up, down (and the next layer's norm and
         // q/k/v): one cluster launch
-        MlpArgs ma{m->att, m->x, Ly.wo, Ly.wgu, Ly.wd, Ly.ffn_norm, m->eps,
+        MlpArgs ma{m->att, m->x, Ly.wo_r, Ly.wgu_r, Ly.wd_r, Ly.ffn_norm, m->eps,
                    m->beta_gate, m->beta_up, H, I};
         if (l + 1 < m->L && m->mlp1_qkv_ok) {
-          ma.wqkv = m->layers[l + 1].wqkv;
+          ma.wqkv = m->layers[l + 1].wqkv_r;
           ma.attn_norm = m->layers[l + 1].attn_norm;
           ma.q = m->q;
           ma.k = m->k;
@@ -1292,7 +1314,9 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
   const size_t o_emb = take(static_cast<size_t>(V) * H * 4), o_final = take(static_cast<size_t>(H) * 4);
   struct LayerOff {
     size_t an, fn, qkv, o, gu, d;
+    size_t qkv_r, o_r, gu_r, d_r;  // [out][in] copies for the one-row cluster launch
   };
+  const bool rows_out = mlp1_fits(H, I, 0);
   std::vector<LayerOff> lo(static_cast<size_t>(L));
   for (auto& x : lo) {
     x.an = take(static_cast<size_t>(H) * 4);
@@ -1301,6 +1325,12 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
     x.o = take(HH * 2);
     x.gu = take(2 * IH * 2);
     x.d = take(IH * 2);
+    if (rows_out) {
+      x.qkv_r = take((HH + 2 * KH) * 2);
+      x.o_r = take(HH * 2);
+      x.gu_r = take(2 * IH * 2);
+      x.d_r = take(IH * 2);
+    }
   }
   std::vector<uint8_t> img(off);
   auto put_f32 = [&](size_t o, const float* src, size_t n) { std::memcpy(img.data() + o, src, n * 4); };
@@ -1312,6 +1342,11 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
     for (int32_t r = 0; r < rows; ++r)
       for (int32_t c2 = 0; c2 < cols; ++c2)
         d[static_cast<size_t>(c2) * ld + col0 + r] = bf16_bits(src[static_cast<size_t>(r) * cols + c2]);
+  };
+  // src [rows][cols] as bf16 rows at byte offset o (the reference's layout)
+  auto put_bf16 = [&](size_t o, const float* src, size_t n) {
+    uint16_t* d = reinterpret_cast<uint16_t*>(img.data() + o);
+    for (size_t i = 0; i < n; ++i) d[i] = bf16_bits(src[i]);
   };
   put_f32(o_emb, h_tensors[0], static_cast<size_t>(V) * H);
   put_f32(o_final, h_tensors[1 + 9 * L], static_cast<size_t>(H));
@@ -1328,6 +1363,15 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
     put_bf16_t(x.gu, t[6], I, H, 2 * I, 0);  // gate columns first
     put_bf16_t(x.gu, t[7], I, H, 2 * I, I);  // then up
     put_bf16_t(x.d, t[8], H, I, H, 0);
+    if (rows_out) {
+      put_bf16(x.qkv_r, t[1], HH);
+      put_bf16(x.qkv_r + HH * 2, t[2], KH);
+      put_bf16(x.qkv_r + (HH + KH) * 2, t[3], KH);
+      put_bf16(x.o_r, t[4], HH);
+      put_bf16(x.gu_r, t[6], IH);
+      put_bf16(x.gu_r + IH * 2, t[7], IH);
+      put_bf16(x.d_r, t[8], IH);
+    }
   }
   auto m = new slm_model();
   m->ctx = ctx;
@@ -1391,9 +1435,9 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
     one_row(proj1_kernel<kProjGU>, proj1_cols<kProjGU>(H), proj1_smem<kProjGU>(H, proj1_cols<kProjGU>(H)), kProjGU);
     one_row(proj1_kernel<kProjDown>, proj1_cols<kProjDown>(I), proj1_smem<kProjDown>(I, proj1_cols<kProjDown>(I)),
             kProjDown);
-    m->mlp1_qkv_ok = mlp1_fits(H, I, KV) && attr(mlp1_kernel, mlp1_smem(H, I, KV)) == cudaSuccess;
+    m->mlp1_qkv_ok = rows_out && mlp1_fits(H, I, KV) && attr(mlp1_kernel, mlp1_smem(H, I, KV)) == cudaSuccess;
     m->mlp1_ok = m->mlp1_qkv_ok ||
-                 (mlp1_fits(H, I, 0) && attr(mlp1_kernel, mlp1_smem(H, I, 0)) == cudaSuccess);
+                 (rows_out && attr(mlp1_kernel, mlp1_smem(H, I, 0)) == cudaSuccess);
   }
   const uint8_t* base = static_cast<const uint8_t*>(m->weights);
   m->emb = reinterpret_cast<const float*>(base + o_emb);
@@ -1422,6 +1466,12 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
     Ly.wo = bf(x.o);
     Ly.wgu = bf(x.gu);
     Ly.wd = bf(x.d);
+    if (rows_out) {
+      Ly.wqkv_r = bf(x.qkv_r);
+      Ly.wo_r = bf(x.o_r);
+      Ly.wgu_r = bf(x.gu_r);
+      Ly.wd_r = bf(x.d_r);
+    }
     // [K rows][columns] bf16, 64 x 64 boxes
     const int32_t nqkv = H + 2 * KV;
     e = encode_row_gemm_map(&Ly.tm_qkv, Ly.wqkv, nqkv, H, 64, 64);
