@@ -1474,15 +1474,18 @@ constexpr int kExactThreads = 128;
 constexpr int kExactChunk = kBlockTokens * D * 4;  // one 16-token block of V, one head
 
 struct ExactSmem {  // byte offsets in dynamic shared memory
-  int stages, ring, full, empty, q, kn, vn, red, ps, total;
+  int stages, kblocks, ring, kst, full, empty, kfull, q, kn, vn, red, ps, total;
 };
-__host__ __device__ inline ExactSmem exact_smem_layout(int max_ctx, int stages) {
+__host__ __device__ inline ExactSmem exact_smem_layout(int max_ctx, int stages, int kblocks) {
   ExactSmem l;
   l.stages = stages;
+  l.kblocks = kblocks;
   l.ring = 0;                                  // stages x 4 KiB, 16-byte aligned
-  l.full = stages * kExactChunk;               // mbarriers
+  l.kst = stages * kExactChunk;                // kblocks x 4 KiB: the first K blocks, fused decode
+  l.full = l.kst + kblocks * kExactChunk;      // mbarriers
   l.empty = l.full + 8 * stages;
-  l.q = l.empty + 8 * stages;                  // 64 floats
+  l.kfull = l.empty + 8 * stages;
+  l.q = l.kfull + 16;                          // 64 floats
   l.kn = l.q + D * 4;                          // the new K row (rotated), fused decode
   l.vn = l.kn + D * 4;                         // the new V row
   l.red = l.vn + D * 4;                        // 8 floats + flags
@@ -1492,13 +1495,15 @@ __host__ __device__ inline ExactSmem exact_smem_layout(int max_ctx, int stages) 
 }
 
 __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const PrefillLaunch p,
-                                                                        int stages) {
+                                                                        int stages, int kblocks) {
   SLMKV_TL(kTlExact);
   extern __shared__ __align__(128) uint8_t sm_exact[];
-  const ExactSmem lay = exact_smem_layout(p.max_ctx, stages);
+  const ExactSmem lay = exact_smem_layout(p.max_ctx, stages, kblocks);
   uint8_t* ring = sm_exact + lay.ring;
+  const float* kst = reinterpret_cast<const float*>(sm_exact + lay.kst);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm_exact + lay.full);
   uint64_t* empty = reinterpret_cast<uint64_t*>(sm_exact + lay.empty);
+  uint64_t* kfull = reinterpret_cast<uint64_t*>(sm_exact + lay.kfull);
   float* qs = reinterpret_cast<float*>(sm_exact + lay.q);
   float* kns = reinterpret_cast<float*>(sm_exact + lay.kn);
   float* vns = reinterpret_cast<float*>(sm_exact + lay.vn);
@@ -1515,6 +1520,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
       mbar_init(&full[st], 1);
       mbar_init(&empty[st], 2);  // one arrival per folding warp
     }
+    mbar_init(kfull, 1);
     fence_mbar_init();
     flags[0] = flags[1] = 0;
     reinterpret_cast<int*>(red)[0] = si;
@@ -1549,6 +1555,19 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
     }
   };
   if (tid == 64 && p.fused) first_copies();
+  // Fused decode: the K blocks of the older positions are staged too (thread
+  // 96, one barrier for all of them; the blocks the V ring stages); the
+  // scores read the staged rows. The new row is never read from there (it
+  // comes from k_new).
+  const int nks = p.fused ? min(kblocks, nload) : 0;
+  if (tid == 96 && nks > 0) {
+    mbar_arrive_expect_tx(kfull, static_cast<uint32_t>(nks) * kExactChunk);
+    for (int b = 0; b < nks; ++b)
+      bulk_load(const_cast<float*>(kst) + b * (kExactChunk / 4), chunk_of(kb, b), kExactChunk, kfull);
+  }
+  // the position's rotation (a constant table) before the wait
+  float2 cs = make_float2(0.f, 0.f);
+  if (warp < 2 && (p.rotate || p.fused)) cs = p.g.rope[static_cast<size_t>(qpos) * (D / 2) + lane];
   // Launched with programmatic stream serialization in the fused form: the
   // inputs (q, new K/V) are the previous kernel's outputs.
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -1557,14 +1576,14 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
   if (tid == 64 && !p.fused) first_copies();
   if (warp == 0) {
     float2 x = reinterpret_cast<const float2*>(p.q + (static_cast<size_t>(r) * Hq + h) * D)[lane];
-    if (p.rotate) x = rope_pair(x, p.g.rope[static_cast<size_t>(qpos) * (D / 2) + lane]);
+    if (p.rotate) x = rope_pair(x, cs);
     reinterpret_cast<float2*>(qs)[lane] = x;
   } else if (warp == 1 && p.fused) {
     // forward_cached_token's append (attention.rs:794-810, kv_cache.rs:182-230)
     const size_t row = (static_cast<size_t>(r) * Hkv + kvh) * D;
     const float2 kx = reinterpret_cast<const float2*>(p.k_new + row)[lane];
     const float2 vx = reinterpret_cast<const float2*>(p.v_new + row)[lane];
-    const float2 kr = rope_pair(kx, p.g.rope[static_cast<size_t>(qpos) * (D / 2) + lane]);
+    const float2 kr = rope_pair(kx, cs);
     const bool fin = finite2(kx) && finite2(vx);
     reinterpret_cast<float2*>(kns)[lane] = kr;
     reinterpret_cast<float2*>(vns)[lane] = vx;
@@ -1580,19 +1599,29 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
     }
   }
   __syncthreads();
+  // the staged K blocks (a bounded wait; on expiry the scores read the pool)
+  int kst_rows = 0;
+  if (nks > 0) {
+    if (mbar_wait_bounded(kfull, 0)) {
+      kst_rows = nks * kBlockTokens;
+    } else if (tid == 0) {
+      atomicOr(p.g.error, kErrTimeout);
+    }
+  }
   // ---- scores, two positions per thread at a time ----------------------------
   bool bad = false;
   float mloc = -INFINITY;
+  auto key_row = [&](int j) {
+    if (p.fused && j == qpos) return reinterpret_cast<const float4*>(kns);
+    if (j < kst_rows) return reinterpret_cast<const float4*>(kst + j * D);
+    return reinterpret_cast<const float4*>(chunk_of(kb, j >> 4) + (j & 15) * D);
+  };
   for (int j0 = tid; j0 < L; j0 += 2 * kExactThreads) {
     const int j1 = j0 + kExactThreads;
     const bool two = j1 < L;
     const int jj1 = two ? j1 : j0;
-    const float4* k0 = (p.fused && j0 == qpos)
-                           ? reinterpret_cast<const float4*>(kns)
-                           : reinterpret_cast<const float4*>(chunk_of(kb, j0 >> 4) + (j0 & 15) * D);
-    const float4* k1 = (p.fused && jj1 == qpos)
-                           ? reinterpret_cast<const float4*>(kns)
-                           : reinterpret_cast<const float4*>(chunk_of(kb, jj1 >> 4) + (jj1 & 15) * D);
+    const float4* k0 = key_row(j0);
+    const float4* k1 = key_row(jj1);
     float a0 = 0.f, a1 = 0.f;
 #pragma unroll
     for (int c = 0; c < D / 4; ++c) {
@@ -1682,6 +1711,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
     // every copy issued lands before the CTA's shared memory is released
     for (int b = max(0, issued - stages); b < issued; ++b)
       mbar_wait_bounded(&full[b % stages], static_cast<uint32_t>(b / stages) & 1u);
+    if (nks > 0 && kst_rows == 0) mbar_wait_bounded(kfull, 0);  // the K copies, after a timeout
   }
   __syncthreads();
   if (tid == 0 && flags[0] && p.status) atomicOr(&p.status[si], kStatusNonFiniteScore);
@@ -1756,8 +1786,16 @@ cudaError_t launch_append(const AppendLaunch& p, cudaStream_t s) {
 int exact_attention_stages(int32_t max_ctx, int64_t items) {
   const int want = items <= 2 * 148 ? 16 : 4;
   for (int st = want; st >= 2; --st)
-    if (exact_smem_layout(max_ctx, st).total <= 227 * 1024) return st;
+    if (exact_smem_layout(max_ctx, st, 0).total <= 227 * 1024) return st;
   return 0;
+}
+// Fused decode with few rows (one CTA an SM or less): the K blocks staged
+// before the wait, as many as the shared memory left holds
+int exact_attention_kblocks(const PrefillLaunch& p, int stages, int64_t items) {
+  if (!p.fused || items > 2 * 148) return 0;
+  const int want = (p.max_ctx + kBlockTokens - 1) / kBlockTokens;
+  const int room = (227 * 1024 - exact_smem_layout(p.max_ctx, stages, 0).total) / kExactChunk;
+  return max(0, min(want, room));
 }
 
 cudaError_t launch_exact_attention(const PrefillLaunch& p0, cudaStream_t s) {
@@ -1768,7 +1806,8 @@ cudaError_t launch_exact_attention(const PrefillLaunch& p0, cudaStream_t s) {
   const int64_t items = static_cast<int64_t>(p.total_tokens) * p.g.q_heads;
   const int stages = exact_attention_stages(p.max_ctx, items);
   if (stages == 0) return cudaErrorInvalidValue;
-  const int smem = exact_smem_layout(p.max_ctx, stages).total;
+  const int kblocks = exact_attention_kblocks(p, stages, items);
+  const int smem = exact_smem_layout(p.max_ctx, stages, kblocks).total;
   cudaError_t e = cudaFuncSetAttribute(exact_attention_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
@@ -1782,7 +1821,7 @@ cudaError_t launch_exact_attention(const PrefillLaunch& p0, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = p.fused ? 1 : 0;  // the fused decode chains onto the q/k/v kernel
-  return cudaLaunchKernelEx(&cfg, exact_attention_kernel, p, stages);
+  return cudaLaunchKernelEx(&cfg, exact_attention_kernel, p, stages, kblocks);
 }
 
 cudaError_t launch_gather(const GatherLaunch& p, cudaStream_t s) {
