@@ -1650,6 +1650,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
   for (int off = 16; off > 0; off >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(kFull, mloc, off));
   if (lane == 0) red[warp] = mloc;
   __syncthreads();
+  SLMKV_TL_MARK(kTlExactScored);
   const float m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   for (int j = tid; j < L; j += kExactThreads) ps[j] = libm::slm_expf(__fsub_rn(ps[j], m));
   __syncthreads();
@@ -1664,6 +1665,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
     red[4] = sum;
   }
   __syncthreads();
+  SLMKV_TL_MARK(kTlExactSummed);
   const float sum = red[4];
   bad |= !(isfinite(sum) && sum > 0.f);
   for (int j = tid; j < L; j += kExactThreads) ps[j] = __fdiv_rn(ps[j], sum);
@@ -1696,6 +1698,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
     }
     if (p.fused && !flags[1]) o = fmaf(vns[tid], ps[qpos], o);
     p.out[(static_cast<size_t>(r) * Hq + h) * D + tid] = o;
+    SLMKV_TL_MARK(kTlExactFolded);
   } else if (tid == 64) {
     for (; issued < nload; ++issued) {
       const int st = issued % stages;
@@ -1789,10 +1792,11 @@ int exact_attention_stages(int32_t max_ctx, int64_t items) {
     if (exact_smem_layout(max_ctx, st, 0).total <= 227 * 1024) return st;
   return 0;
 }
-// Fused decode with few rows (one CTA an SM or less): the K blocks staged
-// before the wait, as many as the shared memory left holds
+// Fused decode with at most one CTA an SM: the K blocks staged before the
+// wait, as many as the shared memory left holds (with more CTAs, staging
+// would leave room for one CTA an SM and need a second wave)
 int exact_attention_kblocks(const PrefillLaunch& p, int stages, int64_t items) {
-  if (!p.fused || items > 2 * 148) return 0;
+  if (!p.fused || items > 148) return 0;
   const int want = (p.max_ctx + kBlockTokens - 1) / kBlockTokens;
   const int room = (227 * 1024 - exact_smem_layout(p.max_ctx, stages, 0).total) / kExactChunk;
   return max(0, min(want, room));

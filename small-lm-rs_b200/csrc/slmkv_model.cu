@@ -950,6 +950,7 @@ __global__ void __launch_bounds__(kMlpThreads) mlp1_kernel(const MlpArgs a) {
     if (a.wqkv) cp_async16(smem_u32(ga + 4 * i), a.attn_norm + 4 * i);
   }
   cp_async_commit();
+  cluster_barrier();  // every CTA of the cluster runs before any writes another's shared memory
   wait_previous_kernel();  // the attention row comes from the previous kernel
   SLMKV_TL_MARK(kTlMlpPhase + 0);
   for (int k = tid; k < H; k += kMlpThreads) xo[k] = round_bf16(a.att[k]);  // the projection's operand

@@ -30,6 +30,9 @@ enum TimelineKind : uint16_t {
   kTlDecodeSliceDone = 25, // a decode warp's slice streamed, its in-CTA merges done
   kTlExactWaited = 26,     // exact attention: past the wait on the previous kernel
   kTlExactSoftmax = 27,    // exact attention: probabilities ready, value folds start
+  kTlExactScored = 28,     // exact attention: scores and their maximum
+  kTlExactSummed = 29,     // exact attention: the softmax sum
+  kTlExactFolded = 30,     // exact attention: a folding warp's outputs stored
   kTlRowGemm = 32,      // + the row GEMM's mode
   kTlRowGemmMmaDone = 40,  // + mode: a CTA's MMAs complete (its epilogue starts)
   kTlRowGemmWaited = 48,   // + mode: the producer passed the wait on the previous kernel

@@ -33,7 +33,7 @@ NAMES = {1: "decode", 2: "decode (layers)", 3: "append", 5: "prefill", 6: "exact
          15: "proj1", 16: "prefill_tc", 17: "mlp1 (cluster)", 32: "gemm_qkv", 33: "gemm_o", 34: "gemm_gu",
          35: "gemm_down"}
 MARK_WAITED, MARK_SLICE_DONE = 24, 25  # decode warps (slmkv_timeline.h)
-EXACT_MARKS = {26: "past the wait", 27: "softmax done"}
+EXACT_MARKS = {26: "past the wait", 28: "scored", 29: "summed", 27: "softmax done", 30: "folded"}
 MLP_MARKS = {56: "past the wait", 57: "weights in", 58: "O + barrier", 59: "FFN norm",
              60: "gate/up + barrier", 61: "down + barrier", 62: "attn norm"}
 
