@@ -424,6 +424,184 @@ __global__ void __launch_bounds__(kProjThreads) proj_kernel(const ProjArgs a) {
   }
 }
 
+// Many-row projections in the reference's order (the exact-order path at 2 ..
+// 1024 rows): one CTA of 128 threads computes a tile of BM = 8 TM rows x 64
+// output columns, each thread TM rows x 4 columns, every output the same
+// in-order fma fold over k from 0, over the same bf16-rounded operands, as
+// proj_kernel's (linear.rs:98-103): the results are proj_kernel's bit for
+// bit. The CTA's rows sit transposed in shared memory for the whole K
+// ([k][row]; for the normed modes the square sums folded in order by one
+// thread a row, then scaled and rounded in place); the weights stream
+// through a ring of 32-row chunks (cp.async), the first ones requested before
+// waiting on the previous kernel. A k step is one shared load of the TM row
+// values, one of the 4 weights, 4 TM fmas; proj_kernel's 64-thread CTAs of 4
+// rows re-read every weight for every 4 rows at 2 warps an SM. GU: a tile is
+// 32 gate and the 32 matching up columns; a thread holds 2 of each and
+// applies SiTU-GLU. K must be a multiple of 32.
+constexpr int kPtThreads = 128;
+constexpr int kPtCols = 64;   // output columns a tile (GU: 32 gate + 32 up)
+constexpr int kPtChunk = 32;  // weight rows a ring stage
+constexpr int kPtStages = 4;
+__host__ __device__ constexpr int pt_rows(int tm) { return 8 * tm; }
+__host__ __device__ constexpr int pt_ld(int tm) { return 8 * tm + 4; }  // padded length of a [k] row
+template <int TM>
+size_t projt_smem(int32_t K) {
+  return static_cast<size_t>(K) * pt_ld(TM) * 4 + static_cast<size_t>(kPtStages) * kPtChunk * kPtCols * 2;
+}
+
+template <int MODE, int TM>
+__global__ void __launch_bounds__(kPtThreads) projt_kernel(const ProjArgs a) {
+  SLMKV_TL(kTlProj);
+  constexpr int BM = pt_rows(TM), LDA = pt_ld(TM);
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int K = a.K, tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  float* xs = reinterpret_cast<float*>(smem);  // [K][LDA]
+  uint16_t* wb = reinterpret_cast<uint16_t*>(smem + static_cast<size_t>(K) * LDA * 4);  // [stage][32][64]
+  __shared__ float inv_s[BM];
+  const int r0 = blockIdx.y * BM, nr = min(BM, a.rows - r0);
+  const int nchunks = K / kPtChunk;
+  // the tile's weight columns: QKV, O, Down 64 adjacent; GU 32 gate columns
+  // c0 .. and the up columns I + c0 ..
+  const int c0 = MODE == kProjGU ? blockIdx.x * (kPtCols / 2) : blockIdx.x * kPtCols;
+  auto load_chunk = [&](int ch, int st) {
+    // 32 weight rows x 8 segments of 8 columns: two 16-byte copies a thread
+    for (int i = tid; i < kPtChunk * 8; i += kPtThreads) {
+      const int kr = i >> 3, seg = i & 7;
+      const int lc = MODE == kProjGU ? c0 + 8 * (seg & 3) : c0 + 8 * seg;  // output column
+      const int col = MODE == kProjGU && seg >= 4 ? a.I + lc : lc;          // weight column
+      if (lc < a.ncols)
+        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(wb + (st * kPtChunk + kr) * kPtCols + 8 * seg)),
+                   a.w + static_cast<size_t>(ch * kPtChunk + kr) * a.ld + col);
+    }
+    cp_async_commit();
+  };
+  for (int ch = 0; ch < kPtStages - 1; ++ch) {
+    if (ch < nchunks) load_chunk(ch, ch);
+    else cp_async_commit();
+  }
+  wait_previous_kernel();  // the rows come from the previous kernels
+  // the rows, transposed (coalesced reads); rows past the end are zeros
+  for (int r = 0; r < BM; ++r) {
+    const size_t src = static_cast<size_t>(r0 + r) * K;
+    for (int k = tid; k < K; k += kPtThreads) {
+      float v = 0.f;
+      if (r < nr) v = MODE == kProjDown ? __bfloat162float(a.xh[src + k]) : a.x[src + k];
+      xs[k * LDA + r] = v;
+    }
+  }
+  __syncthreads();
+  if (MODE == kProjQKV || MODE == kProjGU) {
+    if (tid < nr) {  // rmsnorm.rs:80-91: the square sum in order
+      float s = 0.f;
+#pragma unroll 8
+      for (int k = 0; k < K; ++k) s = fmaf(xs[k * LDA + tid], xs[k * LDA + tid], s);
+      inv_s[tid] = 1.f / sqrtf(__fdiv_rn(s, static_cast<float>(K)) + a.eps);
+    }
+    __syncthreads();
+    for (int k = tid; k < K; k += kPtThreads) {
+      const float g = a.norm_w[k];
+      for (int r = 0; r < nr; ++r) xs[k * LDA + r] = round_bf16(__fmul_rn(__fmul_rn(xs[k * LDA + r], inv_s[r]), g));
+    }
+  } else if (MODE == kProjO) {
+    for (int k = tid; k < K; k += kPtThreads)
+      for (int r = 0; r < nr; ++r) xs[k * LDA + r] = round_bf16(xs[k * LDA + r]);
+  }
+  float acc[TM][4];
+#pragma unroll
+  for (int i = 0; i < TM; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int ch = 0; ch < nchunks; ++ch) {
+    const int st = ch % kPtStages;
+    // the stage chunk ch + 3 fills was read in the previous iteration, which
+    // ended with a barrier
+    if (ch + kPtStages - 1 < nchunks) load_chunk(ch + kPtStages - 1, (ch + kPtStages - 1) % kPtStages);
+    else cp_async_commit();
+    cp_async_wait<kPtStages - 1>();  // chunk ch landed (this thread's copies)
+    __syncthreads();                 // ... and every thread's; the rows, the first time
+    const uint16_t* wst = wb + st * kPtChunk * kPtCols;
+    const float* xk = xs + static_cast<size_t>(ch) * kPtChunk * LDA + ty * TM;
+#pragma unroll 8
+    for (int kk = 0; kk < kPtChunk; ++kk) {
+      float xv[TM];
+      if constexpr (TM == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(xk + kk * LDA);
+        xv[0] = v.x, xv[1] = v.y, xv[2] = v.z, xv[3] = v.w;
+      } else {
+        xv[0] = xk[kk * LDA];
+      }
+      uint32_t w01, w23;
+      if (MODE == kProjGU) {  // a gate pair, the matching up pair
+        w01 = *reinterpret_cast<const uint32_t*>(wst + kk * kPtCols + 2 * tx);
+        w23 = *reinterpret_cast<const uint32_t*>(wst + kk * kPtCols + 32 + 2 * tx);
+      } else {
+        const uint2 w = *reinterpret_cast<const uint2*>(wst + kk * kPtCols + 4 * tx);
+        w01 = w.x, w23 = w.y;
+      }
+      const float w0 = __uint_as_float(w01 << 16), w1 = __uint_as_float(w01 & 0xffff0000u);
+      const float w2 = __uint_as_float(w23 << 16), w3 = __uint_as_float(w23 & 0xffff0000u);
+#pragma unroll
+      for (int i = 0; i < TM; ++i) {
+        acc[i][0] = fmaf(xv[i], w0, acc[i][0]);
+        acc[i][1] = fmaf(xv[i], w1, acc[i][1]);
+        acc[i][2] = fmaf(xv[i], w2, acc[i][2]);
+        acc[i][3] = fmaf(xv[i], w3, acc[i][3]);
+      }
+    }
+    __syncthreads();  // stage st is read: a later chunk may overwrite it
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    const int r = ty * TM + i;
+    if (r >= nr) break;
+    const size_t row = static_cast<size_t>(r0 + r);
+    if (MODE == kProjGU) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int col = c0 + 2 * tx + e;
+        if (col < a.ncols)  // situ_glu.rs:101-107
+          a.h[row * a.I + col] = __float2bfloat16_rn(
+              __fmul_rn(situ_gate(acc[i][e], a.beta_gate), situ_up(acc[i][2 + e], a.beta_up)));
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = c0 + 4 * tx + e;
+        if (col >= a.ncols) continue;
+        if (MODE == kProjQKV) {
+          if (col < a.H) a.y0[row * a.H + col] = acc[i][e];
+          else if (col < a.H + a.KV) a.y1[row * a.KV + col - a.H] = acc[i][e];
+          else a.y2[row * a.KV + col - a.H - a.KV] = acc[i][e];
+        } else {  // transformer.rs add_residual_in_place: hidden += update
+          float* y = a.y0 + row * a.ncols + col;
+          *y = __fadd_rn(*y, acc[i][e]);
+        }
+      }
+    }
+  }
+}
+
+// Shared memory above 48 KB is opted into per device and kernel, raised to
+// the largest launch so far.
+template <int MODE, int TM>
+cudaError_t launch_projt(const ProjArgs& a, cudaStream_t s) {
+  static size_t configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  const size_t smem = projt_smem<TM>(a.K);
+  if (smem > configured[dev]) {
+    e = cudaFuncSetAttribute(projt_kernel<MODE, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = smem;
+  }
+  const int cols = MODE == kProjGU ? kPtCols / 2 : kPtCols;
+  return launch_chained(projt_kernel<MODE, TM>,
+                        dim3((a.ncols + cols - 1) / cols, (a.rows + pt_rows(TM) - 1) / pt_rows(TM)),
+                        dim3(kPtThreads), smem, s, a);
+}
+
 // linear.rs:119-152, the tied vocabulary projection (fp32, unrounded), for
 // up to 64 rows: logits[r][v] = sum_k x[r][k] emb[v][k]. A CTA stages 8 rows
 // in shared memory (small enough for two CTAs an SM, so that enough
@@ -1036,6 +1214,16 @@ cudaError_t launch_proj(const ProjArgs& a, cudaStream_t s) {
     ProjArgs b = a;
     return launch_chained(proj1_kernel<MODE>, dim3((a.ncols + a.cols - 1) / a.cols),
                           dim3(proj_mats<MODE>() * a.cols), proj1_smem<MODE>(a.K, a.cols), s, b);
+  }
+  // several rows: the register-tiled kernel when its rows fit in shared
+  // memory, 32-row tiles when they alone give two waves of CTAs, else 8-row
+  constexpr size_t kSmemMax = 227 * 1024;
+  if (a.rows > 1 && a.K % kPtChunk == 0 && a.ncols % 8 == 0) {
+    const int cols = MODE == kProjGU ? kPtCols / 2 : kPtCols;
+    const int64_t tiles4 = static_cast<int64_t>((a.rows + pt_rows(4) - 1) / pt_rows(4)) *
+                           ((a.ncols + cols - 1) / cols);
+    if (tiles4 >= 2 * 148 && projt_smem<4>(a.K) <= kSmemMax) return launch_projt<MODE, 4>(a, s);
+    if (projt_smem<1>(a.K) <= kSmemMax) return launch_projt<MODE, 1>(a, s);
   }
   const int gx = (a.ncols + kProjCols - 1) / kProjCols;
   if (a.rows == 1)

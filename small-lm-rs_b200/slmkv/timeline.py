@@ -8,7 +8,7 @@ every kernel record its kernel kind, SM and %globaltimer at entry and exit;
 this module runs the scaled GQA model's decode steps on it and prints, per
 kernel, where a step's time goes:
 
-    python -m slmkv.timeline [--workload gqa-model|model] [--steps 6] [--batch 16]
+    python -m slmkv.timeline [--workload gqa-model|model|prefix] [--steps 6] [--batch 16]
 
 (run from the repository root with small-lm-rs_b200 on sys.path, as the
 tests do). The numbers are of the timeline build, whose records cost a few
@@ -58,8 +58,9 @@ def launches(rec):
 
 def run_steps(workload: str, steps: int, batch: int):
     """bench.py's gqa-model workload (the scaled GQA model, 16 sequences of
-    1-8 k tokens, row-GEMM projections) or model workload (the 8M model,
-    batch 1, a 64-token prompt, exact-order projections), one GPU: prefill,
+    1-8 k tokens, row-GEMM projections), model workload (the 8M model,
+    batch 1, a 64-token prompt, exact-order projections) or prefix workload's
+    decode shape (the 8M model, 64 sequences of 384 tokens), one GPU: prefill,
     10 untimed decode steps, then `steps` recorded ones. Returns the records
     sorted by entry time."""
     import torch
@@ -202,7 +203,7 @@ def report(rec):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["gqa-model", "model"], default="gqa-model")
+    ap.add_argument("--workload", choices=["gqa-model", "model", "prefix"], default="gqa-model")
     ap.add_argument("--steps", type=int, default=6)
     ap.add_argument("--batch", type=int, default=None)
     a = ap.parse_args()
