@@ -480,13 +480,32 @@ __global__ void __launch_bounds__(kPtThreads) projt_kernel(const ProjArgs a) {
     else cp_async_commit();
   }
   wait_previous_kernel();  // the rows come from the previous kernels
-  // the rows, transposed (coalesced reads); rows past the end are zeros
-  for (int r = 0; r < BM; ++r) {
-    const size_t src = static_cast<size_t>(r0 + r) * K;
-    for (int k = tid; k < K; k += kPtThreads) {
-      float v = 0.f;
-      if (r < nr) v = MODE == kProjDown ? __bfloat162float(a.xh[src + k]) : a.x[src + k];
-      xs[k * LDA + r] = v;
+  // the rows, transposed: a thread takes features k, k + 128, ... and for
+  // each all BM rows (coalesced across the threads), KI features' loads in
+  // flight before their stores; rows past the end are zeros
+  constexpr int KI = TM == 4 ? 2 : 4;
+  for (int kb = 0; kb < K; kb += KI * kPtThreads) {
+    float v[KI][BM];
+#pragma unroll
+    for (int u = 0; u < KI; ++u) {
+      const int k = kb + u * kPtThreads + tid;
+#pragma unroll
+      for (int r = 0; r < BM; ++r) {
+        v[u][r] = 0.f;
+        if (k < K && r < nr) {
+          const size_t src = static_cast<size_t>(r0 + r) * K + k;
+          v[u][r] = MODE == kProjDown ? __bfloat162float(a.xh[src]) : a.x[src];
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < KI; ++u) {
+      const int k = kb + u * kPtThreads + tid;
+      if (k < K) {
+#pragma unroll
+        for (int r = 0; r < BM; r += 4)
+          *reinterpret_cast<float4*>(xs + k * LDA + r) = make_float4(v[u][r], v[u][r + 1], v[u][r + 2], v[u][r + 3]);
+      }
     }
   }
   __syncthreads();
