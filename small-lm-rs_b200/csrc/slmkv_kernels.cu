@@ -1494,8 +1494,11 @@ __host__ __device__ inline ExactSmem exact_smem_layout(int max_ctx, int stages, 
   return l;
 }
 
+constexpr int kExactRoundBlocks = kExactThreads / kBlockTokens;  // K blocks a round: a position a thread
+
 __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const PrefillLaunch p,
-                                                                        int stages, int kblocks) {
+                                                                        int stages, int kblocks,
+                                                                        int kbufs) {
   SLMKV_TL(kTlExact);
   extern __shared__ __align__(128) uint8_t sm_exact[];
   const ExactSmem lay = exact_smem_layout(p.max_ctx, stages, kblocks);
@@ -1520,7 +1523,8 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
       mbar_init(&full[st], 1);
       mbar_init(&empty[st], 2);  // one arrival per folding warp
     }
-    mbar_init(kfull, 1);
+    mbar_init(&kfull[0], 1);
+    mbar_init(&kfull[1], 1);
     fence_mbar_init();
     flags[0] = flags[1] = 0;
     reinterpret_cast<int*>(red)[0] = si;
@@ -1558,8 +1562,24 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
   // Fused decode: the K blocks of the older positions are staged too (thread
   // 96, one barrier for all of them; the blocks the V ring stages); the
   // scores read the staged rows. The new row is never read from there (it
-  // comes from k_new).
-  const int nks = p.fused ? min(kblocks, nload) : 0;
+  // comes from k_new). With kbufs > 0 (more CTAs than SMs: not every block
+  // fits) K passes instead through kbufs buffers of kExactRoundBlocks
+  // blocks, a round of 128 positions each (a position a thread), the first
+  // rounds requested before the wait and each later one as a buffer frees.
+  const int nks = (p.fused && kbufs == 0) ? min(kblocks, nload) : 0;
+  const int nrounds = kbufs ? (L + kExactThreads - 1) / kExactThreads : 0;
+  auto round_blocks = [&](int rr) { return max(0, min(kExactRoundBlocks, nload - rr * kExactRoundBlocks)); };
+  auto issue_round = [&](int rr) {  // thread 96
+    const int nb = round_blocks(rr), buf = rr % kbufs;
+    if (nb == 0) return;
+    mbar_arrive_expect_tx(&kfull[buf], static_cast<uint32_t>(nb) * kExactChunk);
+    for (int b = 0; b < nb; ++b)
+      bulk_load(const_cast<float*>(kst) + (buf * kExactRoundBlocks + b) * (kExactChunk / 4),
+                chunk_of(kb, rr * kExactRoundBlocks + b), kExactChunk, &kfull[buf]);
+  };
+  int rounds_issued = 0;
+  if (tid == 96)
+    for (; rounds_issued < min(kbufs, nrounds); ++rounds_issued) issue_round(rounds_issued);
   if (tid == 96 && nks > 0) {
     mbar_arrive_expect_tx(kfull, static_cast<uint32_t>(nks) * kExactChunk);
     for (int b = 0; b < nks; ++b)
@@ -1602,7 +1622,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
   // the staged K blocks (a bounded wait; on expiry the scores read the pool)
   int kst_rows = 0;
   if (nks > 0) {
-    if (mbar_wait_bounded(kfull, 0)) {
+    if (mbar_wait_bounded(&kfull[0], 0)) {
       kst_rows = nks * kBlockTokens;
     } else if (tid == 0) {
       atomicOr(p.g.error, kErrTimeout);
@@ -1616,7 +1636,46 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
     if (j < kst_rows) return reinterpret_cast<const float4*>(kst + j * D);
     return reinterpret_cast<const float4*>(chunk_of(kb, j >> 4) + (j & 15) * D);
   };
-  for (int j0 = tid; j0 < L; j0 += 2 * kExactThreads) {
+  // K in rounds through the buffers: position rr * 128 + tid in round rr;
+  // after a bounded wait that expires the round reads the pool instead, and
+  // no later round is requested (flags[1]: the CTA's copies are abandoned)
+  for (int rr = 0; rr < nrounds; ++rr) {
+    const int nb = round_blocks(rr), buf = rr % kbufs;
+    bool staged = false;
+    if (nb > 0 && !flags[1]) {
+      staged = mbar_wait_bounded(&kfull[buf], static_cast<uint32_t>(rr / kbufs) & 1u);
+      if (!staged) {
+        flags[1] = 1;
+        if (tid == 0) atomicOr(p.g.error, kErrTimeout);
+      }
+    }
+    const int j = rr * kExactThreads + tid;
+    if (j < L) {
+      const int bj = (j >> 4) - rr * kExactRoundBlocks;
+      const float4* k0 = (p.fused && j == qpos) ? reinterpret_cast<const float4*>(kns)
+                         : (staged && bj < nb)
+                             ? reinterpret_cast<const float4*>(kst + (buf * kExactRoundBlocks + bj) * (kExactChunk / 4) +
+                                                               (j & 15) * D)
+                             : reinterpret_cast<const float4*>(chunk_of(kb, j >> 4) + (j & 15) * D);
+      float a0 = 0.f;
+#pragma unroll
+      for (int c = 0; c < D / 4; ++c) {
+        const float4 q4 = reinterpret_cast<const float4*>(qs)[c];
+        const float4 x0 = k0[c];
+        a0 = fmaf(q4.x, x0.x, a0);
+        a0 = fmaf(q4.y, x0.y, a0);
+        a0 = fmaf(q4.z, x0.z, a0);
+        a0 = fmaf(q4.w, x0.w, a0);
+      }
+      const float s0 = __fmul_rn(a0, kScaleExact);
+      bad |= !isfinite(s0);
+      ps[j] = s0;
+      mloc = fmaxf(mloc, s0);
+    }
+    __syncthreads();  // buffer buf is read
+    if (tid == 96 && !flags[1] && rounds_issued < nrounds) issue_round(rounds_issued++);
+  }
+  for (int j0 = kbufs ? L : tid; j0 < L; j0 += 2 * kExactThreads) {
     const int j1 = j0 + kExactThreads;
     const bool two = j1 < L;
     const int jj1 = two ? j1 : j0;
@@ -1714,7 +1773,12 @@ __global__ void __launch_bounds__(kExactThreads) exact_attention_kernel(const Pr
     // every copy issued lands before the CTA's shared memory is released
     for (int b = max(0, issued - stages); b < issued; ++b)
       mbar_wait_bounded(&full[b % stages], static_cast<uint32_t>(b / stages) & 1u);
-    if (nks > 0 && kst_rows == 0) mbar_wait_bounded(kfull, 0);  // the K copies, after a timeout
+    if (nks > 0 && kst_rows == 0) mbar_wait_bounded(&kfull[0], 0);  // the K copies, after a timeout
+  } else if (tid == 96 && kbufs > 0) {
+    // K rounds requested and not consumed (after an abandoned round) land
+    // before the CTA's shared memory is released
+    for (int rr = max(0, rounds_issued - kbufs); rr < rounds_issued; ++rr)
+      if (round_blocks(rr) > 0) mbar_wait_bounded(&kfull[rr % kbufs], static_cast<uint32_t>(rr / kbufs) & 1u);
   }
   __syncthreads();
   if (tid == 0 && flags[0] && p.status) atomicOr(&p.status[si], kStatusNonFiniteScore);
@@ -1801,6 +1865,24 @@ int exact_attention_kblocks(const PrefillLaunch& p, int stages, int64_t items) {
   const int room = (227 * 1024 - exact_smem_layout(p.max_ctx, stages, 0).total) / kExactChunk;
   return max(0, min(want, room));
 }
+// Fused decode with more CTAs than SMs: K rounds through two buffers (one
+// CTA in two SMs' worth of rows: two CTAs an SM) or one (more), the V ring 8
+// or 4 deep; none when the rows' probabilities leave no room.
+struct ExactShape {
+  int stages, kblocks, kbufs;
+};
+ExactShape exact_attention_shape(const PrefillLaunch& p, int64_t items) {
+  ExactShape sh{exact_attention_stages(p.max_ctx, items), 0, 0};
+  if (sh.stages == 0) return sh;
+  if (p.fused && items > 148) {
+    const ExactShape r{items <= 2 * 148 ? 8 : 4, 0, items <= 2 * 148 ? 2 : 1};
+    if (exact_smem_layout(p.max_ctx, r.stages, r.kbufs * kExactRoundBlocks).total <= 100 * 1024)
+      return ExactShape{r.stages, r.kbufs * kExactRoundBlocks, r.kbufs};
+    return sh;
+  }
+  sh.kblocks = exact_attention_kblocks(p, sh.stages, items);
+  return sh;
+}
 
 cudaError_t launch_exact_attention(const PrefillLaunch& p0, cudaStream_t s) {
   if (p0.n_seq <= 0 || p0.total_tokens <= 0) return cudaSuccess;
@@ -1808,9 +1890,9 @@ cudaError_t launch_exact_attention(const PrefillLaunch& p0, cudaStream_t s) {
   PrefillLaunch p = p0;
   p.max_ctx = (p.max_ctx + 3) & ~3;
   const int64_t items = static_cast<int64_t>(p.total_tokens) * p.g.q_heads;
-  const int stages = exact_attention_stages(p.max_ctx, items);
-  if (stages == 0) return cudaErrorInvalidValue;
-  const int kblocks = exact_attention_kblocks(p, stages, items);
+  const ExactShape sh = exact_attention_shape(p, items);
+  if (sh.stages == 0) return cudaErrorInvalidValue;
+  const int stages = sh.stages, kblocks = sh.kblocks;
   const int smem = exact_smem_layout(p.max_ctx, stages, kblocks).total;
   cudaError_t e = cudaFuncSetAttribute(exact_attention_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1825,7 +1907,7 @@ cudaError_t launch_exact_attention(const PrefillLaunch& p0, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = p.fused ? 1 : 0;  // the fused decode chains onto the q/k/v kernel
-  return cudaLaunchKernelEx(&cfg, exact_attention_kernel, p, stages, kblocks);
+  return cudaLaunchKernelEx(&cfg, exact_attention_kernel, p, stages, kblocks, sh.kbufs);
 }
 
 cudaError_t launch_gather(const GatherLaunch& p, cudaStream_t s) {

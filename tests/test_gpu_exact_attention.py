@@ -128,12 +128,15 @@ def test_decode_steps_are_bit_exact(hq, hkv, fused):
             assert np.array_equal(bits(c.layer_values(layer)), bits(oc.layer_values(layer)))
 
 
-def test_fused_exact_decode_of_many_sequences_is_bit_exact():
-    # 100 sequences x 4 heads: more rows than the deep-ring shape takes, so
-    # the shallow V ring with several CTAs per SM runs
-    rng = np.random.default_rng(77)
+@pytest.mark.parametrize("n,max_len", [(64, 511), (100, 300)])
+def test_fused_exact_decode_of_many_sequences_is_bit_exact(n, max_len):
+    # more CTAs (sequences x 4 heads) than SMs: K passes through shared
+    # memory in rounds of 128 positions, two buffers with an 8-deep V ring at
+    # 256 CTAs (up to four rounds at these lengths), one buffer with a 4-deep
+    # ring at 400
+    rng = np.random.default_rng(77 + n)
     hq, hkv = 4, 2
-    lengths = [int(x) for x in rng.integers(1, 300, size=100)]
+    lengths = [int(x) for x in rng.integers(1, max_len, size=n)]
     n = len(lengths)
     pool = _pool(hq, hkv, layers=1, seqs=n, blocks=sum(L // 16 + 2 for L in lengths) + 8)
     inv = O.rope_inverse_frequencies(D, 10000.0)
