@@ -444,12 +444,16 @@ constexpr int kPtChunk = 32;  // weight rows a ring stage
 constexpr int kPtStages = 4;
 __host__ __device__ constexpr int pt_rows(int tm) { return 8 * tm; }
 __host__ __device__ constexpr int pt_ld(int tm) { return 8 * tm + 4; }  // padded length of a [k] row
+// FULL: the CTA's whole weight slice (K x 64 columns) is requested before
+// the wait and stays in shared memory (for grids of few CTAs, where the
+// ring's refills would sit on the fold's path); else the 4-stage ring
 template <int TM>
-size_t projt_smem(int32_t K) {
-  return static_cast<size_t>(K) * pt_ld(TM) * 4 + static_cast<size_t>(kPtStages) * kPtChunk * kPtCols * 2;
+size_t projt_smem(int32_t K, bool full = false) {
+  return static_cast<size_t>(K) * pt_ld(TM) * 4 +
+         static_cast<size_t>(full ? K / kPtChunk : kPtStages) * kPtChunk * kPtCols * 2;
 }
 
-template <int MODE, int TM>
+template <int MODE, int TM, bool FULL>
 __global__ void __launch_bounds__(kPtThreads) projt_kernel(const ProjArgs a) {
   SLMKV_TL(kTlProj);
   constexpr int BM = pt_rows(TM), LDA = pt_ld(TM);
@@ -475,9 +479,13 @@ __global__ void __launch_bounds__(kPtThreads) projt_kernel(const ProjArgs a) {
     }
     cp_async_commit();
   };
-  for (int ch = 0; ch < kPtStages - 1; ++ch) {
-    if (ch < nchunks) load_chunk(ch, ch);
-    else cp_async_commit();
+  if constexpr (FULL) {
+    for (int ch = 0; ch < nchunks; ++ch) load_chunk(ch, ch);  // one group a chunk
+  } else {
+    for (int ch = 0; ch < kPtStages - 1; ++ch) {
+      if (ch < nchunks) load_chunk(ch, ch);
+      else cp_async_commit();
+    }
   }
   wait_previous_kernel();  // the rows come from the previous kernels
   // the rows, transposed: a thread takes features k, k + 128, ... and for
@@ -528,14 +536,20 @@ __global__ void __launch_bounds__(kPtThreads) projt_kernel(const ProjArgs a) {
   float acc[TM][4];
 #pragma unroll
   for (int i = 0; i < TM; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  if constexpr (FULL) {
+    cp_async_wait<0>();
+    __syncthreads();
+  }
   for (int ch = 0; ch < nchunks; ++ch) {
-    const int st = ch % kPtStages;
-    // the stage chunk ch + 3 fills was read in the previous iteration, which
-    // ended with a barrier
-    if (ch + kPtStages - 1 < nchunks) load_chunk(ch + kPtStages - 1, (ch + kPtStages - 1) % kPtStages);
-    else cp_async_commit();
-    cp_async_wait<kPtStages - 1>();  // chunk ch landed (this thread's copies)
-    __syncthreads();                 // ... and every thread's; the rows, the first time
+    const int st = FULL ? ch : ch % kPtStages;
+    if constexpr (!FULL) {
+      // the stage chunk ch + 3 fills was read in the previous iteration,
+      // which ended with a barrier
+      if (ch + kPtStages - 1 < nchunks) load_chunk(ch + kPtStages - 1, (ch + kPtStages - 1) % kPtStages);
+      else cp_async_commit();
+      cp_async_wait<kPtStages - 1>();  // chunk ch landed (this thread's copies)
+      __syncthreads();                 // ... and every thread's; the rows, the first time
+    }
     const uint16_t* wst = wb + st * kPtChunk * kPtCols;
     const float* xk = xs + static_cast<size_t>(ch) * kPtChunk * LDA + ty * TM;
 #pragma unroll 8
@@ -565,7 +579,7 @@ __global__ void __launch_bounds__(kPtThreads) projt_kernel(const ProjArgs a) {
         acc[i][3] = fmaf(xv[i], w3, acc[i][3]);
       }
     }
-    __syncthreads();  // stage st is read: a later chunk may overwrite it
+    if constexpr (!FULL) __syncthreads();  // stage st is read: a later chunk may overwrite it
   }
   cp_async_wait<0>();
 #pragma unroll
@@ -601,24 +615,32 @@ __global__ void __launch_bounds__(kPtThreads) projt_kernel(const ProjArgs a) {
 
 // Shared memory above 48 KB is opted into per device and kernel, raised to
 // the largest launch so far.
-template <int MODE, int TM>
+template <int MODE, int TM, bool FULL>
 cudaError_t launch_projt(const ProjArgs& a, cudaStream_t s) {
   static size_t configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 64) return cudaErrorInvalidDevice;
-  const size_t smem = projt_smem<TM>(a.K);
+  const size_t smem = projt_smem<TM>(a.K, FULL);
   if (smem > configured[dev]) {
-    e = cudaFuncSetAttribute(projt_kernel<MODE, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(projt_kernel<MODE, TM, FULL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     configured[dev] = smem;
   }
   const int cols = MODE == kProjGU ? kPtCols / 2 : kPtCols;
-  return launch_chained(projt_kernel<MODE, TM>,
+  return launch_chained(projt_kernel<MODE, TM, FULL>,
                         dim3((a.ncols + cols - 1) / cols, (a.rows + pt_rows(TM) - 1) / pt_rows(TM)),
                         dim3(kPtThreads), smem, s, a);
+}
+// the whole slice when the grid's CTAs all fit at once with it (one wave)
+template <int MODE, int TM>
+cudaError_t launch_projt_best(const ProjArgs& a, cudaStream_t s, int64_t ctas) {
+  const size_t full = projt_smem<TM>(a.K, true);
+  const int64_t per_sm = full <= 227 * 1024 ? (228 * 1024) / static_cast<int64_t>(full + 1024) : 0;
+  if (per_sm > 0 && ctas <= 148 * per_sm) return launch_projt<MODE, TM, true>(a, s);
+  return launch_projt<MODE, TM, false>(a, s);
 }
 
 // linear.rs:119-152, the tied vocabulary projection (fp32, unrounded), for
@@ -1241,8 +1263,9 @@ cudaError_t launch_proj(const ProjArgs& a, cudaStream_t s) {
     const int cols = MODE == kProjGU ? kPtCols / 2 : kPtCols;
     const int64_t tiles4 = static_cast<int64_t>((a.rows + pt_rows(4) - 1) / pt_rows(4)) *
                            ((a.ncols + cols - 1) / cols);
-    if (tiles4 >= 2 * 148 && projt_smem<4>(a.K) <= kSmemMax) return launch_projt<MODE, 4>(a, s);
-    if (projt_smem<1>(a.K) <= kSmemMax) return launch_projt<MODE, 1>(a, s);
+    if (tiles4 >= 2 * 148 && projt_smem<4>(a.K) <= kSmemMax) return launch_projt_best<MODE, 4>(a, s, tiles4);
+    const int64_t tiles1 = static_cast<int64_t>((a.rows + pt_rows(1) - 1) / pt_rows(1)) * ((a.ncols + cols - 1) / cols);
+    if (projt_smem<1>(a.K) <= kSmemMax) return launch_projt_best<MODE, 1>(a, s, tiles1);
   }
   const int gx = (a.ncols + kProjCols - 1) / kProjCols;
   if (a.rows == 1)
