@@ -191,7 +191,7 @@ cudaError_t launch_apply_updates(const PoolGeom& g, const TableUpdate* updates, 
                                  const CopyJob* copies, int32_t n_copies, cudaStream_t s);
 
 // ---- few-row projections on the tensor cores (slmkv_rowgemm.cu) ----
-enum : int { kRowQKV = 0, kRowO = 1, kRowGU = 2, kRowDown = 3 };
+enum : int { kRowQKV = 0, kRowO = 1, kRowGU = 2, kRowDown = 3, kRowHead = 4 };
 struct RowGemmLaunch {
   CUtensorMap tmap_w;  // weights [K][ld] bf16, 64 x 64 boxes, 128-byte swizzle
   CUtensorMap tmap_x;  // rows [rows][K] bf16 (encoded by launch_row_gemm)

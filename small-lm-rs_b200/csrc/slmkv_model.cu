@@ -106,7 +106,7 @@ constexpr int kNormMaxWidth = kNormThreads * 4 * kNormVec;
 __global__ void __launch_bounds__(kNormThreads)
     rmsnorm_kernel(const float* __restrict__ x, int32_t rows, int32_t hidden, const float* __restrict__ w,
                    float eps, uint32_t* __restrict__ out_bf16, float* __restrict__ out_f32,
-                   const SeqEntry* __restrict__ seqs) {
+                   const SeqEntry* __restrict__ seqs, uint32_t* __restrict__ out_split = nullptr) {
   SLMKV_TL(kTlNorm);
   const int row = blockIdx.x, tid = threadIdx.x;
   // The scale vector is a weight (no kernel writes it): fetched while the
@@ -160,6 +160,42 @@ __global__ void __launch_bounds__(kNormThreads)
           make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
     else
       reinterpret_cast<float4*>(out_f32 + static_cast<size_t>(row) * hidden)[i] = make_float4(a, b, c, d);
+    if (out_split) {
+      // the row split hi = bf16(v), lo = bf16(v - hi), laid out for the
+      // head GEMM's K order: 64-feature chunk c as [hi_c | lo_c] in the
+      // first 2H, then hi again
+      const uint2 hi = make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
+      const float ha = __uint_as_float(hi.x << 16), hb = __uint_as_float(hi.x & 0xffff0000u);
+      const float hc = __uint_as_float(hi.y << 16), hd = __uint_as_float(hi.y & 0xffff0000u);
+      const uint2 lo = make_uint2(pack_bf16x2(__fsub_rn(a, ha), __fsub_rn(b, hb)),
+                                  pack_bf16x2(__fsub_rn(c, hc), __fsub_rn(d, hd)));
+      uint2* o = reinterpret_cast<uint2*>(out_split + static_cast<size_t>(row) * (3 * hidden / 2));
+      o[32 * (i >> 4) + (i & 15)] = hi;
+      o[32 * (i >> 4) + 16 + (i & 15)] = lo;
+      o[2 * n4 + i] = hi;
+    }
+  }
+}
+
+// The split-bf16 vocabulary projection's weights: out [2H][V] bf16 =
+// [hi; lo] of emb^T (emb [V][H] fp32), hi = bf16(w), lo = bf16(w - hi)
+__global__ void head_split_kernel(const float* __restrict__ emb, int32_t V, int32_t H,
+                                  __nv_bfloat16* __restrict__ out) {
+  __shared__ float t[32][33];
+  const int v0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int v = v0 + i, k = k0 + threadIdx.x;
+    t[i][threadIdx.x] = (v < V && k < H) ? emb[static_cast<size_t>(v) * H + k] : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int k = k0 + i, v = v0 + threadIdx.x;
+    if (k >= H || v >= V) continue;
+    const float w = t[threadIdx.x][i];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(w);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(w, __bfloat162float(hi)));
+    out[static_cast<size_t>(k) * V + v] = hi;
+    out[static_cast<size_t>(H + k) * V + v] = lo;
   }
 }
 
@@ -804,6 +840,10 @@ struct slm_model {
   const float* final_norm = nullptr;  // [H]
   // Projection matrices bf16 and transposed ([in][out] rows): wqkv [H][H+2KV]
   // (columns q | k | v), wo [H][H], wgu [H][2I] (columns gate | up), wd [I][H].
+  // the tied head for the row-GEMM path (models of hidden >= 512): [2H][V]
+  // bf16 (hi; lo of emb^T) and its tensor map; null otherwise
+  __nv_bfloat16* head3 = nullptr;
+  CUtensorMap tm_head;
   struct Layer {
     const float *attn_norm, *ffn_norm;  // [H]
     const __nv_bfloat16 *wqkv, *wo, *wgu, *wd;
@@ -820,6 +860,7 @@ struct slm_model {
   int32_t rows_cap = 0, out_cap = 0;
   float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *gu = nullptr;
   uint32_t* xb = nullptr;  // bf16 pairs, [rows, max(H, I) / 2]
+  uint32_t* xs3 = nullptr;  // bf16 pairs, [out rows, 3H / 2]: the split head operand
   uint32_t* hb = nullptr;  // bf16 pairs, [rows, I / 2]: the row GEMMs' SiTU-GLU output
   // the row GEMMs' RMSNorm across the projections: bf16(x * g) [rows, H] and
   // each row's square sums over the 128-column tiles [rows, ceil(H / 128)]
@@ -856,10 +897,11 @@ void free_scratch(slm_model* m) {
   for (void* p : {static_cast<void*>(m->x), static_cast<void*>(m->q), static_cast<void*>(m->k),
                   static_cast<void*>(m->v), static_cast<void*>(m->att), static_cast<void*>(m->gu),
                   static_cast<void*>(m->xb), static_cast<void*>(m->hb), static_cast<void*>(m->xf),
-                  static_cast<void*>(m->logits), static_cast<void*>(m->xg), static_cast<void*>(m->ssq)})
+                  static_cast<void*>(m->logits), static_cast<void*>(m->xg), static_cast<void*>(m->ssq),
+                  static_cast<void*>(m->xs3)})
     if (p) cudaFree(p);
   m->x = m->q = m->k = m->v = m->att = m->gu = m->xf = m->logits = m->ssq = nullptr;
-  m->xb = m->hb = nullptr;
+  m->xb = m->hb = m->xs3 = nullptr;
   m->xg = nullptr;
   m->rows_cap = m->out_cap = 0;
 }
@@ -891,6 +933,7 @@ slm_status ensure_scratch(slm_model* m, int32_t rows, int32_t out_rows, cudaStre
                 {reinterpret_cast<void**>(&m->xg), R * m->H * 2},
                 {reinterpret_cast<void**>(&m->ssq), R * ssq_tiles(m->H) * 4},
                 {reinterpret_cast<void**>(&m->xf), O * m->H * 4},
+                {reinterpret_cast<void**>(&m->xs3), O * 3 * m->H * 2},
                 {reinterpret_cast<void**>(&m->logits), O * m->V * 4}};
   for (const A& a : allocs) {
     e = cudaMalloc(a.p, a.bytes);
@@ -1404,7 +1447,8 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
       if (l == 0) {
         launched(launch_chained(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, s,
                                 static_cast<const float*>(m->x), rows, H, Ly.attn_norm, m->eps, m->xb,
-                                static_cast<float*>(nullptr), static_cast<const SeqEntry*>(nullptr)));
+                                static_cast<float*>(nullptr), static_cast<const SeqEntry*>(nullptr),
+                                static_cast<uint32_t*>(nullptr)));
         ++launches;
         if ((rc = gemm(kRowQKV, Ly.tm_qkv, m->xb, H, nqkv))) return rc;
       } else {
@@ -1466,15 +1510,34 @@ slm_status run_step(slm_model* m, slm_batch* b, const BatchRows& br, const int32
   }
   if (logits || next) {
     const SeqEntry* last_rows = prefill ? br.d_seqs : nullptr;
+    // the row-GEMM path's head: tensor cores over the split operands
+    const bool head3 = !fused && m->head3 != nullptr && out_rows <= kRowGemmRows;
     if (fused)
       launched(launch_chained(rmsnorm_kernel, dim3(out_rows), dim3(kNormThreads), 0, s, m->x, out_rows, H,
-                              m->final_norm, m->eps, static_cast<uint32_t*>(nullptr), m->xf, last_rows));
+                              m->final_norm, m->eps, static_cast<uint32_t*>(nullptr), m->xf, last_rows,
+                              static_cast<uint32_t*>(nullptr)));
     else
       rmsnorm_kernel<<<out_rows, kNormThreads, 0, s>>>(m->x, out_rows, H, m->final_norm, m->eps, nullptr,
-                                                       m->xf, last_rows);
+                                                       m->xf, last_rows, head3 ? m->xs3 : nullptr);
     ++launches;
     float* lg = logits ? logits : m->logits;
-    if (out_rows > 1 && out_rows <= kHeadMaxRows && m->head_kernel_ok) {
+    if (head3) {
+      RowGemmLaunch g{};
+      g.rows = out_rows;
+      g.H = H;
+      g.KV = KV;
+      g.I = I;
+      g.err = err;
+      g.tmap_w = m->tm_head;
+      g.x = m->xs3;
+      g.K = 3 * H;
+      g.ncols = m->V;
+      g.y0 = lg;
+      const RowGemmPlan q = plan_row_gemm(kRowHead, out_rows, 3 * H, m->V, m->sms);
+      const cudaError_t e2 = launch_row_gemm(kRowHead, g, q, s);
+      if (e2 != cudaSuccess) return cuda_fail(m->ctx, "slm_model vocabulary projection", e2);
+      ++launches;
+    } else if (out_rows > 1 && out_rows <= kHeadMaxRows && m->head_kernel_ok) {
       const dim3 grid((m->V + kHeadEntries - 1) / kHeadEntries, (out_rows + kHeadRows - 1) / kHeadRows);
       launched(launch_chained(head_kernel, grid, dim3(kHeadThreads), static_cast<size_t>(kHeadRows) * H * 4, s,
                               static_cast<const float*>(m->xf), out_rows, H, m->emb, m->V, lg));
@@ -1715,6 +1778,21 @@ slm_status slm_model_create(slm_ctx* ctx, const slm_model_config* config, const 
     }
     m->layers.push_back(Ly);
   }
+  // the row-GEMM path's tied head as one split-bf16 GEMM (hidden >= 512)
+  if (H >= 512 && H % 64 == 0 && V % 8 == 0) {
+    const size_t n = static_cast<size_t>(2) * H * V;
+    e = cudaMalloc(&m->head3, n * 2);
+    if (e == cudaSuccess) {
+      head_split_kernel<<<dim3((V + 31) / 32, (H + 31) / 32), dim3(32, 8)>>>(m->emb, V, H, m->head3);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = encode_row_gemm_map(&m->tm_head, m->head3, V, 2 * H, 64, 64);
+    if (e != cudaSuccess) {
+      slm_model_destroy(m);
+      return cuda_fail(ctx, "slm_model_create (split head)", e);
+    }
+  }
   *out = m;
   return SLM_OK;
 }
@@ -1736,6 +1814,7 @@ slm_status slm_model_destroy(slm_model* m) {
   if (!m) return SLM_ERR_INVALID_INPUT;
   free_scratch(m);
   if (m->weights) cudaFree(m->weights);
+  if (m->head3) cudaFree(m->head3);
   if (m->blas) cublasDestroy(m->blas);
   delete m;
   return SLM_OK;

@@ -20,6 +20,12 @@
 //         same 64 columns), SiTU-GLU (situ_glu.rs:101-107,131-138:
 //         b_g tanh(g / b_g) sigmoid(g) * b_u tanh(u / b_u)), h as bf16
 //   Down  onto the residual stream
+//   Head  the vocabulary logits (fp32, plain stores): the fp32 tied head as
+//         one bf16 GEMM over K = 3H, the rows split x = xh + xl and the
+//         weights w = wh + wl (both bf16), summing xh.wh + xl.wh + xh.wl:
+//         K chunk 2c is xh_c . wh_c and 2c + 1 xl_c . wh_c (the same weight
+//         box twice in a row, the second read from L2), then xh . wl; the
+//         weights are [wh; wl], [2H][V]
 // The RMSNorm between a residual update and the next projection
 // (rmsnorm.rs:80-91: x * inv_rms * g) needs no kernel of its own: O and Down
 // also write bf16(x * g) and each row's square sum over their tile, and QKV
@@ -183,6 +189,11 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
   const int xa0 = MODE == kRowGU ? kRgChunk * col_tile : kRgTileM * col_tile;
   const int xa1 = MODE == kRowGU ? p.I + kRgChunk * col_tile : xa0 + kRgChunk;
   const int yb = row_tile * RT;
+  // the weight row of K row ky (the head's interleaved order; others: ky)
+  auto a_row = [&](int ky) {
+    if (MODE != kRowHead) return ky;
+    return ky < 2 * p.H ? (ky >> 7) << 6 : ky - p.H;
+  };
   auto stage_a = [&](int s) { return sbase + s * Cfg::kStageBytes; };
   auto stage_b = [&](int s) { return sbase + s * Cfg::kStageBytes + kRgABytes; };
 
@@ -195,9 +206,9 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fb),
                      "r"(Cfg::kStageBytes)
                      : "memory");
-        const int ky = (ch0 + i) * kRgChunk;
-        rg_tma(stage_a(i), &p.tmap_w, xa0, ky, fb);
-        rg_tma(stage_a(i) + kRgABytes / 2, &p.tmap_w, xa1, ky, fb);
+        const int ky = (ch0 + i) * kRgChunk, ay = a_row(ky);
+        rg_tma(stage_a(i), &p.tmap_w, xa0, ay, fb);
+        rg_tma(stage_a(i) + kRgABytes / 2, &p.tmap_w, xa1, ay, fb);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
       SLMKV_TL_MARK(kTlRowGemmWaited + MODE);
@@ -213,9 +224,9 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fb),
                      "r"(Cfg::kStageBytes)
                      : "memory");
-        const int ky = (ch0 + i) * kRgChunk;
-        rg_tma(stage_a(s), &p.tmap_w, xa0, ky, fb);
-        rg_tma(stage_a(s) + kRgABytes / 2, &p.tmap_w, xa1, ky, fb);
+        const int ky = (ch0 + i) * kRgChunk, ay = a_row(ky);
+        rg_tma(stage_a(s), &p.tmap_w, xa0, ay, fb);
+        rg_tma(stage_a(s) + kRgABytes / 2, &p.tmap_w, xa1, ay, fb);
         rg_tma(stage_b(s), &p.tmap_x, ky, yb, fb);
         issued = i + 1;
       }
@@ -357,6 +368,10 @@ __global__ void __launch_bounds__(kRgThreads, 1) row_gemm_kernel(const __grid_co
               __float2bfloat16_rn(__fmul_rn(ga, ua));
         }
       }
+    } else if (MODE == kRowHead) {
+      const int col = kRgTileM * col_tile + m;
+      if (col < p.ncols)
+        for (int r = split; r < nr; r += splits) p.y0[static_cast<size_t>(r0 + r) * p.ncols + col] = reduced(r, m);
     } else if (MODE == kRowQKV) {
       const int col = kRgTileM * col_tile + m;
       if (col < p.ncols) {
@@ -502,6 +517,7 @@ cudaError_t launch_row_gemm(int mode, RowGemmLaunch p, const RowGemmPlan& q, cud
     case kRowQKV: return launch_mode<kRowQKV>(p, q.rt, grid, s);
     case kRowO: return launch_mode<kRowO>(p, q.rt, grid, s);
     case kRowGU: return launch_mode<kRowGU>(p, q.rt, grid, s);
+    case kRowHead: return launch_mode<kRowHead>(p, q.rt, grid, s);
     default: return launch_mode<kRowDown>(p, q.rt, grid, s);
   }
 }

@@ -31,7 +31,7 @@ RECORD = np.dtype([("kind", "<u2"), ("sm", "<u2"), ("block", "<u4"), ("t0", "<u8
 NAMES = {1: "decode", 2: "decode (layers)", 3: "append", 5: "prefill", 6: "exact attention", 7: "apply",
          8: "embed", 9: "rmsnorm", 10: "round", 11: "situ", 12: "proj", 13: "head", 14: "argmax",
          15: "proj1", 16: "prefill_tc", 17: "mlp1 (cluster)", 32: "gemm_qkv", 33: "gemm_o", 34: "gemm_gu",
-         35: "gemm_down"}
+         35: "gemm_down", 36: "gemm_head"}
 MARK_WAITED, MARK_SLICE_DONE = 24, 25  # decode warps (slmkv_timeline.h)
 EXACT_MARKS = {26: "past the wait", 28: "scored", 29: "summed", 27: "softmax done", 30: "folded"}
 MLP_MARKS = {56: "past the wait", 57: "weights in", 58: "O + barrier", 59: "FFN norm",
